@@ -1,0 +1,61 @@
+// extern "C" boundary of libddpm_b200.so: argument checks, thread-local error
+// text, and forwarding into the kernel launchers. Declarations and the
+// reference interface each entry point replaces are in include/ddpm_b200.h.
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+
+#include "common.cuh"
+
+namespace ddpm {
+
+namespace {
+thread_local char g_last_error[512] = "";
+std::atomic<unsigned long long> g_launches{0};
+}  // namespace
+
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+void clear_error() { g_last_error[0] = '\0'; }
+
+int dyncat_fwd(const void* x, int xdt, const void* k, int kdt, void* out, int n, int c, int h,
+               int w, int ks, int d0, int d1, int d2, cudaStream_t st);
+int dyncat_bwd(const void* x, int xdt, const void* k, const void* g, int kdt, void* gx, void* gk,
+               int n, int c, int h, int w, int ks, int d0, int d1, int d2, cudaStream_t st);
+
+}  // namespace ddpm
+
+extern "C" {
+
+int ddpm_version(void) { return 100; }
+
+const char* ddpm_last_error(void) { return ddpm::g_last_error; }
+
+unsigned long long ddpm_launch_count(void) {
+  return ddpm::g_launches.load(std::memory_order_relaxed);
+}
+
+int ddpm_dyncat_fwd(const void* x, int x_dtype, const void* kernels, int k_dtype, void* out, int n,
+                    int c, int h, int w, int ksize, int d0, int d1, int d2, void* stream) {
+  ddpm::clear_error();
+  return ddpm::dyncat_fwd(x, x_dtype, kernels, k_dtype, out, n, c, h, w, ksize, d0, d1, d2,
+                          static_cast<cudaStream_t>(stream));
+}
+
+int ddpm_dyncat_bwd(const void* x, int x_dtype, const void* kernels, const void* grad_out,
+                    int k_dtype, void* grad_x, void* grad_k, int n, int c, int h, int w, int ksize,
+                    int d0, int d1, int d2, void* stream) {
+  ddpm::clear_error();
+  return ddpm::dyncat_bwd(x, x_dtype, kernels, grad_out, k_dtype, grad_x, grad_k, n, c, h, w,
+                          ksize, d0, d1, d2, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,149 @@
+"""Drop-in ``DDPM`` (Dynamic Dilated Pyramid Module) for B200.
+
+Mirrors the reference's ``triton_impl.DDPM`` (``triton_impl.py:247-392``):
+same constructor arguments and validation messages, same parameters and
+state-dict keys (``generator.weight [3CK^2, C, 1, 1]``, ``generator.bias``,
+``fuse.weight [C, 4C, 3, 3]``, ``fuse.bias``), same ``forward(x, y)`` and
+autograd contract, so state dicts interchange with the reference's
+``unfold_impl.DDPM`` and ``triton_impl.DDPM`` in both directions.
+
+What changed is the GPU body: the Triton kernels, autotune tables and the
+silent CPU fallback (``triton_impl.py:23-33, 353-354``) are replaced by the
+sm_100a kernels of ``libddpm_b200.so``. CUDA tensors always take the native
+path; CPU tensors raise (the reference's CPU branches are not part of this
+build). The final 3x3 ``fuse`` convolution stays a PyTorch/cuDNN call, as in
+the reference (``triton_impl.py:294, 392``).
+"""
+
+from __future__ import annotations
+
+import torch
+from torch import nn
+
+from . import _kernels
+
+_DEFAULT_DILATIONS = (1, 3, 5)
+
+
+def _check_inputs(x: torch.Tensor, y: torch.Tensor, channels: int) -> None:
+    """Input contract of the reference (``triton_impl.py:36-44``), same messages."""
+    if x.ndim != 4 or y.ndim != 4:
+        raise ValueError(f"x and y must be NCHW tensors, got {x.shape=} and {y.shape=}")
+    if x.shape != y.shape:
+        raise ValueError(f"x and y must have identical shapes, got {x.shape=} and {y.shape=}")
+    if x.shape[1] != channels:
+        raise ValueError(f"expected {channels} channels, got {x.shape[1]}")
+    if x.device != y.device:
+        raise ValueError(f"x and y must be on the same device, got {x.device} and {y.device}")
+
+
+def _autocast_enabled() -> bool:
+    try:
+        return torch.is_autocast_enabled("cuda")
+    except TypeError:  # older signature
+        return torch.is_autocast_enabled()
+
+
+class DDPM(nn.Module):
+    """Dynamic Dilated Pyramid Module with sm_100a fused and materialised paths.
+
+    Args:
+        dim: Input/output channel count.
+        kernel_size: Odd dynamic depthwise kernel size.
+        spatial_tile_size: Kept for API compatibility (the reference's CPU
+            streaming tile, ``triton_impl.py:253-254``); unused on the GPU.
+        max_generated_bytes: Kept for API compatibility (CPU budget,
+            ``triton_impl.py:255-257``); unused on the GPU.
+        recompute: Kept for API compatibility (CPU checkpointing).
+        fused_generator_inference: Fuse the 1x1 generator with the dynamic
+            filter (taps never reach HBM) when gradients are disabled.
+        fused_generator_training: ``None`` (default) picks the path from the
+            measured crossover, ``True`` always uses the flash-style recompute
+            training path, ``False`` always materialises the taps.
+    """
+
+    def __init__(
+        self,
+        dim: int,
+        kernel_size: int = 3,
+        *,
+        spatial_tile_size: int = 4096,
+        max_generated_bytes: int = 256 * 1024**2,
+        recompute: bool = True,
+        fused_generator_inference: bool = True,
+        fused_generator_training: bool | None = None,
+    ) -> None:
+        super().__init__()
+        if kernel_size < 1 or kernel_size % 2 == 0:
+            raise ValueError(f"kernel_size must be a positive odd integer, got {kernel_size}")
+        if dim < 1:
+            raise ValueError(f"dim must be positive, got {dim}")
+
+        self.dim = dim
+        self.kernel_size = kernel_size
+        self.spatial_tile_size = spatial_tile_size
+        self.max_generated_bytes = max_generated_bytes
+        self.recompute = recompute
+        self.fused_generator_inference = fused_generator_inference
+        self.fused_generator_training = fused_generator_training
+        self.dilations = _DEFAULT_DILATIONS
+        self.generator = nn.Conv2d(dim, 3 * dim * kernel_size**2, 1)
+        self.fuse = nn.Conv2d(4 * dim, dim, 3, 1, 1)
+
+    # ------------------------------------------------------------ dispatch --
+    def _fused_generator_ok(self, x: torch.Tensor, y: torch.Tensor) -> bool:
+        """Dtype/bias/autocast preconditions of the fused generator path
+        (reference ``triton_impl.py:322-329``) plus this build's kernel limits."""
+        gen = self.generator
+        return (
+            not _autocast_enabled()
+            and x.dtype == y.dtype == gen.weight.dtype
+            and gen.bias is not None
+            and gen.bias.dtype == x.dtype
+            and _kernels.fused_generator_supported(self.dim, self.kernel_size, x.dtype)
+        )
+
+    def _use_fused_training(self, x: torch.Tensor) -> bool:
+        requested = self.fused_generator_training
+        if requested is None:
+            requested = _kernels.auto_fuse_training(
+                x.shape[0] * x.shape[2] * x.shape[3], self.dim, self.kernel_size, x.dtype
+            )
+        return bool(requested) and _kernels.fused_training_supported(self.kernel_size)
+
+    def _cuda_cat(self, x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
+        """GPU path selection (replaces ``DDPM._cuda_cat``, ``triton_impl.py:305-348``)."""
+        grad = torch.is_grad_enabled()
+        fuse_training = grad and self._use_fused_training(x)
+        want_fused = (self.fused_generator_inference and not grad) or fuse_training
+        if want_fused and self._fused_generator_ok(x, y):
+            return _kernels.fused_generator_dynamic_cat(
+                x,
+                y,
+                self.generator.weight,
+                self.generator.bias,
+                self.kernel_size,
+                self.dilations,
+            )
+        kernels = self.generator(y).reshape(
+            x.shape[0],
+            len(self.dilations),
+            self.dim,
+            self.kernel_size**2,
+            x.shape[2],
+            x.shape[3],
+        )
+        return _kernels.fused_dynamic_cat(x, kernels, self.kernel_size, self.dilations)
+
+    def forward(self, x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
+        _check_inputs(x, y, self.dim)
+        if not x.is_cuda:
+            raise RuntimeError(
+                "DDPM (B200 build) runs on CUDA tensors only; got tensors on "
+                f"{x.device}. The reference's CPU paths are not part of this build."
+            )
+        cat_out = self._cuda_cat(x, y)
+        return self.fuse(cat_out)
+
+
+__all__ = ["DDPM"]

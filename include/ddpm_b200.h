@@ -1,0 +1,99 @@
+/*
+ * ddpm_b200.h — C ABI of the B200 (sm_100a) DDPM dynamic-convolution library.
+ *
+ * The library replaces the GPU half of lartpang/DynamicConvolutionOperator:
+ * every Triton kernel in `_triton_kernels.py` and the launch logic of its two
+ * autograd functions. All entry points are plain C: device pointers, sizes,
+ * dtype codes and a CUDA stream handle. No entry point allocates, frees or
+ * synchronises; callers own every buffer (outputs and workspaces included).
+ * Work is enqueued on `stream` (a `cudaStream_t`, NULL = legacy default stream).
+ *
+ * Layout conventions (identical to the reference, which forces `.contiguous()`
+ * at `_triton_kernels.py:817-818, 874-877`):
+ *   x, y, grad_x, grad_y : [N, C, H, W]            contiguous NCHW
+ *   kernels, grad_k      : [N, 3, C, K*K, H, W]    contiguous
+ *   out, grad_out        : [N, 4*C, H, W]          = concat(x, d0, d1, d2)
+ *   weight, grad_weight  : [3*C*K*K, C] (a Conv2d [3CK^2, C, 1, 1] weight)
+ *   bias, grad_bias      : [3*C*K*K]
+ * Weight row index = (branch*C + c)*K*K + tap (`_triton_kernels.py:322`).
+ *
+ * Return value: 0 on success, a negative DDPM_ERR_* code otherwise; the
+ * message of the last error on the calling thread is `ddpm_last_error()`.
+ */
+#ifndef DDPM_B200_H
+#define DDPM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define DDPM_API __attribute__((visibility("default")))
+#else
+#define DDPM_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element types (torch.float32 / torch.bfloat16 / torch.float16). */
+#define DDPM_F32  0
+#define DDPM_BF16 1
+#define DDPM_F16  2
+
+#define DDPM_OK                 0
+#define DDPM_ERR_INVALID_ARG   -1  /* bad size, dtype, null pointer, misalignment */
+#define DDPM_ERR_UNSUPPORTED   -2  /* valid request outside this build's limits   */
+#define DDPM_ERR_CUDA          -3  /* a CUDA launch/runtime call failed           */
+#define DDPM_ERR_WORKSPACE     -4  /* workspace pointer/size too small            */
+
+/* Library ABI version (major*100 + minor). */
+DDPM_API int ddpm_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+DDPM_API const char* ddpm_last_error(void);
+
+/* Number of kernels this library has launched in this process (all devices,
+ * all threads). Benchmarks read it to count the library's launches. */
+DDPM_API unsigned long long ddpm_launch_count(void);
+
+/*
+ * Materialised dynamic filter, forward.
+ * Replaces `_DynamicCat.forward` + `_dynamic_cat_fwd`
+ * (reference `_triton_kernels.py:814-842` and `:21-101`).
+ *   out[n, 0:C]         = x
+ *   out[n, (b+1)C + c]  = sum_tap x[c, p + off(tap)*d_b] * kernels[n, b, c, tap, p]
+ * with zero padding, FP32 accumulation, and out stored in `k_dtype`
+ * (the reference allocates `out` with `kernels.dtype`, `:820-822`).
+ * `x_dtype` may differ from `k_dtype` (autocast: fp32 x, bf16 kernels).
+ * ksize must be odd, 1 <= ksize <= 7; dilations >= 1.
+ */
+DDPM_API int ddpm_dyncat_fwd(const void* x, int x_dtype,
+                    const void* kernels, int k_dtype,
+                    void* out,
+                    int n, int c, int h, int w,
+                    int ksize, int d0, int d1, int d2,
+                    void* stream);
+
+/*
+ * Materialised dynamic filter, backward.
+ * Replaces `_DynamicCat.backward` + `_dynamic_cat_bwd_x` + `_dynamic_cat_bwd_k`
+ * (reference `_triton_kernels.py:844-866`, `:104-190`, `:193-254`).
+ *   grad_x[c,q] = grad_out[c,q]
+ *               + sum_{b,tap} kernels[b,c,tap,q-off*d_b] * grad_out[(b+1)C+c, q-off*d_b]
+ *   grad_k[b,c,tap,p] = x[c, p+off*d_b] * grad_out[(b+1)C+c, p]
+ * grad_out has `k_dtype`; grad_x has `x_dtype`; grad_k has `k_dtype`.
+ * Either output may be NULL to skip it (one fused launch computes both).
+ */
+DDPM_API int ddpm_dyncat_bwd(const void* x, int x_dtype,
+                    const void* kernels, const void* grad_out, int k_dtype,
+                    void* grad_x, void* grad_k,
+                    int n, int c, int h, int w,
+                    int ksize, int d0, int d1, int d2,
+                    void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* DDPM_B200_H */

@@ -1,0 +1,76 @@
+"""Host-side contract of the drop-in DDPM (CPU, no GPU needed).
+
+Mirrors the reference's own unit tests for the API (``test_triton_impl.py:58-65``)
+and the constructor / input checks (``triton_impl.py:36-44, 280-283``).
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from dynamicconvolutionoperator_b200 import DDPM, fused_dynamic_cat
+from dynamicconvolutionoperator_b200 import triton_impl as drop_in
+from oracle import ddpm_oracle as orc
+
+
+def test_rejects_invalid_shapes():
+    model = DDPM(4, 3)
+    with pytest.raises(ValueError, match="identical shapes"):
+        model(torch.randn(1, 4, 5, 5), torch.randn(1, 4, 4, 5))
+
+
+def test_rejects_even_kernel():
+    with pytest.raises(ValueError, match="positive odd"):
+        DDPM(4, 2)
+
+
+@pytest.mark.parametrize("ks", [0, -1, 4])
+def test_rejects_bad_kernel_sizes(ks):
+    with pytest.raises(ValueError, match="positive odd"):
+        DDPM(4, ks)
+
+
+def test_rejects_bad_dim():
+    with pytest.raises(ValueError, match="dim must be positive"):
+        DDPM(0, 3)
+
+
+def test_rejects_non_nchw_and_channel_mismatch():
+    model = DDPM(4, 3)
+    with pytest.raises(ValueError, match="NCHW"):
+        model(torch.randn(4, 5, 5), torch.randn(4, 5, 5))
+    with pytest.raises(ValueError, match="expected 4 channels"):
+        model(torch.randn(1, 3, 5, 5), torch.randn(1, 3, 5, 5))
+
+
+def test_cpu_tensors_fail_loudly():
+    """No CPU fallback: CPU tensors that pass the input checks raise."""
+    model = DDPM(4, 3)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        model(torch.randn(1, 4, 5, 5), torch.randn(1, 4, 5, 5))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        fused_dynamic_cat(torch.randn(1, 2, 3, 3), torch.randn(1, 3, 2, 9, 3, 3), 3, (1, 3, 5))
+
+
+@pytest.mark.parametrize("ks", [1, 3, 5])
+def test_state_dict_interchange_with_unfold_reference(ks):
+    """Parameter names/shapes match the reference (``unfold_impl.py:15,19``)."""
+    ref = orc.make_model(6, ks, seed=11)
+    new = DDPM(6, ks)
+    new.load_state_dict(ref.state_dict())
+    back = orc.UnfoldDDPM(6, ks)
+    back.load_state_dict(new.state_dict())
+    for k, v in ref.state_dict().items():
+        torch.testing.assert_close(back.state_dict()[k], v, rtol=0, atol=0)
+    assert new.generator.weight.shape == (3 * 6 * ks * ks, 6, 1, 1)
+    assert new.fuse.weight.shape == (6, 24, 3, 3)
+
+
+def test_ctor_keeps_reference_attributes():
+    m = DDPM(8, 3, spatial_tile_size=11, max_generated_bytes=0, recompute=False,
+             fused_generator_inference=False, fused_generator_training=True)
+    assert (m.dim, m.kernel_size, m.spatial_tile_size, m.max_generated_bytes) == (8, 3, 11, 0)
+    assert m.recompute is False and m.fused_generator_inference is False
+    assert m.fused_generator_training is True and m.dilations == (1, 3, 5)
+    assert drop_in.DDPM is DDPM

@@ -1,0 +1,99 @@
+"""Materialised dynamic filter kernels (ddpm_dyncat_fwd / ddpm_dyncat_bwd)
+against the oracle's closed-form math in float64 (``_triton_kernels.py:21-254``).
+
+Edge cases follow the reference's own coverage (non-power-of-2 channels,
+non-square borders, cross-tile neighbourhoods: ``gpu_validate.py:39-41``) plus
+1x1 images, images smaller than the dilation halo, multi-tile planes with
+ragged edges, K up to 7, custom dilations and the autocast dtype pair.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from oracle import ddpm_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(2, 3, 5, 7), (2, 24, 15, 17), (1, 4, 1, 1), (1, 2, 3, 200), (3, 5, 33, 130)]
+TOLS = {torch.float32: (1e-5, 1e-5), torch.bfloat16: (8e-3, 2e-3), torch.float16: (1e-3, 1e-4)}
+
+
+def _inputs(shape, ks, xdt, kdt, seed=0):
+    gen = torch.Generator().manual_seed(seed)
+    n, c, h, w = shape
+    x = torch.randn(shape, generator=gen).to(xdt)
+    k = torch.randn((n, 3, c, ks * ks, h, w), generator=gen).to(kdt)
+    g = torch.randn((n, 4 * c, h, w), generator=gen).to(kdt)
+    return x, k, g
+
+
+def _check(actual, gold, dtype):
+    rtol, atol = TOLS[dtype]
+    torch.testing.assert_close(actual.double().cpu(), gold, rtol=rtol, atol=atol)
+
+
+@pytest.mark.parametrize("shape", SHAPES)
+@pytest.mark.parametrize("ks", [1, 3, 5, 7])
+@pytest.mark.parametrize(
+    "xdt,kdt",
+    [(torch.float32, torch.float32), (torch.bfloat16, torch.bfloat16),
+     (torch.float16, torch.float16), (torch.float32, torch.bfloat16)],
+)
+def test_dyncat_forward_backward(shape, ks, xdt, kdt):
+    from dynamicconvolutionoperator_b200 import fused_dynamic_cat
+
+    dil = (1, 3, 5)
+    x, k, g = _inputs(shape, ks, xdt, kdt)
+    xd = x.cuda().requires_grad_(True)
+    kd = k.cuda().requires_grad_(True)
+    out = fused_dynamic_cat(xd, kd, ks, dil)
+    assert out.dtype == kdt and out.shape == (shape[0], 4 * shape[1], *shape[2:])
+    gx, gk = torch.autograd.grad(out, (xd, kd), g.cuda())
+    gold_out = orc.dynamic_cat(x.double(), k.double(), ks, dil)
+    gold_gx, gold_gk = orc.dynamic_cat_backward(x.double(), k.double(), g.double(), ks, dil)
+    _check(out, gold_out, kdt)
+    _check(gx, gold_gx, xdt if xdt != torch.float32 else kdt)
+    _check(gk, gold_gk, kdt)
+
+
+@pytest.mark.parametrize("dil", [(2, 1, 4), (1, 1, 1), (7, 2, 3)])
+def test_dyncat_custom_dilations(dil):
+    from dynamicconvolutionoperator_b200 import fused_dynamic_cat
+
+    x, k, g = _inputs((2, 6, 19, 23), 3, torch.float32, torch.float32, seed=3)
+    xd = x.cuda().requires_grad_(True)
+    kd = k.cuda().requires_grad_(True)
+    out = fused_dynamic_cat(xd, kd, 3, dil)
+    gx, gk = torch.autograd.grad(out, (xd, kd), g.cuda())
+    _check(out, orc.dynamic_cat(x.double(), k.double(), 3, dil), torch.float32)
+    ggx, ggk = orc.dynamic_cat_backward(x.double(), k.double(), g.double(), 3, dil)
+    _check(gx, ggx, torch.float32)
+    _check(gk, ggk, torch.float32)
+
+
+def test_dyncat_only_requested_grads():
+    from dynamicconvolutionoperator_b200 import fused_dynamic_cat
+
+    x, k, g = _inputs((1, 4, 9, 9), 3, torch.float32, torch.float32)
+    kd = k.cuda().requires_grad_(True)
+    out = fused_dynamic_cat(x.cuda(), kd, 3, (1, 3, 5))
+    (gk,) = torch.autograd.grad(out, (kd,), g.cuda())
+    _, ggk = orc.dynamic_cat_backward(x.double(), k.double(), g.double(), 3, (1, 3, 5))
+    _check(gk, ggk, torch.float32)
+
+
+def test_dyncat_large_plane_bf16():
+    """128x128 C=64 (BASELINE configs[2] filter shape), fwd + bwd."""
+    from dynamicconvolutionoperator_b200 import fused_dynamic_cat
+
+    x, k, g = _inputs((1, 64, 128, 128), 3, torch.bfloat16, torch.bfloat16, seed=5)
+    xd = x.cuda().requires_grad_(True)
+    kd = k.cuda().requires_grad_(True)
+    out = fused_dynamic_cat(xd, kd, 3, (1, 3, 5))
+    gx, gk = torch.autograd.grad(out, (xd, kd), g.cuda())
+    _check(out, orc.dynamic_cat(x.double(), k.double(), 3), torch.bfloat16)
+    ggx, ggk = orc.dynamic_cat_backward(x.double(), k.double(), g.double(), 3)
+    _check(gx, ggx, torch.bfloat16)
+    _check(gk, ggk, torch.bfloat16)

@@ -1,0 +1,49 @@
+"""The C-ABI shared library loads and exports every declared entry point (CPU).
+
+No compute call is made here; only argument validation paths that return
+before touching the GPU are exercised.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from dynamicconvolutionoperator_b200 import _lib
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "ddpm_b200.h"
+
+
+def declared_symbols() -> list[str]:
+    text = HEADER.read_text()
+    return re.findall(r"DDPM_API\s+[\w\s\*]+?\b(ddpm_\w+)\s*\(", text)
+
+
+def test_header_and_binding_agree():
+    decl = set(declared_symbols())
+    assert decl, "no declarations parsed from the header"
+    assert decl == set(_lib.exported_symbols())
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(str(_lib.LIB_PATH))
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+    assert _lib.load().ddpm_version() >= 100
+
+
+def test_argument_errors_return_codes_without_gpu():
+    lib = _lib.load()
+    rc = lib.ddpm_dyncat_fwd(None, 0, None, 0, None, 1, 1, 1, 1, 3, 1, 3, 5, None)
+    assert rc == -1
+    assert b"null" in lib.ddpm_last_error()
+    rc = lib.ddpm_dyncat_fwd(1, 0, 1, 0, 1, 1, 1, 1, 1, 2, 1, 3, 5, None)
+    assert rc == -1
+    assert b"odd" in lib.ddpm_last_error()
+    rc = lib.ddpm_dyncat_fwd(1, 7, 1, 0, 1, 1, 1, 1, 1, 3, 1, 3, 5, None)
+    assert rc == -1
+    with pytest.raises(RuntimeError, match="dtype"):
+        _lib.call("ddpm_dyncat_bwd", 1, 9, 1, 1, 0, 1, 1, 1, 1, 1, 1, 3, 1, 3, 5, None)
