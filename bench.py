@@ -61,6 +61,9 @@ def parse_args(argv=None):
     ap.add_argument("--no-graph", action="store_true", help="time eager steps for 'value'")
     ap.add_argument("--skip-extra", action="store_true", help="headline dtype only")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU oracle baseline leg")
+    ap.add_argument("--profile-kernel", default=None,
+                    help="only launch this library kernel (ncu capture target)")
+    ap.add_argument("--profile-iters", type=int, default=3)
     return ap.parse_args(argv)
 
 
@@ -288,14 +291,12 @@ def load_peaks():
 NCU_TRAFFIC_BYTES: dict[tuple[str, str], float] = {}
 
 
-def kernel_roofline(model, x, y, dtype, steps, device):
-    """Time the library's kernels of the step in isolation (CUDA events, L2
-    flushed before every launch) and return per-kernel roofline entries."""
+def library_kernels(model, x, y, dtype, device):
+    """Thunks launching each library kernel of the step on its own, with the
+    operands it sees inside the step, and each kernel's roofline work unit:
+    (thunk, bound, algorithmic bytes or FLOPs per launch)."""
     from dynamicconvolutionoperator_b200 import _lib
 
-    hbm, tflops, src = load_peaks()
-    stream = torch.cuda.current_stream(device)
-    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
     n = x.shape[0]
     elt = x.element_size()
     ncp = n * C * H * W
@@ -307,34 +308,77 @@ def kernel_roofline(model, x, y, dtype, steps, device):
     gk = torch.empty_like(taps)
     code = _lib.dtype_code(dtype)
     sh = _lib.stream_handle(device)
-    kernels = {
+    from dynamicconvolutionoperator_b200 import _kernels
+
+    gen_w = model.generator.weight.detach()
+    gen_b = model.generator.bias.detach()
+    packed = _kernels.pack_generator_weight(gen_w, C, K, use_cache=False)
+    out2 = torch.empty_like(out)
+    keep = (taps, out, gout, gx, gk, packed, out2)
+    return keep, {
+        "gencat_fwd": (
+            lambda: _lib.call("ddpm_gencat_fwd", x.data_ptr(), y.data_ptr(), packed.data_ptr(),
+                              gen_b.data_ptr(), out2.data_ptr(), n, C, H, W, K, *DILATIONS,
+                              code, sh),
+            "tensor", 2 * (3 * C * K * K) * C * n * H * W,
+        ),
         "dyncat_fwd": (
             lambda: _lib.call("ddpm_dyncat_fwd", x.data_ptr(), code, taps.data_ptr(), code,
                               out.data_ptr(), n, C, H, W, K, *DILATIONS, sh),
-            (3 * K * K + 5) * ncp * elt,
+            "hbm", (3 * K * K + 5) * ncp * elt,
         ),
         "dyncat_bwd": (
             lambda: _lib.call("ddpm_dyncat_bwd", x.data_ptr(), code, taps.data_ptr(),
                               gout.data_ptr(), code, gx.data_ptr(), gk.data_ptr(),
                               n, C, H, W, K, *DILATIONS, sh),
-            (6 * K * K + 9) * ncp * elt,
+            "hbm", (6 * K * K + 9) * ncp * elt,
         ),
     }
+
+
+def kernel_roofline(model, x, y, dtype, steps, device):
+    """Time the library's kernels of the step in isolation (CUDA events, L2
+    flushed before every launch) and return per-kernel roofline entries."""
+    hbm, tflops, src = load_peaks()
+    stream = torch.cuda.current_stream(device)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
+    keep, kernels = library_kernels(model, x, y, dtype, device)
     res = {}
-    for name, (fn, alg_bytes) in kernels.items():
+    for name, (fn, bound, work) in kernels.items():
         for _ in range(3):
             fn()
         ts = time_steps(fn, max(steps, 5), flush, stream)
         t = sum(ts) / len(ts)
-        achieved = alg_bytes / (t * 1e-3) / 1e9
+        if bound == "hbm":
+            achieved, peak, unit = work / (t * 1e-3) / 1e9, hbm, "GB/s"
+        else:
+            achieved, peak, unit = work / (t * 1e-3) / 1e12, tflops, "TFLOP/s"
         traffic = NCU_TRAFFIC_BYTES.get((name, str(dtype)))
         res[name] = {
-            "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-            "frac": round(achieved / hbm, 4), "traffic": traffic, "alg_bytes": alg_bytes,
+            "bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
+            "frac": round(achieved / peak, 4), "traffic": traffic, "work": work,
             "ms": round(t, 5), "peak_source": src,
         }
-    del taps, gk
+    del keep
     return res
+
+
+def profile_kernel(args):
+    """Launch one library kernel ``--profile-iters`` times at the bench config
+    (the target of the committed ncu captures; prints nothing but 'ok')."""
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    dtype = DTYPES[args.dtype]
+    model, _ = build_model(dtype, args.path, device)
+    x, y, _ = [t.to(device) for t in make_inputs(args.batch, dtype, 0)]
+    keep, kernels = library_kernels(model, x, y, dtype, device)
+    fn = kernels[args.profile_kernel][0]
+    for _ in range(args.profile_iters):
+        fn()
+    torch.cuda.synchronize()
+    del keep
+    print("ok")
+    return 0
 
 
 # -------------------------------------------------------------- CPU legs --
@@ -396,6 +440,8 @@ def main(argv=None):
     args = parse_args(argv)
     if args.impl == "reference":
         return run_reference_arm(args)
+    if args.profile_kernel:
+        return profile_kernel(args)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -465,7 +511,7 @@ def main(argv=None):
                     "h2d_bytes_per_step": headline["h2d_bytes"],
                     "d2h_bytes_per_step": headline["d2h_bytes"]},
             "gpu_launches": int(headline["launches_per_step"] * args.steps),
-            "roofline": {k: v for k, v in roof[dominant].items() if k != "alg_bytes"}
+            "roofline": {k: v for k, v in roof[dominant].items() if k != "work"}
             | {"kernel": dominant},
             "kernels": roof,
             "clocks": headline["clocks"],

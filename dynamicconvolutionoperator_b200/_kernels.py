@@ -100,17 +100,23 @@ def fused_dynamic_cat(x, kernels, kernel_size, dilations):
 # padded channel count in shared memory and TMEM).
 FUSED_MAX_CHANNELS = 64
 FUSED_KERNEL_SIZES = (1, 3)
+# The flash-style recompute backward kernels.
+FUSED_BACKWARD_AVAILABLE = False
 
 
 def fused_generator_supported(channels: int, kernel_size: int, dtype: torch.dtype) -> bool:
     """Whether the fused generator+filter kernels cover this configuration."""
-    return False
+    return (
+        channels <= FUSED_MAX_CHANNELS
+        and kernel_size in FUSED_KERNEL_SIZES
+        and dtype in _lib.DTYPE_CODE
+    )
 
 
 def fused_training_supported(kernel_size: int) -> bool:
     """The flash-style recompute backward covers K <= 3, like the reference
     (``triton_impl.py:320``)."""
-    return kernel_size in FUSED_KERNEL_SIZES
+    return FUSED_BACKWARD_AVAILABLE and kernel_size in FUSED_KERNEL_SIZES
 
 
 def auto_fuse_training(tokens: int, channels: int, kernel_size: int, dtype: torch.dtype) -> bool:
@@ -122,9 +128,101 @@ def auto_fuse_training(tokens: int, channels: int, kernel_size: int, dtype: torc
     return tokens > 16384 or (tokens == 16384 and dtype == torch.float32)
 
 
+# ------------------------------------------------------- weight packing ----
+_pack_cache: dict[tuple, tuple] = {}
+
+
+def pack_generator_weight(weight: torch.Tensor, channels: int, kernel_size: int,
+                          use_cache: bool) -> torch.Tensor:
+    """Packed copy of the generator weight in the fused kernels' operand layout.
+
+    With ``use_cache`` the packed copy is reused while ``weight`` (same tensor
+    object, same in-place version counter) is unchanged; autograd and CUDA-graph
+    paths pack on every call so a captured step repacks updated weights.
+    """
+    w2 = weight.reshape(weight.shape[0], -1).contiguous()
+    key = (weight.data_ptr(), weight.device, weight.dtype, channels, kernel_size)
+    if use_cache:
+        hit = _pack_cache.get(key)
+        if hit is not None and hit[0]() is weight and hit[1] == weight._version:
+            return hit[2]
+    code = _lib.dtype_code(weight.dtype)
+    nbytes = int(_lib.load().ddpm_gencat_pack_bytes(channels, kernel_size, code))
+    packed = torch.empty(nbytes, dtype=torch.uint8, device=weight.device)
+    _lib.call("ddpm_gencat_pack", w2.data_ptr(), channels, kernel_size, code,
+              packed.data_ptr(), nbytes, _lib.stream_handle(weight.device))
+    if use_cache:
+        import weakref
+
+        _pack_cache.clear()  # one live entry per process is plenty (one DDPM layer)
+        _pack_cache[key] = (weakref.ref(weight), weight._version, packed)
+    return packed
+
+
+def _launch_gencat_fwd(x, y, packed, bias, kernel_size, dilations):
+    n, c, h, w = x.shape
+    out = torch.empty((n, 4 * c, h, w), dtype=x.dtype, device=x.device)
+    d0, d1, d2 = _dil(dilations)
+    _lib.call(
+        "ddpm_gencat_fwd",
+        x.data_ptr(), y.data_ptr(), packed.data_ptr(), bias.data_ptr(), out.data_ptr(),
+        n, c, h, w, int(kernel_size), d0, d1, d2, _lib.dtype_code(x.dtype),
+        _lib.stream_handle(x.device),
+    )
+    return out
+
+
+def _prepare(x, y, weight, bias, kernel_size):
+    x, y = x.contiguous(), y.contiguous()
+    bias = bias.contiguous()
+    _require_cuda(x, y, weight, bias)
+    n, c, h, w = x.shape
+    if not (x.dtype == y.dtype == weight.dtype == bias.dtype):
+        raise RuntimeError("fused generator path needs x, y, weight and bias of one dtype")
+    if weight.shape[0] != 3 * c * kernel_size**2 or weight.numel() != weight.shape[0] * c:
+        raise ValueError(f"generator weight must be [3*C*K^2, C(,1,1)], got {tuple(weight.shape)}")
+    if not fused_generator_supported(c, kernel_size, x.dtype):
+        raise RuntimeError(
+            f"fused generator kernels support C <= {FUSED_MAX_CHANNELS} and K in "
+            f"{FUSED_KERNEL_SIZES}; got C={c}, K={kernel_size}"
+        )
+    return x, y, bias
+
+
+class _GeneratorDynamicCat(torch.autograd.Function):
+    """Fused generator + filter (reference ``_GeneratorDynamicCat``,
+    ``_triton_kernels.py:911-1053``): saves only ``(x, y, weight, bias)``."""
+
+    @staticmethod
+    def forward(ctx, x, y, weight, bias, kernel_size, dilations):
+        x, y, bias = _prepare(x, y, weight, bias, kernel_size)
+        with torch.cuda.device(x.device):
+            packed = pack_generator_weight(weight, x.shape[1], kernel_size, use_cache=False)
+            out = _launch_gencat_fwd(x, y, packed, bias, kernel_size, dilations)
+        ctx.save_for_backward(x, y, weight, bias)
+        ctx.packed = packed
+        ctx.kernel_size = int(kernel_size)
+        ctx.dilations = _dil(dilations)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        raise NotImplementedError("fused generator backward kernels are not built yet")
+
+
 def fused_generator_dynamic_cat(x, y, weight, bias, kernel_size, dilations):
-    """Fused 1x1 generator + dynamic filter (reference ``_triton_kernels.py:1056``)."""
-    raise NotImplementedError("fused generator kernels are not built in this version")
+    """Fused 1x1 generator + dynamic filter (reference ``_triton_kernels.py:1056-1065``).
+
+    Differentiable w.r.t. x, y, weight and bias; without gradients it is a
+    single launch (plus a cached weight packing).
+    """
+    if torch.is_grad_enabled() and any(t.requires_grad for t in (x, y, weight, bias)):
+        return _GeneratorDynamicCat.apply(x, y, weight, bias, kernel_size, dilations)
+    x, y, bias = _prepare(x, y, weight, bias, kernel_size)
+    with torch.cuda.device(x.device):
+        capturing = torch.cuda.is_current_stream_capturing()
+        packed = pack_generator_weight(weight, x.shape[1], kernel_size, use_cache=not capturing)
+        return _launch_gencat_fwd(x, y, packed, bias, kernel_size, dilations)
 
 
 __all__ = ["fused_dynamic_cat", "fused_generator_dynamic_cat"]

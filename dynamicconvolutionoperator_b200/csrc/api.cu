@@ -31,6 +31,16 @@ int dyncat_fwd(const void* x, int xdt, const void* k, int kdt, void* out, int n,
 int dyncat_bwd(const void* x, int xdt, const void* k, const void* g, int kdt, void* gx, void* gk,
                int n, int c, int h, int w, int ks, int d0, int d1, int d2, cudaStream_t st);
 
+int umma_selftest(int variant, const void* a, const void* b, float* d, int n, int k, int shift,
+                  cudaStream_t st);
+
+size_t gencat_pack_bytes(int c, int ks, int dt);
+int gencat_pack(const void* w, int c, int ks, int dt, void* packed, size_t packed_bytes,
+                cudaStream_t st);
+int gencat_fwd(const void* x, const void* y, const void* wpack, const void* bias, void* out,
+               int n, int c, int h, int w, int ks, int d0, int d1, int d2, int dt,
+               cudaStream_t st);
+
 }  // namespace ddpm
 
 extern "C" {
@@ -56,6 +66,31 @@ int ddpm_dyncat_bwd(const void* x, int x_dtype, const void* kernels, const void*
   ddpm::clear_error();
   return ddpm::dyncat_bwd(x, x_dtype, kernels, grad_out, k_dtype, grad_x, grad_k, n, c, h, w,
                           ksize, d0, d1, d2, static_cast<cudaStream_t>(stream));
+}
+
+int ddpm_umma_selftest(int variant, const void* a, const void* b, float* d, int n, int k,
+                       int shift, void* stream) {
+  ddpm::clear_error();
+  return ddpm::umma_selftest(variant, a, b, d, n, k, shift, static_cast<cudaStream_t>(stream));
+}
+
+size_t ddpm_gencat_pack_bytes(int c, int ksize, int dtype) {
+  return ddpm::gencat_pack_bytes(c, ksize, dtype);
+}
+
+int ddpm_gencat_pack(const void* weight, int c, int ksize, int dtype, void* packed,
+                     size_t packed_bytes, void* stream) {
+  ddpm::clear_error();
+  return ddpm::gencat_pack(weight, c, ksize, dtype, packed, packed_bytes,
+                           static_cast<cudaStream_t>(stream));
+}
+
+int ddpm_gencat_fwd(const void* x, const void* y, const void* packed, const void* bias, void* out,
+                    int n, int c, int h, int w, int ksize, int d0, int d1, int d2, int dtype,
+                    void* stream) {
+  ddpm::clear_error();
+  return ddpm::gencat_fwd(x, y, packed, bias, out, n, c, h, w, ksize, d0, d1, d2, dtype,
+                          static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -92,6 +92,46 @@ DDPM_API int ddpm_dyncat_bwd(const void* x, int x_dtype,
                     int ksize, int d0, int d1, int d2,
                     void* stream);
 
+/*
+ * Fused generator + dynamic filter: weight packing.
+ * The fused kernels read the generator weight W [3*C*K*K, C] (the Conv2d
+ * weight of reference `triton_impl.py:293`, row (b*C + c)*K*K + tap) from a
+ * packed copy in the exact shared-memory operand layout of the tensor-core
+ * MMAs (fp32 weights are split into bf16 hi + lo parts). Callers pack once per
+ * weight version into a buffer of ddpm_gencat_pack_bytes() bytes (16-byte
+ * aligned) and pass it to every fused launch that uses that weight.
+ * Limits of this build: C <= 64, K in {1, 3}; other sizes return
+ * DDPM_ERR_UNSUPPORTED (callers then take the materialised path).
+ */
+DDPM_API size_t ddpm_gencat_pack_bytes(int c, int ksize, int dtype);
+DDPM_API int ddpm_gencat_pack(const void* weight, int c, int ksize, int dtype,
+                              void* packed, size_t packed_bytes, void* stream);
+
+/*
+ * Fused generator + dynamic filter, forward (inference and training forward).
+ * Replaces `_launch_generator_dynamic_cat` + `_generator_dynamic_cat_fwd`
+ * (reference `_triton_kernels.py:873-908`, `:268-420`):
+ *   gen = W * y + bias (tensor cores, FP32 accumulation), rounded to `dtype`
+ *   for bf16/fp16 as the reference does (`:332-335`), then
+ *   out = cat(x, sum_tap gen * shifted x for dilations d0, d1, d2).
+ * x, y, bias, out share `dtype`; the taps never reach global memory.
+ */
+DDPM_API int ddpm_gencat_fwd(const void* x, const void* y, const void* packed,
+                             const void* bias, void* out,
+                             int n, int c, int h, int w,
+                             int ksize, int d0, int d1, int d2, int dtype,
+                             void* stream);
+
+/*
+ * Diagnostic (no reference counterpart): one 128 x n x k bf16 tcgen05 UMMA
+ * on a single CTA with the operand layouts the fused kernels use.
+ * a: [128 + shift, k] row-major bf16, b: [n, k] row-major bf16,
+ * d: [128, n] row-major fp32, d[m, j] = sum_i a[shift + m, i] * b[j, i].
+ * variant 0: K-major A; 1: MN-major A; 2: K-major A read from row `shift`.
+ */
+DDPM_API int ddpm_umma_selftest(int variant, const void* a, const void* b, float* d,
+                                int n, int k, int shift, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

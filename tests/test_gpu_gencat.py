@@ -1,0 +1,85 @@
+"""Fused generator + dynamic filter (ddpm_gencat_*) against the oracle.
+
+The oracle restates the reference's fused semantics (``_triton_kernels.py:
+268-420``): taps = W*y + b accumulated in FP32, rounded to the I/O dtype for
+bf16/fp16 (``:332-335``), then multiplied with shifted x. Shapes cover the
+reference's regression set (C=24 -> channel padding, 15x17 borders, tiles that
+straddle the image edge), a 1x1 image, C=3, and the 128x128 C=64 config.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from oracle import ddpm_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(2, 24, 15, 17), (1, 3, 5, 7), (1, 4, 1, 1), (2, 16, 9, 40), (1, 64, 48, 48),
+          (1, 64, 128, 128), (3, 40, 33, 30)]
+# Error budget: fp32 operands carried as bf16 hi+lo pairs (~1e-5 relative per
+# product); bf16/fp16 taps may round one ulp apart where the FP32 sum lands
+# near a rounding boundary, plus the output rounding.
+TOL = {torch.float32: (1e-4, 1e-4), torch.bfloat16: (1e-2, 3e-2), torch.float16: (2e-3, 4e-3)}
+
+
+def _case(shape, ks, dtype, seed=0):
+    n, c, h, w = shape
+    gen = torch.Generator().manual_seed(seed)
+    x = torch.randn(shape, generator=gen).to(dtype)
+    y = torch.randn(shape, generator=gen).to(dtype)
+    bound = 1.0 / c**0.5
+    wt = ((torch.rand((3 * c * ks * ks, c, 1, 1), generator=gen) * 2 - 1) * bound).to(dtype)
+    b = ((torch.rand(3 * c * ks * ks, generator=gen) * 2 - 1) * bound).to(dtype)
+    return x, y, wt, b
+
+
+@pytest.mark.parametrize("shape", SHAPES)
+@pytest.mark.parametrize("ks", [1, 3])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_gencat_forward(shape, ks, dtype):
+    from dynamicconvolutionoperator_b200 import fused_generator_dynamic_cat
+
+    x, y, wt, b = _case(shape, ks, dtype)
+    with torch.no_grad():
+        out = fused_generator_dynamic_cat(x.cuda(), y.cuda(), wt.cuda(), b.cuda(), ks, (1, 3, 5))
+    torch.cuda.synchronize()
+    gold = orc.fused_generator_cat(x, y, wt, b, ks, quantize=True)
+    rtol, atol = TOL[dtype]
+    c = shape[1]
+    torch.testing.assert_close(out[:, :c].cpu(), x, rtol=0, atol=0)
+    torch.testing.assert_close(out.float().cpu(), gold.float(), rtol=rtol, atol=atol)
+
+
+def test_gencat_custom_dilations_and_repeat_calls():
+    """Custom dilations; repeated calls reuse the cached packed weight and an
+    in-place weight update invalidates it."""
+    from dynamicconvolutionoperator_b200 import fused_generator_dynamic_cat
+
+    x, y, wt, b = _case((2, 32, 20, 24), 3, torch.float32, seed=3)
+    xd, yd, wd, bd = x.cuda(), y.cuda(), wt.cuda(), b.cuda()
+    dil = (2, 1, 4)
+    with torch.no_grad():
+        o1 = fused_generator_dynamic_cat(xd, yd, wd, bd, 3, dil)
+        o2 = fused_generator_dynamic_cat(xd, yd, wd, bd, 3, dil)
+        wd.mul_(0.5)
+        o3 = fused_generator_dynamic_cat(xd, yd, wd, bd, 3, dil)
+    torch.testing.assert_close(o1, o2, rtol=0, atol=0)
+    gold1 = orc.fused_generator_cat(x, y, wt, b, 3, dil)
+    gold3 = orc.fused_generator_cat(x, y, wt * 0.5, b, 3, dil)
+    torch.testing.assert_close(o1.cpu(), gold1, rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(o3.cpu(), gold3, rtol=1e-4, atol=1e-4)
+
+
+def test_gencat_multiple_tiles_per_cta():
+    """More tiles than SMs: every persistent CTA loops over several tiles and
+    the TMEM / weight rings wrap many times."""
+    from dynamicconvolutionoperator_b200 import fused_generator_dynamic_cat
+
+    x, y, wt, b = _case((4, 64, 96, 128), 3, torch.bfloat16, seed=9)
+    with torch.no_grad():
+        out = fused_generator_dynamic_cat(x.cuda(), y.cuda(), wt.cuda(), b.cuda(), 3, (1, 3, 5))
+    gold = orc.fused_generator_cat(x, y, wt, b, 3, quantize=True)
+    rtol, atol = TOL[torch.bfloat16]
+    torch.testing.assert_close(out.float().cpu(), gold.float(), rtol=rtol, atol=atol)
