@@ -146,6 +146,10 @@ def make_inputs(batch, dtype, rank):
 
 
 def step_fn(model, x, y, g, allreduce):
+    # x and y take part in autograd (dX and dY are computed), as in the
+    # reference's training benchmarks (gpu_bench.py:275-300).
+    x = x.detach().requires_grad_(True)
+    y = y.detach().requires_grad_(True)
     out = model(x, y)
     loss = (out.float() * g.float()).sum()
     loss.backward()
@@ -312,10 +316,28 @@ def library_kernels(model, x, y, dtype, device):
 
     gen_w = model.generator.weight.detach()
     gen_b = model.generator.bias.detach()
-    packed = _kernels.pack_generator_weight(gen_w, C, K, use_cache=False)
+    packed = _kernels.pack_generator_weight(gen_w, gen_b, C, K, use_cache=False)
     out2 = torch.empty_like(out)
-    keep = (taps, out, gout, gx, gk, packed, out2)
+    gy = torch.empty_like(y)
+    gw = torch.empty((3 * C * K * K, C), dtype=dtype, device=device)
+    gb = torch.empty(3 * C * K * K, dtype=dtype, device=device)
+    ws_bytes = int(_lib.load().ddpm_gencat_bwd_workspace_bytes(n, C, H, W, K))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
+    gen_flops = 2 * (3 * C * K * K) * C * n * H * W
+    keep = (taps, out, gout, gx, gk, packed, out2, gy, gw, gb, ws)
     return keep, {
+        "gencat_bwd_x": (
+            lambda: _lib.call("ddpm_gencat_bwd_x", y.data_ptr(), packed.data_ptr(),
+                              gen_b.data_ptr(), gout.data_ptr(), gx.data_ptr(), n, C, H, W, K,
+                              *DILATIONS, code, sh),
+            "tensor", gen_flops,
+        ),
+        "gencat_bwd_yw": (
+            lambda: _lib.call("ddpm_gencat_bwd_yw", x.data_ptr(), y.data_ptr(), packed.data_ptr(),
+                              gout.data_ptr(), gy.data_ptr(), gw.data_ptr(), gb.data_ptr(),
+                              ws.data_ptr(), ws_bytes, n, C, H, W, K, *DILATIONS, code, sh),
+            "tensor", 2 * gen_flops,
+        ),
         "gencat_fwd": (
             lambda: _lib.call("ddpm_gencat_fwd", x.data_ptr(), y.data_ptr(), packed.data_ptr(),
                               gen_b.data_ptr(), out2.data_ptr(), n, C, H, W, K, *DILATIONS,

@@ -101,15 +101,20 @@ def fused_dynamic_cat(x, kernels, kernel_size, dilations):
 FUSED_MAX_CHANNELS = 64
 FUSED_KERNEL_SIZES = (1, 3)
 # The flash-style recompute backward kernels.
-FUSED_BACKWARD_AVAILABLE = False
+FUSED_BACKWARD_AVAILABLE = True
 
 
-def fused_generator_supported(channels: int, kernel_size: int, dtype: torch.dtype) -> bool:
+FUSED_MAX_HALO = 8
+
+
+def fused_generator_supported(channels: int, kernel_size: int, dtype: torch.dtype,
+                              dilations=(1, 3, 5)) -> bool:
     """Whether the fused generator+filter kernels cover this configuration."""
     return (
         channels <= FUSED_MAX_CHANNELS
         and kernel_size in FUSED_KERNEL_SIZES
         and dtype in _lib.DTYPE_CODE
+        and (kernel_size // 2) * max(dilations) <= FUSED_MAX_HALO
     )
 
 
@@ -132,30 +137,35 @@ def auto_fuse_training(tokens: int, channels: int, kernel_size: int, dtype: torc
 _pack_cache: dict[tuple, tuple] = {}
 
 
-def pack_generator_weight(weight: torch.Tensor, channels: int, kernel_size: int,
-                          use_cache: bool) -> torch.Tensor:
-    """Packed copy of the generator weight in the fused kernels' operand layout.
+def pack_generator_weight(weight: torch.Tensor, bias: torch.Tensor, channels: int,
+                          kernel_size: int, use_cache: bool) -> torch.Tensor:
+    """Packed copy of the generator weight and bias in the fused kernels'
+    operand layout (all three images: forward, dX and dY).
 
-    With ``use_cache`` the packed copy is reused while ``weight`` (same tensor
-    object, same in-place version counter) is unchanged; autograd and CUDA-graph
-    paths pack on every call so a captured step repacks updated weights.
+    With ``use_cache`` the packed copy is reused while ``weight`` and ``bias``
+    (same tensor objects, same in-place version counters) are unchanged;
+    autograd and CUDA-graph paths pack on every call so a captured step repacks
+    updated weights.
     """
     w2 = weight.reshape(weight.shape[0], -1).contiguous()
-    key = (weight.data_ptr(), weight.device, weight.dtype, channels, kernel_size)
+    b1 = bias.contiguous()
+    key = (weight.data_ptr(), bias.data_ptr(), weight.device, weight.dtype, channels, kernel_size)
     if use_cache:
         hit = _pack_cache.get(key)
-        if hit is not None and hit[0]() is weight and hit[1] == weight._version:
-            return hit[2]
+        if (hit is not None and hit[0]() is weight and hit[1]() is bias
+                and hit[2] == (weight._version, bias._version)):
+            return hit[3]
     code = _lib.dtype_code(weight.dtype)
     nbytes = int(_lib.load().ddpm_gencat_pack_bytes(channels, kernel_size, code))
     packed = torch.empty(nbytes, dtype=torch.uint8, device=weight.device)
-    _lib.call("ddpm_gencat_pack", w2.data_ptr(), channels, kernel_size, code,
+    _lib.call("ddpm_gencat_pack", w2.data_ptr(), b1.data_ptr(), channels, kernel_size, code,
               packed.data_ptr(), nbytes, _lib.stream_handle(weight.device))
     if use_cache:
         import weakref
 
         _pack_cache.clear()  # one live entry per process is plenty (one DDPM layer)
-        _pack_cache[key] = (weakref.ref(weight), weight._version, packed)
+        _pack_cache[key] = (weakref.ref(weight), weakref.ref(bias),
+                            (weight._version, bias._version), packed)
     return packed
 
 
@@ -172,7 +182,7 @@ def _launch_gencat_fwd(x, y, packed, bias, kernel_size, dilations):
     return out
 
 
-def _prepare(x, y, weight, bias, kernel_size):
+def _prepare(x, y, weight, bias, kernel_size, dilations):
     x, y = x.contiguous(), y.contiguous()
     bias = bias.contiguous()
     _require_cuda(x, y, weight, bias)
@@ -181,10 +191,11 @@ def _prepare(x, y, weight, bias, kernel_size):
         raise RuntimeError("fused generator path needs x, y, weight and bias of one dtype")
     if weight.shape[0] != 3 * c * kernel_size**2 or weight.numel() != weight.shape[0] * c:
         raise ValueError(f"generator weight must be [3*C*K^2, C(,1,1)], got {tuple(weight.shape)}")
-    if not fused_generator_supported(c, kernel_size, x.dtype):
+    if not fused_generator_supported(c, kernel_size, x.dtype, _dil(dilations)):
         raise RuntimeError(
-            f"fused generator kernels support C <= {FUSED_MAX_CHANNELS} and K in "
-            f"{FUSED_KERNEL_SIZES}; got C={c}, K={kernel_size}"
+            f"fused generator kernels support C <= {FUSED_MAX_CHANNELS}, K in "
+            f"{FUSED_KERNEL_SIZES} and a dilation halo <= {FUSED_MAX_HALO}; got C={c}, "
+            f"K={kernel_size}, dilations={tuple(dilations)}"
         )
     return x, y, bias
 
@@ -195,9 +206,9 @@ class _GeneratorDynamicCat(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, x, y, weight, bias, kernel_size, dilations):
-        x, y, bias = _prepare(x, y, weight, bias, kernel_size)
+        x, y, bias = _prepare(x, y, weight, bias, kernel_size, dilations)
         with torch.cuda.device(x.device):
-            packed = pack_generator_weight(weight, x.shape[1], kernel_size, use_cache=False)
+            packed = pack_generator_weight(weight, bias, x.shape[1], kernel_size, use_cache=False)
             out = _launch_gencat_fwd(x, y, packed, bias, kernel_size, dilations)
         ctx.save_for_backward(x, y, weight, bias)
         ctx.packed = packed
@@ -207,7 +218,41 @@ class _GeneratorDynamicCat(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_out):
-        raise NotImplementedError("fused generator backward kernels are not built yet")
+        x, y, weight, bias = ctx.saved_tensors
+        packed = ctx.packed
+        grad_out = grad_out.to(x.dtype).contiguous()
+        n, c, h, w = x.shape
+        ks = ctx.kernel_size
+        d0, d1, d2 = ctx.dilations
+        code = _lib.dtype_code(x.dtype)
+        need_x, need_y, need_w, need_b = ctx.needs_input_grad[:4]
+        grad_x = torch.empty_like(x) if need_x else None
+        grad_y = torch.empty_like(y) if need_y else None
+        grad_w = grad_b = None
+        if need_w or need_b:
+            grad_w = torch.empty((3 * c * ks * ks, c), dtype=x.dtype, device=x.device)
+            grad_b = torch.empty(3 * c * ks * ks, dtype=x.dtype, device=x.device)
+        with torch.cuda.device(x.device):
+            stream = _lib.stream_handle(x.device)
+            if need_x:
+                _lib.call("ddpm_gencat_bwd_x", y.data_ptr(), packed.data_ptr(), bias.data_ptr(),
+                          grad_out.data_ptr(), grad_x.data_ptr(), n, c, h, w, ks, d0, d1, d2,
+                          code, stream)
+            if need_y or grad_w is not None:
+                ws = None
+                ws_bytes = 0
+                if grad_w is not None:
+                    ws_bytes = int(_lib.load().ddpm_gencat_bwd_workspace_bytes(n, c, h, w, ks))
+                    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
+                _lib.call("ddpm_gencat_bwd_yw", x.data_ptr(), y.data_ptr(), packed.data_ptr(),
+                          grad_out.data_ptr(), grad_y.data_ptr() if need_y else None,
+                          grad_w.data_ptr() if grad_w is not None else None,
+                          grad_b.data_ptr() if grad_b is not None else None,
+                          ws.data_ptr() if ws is not None else None, ws_bytes,
+                          n, c, h, w, ks, d0, d1, d2, code, stream)
+        gw = grad_w.view_as(weight) if (grad_w is not None and need_w) else None
+        gb = grad_b if need_b else None
+        return grad_x, grad_y, gw, gb, None, None
 
 
 def fused_generator_dynamic_cat(x, y, weight, bias, kernel_size, dilations):
@@ -218,10 +263,11 @@ def fused_generator_dynamic_cat(x, y, weight, bias, kernel_size, dilations):
     """
     if torch.is_grad_enabled() and any(t.requires_grad for t in (x, y, weight, bias)):
         return _GeneratorDynamicCat.apply(x, y, weight, bias, kernel_size, dilations)
-    x, y, bias = _prepare(x, y, weight, bias, kernel_size)
+    x, y, bias = _prepare(x, y, weight, bias, kernel_size, dilations)
     with torch.cuda.device(x.device):
         capturing = torch.cuda.is_current_stream_capturing()
-        packed = pack_generator_weight(weight, x.shape[1], kernel_size, use_cache=not capturing)
+        packed = pack_generator_weight(weight, bias, x.shape[1], kernel_size,
+                                       use_cache=not capturing)
         return _launch_gencat_fwd(x, y, packed, bias, kernel_size, dilations)
 
 

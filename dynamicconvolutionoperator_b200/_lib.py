@@ -39,10 +39,21 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         + [_c_ptr],
     ),
     "ddpm_gencat_pack_bytes": (_c_size, [_c_int, _c_int, _c_int]),
-    "ddpm_gencat_pack": (_c_int, [_c_ptr, _c_int, _c_int, _c_int, _c_ptr, _c_size, _c_ptr]),
+    "ddpm_gencat_pack": (
+        _c_int, [_c_ptr, _c_ptr, _c_int, _c_int, _c_int, _c_ptr, _c_size, _c_ptr]
+    ),
     "ddpm_gencat_fwd": (
         _c_int,
         [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr] + [_c_int] * 4 + [_c_int] * 5 + [_c_ptr],
+    ),
+    "ddpm_gencat_bwd_x": (
+        _c_int,
+        [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr] + [_c_int] * 4 + [_c_int] * 5 + [_c_ptr],
+    ),
+    "ddpm_gencat_bwd_workspace_bytes": (_c_size, [_c_int] * 5),
+    "ddpm_gencat_bwd_yw": (
+        _c_int,
+        [_c_ptr] * 8 + [_c_size] + [_c_int] * 4 + [_c_int] * 5 + [_c_ptr],
     ),
     "ddpm_umma_selftest": (
         _c_int, [_c_int, _c_ptr, _c_ptr, _c_ptr, _c_int, _c_int, _c_int, _c_ptr]

@@ -35,11 +35,20 @@ int umma_selftest(int variant, const void* a, const void* b, float* d, int n, in
                   cudaStream_t st);
 
 size_t gencat_pack_bytes(int c, int ks, int dt);
-int gencat_pack(const void* w, int c, int ks, int dt, void* packed, size_t packed_bytes,
-                cudaStream_t st);
+int gencat_pack(const void* w, const void* bias, int c, int ks, int dt, void* packed,
+                size_t packed_bytes, cudaStream_t st);
 int gencat_fwd(const void* x, const void* y, const void* wpack, const void* bias, void* out,
                int n, int c, int h, int w, int ks, int d0, int d1, int d2, int dt,
                cudaStream_t st);
+
+int gencat_bwd_x(const void* y, const void* wpack, const void* bias, const void* gout, void* gx,
+                 int n, int c, int h, int w, int ks, int d0, int d1, int d2, int dt,
+                 cudaStream_t st);
+
+size_t gencat_bwd_workspace_bytes(int n, int c, int h, int w, int ks);
+int gencat_bwd_yw(const void* x, const void* y, const void* wpack, const void* gout, void* gy,
+                  void* gw, void* gb, void* workspace, size_t ws_bytes, int n, int c, int h, int w,
+                  int ks, int d0, int d1, int d2, int dt, cudaStream_t st);
 
 }  // namespace ddpm
 
@@ -78,10 +87,10 @@ size_t ddpm_gencat_pack_bytes(int c, int ksize, int dtype) {
   return ddpm::gencat_pack_bytes(c, ksize, dtype);
 }
 
-int ddpm_gencat_pack(const void* weight, int c, int ksize, int dtype, void* packed,
-                     size_t packed_bytes, void* stream) {
+int ddpm_gencat_pack(const void* weight, const void* bias, int c, int ksize, int dtype,
+                     void* packed, size_t packed_bytes, void* stream) {
   ddpm::clear_error();
-  return ddpm::gencat_pack(weight, c, ksize, dtype, packed, packed_bytes,
+  return ddpm::gencat_pack(weight, bias, c, ksize, dtype, packed, packed_bytes,
                            static_cast<cudaStream_t>(stream));
 }
 
@@ -91,6 +100,28 @@ int ddpm_gencat_fwd(const void* x, const void* y, const void* packed, const void
   ddpm::clear_error();
   return ddpm::gencat_fwd(x, y, packed, bias, out, n, c, h, w, ksize, d0, d1, d2, dtype,
                           static_cast<cudaStream_t>(stream));
+}
+
+int ddpm_gencat_bwd_x(const void* y, const void* packed, const void* bias, const void* grad_out,
+                      void* grad_x, int n, int c, int h, int w, int ksize, int d0, int d1, int d2,
+                      int dtype, void* stream) {
+  ddpm::clear_error();
+  return ddpm::gencat_bwd_x(y, packed, bias, grad_out, grad_x, n, c, h, w, ksize, d0, d1, d2,
+                            dtype, static_cast<cudaStream_t>(stream));
+}
+
+size_t ddpm_gencat_bwd_workspace_bytes(int n, int c, int h, int w, int ksize) {
+  return ddpm::gencat_bwd_workspace_bytes(n, c, h, w, ksize);
+}
+
+int ddpm_gencat_bwd_yw(const void* x, const void* y, const void* packed, const void* grad_out,
+                       void* grad_y, void* grad_weight, void* grad_bias, void* workspace,
+                       size_t workspace_bytes, int n, int c, int h, int w, int ksize, int d0,
+                       int d1, int d2, int dtype, void* stream) {
+  ddpm::clear_error();
+  return ddpm::gencat_bwd_yw(x, y, packed, grad_out, grad_y, grad_weight, grad_bias, workspace,
+                             workspace_bytes, n, c, h, w, ksize, d0, d1, d2, dtype,
+                             static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -2,6 +2,8 @@
 // I/O traits, tile geometry, operand staging helpers, bounded-wait helpers.
 #pragma once
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "tc.cuh"
 
@@ -13,6 +15,11 @@ constexpr int kTileM = 128;
 constexpr int kTileH = 8;
 constexpr int kTileW = 16;
 constexpr int kMaxChannels = 64;
+// Width (pixels) of the staged x halo tile: the 16 tile columns plus 8 on each
+// side, so dilation halos up to 8 pixels are covered and 8-pixel loads stay
+// aligned with the tile origin.
+constexpr int kHaloCols = 32;
+constexpr int kMaxHalo = 8;
 // Upper bound for any single mbarrier wait before the kernel gives up, records
 // an error and unwinds (no legitimate wait in these kernels lasts this long).
 constexpr uint64_t kWaitNs = 2000000000ull;
@@ -46,6 +53,48 @@ template <> struct IoTraits<float> {
 };
 
 inline int padded_channels(int c) { return (c + 15) / 16 * 16; }
+// GEMM K extent of the generator: C input channels + one constant-one channel
+// carrying the bias, padded to the MMA K step of 16.
+inline int augmented_channels(int c) { return (c + 1 + 15) / 16 * 16; }
+
+// Layout of the packed generator weight (three operand images back to back).
+//   fwd : chunks q = (cg*3 + b)*K + ki, each [part][Ck/8][16*K rows][8];
+//         row kj*16 + cl <-> weight row (b*C + cg*16 + cl)*K^2 + ki*K + kj,
+//         K dimension = augmented input channels (bias at index C).
+//   bx  : chunks q = b*K^2 + tap, each [part][Ck/8][Cp rows (c)][8].
+//   by  : groups g = (cg16, slot octet) of 128 weight rows, row j*16 + cl <->
+//         slot s = octet*8 + j = b*K^2 + tap, channel cg16*16 + cl; each group
+//         [part][16 row groups][Cp (input channel i)][8 rows]: the transposed
+//         weight, K dimension = weight rows.
+// All sizes in 16-byte rows; `parts` = 2 for fp32 (bf16 hi + lo images).
+struct PackLayout {
+  int C, KS, Cp, Ck, Cq, spg, NG, parts;
+  int bias_col;  // K index carrying the bias (bf16/fp16), -1 if the bias is added later
+  long long fwd_rows, bx_rows, by_rows;
+  __host__ __device__ size_t bx_offset() const { return (size_t)fwd_rows * 16; }
+  __host__ __device__ size_t by_offset() const { return (size_t)(fwd_rows + bx_rows) * 16; }
+  __host__ __device__ size_t total_bytes() const {
+    return (size_t)(fwd_rows + bx_rows + by_rows) * 16;
+  }
+  static PackLayout make(int c, int ks, int dt) {
+    PackLayout L;
+    L.C = c;
+    L.KS = ks;
+    L.Cp = padded_channels(c);
+    L.parts = dt == DDPM_F32 ? 2 : 1;
+    // fp32 keeps K = Cp (shared memory budget) and adds the bias in the epilogue
+    L.Ck = dt == DDPM_F32 ? L.Cp : augmented_channels(c);
+    L.bias_col = dt == DDPM_F32 ? -1 : c;
+    // dY / dW groups: 8 (branch, tap) slots x 16 channels = 128 weight rows
+    L.Cq = 16;
+    L.spg = 8;
+    L.NG = (L.Cp / 16) * ((3 * ks * ks + 7) / 8);
+    L.fwd_rows = (long long)(L.Cp / 16) * 3 * ks * L.parts * (L.Ck / 8) * 16 * ks;
+    L.bx_rows = (long long)3 * ks * ks * L.parts * (L.Ck / 8) * L.Cp;
+    L.by_rows = (long long)L.NG * L.parts * 16 * L.Cp;
+    return L;
+  }
+};
 
 __device__ __forceinline__ void tile_origin(int tile, int tiles_w, int tiles_h, int& n, int& h0,
                                             int& w0) {
@@ -69,39 +118,37 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity,
   return __all_sync(0xffffffffu, ok);
 }
 
-// Load 8 consecutive pixels y[n, c, h, w0 .. w0+7] as floats, zero outside
-// the image / channel range. Vector path when the run is in range and 16-byte
-// aligned.
+// Load plane[h, w0 .. w0+7] (row-major H x W plane) as floats, zero outside
+// the plane. Vector path when the whole run is inside and 16-byte aligned.
 template <typename T>
-__device__ __forceinline__ void load8(const T* __restrict__ base, int n, int c, int C, int H,
-                                      int W, int h, int w0, float (&v)[8]) {
-  if (c >= C || h >= H || w0 >= W) {
+__device__ __forceinline__ void load8(const T* __restrict__ plane, int H, int W, int h, int w0,
+                                      float (&v)[8]) {
+  if (h < 0 || h >= H || w0 >= W || w0 + 8 <= 0) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[i] = 0.f;
     return;
   }
-  const T* src = base + ((size_t)(n * C + c) * H + h) * W + w0;
-  const bool full = (w0 + 8 <= W) &&
-                    ((reinterpret_cast<uintptr_t>(src) & 15u) == 0);
-  if constexpr (sizeof(T) == 2) {
-    if (full) {
+  const T* src = plane + (ptrdiff_t)h * W + w0;
+  const bool full = (w0 >= 0) && (w0 + 8 <= W) && ((reinterpret_cast<uintptr_t>(src) & 15u) == 0);
+  if (full) {
+    if constexpr (sizeof(T) == 2) {
       const uint4 u = __ldg(reinterpret_cast<const uint4*>(src));
       const T* e = reinterpret_cast<const T*>(&u);
 #pragma unroll
       for (int i = 0; i < 8; ++i) v[i] = to_f32<T>(e[i]);
-      return;
-    }
-  } else {
-    if (full) {
+    } else {
       const float4 a = __ldg(reinterpret_cast<const float4*>(src));
       const float4 b = __ldg(reinterpret_cast<const float4*>(src) + 1);
       v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
       v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-      return;
     }
+    return;
   }
 #pragma unroll
-  for (int i = 0; i < 8; ++i) v[i] = (w0 + i < W) ? to_f32<T>(__ldg(src + i)) : 0.f;
+  for (int i = 0; i < 8; ++i) {
+    const int w = w0 + i;
+    v[i] = (w >= 0 && w < W) ? to_f32<T>(__ldg(src + i)) : 0.f;
+  }
 }
 
 template <typename Op> __device__ __forceinline__ Op op_from(float v);
@@ -133,6 +180,163 @@ __device__ __forceinline__ void store8_split(uint8_t* dst_hi, uint8_t* dst_lo,
 #pragma unroll
     for (int i = 0; i < 8; ++i) lo.e[i] = op_from<Op>(v[i] - op_to<Op>(hi.e[i]));
     *reinterpret_cast<uint4*>(dst_lo) = lo.u;
+  }
+}
+
+// Eight consecutive elements of a row, kept in their storage format until
+// they are written to shared memory (no float round trip for 16-bit data).
+template <typename T> struct Raw8 {
+  uint4 u;  // 8 x 16-bit
+  __device__ __forceinline__ void zero() { u = make_uint4(0u, 0u, 0u, 0u); }
+  __device__ __forceinline__ float get(int i) const {
+    return to_f32<T>(reinterpret_cast<const T*>(&u)[i]);
+  }
+};
+template <> struct Raw8<float> {
+  float4 a, b;
+  __device__ __forceinline__ void zero() { a = b = make_float4(0.f, 0.f, 0.f, 0.f); }
+  __device__ __forceinline__ float get(int i) const {
+    const float e[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    return e[i];
+  }
+};
+
+// plane[h, w0 .. w0+7] of a row-major H x W plane, zero outside the plane.
+template <typename T>
+__device__ __forceinline__ Raw8<T> load_raw8(const T* __restrict__ plane, int H, int W, int h,
+                                             int w0) {
+  Raw8<T> r;
+  r.zero();
+  if (h < 0 || h >= H || w0 >= W || w0 + 8 <= 0) return r;
+  const T* src = plane + (ptrdiff_t)h * W + w0;
+  if (w0 >= 0 && w0 + 8 <= W && (reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
+    if constexpr (sizeof(T) == 2) {
+      r.u = __ldg(reinterpret_cast<const uint4*>(src));
+    } else {
+      r.a = __ldg(reinterpret_cast<const float4*>(src));
+      r.b = __ldg(reinterpret_cast<const float4*>(src) + 1);
+    }
+    return r;
+  }
+  T* e = reinterpret_cast<T*>(&r);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int w = w0 + i;
+    if (w >= 0 && w < W) e[i] = __ldg(src + i);
+  }
+  return r;
+}
+
+// Write 8 elements as one 16-byte MMA operand row (bf16/fp16 copy through;
+// fp32 split into a bf16 hi row at `hi` and a bf16 residual row at `lo`).
+template <typename T, typename Op, bool kSplit>
+__device__ __forceinline__ void store_raw8(uint8_t* hi, uint8_t* lo, const Raw8<T>& r) {
+  if constexpr (!kSplit) {
+    *reinterpret_cast<uint4*>(hi) = r.u;
+  } else {
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = r.get(i);
+    store8_split<Op, true>(hi, lo, v);
+  }
+}
+
+// Stage the y tile of an 8 x 16 pixel tile as the MN-major MMA operand:
+// 16 eight-pixel groups (row g/2, half g%2) x Ck augmented channels, one
+// 16-byte row per (group, channel) at g*Ck*16 + (c/8)*128 + (c%8)*16.
+// Channel `ones_c` is the constant one (bias; -1 = none), others past C zero.
+// With kSplit, the bf16 residual goes to the same offset in `lo`. Each of the
+// `nthreads` threads issues all of its loads before its first store.
+template <typename T, typename Op, bool kSplit, int kMaxItems>
+__device__ __forceinline__ void stage_y_mn(const T* __restrict__ y, uint8_t* hi, uint8_t* lo, int n,
+                                           int C, int Ck, int ones_c, int H, int W, int h0, int w0,
+                                           int tid, int nthreads) {
+  const int items = 16 * Ck;
+  const size_t P = (size_t)H * W;
+  Raw8<T> v[kMaxItems];
+#pragma unroll
+  for (int u = 0; u < kMaxItems; ++u) {
+    const int item = tid + u * nthreads;
+    const int c = item % Ck;
+    const int g = item / Ck;
+    if (item < items && c < C)
+      v[u] = load_raw8<T>(y + ((size_t)n * C + c) * P, H, W, h0 + (g >> 1), w0 + (g & 1) * 8);
+  }
+#pragma unroll
+  for (int u = 0; u < kMaxItems; ++u) {
+    const int item = tid + u * nthreads;
+    if (item >= items) break;
+    const int c = item % Ck;
+    const int g = item / Ck;
+    const uint32_t off = g * Ck * 16 + (c >> 3) * 128 + (c & 7) * 16;
+    if (c < C) {
+      store_raw8<T, Op, kSplit>(hi + off, lo + off, v[u]);
+    } else {
+      float f[8];
+      const float one = (c == ones_c) ? 1.f : 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) f[i] = one;
+      store8_split<Op, kSplit>(hi + off, lo + off, f);
+    }
+  }
+}
+
+// Stage the x halo of one 16-channel group: rows hs .. hs+rows-1, columns
+// ws .. ws+31 of channels c0 .. c0+15, as FP32 float4 cells holding four
+// consecutive channels: cell (q4, row, col) = xr[(q4*rows + row)*32 + col].
+// Zero outside the image and for channels >= C.
+template <typename T, int kMaxItems>
+__device__ __forceinline__ void stage_halo(const T* __restrict__ x, float4* xr, int n, int C,
+                                           int H, int W, int c0, int hs, int ws, int rows,
+                                           int tid, int nthreads) {
+  const size_t P = (size_t)H * W;
+  const int items = 4 * rows * 4;  // (q4, row, 8-column block)
+  Raw8<T> v[kMaxItems][4];
+#pragma unroll
+  for (int u = 0; u < kMaxItems; ++u) {
+    const int item = tid + u * nthreads;
+    const int blk = item & 3;
+    const int row = (item >> 2) % rows;
+    const int q4 = (item >> 2) / rows;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int c = c0 + q4 * 4 + k;
+      if (item < items && c < C)
+        v[u][k] = load_raw8<T>(x + ((size_t)n * C + c) * P, H, W, hs + row, ws + blk * 8);
+      else
+        v[u][k].zero();
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < kMaxItems; ++u) {
+    const int item = tid + u * nthreads;
+    if (item >= items) break;
+    const int blk = item & 3;
+    const int row = (item >> 2) % rows;
+    const int q4 = (item >> 2) / rows;
+    float4* dst = xr + (q4 * rows + row) * kHaloCols + blk * 8;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      dst[i] = make_float4(v[u][0].get(i), v[u][1].get(i), v[u][2].get(i), v[u][3].get(i));
+  }
+}
+
+// Round generated taps to the I/O precision (bf16 / fp16), as the reference
+// does before using them (`_triton_kernels.py:332-335`); identity for fp32.
+// bf16 uses integer round-to-nearest-even on the bit pattern (full-rate ALU
+// ops instead of conversion instructions); taps are finite by construction.
+template <typename T>
+__device__ __forceinline__ void round_taps(float (&v)[16]) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      uint32_t u = __float_as_uint(v[i]);
+      u = (u + 0x7FFFu + ((u >> 16) & 1u)) & 0xFFFF0000u;
+      v[i] = __uint_as_float(u);
+    }
+  } else if constexpr (sizeof(T) == 2) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = IoTraits<T>::round_io(v[i]);
   }
 }
 

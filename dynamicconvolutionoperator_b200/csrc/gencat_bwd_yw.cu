@@ -1,0 +1,825 @@
+// Fused generator backward: dY, and dW / db, with dK formed on chip.
+// Replaces `_generator_dynamic_cat_bwd_y` (reference `_triton_kernels.py:534-623`),
+// `_generator_dynamic_cat_bwd_weight_partial` (`:626-751`) and
+// `_generator_dynamic_cat_bwd_weight_reduce` (`:754-811`):
+//
+//   dK[(b,c,tap), p] = x[c, p + o] * g_b[c, p]            (never stored to HBM)
+//   dY[i, p]         = sum_{(b,c,tap)} W[(b,c,tap), i] * dK[(b,c,tap), p]
+//   dW[(b,c,tap), i] = sum_p dK[(b,c,tap), p] * y[i, p]
+//   db[(b,c,tap)]    = sum_p dK[(b,c,tap), p]
+//
+// Both GEMMs take dK as their A operand. Weight rows are processed in groups
+// of 128 = 8 (branch, tap) "slots" x 16 channels (one x-halo channel group).
+// A group's dK tile is built in shared memory by CUDA-core builder warps,
+// thread = pixel: for each slot one 16-channel x neighbour (four LDS.128 from
+// the staged FP32 halo, as in the forward) times the 16 g_b values of the
+// pixel, written as two 16-byte rows. The tile layout
+//   (pixel m, row) at (m/8)*2048 + (row/8)*128 + (m%8)*16 + (row%8)*2
+// is at once the K-major operand [pixels x rows] of the dY GEMM and the
+// MN-major operand [rows x pixels] of the dW GEMM (same core matrices).
+//
+// dY kernel: persistent over 8x16 pixel tiles; D_y (128 pixels x Cp) sits in
+// TMEM for the whole tile while the transposed-weight groups (packed "by"
+// image) stream through a ring; builders drain D_y to dY at the end of a tile.
+// dW kernel: grid = (group batch, spatial split); D_w of up to 6 groups
+// (128 rows x Nw each, Nw = round16(C + 1): the y tile carries a constant-one
+// channel at index C so column C of D_w is db) accumulates over all tiles of
+// the split; partials go to a workspace and a short kernel reduces them into
+// the Conv2d weight layout.
+#include "common.cuh"
+#include "tc.cuh"
+#include "gencat.cuh"
+
+namespace ddpm {
+namespace {
+
+using namespace gencat;
+
+constexpr int kDkBytes = kTileM * 128 * 2;  // one dK tile part (bf16 / fp16)
+
+// ----------------------------------------------------------- dK builder -----
+// Slots of octet OCT: s = OCT*8 + j -> (b, tap) = (s / K^2, s % K^2); s >= 3K^2
+// is padding (zero rows). gv[b][cl] = g_b[cg16*16 + cl, p] of this pixel.
+template <typename T, typename Op, bool kSplit, int KS, int OCT>
+__device__ __forceinline__ void build_octet(uint8_t* dk, const float4* xc, int xr_plane,
+                                            const float (&gv)[3][16], const int (&dil)[3], int m) {
+  constexpr int KK = KS * KS;
+  constexpr int r = KS / 2;
+  const uint32_t base = (m >> 3) * 2048 + (m & 7) * 16;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int s = OCT * 8 + j;
+    float prod[16];
+    if (s < 3 * KK) {
+      const int b = s / KK, tap = s % KK;
+      const int dy = (tap / KS - r) * dil[b], dx = (tap % KS - r) * dil[b];
+      const float4* cell = xc + dy * kHaloCols + dx;
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        const float4 v = cell[q4 * xr_plane];
+        prod[q4 * 4 + 0] = v.x * gv[b][q4 * 4 + 0];
+        prod[q4 * 4 + 1] = v.y * gv[b][q4 * 4 + 1];
+        prod[q4 * 4 + 2] = v.z * gv[b][q4 * 4 + 2];
+        prod[q4 * 4 + 3] = v.w * gv[b][q4 * 4 + 3];
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) prod[i] = 0.f;
+    }
+    float lo8[8], hi8[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      lo8[i] = prod[i];
+      hi8[i] = prod[8 + i];
+    }
+    const uint32_t off = base + (j * 2) * 128;
+    store8_split<Op, kSplit>(dk + off, dk + kDkBytes + off, lo8);
+    store8_split<Op, kSplit>(dk + off + 128, dk + kDkBytes + off + 128, hi8);
+  }
+}
+
+template <typename T, typename Op, bool kSplit, int KS>
+__device__ __forceinline__ void build_dk(uint8_t* dk, int octet, const float4* xc, int xr_plane,
+                                         const float (&gv)[3][16], const int (&dil)[3], int m) {
+  switch (octet) {
+    case 0: build_octet<T, Op, kSplit, KS, 0>(dk, xc, xr_plane, gv, dil, m); break;
+    case 1: build_octet<T, Op, kSplit, KS, 1>(dk, xc, xr_plane, gv, dil, m); break;
+    case 2: build_octet<T, Op, kSplit, KS, 2>(dk, xc, xr_plane, gv, dil, m); break;
+    default: build_octet<T, Op, kSplit, KS, 3>(dk, xc, xr_plane, gv, dil, m); break;
+  }
+}
+
+// g_b[cg16*16 + cl, pixel] for the three branches (zero off-image / c >= C).
+template <typename T>
+__device__ __forceinline__ void load_gv(float (&gv)[3][16], const T* gn, int C, size_t P,
+                                        int cg16, size_t pix, bool px_ok) {
+#pragma unroll
+  for (int b = 0; b < 3; ++b)
+#pragma unroll
+    for (int cl = 0; cl < 16; ++cl) {
+      const int c = cg16 * 16 + cl;
+      gv[b][cl] = (px_ok && c < C) ? to_f32<T>(__ldg(gn + (size_t)((b + 1) * C + c) * P + pix))
+                                   : 0.f;
+    }
+}
+
+// =============================================================== dY =========
+template <typename T, int KS>
+struct ByCfg {
+  static constexpr bool kSplit = IoTraits<T>::kSplit;
+  static constexpr int kParts = kSplit ? 2 : 1;
+  static constexpr int kDkSlots = kSplit ? 1 : 2;
+  static constexpr int kWStages = kSplit ? 2 : 3;
+  static constexpr int kProducers = 128;
+  static constexpr int kXItems = (16 * (kTileH + 2 * kMaxHalo) + kProducers - 1) / kProducers;
+  static constexpr int kThreads = 32 * (2 + 4 + 4);
+  static constexpr int kOct = (3 * KS * KS + 7) / 8;
+};
+
+struct BySmem {
+  uint32_t xr, dk, w, bars, total, xr_bytes, dk_bytes, w_bytes;
+};
+
+template <typename T, int KS>
+__host__ __device__ inline BySmem by_smem_layout(int Cp, int R) {
+  using Cfg = ByCfg<T, KS>;
+  BySmem L;
+  L.xr_bytes = (uint32_t)16 * (kTileH + 2 * R) * kHaloCols * 4;
+  L.dk_bytes = (uint32_t)Cfg::kParts * kDkBytes;
+  L.w_bytes = (uint32_t)Cfg::kParts * 128 * Cp * 2;
+  L.xr = 0;
+  L.dk = L.xr + 2 * L.xr_bytes;
+  L.w = L.dk + Cfg::kDkSlots * L.dk_bytes;
+  L.bars = L.w + Cfg::kWStages * L.w_bytes;
+  L.total = L.bars + 8 * (4 + 2 * Cfg::kDkSlots + 2 * Cfg::kWStages + 4);
+  return L;
+}
+
+struct ByParams {
+  const void* x;
+  const void* wpack;  // "by" image
+  const void* gout;
+  void* gy;
+  int N, C, H, W, Cp, R;
+  int d[3];
+  int tiles_w, tiles_h, num_tiles;
+  int* status;
+};
+
+template <typename T, int KS>
+__global__ void __launch_bounds__(ByCfg<T, KS>::kThreads, 1)
+gencat_bwd_y_kernel(const ByParams p) {
+  using Cfg = ByCfg<T, KS>;
+  using Op = typename IoTraits<T>::Op;
+  constexpr int NS = Cfg::kDkSlots;
+  constexpr int S = Cfg::kWStages;
+  constexpr int NOCT = Cfg::kOct;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ uint32_t tmem_base_s;
+  __shared__ int abort_s;
+
+  const int C = p.C, Cp = p.Cp, H = p.H, W = p.W, R = p.R;
+  const size_t P = (size_t)H * W;
+  const BySmem L = by_smem_layout<T, KS>(Cp, R);
+  const int ncg = Cp / 16;
+  const int ngroups = ncg * NOCT;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint64_t* x_full = bars;             // [2]
+  uint64_t* x_empty = bars + 2;        // [2]
+  uint64_t* k_full = bars + 4;         // [NS]
+  uint64_t* k_empty = k_full + NS;     // [NS]
+  uint64_t* w_full = k_empty + NS;     // [S]
+  uint64_t* w_empty = w_full + S;      // [S]
+  uint64_t* d_full = w_empty + S;      // [2]
+  uint64_t* d_empty = d_full + 2;      // [2]
+  const int xr_rows = kTileH + 2 * R;
+  const int xr_plane = xr_rows * kHaloCols;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (warp == 0) {
+    tc::tmem_alloc(&tmem_base_s, 128);
+    tc::tmem_relinquish();
+  }
+  if (threadIdx.x == 32) {
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(&x_full[i], Cfg::kProducers);
+      tc::mbar_init(&x_empty[i], 128);
+      tc::mbar_init(&d_full[i], 1);
+      tc::mbar_init(&d_empty[i], 128);
+    }
+    for (int i = 0; i < NS; ++i) {
+      tc::mbar_init(&k_full[i], 128);
+      tc::mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < S; ++i) {
+      tc::mbar_init(&w_full[i], 1);
+      tc::mbar_init(&w_empty[i], 1);
+    }
+    tc::fence_mbar_init();
+    abort_s = 0;
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem_base = tmem_base_s;
+  volatile int* abort_flag = &abort_s;
+
+  if (warp == 0) {
+    // ---- transposed-weight groups through the ring -------------------------
+    if (lane == 0) {
+      const uint8_t* wsrc = static_cast<const uint8_t*>(p.wpack);
+      uint32_t wq = 0;
+      for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+        for (int g = 0; g < ngroups; ++g, ++wq) {
+          const int s = wq % S;
+          if (!tc::mbar_wait(&w_empty[s], ((wq / S) & 1) ^ 1, abort_flag, kWaitNs)) {
+            fail(abort_flag, p.status, 30);
+            goto done;
+          }
+          tc::mbar_arrive_expect_tx(&w_full[s], L.w_bytes);
+          tc::bulk_g2s(smem + L.w + s * L.w_bytes, wsrc + (size_t)g * L.w_bytes, L.w_bytes,
+                       &w_full[s]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA: D_y[tile] += dK . W^T, over all groups -----------------------
+    if (lane == 0) {
+      const uint32_t idesc = tc::idesc_f16(kTileM, Cp, IoTraits<T>::kBf16, false, false);
+      const uint32_t b_lbo = Cp * 16;
+      const uint32_t wpart = 128 * Cp * 2;
+      uint32_t wq = 0, kq = 0, it = 0;
+      for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
+        const int tb = it & 1;
+        if (!tc::mbar_wait(&d_empty[tb], ((it >> 1) & 1) ^ 1, abort_flag, kWaitNs)) {
+          fail(abort_flag, p.status, 31);
+          goto done;
+        }
+        tc::tc_fence_after();
+        const uint32_t dt = tmem_base + tb * Cp;
+        for (int g = 0; g < ngroups; ++g, ++wq, ++kq) {
+          const int s = wq % S, ks_ = kq % NS;
+          if (!tc::mbar_wait(&k_full[ks_], (kq / NS) & 1, abort_flag, kWaitNs) ||
+              !tc::mbar_wait(&w_full[s], (wq / S) & 1, abort_flag, kWaitNs)) {
+            fail(abort_flag, p.status, 32);
+            goto done;
+          }
+          tc::tc_fence_after();
+          const uint32_t ka = tc::smem_u32(smem + L.dk + ks_ * L.dk_bytes);
+          const uint32_t wb = tc::smem_u32(smem + L.w + s * L.w_bytes);
+          for (int ks = 0; ks < 8; ++ks) {
+            // A: dK, K-major (rows are K): row-group stride 128, pixel-group stride 2048
+            const uint64_t a_hi = tc::smem_desc(ka + ks * 256, 128, 2048);
+            const uint64_t b_hi = tc::smem_desc(wb + ks * 2 * b_lbo, b_lbo, 128);
+            tc::mma_f16(dt, a_hi, b_hi, idesc, (g > 0 || ks > 0) ? 1u : 0u);
+            if constexpr (Cfg::kSplit) {
+              const uint64_t a_lo = tc::smem_desc(ka + kDkBytes + ks * 256, 128, 2048);
+              const uint64_t b_lo = tc::smem_desc(wb + wpart + ks * 2 * b_lbo, b_lbo, 128);
+              tc::mma_f16(dt, a_lo, b_hi, idesc, 1u);
+              tc::mma_f16(dt, a_hi, b_lo, idesc, 1u);
+            }
+          }
+          tc::mma_commit(&k_empty[ks_]);
+          tc::mma_commit(&w_empty[s]);
+        }
+        tc::mma_commit(&d_full[tb]);
+      }
+    }
+  } else if (warp < 6) {
+    // ---- x-halo producers (per tile and 16-channel group) ------------------
+    const int pt = threadIdx.x - 64;
+    uint32_t xq = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x) {
+      int n, h0, w0;
+      tile_origin(tile, p.tiles_w, p.tiles_h, n, h0, w0);
+      for (int cg = 0; cg < ncg; ++cg, ++xq) {
+        const int xb = xq & 1;
+        if (!warp_wait(&x_empty[xb], ((xq >> 1) & 1) ^ 1, abort_flag)) {
+          fail(abort_flag, p.status, 33);
+          break;
+        }
+        float4* xr = reinterpret_cast<float4*>(smem + L.xr + xb * L.xr_bytes);
+        stage_halo<T, Cfg::kXItems>(static_cast<const T*>(p.x), xr, n, C, H, W, cg * 16, h0 - R,
+                                    w0 - 8, xr_rows, pt, Cfg::kProducers);
+        tc::mbar_arrive(&x_full[xb]);
+      }
+    }
+  } else {
+    // ---- builders (thread = pixel = TMEM lane) + D_y drain ----------------
+    const int quad = warp & 3;
+    const int m = quad * 32 + lane;
+    const int mr = m >> 4, mc = m & 15;
+    const T* gout = static_cast<const T*>(p.gout);
+    T* gy = static_cast<T*>(p.gy);
+    const int dil[3] = {p.d[0], p.d[1], p.d[2]};
+    uint32_t xq = 0, kq = 0, it = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
+      int n, h0, w0;
+      tile_origin(tile, p.tiles_w, p.tiles_h, n, h0, w0);
+      const int h = h0 + mr, w = w0 + mc;
+      const bool px_ok = (h < H) && (w < W);
+      const size_t pix = px_ok ? (size_t)h * W + w : 0;
+      const T* gn = gout + (size_t)n * 4 * C * P;
+      bool failed = false;
+      for (int cg = 0; cg < ncg && !failed; ++cg, ++xq) {
+        float gv[3][16];
+        load_gv<T>(gv, gn, C, P, cg, pix, px_ok);
+        const int xb = xq & 1;
+        if (!warp_wait(&x_full[xb], (xq >> 1) & 1, abort_flag)) {
+          fail(abort_flag, p.status, 34);
+          failed = true;
+          break;
+        }
+        const float4* xc = reinterpret_cast<const float4*>(smem + L.xr + xb * L.xr_bytes) +
+                           (mr + R) * kHaloCols + (mc + 8);
+        for (int oct = 0; oct < NOCT; ++oct, ++kq) {
+          const int ks_ = kq % NS;
+          if (!warp_wait(&k_empty[ks_], ((kq / NS) & 1) ^ 1, abort_flag)) {
+            fail(abort_flag, p.status, 35);
+            failed = true;
+            break;
+          }
+          build_dk<T, Op, Cfg::kSplit, KS>(smem + L.dk + ks_ * L.dk_bytes, oct, xc, xr_plane, gv,
+                                           dil, m);
+          tc::fence_proxy_async_smem();
+          tc::mbar_arrive(&k_full[ks_]);
+        }
+        tc::mbar_arrive(&x_empty[xb]);
+      }
+      if (failed) break;
+      // drain D_y of this tile
+      const int tb = it & 1;
+      if (!warp_wait(&d_full[tb], (it >> 1) & 1, abort_flag)) {
+        fail(abort_flag, p.status, 36);
+        break;
+      }
+      tc::tc_fence_after();
+      for (int i0 = 0; i0 < Cp; i0 += 16) {
+        float dv[16];
+        tc::tmem_ld16(tmem_base + ((uint32_t)(quad * 32) << 16) + tb * Cp + i0, dv);
+        tc::tmem_ld_wait();
+        if (px_ok) {
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            const int i = i0 + k;
+            if (i < C) gy[((size_t)n * C + i) * P + pix] = from_f32<T>(dv[k]);
+          }
+        }
+      }
+      tc::tc_fence_before();
+      tc::mbar_arrive(&d_empty[tb]);
+    }
+  }
+done:
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem_base, 128);
+  }
+}
+
+// =============================================================== dW =========
+template <typename T, int KS>
+struct BwCfg {
+  static constexpr bool kSplit = IoTraits<T>::kSplit;
+  static constexpr int kParts = kSplit ? 2 : 1;
+  static constexpr int kDkSlots = kSplit ? 1 : 2;
+  static constexpr int kYBufs = kSplit ? 1 : 2;
+  static constexpr int kProducers = 128;
+  static constexpr int kXItems = (16 * (kTileH + 2 * kMaxHalo) + kProducers - 1) / kProducers;
+  static constexpr int kYItems = (16 * 80 + kProducers - 1) / kProducers;
+  static constexpr int kThreads = 32 * (2 + 4 + 4 + 4);
+  static constexpr int kOct = (3 * KS * KS + 7) / 8;
+};
+
+struct BwSmem {
+  uint32_t xr, y, dk, bars, total, xr_bytes, y_bytes, dk_bytes;
+};
+
+template <typename T, int KS>
+__host__ __device__ inline BwSmem bw_smem_layout(int Nw, int R) {
+  using Cfg = BwCfg<T, KS>;
+  BwSmem L;
+  L.xr_bytes = (uint32_t)16 * (kTileH + 2 * R) * kHaloCols * 4;
+  L.y_bytes = (uint32_t)Cfg::kParts * kTileM * Nw * 2;
+  L.dk_bytes = (uint32_t)Cfg::kParts * kDkBytes;
+  L.xr = 0;
+  L.y = L.xr + 2 * L.xr_bytes;
+  L.dk = L.y + Cfg::kYBufs * L.y_bytes;
+  L.bars = L.dk + Cfg::kDkSlots * L.dk_bytes;
+  L.total = L.bars + 8 * (8 + 2 * Cfg::kDkSlots + 1);
+  return L;
+}
+
+struct BwParams {
+  const void* x;
+  const void* y;
+  const void* gout;
+  float* partial;  // [splits][NG][128][Nw]
+  int N, C, H, W, Cp, Nw, R;
+  int d[3];
+  int tiles_w, tiles_h, num_tiles;
+  int ngroups, gb;    // groups; groups per batch
+  int splits;
+  int* status;
+};
+
+template <typename T, int KS>
+__global__ void __launch_bounds__(BwCfg<T, KS>::kThreads, 1)
+gencat_bwd_w_kernel(const BwParams p) {
+  using Cfg = BwCfg<T, KS>;
+  using Op = typename IoTraits<T>::Op;
+  constexpr int NS = Cfg::kDkSlots;
+  constexpr int NY = Cfg::kYBufs;
+  constexpr int NOCT = Cfg::kOct;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ uint32_t tmem_base_s;
+  __shared__ int abort_s;
+
+  const int C = p.C, H = p.H, W = p.W, R = p.R, Nw = p.Nw;
+  const size_t P = (size_t)H * W;
+  const BwSmem L = bw_smem_layout<T, KS>(Nw, R);
+  const int batch = blockIdx.x % ((p.ngroups + p.gb - 1) / p.gb);
+  const int split = blockIdx.x / ((p.ngroups + p.gb - 1) / p.gb);
+  const int g0 = batch * p.gb;
+  const int g1 = min(p.ngroups, g0 + p.gb);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint64_t* x_full = bars;          // [2]
+  uint64_t* x_empty = bars + 2;     // [2]
+  uint64_t* y_full = bars + 4;      // [2]
+  uint64_t* y_empty = bars + 6;     // [2]
+  uint64_t* k_full = bars + 8;      // [NS]
+  uint64_t* k_empty = k_full + NS;  // [NS]
+  uint64_t* d_full = k_empty + NS;  // [1]
+  const int xr_rows = kTileH + 2 * R;
+  const int xr_plane = xr_rows * kHaloCols;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (warp == 0) {
+    tc::tmem_alloc(&tmem_base_s, 512);
+    tc::tmem_relinquish();
+  }
+  if (threadIdx.x == 32) {
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(&x_full[i], Cfg::kProducers);
+      tc::mbar_init(&x_empty[i], 128);
+      tc::mbar_init(&y_full[i], Cfg::kProducers);
+      tc::mbar_init(&y_empty[i], 1);
+    }
+    for (int i = 0; i < NS; ++i) {
+      tc::mbar_init(&k_full[i], 128);
+      tc::mbar_init(&k_empty[i], 1);
+    }
+    tc::mbar_init(d_full, 1);
+    tc::fence_mbar_init();
+    abort_s = 0;
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem_base = tmem_base_s;
+  volatile int* abort_flag = &abort_s;
+
+  if (warp == 0) {
+    // idle after TMEM allocation
+  } else if (warp == 1) {
+    // ---- MMA: D_w[g] += dK^T . y_tile, over the split's tiles --------------
+    if (lane == 0) {
+      const uint32_t idesc = tc::idesc_f16(kTileM, Nw, IoTraits<T>::kBf16, true, false);
+      const uint32_t b_lbo = Nw * 16;          // pixel-group stride of the y tile
+      const uint32_t ypart = kTileM * Nw * 2;
+      uint32_t kq = 0, it = 0;
+      bool first = true;
+      for (int tile = split; tile < p.num_tiles; tile += p.splits, ++it) {
+        const int yb = it % NY;
+        if (!tc::mbar_wait(&y_full[yb], (it / NY) & 1, abort_flag, kWaitNs)) {
+          fail(abort_flag, p.status, 40);
+          goto done;
+        }
+        tc::tc_fence_after();
+        const uint32_t ya = tc::smem_u32(smem + L.y + yb * L.y_bytes);
+        for (int g = g0; g < g1; ++g, ++kq) {
+          const int ks_ = kq % NS;
+          if (!tc::mbar_wait(&k_full[ks_], (kq / NS) & 1, abort_flag, kWaitNs)) {
+            fail(abort_flag, p.status, 41);
+            goto done;
+          }
+          tc::tc_fence_after();
+          const uint32_t ka = tc::smem_u32(smem + L.dk + ks_ * L.dk_bytes);
+          const uint32_t dt = tmem_base + (g - g0) * Nw;
+          for (int ks = 0; ks < 8; ++ks) {
+            // A: dK, MN-major (rows are M, pixels are K): K-group stride 2048, M-group 128
+            const uint64_t a_hi = tc::smem_desc(ka + ks * 2 * 2048, 2048, 128);
+            const uint64_t b_hi = tc::smem_desc(ya + ks * 2 * b_lbo, b_lbo, 128);
+            tc::mma_f16(dt, a_hi, b_hi, idesc, (!first || ks > 0) ? 1u : 0u);
+            if constexpr (Cfg::kSplit) {
+              const uint64_t a_lo = tc::smem_desc(ka + kDkBytes + ks * 2 * 2048, 2048, 128);
+              const uint64_t b_lo = tc::smem_desc(ya + ypart + ks * 2 * b_lbo, b_lbo, 128);
+              tc::mma_f16(dt, a_lo, b_hi, idesc, 1u);
+              tc::mma_f16(dt, a_hi, b_lo, idesc, 1u);
+            }
+          }
+          tc::mma_commit(&k_empty[ks_]);
+        }
+        tc::mma_commit(&y_empty[yb]);
+        first = false;
+      }
+      tc::mma_commit(d_full);
+    }
+  } else if (warp < 6) {
+    // ---- x-halo producers ----------------------------------------------------
+    const int pt = threadIdx.x - 64;
+    uint32_t xq = 0;
+    for (int tile = split; tile < p.num_tiles && !*abort_flag; tile += p.splits) {
+      int n, h0, w0;
+      tile_origin(tile, p.tiles_w, p.tiles_h, n, h0, w0);
+      int cur = -1;
+      for (int g = g0; g < g1; ++g) {
+        const int cg = g / NOCT;
+        if (cg == cur) continue;
+        cur = cg;
+        const int xb = xq & 1;
+        if (!warp_wait(&x_empty[xb], ((xq >> 1) & 1) ^ 1, abort_flag)) {
+          fail(abort_flag, p.status, 42);
+          break;
+        }
+        float4* xr = reinterpret_cast<float4*>(smem + L.xr + xb * L.xr_bytes);
+        stage_halo<T, Cfg::kXItems>(static_cast<const T*>(p.x), xr, n, C, H, W, cg * 16, h0 - R,
+                                    w0 - 8, xr_rows, pt, Cfg::kProducers);
+        tc::mbar_arrive(&x_full[xb]);
+        ++xq;
+      }
+    }
+  } else if (warp < 10) {
+    // ---- y-tile producers (B operand, ones channel at C for db) -----------
+    const int pt = threadIdx.x - 192;
+    uint32_t it = 0;
+    for (int tile = split; tile < p.num_tiles; tile += p.splits, ++it) {
+      const int yb = it % NY;
+      if (!warp_wait(&y_empty[yb], ((it / NY) & 1) ^ 1, abort_flag)) {
+        fail(abort_flag, p.status, 43);
+        break;
+      }
+      int n, h0, w0;
+      tile_origin(tile, p.tiles_w, p.tiles_h, n, h0, w0);
+      uint8_t* ys = smem + L.y + yb * L.y_bytes;
+      stage_y_mn<T, Op, Cfg::kSplit, Cfg::kYItems>(static_cast<const T*>(p.y), ys,
+                                                   ys + kTileM * Nw * 2, n, C, Nw, C, H, W, h0,
+                                                   w0, pt, Cfg::kProducers);
+      tc::fence_proxy_async_smem();
+      tc::mbar_arrive(&y_full[yb]);
+    }
+  } else {
+    // ---- builders (thread = pixel) then the D_w drain (thread = row) -------
+    const int quad = warp & 3;
+    const int m = quad * 32 + lane;
+    const int mr = m >> 4, mc = m & 15;
+    const T* gout = static_cast<const T*>(p.gout);
+    const int dil[3] = {p.d[0], p.d[1], p.d[2]};
+    uint32_t xq = 0, kq = 0;
+    bool failed = false;
+    for (int tile = split; tile < p.num_tiles && !failed; tile += p.splits) {
+      int n, h0, w0;
+      tile_origin(tile, p.tiles_w, p.tiles_h, n, h0, w0);
+      const int h = h0 + mr, w = w0 + mc;
+      const bool px_ok = (h < H) && (w < W);
+      const size_t pix = px_ok ? (size_t)h * W + w : 0;
+      const T* gn = gout + (size_t)n * 4 * C * P;
+      int cur = -1;
+      float gv[3][16];
+      const float4* xc = nullptr;
+      int xb = 0;
+      for (int g = g0; g < g1; ++g, ++kq) {
+        const int cg = g / NOCT;
+        if (cg != cur) {
+          if (cur >= 0) {
+            tc::mbar_arrive(&x_empty[xb]);
+            ++xq;
+          }
+          cur = cg;
+          load_gv<T>(gv, gn, C, P, cg, pix, px_ok);
+          xb = xq & 1;
+          if (!warp_wait(&x_full[xb], (xq >> 1) & 1, abort_flag)) {
+            fail(abort_flag, p.status, 44);
+            failed = true;
+            break;
+          }
+          xc = reinterpret_cast<const float4*>(smem + L.xr + xb * L.xr_bytes) +
+               (mr + R) * kHaloCols + (mc + 8);
+        }
+        const int ks_ = kq % NS;
+        if (!warp_wait(&k_empty[ks_], ((kq / NS) & 1) ^ 1, abort_flag)) {
+          fail(abort_flag, p.status, 45);
+          failed = true;
+          break;
+        }
+        build_dk<T, Op, Cfg::kSplit, KS>(smem + L.dk + ks_ * L.dk_bytes, g % NOCT, xc, xr_plane,
+                                         gv, dil, m);
+        tc::fence_proxy_async_smem();
+        tc::mbar_arrive(&k_full[ks_]);
+      }
+      if (!failed && cur >= 0) {
+        tc::mbar_arrive(&x_empty[xb]);
+        ++xq;
+      }
+    }
+    // drain: lane = weight row of the group, columns = Nw
+    if (!failed && warp_wait(d_full, 0, abort_flag)) {
+      tc::tc_fence_after();
+      for (int g = g0; g < g1; ++g) {
+        float* dst = p.partial + (((size_t)split * p.ngroups + g) * 128 + m) * Nw;
+        for (int c0 = 0; c0 < Nw; c0 += 16) {
+          float dv[16];
+          tc::tmem_ld16(tmem_base + ((uint32_t)(quad * 32) << 16) + (g - g0) * Nw + c0, dv);
+          tc::tmem_ld_wait();
+#pragma unroll
+          for (int k = 0; k < 16; k += 4)
+            *reinterpret_cast<float4*>(dst + c0 + k) =
+                make_float4(dv[k], dv[k + 1], dv[k + 2], dv[k + 3]);
+        }
+      }
+    } else if (!failed) {
+      fail(abort_flag, p.status, 46);
+    }
+  }
+done:
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem_base, 512);
+  }
+}
+
+// Sum the split partials into the Conv2d layout: gw[(b*C + c)*K^2 + tap, i],
+// gb[(b*C + c)*K^2 + tap] (column C of the partials is the bias gradient).
+template <typename T>
+__global__ void gencat_wreduce_kernel(const float* __restrict__ partial, T* __restrict__ gw,
+                                      T* __restrict__ gb, int C, int KS, int ngroups, int Nw,
+                                      int splits) {
+  const int KK = KS * KS;
+  const int noct = (3 * KK + 7) / 8;
+  const long long total = (long long)ngroups * 128 * (C + 1);
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int i = (int)(idx % (C + 1));
+    const int row = (int)((idx / (C + 1)) % 128);
+    const int g = (int)(idx / ((long long)(C + 1) * 128));
+    const int slot = (g % noct) * 8 + row / 16;
+    const int c = (g / noct) * 16 + row % 16;
+    if (slot >= 3 * KK || c >= C) continue;
+    float acc = 0.f;
+    const float* src = partial + ((size_t)g * 128 + row) * Nw + i;
+    for (int s = 0; s < splits; ++s) acc += src[(size_t)s * ngroups * 128 * Nw];
+    const int b = slot / KK, tap = slot % KK;
+    const long long mrow = (long long)(b * C + c) * KK + tap;
+    if (i < C) gw[mrow * C + i] = from_f32<T>(acc);
+    else gb[mrow] = from_f32<T>(acc);
+  }
+}
+
+// ------------------------------------------------------------- launchers ----
+template <typename T, int KS>
+int launch_y(const ByParams& prm, cudaStream_t st) {
+  using Cfg = ByCfg<T, KS>;
+  const BySmem L = by_smem_layout<T, KS>(prm.Cp, prm.R);
+  auto fn = gencat_bwd_y_kernel<T, KS>;
+  DDPM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total));
+  const int grid = prm.num_tiles < num_sms() ? prm.num_tiles : num_sms();
+  fn<<<grid, Cfg::kThreads, L.total, st>>>(prm);
+  DDPM_CHECK_LAUNCH("gencat_bwd_y_kernel");
+  return DDPM_OK;
+}
+
+template <typename T, int KS>
+int launch_w(BwParams prm, int nbatches, cudaStream_t st) {
+  using Cfg = BwCfg<T, KS>;
+  const BwSmem L = bw_smem_layout<T, KS>(prm.Nw, prm.R);
+  auto fn = gencat_bwd_w_kernel<T, KS>;
+  DDPM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total));
+  fn<<<nbatches * prm.splits, Cfg::kThreads, L.total, st>>>(prm);
+  DDPM_CHECK_LAUNCH("gencat_bwd_w_kernel");
+  return DDPM_OK;
+}
+
+template <typename T>
+int launch_reduce(const float* partial, void* gw, void* gb, int C, int KS, int ngroups, int Nw,
+                  int splits, cudaStream_t st) {
+  const long long total = (long long)ngroups * 128 * (C + 1);
+  const int threads = 256;
+  const long long want = (total + threads - 1) / threads;
+  gencat_wreduce_kernel<T><<<(int)(want < 2048 ? want : 2048), threads, 0, st>>>(
+      partial, static_cast<T*>(gw), static_cast<T*>(gb), C, KS, ngroups, Nw, splits);
+  DDPM_CHECK_LAUNCH("gencat_wreduce_kernel");
+  return DDPM_OK;
+}
+
+struct WPlan {
+  int Nw, gb, nbatches, splits;
+  size_t ws_bytes;
+};
+
+WPlan plan_w(int n, int c, int h, int w, int ks) {
+  const gencat::PackLayout pl = gencat::PackLayout::make(c, ks, DDPM_BF16);
+  WPlan q;
+  q.Nw = gencat::augmented_channels(c);  // input channels + the constant-one (db) column
+  q.gb = 512 / q.Nw;
+  if (q.gb > pl.NG) q.gb = pl.NG;
+  q.nbatches = (pl.NG + q.gb - 1) / q.gb;
+  const int tiles = n * ((h + gencat::kTileH - 1) / gencat::kTileH) *
+                    ((w + gencat::kTileW - 1) / gencat::kTileW);
+  int sp = num_sms() / q.nbatches;
+  if (sp < 1) sp = 1;
+  if (sp > tiles) sp = tiles;
+  q.splits = sp;
+  q.ws_bytes = (size_t)sp * pl.NG * 128 * q.Nw * sizeof(float);
+  return q;
+}
+
+}  // namespace
+
+size_t gencat_bwd_workspace_bytes(int n, int c, int h, int w, int ks) {
+  if (n < 1 || c < 1 || c > gencat::kMaxChannels || h < 1 || w < 1 || (ks != 1 && ks != 3))
+    return 0;
+  return plan_w(n, c, h, w, ks).ws_bytes;
+}
+
+int gencat_bwd_yw(const void* x, const void* y, const void* wpack, const void* gout, void* gy,
+                  void* gw, void* gb, void* workspace, size_t ws_bytes, int n, int c, int h, int w,
+                  int ks, int d0, int d1, int d2, int dt, cudaStream_t st) {
+  int rc = gencat::check_shape(n, c, h, w, ks, d0, d1, d2, dt);
+  if (rc) return rc;
+  DDPM_CHECK_ARG(x && y && wpack && gout, "null pointer");
+  const gencat::PackLayout pl = gencat::PackLayout::make(c, ks, dt);
+  const int R = (ks / 2) * max3(d0, d1, d2);
+  const int tiles_w = (w + gencat::kTileW - 1) / gencat::kTileW;
+  const int tiles_h = (h + gencat::kTileH - 1) / gencat::kTileH;
+  int* status = nullptr;
+  rc = gencat::status_ptr(&status);
+  if (rc) return rc;
+
+  if (gy != nullptr) {
+    ByParams bp{};
+    bp.x = x;
+    bp.wpack = static_cast<const uint8_t*>(wpack) + pl.by_offset();
+    bp.gout = gout;
+    bp.gy = gy;
+    bp.N = n;
+    bp.C = c;
+    bp.H = h;
+    bp.W = w;
+    bp.Cp = pl.Cp;
+    bp.R = R;
+    bp.d[0] = d0;
+    bp.d[1] = d1;
+    bp.d[2] = d2;
+    bp.tiles_w = tiles_w;
+    bp.tiles_h = tiles_h;
+    bp.num_tiles = n * tiles_w * tiles_h;
+    bp.status = status;
+    switch (dt * 10 + ks) {
+      case DDPM_BF16 * 10 + 1: rc = launch_y<__nv_bfloat16, 1>(bp, st); break;
+      case DDPM_BF16 * 10 + 3: rc = launch_y<__nv_bfloat16, 3>(bp, st); break;
+      case DDPM_F16 * 10 + 1: rc = launch_y<__half, 1>(bp, st); break;
+      case DDPM_F16 * 10 + 3: rc = launch_y<__half, 3>(bp, st); break;
+      case DDPM_F32 * 10 + 1: rc = launch_y<float, 1>(bp, st); break;
+      case DDPM_F32 * 10 + 3: rc = launch_y<float, 3>(bp, st); break;
+      default: rc = set_error(DDPM_ERR_UNSUPPORTED, "unsupported dtype/kernel size");
+    }
+    if (rc) return rc;
+  }
+  if (gw != nullptr || gb != nullptr) {
+    DDPM_CHECK_ARG(gw && gb, "grad_weight and grad_bias must both be given");
+    const WPlan q = plan_w(n, c, h, w, ks);
+    if (workspace == nullptr || ws_bytes < q.ws_bytes)
+      return set_error(DDPM_ERR_WORKSPACE, "workspace too small (%zu < %zu)", ws_bytes, q.ws_bytes);
+    DDPM_CHECK_ARG((reinterpret_cast<uintptr_t>(workspace) & 15u) == 0,
+                   "workspace must be 16-byte aligned");
+    BwParams wp{};
+    wp.x = x;
+    wp.y = y;
+    wp.gout = gout;
+    wp.partial = static_cast<float*>(workspace);
+    wp.N = n;
+    wp.C = c;
+    wp.H = h;
+    wp.W = w;
+    wp.Cp = pl.Cp;
+    wp.Nw = q.Nw;
+    wp.R = R;
+    wp.d[0] = d0;
+    wp.d[1] = d1;
+    wp.d[2] = d2;
+    wp.tiles_w = tiles_w;
+    wp.tiles_h = tiles_h;
+    wp.num_tiles = n * tiles_w * tiles_h;
+    wp.ngroups = pl.NG;
+    wp.gb = q.gb;
+    wp.splits = q.splits;
+    wp.status = status;
+    switch (dt * 10 + ks) {
+      case DDPM_BF16 * 10 + 1: rc = launch_w<__nv_bfloat16, 1>(wp, q.nbatches, st); break;
+      case DDPM_BF16 * 10 + 3: rc = launch_w<__nv_bfloat16, 3>(wp, q.nbatches, st); break;
+      case DDPM_F16 * 10 + 1: rc = launch_w<__half, 1>(wp, q.nbatches, st); break;
+      case DDPM_F16 * 10 + 3: rc = launch_w<__half, 3>(wp, q.nbatches, st); break;
+      case DDPM_F32 * 10 + 1: rc = launch_w<float, 1>(wp, q.nbatches, st); break;
+      case DDPM_F32 * 10 + 3: rc = launch_w<float, 3>(wp, q.nbatches, st); break;
+      default: rc = set_error(DDPM_ERR_UNSUPPORTED, "unsupported dtype/kernel size");
+    }
+    if (rc) return rc;
+    switch (dt) {
+      case DDPM_BF16:
+        return launch_reduce<__nv_bfloat16>(wp.partial, gw, gb, c, ks, pl.NG, q.Nw, q.splits, st);
+      case DDPM_F16:
+        return launch_reduce<__half>(wp.partial, gw, gb, c, ks, pl.NG, q.Nw, q.splits, st);
+      case DDPM_F32:
+        return launch_reduce<float>(wp.partial, gw, gb, c, ks, pl.NG, q.Nw, q.splits, st);
+    }
+  }
+  return DDPM_OK;
+}
+
+}  // namespace ddpm

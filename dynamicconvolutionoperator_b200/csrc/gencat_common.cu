@@ -1,13 +1,13 @@
 // Host-side helpers of the fused generator kernels and the weight packer.
 //
 // The generator weight W [3*C*K^2, C] (a Conv2d [3CK^2, C, 1, 1] weight,
-// row index (b*C + c)*K^2 + tap, reference `_triton_kernels.py:322`) is
-// re-laid-out once per weight version into the exact shared-memory images the
-// tensor-core kernels consume, so the kernels stream it with plain 1-D bulk
-// copies. Forward image, per chunk q = (cg*3 + b)*K + ki:
-//   [part (hi, lo for fp32)][Cp/8 input-channel groups][16*K rows][8]
-// with row kj*16 + cl <-> weight row (b*C + cg*16 + cl)*K^2 + ki*K + kj.
-// Rows/columns past C are zero (channel padding to a multiple of 16).
+// row index (b*C + c)*K^2 + tap, reference `_triton_kernels.py:322`) and its
+// bias are re-laid-out once per weight version into the exact shared-memory
+// operand images the tensor-core kernels consume, so the kernels stream them
+// with plain 1-D bulk copies. Three images, back to back (see gencat.cuh,
+// PackLayout): forward chunks, dX chunks and the transposed dY groups. Each
+// 16-byte row holds 8 consecutive K-dimension values; fp32 weights are stored
+// as a bf16 hi image followed by a bf16 lo (residual) image.
 #include <mutex>
 
 #include "common.cuh"
@@ -30,9 +30,10 @@ int check_shape(int n, int c, int h, int w, int ks, int d0, int d1, int d2, int 
                      kMaxChannels, c);
   if (ks != 1 && ks != 3)
     return set_error(DDPM_ERR_UNSUPPORTED, "fused generator supports K in {1, 3} (got %d)", ks);
-  DDPM_CHECK_ARG((long long)n * ((h + kTileH - 1) / kTileH) * ((w + kTileW - 1) / kTileW) <
-                     (1LL << 31),
-                 "too many tiles");
+  if ((ks / 2) * max3(d0, d1, d2) > kMaxHalo)
+    return set_error(DDPM_ERR_UNSUPPORTED, "fused generator supports dilation halos <= %d",
+                     kMaxHalo);
+  DDPM_CHECK_ARG((long long)n * h * ((w + 127) / 128) < (1LL << 31), "too many tiles");
   return DDPM_OK;
 }
 
@@ -61,40 +62,86 @@ int num_sms() {
 namespace {
 
 using gencat::IoTraits;
+using gencat::PackLayout;
 
-// One thread writes one 16-byte row (8 input channels) of the forward image.
+// One thread writes one 16-byte row (8 K-dimension values) of one image.
 template <typename T>
-__global__ void pack_fwd_kernel(const T* __restrict__ W, typename IoTraits<T>::Op* __restrict__ out,
-                                int C, int Cp, int KS) {
+__global__ void pack_kernel(const T* __restrict__ W, const T* __restrict__ bias,
+                            typename IoTraits<T>::Op* __restrict__ out, PackLayout L) {
   using Op = typename IoTraits<T>::Op;
-  constexpr int kParts = IoTraits<T>::kSplit ? 2 : 1;
-  const int KK = KS * KS;
-  const int kN = 16 * KS;
-  const int kg_n = Cp / 8;
-  const long long rows_per_chunk = (long long)kParts * kg_n * kN;
-  const long long total = (long long)(Cp / 16) * 3 * KS * rows_per_chunk;
+  const int C = L.C, KS = L.KS, KK = KS * KS;
+  const long long total = L.fwd_rows + L.bx_rows + L.by_rows;
   for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
        idx += (long long)gridDim.x * blockDim.x) {
-    const int q = (int)(idx / rows_per_chunk);
-    int rem = (int)(idx - (long long)q * rows_per_chunk);
-    const int part = rem / (kg_n * kN);
-    rem -= part * kg_n * kN;
-    const int kg = rem / kN;
-    const int nrow = rem - kg * kN;
-    const int cg = q / (3 * KS);
-    const int b = (q / KS) % 3;
-    const int ki = q % KS;
-    const int kj = nrow / 16;
-    const int c = cg * 16 + (nrow % 16);
-    const long long m = (long long)(b * C + c) * KK + ki * KS + kj;
+    long long m = -1;   // weight row
+    int k0 = 0;         // first K-dimension index of this 16-byte row
+    int part = 0;
+    bool kdim_is_row = false;  // dY image: the K dimension runs over weight rows
+    int i_col = 0;             // dY image: the weight column (input channel)
+    if (idx < L.fwd_rows) {
+      // [q][part][Ck/8][16K][8]; q = (cg*3 + b)*K + ki; row kj*16 + cl
+      const long long per_chunk = (long long)L.parts * (L.Ck / 8) * 16 * KS;
+      const int q = (int)(idx / per_chunk);
+      int rem = (int)(idx - q * per_chunk);
+      part = rem / ((L.Ck / 8) * 16 * KS);
+      rem -= part * (L.Ck / 8) * 16 * KS;
+      const int kg = rem / (16 * KS);
+      const int row = rem - kg * 16 * KS;
+      const int cg = q / (3 * KS), b = (q / KS) % 3, ki = q % KS;
+      const int kj = row / 16, c = cg * 16 + row % 16;
+      if (c < C) m = (long long)(b * C + c) * KK + ki * KS + kj;
+      k0 = kg * 8;
+    } else if (idx < L.fwd_rows + L.bx_rows) {
+      // [q][part][Ck/8][Cp][8]; q = b*K^2 + tap; row = c
+      const long long j = idx - L.fwd_rows;
+      const long long per_chunk = (long long)L.parts * (L.Ck / 8) * L.Cp;
+      const int q = (int)(j / per_chunk);
+      int rem = (int)(j - q * per_chunk);
+      part = rem / ((L.Ck / 8) * L.Cp);
+      rem -= part * (L.Ck / 8) * L.Cp;
+      const int kg = rem / L.Cp;
+      const int c = rem - kg * L.Cp;
+      const int b = q / KK, tap = q % KK;
+      if (c < C) m = (long long)(b * C + c) * KK + tap;
+      k0 = kg * 8;
+    } else {
+      // [g][part][16 row groups][Cp][8 rows]; g = cg16*octets + octet,
+      // group row = j*16 + cl with slot = octet*8 + j
+      const long long j = idx - L.fwd_rows - L.bx_rows;
+      const long long per_group = (long long)L.parts * 16 * L.Cp;
+      const int g = (int)(j / per_group);
+      int rem = (int)(j - g * per_group);
+      part = rem / (16 * L.Cp);
+      rem -= part * 16 * L.Cp;
+      const int rg = rem / L.Cp;
+      i_col = rem - rg * L.Cp;
+      k0 = rg * 8;
+      kdim_is_row = true;
+      m = g;  // group index, resolved per element below
+    }
     union {
       uint4 u;
       Op e[8];
     } row;
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      const int i = kg * 8 + e;
-      const float w = (c < C && i < C) ? to_f32<T>(W[m * C + i]) : 0.f;
+      float w = 0.f;
+      if (!kdim_is_row) {
+        const int i = k0 + e;
+        if (m >= 0) {
+          if (i < C) w = to_f32<T>(W[m * C + i]);
+          else if (i == L.bias_col) w = to_f32<T>(bias[m]);
+        }
+      } else {
+        const int grow = k0 + e;                 // row within the 128-row group
+        const int octets = (3 * KK + 7) / 8;
+        const int slot = ((int)m % octets) * 8 + grow / 16;
+        const int c = ((int)m / octets) * 16 + grow % 16;
+        if (slot < 3 * KK && c < C && i_col < C) {
+          const int b = slot / KK, tap = slot % KK;
+          w = to_f32<T>(W[((long long)(b * C + c) * KK + tap) * C + i_col]);
+        }
+      }
       const Op hi = gencat::op_from<Op>(w);
       row.e[e] = part == 0 ? hi : gencat::op_from<Op>(w - gencat::op_to<Op>(hi));
     }
@@ -103,41 +150,40 @@ __global__ void pack_fwd_kernel(const T* __restrict__ W, typename IoTraits<T>::O
 }
 
 template <typename T>
-int launch_pack(const void* w, void* packed, int c, int ks, cudaStream_t st) {
-  const int Cp = gencat::padded_channels(c);
-  const int parts = IoTraits<T>::kSplit ? 2 : 1;
-  const long long rows = (long long)(Cp / 16) * 3 * ks * parts * (Cp / 8) * 16 * ks;
+int launch_pack(const void* w, const void* bias, void* packed, const PackLayout& L,
+                cudaStream_t st) {
+  const long long rows = L.fwd_rows + L.bx_rows + L.by_rows;
   const int threads = 256;
-  const int blocks = (int)((rows + threads - 1) / threads);
-  pack_fwd_kernel<T><<<blocks, threads, 0, st>>>(
-      static_cast<const T*>(w), static_cast<typename IoTraits<T>::Op*>(packed), c, Cp, ks);
-  DDPM_CHECK_LAUNCH("pack_fwd_kernel");
+  const long long want = (rows + threads - 1) / threads;
+  const int blocks = (int)(want < 4096 ? want : 4096);
+  pack_kernel<T><<<blocks, threads, 0, st>>>(static_cast<const T*>(w), static_cast<const T*>(bias),
+                                            static_cast<typename IoTraits<T>::Op*>(packed), L);
+  DDPM_CHECK_LAUNCH("pack_kernel");
   return DDPM_OK;
 }
 
 }  // namespace
 
 size_t gencat_pack_bytes(int c, int ks, int dt) {
-  if (c < 1 || ks < 1 || dtype_size(dt) == 0) return 0;
-  const size_t Cp = gencat::padded_channels(c);
-  const size_t parts = dt == DDPM_F32 ? 2 : 1;
-  return (Cp / 16) * 3 * ks * parts * Cp * 16 * ks * 2;
+  if (c < 1 || c > gencat::kMaxChannels || ks < 1 || dtype_size(dt) == 0) return 0;
+  return gencat::PackLayout::make(c, ks, dt).total_bytes();
 }
 
-int gencat_pack(const void* w, int c, int ks, int dt, void* packed, size_t packed_bytes,
-                cudaStream_t st) {
+int gencat_pack(const void* w, const void* bias, int c, int ks, int dt, void* packed,
+                size_t packed_bytes, cudaStream_t st) {
   int rc = gencat::check_shape(1, c, 1, 1, ks, 1, 1, 1, dt);
   if (rc) return rc;
-  DDPM_CHECK_ARG(w && packed, "null pointer");
+  DDPM_CHECK_ARG(w && bias && packed, "null pointer");
   DDPM_CHECK_ARG((reinterpret_cast<uintptr_t>(packed) & 15u) == 0,
                  "packed weight buffer must be 16-byte aligned");
-  if (packed_bytes < gencat_pack_bytes(c, ks, dt))
+  const PackLayout L = PackLayout::make(c, ks, dt);
+  if (packed_bytes < L.total_bytes())
     return set_error(DDPM_ERR_WORKSPACE, "packed weight buffer too small (%zu < %zu)",
-                     packed_bytes, gencat_pack_bytes(c, ks, dt));
+                     packed_bytes, L.total_bytes());
   switch (dt) {
-    case DDPM_BF16: return launch_pack<__nv_bfloat16>(w, packed, c, ks, st);
-    case DDPM_F16: return launch_pack<__half>(w, packed, c, ks, st);
-    case DDPM_F32: return launch_pack<float>(w, packed, c, ks, st);
+    case DDPM_BF16: return launch_pack<__nv_bfloat16>(w, bias, packed, L, st);
+    case DDPM_F16: return launch_pack<__half>(w, bias, packed, L, st);
+    case DDPM_F32: return launch_pack<float>(w, bias, packed, L, st);
   }
   return set_error(DDPM_ERR_INVALID_ARG, "unknown dtype %d", dt);
 }

@@ -11,23 +11,42 @@
 // TMEM) and the epilogue warps consume the taps straight out of TMEM.
 //
 // Work decomposition (persistent CTAs, one per SM, 512 TMEM columns):
+//   * every CTA owns ONE output channel group cg of 16 channels; the weight
+//             rows of that group (3 branches x K^2 taps x 16 channels, i.e.
+//             3*K chunks) are loaded into shared memory once and stay resident,
+//             so no weight traffic recurs per tile (re-streaming the full
+//             weight per 128-pixel tile would need ~18 TB/s of L2 bandwidth);
 //   * tile  = 8 x 16 output pixels of one image = the 128 rows of the MMA's
 //             M dimension = the 128 TMEM lanes (lane m <-> pixel (m/16, m%16));
-//   * chunk = (channel group cg of 16, branch b, kernel row ki): N = 16*K
+//             CTAs of the same cg split the tiles between them;
+//   * chunk = (branch b, kernel row ki) of the CTA's group: N = 16*K
 //             accumulator columns, column kj*16 + cl <-> tap (ki, kj) of
-//             channel cg*16 + cl. A tile is (Cp/16) * 3 * K chunks.
+//             channel cg*16 + cl. A tile is 3 * K chunks.
+//   * GEMM K dimension = the Ck "augmented" input channels. For bf16/fp16:
+//             y's C channels, then a constant-one channel whose weight column
+//             is the bias, then zeros (Ck = round_up(C + 1, 16)) - the bias add
+//             is part of the MMA. For fp32 (shared memory is tighter there) Ck
+//             = Cp and the epilogue adds the bias.
 //   * operands: A = the y tile, MN-major in shared memory ([8-pixel group]
-//             [channel][8 pixels], so each 16-byte row is one contiguous global
-//             segment of 8 pixels of one channel); B = the chunk's weight rows,
+//             [channel][8 pixels]); B = the group's resident weight chunks,
 //             pre-packed in global memory in the exact K-major smem image and
-//             streamed through a 4-stage ring with 1-D bulk async copies.
+//             fetched with 1-D bulk async copies.
 //   * FP32 I/O: y and W are split into bf16 hi + lo parts and each MMA step
 //             is hi*hi + lo*hi + hi*lo (relative error ~2^-16 per product).
+//   * x halo: for each channel group the (8+2R) x 32 pixel neighbourhood of the
+//             tile is staged in shared memory as FP32, four channels per
+//             16-byte cell ([4-channel group][row][32 cols][4]), zero outside the
+//             image. An epilogue thread reads the 16 channels of one tap with
+//             four LDS.128 and needs no bounds checks.
 //
-// Warp roles (12 warps): w0 = TMEM allocator + weight producer, w1 = MMA
-// issuer, w2-w3 = y-tile producers, w4-w11 = two epilogue warpgroups. Output
-// group (cg, b) belongs to warpgroup (cg*3+b) % 2, which consumes its K chunks
-// in order from a ring of TMEM accumulator buffers.
+// Warp roles (18 warps): w0 = TMEM allocator + weight loader, w1 = MMA
+// issuer, w2-w5 = y-tile producers, w6-w9 = x-halo producers, w10-w17 = two
+// epilogue warpgroups; output group (tile, b) belongs to warpgroup
+// (tile_iter*3 + b) % 2, which consumes its chunks in order from a ring of
+// TMEM buffers. Each producer thread issues all of its loads for a tile before
+// its first shared-memory store, so a tile costs one memory latency, not
+// several; each epilogue thread issues the three TMEM loads of a chunk before
+// a single wait.
 #include "common.cuh"
 #include "tc.cuh"
 #include "gencat.cuh"
@@ -43,41 +62,53 @@ struct FwdCfg {
   static constexpr int kParts = kSplit ? 2 : 1;
   static constexpr int kN = 16 * KS;                         // accumulator columns per chunk
   static constexpr int kNumBuf = (512 / kN) > 8 ? 8 : (512 / kN);
-  static constexpr int kWStages = 4;
+  static constexpr int kChunks = 3 * KS;                      // per tile (one channel group)
+  static constexpr int kYBufs = kSplit ? 1 : 2;               // smem budget (see layout)
+  static constexpr bool kBiasInGemm = !kSplit;
   static constexpr int kEpiWG = 2;
-  static constexpr int kThreads = 32 * (4 + 4 * kEpiWG);
+  static constexpr int kProducers = 128;                      // threads per producer role
+  static constexpr int kFirstEpiWarp = 2 + 2 * (kProducers / 32);
+  static constexpr int kThreads = 32 * (kFirstEpiWarp + 4 * kEpiWG);
+  // loads per producer thread and tile (whole tile in one batch)
+  // y items per thread: 16 pixel groups x Ck (<= 80 for bf16/fp16, = Cp <= 64 for fp32)
+  static constexpr int kYItems = (16 * (kSplit ? 64 : 80) + kProducers - 1) / kProducers;
+  static constexpr int kXItems = (16 * (kTileH + 2 * kMaxHalo) + kProducers - 1) / kProducers;
 };
 
 struct FwdSmem {
   // byte offsets into dynamic shared memory
-  uint32_t y, w, bias, bars, total;
-  uint32_t y_bytes, w_bytes;
+  uint32_t y, w, xr, bias, bars, total;
+  uint32_t y_bytes, w_bytes, xr_bytes;
 };
 
+// Resident weights of one channel group + y tile(s) + two x-halo buffers.
+// C=64, K=3: bf16 69 + 2x20 + 2x36 KB = 181 KB; fp32 108 + 32 + 72 KB = 214 KB.
 template <typename T, int KS>
-__host__ __device__ inline FwdSmem fwd_smem_layout(int C, int Cp) {
+__host__ __device__ inline FwdSmem fwd_smem_layout(int Ck, int R) {
   using Cfg = FwdCfg<T, KS>;
   FwdSmem L;
-  L.y_bytes = (uint32_t)Cfg::kParts * kTileM * Cp * 2;
-  L.w_bytes = (uint32_t)Cfg::kParts * Cfg::kN * Cp * 2;
+  L.y_bytes = (uint32_t)Cfg::kParts * kTileM * Ck * 2;
+  L.w_bytes = (uint32_t)Cfg::kParts * Cfg::kN * Ck * 2;  // one chunk
+  L.xr_bytes = (uint32_t)16 * (kTileH + 2 * R) * kHaloCols * 4;
   L.y = 0;
-  L.w = L.y + 2 * L.y_bytes;
-  L.bias = L.w + Cfg::kWStages * L.w_bytes;
-  uint32_t bias_bytes = (uint32_t)(3 * C * KS * KS) * 4;
-  L.bars = (L.bias + bias_bytes + 15) & ~15u;
-  L.total = L.bars + 8 * (4 + 2 * Cfg::kWStages + 2 * Cfg::kNumBuf) + 16;
+  L.w = L.y + Cfg::kYBufs * L.y_bytes;
+  L.xr = L.w + Cfg::kChunks * L.w_bytes;
+  L.bias = L.xr + 2 * L.xr_bytes;
+  L.bars = L.bias + (Cfg::kBiasInGemm ? 0u : (uint32_t)(3 * 16 * KS * KS * 4));
+  L.total = L.bars + 8 * (9 + 2 * Cfg::kNumBuf);
   return L;
 }
 
 struct FwdParams {
   const void* x;
   const void* y;
-  const void* wpack;
-  const void* bias;
+  const void* wpack;  // forward image (all channel groups)
+  const void* bias;   // used by the fp32 epilogue (bias not folded into the GEMM)
   void* out;
-  int N, C, H, W, Cp;
+  int N, C, H, W, Cp, Ck, R;
   int d[3];
   int tiles_w, tiles_h, num_tiles;
+  int ncg, per_cg;    // channel groups; CTAs per channel group
   int* status;
 };
 
@@ -88,29 +119,33 @@ gencat_fwd_kernel(const FwdParams p) {
   using Op = typename IoTraits<T>::Op;
   constexpr int kN = Cfg::kN;
   constexpr int NB = Cfg::kNumBuf;
-  constexpr int S = Cfg::kWStages;
+  constexpr int NQ = Cfg::kChunks;
+  constexpr int NY = Cfg::kYBufs;
   constexpr int KK = KS * KS;
   constexpr int r = KS / 2;
   extern __shared__ __align__(1024) uint8_t smem[];
   __shared__ uint32_t tmem_base_s;
   __shared__ int abort_s;
 
-  const int C = p.C, Cp = p.Cp, H = p.H, W = p.W;
+  const int C = p.C, Ck = p.Ck, H = p.H, W = p.W, R = p.R;
   const size_t P = (size_t)H * W;
-  const FwdSmem L = fwd_smem_layout<T, KS>(C, Cp);
+  const FwdSmem L = fwd_smem_layout<T, KS>(Ck, R);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint64_t* y_full = bars;           // [2]
   uint64_t* y_empty = bars + 2;      // [2]
-  uint64_t* w_full = bars + 4;       // [S]
-  uint64_t* w_empty = w_full + S;    // [S]
-  uint64_t* t_full = w_empty + S;    // [NB]
+  uint64_t* x_full = bars + 4;       // [2]
+  uint64_t* x_empty = bars + 6;      // [2]
+  uint64_t* w_full = bars + 8;       // [1]
+  uint64_t* t_full = bars + 9;       // [NB]
   uint64_t* t_empty = t_full + NB;   // [NB]
-  float* bias_s = reinterpret_cast<float*>(smem + L.bias);
+  const int xr_rows = kTileH + 2 * R;
+  const int xr_plane = xr_rows * kHaloCols;  // 16-byte cells per 4-channel group
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int nchunks = (Cp / 16) * 3 * KS;
-  const uint32_t chunk_bytes = L.w_bytes;
+  const int cg = blockIdx.x % p.ncg;           // this CTA's output channel group
+  const int first_tile = blockIdx.x / p.ncg;
+  const int tile_step = p.per_cg;
 
   // ---- setup --------------------------------------------------------------
   if (warp == 0) {
@@ -119,13 +154,12 @@ gencat_fwd_kernel(const FwdParams p) {
   }
   if (threadIdx.x == 32) {
     for (int i = 0; i < 2; ++i) {
-      tc::mbar_init(&y_full[i], 64);
+      tc::mbar_init(&y_full[i], Cfg::kProducers);
       tc::mbar_init(&y_empty[i], 1);
+      tc::mbar_init(&x_full[i], Cfg::kProducers);
+      tc::mbar_init(&x_empty[i], 128 * Cfg::kEpiWG);
     }
-    for (int i = 0; i < S; ++i) {
-      tc::mbar_init(&w_full[i], 1);
-      tc::mbar_init(&w_empty[i], 1);
-    }
+    tc::mbar_init(w_full, 1);
     for (int i = 0; i < NB; ++i) {
       tc::mbar_init(&t_full[i], 1);
       tc::mbar_init(&t_empty[i], 128);
@@ -133,9 +167,14 @@ gencat_fwd_kernel(const FwdParams p) {
     tc::fence_mbar_init();
     abort_s = 0;
   }
-  {
+  if constexpr (!Cfg::kBiasInGemm) {
+    float* bias_s = reinterpret_cast<float*>(smem + L.bias);
     const T* bias = static_cast<const T*>(p.bias);
-    for (int i = threadIdx.x; i < 3 * C * KK; i += blockDim.x) bias_s[i] = to_f32<T>(bias[i]);
+    for (int i = threadIdx.x; i < 3 * 16 * KK; i += blockDim.x) {
+      const int b = i / (16 * KK), cl = (i / KK) % 16, tap = i % KK;
+      const int c = cg * 16 + cl;
+      bias_s[i] = c < C ? to_f32<T>(bias[(b * C + c) * KK + tap]) : 0.f;
+    }
   }
   tc::tc_fence_before();
   __syncthreads();
@@ -144,52 +183,45 @@ gencat_fwd_kernel(const FwdParams p) {
   volatile int* abort_flag = &abort_s;
 
   if (warp == 0) {
-    // ---- weight producer: stream packed chunks through the ring ----------
+    // ---- weight loader: the group's chunks, once, resident afterwards -----
     if (lane == 0) {
-      const uint8_t* wsrc = static_cast<const uint8_t*>(p.wpack);
-      uint32_t wq = 0;
-      for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
-        for (int q = 0; q < nchunks; ++q, ++wq) {
-          const int s = wq % S;
-          if (!tc::mbar_wait(&w_empty[s], ((wq / S) & 1) ^ 1, abort_flag, kWaitNs)) {
-            fail(abort_flag, p.status, 10);
-            goto done;
-          }
-          tc::mbar_arrive_expect_tx(&w_full[s], chunk_bytes);
-          tc::bulk_g2s(smem + L.w + s * chunk_bytes, wsrc + (size_t)q * chunk_bytes, chunk_bytes,
-                       &w_full[s]);
-        }
-      }
+      const uint32_t bytes = NQ * L.w_bytes;
+      const uint8_t* src = static_cast<const uint8_t*>(p.wpack) + (size_t)cg * bytes;
+      tc::mbar_arrive_expect_tx(w_full, bytes);
+      for (int q = 0; q < NQ; ++q)
+        tc::bulk_g2s(smem + L.w + q * L.w_bytes, src + (size_t)q * L.w_bytes, L.w_bytes, w_full);
     }
   } else if (warp == 1) {
     // ---- MMA issuer --------------------------------------------------------
     if (lane == 0) {
       const uint32_t idesc = tc::idesc_f16(kTileM, kN, IoTraits<T>::kBf16, true, false);
-      const uint32_t a_sbo = Cp * 16;           // 8-pixel groups
-      const uint32_t b_lbo = kN * 16;           // 8-channel groups of the weight chunk
-      const uint32_t ypart = kTileM * Cp * 2;   // hi -> lo offset of the y tile
-      const uint32_t wpart = kN * Cp * 2;       // hi -> lo offset of a weight chunk
-      uint32_t wq = 0, tq = 0, it = 0;
-      for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
-        const int yb = it & 1;
-        if (!tc::mbar_wait(&y_full[yb], (it >> 1) & 1, abort_flag, kWaitNs)) {
+      const uint32_t a_sbo = Ck * 16;           // 8-pixel groups
+      const uint32_t b_lbo = kN * 16;           // 8-channel groups of a weight chunk
+      const uint32_t ypart = kTileM * Ck * 2;   // hi -> lo offset of the y tile
+      const uint32_t wpart = kN * Ck * 2;       // hi -> lo offset of a weight chunk
+      if (!tc::mbar_wait(w_full, 0, abort_flag, kWaitNs)) {
+        fail(abort_flag, p.status, 10);
+        goto done;
+      }
+      uint32_t tq = 0, it = 0;
+      for (int tile = first_tile; tile < p.num_tiles; tile += tile_step, ++it) {
+        const int yb = it % NY;
+        if (!tc::mbar_wait(&y_full[yb], (it / NY) & 1, abort_flag, kWaitNs)) {
           fail(abort_flag, p.status, 11);
           goto done;
         }
         tc::tc_fence_after();
         const uint32_t ya = tc::smem_u32(smem + L.y + yb * L.y_bytes);
-        for (int q = 0; q < nchunks; ++q, ++wq, ++tq) {
-          const int s = wq % S;
+        for (int q = 0; q < NQ; ++q, ++tq) {
           const int j = tq % NB;
-          if (!tc::mbar_wait(&w_full[s], (wq / S) & 1, abort_flag, kWaitNs) ||
-              !tc::mbar_wait(&t_empty[j], ((tq / NB) & 1) ^ 1, abort_flag, kWaitNs)) {
+          if (!tc::mbar_wait(&t_empty[j], ((tq / NB) & 1) ^ 1, abort_flag, kWaitNs)) {
             fail(abort_flag, p.status, 12);
             goto done;
           }
           tc::tc_fence_after();
-          const uint32_t wb = tc::smem_u32(smem + L.w + s * chunk_bytes);
+          const uint32_t wb = tc::smem_u32(smem + L.w + q * L.w_bytes);
           const uint32_t d = tmem_base + j * kN;
-          for (int ks = 0; ks < Cp / 16; ++ks) {
+          for (int ks = 0; ks < Ck / 16; ++ks) {
             const uint64_t a_hi = tc::smem_desc(ya + ks * 256, 128, a_sbo);
             const uint64_t b_hi = tc::smem_desc(wb + ks * 2 * b_lbo, b_lbo, 128);
             tc::mma_f16(d, a_hi, b_hi, idesc, ks > 0 ? 1u : 0u);
@@ -200,148 +232,150 @@ gencat_fwd_kernel(const FwdParams p) {
               tc::mma_f16(d, a_hi, b_lo, idesc, 1u);
             }
           }
-          tc::mma_commit(&w_empty[s]);
           tc::mma_commit(&t_full[j]);
         }
         tc::mma_commit(&y_empty[yb]);
       }
     }
-  } else if (warp < 4) {
-    // ---- y-tile producers (64 threads) -------------------------------------
+  } else if (warp < 2 + Cfg::kProducers / 32) {
+    // ---- y-tile producers ----------------------------------------------------
     const int pt = threadIdx.x - 64;
     uint32_t it = 0;
-    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
-      const int yb = it & 1;
-      if (!warp_wait(&y_empty[yb], ((it >> 1) & 1) ^ 1, abort_flag)) {
+    for (int tile = first_tile; tile < p.num_tiles; tile += tile_step, ++it) {
+      const int yb = it % NY;
+      if (!warp_wait(&y_empty[yb], ((it / NY) & 1) ^ 1, abort_flag)) {
         fail(abort_flag, p.status, 13);
         break;
       }
       int n, h0, w0;
       tile_origin(tile, p.tiles_w, p.tiles_h, n, h0, w0);
       uint8_t* ys = smem + L.y + yb * L.y_bytes;
-      // 16 eight-pixel groups x Cp channels; one 16-byte smem row each.
-      // Loads are issued in batches of 8 independent rows per thread so the
-      // global latency is paid once per batch, not once per row.
-      constexpr int kBatch = 8;
-      for (int base = pt; base < 16 * Cp; base += 64 * kBatch) {
-        float v[kBatch][8];
-#pragma unroll
-        for (int u = 0; u < kBatch; ++u) {
-          const int item = base + u * 64;
-          const int c = item % Cp;
-          const int g = item / Cp;             // 8-pixel group: row g/2, half g%2
-          if (item < 16 * Cp)
-            load8<T>(static_cast<const T*>(p.y), n, c, C, H, W, h0 + (g >> 1), w0 + (g & 1) * 8,
-                     v[u]);
-        }
-#pragma unroll
-        for (int u = 0; u < kBatch; ++u) {
-          const int item = base + u * 64;
-          if (item >= 16 * Cp) break;
-          const int c = item % Cp;
-          const int g = item / Cp;
-          // MN-major interleaved: group g at g*Cp*16, channel c at (c/8)*128 + (c%8)*16
-          const uint32_t off = g * Cp * 16 + (c >> 3) * 128 + (c & 7) * 16;
-          store8_split<Op, Cfg::kSplit>(ys + off, ys + kTileM * Cp * 2 + off, v[u]);
-        }
-      }
+      // 16 eight-pixel groups x Ck channels; one 16-byte smem row each.
+      // MN-major interleaved: group g at g*Ck*16, channel c at (c/8)*128 + (c%8)*16.
+      stage_y_mn<T, Op, Cfg::kSplit, Cfg::kYItems>(static_cast<const T*>(p.y), ys,
+                                                   ys + kTileM * Ck * 2, n, C, Ck,
+                                                   Cfg::kBiasInGemm ? C : -1, H, W, h0, w0, pt,
+                                                   Cfg::kProducers);
       tc::fence_proxy_async_smem();
       tc::mbar_arrive(&y_full[yb]);
     }
+  } else if (warp < Cfg::kFirstEpiWarp) {
+    // ---- x-halo producers ----------------------------------------------------
+    const int pt = threadIdx.x - 64 - Cfg::kProducers;
+    uint32_t it = 0;
+    for (int tile = first_tile; tile < p.num_tiles; tile += tile_step, ++it) {
+      const int xb = it & 1;
+      if (!warp_wait(&x_empty[xb], ((it >> 1) & 1) ^ 1, abort_flag)) {
+        fail(abort_flag, p.status, 15);
+        break;
+      }
+      int n, h0, w0;
+      tile_origin(tile, p.tiles_w, p.tiles_h, n, h0, w0);
+      float4* xr = reinterpret_cast<float4*>(smem + L.xr + xb * L.xr_bytes);
+      stage_halo<T, Cfg::kXItems>(static_cast<const T*>(p.x), xr, n, C, H, W, cg * 16, h0 - R,
+                                  w0 - 8, xr_rows, pt, Cfg::kProducers);
+      tc::mbar_arrive(&x_full[xb]);
+    }
   } else {
     // ---- epilogue warpgroups -----------------------------------------------
-    const int ew = warp - 4;
+    const int ew = warp - Cfg::kFirstEpiWarp;
     const int wg = ew >> 2;
     const int quad = warp & 3;               // TMEM lane quadrant of this warp
     const int m = quad * 32 + lane;          // pixel row of the MMA tile
-    const T* x = static_cast<const T*>(p.x);
+    const int mr = m >> 4, mc = m & 15;
+    const float* bias_s = reinterpret_cast<const float*>(smem + L.bias);
     T* out = static_cast<T*>(p.out);
-    uint32_t tq = 0;
-    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+    uint32_t tq = 0, it = 0;
+    for (int tile = first_tile; tile < p.num_tiles; tile += tile_step, ++it) {
       int n, h0, w0;
       tile_origin(tile, p.tiles_w, p.tiles_h, n, h0, w0);
-      const int h = h0 + (m >> 4);
-      const int w = w0 + (m & 15);
+      const int h = h0 + mr;
+      const int w = w0 + mc;
       const bool px_ok = (h < H) && (w < W);
       const size_t pix = (size_t)h * W + w;
-      const T* xn = x + (size_t)n * C * P;
       T* on = out + (size_t)n * 4 * C * P;
+      const int xb = it & 1;
+      if (!warp_wait(&x_full[xb], (it >> 1) & 1, abort_flag)) {
+        fail(abort_flag, p.status, 16);
+        break;
+      }
+      const float4* xr = reinterpret_cast<const float4*>(smem + L.xr + xb * L.xr_bytes);
+      // this pixel's cell in the halo tile; a tap shifts it by (dy, dx)
+      const float4* xc = xr + (mr + R) * kHaloCols + (mc + 8);
       bool failed = false;
-      for (int cg = 0; cg < Cp / 16 && !failed; ++cg) {
-        for (int b = 0; b < 3; ++b) {
-          const bool mine = ((cg * 3 + b) % Cfg::kEpiWG) == wg;
-          if (!mine) {
-            tq += KS;
-            continue;
+      for (int b = 0; b < 3; ++b) {
+        const bool mine = ((it * 3 + b) % Cfg::kEpiWG) == (uint32_t)wg;
+        if (!mine) {
+          tq += KS;
+          continue;
+        }
+        const int d = p.d[b];
+        float acc[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+#pragma unroll
+        for (int ki = 0; ki < KS; ++ki, ++tq) {
+          const int j = tq % NB;
+          if (!warp_wait(&t_full[j], (tq / NB) & 1, abort_flag)) {
+            fail(abort_flag, p.status, 14);
+            failed = true;
+            break;
           }
-          const int d = p.d[b];
-          float acc[16];
+          tc::tc_fence_after();
+          const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + j * kN;
+          const float4* xrow = xc + (ki - r) * d * kHaloCols;
+          float dv[KS][16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+          for (int kj = 0; kj < KS; ++kj) tc::tmem_ld16(taddr + kj * 16, dv[kj]);
+          tc::tmem_ld_wait();
+          tc::tc_fence_before();
+          tc::mbar_arrive(&t_empty[j]);  // accumulator values are in registers now
 #pragma unroll
-          for (int ki = 0; ki < KS; ++ki, ++tq) {
-            const int dy = (ki - r) * d;
-            const bool row_ok = px_ok && (unsigned)(h + dy) < (unsigned)H;
-            const T* xrow = xn + (size_t)(cg * 16) * P + (ptrdiff_t)(pix + (ptrdiff_t)dy * W);
-            // x neighbours of tap (ki, kj) for the 16 channels of the group;
-            // independent of the MMA result, so the first batch is issued
-            // before waiting for the accumulator.
-            auto load_x = [&](int kj, float (&xv)[16]) {
-              const int dx = (kj - r) * d;
-              const bool ok = row_ok && (unsigned)(w + dx) < (unsigned)W;
-#pragma unroll
-              for (int cl = 0; cl < 16; ++cl) {
-                const bool okc = ok && (cg * 16 + cl < C);
-                xv[cl] = okc ? to_f32<T>(__ldg(xrow + (size_t)cl * P + dx)) : 0.f;
-              }
-            };
+          for (int kj = 0; kj < KS; ++kj) {
+            const float4* cell = xrow + (kj - r) * d;
             float xv[16];
-            load_x(0, xv);
-            const int j = tq % NB;
-            if (!warp_wait(&t_full[j], (tq / NB) & 1, abort_flag)) {
-              fail(abort_flag, p.status, 14);
-              failed = true;
-              break;
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) {
+              const float4 v = cell[q4 * xr_plane];
+              xv[q4 * 4 + 0] = v.x;
+              xv[q4 * 4 + 1] = v.y;
+              xv[q4 * 4 + 2] = v.z;
+              xv[q4 * 4 + 3] = v.w;
             }
-            tc::tc_fence_after();
-            const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + j * kN;
+            if constexpr (!Cfg::kBiasInGemm) {
+              const float* bs = bias_s + b * 16 * KK + ki * KS + kj;
 #pragma unroll
-            for (int kj = 0; kj < KS; ++kj) {
-              float dv[16];
-              tc::tmem_ld16(taddr + kj * 16, dv);
-              float xnext[16];
-              if (kj + 1 < KS) load_x(kj + 1, xnext);
-              tc::tmem_ld_wait();
-              const float* bs = bias_s + (size_t)(b * C + cg * 16) * KK + ki * KS + kj;
-#pragma unroll
-              for (int cl = 0; cl < 16; ++cl) {
-                const float bv = (cg * 16 + cl < C) ? bs[cl * KK] : 0.f;
-                const float g = IoTraits<T>::round_io(dv[cl] + bv);
-                acc[cl] = fmaf(g, xv[cl], acc[cl]);
-              }
-              if (kj + 1 < KS) {
-#pragma unroll
-                for (int cl = 0; cl < 16; ++cl) xv[cl] = xnext[cl];
-              }
+              for (int cl = 0; cl < 16; ++cl) dv[kj][cl] += bs[cl * KK];
             }
-            tc::tc_fence_before();
-            tc::mbar_arrive(&t_empty[j]);
+            round_taps<T>(dv[kj]);
+#pragma unroll
+            for (int cl = 0; cl < 16; ++cl) acc[cl] = fmaf(dv[kj][cl], xv[cl], acc[cl]);
           }
-          if (failed) break;
-          if (px_ok) {
+        }
+        if (failed) break;
+        if (px_ok) {
 #pragma unroll
-            for (int cl = 0; cl < 16; ++cl) {
-              const int c = cg * 16 + cl;
-              if (c < C) on[(size_t)((b + 1) * C + c) * P + pix] = from_f32<T>(acc[cl]);
-            }
+          for (int cl = 0; cl < 16; ++cl) {
+            const int c = cg * 16 + cl;
+            if (c < C) on[(size_t)((b + 1) * C + c) * P + pix] = from_f32<T>(acc[cl]);
           }
         }
       }
       if (failed) break;
-      // passthrough out[:, 0:C] = x, channels split across the warpgroups
-      if (px_ok) {
-        for (int c = wg; c < C; c += Cfg::kEpiWG) on[(size_t)c * P + pix] = xn[(size_t)c * P + pix];
+      // passthrough out[:, cg*16 : cg*16+16] = x, written from the halo tile
+      if (px_ok && (it % Cfg::kEpiWG) == (uint32_t)wg) {
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const float4 v = xc[q4 * xr_plane];
+          const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int c = cg * 16 + q4 * 4 + k;
+            if (c < C) on[(size_t)c * P + pix] = from_f32<T>(e[k]);
+          }
+        }
       }
+      tc::mbar_arrive(&x_empty[xb]);
     }
   }
 done:
@@ -356,11 +390,14 @@ done:
 template <typename T, int KS>
 int launch(const FwdParams& prm, cudaStream_t st) {
   using Cfg = FwdCfg<T, KS>;
-  const FwdSmem L = fwd_smem_layout<T, KS>(prm.C, prm.Cp);
+  const FwdSmem L = fwd_smem_layout<T, KS>(prm.Ck, prm.R);
   auto fn = gencat_fwd_kernel<T, KS>;
   DDPM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total));
-  const int grid = prm.num_tiles < num_sms() ? prm.num_tiles : num_sms();
-  fn<<<grid, Cfg::kThreads, L.total, st>>>(prm);
+  FwdParams q = prm;
+  const int per_cg = num_sms() / q.ncg;
+  q.per_cg = q.num_tiles < per_cg ? q.num_tiles : per_cg;
+  const int grid = q.ncg * q.per_cg;
+  fn<<<grid, Cfg::kThreads, L.total, st>>>(q);
   DDPM_CHECK_LAUNCH("gencat_fwd_kernel");
   return DDPM_OK;
 }
@@ -392,7 +429,11 @@ int gencat_fwd(const void* x, const void* y, const void* wpack, const void* bias
   prm.C = c;
   prm.H = h;
   prm.W = w;
-  prm.Cp = gencat::padded_channels(c);
+  const gencat::PackLayout pl = gencat::PackLayout::make(c, ks, dt);
+  prm.Cp = pl.Cp;
+  prm.Ck = pl.Ck;
+  prm.ncg = pl.Cp / 16;
+  prm.R = (ks / 2) * max3(d0, d1, d2);
   prm.d[0] = d0;
   prm.d[1] = d1;
   prm.d[2] = d2;

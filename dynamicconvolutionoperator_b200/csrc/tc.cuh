@@ -61,6 +61,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps (without issuing) until
+// the phase completes or about `hint_ns` pass.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity,
+                                                    uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for the phase with `parity` to complete, for at most `limit_ns`.
 // Returns false on timeout (the caller records the failure and unwinds);
 // `abort_flag` (shared) lets one role stop the others early.
@@ -70,8 +85,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   const uint64_t t0 = globaltimer_ns();
   uint32_t spins = 0;
   while (true) {
+    // try_wait itself parks the thread for a short, hardware-chosen time
     if (mbar_try_wait(bar, parity)) return true;
-    if ((++spins & 255u) == 0) {
+    if ((++spins & 63u) == 0) {
       if (abort_flag != nullptr && *abort_flag) return false;
       if (globaltimer_ns() - t0 > limit_ns) return false;
     }

@@ -100,7 +100,8 @@ class DDPM(nn.Module):
             and x.dtype == y.dtype == gen.weight.dtype
             and gen.bias is not None
             and gen.bias.dtype == x.dtype
-            and _kernels.fused_generator_supported(self.dim, self.kernel_size, x.dtype)
+            and _kernels.fused_generator_supported(self.dim, self.kernel_size, x.dtype,
+                                                   self.dilations)
         )
 
     def _use_fused_training(self, x: torch.Tensor) -> bool:

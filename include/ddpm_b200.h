@@ -104,8 +104,8 @@ DDPM_API int ddpm_dyncat_bwd(const void* x, int x_dtype,
  * DDPM_ERR_UNSUPPORTED (callers then take the materialised path).
  */
 DDPM_API size_t ddpm_gencat_pack_bytes(int c, int ksize, int dtype);
-DDPM_API int ddpm_gencat_pack(const void* weight, int c, int ksize, int dtype,
-                              void* packed, size_t packed_bytes, void* stream);
+DDPM_API int ddpm_gencat_pack(const void* weight, const void* bias, int c, int ksize,
+                              int dtype, void* packed, size_t packed_bytes, void* stream);
 
 /*
  * Fused generator + dynamic filter, forward (inference and training forward).
@@ -114,13 +114,51 @@ DDPM_API int ddpm_gencat_pack(const void* weight, int c, int ksize, int dtype,
  *   gen = W * y + bias (tensor cores, FP32 accumulation), rounded to `dtype`
  *   for bf16/fp16 as the reference does (`:332-335`), then
  *   out = cat(x, sum_tap gen * shifted x for dilations d0, d1, d2).
- * x, y, bias, out share `dtype`; the taps never reach global memory.
+ * x, y, bias, out share `dtype` (bias: the generator bias [3*C*K*K], also
+ * packed; which copy a kernel reads is an implementation detail). The taps
+ * never reach global memory.
  */
 DDPM_API int ddpm_gencat_fwd(const void* x, const void* y, const void* packed,
                              const void* bias, void* out,
                              int n, int c, int h, int w,
                              int ksize, int d0, int d1, int d2, int dtype,
                              void* stream);
+
+/*
+ * Fused generator backward: input gradient dX, recomputing the taps.
+ * Replaces `_generator_dynamic_cat_bwd_x` (reference `_triton_kernels.py:430-531`):
+ *   grad_x[c,q] = grad_out[c,q]
+ *               + sum_{b,tap} gen[(b,c,tap), q-o] * grad_out[(b+1)C+c, q-o]
+ * with gen = round_dtype(W*y + bias) exactly as in the forward. `packed` is
+ * the buffer filled by ddpm_gencat_pack for the same weight and bias.
+ */
+DDPM_API int ddpm_gencat_bwd_x(const void* y, const void* packed, const void* bias,
+                               const void* grad_out, void* grad_x,
+                               int n, int c, int h, int w,
+                               int ksize, int d0, int d1, int d2, int dtype,
+                               void* stream);
+
+/*
+ * Fused generator backward: dY and dW/db with dK = shifted(x) * grad formed on
+ * chip. Replaces `_generator_dynamic_cat_bwd_y` (`_triton_kernels.py:534-623`),
+ * `_generator_dynamic_cat_bwd_weight_partial` (`:626-751`) and
+ * `_generator_dynamic_cat_bwd_weight_reduce` (`:754-811`):
+ *   grad_y[i,p]        = sum_{b,c,tap} W[(b,c,tap), i] * dK[(b,c,tap), p]
+ *   grad_weight[m, i]  = sum_p dK[m, p] * y[i, p]       ([3*C*K*K, C], dtype)
+ *   grad_bias[m]       = sum_p dK[m, p]                  ([3*C*K*K], dtype)
+ * grad_y may be NULL (skipped); grad_weight and grad_bias are given together
+ * or both NULL. The weight gradient is a split spatial reduction into FP32
+ * partials in `workspace` (ddpm_gencat_bwd_workspace_bytes() bytes, 16-byte
+ * aligned) followed by a short reduce kernel.
+ */
+DDPM_API size_t ddpm_gencat_bwd_workspace_bytes(int n, int c, int h, int w, int ksize);
+DDPM_API int ddpm_gencat_bwd_yw(const void* x, const void* y, const void* packed,
+                                const void* grad_out, void* grad_y,
+                                void* grad_weight, void* grad_bias,
+                                void* workspace, size_t workspace_bytes,
+                                int n, int c, int h, int w,
+                                int ksize, int d0, int d1, int d2, int dtype,
+                                void* stream);
 
 /*
  * Diagnostic (no reference counterpart): one 128 x n x k bf16 tcgen05 UMMA
