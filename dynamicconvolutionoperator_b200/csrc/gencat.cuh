@@ -243,32 +243,63 @@ __device__ __forceinline__ void store_raw8(uint8_t* hi, uint8_t* lo, const Raw8<
 
 // Stage the y tile of an 8 x 16 pixel tile as the MN-major MMA operand:
 // 16 eight-pixel groups (row g/2, half g%2) x Ck augmented channels, one
-// 16-byte row per (group, channel) at g*Ck*16 + (c/8)*128 + (c%8)*16.
-// Channel `ones_c` is the constant one (bias; -1 = none), others past C zero.
-// With kSplit, the bf16 residual goes to the same offset in `lo`. Each of the
-// `nthreads` threads issues all of its loads before its first store.
-template <typename T, typename Op, bool kSplit, int kMaxItems>
-__device__ __forceinline__ void stage_y_mn(const T* __restrict__ y, uint8_t* hi, uint8_t* lo, int n,
-                                           int C, int Ck, int ones_c, int H, int W, int h0, int w0,
-                                           int tid, int nthreads) {
-  const int items = 16 * Ck;
-  const size_t P = (size_t)H * W;
-  Raw8<T> v[kMaxItems];
+// 16-byte row per (group, channel) at g*Ck*16 + c*16. Channel `ones_c` is the
+// constant one (bias; -1 = none), others past C zero. With kSplit, the bf16
+// residual goes to the same offset in `lo`.
+// The item -> (channel, group) mapping is the same for every tile, so each
+// thread computes it once (YPlan) and only adds the tile origin per tile.
+template <int N>
+struct YPlan {
+  int c[N];  // channel, or -1 when the item is past the end
+  int g[N];  // 8-pixel group
+};
+
+template <int N>
+__device__ __forceinline__ YPlan<N> make_yplan(int Ck, int tid, int nthreads) {
+  YPlan<N> pl;
 #pragma unroll
-  for (int u = 0; u < kMaxItems; ++u) {
+  for (int u = 0; u < N; ++u) {
     const int item = tid + u * nthreads;
-    const int c = item % Ck;
-    const int g = item / Ck;
-    if (item < items && c < C)
-      v[u] = load_raw8<T>(y + ((size_t)n * C + c) * P, H, W, h0 + (g >> 1), w0 + (g & 1) * 8);
+    pl.c[u] = item < 16 * Ck ? item % Ck : -1;
+    pl.g[u] = item / Ck;
+  }
+  return pl;
+}
+
+template <typename T, typename Op, bool kSplit, int N>
+__device__ __forceinline__ void stage_y_mn(const YPlan<N>& pl, const T* __restrict__ y,
+                                           uint8_t* hi, uint8_t* lo, int n, int C, int Ck,
+                                           int ones_c, int H, int W, int h0, int w0) {
+  const size_t P = (size_t)H * W;
+  const T* ybase = y + (size_t)n * C * P;
+  // interior tile: every 8-pixel run is in the image and 16-byte aligned
+  const bool interior = (h0 + kTileH <= H) && (w0 + kTileW <= W) &&
+                        (((size_t)W * sizeof(T)) % 16 == 0) && (P * sizeof(T)) % 16 == 0 &&
+                        ((reinterpret_cast<uintptr_t>(ybase + (size_t)h0 * W + w0) & 15u) == 0);
+  Raw8<T> v[N];
+#pragma unroll
+  for (int u = 0; u < N; ++u) {
+    const int c = pl.c[u];
+    if (c >= 0 && c < C) {
+      const int g = pl.g[u];
+      if (interior) {
+        const T* src = ybase + (size_t)c * P + (size_t)(h0 + (g >> 1)) * W + w0 + (g & 1) * 8;
+        if constexpr (sizeof(T) == 2) {
+          v[u].u = __ldg(reinterpret_cast<const uint4*>(src));
+        } else {
+          v[u].a = __ldg(reinterpret_cast<const float4*>(src));
+          v[u].b = __ldg(reinterpret_cast<const float4*>(src) + 1);
+        }
+      } else {
+        v[u] = load_raw8<T>(ybase + (size_t)c * P, H, W, h0 + (g >> 1), w0 + (g & 1) * 8);
+      }
+    }
   }
 #pragma unroll
-  for (int u = 0; u < kMaxItems; ++u) {
-    const int item = tid + u * nthreads;
-    if (item >= items) break;
-    const int c = item % Ck;
-    const int g = item / Ck;
-    const uint32_t off = g * Ck * 16 + (c >> 3) * 128 + (c & 7) * 16;
+  for (int u = 0; u < N; ++u) {
+    const int c = pl.c[u];
+    if (c < 0) continue;
+    const uint32_t off = pl.g[u] * Ck * 16 + c * 16;
     if (c < C) {
       store_raw8<T, Op, kSplit>(hi + off, lo + off, v[u]);
     } else {
@@ -284,41 +315,109 @@ __device__ __forceinline__ void stage_y_mn(const T* __restrict__ y, uint8_t* hi,
 // Stage the x halo of one 16-channel group: rows hs .. hs+rows-1, columns
 // ws .. ws+31 of channels c0 .. c0+15, as FP32 float4 cells holding four
 // consecutive channels: cell (q4, row, col) = xr[(q4*rows + row)*32 + col].
-// Zero outside the image and for channels >= C.
-template <typename T, int kMaxItems>
-__device__ __forceinline__ void stage_halo(const T* __restrict__ x, float4* xr, int n, int C,
-                                           int H, int W, int c0, int hs, int ws, int rows,
-                                           int tid, int nthreads) {
-  const size_t P = (size_t)H * W;
-  const int items = 4 * rows * 4;  // (q4, row, 8-column block)
-  Raw8<T> v[kMaxItems][4];
+// Zero outside the image and for channels >= C. Items = (q4, row, 8-column
+// block); the mapping is precomputed per thread (XPlan).
+template <int N>
+struct XPlan {
+  int q4[N];   // 4-channel group, or -1
+  int row[N];
+  int blk[N];
+};
+
+template <int N>
+__device__ __forceinline__ XPlan<N> make_xplan(int rows, int tid, int nthreads) {
+  XPlan<N> pl;
 #pragma unroll
-  for (int u = 0; u < kMaxItems; ++u) {
+  for (int u = 0; u < N; ++u) {
     const int item = tid + u * nthreads;
-    const int blk = item & 3;
-    const int row = (item >> 2) % rows;
-    const int q4 = (item >> 2) / rows;
+    pl.blk[u] = item & 3;
+    pl.row[u] = (item >> 2) % rows;
+    pl.q4[u] = item < 16 * rows ? (item >> 2) / rows : -1;
+  }
+  return pl;
+}
+
+template <typename T, int N>
+__device__ __forceinline__ void stage_halo(const XPlan<N>& pl, const T* __restrict__ x, float4* xr,
+                                           int n, int C, int H, int W, int c0, int hs, int ws,
+                                           int rows) {
+  const size_t P = (size_t)H * W;
+  const T* xbase = x + ((size_t)n * C + c0) * P;
+  const bool interior = hs >= 0 && hs + rows <= H && ws >= 0 && ws + kHaloCols <= W &&
+                        c0 + 16 <= C && (((size_t)W * sizeof(T)) % 16 == 0) &&
+                        (P * sizeof(T)) % 16 == 0 &&
+                        ((reinterpret_cast<uintptr_t>(xbase + (size_t)hs * W + ws) & 15u) == 0);
+  Raw8<T> v[N][4];
+#pragma unroll
+  for (int u = 0; u < N; ++u) {
+    const int q4 = pl.q4[u];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const int c = c0 + q4 * 4 + k;
-      if (item < items && c < C)
-        v[u][k] = load_raw8<T>(x + ((size_t)n * C + c) * P, H, W, hs + row, ws + blk * 8);
-      else
-        v[u][k].zero();
+      v[u][k].zero();
+      if (q4 < 0) continue;
+      const int c = q4 * 4 + k;
+      if (interior) {
+        const T* src = xbase + (size_t)c * P + (size_t)(hs + pl.row[u]) * W + ws + pl.blk[u] * 8;
+        if constexpr (sizeof(T) == 2) {
+          v[u][k].u = __ldg(reinterpret_cast<const uint4*>(src));
+        } else {
+          v[u][k].a = __ldg(reinterpret_cast<const float4*>(src));
+          v[u][k].b = __ldg(reinterpret_cast<const float4*>(src) + 1);
+        }
+      } else if (c0 + c < C) {
+        v[u][k] = load_raw8<T>(xbase + (size_t)c * P, H, W, hs + pl.row[u], ws + pl.blk[u] * 8);
+      }
     }
   }
 #pragma unroll
-  for (int u = 0; u < kMaxItems; ++u) {
-    const int item = tid + u * nthreads;
-    if (item >= items) break;
-    const int blk = item & 3;
-    const int row = (item >> 2) % rows;
-    const int q4 = (item >> 2) / rows;
-    float4* dst = xr + (q4 * rows + row) * kHaloCols + blk * 8;
+  for (int u = 0; u < N; ++u) {
+    if (pl.q4[u] < 0) continue;
+    float4* dst = xr + (pl.q4[u] * rows + pl.row[u]) * kHaloCols + pl.blk[u] * 8;
 #pragma unroll
     for (int i = 0; i < 8; ++i)
       dst[i] = make_float4(v[u][0].get(i), v[u][1].get(i), v[u][2].get(i), v[u][3].get(i));
   }
+}
+
+// ------------------------------------------------------ packed FP32 math ---
+// sm_100 executes two FP32 FMAs per instruction on register pairs.
+__device__ __forceinline__ unsigned long long f2_pack(float lo, float hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(unsigned long long v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsigned long long b,
+                                                     unsigned long long c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// Two FP32 values rounded to bf16 (round to nearest even) and back, packed.
+__device__ __forceinline__ unsigned long long f2_round_bf16(float lo, float hi) {
+  uint32_t p;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(p) : "f"(hi), "f"(lo));
+  return f2_pack(__uint_as_float(p << 16), __uint_as_float(p & 0xFFFF0000u));
+}
+__device__ __forceinline__ unsigned long long f2_round_f16(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  const float2 f = __half22float2(h);
+  return f2_pack(f.x, f.y);
+}
+// Tap pair (lo, hi) as used by the filter: rounded to the I/O dtype (bf16/fp16
+// taps are rounded like the reference, `_triton_kernels.py:332-335`).
+template <typename T>
+__device__ __forceinline__ unsigned long long tap_pair(float lo, float hi) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) return f2_round_bf16(lo, hi);
+  else if constexpr (std::is_same<T, __half>::value) return f2_round_f16(lo, hi);
+  else return f2_pack(lo, hi);
 }
 
 // Round generated taps to the I/O precision (bf16 / fp16), as the reference

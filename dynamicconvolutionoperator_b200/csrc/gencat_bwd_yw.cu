@@ -269,6 +269,7 @@ gencat_bwd_y_kernel(const ByParams p) {
   } else if (warp < 6) {
     // ---- x-halo producers (per tile and 16-channel group) ------------------
     const int pt = threadIdx.x - 64;
+    const XPlan<Cfg::kXItems> plan = make_xplan<Cfg::kXItems>(xr_rows, pt, Cfg::kProducers);
     uint32_t xq = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x) {
       int n, h0, w0;
@@ -280,8 +281,8 @@ gencat_bwd_y_kernel(const ByParams p) {
           break;
         }
         float4* xr = reinterpret_cast<float4*>(smem + L.xr + xb * L.xr_bytes);
-        stage_halo<T, Cfg::kXItems>(static_cast<const T*>(p.x), xr, n, C, H, W, cg * 16, h0 - R,
-                                    w0 - 8, xr_rows, pt, Cfg::kProducers);
+        stage_halo<T, Cfg::kXItems>(plan, static_cast<const T*>(p.x), xr, n, C, H, W, cg * 16,
+                                    h0 - R, w0 - 8, xr_rows);
         tc::mbar_arrive(&x_full[xb]);
       }
     }
@@ -512,6 +513,7 @@ gencat_bwd_w_kernel(const BwParams p) {
   } else if (warp < 6) {
     // ---- x-halo producers ----------------------------------------------------
     const int pt = threadIdx.x - 64;
+    const XPlan<Cfg::kXItems> plan = make_xplan<Cfg::kXItems>(xr_rows, pt, Cfg::kProducers);
     uint32_t xq = 0;
     for (int tile = split; tile < p.num_tiles && !*abort_flag; tile += p.splits) {
       int n, h0, w0;
@@ -527,8 +529,8 @@ gencat_bwd_w_kernel(const BwParams p) {
           break;
         }
         float4* xr = reinterpret_cast<float4*>(smem + L.xr + xb * L.xr_bytes);
-        stage_halo<T, Cfg::kXItems>(static_cast<const T*>(p.x), xr, n, C, H, W, cg * 16, h0 - R,
-                                    w0 - 8, xr_rows, pt, Cfg::kProducers);
+        stage_halo<T, Cfg::kXItems>(plan, static_cast<const T*>(p.x), xr, n, C, H, W, cg * 16,
+                                    h0 - R, w0 - 8, xr_rows);
         tc::mbar_arrive(&x_full[xb]);
         ++xq;
       }
@@ -536,6 +538,7 @@ gencat_bwd_w_kernel(const BwParams p) {
   } else if (warp < 10) {
     // ---- y-tile producers (B operand, ones channel at C for db) -----------
     const int pt = threadIdx.x - 192;
+    const YPlan<Cfg::kYItems> plan = make_yplan<Cfg::kYItems>(Nw, pt, Cfg::kProducers);
     uint32_t it = 0;
     for (int tile = split; tile < p.num_tiles; tile += p.splits, ++it) {
       const int yb = it % NY;
@@ -546,9 +549,9 @@ gencat_bwd_w_kernel(const BwParams p) {
       int n, h0, w0;
       tile_origin(tile, p.tiles_w, p.tiles_h, n, h0, w0);
       uint8_t* ys = smem + L.y + yb * L.y_bytes;
-      stage_y_mn<T, Op, Cfg::kSplit, Cfg::kYItems>(static_cast<const T*>(p.y), ys,
+      stage_y_mn<T, Op, Cfg::kSplit, Cfg::kYItems>(plan, static_cast<const T*>(p.y), ys,
                                                    ys + kTileM * Nw * 2, n, C, Nw, C, H, W, h0,
-                                                   w0, pt, Cfg::kProducers);
+                                                   w0);
       tc::fence_proxy_async_smem();
       tc::mbar_arrive(&y_full[yb]);
     }

@@ -240,6 +240,7 @@ gencat_fwd_kernel(const FwdParams p) {
   } else if (warp < 2 + Cfg::kProducers / 32) {
     // ---- y-tile producers ----------------------------------------------------
     const int pt = threadIdx.x - 64;
+    const YPlan<Cfg::kYItems> plan = make_yplan<Cfg::kYItems>(Ck, pt, Cfg::kProducers);
     uint32_t it = 0;
     for (int tile = first_tile; tile < p.num_tiles; tile += tile_step, ++it) {
       const int yb = it % NY;
@@ -252,16 +253,16 @@ gencat_fwd_kernel(const FwdParams p) {
       uint8_t* ys = smem + L.y + yb * L.y_bytes;
       // 16 eight-pixel groups x Ck channels; one 16-byte smem row each.
       // MN-major interleaved: group g at g*Ck*16, channel c at (c/8)*128 + (c%8)*16.
-      stage_y_mn<T, Op, Cfg::kSplit, Cfg::kYItems>(static_cast<const T*>(p.y), ys,
+      stage_y_mn<T, Op, Cfg::kSplit, Cfg::kYItems>(plan, static_cast<const T*>(p.y), ys,
                                                    ys + kTileM * Ck * 2, n, C, Ck,
-                                                   Cfg::kBiasInGemm ? C : -1, H, W, h0, w0, pt,
-                                                   Cfg::kProducers);
+                                                   Cfg::kBiasInGemm ? C : -1, H, W, h0, w0);
       tc::fence_proxy_async_smem();
       tc::mbar_arrive(&y_full[yb]);
     }
   } else if (warp < Cfg::kFirstEpiWarp) {
     // ---- x-halo producers ----------------------------------------------------
     const int pt = threadIdx.x - 64 - Cfg::kProducers;
+    const XPlan<Cfg::kXItems> plan = make_xplan<Cfg::kXItems>(xr_rows, pt, Cfg::kProducers);
     uint32_t it = 0;
     for (int tile = first_tile; tile < p.num_tiles; tile += tile_step, ++it) {
       const int xb = it & 1;
@@ -272,8 +273,8 @@ gencat_fwd_kernel(const FwdParams p) {
       int n, h0, w0;
       tile_origin(tile, p.tiles_w, p.tiles_h, n, h0, w0);
       float4* xr = reinterpret_cast<float4*>(smem + L.xr + xb * L.xr_bytes);
-      stage_halo<T, Cfg::kXItems>(static_cast<const T*>(p.x), xr, n, C, H, W, cg * 16, h0 - R,
-                                  w0 - 8, xr_rows, pt, Cfg::kProducers);
+      stage_halo<T, Cfg::kXItems>(plan, static_cast<const T*>(p.x), xr, n, C, H, W, cg * 16,
+                                  h0 - R, w0 - 8, xr_rows);
       tc::mbar_arrive(&x_full[xb]);
     }
   } else {
@@ -310,9 +311,9 @@ gencat_fwd_kernel(const FwdParams p) {
           continue;
         }
         const int d = p.d[b];
-        float acc[16];
+        unsigned long long acc[8];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+        for (int i = 0; i < 8; ++i) acc[i] = 0ull;
 #pragma unroll
         for (int ki = 0; ki < KS; ++ki, ++tq) {
           const int j = tq % NB;
@@ -333,31 +334,32 @@ gencat_fwd_kernel(const FwdParams p) {
 #pragma unroll
           for (int kj = 0; kj < KS; ++kj) {
             const float4* cell = xrow + (kj - r) * d;
-            float xv[16];
 #pragma unroll
             for (int q4 = 0; q4 < 4; ++q4) {
               const float4 v = cell[q4 * xr_plane];
-              xv[q4 * 4 + 0] = v.x;
-              xv[q4 * 4 + 1] = v.y;
-              xv[q4 * 4 + 2] = v.z;
-              xv[q4 * 4 + 3] = v.w;
+              float g0 = dv[kj][q4 * 4 + 0], g1 = dv[kj][q4 * 4 + 1];
+              float g2 = dv[kj][q4 * 4 + 2], g3 = dv[kj][q4 * 4 + 3];
+              if constexpr (!Cfg::kBiasInGemm) {
+                const float* bs = bias_s + (b * 16 + q4 * 4) * KK + ki * KS + kj;
+                g0 += bs[0];
+                g1 += bs[KK];
+                g2 += bs[2 * KK];
+                g3 += bs[3 * KK];
+              }
+              acc[q4 * 2 + 0] = f2_fma(tap_pair<T>(g0, g1), f2_pack(v.x, v.y), acc[q4 * 2 + 0]);
+              acc[q4 * 2 + 1] = f2_fma(tap_pair<T>(g2, g3), f2_pack(v.z, v.w), acc[q4 * 2 + 1]);
             }
-            if constexpr (!Cfg::kBiasInGemm) {
-              const float* bs = bias_s + b * 16 * KK + ki * KS + kj;
-#pragma unroll
-              for (int cl = 0; cl < 16; ++cl) dv[kj][cl] += bs[cl * KK];
-            }
-            round_taps<T>(dv[kj]);
-#pragma unroll
-            for (int cl = 0; cl < 16; ++cl) acc[cl] = fmaf(dv[kj][cl], xv[cl], acc[cl]);
           }
         }
         if (failed) break;
         if (px_ok) {
 #pragma unroll
-          for (int cl = 0; cl < 16; ++cl) {
-            const int c = cg * 16 + cl;
-            if (c < C) on[(size_t)((b + 1) * C + c) * P + pix] = from_f32<T>(acc[cl]);
+          for (int i = 0; i < 8; ++i) {
+            float a0, a1;
+            f2_unpack(acc[i], a0, a1);
+            const int c = cg * 16 + 2 * i;
+            if (c < C) on[(size_t)((b + 1) * C + c) * P + pix] = from_f32<T>(a0);
+            if (c + 1 < C) on[(size_t)((b + 1) * C + c + 1) * P + pix] = from_f32<T>(a1);
           }
         }
       }
