@@ -55,6 +55,10 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _c_int,
         [_c_ptr] * 8 + [_c_size] + [_c_int] * 4 + [_c_int] * 5 + [_c_ptr],
     ),
+    "ddpm_gencat_bwd_yw_static": (
+        _c_int,
+        [_c_ptr] * 7 + [_c_int] * 4 + [_c_int] * 5 + [_c_ptr],
+    ),
     "ddpm_umma_selftest": (
         _c_int, [_c_int, _c_ptr, _c_ptr, _c_ptr, _c_int, _c_int, _c_int, _c_ptr]
     ),

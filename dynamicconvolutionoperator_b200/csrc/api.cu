@@ -50,6 +50,9 @@ int gencat_bwd_yw(const void* x, const void* y, const void* wpack, const void* g
                   void* gw, void* gb, void* workspace, size_t ws_bytes, int n, int c, int h, int w,
                   int ks, int d0, int d1, int d2, int dt, cudaStream_t st);
 
+int gencat_bwd_yw_static(const void* x, const void* y, const void* wpack, const void* gout,
+                         void* gy, void* gw, void* gb, int n, int c, int h, int w, int ks, int d0,
+                         int d1, int d2, int dt, cudaStream_t st);
 }  // namespace ddpm
 
 extern "C" {
@@ -122,6 +125,16 @@ int ddpm_gencat_bwd_yw(const void* x, const void* y, const void* packed, const v
   return ddpm::gencat_bwd_yw(x, y, packed, grad_out, grad_y, grad_weight, grad_bias, workspace,
                              workspace_bytes, n, c, h, w, ksize, d0, d1, d2, dtype,
                              static_cast<cudaStream_t>(stream));
+}
+
+int ddpm_gencat_bwd_yw_static(const void* x, const void* y, const void* packed,
+                              const void* grad_out, void* grad_y, void* grad_weight,
+                              void* grad_bias, int n, int c, int h, int w, int ksize, int d0,
+                              int d1, int d2, int dtype, void* stream) {
+  ddpm::clear_error();
+  return ddpm::gencat_bwd_yw_static(x, y, packed, grad_out, grad_y, grad_weight, grad_bias, n, c,
+                                    h, w, ksize, d0, d1, d2, dtype,
+                                    static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

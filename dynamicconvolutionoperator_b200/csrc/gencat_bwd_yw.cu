@@ -26,6 +26,8 @@
 // channel at index C so column C of D_w is db) accumulates over all tiles of
 // the split; partials go to a workspace and a short kernel reduces them into
 // the Conv2d weight layout.
+#include <mutex>
+
 #include "common.cuh"
 #include "tc.cuh"
 #include "gencat.cuh"
@@ -823,6 +825,138 @@ int gencat_bwd_yw(const void* x, const void* y, const void* wpack, const void* g
     }
   }
   return DDPM_OK;
+}
+
+// --------------------------------------------- no-allocation variant -----
+// gencat_bwd_yw_static computes the same dY, dW and db as gencat_bwd_yw but
+// keeps the FP32 weight-gradient partials in a fixed file-scope device array
+// instead of a caller-provided workspace, so the call itself allocates no
+// device memory. It serves hosts that cannot hand us a workspace: a plain C
+// caller that only owns the tensors of the step (no allocator of its own), or
+// a step loop that must not call cudaMalloc because that call can synchronise
+// the whole device and stall work queued on other streams.
+//
+// Limits and contract:
+//  * the scratch is kStaticScratchBytes (8 MiB) per device. The spatial split
+//    count of the weight-gradient reduction is capped so that
+//    splits * groups * 128 * Nw FP32 partials fit; a shape whose single split
+//    would not fit is rejected with DDPM_ERR_WORKSPACE (cannot happen within
+//    the fused kernels' C <= 64, K <= 3 limits: one split is at most 640 KiB).
+//    Fewer splits than the workspace path means fewer CTAs on the dW kernel,
+//    so this variant is slower on large images; the summation order differs
+//    from gencat_bwd_yw's, so dW / db agree to FP32 rounding, not bit for bit.
+//  * nothing in the scratch needs to start at zero: every partial the reduce
+//    kernel reads is written by the dW kernel earlier in the same call.
+//  * the scratch is shared by every call on a device. Two calls whose kernels
+//    can overlap (different streams without ordering, or several host
+//    threads) race on it and corrupt each other's dW / db; callers must
+//    order them, e.g. by issuing them on one stream.
+//  * the device address of the scratch is looked up once per device, on the
+//    first call made while that device is current, with
+//    cudaGetSymbolAddress; that first call should therefore come before any
+//    stream capture is begun on the device.
+namespace {
+
+constexpr size_t kStaticScratchBytes = size_t(8) << 20;
+constexpr int kMaxScratchDevices = 64;
+
+__device__ __align__(256) unsigned char g_bwd_static_scratch[kStaticScratchBytes];
+
+std::mutex g_static_scratch_mu;
+void* g_static_scratch_addr[kMaxScratchDevices] = {};
+
+// Device address of this device's scratch, looked up on first use.
+int static_scratch(void** out) {
+  int dev = -1;
+  DDPM_CUDA_TRY(cudaGetDevice(&dev));
+  DDPM_CHECK_ARG(dev >= 0 && dev < kMaxScratchDevices, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_static_scratch_mu);
+  if (g_static_scratch_addr[dev] == nullptr) {
+    void* addr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&addr, g_bwd_static_scratch);
+    if (e != cudaSuccess || addr == nullptr)
+      return set_error(DDPM_ERR_CUDA, "cudaGetSymbolAddress(static scratch) failed: %s",
+                       cudaGetErrorString(e));
+    g_static_scratch_addr[dev] = addr;
+  }
+  *out = g_static_scratch_addr[dev];
+  return DDPM_OK;
+}
+
+}  // namespace
+
+int gencat_bwd_yw_static(const void* x, const void* y, const void* wpack, const void* gout,
+                         void* gy, void* gw, void* gb, int n, int c, int h, int w, int ks, int d0,
+                         int d1, int d2, int dt, cudaStream_t st) {
+  int rc = gencat::check_shape(n, c, h, w, ks, d0, d1, d2, dt);
+  if (rc) return rc;
+  DDPM_CHECK_ARG(x && y && wpack && gout, "null pointer");
+  DDPM_CHECK_ARG((gw == nullptr) == (gb == nullptr),
+                 "grad_weight and grad_bias must both be given");
+  void* scratch = nullptr;
+  rc = static_scratch(&scratch);
+  if (rc) return rc;
+  // dY needs no scratch: the workspace path's dY launch is used as is.
+  if (gy != nullptr) {
+    rc = gencat_bwd_yw(x, y, wpack, gout, gy, nullptr, nullptr, nullptr, 0, n, c, h, w, ks, d0,
+                       d1, d2, dt, st);
+    if (rc) return rc;
+  }
+  if (gw == nullptr) return DDPM_OK;
+
+  const gencat::PackLayout pl = gencat::PackLayout::make(c, ks, dt);
+  WPlan q = plan_w(n, c, h, w, ks);
+  const size_t split_bytes = (size_t)pl.NG * 128 * q.Nw * sizeof(float);
+  if (split_bytes > kStaticScratchBytes)
+    return set_error(DDPM_ERR_WORKSPACE,
+                     "shape needs %zu bytes of static scratch, the limit is %zu bytes",
+                     split_bytes, kStaticScratchBytes);
+  const int max_splits = (int)(kStaticScratchBytes / split_bytes);
+  if (q.splits > max_splits) q.splits = max_splits;
+  int* status = nullptr;
+  rc = gencat::status_ptr(&status);
+  if (rc) return rc;
+
+  BwParams wp{};
+  wp.x = x;
+  wp.y = y;
+  wp.gout = gout;
+  wp.partial = static_cast<float*>(scratch);
+  wp.N = n;
+  wp.C = c;
+  wp.H = h;
+  wp.W = w;
+  wp.Cp = pl.Cp;
+  wp.Nw = q.Nw;
+  wp.R = (ks / 2) * max3(d0, d1, d2);
+  wp.d[0] = d0;
+  wp.d[1] = d1;
+  wp.d[2] = d2;
+  wp.tiles_w = (w + gencat::kTileW - 1) / gencat::kTileW;
+  wp.tiles_h = (h + gencat::kTileH - 1) / gencat::kTileH;
+  wp.num_tiles = n * wp.tiles_w * wp.tiles_h;
+  wp.ngroups = pl.NG;
+  wp.gb = q.gb;
+  wp.splits = q.splits;
+  wp.status = status;
+  switch (dt * 10 + ks) {
+    case DDPM_BF16 * 10 + 1: rc = launch_w<__nv_bfloat16, 1>(wp, q.nbatches, st); break;
+    case DDPM_BF16 * 10 + 3: rc = launch_w<__nv_bfloat16, 3>(wp, q.nbatches, st); break;
+    case DDPM_F16 * 10 + 1: rc = launch_w<__half, 1>(wp, q.nbatches, st); break;
+    case DDPM_F16 * 10 + 3: rc = launch_w<__half, 3>(wp, q.nbatches, st); break;
+    case DDPM_F32 * 10 + 1: rc = launch_w<float, 1>(wp, q.nbatches, st); break;
+    case DDPM_F32 * 10 + 3: rc = launch_w<float, 3>(wp, q.nbatches, st); break;
+    default: rc = set_error(DDPM_ERR_UNSUPPORTED, "unsupported dtype/kernel size");
+  }
+  if (rc) return rc;
+  switch (dt) {
+    case DDPM_BF16:
+      return launch_reduce<__nv_bfloat16>(wp.partial, gw, gb, c, ks, pl.NG, q.Nw, q.splits, st);
+    case DDPM_F16:
+      return launch_reduce<__half>(wp.partial, gw, gb, c, ks, pl.NG, q.Nw, q.splits, st);
+    default:
+      return launch_reduce<float>(wp.partial, gw, gb, c, ks, pl.NG, q.Nw, q.splits, st);
+  }
 }
 
 }  // namespace ddpm

@@ -161,6 +161,30 @@ DDPM_API int ddpm_gencat_bwd_yw(const void* x, const void* y, const void* packed
                                 void* stream);
 
 /*
+ * No-allocation variant of ddpm_gencat_bwd_yw (no counterpart in the
+ * reference, whose Triton backward allocates its partials with torch).
+ * Same arguments and results minus the workspace: the FP32 dW/db partials
+ * live in an 8 MiB static device array inside the library, so the call
+ * allocates nothing. For hosts that own no allocator, or that must not call
+ * cudaMalloc mid-step because it can synchronise the device.
+ *  - The split count of the dW reduction is capped to fit the 8 MiB; shapes
+ *    whose single split does not fit return DDPM_ERR_WORKSPACE. dW/db match
+ *    ddpm_gencat_bwd_yw to FP32 rounding (different summation order).
+ *  - Nothing needs to start at zero: every partial read is written earlier
+ *    in the same call.
+ *  - The scratch is shared per device: overlapping calls (unordered streams,
+ *    several host threads) race and corrupt dW/db; order them.
+ *  - The first call on a device (with that device current) looks up the
+ *    scratch's device address; make it before any stream capture begins.
+ */
+DDPM_API int ddpm_gencat_bwd_yw_static(const void* x, const void* y, const void* packed,
+                                       const void* grad_out, void* grad_y,
+                                       void* grad_weight, void* grad_bias,
+                                       int n, int c, int h, int w,
+                                       int ksize, int d0, int d1, int d2, int dtype,
+                                       void* stream);
+
+/*
  * Diagnostic (no reference counterpart): one 128 x n x k bf16 tcgen05 UMMA
  * on a single CTA with the operand layouts the fused kernels use.
  * a: [128 + shift, k] row-major bf16, b: [n, k] row-major bf16,
