@@ -74,3 +74,20 @@ def test_ctor_keeps_reference_attributes():
     assert m.recompute is False and m.fused_generator_inference is False
     assert m.fused_generator_training is True and m.dilations == (1, 3, 5)
     assert drop_in.DDPM is DDPM
+
+
+def test_fuse_bias_fold_matches_conv2d():
+    """The bias-folded fuse conv equals ``nn.Conv2d`` (values and gradients)."""
+    from dynamicconvolutionoperator_b200.ddpm import _fuse_single_rounding
+
+    gen = torch.Generator().manual_seed(3)
+    cat = torch.randn(2, 16, 7, 9, generator=gen, dtype=torch.float64, requires_grad=True)
+    wt = torch.randn(4, 16, 3, 3, generator=gen, dtype=torch.float64, requires_grad=True)
+    b = torch.randn(4, generator=gen, dtype=torch.float64, requires_grad=True)
+    g = torch.randn(2, 4, 7, 9, generator=gen, dtype=torch.float64)
+    got = _fuse_single_rounding(cat, wt, b)
+    ref = torch.nn.functional.conv2d(cat, wt, b, 1, 1)
+    torch.testing.assert_close(got, ref, rtol=1e-12, atol=1e-12)
+    for a, e in zip(torch.autograd.grad(got, (cat, wt, b), g),
+                    torch.autograd.grad(ref, (cat, wt, b), g)):
+        torch.testing.assert_close(a, e, rtol=1e-12, atol=1e-12)
