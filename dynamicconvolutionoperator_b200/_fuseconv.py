@@ -1,0 +1,110 @@
+"""Native 3x3 fuse convolution of the DDPM (``nn.Conv2d(4C, C, 3, 1, 1)``).
+
+The reference leaves this convolution to cuDNN (``triton_impl.py:294, 392``).
+On B200 that call runs true FP32 on cuDNN's FFT / SIMT kernels (about 2 ms of
+a 3 ms training step at 256^2) and, for bf16 / fp16 outputs, adds the bias
+after the convolution has been rounded (two roundings). ``fuse_conv`` runs it
+on the library's tensor-core kernels instead (``ddpm_fuseconv_*`` in
+``include/ddpm_b200.h``): FP32 as bf16 hi + lo operands, the bias added to the
+FP32 accumulator before a single output rounding. Same parameters, same
+autograd contract as ``nn.Conv2d``.
+
+The weight gradient still goes through ``torch.nn.grad.conv2d_weight``.
+"""
+
+from __future__ import annotations
+
+import weakref
+
+import torch
+
+from . import _lib
+
+FUSE_MAX_CIN = 256
+FUSE_MAX_COUT = 64
+
+_cache: dict[tuple, tuple] = {}
+
+
+def fuse_conv_supported(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None) -> bool:
+    """Shapes and dtypes the native kernels cover (stride 1, padding 1, 3x3)."""
+    return (
+        x.is_cuda
+        and x.ndim == 4
+        and x.dtype in _lib.DTYPE_CODE
+        and weight.dtype == x.dtype
+        and (bias is None or bias.dtype == x.dtype)
+        and tuple(weight.shape[2:]) == (3, 3)
+        and weight.shape[1] == x.shape[1]
+        and weight.shape[0] <= FUSE_MAX_COUT
+        and weight.shape[1] <= FUSE_MAX_CIN
+    )
+
+
+def pack_fuse_weight(weight: torch.Tensor, use_cache: bool) -> torch.Tensor:
+    """The weight in the kernels' shared-memory operand layout (forward and
+    data-gradient images), reused while the same tensor is unchanged."""
+    key = (weight.data_ptr(), weight.device, weight.dtype, tuple(weight.shape))
+    if use_cache:
+        hit = _cache.get(key)
+        if hit is not None and hit[0]() is weight and hit[1] == weight._version:
+            return hit[2]
+    cout, cin = weight.shape[0], weight.shape[1]
+    code = _lib.dtype_code(weight.dtype)
+    nbytes = int(_lib.load().ddpm_fuseconv_pack_bytes(cin, cout, code))
+    packed = torch.empty(nbytes, dtype=torch.uint8, device=weight.device)
+    w = weight.contiguous()
+    _lib.call("ddpm_fuseconv_pack", w.data_ptr(), cin, cout, code, packed.data_ptr(), nbytes,
+              _lib.stream_handle(weight.device))
+    if use_cache:
+        _cache.clear()
+        _cache[key] = (weakref.ref(weight), weight._version, packed)
+    return packed
+
+
+class _FuseConv(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, bias, use_cache):
+        x = x.contiguous()
+        n, cin, h, w = x.shape
+        cout = weight.shape[0]
+        packed = pack_fuse_weight(weight, use_cache)
+        out = torch.empty((n, cout, h, w), dtype=x.dtype, device=x.device)
+        b = bias.contiguous() if bias is not None else None
+        _lib.call("ddpm_fuseconv_fwd", x.data_ptr(), packed.data_ptr(),
+                  b.data_ptr() if b is not None else None, out.data_ptr(),
+                  n, cin, cout, h, w, _lib.dtype_code(x.dtype), _lib.stream_handle(x.device))
+        ctx.save_for_backward(x, weight)
+        ctx.packed = packed
+        ctx.has_bias = bias is not None
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        x, weight = ctx.saved_tensors
+        g = grad_out.contiguous()
+        n, cin, h, w = x.shape
+        cout = weight.shape[0]
+        gx = gw = gb = None
+        if ctx.needs_input_grad[0]:
+            gx = torch.empty_like(x)
+            _lib.call("ddpm_fuseconv_bwd_data", g.data_ptr(), ctx.packed.data_ptr(),
+                      gx.data_ptr(), n, cin, cout, h, w, _lib.dtype_code(x.dtype),
+                      _lib.stream_handle(x.device))
+        if ctx.needs_input_grad[1]:
+            gw = torch.nn.grad.conv2d_weight(x, weight.shape, g, 1, 1)
+        if ctx.has_bias and ctx.needs_input_grad[2]:
+            gb = g.sum(dim=(0, 2, 3))
+        return gx, gw, gb, None
+
+
+def fuse_conv(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None) -> torch.Tensor:
+    """``F.conv2d(x, weight, bias, 1, 1)`` for a 3x3 weight on the native kernels."""
+    _lib.load()
+    grad = torch.is_grad_enabled() and (
+        x.requires_grad or weight.requires_grad or (bias is not None and bias.requires_grad)
+    )
+    return _FuseConv.apply(x, weight, bias, not grad)
+
+
+__all__ = ["fuse_conv", "fuse_conv_supported", "pack_fuse_weight"]

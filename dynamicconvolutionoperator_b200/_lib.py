@@ -59,6 +59,10 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _c_int,
         [_c_ptr] * 7 + [_c_int] * 4 + [_c_int] * 5 + [_c_ptr],
     ),
+    "ddpm_fuseconv_pack_bytes": (_c_size, [_c_int] * 3),
+    "ddpm_fuseconv_pack": (_c_int, [_c_ptr, _c_int, _c_int, _c_int, _c_ptr, _c_size, _c_ptr]),
+    "ddpm_fuseconv_fwd": (_c_int, [_c_ptr] * 4 + [_c_int] * 6 + [_c_ptr]),
+    "ddpm_fuseconv_bwd_data": (_c_int, [_c_ptr] * 3 + [_c_int] * 6 + [_c_ptr]),
     "ddpm_umma_selftest": (
         _c_int, [_c_int, _c_ptr, _c_ptr, _c_ptr, _c_int, _c_int, _c_int, _c_ptr]
     ),

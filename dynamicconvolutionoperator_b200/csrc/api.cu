@@ -53,6 +53,13 @@ int gencat_bwd_yw(const void* x, const void* y, const void* wpack, const void* g
 int gencat_bwd_yw_static(const void* x, const void* y, const void* wpack, const void* gout,
                          void* gy, void* gw, void* gb, int n, int c, int h, int w, int ks, int d0,
                          int d1, int d2, int dt, cudaStream_t st);
+size_t fuseconv_pack_bytes(int cin, int cout, int dt);
+int fuseconv_pack(const void* w, int cin, int cout, int dt, void* packed, size_t bytes,
+                  cudaStream_t st);
+int fuseconv_fwd(const void* cat, const void* packed, const void* bias, void* out, int n, int cin,
+                 int cout, int h, int w, int dt, cudaStream_t st);
+int fuseconv_dgrad(const void* gout, const void* packed, void* gcat, int n, int cin, int cout,
+                   int h, int w, int dt, cudaStream_t st);
 }  // namespace ddpm
 
 extern "C" {
@@ -135,6 +142,31 @@ int ddpm_gencat_bwd_yw_static(const void* x, const void* y, const void* packed,
   return ddpm::gencat_bwd_yw_static(x, y, packed, grad_out, grad_y, grad_weight, grad_bias, n, c,
                                     h, w, ksize, d0, d1, d2, dtype,
                                     static_cast<cudaStream_t>(stream));
+}
+
+size_t ddpm_fuseconv_pack_bytes(int cin, int cout, int dtype) {
+  return ddpm::fuseconv_pack_bytes(cin, cout, dtype);
+}
+
+int ddpm_fuseconv_pack(const void* weight, int cin, int cout, int dtype, void* packed,
+                       size_t packed_bytes, void* stream) {
+  ddpm::clear_error();
+  return ddpm::fuseconv_pack(weight, cin, cout, dtype, packed, packed_bytes,
+                             static_cast<cudaStream_t>(stream));
+}
+
+int ddpm_fuseconv_fwd(const void* x, const void* packed, const void* bias, void* out, int n,
+                      int cin, int cout, int h, int w, int dtype, void* stream) {
+  ddpm::clear_error();
+  return ddpm::fuseconv_fwd(x, packed, bias, out, n, cin, cout, h, w, dtype,
+                            static_cast<cudaStream_t>(stream));
+}
+
+int ddpm_fuseconv_bwd_data(const void* grad_out, const void* packed, void* grad_x, int n,
+                           int cin, int cout, int h, int w, int dtype, void* stream) {
+  ddpm::clear_error();
+  return ddpm::fuseconv_dgrad(grad_out, packed, grad_x, n, cin, cout, h, w, dtype,
+                              static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

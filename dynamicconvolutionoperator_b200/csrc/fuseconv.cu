@@ -1,0 +1,610 @@
+// Native 3x3 "fuse" convolution of the DDPM (4C -> C, stride 1, zero pad 1).
+// Replaces the cuDNN call `self.fuse(cat_out)` (reference `triton_impl.py:294,
+// 392`) and its backward (cuDNN dgrad + wgrad):
+//
+//   out[o, p]   = bias[o] + sum_{t, i} W[o, i, t] * cat[i, p + off(t)]
+//   dcat[i, p]  = sum_{t, o} W[o, i, t] * dout[o, p - off(t)]
+//   dW[o, i, t] = sum_p dout[o, p] * cat[i, p + off(t)]     (fuseconv_wgrad.cu)
+//   off(t) = (ky - 1, kx - 1), t = ky * 3 + kx, zero outside the image.
+//
+// Why native: in true FP32 (no TF32) cuDNN runs this convolution on its FFT
+// and SIMT paths, ~2 ms of a ~3 ms training step at 256^2 on B200; and for
+// 16-bit outputs `nn.Conv2d` adds the bias after the convolution has already
+// been rounded, so the output is rounded twice. Here the convolution runs on
+// the tensor cores (FP32 via bf16 hi + lo operands, 3 MMAs per step) and the
+// bias is added to the FP32 accumulator before the single output rounding.
+//
+// Forward and data gradient are the same shifted-window GEMM (as in the fused
+// generator's dX kernel): a unit is TWO consecutive output rows h0, h0 + 1 of
+// 128 pixels (w0 .. w0 + 127); the 4 source rows they need (h0 - 1 .. h0 + 2)
+// x 144 columns (w0 - 8 .. w0 + 135) of one channel slab are staged in the
+// K-major interleaved operand layout [slab channel/8][row][pixel][8] (one
+// 16-byte row = 8 channels of one pixel), so the A operand of tap t for output
+// row h0 + mh is a descriptor whose start moves by whole pixel rows. Each tap
+// and slab is one M=128 x N x K=slab GEMM per output row; the weight chunk of
+// (slab, tap) is shared by both rows. Weights are pre-packed per weight
+// version into the exact shared-memory B images and streamed by bulk copies.
+//
+// Warp roles (14 warps): w0 = TMEM allocator + weight producer, w1 = MMA
+// issuer, w2-w5 = slab producers, w6-w13 = two epilogue warpgroups (one per
+// output row of the unit).
+#include "common.cuh"
+#include "tc.cuh"
+#include "gencat.cuh"
+#include "fuseconv.cuh"
+
+namespace ddpm {
+namespace {
+
+using namespace gencat;
+
+constexpr int kSeg = fuseconv::kSeg;
+constexpr int kRows = 4;           // staged source rows per unit
+constexpr int kMaxRegBufs = 4;
+constexpr int kMaxWStages = 16;
+
+struct FcParams {
+  const void* src;      // staged tensor: cat (forward) or dout (data gradient)
+  const uint8_t* wimg;  // packed B image of this pass
+  const void* bias;     // forward only (nullptr for the data gradient)
+  void* dst;
+  int N, H, W;
+  int Csrc;             // channels of src (GEMM K before padding)
+  int Cdst;             // channels of dst
+  int KC, nslab;        // slab channels, slabs
+  int Nn;               // MMA N = dst channels per unit (<= 128)
+  int nhalf;            // dst channel blocks of Nn (data gradient: ceil(Cin / 128))
+  int tiles_w, hpairs, num_units;
+  int reg_bufs, w_stages;
+  uint32_t reg_part, reg_bytes, w_chunk;
+  int* status;
+};
+
+struct FcSmem {
+  uint32_t reg, w, bias, bars, total;
+};
+
+__host__ __device__ inline FcSmem fc_smem_layout(const FcParams& p) {
+  FcSmem L;
+  L.reg = 0;
+  L.w = L.reg + p.reg_bufs * p.reg_bytes;
+  L.bias = L.w + p.w_stages * p.w_chunk;
+  L.bars = L.bias + 128 * 4;
+  L.total = L.bars + 8 * (2 * kMaxRegBufs + 2 * kMaxWStages + 4);
+  return L;
+}
+
+// Transpose 8 channels x 8 pixels (one Raw8 per channel) into 8 operand rows
+// of 8 channels each, at dst + px * 16 (and the bf16 residual at + lo_off).
+template <typename T, typename Op, bool kSplit>
+__device__ __forceinline__ void store_transposed(uint8_t* dst, uint32_t lo_off,
+                                                 const Raw8<T> (&v)[8]) {
+  if constexpr (sizeof(T) == 2 && !kSplit) {
+    const uint32_t* w[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) w[e] = reinterpret_cast<const uint32_t*>(&v[e].u);
+#pragma unroll
+    for (int px = 0; px < 8; ++px) {
+      const uint32_t sel = (px & 1) ? 0x7632u : 0x5410u;
+      uint4 row;
+      row.x = __byte_perm(w[0][px >> 1], w[1][px >> 1], sel);
+      row.y = __byte_perm(w[2][px >> 1], w[3][px >> 1], sel);
+      row.z = __byte_perm(w[4][px >> 1], w[5][px >> 1], sel);
+      row.w = __byte_perm(w[6][px >> 1], w[7][px >> 1], sel);
+      *reinterpret_cast<uint4*>(dst + px * 16) = row;
+    }
+  } else {
+#pragma unroll
+    for (int px = 0; px < 8; ++px) {
+      float col[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) col[e] = v[e].get(px);
+      store8_split<Op, kSplit>(dst + px * 16, dst + lo_off + px * 16, col);
+    }
+  }
+}
+
+template <typename T, bool kDgrad>
+struct FcCfg {
+  static constexpr bool kSplit = IoTraits<T>::kSplit;
+  // K slab: input channels (forward) or output channels (data gradient)
+  static constexpr int KC = kDgrad ? (kSplit ? 32 : 64) : (kSplit ? 16 : 32);
+  static constexpr int kSteps = KC / 16;
+  static constexpr int kProducers = 256;
+  static constexpr int kItems = (KC / 8) * kRows * (kSeg / 8);  // 8 channels x 8 pixels each
+  static constexpr int kItemsMax = sizeof(T) == 4 ? 1 : 2;      // per thread and round
+  static constexpr int kRounds = (kItems + kProducers * kItemsMax - 1) / (kProducers * kItemsMax);
+  static constexpr int kFirstProducerWarp = 3;
+  static constexpr int kFirstEpiWarp = kFirstProducerWarp + kProducers / 32;
+  static constexpr int kThreads = 32 * (kFirstEpiWarp + 4);
+};
+
+// kDgrad = false: forward (window of tap (ky, kx) for output row h0 + mh starts
+// at source row h0 + mh + ky - 1, column + kx - 1); true: data gradient
+// (source row h0 + mh - ky + 1, column - kx + 1).
+//
+// Two MMA issuer warps, one per output row: a tcgen05.mma costs its issuing
+// thread ~55 cycles, so with N <= 128 a single issuer would leave the tensor
+// pipe idle between instructions. Their inner loops are unrolled over taps
+// and K steps with descriptors advanced by constants.
+template <typename T, bool kDgrad>
+__global__ void __launch_bounds__(FcCfg<T, kDgrad>::kThreads, 1)
+fuseconv_kernel(const FcParams p) {
+  using Cfg = FcCfg<T, kDgrad>;
+  using Op = typename IoTraits<T>::Op;
+  constexpr bool kSplit = Cfg::kSplit;
+  constexpr int KC = Cfg::KC;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ uint32_t tmem_base_s;
+  __shared__ int abort_s;
+
+  const FcSmem L = fc_smem_layout(p);
+  const int NR = p.reg_bufs, S = p.w_stages, Nn = p.Nn;
+  const int H = p.H, W = p.W;
+  const size_t P = (size_t)H * W;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint64_t* r_full = bars;                    // [NR]
+  uint64_t* r_empty = bars + kMaxRegBufs;     // [NR]
+  uint64_t* w_full = bars + 2 * kMaxRegBufs;  // [S]
+  uint64_t* w_empty = w_full + kMaxWStages;   // [S]
+  uint64_t* t_full = w_empty + kMaxWStages;   // [2]
+  uint64_t* t_empty = t_full + 2;             // [2]
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (warp == 0) {
+    tc::tmem_alloc(&tmem_base_s, 512);
+    tc::tmem_relinquish();
+  }
+  if (threadIdx.x == 32) {
+    for (int i = 0; i < NR; ++i) {
+      tc::mbar_init(&r_full[i], Cfg::kProducers);
+      tc::mbar_init(&r_empty[i], 2);
+    }
+    for (int i = 0; i < S; ++i) {
+      tc::mbar_init(&w_full[i], 1);
+      tc::mbar_init(&w_empty[i], 2);
+    }
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(&t_full[i], 2);
+      tc::mbar_init(&t_empty[i], 128);
+    }
+    tc::fence_mbar_init();
+    abort_s = 0;
+  }
+  {
+    float* bias_s = reinterpret_cast<float*>(smem + L.bias);
+    const T* bias = static_cast<const T*>(p.bias);
+    for (int i = threadIdx.x; i < 128; i += blockDim.x)
+      bias_s[i] = (bias != nullptr && i < p.Cdst) ? to_f32<T>(bias[i]) : 0.f;
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem_base = tmem_base_s;
+  volatile int* abort_flag = &abort_s;
+  const int chunks = p.nslab * 9;  // weight chunks per unit
+
+  if (warp == 0) {
+    // ---- weight producer ------------------------------------------------------
+    if (lane == 0) {
+      uint32_t wq = 0;
+      for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
+        const int half = u % p.nhalf;
+        const uint8_t* base = p.wimg + (size_t)half * chunks * p.w_chunk;
+        for (int q = 0; q < chunks; ++q, ++wq) {
+          const int s = wq % S;
+          if (!tc::mbar_wait(&w_empty[s], ((wq / S) & 1) ^ 1, abort_flag, kWaitNs)) {
+            fail(abort_flag, p.status, 60);
+            goto done;
+          }
+          tc::mbar_arrive_expect_tx(&w_full[s], p.w_chunk);
+          tc::bulk_g2s(smem + L.w + s * p.w_chunk, base + (size_t)q * p.w_chunk, p.w_chunk,
+                       &w_full[s]);
+        }
+      }
+    }
+  } else if (warp < Cfg::kFirstProducerWarp) {
+    // ---- MMA issuers: warp 1 -> output row h0, warp 2 -> row h0 + 1 ----------
+    if (lane == 0) {
+      const int mh = warp - 1;
+      const uint32_t idesc = tc::idesc_f16(128, Nn, IoTraits<T>::kBf16, false, false);
+      constexpr uint32_t a_lbo = kRows * kSeg * 16;  // channel-group stride of a slab
+      const uint32_t b_lbo = Nn * 16;                // channel-group stride of a weight chunk
+      // descriptor increments (units of 16 bytes)
+      constexpr uint64_t a_step = (2 * a_lbo) >> 4;  // one K step (16 channels)
+      const uint64_t b_step = (2 * b_lbo) >> 4;
+      const uint64_t a_lo = p.reg_part >> 4;          // hi -> lo part of the slab
+      const uint64_t b_lo = (Nn * KC * 2) >> 4;       // hi -> lo part of a weight chunk
+      uint32_t wq = 0, rq = 0, ti = 0;
+      for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++ti) {
+        const int tb = ti & 1;
+        if (!tc::mbar_wait(&t_empty[tb], ((ti >> 1) & 1) ^ 1, abort_flag, kWaitNs)) {
+          fail(abort_flag, p.status, 61);
+          goto done;
+        }
+        tc::tc_fence_after();
+        const uint32_t d = tmem_base + tb * 256 + mh * 128;
+        for (int sl = 0; sl < p.nslab; ++sl, ++rq) {
+          const int rb = rq % NR;
+          if (!tc::mbar_wait(&r_full[rb], (rq / NR) & 1, abort_flag, kWaitNs)) {
+            fail(abort_flag, p.status, 62);
+            goto done;
+          }
+          tc::tc_fence_after();
+          const uint64_t a_base =
+              tc::smem_desc(tc::smem_u32(smem + L.reg + rb * p.reg_bytes), a_lbo, 128);
+#pragma unroll
+          for (int t = 0; t < 9; ++t) {
+            const int s = (wq + t) % S;
+            if (!tc::mbar_wait(&w_full[s], ((wq + t) / S) & 1, abort_flag, kWaitNs)) {
+              fail(abort_flag, p.status, 63);
+              goto done;
+            }
+            tc::tc_fence_after();
+            const int ky = t / 3, kx = t % 3;
+            const int seg = kDgrad ? (mh - ky + 2) : (mh + ky);
+            const int col = kDgrad ? (9 - kx) : (7 + kx);
+            const uint64_t ad = a_base + (uint64_t)(seg * kSeg + col);
+            const uint64_t bd = tc::smem_desc(tc::smem_u32(smem + L.w + s * p.w_chunk), b_lbo, 128);
+#pragma unroll
+            for (int ks = 0; ks < Cfg::kSteps; ++ks) {
+              const uint32_t acc = (sl > 0 || t > 0 || ks > 0) ? 1u : 0u;
+              tc::mma_f16(d, ad + ks * a_step, bd + ks * b_step, idesc, acc);
+              if constexpr (kSplit) {
+                tc::mma_f16(d, ad + a_lo + ks * a_step, bd + ks * b_step, idesc, 1u);
+                tc::mma_f16(d, ad + ks * a_step, bd + b_lo + ks * b_step, idesc, 1u);
+              }
+            }
+            tc::mma_commit(&w_empty[s]);
+          }
+          wq += 9;
+          tc::mma_commit(&r_empty[rb]);
+        }
+        tc::mma_commit(&t_full[tb]);
+      }
+    }
+  } else if (warp < Cfg::kFirstEpiWarp) {
+    // ---- slab producers (256 threads) -----------------------------------------
+    const int pt = threadIdx.x - 32 * Cfg::kFirstProducerWarp;
+    const T* src = static_cast<const T*>(p.src);
+    uint32_t rq = 0;
+    for (int u = blockIdx.x; u < p.num_units && !*abort_flag; u += gridDim.x) {
+      const int v_ = u / p.nhalf;
+      const int wt = v_ % p.tiles_w;
+      const int hp = (v_ / p.tiles_w) % p.hpairs;
+      const int n = v_ / (p.tiles_w * p.hpairs);
+      const int h0 = 2 * hp, w0 = wt * 128;
+      const T* srcn = src + (size_t)n * p.Csrc * P;
+      for (int sl = 0; sl < p.nslab; ++sl, ++rq) {
+        const int rb = rq % NR;
+        uint8_t* reg = smem + L.reg + rb * p.reg_bytes;
+        bool failed = false;
+#pragma unroll 1
+        for (int round = 0; round < Cfg::kRounds; ++round) {
+          const int base = round * Cfg::kProducers * Cfg::kItemsMax;
+          // loads first: they do not depend on the buffer being free
+          Raw8<T> v[Cfg::kItemsMax][8];
+#pragma unroll
+          for (int k = 0; k < Cfg::kItemsMax; ++k) {
+            const int item = base + k * Cfg::kProducers + pt;
+            const int jb = item % (kSeg / 8);
+            const int seg = (item / (kSeg / 8)) % kRows;
+            const int kg = item / ((kSeg / 8) * kRows);
+            const int hr = h0 - 1 + seg;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const int c = sl * KC + kg * 8 + e;
+              if (item < Cfg::kItems && c < p.Csrc)
+                v[k][e] = load_raw8<T>(srcn + (size_t)c * P, H, W, hr, w0 - 8 + jb * 8);
+              else
+                v[k][e].zero();
+            }
+          }
+          if (round == 0 && !warp_wait(&r_empty[rb], ((rq / NR) & 1) ^ 1, abort_flag)) {
+            fail(abort_flag, p.status, 64);
+            failed = true;
+            break;
+          }
+#pragma unroll
+          for (int k = 0; k < Cfg::kItemsMax; ++k) {
+            const int item = base + k * Cfg::kProducers + pt;
+            if (item >= Cfg::kItems) continue;
+            const int jb = item % (kSeg / 8);
+            const int seg = (item / (kSeg / 8)) % kRows;
+            const int kg = item / ((kSeg / 8) * kRows);
+            const uint32_t off = ((kg * kRows + seg) * kSeg + jb * 8) * 16;
+            store_transposed<T, Op, kSplit>(reg + off, p.reg_part, v[k]);
+          }
+        }
+        if (failed) break;
+        tc::fence_proxy_async_smem();
+        tc::mbar_arrive(&r_full[rb]);
+      }
+    }
+  } else {
+    // ---- epilogue (128 threads): both output rows of a unit ------------------
+    const int quad = warp & 3;
+    const int m = quad * 32 + lane;
+    const float* bias_s = reinterpret_cast<const float*>(smem + L.bias);
+    T* dst = static_cast<T*>(p.dst);
+    uint32_t ti = 0;
+    for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++ti) {
+      const int half = u % p.nhalf;
+      const int v_ = u / p.nhalf;
+      const int wt = v_ % p.tiles_w;
+      const int hp = (v_ / p.tiles_w) % p.hpairs;
+      const int n = v_ / (p.tiles_w * p.hpairs);
+      const int w = wt * 128 + m;
+      const int tb = ti & 1;
+      if (!warp_wait(&t_full[tb], (ti >> 1) & 1, abort_flag)) {
+        fail(abort_flag, p.status, 65);
+        break;
+      }
+      tc::tc_fence_after();
+      const int c0 = half * Nn;
+#pragma unroll 1
+      for (int mh = 0; mh < 2; ++mh) {
+        const int h = 2 * hp + mh;
+        const bool ok = h < H && w < W;
+        const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + tb * 256 + mh * 128;
+        T* out = dst + ((size_t)n * p.Cdst + c0) * P + (size_t)h * W + w;
+        for (int blk = 0; blk < Nn; blk += 32) {
+          float a[2][16];
+          tc::tmem_ld16(taddr + blk, a[0]);
+          tc::tmem_ld16(taddr + blk + 16, a[1]);
+          tc::tmem_ld_wait();
+          if (ok) {
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+              for (int e = 0; e < 16; ++e) {
+                const int c = blk + hh * 16 + e;
+                const float bv = kDgrad ? 0.f : bias_s[c];
+                if (c0 + c < p.Cdst) out[(size_t)c * P] = from_f32<T>(a[hh][e] + bv);
+              }
+          }
+        }
+      }
+      tc::tc_fence_before();
+      tc::mbar_arrive(&t_empty[tb]);
+    }
+  }
+done:
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem_base, 512);
+  }
+}
+
+// ------------------------------------------------------------- weight pack ----
+// One thread per 16-byte B-operand row (8 K-dimension values).
+template <typename T>
+__global__ void fuseconv_pack_kernel(const T* __restrict__ w, typename IoTraits<T>::Op* out,
+                                     fuseconv::Layout L) {
+  using Op = typename IoTraits<T>::Op;
+  const long long fwd_rows = (long long)L.fwd_bytes / 16;
+  const long long total = (long long)(L.fwd_bytes + L.dg_bytes) / 16;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    int o0, i0, t, part;  // first element; the 8 values run over i (forward) or o (dgrad)
+    bool run_i;
+    if (idx < fwd_rows) {
+      // chunk (slab, tap): [part][KC/8][Np][8]
+      const long long per_chunk = (long long)L.parts * (L.KC / 8) * L.Np;
+      const long long ch = idx / per_chunk;
+      long long r = idx % per_chunk;
+      part = (int)(r / ((L.KC / 8) * L.Np));
+      r %= (L.KC / 8) * L.Np;
+      const int kg = (int)(r / L.Np);
+      o0 = (int)(r % L.Np);
+      const int slab = (int)(ch / 9);
+      t = (int)(ch % 9);
+      i0 = slab * L.KC + kg * 8;
+      run_i = true;
+    } else {
+      // chunk (half, slab, tap): [part][KD/8][128][8]
+      const long long j = idx - fwd_rows;
+      const long long per_chunk = (long long)L.parts * (L.KD / 8) * 128;
+      const long long ch = j / per_chunk;
+      long long r = j % per_chunk;
+      part = (int)(r / ((L.KD / 8) * 128));
+      r %= (L.KD / 8) * 128;
+      const int kg = (int)(r / 128);
+      const int il = (int)(r % 128);
+      const int half = (int)(ch / (L.nslabD * 9));
+      const int slab = (int)((ch / 9) % L.nslabD);
+      t = (int)(ch % 9);
+      i0 = half * 128 + il;
+      o0 = slab * L.KD + kg * 8;
+      run_i = false;
+    }
+    union {
+      uint4 u;
+      Op e[8];
+    } row;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int o = run_i ? o0 : o0 + e;
+      const int i = run_i ? i0 + e : i0;
+      float v = 0.f;
+      if (o < L.Cout && i < L.Cin) v = to_f32<T>(w[((size_t)o * L.Cin + i) * 9 + t]);
+      const Op hi = op_from<Op>(v);
+      row.e[e] = part == 0 ? hi : op_from<Op>(v - op_to<Op>(hi));
+    }
+    reinterpret_cast<uint4*>(out)[idx] = row.u;
+  }
+}
+
+template <typename T, bool kDgrad>
+int launch_conv(FcParams prm, cudaStream_t st) {
+  const FcSmem L = fc_smem_layout(prm);
+  auto fn = fuseconv_kernel<T, kDgrad>;
+  DDPM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total));
+  const int grid = prm.num_units < num_sms() ? prm.num_units : num_sms();
+  fn<<<grid, FcCfg<T, kDgrad>::kThreads, L.total, st>>>(prm);
+  DDPM_CHECK_LAUNCH(kDgrad ? "fuseconv_dgrad_kernel" : "fuseconv_fwd_kernel");
+  return DDPM_OK;
+}
+
+template <typename T>
+int dispatch_conv(bool dgrad, const FcParams& prm, cudaStream_t st) {
+  return dgrad ? launch_conv<T, true>(prm, st) : launch_conv<T, false>(prm, st);
+}
+
+int check_conv(int n, int cin, int cout, int h, int w, int dt) {
+  DDPM_CHECK_ARG(n >= 1 && h >= 1 && w >= 1 && cin >= 1 && cout >= 1, "sizes must be positive");
+  DDPM_CHECK_ARG(dtype_size(dt) > 0, "unknown dtype code %d", dt);
+  if (cin > fuseconv::kMaxCin || cout > fuseconv::kMaxCout)
+    return set_error(DDPM_ERR_UNSUPPORTED, "native fuse conv supports Cin <= %d, Cout <= %d",
+                     fuseconv::kMaxCin, fuseconv::kMaxCout);
+  DDPM_CHECK_ARG((long long)n * ((h + 1) / 2) * ((w + 127) / 128) * 2 < (1LL << 31),
+                 "too many tiles");
+  return DDPM_OK;
+}
+
+FcParams common_params(int n, int h, int w, int nhalf, int* status) {
+  FcParams q{};
+  q.N = n;
+  q.H = h;
+  q.W = w;
+  q.tiles_w = (w + 127) / 128;
+  q.hpairs = (h + 1) / 2;
+  q.nhalf = nhalf;
+  q.num_units = n * q.hpairs * q.tiles_w * nhalf;
+  q.status = status;
+  return q;
+}
+
+int dispatch_dt(int dt, bool dgrad, const FcParams& prm, cudaStream_t st) {
+  switch (dt) {
+    case DDPM_BF16: return dispatch_conv<__nv_bfloat16>(dgrad, prm, st);
+    case DDPM_F16: return dispatch_conv<__half>(dgrad, prm, st);
+    case DDPM_F32: return dispatch_conv<float>(dgrad, prm, st);
+  }
+  return set_error(DDPM_ERR_INVALID_ARG, "unknown dtype %d", dt);
+}
+
+}  // namespace
+
+namespace fuseconv {
+
+Layout Layout::make(int cin, int cout, int dt) {
+  Layout L{};
+  const bool split = dt == DDPM_F32;
+  L.Cin = cin;
+  L.Cout = cout;
+  L.parts = split ? 2 : 1;
+  L.Np = (cout + 15) / 16 * 16;
+  L.KC = split ? 16 : 32;
+  L.nslab = (cin + L.KC - 1) / L.KC;
+  L.KD = split ? 32 : 64;
+  L.nslabD = (cout + L.KD - 1) / L.KD;
+  L.nhalf = (cin + 127) / 128;
+  L.fwd_chunk = (size_t)L.parts * L.KC * L.Np * 2;
+  L.dg_chunk = (size_t)L.parts * L.KD * 128 * 2;
+  L.fwd_bytes = (size_t)L.nslab * 9 * L.fwd_chunk;
+  L.dg_bytes = (size_t)L.nhalf * L.nslabD * 9 * L.dg_chunk;
+  return L;
+}
+
+}  // namespace fuseconv
+
+size_t fuseconv_pack_bytes(int cin, int cout, int dt) {
+  if (cin < 1 || cout < 1 || cin > fuseconv::kMaxCin || cout > fuseconv::kMaxCout ||
+      dtype_size(dt) == 0)
+    return 0;
+  const fuseconv::Layout L = fuseconv::Layout::make(cin, cout, dt);
+  return L.fwd_bytes + L.dg_bytes;
+}
+
+int fuseconv_pack(const void* w, int cin, int cout, int dt, void* packed, size_t bytes,
+                  cudaStream_t st) {
+  int rc = check_conv(1, cin, cout, 1, 1, dt);
+  if (rc) return rc;
+  DDPM_CHECK_ARG(w && packed, "null pointer");
+  DDPM_CHECK_ARG((reinterpret_cast<uintptr_t>(packed) & 15u) == 0,
+                 "packed weight buffer must be 16-byte aligned");
+  const fuseconv::Layout L = fuseconv::Layout::make(cin, cout, dt);
+  if (bytes < L.fwd_bytes + L.dg_bytes)
+    return set_error(DDPM_ERR_WORKSPACE, "packed weight buffer too small (%zu < %zu)", bytes,
+                     L.fwd_bytes + L.dg_bytes);
+  const long long rows = (long long)(L.fwd_bytes + L.dg_bytes) / 16;
+  const int threads = 256;
+  const long long want = (rows + threads - 1) / threads;
+  const int blocks = (int)(want < 4096 ? want : 4096);
+  switch (dt) {
+    case DDPM_BF16:
+      fuseconv_pack_kernel<__nv_bfloat16><<<blocks, threads, 0, st>>>(
+          static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(packed), L);
+      break;
+    case DDPM_F16:
+      fuseconv_pack_kernel<__half><<<blocks, threads, 0, st>>>(
+          static_cast<const __half*>(w), static_cast<__half*>(packed), L);
+      break;
+    default:
+      fuseconv_pack_kernel<float><<<blocks, threads, 0, st>>>(
+          static_cast<const float*>(w), static_cast<__nv_bfloat16*>(packed), L);
+  }
+  DDPM_CHECK_LAUNCH("fuseconv_pack_kernel");
+  return DDPM_OK;
+}
+
+int fuseconv_fwd(const void* cat, const void* packed, const void* bias, void* out, int n, int cin,
+                 int cout, int h, int w, int dt, cudaStream_t st) {
+  int rc = check_conv(n, cin, cout, h, w, dt);
+  if (rc) return rc;
+  DDPM_CHECK_ARG(cat && packed && out, "null pointer");
+  int* status = nullptr;
+  rc = gencat::status_ptr(&status);
+  if (rc) return rc;
+  const fuseconv::Layout L = fuseconv::Layout::make(cin, cout, dt);
+  FcParams q = common_params(n, h, w, 1, status);
+  q.src = cat;
+  q.wimg = static_cast<const uint8_t*>(packed);
+  q.bias = bias;
+  q.dst = out;
+  q.Csrc = cin;
+  q.Cdst = cout;
+  q.KC = L.KC;
+  q.nslab = L.nslab;
+  q.Nn = L.Np;
+  q.reg_part = (uint32_t)L.KC * kRows * kSeg * 2;
+  q.reg_bytes = q.reg_part * L.parts;
+  q.reg_bufs = 3;
+  q.w_chunk = (uint32_t)L.fwd_chunk;
+  q.w_stages = 16;
+  return dispatch_dt(dt, false, q, st);
+}
+
+int fuseconv_dgrad(const void* gout, const void* packed, void* gcat, int n, int cin, int cout,
+                   int h, int w, int dt, cudaStream_t st) {
+  int rc = check_conv(n, cin, cout, h, w, dt);
+  if (rc) return rc;
+  DDPM_CHECK_ARG(gout && packed && gcat, "null pointer");
+  int* status = nullptr;
+  rc = gencat::status_ptr(&status);
+  if (rc) return rc;
+  const fuseconv::Layout L = fuseconv::Layout::make(cin, cout, dt);
+  FcParams q = common_params(n, h, w, L.nhalf, status);
+  q.src = gout;
+  q.wimg = static_cast<const uint8_t*>(packed) + L.fwd_bytes;
+  q.bias = nullptr;
+  q.dst = gcat;
+  q.Csrc = cout;
+  q.Cdst = cin;
+  q.KC = L.KD;
+  q.nslab = L.nslabD;
+  q.Nn = 128;
+  q.reg_part = (uint32_t)L.KD * kRows * kSeg * 2;
+  q.reg_bytes = q.reg_part * L.parts;
+  q.reg_bufs = 2;
+  q.w_chunk = (uint32_t)L.dg_chunk;
+  q.w_stages = 4;
+  return dispatch_dt(dt, true, q, st);
+}
+
+}  // namespace ddpm

@@ -1,0 +1,32 @@
+// Shared definitions of the native 3x3 fuse convolution (fuseconv*.cu).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+
+namespace ddpm {
+namespace fuseconv {
+
+constexpr int kSeg = 144;      // staged pixels per source row (128 + 8 on each side)
+constexpr int kMaxCin = 256;   // 4C for C <= 64
+constexpr int kMaxCout = 64;
+
+// Packed weight images (one per weight version), back to back:
+//   forward B chunks   [slab][tap][part][KC/8][Np][8]          (K = input channels)
+//   data-grad chunks   [half][slab][tap][part][KD/8][128][8]   (K = output channels)
+// `part` = 2 (bf16 hi + residual lo) for FP32 weights, else 1.
+struct Layout {
+  int Cin, Cout, parts;
+  int Np;           // output channels padded to 16 (forward MMA N)
+  int KC, nslab;    // forward K slab (input channels) and slab count
+  int KD, nslabD;   // data-gradient K slab (output channels) and slab count
+  int nhalf;        // data-gradient N blocks of 128 input channels
+  size_t fwd_chunk, dg_chunk, fwd_bytes, dg_bytes;
+  static Layout make(int cin, int cout, int dt);
+};
+
+}  // namespace fuseconv
+
+size_t fuseconv_pack_bytes(int cin, int cout, int dt);
+
+}  // namespace ddpm

@@ -11,8 +11,9 @@ What changed is the GPU body: the Triton kernels, autotune tables and the
 silent CPU fallback (``triton_impl.py:23-33, 353-354``) are replaced by the
 sm_100a kernels of ``libddpm_b200.so``. CUDA tensors always take the native
 path; CPU tensors raise (the reference's CPU branches are not part of this
-build). The final 3x3 ``fuse`` convolution stays a PyTorch/cuDNN call, as in
-the reference (``triton_impl.py:294, 392``).
+build). The final 3x3 ``fuse`` convolution (a cuDNN call in the reference,
+``triton_impl.py:294, 392``) runs on the library's own tensor-core kernels for
+C <= 64 (``native_fuse=True``, the default) and on cuDNN otherwise.
 """
 
 from __future__ import annotations
@@ -20,7 +21,7 @@ from __future__ import annotations
 import torch
 from torch import nn
 
-from . import _kernels
+from . import _fuseconv, _kernels
 
 _DEFAULT_DILATIONS = (1, 3, 5)
 
@@ -60,6 +61,9 @@ class DDPM(nn.Module):
         fused_generator_training: ``None`` (default) picks the path from the
             measured crossover, ``True`` always uses the flash-style recompute
             training path, ``False`` always materialises the taps.
+        native_fuse: Run the 3x3 ``fuse`` convolution on this library's
+            tensor-core kernels (C <= 64; single rounding of conv + bias, no
+            TF32). ``False`` keeps the reference's cuDNN call.
     """
 
     def __init__(
@@ -72,6 +76,7 @@ class DDPM(nn.Module):
         recompute: bool = True,
         fused_generator_inference: bool = True,
         fused_generator_training: bool | None = None,
+        native_fuse: bool = True,
     ) -> None:
         super().__init__()
         if kernel_size < 1 or kernel_size % 2 == 0:
@@ -86,6 +91,7 @@ class DDPM(nn.Module):
         self.recompute = recompute
         self.fused_generator_inference = fused_generator_inference
         self.fused_generator_training = fused_generator_training
+        self.native_fuse = native_fuse
         self.dilations = _DEFAULT_DILATIONS
         self.generator = nn.Conv2d(dim, 3 * dim * kernel_size**2, 1)
         self.fuse = nn.Conv2d(4 * dim, dim, 3, 1, 1)
@@ -145,6 +151,12 @@ class DDPM(nn.Module):
             )
         cat_out = self._cuda_cat(x, y)
         fuse = self.fuse
+        if (
+            self.native_fuse
+            and not _autocast_enabled()
+            and _fuseconv.fuse_conv_supported(cat_out, fuse.weight, fuse.bias)
+        ):
+            return _fuseconv.fuse_conv(cat_out, fuse.weight, fuse.bias)
         if (
             cat_out.dtype in (torch.bfloat16, torch.float16)
             and fuse.weight.dtype == cat_out.dtype

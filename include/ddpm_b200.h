@@ -161,6 +161,26 @@ DDPM_API int ddpm_gencat_bwd_yw(const void* x, const void* y, const void* packed
                                 void* stream);
 
 /*
+ * Native 3x3 fuse convolution (stride 1, zero padding 1, Cin <= 256,
+ * Cout <= 64), replacing the cuDNN call `self.fuse(cat_out)` of
+ * `triton_impl.py:294, 392` and its backward. FP32 runs on the tensor cores as
+ * bf16 hi + lo operands (3 MMAs per step, no TF32); the bias is added to the
+ * FP32 accumulator before the one output rounding. Weights are packed once
+ * per weight version (ddpm_fuseconv_pack_bytes() bytes, 16-byte aligned).
+ *   weight [Cout, Cin, 3, 3], bias [Cout] (may be NULL), x/grad_x [N, Cin, H, W],
+ *   out/grad_out [N, Cout, H, W], all of `dtype`.
+ */
+DDPM_API size_t ddpm_fuseconv_pack_bytes(int cin, int cout, int dtype);
+DDPM_API int ddpm_fuseconv_pack(const void* weight, int cin, int cout, int dtype,
+                                void* packed, size_t packed_bytes, void* stream);
+DDPM_API int ddpm_fuseconv_fwd(const void* x, const void* packed, const void* bias, void* out,
+                               int n, int cin, int cout, int h, int w, int dtype, void* stream);
+/* grad_x[i, p] = sum_{o, t} W[o, i, t] * grad_out[o, p - off(t)] */
+DDPM_API int ddpm_fuseconv_bwd_data(const void* grad_out, const void* packed, void* grad_x,
+                                    int n, int cin, int cout, int h, int w, int dtype,
+                                    void* stream);
+
+/*
  * No-allocation variant of ddpm_gencat_bwd_yw (no counterpart in the
  * reference, whose Triton backward allocates its partials with torch).
  * Same arguments and results minus the workspace: the FP32 dW/db partials

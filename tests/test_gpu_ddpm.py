@@ -88,3 +88,13 @@ def test_cfg4_training_256(dtype, fused):
     stats, fails = ddpm_parity((1, 64, 256, 256), 3, dtype, seed=30, input_seed=31,
                                fused_generator_training=fused)
     _assert_ok(stats, fails)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("ks", [1, 3])
+def test_cudnn_fuse_path_training(dtype, ks):
+    """``native_fuse=False``: the fuse conv through cuDNN (bias folded into the
+    contraction for 16-bit outputs), every gradient within tolerance."""
+    stats, fails = ddpm_parity((2, 24, 15, 17), ks, dtype, seed=7, input_seed=8,
+                               native_fuse=False)
+    _assert_ok(stats, fails)

@@ -1,0 +1,92 @@
+"""Native 3x3 fuse convolution (forward and data gradient) against a float64
+reference of the same convolution (``nn.Conv2d(4C, C, 3, 1, 1)``,
+reference ``triton_impl.py:294``), through the C ABI."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+# (n, cin, cout, h, w): DDPM shapes (cin = 4 * cout) plus ragged edges
+SHAPES = [
+    (2, 96, 24, 15, 17),
+    (1, 12, 3, 5, 7),
+    (1, 256, 64, 64, 64),
+    (3, 160, 40, 33, 130),
+    (1, 256, 64, 256, 256),
+    (1, 64, 16, 1, 1),
+    (2, 200, 50, 9, 257),
+]
+# fp32: bf16 hi + lo operands (~1e-5 relative per product); 16-bit: one output
+# rounding of the FP32 accumulator (half an ulp) plus accumulation order.
+TOL = {torch.float32: (2e-5, 2e-4), torch.bfloat16: (8e-3, 2e-2), torch.float16: (1e-3, 4e-3)}
+
+
+def _inputs(shape, dtype, seed=0):
+    n, cin, cout, h, w = shape
+    gen = torch.Generator().manual_seed(seed)
+    x = torch.randn((n, cin, h, w), generator=gen).to(dtype)
+    bound = 1.0 / (cin * 9) ** 0.5
+    wt = ((torch.rand((cout, cin, 3, 3), generator=gen) * 2 - 1) * bound).to(dtype)
+    b = ((torch.rand(cout, generator=gen) * 2 - 1) * bound).to(dtype)
+    g = torch.randn((n, cout, h, w), generator=gen).to(dtype)
+    return x, wt, b, g
+
+
+def _pack(wt, cin, cout, dtype):
+    from dynamicconvolutionoperator_b200 import _lib
+
+    nbytes = int(_lib.load().ddpm_fuseconv_pack_bytes(cin, cout, _lib.dtype_code(dtype)))
+    packed = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    _lib.call("ddpm_fuseconv_pack", wt.data_ptr(), cin, cout, _lib.dtype_code(dtype),
+              packed.data_ptr(), nbytes, _lib.stream_handle(packed.device))
+    return packed
+
+
+@pytest.mark.parametrize("shape", SHAPES)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_fuseconv_forward(shape, dtype):
+    from dynamicconvolutionoperator_b200 import _lib
+
+    n, cin, cout, h, w = shape
+    x, wt, b, _ = _inputs(shape, dtype)
+    xd, wd, bd = x.cuda(), wt.cuda(), b.cuda()
+    packed = _pack(wd, cin, cout, dtype)
+    out = torch.full((n, cout, h, w), float("nan"), dtype=dtype, device="cuda")
+    _lib.call("ddpm_fuseconv_fwd", xd.data_ptr(), packed.data_ptr(), bd.data_ptr(),
+              out.data_ptr(), n, cin, cout, h, w, _lib.dtype_code(dtype),
+              _lib.stream_handle(out.device))
+    torch.cuda.synchronize()
+    gold = F.conv2d(xd.double(), wd.double(), bd.double(), 1, 1)
+    rtol, atol = TOL[dtype]
+    torch.testing.assert_close(out.double(), gold, rtol=rtol, atol=atol)
+
+
+@pytest.mark.parametrize("shape", SHAPES)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_fuseconv_bwd_data(shape, dtype):
+    from dynamicconvolutionoperator_b200 import _lib
+
+    n, cin, cout, h, w = shape
+    x, wt, _, g = _inputs(shape, dtype, seed=1)
+    wd, gd = wt.cuda(), g.cuda()
+    packed = _pack(wd, cin, cout, dtype)
+    gx = torch.full((n, cin, h, w), float("nan"), dtype=dtype, device="cuda")
+    _lib.call("ddpm_fuseconv_bwd_data", gd.data_ptr(), packed.data_ptr(), gx.data_ptr(),
+              n, cin, cout, h, w, _lib.dtype_code(dtype), _lib.stream_handle(gx.device))
+    torch.cuda.synchronize()
+    gold = torch.nn.grad.conv2d_input((n, cin, h, w), wd.double(), gd.double(), 1, 1)
+    rtol, atol = TOL[dtype]
+    torch.testing.assert_close(gx.double(), gold, rtol=rtol, atol=atol)
+
+
+def test_fuseconv_rejects_unsupported():
+    from dynamicconvolutionoperator_b200 import _lib
+
+    lib = _lib.load()
+    assert lib.ddpm_fuseconv_pack_bytes(257, 64, 0) == 0
+    rc = lib.ddpm_fuseconv_fwd(None, None, None, None, 1, 256, 65, 4, 4, 0, None)
+    assert rc == -2
