@@ -27,6 +27,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ddpm_version": (_c_int, []),
     "ddpm_last_error": (ctypes.c_char_p, []),
     "ddpm_launch_count": (ctypes.c_ulonglong, []),
+    "ddpm_device_status": (_c_int, [_c_int, ctypes.POINTER(ctypes.c_int)]),
     "ddpm_dyncat_fwd": (
         _c_int,
         [_c_ptr, _c_int, _c_ptr, _c_int, _c_ptr] + [_c_int] * 4 + [_c_int] * 4 + [_c_ptr],
@@ -106,6 +107,14 @@ def call(name: str, *args) -> None:
     if rc != 0:
         msg = lib.ddpm_last_error().decode(errors="replace")
         raise RuntimeError(f"{name} failed (code {rc}): {msg}")
+
+
+def device_status(reset: bool = True) -> int:
+    """Failure code recorded by a bounded wait inside a kernel (0 = none) on
+    the current device; synchronises. With ``reset`` the code is cleared."""
+    code = ctypes.c_int(0)
+    call("ddpm_device_status", 1 if reset else 0, ctypes.byref(code))
+    return code.value
 
 
 def launch_count() -> int:

@@ -60,6 +60,9 @@ int fuseconv_fwd(const void* cat, const void* packed, const void* bias, void* ou
                  int cout, int h, int w, int dt, cudaStream_t st);
 int fuseconv_dgrad(const void* gout, const void* packed, void* gcat, int n, int cin, int cout,
                    int h, int w, int dt, cudaStream_t st);
+namespace gencat {
+int read_status(int reset, int* code);
+}
 }  // namespace ddpm
 
 extern "C" {
@@ -167,6 +170,11 @@ int ddpm_fuseconv_bwd_data(const void* grad_out, const void* packed, void* grad_
   ddpm::clear_error();
   return ddpm::fuseconv_dgrad(grad_out, packed, grad_x, n, cin, cout, h, w, dtype,
                               static_cast<cudaStream_t>(stream));
+}
+
+int ddpm_device_status(int reset, int* code) {
+  ddpm::clear_error();
+  return ddpm::gencat::read_status(reset, code);
 }
 
 }  // extern "C"

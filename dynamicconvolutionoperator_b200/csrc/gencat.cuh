@@ -442,6 +442,7 @@ __device__ __forceinline__ void round_taps(float (&v)[16]) {
 // Host helpers (gencat_common.cu).
 int check_shape(int n, int c, int h, int w, int ks, int d0, int d1, int d2, int dt);
 int status_ptr(int** out);
+int read_status(int reset, int* code);
 int num_sms();
 
 }  // namespace gencat

@@ -21,8 +21,10 @@
 // Epilogue warpgroup h owns the 16-channel blocks h, h+2 of every chunk and
 // multiplies with g_b at q - o read through L1.
 //
-// Warp roles (14 warps): w0 = TMEM allocator + weight producer, w1 = MMA
-// issuer, w2-w5 = region producers, w6-w13 = two epilogue warpgroups.
+// Warp roles (15 warps): w0 = TMEM allocator + weight producer, w1-w2 = MMA
+// issuers (even / odd chunks: one thread issuing N=Cp MMAs back to back
+// leaves the tensor pipe idle ~half the time), w3-w6 = region producers,
+// w7-w14 = two epilogue warpgroups.
 #include "common.cuh"
 #include "tc.cuh"
 #include "gencat.cuh"
@@ -41,7 +43,9 @@ struct BxCfg {
   static constexpr int kRegBufs = kSplit ? 1 : 2;
   static constexpr int kWStages = 6;
   static constexpr bool kBiasInGemm = !kSplit;
-  static constexpr int kFirstEpiWarp = 6;
+  static constexpr int kIssuers = 2;        // MMA issuer warps (alternate chunks)
+  static constexpr int kFirstProducerWarp = 1 + kIssuers;
+  static constexpr int kFirstEpiWarp = kFirstProducerWarp + 4;
   static constexpr int kThreads = 32 * (kFirstEpiWarp + 8);
 };
 
@@ -113,7 +117,7 @@ gencat_bwd_x_kernel(const BxParams p) {
   if (threadIdx.x == 32) {
     for (int i = 0; i < 2; ++i) {
       tc::mbar_init(&r_full[i], 128);
-      tc::mbar_init(&r_empty[i], 1);
+      tc::mbar_init(&r_empty[i], Cfg::kIssuers);
     }
     for (int i = 0; i < S; ++i) {
       tc::mbar_init(&w_full[i], 1);
@@ -160,13 +164,18 @@ gencat_bwd_x_kernel(const BxParams p) {
         }
       }
     }
-  } else if (warp == 1) {
-    // ---- MMA issuer --------------------------------------------------------
+  } else if (warp < Cfg::kFirstProducerWarp) {
+    // ---- MMA issuers: warp 1 + i issues the chunks q with q % 2 == i --------
     if (lane == 0) {
+      const uint32_t me = warp - 1;
       const uint32_t idesc = tc::idesc_f16(kTileM, Cp, IoTraits<T>::kBf16, false, false);
       const uint32_t a_lbo = KS * kSeg * 16;    // channel-group stride of the region
       const uint32_t b_lbo = Cp * 16;           // channel-group stride of a weight chunk
-      const uint32_t wpart = Cp * Ck * 2;
+      const uint64_t a_step = (2 * a_lbo) >> 4;  // descriptor advance per K step
+      const uint64_t b_step = (2 * b_lbo) >> 4;
+      const uint64_t a_lo = L.reg_part >> 4;     // hi -> lo part offsets
+      const uint64_t b_lo = (Cp * Ck * 2) >> 4;
+      const int nks = Ck / 16;
       uint32_t wq = 0, tq = 0, rq = 0;
       for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
         for (int b = 0; b < 3; ++b, ++rq) {
@@ -176,9 +185,11 @@ gencat_bwd_x_kernel(const BxParams p) {
             goto done;
           }
           tc::tc_fence_after();
-          const uint32_t ra = tc::smem_u32(smem + L.reg + rb * L.reg_bytes);
+          const uint64_t a_base =
+              tc::smem_desc(tc::smem_u32(smem + L.reg + rb * L.reg_bytes), a_lbo, 128);
           const int d = p.d[b];
           for (int tap = 0; tap < KK; ++tap, ++wq, ++tq) {
+            if ((wq & 1u) != me) continue;
             const int s = wq % S;
             const int j = tq % NB;
             if (!tc::mbar_wait(&w_full[s], (wq / S) & 1, abort_flag, kWaitNs) ||
@@ -190,18 +201,16 @@ gencat_bwd_x_kernel(const BxParams p) {
             const int ki = tap / KS, kj = tap % KS;
             const int dx = (kj - r) * d;
             // window: row segment ki, pixels (8 - dx) .. (8 - dx) + 127
-            const uint32_t a0 = ra + (uint32_t)(ki * kSeg + 8 - dx) * 16;
-            const uint32_t wb = tc::smem_u32(smem + L.w + s * L.w_bytes);
+            const uint64_t ad = a_base + (uint64_t)(ki * kSeg + 8 - dx);
+            const uint64_t bd =
+                tc::smem_desc(tc::smem_u32(smem + L.w + s * L.w_bytes), b_lbo, 128);
             const uint32_t dt = tmem_base + j * Cp;
-            for (int ks = 0; ks < Ck / 16; ++ks) {
-              const uint64_t a_hi = tc::smem_desc(a0 + ks * 2 * a_lbo, a_lbo, 128);
-              const uint64_t b_hi = tc::smem_desc(wb + ks * 2 * b_lbo, b_lbo, 128);
-              tc::mma_f16(dt, a_hi, b_hi, idesc, ks > 0 ? 1u : 0u);
+            // plain runtime loop (no MMA under a per-step condition in an unrolled loop)
+            for (int ks = 0; ks < nks; ++ks) {
+              tc::mma_f16(dt, ad + ks * a_step, bd + ks * b_step, idesc, ks > 0 ? 1u : 0u);
               if constexpr (Cfg::kSplit) {
-                const uint64_t a_lo = tc::smem_desc(a0 + L.reg_part + ks * 2 * a_lbo, a_lbo, 128);
-                const uint64_t b_lo = tc::smem_desc(wb + wpart + ks * 2 * b_lbo, b_lbo, 128);
-                tc::mma_f16(dt, a_lo, b_hi, idesc, 1u);
-                tc::mma_f16(dt, a_hi, b_lo, idesc, 1u);
+                tc::mma_f16(dt, ad + a_lo + ks * a_step, bd + ks * b_step, idesc, 1u);
+                tc::mma_f16(dt, ad + ks * a_step, bd + b_lo + ks * b_step, idesc, 1u);
               }
             }
             tc::mma_commit(&w_empty[s]);
@@ -213,7 +222,7 @@ gencat_bwd_x_kernel(const BxParams p) {
     }
   } else if (warp < Cfg::kFirstEpiWarp) {
     // ---- region producers (128 threads) ------------------------------------
-    const int pt = threadIdx.x - 64;
+    const int pt = threadIdx.x - 32 * Cfg::kFirstProducerWarp;
     const T* y = static_cast<const T*>(p.y);
     const int ones_c = Cfg::kBiasInGemm ? C : -1;
     uint32_t rq = 0;

@@ -230,7 +230,8 @@ gencat_bwd_y_kernel(const ByParams p) {
     if (lane == 0) {
       const uint32_t idesc = tc::idesc_f16(kTileM, Cp, IoTraits<T>::kBf16, false, false);
       const uint32_t b_lbo = Cp * 16;
-      const uint32_t wpart = 128 * Cp * 2;
+      const uint64_t b_step = (2 * b_lbo) >> 4;      // descriptor advance per K step
+      const uint64_t b_lo = (128 * Cp * 2) >> 4;     // hi -> lo part of a weight group
       uint32_t wq = 0, kq = 0, it = 0;
       for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
         const int tb = it & 1;
@@ -248,18 +249,19 @@ gencat_bwd_y_kernel(const ByParams p) {
             goto done;
           }
           tc::tc_fence_after();
-          const uint32_t ka = tc::smem_u32(smem + L.dk + ks_ * L.dk_bytes);
-          const uint32_t wb = tc::smem_u32(smem + L.w + s * L.w_bytes);
+          // A: dK, K-major (rows are K): row-group stride 128, pixel-group stride 2048
+          const uint64_t ad =
+              tc::smem_desc(tc::smem_u32(smem + L.dk + ks_ * L.dk_bytes), 128, 2048);
+          const uint64_t bd = tc::smem_desc(tc::smem_u32(smem + L.w + s * L.w_bytes), b_lbo, 128);
+          const uint32_t acc0 = g > 0 ? 1u : 0u;
+#pragma unroll
           for (int ks = 0; ks < 8; ++ks) {
-            // A: dK, K-major (rows are K): row-group stride 128, pixel-group stride 2048
-            const uint64_t a_hi = tc::smem_desc(ka + ks * 256, 128, 2048);
-            const uint64_t b_hi = tc::smem_desc(wb + ks * 2 * b_lbo, b_lbo, 128);
-            tc::mma_f16(dt, a_hi, b_hi, idesc, (g > 0 || ks > 0) ? 1u : 0u);
+            const uint64_t a_k = ad + ks * (256 >> 4);
+            const uint64_t b_k = bd + ks * b_step;
+            tc::mma_f16(dt, a_k, b_k, idesc, ks > 0 ? 1u : acc0);
             if constexpr (Cfg::kSplit) {
-              const uint64_t a_lo = tc::smem_desc(ka + kDkBytes + ks * 256, 128, 2048);
-              const uint64_t b_lo = tc::smem_desc(wb + wpart + ks * 2 * b_lbo, b_lbo, 128);
-              tc::mma_f16(dt, a_lo, b_hi, idesc, 1u);
-              tc::mma_f16(dt, a_hi, b_lo, idesc, 1u);
+              tc::mma_f16(dt, a_k + (kDkBytes >> 4), b_k, idesc, 1u);
+              tc::mma_f16(dt, a_k, b_k + b_lo, idesc, 1u);
             }
           }
           tc::mma_commit(&k_empty[ks_]);
@@ -473,7 +475,8 @@ gencat_bwd_w_kernel(const BwParams p) {
     if (lane == 0) {
       const uint32_t idesc = tc::idesc_f16(kTileM, Nw, IoTraits<T>::kBf16, true, false);
       const uint32_t b_lbo = Nw * 16;          // pixel-group stride of the y tile
-      const uint32_t ypart = kTileM * Nw * 2;
+      const uint64_t b_step = (2 * b_lbo) >> 4;  // descriptor advance per K step
+      const uint64_t y_lo = (kTileM * Nw * 2) >> 4;  // hi -> lo part of the y tile
       uint32_t kq = 0, it = 0;
       bool first = true;
       for (int tile = split; tile < p.num_tiles; tile += p.splits, ++it) {
@@ -483,7 +486,7 @@ gencat_bwd_w_kernel(const BwParams p) {
           goto done;
         }
         tc::tc_fence_after();
-        const uint32_t ya = tc::smem_u32(smem + L.y + yb * L.y_bytes);
+        const uint64_t yd = tc::smem_desc(tc::smem_u32(smem + L.y + yb * L.y_bytes), b_lbo, 128);
         for (int g = g0; g < g1; ++g, ++kq) {
           const int ks_ = kq % NS;
           if (!tc::mbar_wait(&k_full[ks_], (kq / NS) & 1, abort_flag, kWaitNs)) {
@@ -491,18 +494,19 @@ gencat_bwd_w_kernel(const BwParams p) {
             goto done;
           }
           tc::tc_fence_after();
-          const uint32_t ka = tc::smem_u32(smem + L.dk + ks_ * L.dk_bytes);
+          // A: dK, MN-major (rows are M, pixels are K): K-group stride 2048, M-group 128
+          const uint64_t ad =
+              tc::smem_desc(tc::smem_u32(smem + L.dk + ks_ * L.dk_bytes), 2048, 128);
           const uint32_t dt = tmem_base + (g - g0) * Nw;
+          const uint32_t acc0 = first ? 0u : 1u;
+#pragma unroll
           for (int ks = 0; ks < 8; ++ks) {
-            // A: dK, MN-major (rows are M, pixels are K): K-group stride 2048, M-group 128
-            const uint64_t a_hi = tc::smem_desc(ka + ks * 2 * 2048, 2048, 128);
-            const uint64_t b_hi = tc::smem_desc(ya + ks * 2 * b_lbo, b_lbo, 128);
-            tc::mma_f16(dt, a_hi, b_hi, idesc, (!first || ks > 0) ? 1u : 0u);
+            const uint64_t a_k = ad + ks * ((2 * 2048) >> 4);
+            const uint64_t b_k = yd + ks * b_step;
+            tc::mma_f16(dt, a_k, b_k, idesc, ks > 0 ? 1u : acc0);
             if constexpr (Cfg::kSplit) {
-              const uint64_t a_lo = tc::smem_desc(ka + kDkBytes + ks * 2 * 2048, 2048, 128);
-              const uint64_t b_lo = tc::smem_desc(ya + ypart + ks * 2 * b_lbo, b_lbo, 128);
-              tc::mma_f16(dt, a_lo, b_hi, idesc, 1u);
-              tc::mma_f16(dt, a_hi, b_lo, idesc, 1u);
+              tc::mma_f16(dt, a_k + (kDkBytes >> 4), b_k, idesc, 1u);
+              tc::mma_f16(dt, a_k, b_k + y_lo, idesc, 1u);
             }
           }
           tc::mma_commit(&k_empty[ks_]);

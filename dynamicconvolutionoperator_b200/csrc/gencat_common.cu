@@ -42,6 +42,20 @@ int status_ptr(int** out) {
   return DDPM_OK;
 }
 
+// Reads (and with `reset` clears) the device-side failure code of the current
+// device: 0, or the code of the first bounded wait that gave up. Synchronises
+// the device; meant for tests and error paths, not for the step loop.
+int read_status(int reset, int* code) {
+  DDPM_CHECK_ARG(code != nullptr, "null pointer");
+  DDPM_CUDA_TRY(cudaDeviceSynchronize());
+  DDPM_CUDA_TRY(cudaMemcpyFromSymbol(code, g_gencat_status, sizeof(int)));
+  if (reset) {
+    const int zero = 0;
+    DDPM_CUDA_TRY(cudaMemcpyToSymbol(g_gencat_status, &zero, sizeof(int)));
+  }
+  return DDPM_OK;
+}
+
 int num_sms() {
   static std::mutex mu;
   static int cache[64] = {0};
@@ -79,17 +93,17 @@ __global__ void pack_kernel(const T* __restrict__ W, const T* __restrict__ bias,
     bool kdim_is_row = false;  // dY image: the K dimension runs over weight rows
     int i_col = 0;             // dY image: the weight column (input channel)
     if (idx < L.fwd_rows) {
-      // [q][part][Ck/8][16K][8]; q = (cg*3 + b)*K + ki; row kj*16 + cl
-      const long long per_chunk = (long long)L.parts * (L.Ck / 8) * 16 * KS;
-      const int q = (int)(idx / per_chunk);
-      int rem = (int)(idx - q * per_chunk);
-      part = rem / ((L.Ck / 8) * 16 * KS);
-      rem -= part * (L.Ck / 8) * 16 * KS;
-      const int kg = rem / (16 * KS);
-      const int row = rem - kg * 16 * KS;
-      const int cg = q / (3 * KS), b = (q / KS) % 3, ki = q % KS;
-      const int kj = row / 16, c = cg * 16 + row % 16;
-      if (c < C) m = (long long)(b * C + c) * KK + ki * KS + kj;
+      // [cg][part][Ck/8][3*K^2*16][8]; row = (b*K^2 + tap)*16 + cl
+      const int nrow = 48 * KK;
+      const long long per_cg = (long long)L.parts * (L.Ck / 8) * nrow;
+      const int cg = (int)(idx / per_cg);
+      int rem = (int)(idx - cg * per_cg);
+      part = rem / ((L.Ck / 8) * nrow);
+      rem -= part * (L.Ck / 8) * nrow;
+      const int kg = rem / nrow;
+      const int row = rem - kg * nrow;
+      const int b = row / (16 * KK), tap = (row / 16) % KK, c = cg * 16 + row % 16;
+      if (c < C) m = (long long)(b * C + c) * KK + tap;
       k0 = kg * 8;
     } else if (idx < L.fwd_rows + L.bx_rows) {
       // [q][part][Ck/8][Cp][8]; q = b*K^2 + tap; row = c

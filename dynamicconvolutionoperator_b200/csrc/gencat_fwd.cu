@@ -19,9 +19,12 @@
 //   * tile  = 8 x 16 output pixels of one image = the 128 rows of the MMA's
 //             M dimension = the 128 TMEM lanes (lane m <-> pixel (m/16, m%16));
 //             CTAs of the same cg split the tiles between them;
-//   * chunk = (branch b, kernel row ki) of the CTA's group: N = 16*K
-//             accumulator columns, column kj*16 + cl <-> tap (ki, kj) of
-//             channel cg*16 + cl. A tile is 3 * K chunks.
+//   * slot  = one branch b (K = 3) or all three branches (K = 1) of the
+//             CTA's group: ONE MMA per K step with N = branches * K^2 * 16
+//             accumulator columns (144 or 48), column (b', tap)*16 + cl <->
+//             branch b0 + b', tap, channel cg*16 + cl. A tcgen05.mma costs
+//             its issuing thread ~55 cycles whatever its N, so the widest N
+//             the weight layout allows keeps the tensor pipe busy.
 //   * GEMM K dimension = the Ck "augmented" input channels. For bf16/fp16:
 //             y's C channels, then a constant-one channel whose weight column
 //             is the bias, then zeros (Ck = round_up(C + 1, 16)) - the bias add
@@ -29,8 +32,9 @@
 //             = Cp and the epilogue adds the bias.
 //   * operands: A = the y tile, MN-major in shared memory ([8-pixel group]
 //             [channel][8 pixels]); B = the group's resident weight chunks,
-//             pre-packed in global memory in the exact K-major smem image and
-//             fetched with 1-D bulk async copies.
+//             pre-packed in global memory in the exact K-major smem image
+//             [Ck/8][3*K^2*16 rows][8] (any branch's rows are a contiguous
+//             N range) and fetched with one 1-D bulk async copy.
 //   * FP32 I/O: y and W are split into bf16 hi + lo parts and each MMA step
 //             is hi*hi + lo*hi + hi*lo (relative error ~2^-16 per product).
 //   * x halo: for each channel group the (8+2R) x 32 pixel neighbourhood of the
@@ -41,8 +45,8 @@
 //
 // Warp roles (18 warps): w0 = TMEM allocator + weight loader, w1 = MMA
 // issuer, w2-w5 = y-tile producers, w6-w9 = x-halo producers, w10-w17 = two
-// epilogue warpgroups; output group (tile, b) belongs to warpgroup
-// (tile_iter*3 + b) % 2, which consumes its chunks in order from a ring of
+// epilogue warpgroups; slot number s (counted over the CTA's tiles) belongs
+// to warpgroup s % 2, which consumes its slots in order from its own ring of
 // TMEM buffers. Each producer thread issues all of its loads for a tile before
 // its first shared-memory store, so a tile costs one memory latency, not
 // several; each epilogue thread issues the three TMEM loads of a chunk before
@@ -60,9 +64,15 @@ template <typename T, int KS>
 struct FwdCfg {
   static constexpr bool kSplit = IoTraits<T>::kSplit;
   static constexpr int kParts = kSplit ? 2 : 1;
-  static constexpr int kN = 16 * KS;                         // accumulator columns per chunk
+  static constexpr int kBr = KS == 1 ? 3 : 1;                 // branches per slot
+  static constexpr int kSlots = 3 / kBr;                      // slots per tile
+  static constexpr int kN = kBr * KS * KS * 16;               // accumulator columns per slot
+  static constexpr int kRows = 3 * KS * KS * 16;              // weight rows of a channel group
   static constexpr int kNumBuf = (512 / kN) > 8 ? 8 : (512 / kN);
-  static constexpr int kChunks = 3 * KS;                      // per tile (one channel group)
+  // Each epilogue warpgroup owns kNumBuf / 2 TMEM buffers: every buffer has a
+  // single consumer that sees all of its phases in order.
+  static constexpr int kBufPerWG = kNumBuf / 2;
+  static_assert(kBufPerWG >= 1, "two TMEM slots must fit");
   static constexpr int kYBufs = kSplit ? 1 : 2;               // smem budget (see layout)
   static constexpr bool kBiasInGemm = !kSplit;
   static constexpr int kEpiWG = 2;
@@ -88,11 +98,11 @@ __host__ __device__ inline FwdSmem fwd_smem_layout(int Ck, int R) {
   using Cfg = FwdCfg<T, KS>;
   FwdSmem L;
   L.y_bytes = (uint32_t)Cfg::kParts * kTileM * Ck * 2;
-  L.w_bytes = (uint32_t)Cfg::kParts * Cfg::kN * Ck * 2;  // one chunk
+  L.w_bytes = (uint32_t)Cfg::kParts * Cfg::kRows * Ck * 2;  // the group's whole image
   L.xr_bytes = (uint32_t)16 * (kTileH + 2 * R) * kHaloCols * 4;
   L.y = 0;
   L.w = L.y + Cfg::kYBufs * L.y_bytes;
-  L.xr = L.w + Cfg::kChunks * L.w_bytes;
+  L.xr = L.w + L.w_bytes;
   L.bias = L.xr + 2 * L.xr_bytes;
   L.bars = L.bias + (Cfg::kBiasInGemm ? 0u : (uint32_t)(3 * 16 * KS * KS * 4));
   L.total = L.bars + 8 * (9 + 2 * Cfg::kNumBuf);
@@ -119,7 +129,6 @@ gencat_fwd_kernel(const FwdParams p) {
   using Op = typename IoTraits<T>::Op;
   constexpr int kN = Cfg::kN;
   constexpr int NB = Cfg::kNumBuf;
-  constexpr int NQ = Cfg::kChunks;
   constexpr int NY = Cfg::kYBufs;
   constexpr int KK = KS * KS;
   constexpr int r = KS / 2;
@@ -185,24 +194,29 @@ gencat_fwd_kernel(const FwdParams p) {
   if (warp == 0) {
     // ---- weight loader: the group's chunks, once, resident afterwards -----
     if (lane == 0) {
-      const uint32_t bytes = NQ * L.w_bytes;
+      const uint32_t bytes = L.w_bytes;
       const uint8_t* src = static_cast<const uint8_t*>(p.wpack) + (size_t)cg * bytes;
       tc::mbar_arrive_expect_tx(w_full, bytes);
-      for (int q = 0; q < NQ; ++q)
-        tc::bulk_g2s(smem + L.w + q * L.w_bytes, src + (size_t)q * L.w_bytes, L.w_bytes, w_full);
+      for (uint32_t off = 0; off < bytes; off += 32768) {
+        const uint32_t len = bytes - off < 32768 ? bytes - off : 32768;
+        tc::bulk_g2s(smem + L.w + off, src + off, len, w_full);
+      }
     }
   } else if (warp == 1) {
     // ---- MMA issuer --------------------------------------------------------
     if (lane == 0) {
       const uint32_t idesc = tc::idesc_f16(kTileM, kN, IoTraits<T>::kBf16, true, false);
-      const uint32_t a_sbo = Ck * 16;           // 8-pixel groups
-      const uint32_t b_lbo = kN * 16;           // 8-channel groups of a weight chunk
-      const uint32_t ypart = kTileM * Ck * 2;   // hi -> lo offset of the y tile
-      const uint32_t wpart = kN * Ck * 2;       // hi -> lo offset of a weight chunk
+      const uint32_t b_lbo = Cfg::kRows * 16;   // 8-channel groups of the weight image
+      const uint64_t a_step = 256 >> 4;         // descriptor advance per K step
+      const uint64_t b_step = (2 * b_lbo) >> 4;
+      const uint64_t a_lo = (kTileM * Ck * 2) >> 4;        // hi -> lo part of the y tile
+      const uint64_t b_lo = (Cfg::kRows * Ck * 2) >> 4;    // hi -> lo part of the weights
+      const int nks = Ck / 16;
       if (!tc::mbar_wait(w_full, 0, abort_flag, kWaitNs)) {
         fail(abort_flag, p.status, 10);
         goto done;
       }
+      const uint64_t w_desc = tc::smem_desc(tc::smem_u32(smem + L.w), b_lbo, 128);
       uint32_t tq = 0, it = 0;
       for (int tile = first_tile; tile < p.num_tiles; tile += tile_step, ++it) {
         const int yb = it % NY;
@@ -211,31 +225,40 @@ gencat_fwd_kernel(const FwdParams p) {
           goto done;
         }
         tc::tc_fence_after();
-        const uint32_t ya = tc::smem_u32(smem + L.y + yb * L.y_bytes);
-        for (int q = 0; q < NQ; ++q, ++tq) {
-          const int j = tq % NB;
-          if (!tc::mbar_wait(&t_empty[j], ((tq / NB) & 1) ^ 1, abort_flag, kWaitNs)) {
+        const uint64_t y_desc =
+            tc::smem_desc(tc::smem_u32(smem + L.y + yb * L.y_bytes), 128, Ck * 16);
+        for (int q = 0; q < Cfg::kSlots; ++q, ++tq) {
+          // slot tq belongs to epilogue warpgroup tq % 2 (its (tq / 2)-th slot)
+          const uint32_t own = tq >> 1;
+          const int j = (tq & 1) * Cfg::kBufPerWG + own % Cfg::kBufPerWG;
+          if (!tc::mbar_wait(&t_empty[j], ((own / Cfg::kBufPerWG) & 1) ^ 1, abort_flag,
+                             kWaitNs)) {
             fail(abort_flag, p.status, 12);
             goto done;
           }
           tc::tc_fence_after();
-          const uint32_t wb = tc::smem_u32(smem + L.w + q * L.w_bytes);
+          // rows of branch q (K = 3) or of all branches (K = 1): (q * kN) * 16 bytes in
+          const uint64_t bd = w_desc + (uint64_t)(q * kN);
           const uint32_t d = tmem_base + j * kN;
-          for (int ks = 0; ks < Ck / 16; ++ks) {
-            const uint64_t a_hi = tc::smem_desc(ya + ks * 256, 128, a_sbo);
-            const uint64_t b_hi = tc::smem_desc(wb + ks * 2 * b_lbo, b_lbo, 128);
-            tc::mma_f16(d, a_hi, b_hi, idesc, ks > 0 ? 1u : 0u);
+          // A plain runtime loop: an MMA under a per-step condition inside an
+          // unrolled loop was compiled into wrong issue (results corrupted).
+          for (int ks = 0; ks < nks; ++ks) {
+            const uint64_t a_k = y_desc + ks * a_step;
+            const uint64_t b_k = bd + ks * b_step;
+            tc::mma_f16(d, a_k, b_k, idesc, ks > 0 ? 1u : 0u);
             if constexpr (Cfg::kSplit) {
-              const uint64_t a_lo = tc::smem_desc(ya + ypart + ks * 256, 128, a_sbo);
-              const uint64_t b_lo = tc::smem_desc(wb + wpart + ks * 2 * b_lbo, b_lbo, 128);
-              tc::mma_f16(d, a_lo, b_hi, idesc, 1u);
-              tc::mma_f16(d, a_hi, b_lo, idesc, 1u);
+              tc::mma_f16(d, a_k + a_lo, b_k, idesc, 1u);
+              tc::mma_f16(d, a_k, b_k + b_lo, idesc, 1u);
             }
           }
           tc::mma_commit(&t_full[j]);
         }
         tc::mma_commit(&y_empty[yb]);
       }
+      // Teardown frees TMEM: wait until every issued MMA has completed
+      // (w_full's phase 1, after the weight load's phase 0).
+      tc::mma_commit(w_full);
+      if (!tc::mbar_wait(w_full, 1, abort_flag, kWaitNs)) fail(abort_flag, p.status, 17);
     }
   } else if (warp < 2 + Cfg::kProducers / 32) {
     // ---- y-tile producers ----------------------------------------------------
@@ -304,62 +327,65 @@ gencat_fwd_kernel(const FwdParams p) {
       // this pixel's cell in the halo tile; a tap shifts it by (dy, dx)
       const float4* xc = xr + (mr + R) * kHaloCols + (mc + 8);
       bool failed = false;
-      for (int b = 0; b < 3; ++b) {
-        const bool mine = ((it * 3 + b) % Cfg::kEpiWG) == (uint32_t)wg;
-        if (!mine) {
-          tq += KS;
-          continue;
+      for (int q = 0; q < Cfg::kSlots && !failed; ++q, ++tq) {
+        if ((tq & 1) != (uint32_t)wg) continue;  // the other warpgroup's slot
+        const uint32_t own = tq >> 1;
+        const int j = wg * Cfg::kBufPerWG + own % Cfg::kBufPerWG;
+        if (!warp_wait(&t_full[j], (own / Cfg::kBufPerWG) & 1, abort_flag)) {
+          fail(abort_flag, p.status, 14);
+          failed = true;
+          break;
         }
-        const int d = p.d[b];
-        unsigned long long acc[8];
+        tc::tc_fence_after();
+        const uint32_t slot_addr = tmem_base + ((uint32_t)(quad * 32) << 16) + j * kN;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] = 0ull;
+        for (int bb = 0; bb < Cfg::kBr; ++bb) {
+          const int b = q * Cfg::kBr + bb;
+          const int d = p.d[b];
+          unsigned long long acc[8];
 #pragma unroll
-        for (int ki = 0; ki < KS; ++ki, ++tq) {
-          const int j = tq % NB;
-          if (!warp_wait(&t_full[j], (tq / NB) & 1, abort_flag)) {
-            fail(abort_flag, p.status, 14);
-            failed = true;
-            break;
-          }
-          tc::tc_fence_after();
-          const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + j * kN;
-          const float4* xrow = xc + (ki - r) * d * kHaloCols;
-          float dv[KS][16];
+          for (int i = 0; i < 8; ++i) acc[i] = 0ull;
 #pragma unroll
-          for (int kj = 0; kj < KS; ++kj) tc::tmem_ld16(taddr + kj * 16, dv[kj]);
-          tc::tmem_ld_wait();
-          tc::tc_fence_before();
-          tc::mbar_arrive(&t_empty[j]);  // accumulator values are in registers now
+          for (int ki = 0; ki < KS; ++ki) {
+            const uint32_t taddr = slot_addr + (bb * KK + ki * KS) * 16;
+            const float4* xrow = xc + (ki - r) * d * kHaloCols;
+            float dv[KS][16];
 #pragma unroll
-          for (int kj = 0; kj < KS; ++kj) {
-            const float4* cell = xrow + (kj - r) * d;
+            for (int kj = 0; kj < KS; ++kj) tc::tmem_ld16(taddr + kj * 16, dv[kj]);
+            tc::tmem_ld_wait();
+            if (bb == Cfg::kBr - 1 && ki == KS - 1) {
+              tc::tc_fence_before();
+              tc::mbar_arrive(&t_empty[j]);  // the slot's accumulators are in registers now
+            }
 #pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4) {
-              const float4 v = cell[q4 * xr_plane];
-              float g0 = dv[kj][q4 * 4 + 0], g1 = dv[kj][q4 * 4 + 1];
-              float g2 = dv[kj][q4 * 4 + 2], g3 = dv[kj][q4 * 4 + 3];
-              if constexpr (!Cfg::kBiasInGemm) {
-                const float* bs = bias_s + (b * 16 + q4 * 4) * KK + ki * KS + kj;
-                g0 += bs[0];
-                g1 += bs[KK];
-                g2 += bs[2 * KK];
-                g3 += bs[3 * KK];
+            for (int kj = 0; kj < KS; ++kj) {
+              const float4* cell = xrow + (kj - r) * d;
+#pragma unroll
+              for (int q4 = 0; q4 < 4; ++q4) {
+                const float4 v = cell[q4 * xr_plane];
+                float g0 = dv[kj][q4 * 4 + 0], g1 = dv[kj][q4 * 4 + 1];
+                float g2 = dv[kj][q4 * 4 + 2], g3 = dv[kj][q4 * 4 + 3];
+                if constexpr (!Cfg::kBiasInGemm) {
+                  const float* bs = bias_s + (b * 16 + q4 * 4) * KK + ki * KS + kj;
+                  g0 += bs[0];
+                  g1 += bs[KK];
+                  g2 += bs[2 * KK];
+                  g3 += bs[3 * KK];
+                }
+                acc[q4 * 2 + 0] = f2_fma(tap_pair<T>(g0, g1), f2_pack(v.x, v.y), acc[q4 * 2 + 0]);
+                acc[q4 * 2 + 1] = f2_fma(tap_pair<T>(g2, g3), f2_pack(v.z, v.w), acc[q4 * 2 + 1]);
               }
-              acc[q4 * 2 + 0] = f2_fma(tap_pair<T>(g0, g1), f2_pack(v.x, v.y), acc[q4 * 2 + 0]);
-              acc[q4 * 2 + 1] = f2_fma(tap_pair<T>(g2, g3), f2_pack(v.z, v.w), acc[q4 * 2 + 1]);
             }
           }
-        }
-        if (failed) break;
-        if (px_ok) {
+          if (px_ok) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            float a0, a1;
-            f2_unpack(acc[i], a0, a1);
-            const int c = cg * 16 + 2 * i;
-            if (c < C) on[(size_t)((b + 1) * C + c) * P + pix] = from_f32<T>(a0);
-            if (c + 1 < C) on[(size_t)((b + 1) * C + c + 1) * P + pix] = from_f32<T>(a1);
+            for (int i = 0; i < 8; ++i) {
+              float a0, a1;
+              f2_unpack(acc[i], a0, a1);
+              const int c = cg * 16 + 2 * i;
+              if (c < C) on[(size_t)((b + 1) * C + c) * P + pix] = from_f32<T>(a0);
+              if (c + 1 < C) on[(size_t)((b + 1) * C + c + 1) * P + pix] = from_f32<T>(a1);
+            }
           }
         }
       }

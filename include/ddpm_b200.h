@@ -57,6 +57,12 @@ DDPM_API const char* ddpm_last_error(void);
  * all threads). Benchmarks read it to count the library's launches. */
 DDPM_API unsigned long long ddpm_launch_count(void);
 
+/* Device-side failure code of the current device (no reference counterpart):
+ * every wait inside the tensor-core kernels is bounded; one that gives up
+ * records a nonzero code here and the kernel returns early (its outputs are
+ * then invalid). Synchronises the device; `reset` != 0 clears the code. */
+DDPM_API int ddpm_device_status(int reset, int* code);
+
 /*
  * Materialised dynamic filter, forward.
  * Replaces `_DynamicCat.forward` + `_dynamic_cat_fwd`

@@ -56,15 +56,16 @@ def compare(dev_out, dev_grads, gold_out, gold_grads, dtype):
         s = orc.error_stats(a, e)
         s["norm_rmse"] = s["rmse"] / s["ref_max"]
         stats[name] = s
+        # written as "not (err <= tol)" so that a NaN error fails
         if name in ("out", "x", "y"):
-            if s["max_abs"] > tol["max_abs"]:
+            if not s["max_abs"] <= tol["max_abs"]:
                 fails.append(f"{name}: max_abs {s['max_abs']:.3e} > {tol['max_abs']}")
-            if tol["rmse"] is not None and s["rmse"] > tol["rmse"]:
+            if tol["rmse"] is not None and not s["rmse"] <= tol["rmse"]:
                 fails.append(f"{name}: rmse {s['rmse']:.3e} > {tol['rmse']}")
         else:
-            if s["norm_max"] > tol["norm_max"]:
+            if not s["norm_max"] <= tol["norm_max"]:
                 fails.append(f"{name}: norm_max {s['norm_max']:.3e} > {tol['norm_max']}")
-            if tol["norm_rmse"] is not None and s["norm_rmse"] > tol["norm_rmse"]:
+            if tol["norm_rmse"] is not None and not s["norm_rmse"] <= tol["norm_rmse"]:
                 fails.append(f"{name}: norm_rmse {s['norm_rmse']:.3e} > {tol['norm_rmse']}")
     return stats, fails
 
