@@ -290,9 +290,24 @@ def load_peaks():
     return 6650.0, 1590.0, "fallback"
 
 
-# dram bytes per launch from committed ncu captures (profiles/*.md), keyed by
-# (kernel, dtype); None where no capture exists yet.
-NCU_TRAFFIC_BYTES: dict[tuple[str, str], float] = {}
+# DRAM bytes (read + write) per launch at this configuration, from the ncu
+# captures summarised in profiles/<kernel>_256.md, keyed by (kernel, dtype);
+# None where no capture exists. Outputs still resident in L2 when a captured
+# launch ends are not counted as writes.
+NCU_TRAFFIC_BYTES: dict[tuple[str, str], float] = {
+    ("gencat_fwd", "torch.float32"): 68486144,
+    ("gencat_fwd", "torch.bfloat16"): 19637504,
+    ("gencat_bwd_x", "torch.float32"): 97914368,
+    ("gencat_bwd_x", "torch.bfloat16"): 43072768,
+    ("gencat_bwd_yw", "torch.float32"): 161953792,
+    ("gencat_bwd_yw", "torch.bfloat16"): 77374720,
+    ("fuseconv_fwd", "torch.float32"): 70569472,
+    ("fuseconv_fwd", "torch.bfloat16"): 33930240,
+    ("fuseconv_dgrad", "torch.float32"): 26131200,
+    ("fuseconv_dgrad", "torch.bfloat16"): 8801280,
+    ("dyncat_fwd", "torch.float32"): 489555712,
+    ("dyncat_bwd", "torch.float32"): 1098030336,
+}
 
 
 def library_kernels(model, x, y, dtype, device):
