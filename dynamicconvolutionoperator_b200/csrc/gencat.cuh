@@ -411,6 +411,54 @@ __device__ __forceinline__ unsigned long long f2_round_f16(float lo, float hi) {
   const float2 f = __half22float2(h);
   return f2_pack(f.x, f.y);
 }
+// Two floats -> one 32-bit word of two Op values (first value in bits 0-15),
+// round to nearest even; and back.
+template <typename Op> __device__ __forceinline__ uint32_t cvt2(float lo, float hi);
+template <> __device__ __forceinline__ uint32_t cvt2<__nv_bfloat16>(float lo, float hi) {
+  uint32_t p;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(p) : "f"(hi), "f"(lo));
+  return p;
+}
+template <> __device__ __forceinline__ uint32_t cvt2<__half>(float lo, float hi) {
+  uint32_t p;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(p) : "f"(hi), "f"(lo));
+  return p;
+}
+template <typename Op> __device__ __forceinline__ unsigned long long uncvt2(uint32_t p);
+template <> __device__ __forceinline__ unsigned long long uncvt2<__nv_bfloat16>(uint32_t p) {
+  return f2_pack(__uint_as_float(p << 16), __uint_as_float(p & 0xFFFF0000u));
+}
+template <> __device__ __forceinline__ unsigned long long uncvt2<__half>(uint32_t p) {
+  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&p));
+  return f2_pack(f.x, f.y);
+}
+
+// Eight floats, held as four packed pairs, stored as one 16-byte operand row;
+// with kSplit also the residual (v - hi) row at dst_lo (exact subtraction).
+template <typename Op, bool kSplit>
+__device__ __forceinline__ void store8x2_split(uint8_t* dst_hi, uint8_t* dst_lo,
+                                               const unsigned long long (&v)[4]) {
+  uint32_t h[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float a, b;
+    f2_unpack(v[i], a, b);
+    h[i] = cvt2<Op>(a, b);
+  }
+  *reinterpret_cast<uint4*>(dst_hi) = make_uint4(h[0], h[1], h[2], h[3]);
+  if constexpr (kSplit) {
+    const unsigned long long neg1 = f2_pack(-1.f, -1.f);
+    uint32_t l[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float a, b;
+      f2_unpack(f2_fma(uncvt2<Op>(h[i]), neg1, v[i]), a, b);
+      l[i] = cvt2<Op>(a, b);
+    }
+    *reinterpret_cast<uint4*>(dst_lo) = make_uint4(l[0], l[1], l[2], l[3]);
+  }
+}
+
 // Tap pair (lo, hi) as used by the filter: rounded to the I/O dtype (bf16/fp16
 // taps are rounded like the reference, `_triton_kernels.py:332-335`).
 template <typename T>

@@ -41,17 +41,21 @@ constexpr int kDkBytes = kTileM * 128 * 2;  // one dK tile part (bf16 / fp16)
 
 // ----------------------------------------------------------- dK builder -----
 // Slots of octet OCT: s = OCT*8 + j -> (b, tap) = (s / K^2, s % K^2); s >= 3K^2
-// is padding (zero rows). gv[b][cl] = g_b[cg16*16 + cl, p] of this pixel.
+// is padding (zero rows). gv[b][i] = the pair (g_b[2i], g_b[2i+1]) of this
+// pixel's 16-channel group, packed; products and conversions run on f32x2 /
+// bf16x2 pairs.
 template <typename T, typename Op, bool kSplit, int KS, int OCT>
 __device__ __forceinline__ void build_octet(uint8_t* dk, const float4* xc, int xr_plane,
-                                            const float (&gv)[3][16], const int (&dil)[3], int m) {
+                                            const unsigned long long (&gv)[3][8],
+                                            const int (&dil)[3], int m) {
   constexpr int KK = KS * KS;
   constexpr int r = KS / 2;
   const uint32_t base = (m >> 3) * 2048 + (m & 7) * 16;
+  const unsigned long long zero2 = 0ull;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const int s = OCT * 8 + j;
-    float prod[16];
+    unsigned long long prod[8];
     if (s < 3 * KK) {
       const int b = s / KK, tap = s % KK;
       const int dy = (tap / KS - r) * dil[b], dx = (tap % KS - r) * dil[b];
@@ -59,30 +63,25 @@ __device__ __forceinline__ void build_octet(uint8_t* dk, const float4* xc, int x
 #pragma unroll
       for (int q4 = 0; q4 < 4; ++q4) {
         const float4 v = cell[q4 * xr_plane];
-        prod[q4 * 4 + 0] = v.x * gv[b][q4 * 4 + 0];
-        prod[q4 * 4 + 1] = v.y * gv[b][q4 * 4 + 1];
-        prod[q4 * 4 + 2] = v.z * gv[b][q4 * 4 + 2];
-        prod[q4 * 4 + 3] = v.w * gv[b][q4 * 4 + 3];
+        prod[q4 * 2 + 0] = f2_fma(f2_pack(v.x, v.y), gv[b][q4 * 2 + 0], zero2);
+        prod[q4 * 2 + 1] = f2_fma(f2_pack(v.z, v.w), gv[b][q4 * 2 + 1], zero2);
       }
     } else {
 #pragma unroll
-      for (int i = 0; i < 16; ++i) prod[i] = 0.f;
+      for (int i = 0; i < 8; ++i) prod[i] = zero2;
     }
-    float lo8[8], hi8[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      lo8[i] = prod[i];
-      hi8[i] = prod[8 + i];
-    }
+    const unsigned long long lo8[4] = {prod[0], prod[1], prod[2], prod[3]};
+    const unsigned long long hi8[4] = {prod[4], prod[5], prod[6], prod[7]};
     const uint32_t off = base + (j * 2) * 128;
-    store8_split<Op, kSplit>(dk + off, dk + kDkBytes + off, lo8);
-    store8_split<Op, kSplit>(dk + off + 128, dk + kDkBytes + off + 128, hi8);
+    store8x2_split<Op, kSplit>(dk + off, dk + kDkBytes + off, lo8);
+    store8x2_split<Op, kSplit>(dk + off + 128, dk + kDkBytes + off + 128, hi8);
   }
 }
 
 template <typename T, typename Op, bool kSplit, int KS>
 __device__ __forceinline__ void build_dk(uint8_t* dk, int octet, const float4* xc, int xr_plane,
-                                         const float (&gv)[3][16], const int (&dil)[3], int m) {
+                                         const unsigned long long (&gv)[3][8],
+                                         const int (&dil)[3], int m) {
   switch (octet) {
     case 0: build_octet<T, Op, kSplit, KS, 0>(dk, xc, xr_plane, gv, dil, m); break;
     case 1: build_octet<T, Op, kSplit, KS, 1>(dk, xc, xr_plane, gv, dil, m); break;
@@ -93,16 +92,21 @@ __device__ __forceinline__ void build_dk(uint8_t* dk, int octet, const float4* x
 
 // g_b[cg16*16 + cl, pixel] for the three branches (zero off-image / c >= C).
 template <typename T>
-__device__ __forceinline__ void load_gv(float (&gv)[3][16], const T* gn, int C, size_t P,
-                                        int cg16, size_t pix, bool px_ok) {
+__device__ __forceinline__ void load_gv(unsigned long long (&gv)[3][8], const T* gn, int C,
+                                        size_t P, int cg16, size_t pix, bool px_ok) {
+  float v[3][16];
 #pragma unroll
   for (int b = 0; b < 3; ++b)
 #pragma unroll
     for (int cl = 0; cl < 16; ++cl) {
       const int c = cg16 * 16 + cl;
-      gv[b][cl] = (px_ok && c < C) ? to_f32<T>(__ldg(gn + (size_t)((b + 1) * C + c) * P + pix))
-                                   : 0.f;
+      v[b][cl] = (px_ok && c < C) ? to_f32<T>(__ldg(gn + (size_t)((b + 1) * C + c) * P + pix))
+                                  : 0.f;
     }
+#pragma unroll
+  for (int b = 0; b < 3; ++b)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) gv[b][i] = f2_pack(v[b][2 * i], v[b][2 * i + 1]);
 }
 
 // =============================================================== dY =========
@@ -308,7 +312,7 @@ gencat_bwd_y_kernel(const ByParams p) {
       const T* gn = gout + (size_t)n * 4 * C * P;
       bool failed = false;
       for (int cg = 0; cg < ncg && !failed; ++cg, ++xq) {
-        float gv[3][16];
+        unsigned long long gv[3][16 / 2];
         load_gv<T>(gv, gn, C, P, cg, pix, px_ok);
         const int xb = xq & 1;
         if (!warp_wait(&x_full[xb], (xq >> 1) & 1, abort_flag)) {
@@ -578,7 +582,7 @@ gencat_bwd_w_kernel(const BwParams p) {
       const size_t pix = px_ok ? (size_t)h * W + w : 0;
       const T* gn = gout + (size_t)n * 4 * C * P;
       int cur = -1;
-      float gv[3][16];
+      unsigned long long gv[3][16 / 2];
       const float4* xc = nullptr;
       int xb = 0;
       for (int g = g0; g < g1; ++g, ++kq) {
