@@ -74,36 +74,6 @@ __host__ __device__ inline FcSmem fc_smem_layout(const FcParams& p) {
   return L;
 }
 
-// Transpose 8 channels x 8 pixels (one Raw8 per channel) into 8 operand rows
-// of 8 channels each, at dst + px * 16 (and the bf16 residual at + lo_off).
-template <typename T, typename Op, bool kSplit>
-__device__ __forceinline__ void store_transposed(uint8_t* dst, uint32_t lo_off,
-                                                 const Raw8<T> (&v)[8]) {
-  if constexpr (sizeof(T) == 2 && !kSplit) {
-    const uint32_t* w[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) w[e] = reinterpret_cast<const uint32_t*>(&v[e].u);
-#pragma unroll
-    for (int px = 0; px < 8; ++px) {
-      const uint32_t sel = (px & 1) ? 0x7632u : 0x5410u;
-      uint4 row;
-      row.x = __byte_perm(w[0][px >> 1], w[1][px >> 1], sel);
-      row.y = __byte_perm(w[2][px >> 1], w[3][px >> 1], sel);
-      row.z = __byte_perm(w[4][px >> 1], w[5][px >> 1], sel);
-      row.w = __byte_perm(w[6][px >> 1], w[7][px >> 1], sel);
-      *reinterpret_cast<uint4*>(dst + px * 16) = row;
-    }
-  } else {
-#pragma unroll
-    for (int px = 0; px < 8; ++px) {
-      float col[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) col[e] = v[e].get(px);
-      store8_split<Op, kSplit>(dst + px * 16, dst + lo_off + px * 16, col);
-    }
-  }
-}
-
 template <typename T, bool kDgrad>
 struct FcCfg {
   static constexpr bool kSplit = IoTraits<T>::kSplit;

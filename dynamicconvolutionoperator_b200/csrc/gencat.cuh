@@ -188,6 +188,10 @@ __device__ __forceinline__ void store8_split(uint8_t* dst_hi, uint8_t* dst_lo,
 template <typename T> struct Raw8 {
   uint4 u;  // 8 x 16-bit
   __device__ __forceinline__ void zero() { u = make_uint4(0u, 0u, 0u, 0u); }
+  __device__ __forceinline__ void ones() {
+    const uint32_t one2 = std::is_same<T, __half>::value ? 0x3C003C00u : 0x3F803F80u;
+    u = make_uint4(one2, one2, one2, one2);
+  }
   __device__ __forceinline__ float get(int i) const {
     return to_f32<T>(reinterpret_cast<const T*>(&u)[i]);
   }
@@ -195,6 +199,7 @@ template <typename T> struct Raw8 {
 template <> struct Raw8<float> {
   float4 a, b;
   __device__ __forceinline__ void zero() { a = b = make_float4(0.f, 0.f, 0.f, 0.f); }
+  __device__ __forceinline__ void ones() { a = b = make_float4(1.f, 1.f, 1.f, 1.f); }
   __device__ __forceinline__ float get(int i) const {
     const float e[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
     return e[i];
@@ -456,6 +461,38 @@ __device__ __forceinline__ void store8x2_split(uint8_t* dst_hi, uint8_t* dst_lo,
       l[i] = cvt2<Op>(a, b);
     }
     *reinterpret_cast<uint4*>(dst_lo) = make_uint4(l[0], l[1], l[2], l[3]);
+  }
+}
+
+// Transpose 8 channels x 8 pixels (one Raw8 per channel) into 8 K-major
+// operand rows of 8 channels each at dst + px*16 (the bf16 residual rows at
+// dst + lo_off + px*16 when kSplit). 16-bit data is permuted without a float
+// round trip; FP32 data is split with packed bf16x2 conversions.
+template <typename T, typename Op, bool kSplit>
+__device__ __forceinline__ void store_transposed(uint8_t* dst, uint32_t lo_off,
+                                                 const Raw8<T> (&v)[8]) {
+  if constexpr (sizeof(T) == 2 && !kSplit) {
+    const uint32_t* w[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) w[e] = reinterpret_cast<const uint32_t*>(&v[e].u);
+#pragma unroll
+    for (int px = 0; px < 8; ++px) {
+      const uint32_t sel = (px & 1) ? 0x7632u : 0x5410u;
+      uint4 row;
+      row.x = __byte_perm(w[0][px >> 1], w[1][px >> 1], sel);
+      row.y = __byte_perm(w[2][px >> 1], w[3][px >> 1], sel);
+      row.z = __byte_perm(w[4][px >> 1], w[5][px >> 1], sel);
+      row.w = __byte_perm(w[6][px >> 1], w[7][px >> 1], sel);
+      *reinterpret_cast<uint4*>(dst + px * 16) = row;
+    }
+  } else {
+#pragma unroll
+    for (int px = 0; px < 8; ++px) {
+      unsigned long long pr[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) pr[e] = f2_pack(v[2 * e].get(px), v[2 * e + 1].get(px));
+      store8x2_split<Op, kSplit>(dst + px * 16, dst + lo_off + px * 16, pr);
+    }
   }
 }
 

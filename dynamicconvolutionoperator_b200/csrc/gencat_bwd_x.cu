@@ -6,25 +6,28 @@
 //   o        = ((ki - r) * d_b, (kj - r) * d_b), zero outside the image.
 //
 // The taps needed at q are the generator outputs at the SHIFTED pixel q - o.
-// Instead of 27 reloads of shifted y tiles (the reference's approach), one
-// shared-memory copy of the y rows a tile needs is staged per branch in the
-// K-major interleaved operand layout ([channel group][row segment][pixel][8]):
-// pixel rows are 16 bytes apart, so the MMA operand for tap (ki, kj) is just
-// a descriptor whose start address is moved by (8 - dx) pixels inside row
-// segment ki. Each (branch, tap) chunk is one M=128 x N=Cp GEMM whose rows
-// are already the shifted taps of the tile's pixels.
-//
 // Tile = 128 consecutive pixels of one image row (TMEM lane m <-> column
-// w0 + m). Per branch the staged region is K rows x 144 pixels (columns
-// w0-8 .. w0+135) x Ck channels. The weight chunk of (b, tap) is the packed
-// "bx" image row block [Ck/8][Cp][8], streamed through a ring of bulk copies.
-// Epilogue warpgroup h owns the 16-channel blocks h, h+2 of every chunk and
-// multiplies with g_b at q - o read through L1.
+// w0 + m). Work advances in units = (tile, branch b, kernel row ki): the y row
+// h - (ki - r) d_b, columns w0-8 .. w0+135, is staged once per unit in the
+// K-major interleaved operand layout ([channel group][pixel][8]); pixel rows
+// are 16 bytes apart, so the operand of tap (ki, kj) is the staged segment
+// with the descriptor start moved by (8 - dx) pixels, and each (b, tap) chunk
+// is one M=128 x N=Cp GEMM whose rows are already the shifted taps. Instead
+// of 27 reloads of shifted y tiles (the reference's approach) a tile stages
+// 3K row segments.
 //
-// Warp roles (15 warps): w0 = TMEM allocator + weight producer, w1-w2 = MMA
+// The same unit also stages the upstream-gradient row g_b[:, h - dy, w0-8 ..
+// w0+135] (all Cp channels, I/O dtype) with 1-D bulk copies that complete on
+// the unit's barrier, so the epilogue reads g_b at q - o from shared memory
+// instead of gathering it through L1 (27 x 64 scalar loads per pixel and tile
+// bounded the earlier version by memory latency). Units are double buffered.
+//
+// Warp roles (19 warps): w0 = TMEM allocator + weight producer, w1-w2 = MMA
 // issuers (even / odd chunks: one thread issuing N=Cp MMAs back to back
-// leaves the tensor pipe idle ~half the time), w3-w6 = region producers,
-// w7-w14 = two epilogue warpgroups.
+// leaves the tensor pipe idle ~half the time), w3-w10 = unit producers
+// (operand transpose + gradient bulk copies; each thread issues its global
+// loads before waiting for a free buffer), w11-w18 = two epilogue warpgroups
+// owning the 16-channel blocks {0, 2} and {1, 3} of every chunk.
 #include "common.cuh"
 #include "tc.cuh"
 #include "gencat.cuh"
@@ -40,33 +43,38 @@ template <typename T, int KS>
 struct BxCfg {
   static constexpr bool kSplit = IoTraits<T>::kSplit;
   static constexpr int kParts = kSplit ? 2 : 1;
-  static constexpr int kRegBufs = kSplit ? 1 : 2;
-  static constexpr int kWStages = 6;
+  static constexpr int kUnitBufs = 2;                 // staged units in flight
+  static constexpr int kWStages = kSplit ? 4 : 6;
   static constexpr bool kBiasInGemm = !kSplit;
   static constexpr int kIssuers = 2;        // MMA issuer warps (alternate chunks)
   static constexpr int kFirstProducerWarp = 1 + kIssuers;
-  static constexpr int kFirstEpiWarp = kFirstProducerWarp + 4;
+  static constexpr int kProducers = 256;
+  static constexpr int kFirstEpiWarp = kFirstProducerWarp + kProducers / 32;
   static constexpr int kThreads = 32 * (kFirstEpiWarp + 8);
 };
 
 struct BxSmem {
-  uint32_t reg, w, bias, bars, total;
-  uint32_t reg_part, reg_bytes, w_bytes;
+  uint32_t reg, gs, w, bias, bars, total;
+  uint32_t reg_part, reg_bytes, g_bytes, w_bytes;
 };
 
+// One unit buffer = the y row segment (both parts) + the gradient row segment.
+// C=64: fp32 2x36 + 2x36 + 4x16 + 7 KB = 215 KB; bf16 2x23 + 2x18 + 6x10 KB = 143 KB.
 template <typename T, int KS>
 __host__ __device__ inline BxSmem bx_smem_layout(int Cp, int Ck, int C) {
   using Cfg = BxCfg<T, KS>;
   BxSmem L;
-  L.reg_part = (uint32_t)Ck * KS * kSeg * 2;
+  L.reg_part = (uint32_t)Ck * kSeg * 2;
   L.reg_bytes = Cfg::kParts * L.reg_part;
+  L.g_bytes = (uint32_t)Cp * kSeg * sizeof(T);
   L.w_bytes = (uint32_t)Cfg::kParts * Cp * Ck * 2;
   L.reg = 0;
-  L.w = L.reg + Cfg::kRegBufs * L.reg_bytes;
+  L.gs = L.reg + Cfg::kUnitBufs * L.reg_bytes;
+  L.w = L.gs + Cfg::kUnitBufs * L.g_bytes;
   L.bias = L.w + Cfg::kWStages * L.w_bytes;
   L.bars = L.bias + (Cfg::kBiasInGemm ? 0u : (uint32_t)(3 * KS * KS * Cp * 4));
   const int nb = 512 / Cp > 8 ? 8 : 512 / Cp;
-  L.total = L.bars + 8 * (4 + 2 * Cfg::kWStages + 2 * nb);
+  L.total = L.bars + 8 * (3 * Cfg::kUnitBufs + 2 * Cfg::kWStages + 2 * nb);
   return L;
 }
 
@@ -88,7 +96,7 @@ gencat_bwd_x_kernel(const BxParams p) {
   using Cfg = BxCfg<T, KS>;
   using Op = typename IoTraits<T>::Op;
   constexpr int S = Cfg::kWStages;
-  constexpr int NR = Cfg::kRegBufs;
+  constexpr int NU = Cfg::kUnitBufs;
   constexpr int KK = KS * KS;
   constexpr int r = KS / 2;
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -100,12 +108,13 @@ gencat_bwd_x_kernel(const BxParams p) {
   const BxSmem L = bx_smem_layout<T, KS>(Cp, Ck, C);
   const int NB = 512 / Cp > 8 ? 8 : 512 / Cp;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
-  uint64_t* r_full = bars;           // [2]
-  uint64_t* r_empty = bars + 2;      // [2]
-  uint64_t* w_full = bars + 4;       // [S]
-  uint64_t* w_empty = w_full + S;    // [S]
-  uint64_t* t_full = w_empty + S;    // [NB]
-  uint64_t* t_empty = t_full + NB;   // [NB]
+  uint64_t* u_full = bars;              // [NU] producers (128 arrivals) + gradient bytes
+  uint64_t* r_empty = bars + NU;        // [NU] MMAs done with the y segment
+  uint64_t* g_empty = bars + 2 * NU;    // [NU] epilogue done with the gradient segment
+  uint64_t* w_full = bars + 3 * NU;     // [S]
+  uint64_t* w_empty = w_full + S;       // [S]
+  uint64_t* t_full = w_empty + S;       // [NB]
+  uint64_t* t_empty = t_full + NB;      // [NB]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -115,9 +124,10 @@ gencat_bwd_x_kernel(const BxParams p) {
     tc::tmem_relinquish();
   }
   if (threadIdx.x == 32) {
-    for (int i = 0; i < 2; ++i) {
-      tc::mbar_init(&r_full[i], 128);
+    for (int i = 0; i < NU; ++i) {
+      tc::mbar_init(&u_full[i], Cfg::kProducers);
       tc::mbar_init(&r_empty[i], Cfg::kIssuers);
+      tc::mbar_init(&g_empty[i], 256);
     }
     for (int i = 0; i < S; ++i) {
       tc::mbar_init(&w_full[i], 1);
@@ -145,9 +155,10 @@ gencat_bwd_x_kernel(const BxParams p) {
   tc::tc_fence_after();
   const uint32_t tmem_base = tmem_base_s;
   volatile int* abort_flag = &abort_s;
+  constexpr int kUnits = 3 * KS;  // (branch, kernel row) units per tile
 
   if (warp == 0) {
-    // ---- weight producer: 3*K^2 chunks per tile ---------------------------
+    // ---- weight producer: 3*K^2 chunks per tile, in (b, ki, kj) order -----
     if (lane == 0) {
       const uint8_t* wsrc = static_cast<const uint8_t*>(p.wpack);
       uint32_t wq = 0;
@@ -165,47 +176,46 @@ gencat_bwd_x_kernel(const BxParams p) {
       }
     }
   } else if (warp < Cfg::kFirstProducerWarp) {
-    // ---- MMA issuers: warp 1 + i issues the chunks q with q % 2 == i --------
+    // ---- MMA issuers: warp 1 + i issues the chunks with index % 2 == i ------
     if (lane == 0) {
       const uint32_t me = warp - 1;
       const uint32_t idesc = tc::idesc_f16(kTileM, Cp, IoTraits<T>::kBf16, false, false);
-      const uint32_t a_lbo = KS * kSeg * 16;    // channel-group stride of the region
+      constexpr uint32_t a_lbo = kSeg * 16;     // channel-group stride of a y segment
       const uint32_t b_lbo = Cp * 16;           // channel-group stride of a weight chunk
-      const uint64_t a_step = (2 * a_lbo) >> 4;  // descriptor advance per K step
+      constexpr uint64_t a_step = (2 * a_lbo) >> 4;  // descriptor advance per K step
       const uint64_t b_step = (2 * b_lbo) >> 4;
       const uint64_t a_lo = L.reg_part >> 4;     // hi -> lo part offsets
       const uint64_t b_lo = (Cp * Ck * 2) >> 4;
       const int nks = Ck / 16;
-      uint32_t wq = 0, tq = 0, rq = 0;
+      uint32_t wq = 0, uq = 0;
       for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
-        for (int b = 0; b < 3; ++b, ++rq) {
-          const int rb = rq % NR;
-          if (!tc::mbar_wait(&r_full[rb], (rq / NR) & 1, abort_flag, kWaitNs)) {
+        for (int u = 0; u < kUnits; ++u, ++uq) {
+          const int b = u / KS;
+          const int ub = uq % NU;
+          if (!tc::mbar_wait(&u_full[ub], (uq / NU) & 1, abort_flag, kWaitNs)) {
             fail(abort_flag, p.status, 21);
             goto done;
           }
           tc::tc_fence_after();
           const uint64_t a_base =
-              tc::smem_desc(tc::smem_u32(smem + L.reg + rb * L.reg_bytes), a_lbo, 128);
+              tc::smem_desc(tc::smem_u32(smem + L.reg + ub * L.reg_bytes), a_lbo, 128);
           const int d = p.d[b];
-          for (int tap = 0; tap < KK; ++tap, ++wq, ++tq) {
+          for (int kj = 0; kj < KS; ++kj, ++wq) {
             if ((wq & 1u) != me) continue;
             const int s = wq % S;
-            const int j = tq % NB;
+            const int j = wq % NB;  // chunk counter == weight counter
             if (!tc::mbar_wait(&w_full[s], (wq / S) & 1, abort_flag, kWaitNs) ||
-                !tc::mbar_wait(&t_empty[j], ((tq / NB) & 1) ^ 1, abort_flag, kWaitNs)) {
+                !tc::mbar_wait(&t_empty[j], ((wq / NB) & 1) ^ 1, abort_flag, kWaitNs)) {
               fail(abort_flag, p.status, 22);
               goto done;
             }
             tc::tc_fence_after();
-            const int ki = tap / KS, kj = tap % KS;
             const int dx = (kj - r) * d;
-            // window: row segment ki, pixels (8 - dx) .. (8 - dx) + 127
-            const uint64_t ad = a_base + (uint64_t)(ki * kSeg + 8 - dx);
+            // window: pixels (8 - dx) .. (8 - dx) + 127 of the staged segment
+            const uint64_t ad = a_base + (uint64_t)(8 - dx);
             const uint64_t bd =
                 tc::smem_desc(tc::smem_u32(smem + L.w + s * L.w_bytes), b_lbo, 128);
             const uint32_t dt = tmem_base + j * Cp;
-            // plain runtime loop (no MMA under a per-step condition in an unrolled loop)
             for (int ks = 0; ks < nks; ++ks) {
               tc::mma_f16(dt, ad + ks * a_step, bd + ks * b_step, idesc, ks > 0 ? 1u : 0u);
               if constexpr (Cfg::kSplit) {
@@ -216,60 +226,99 @@ gencat_bwd_x_kernel(const BxParams p) {
             tc::mma_commit(&w_empty[s]);
             tc::mma_commit(&t_full[j]);
           }
-          tc::mma_commit(&r_empty[rb]);
+          tc::mma_commit(&r_empty[ub]);
         }
       }
+      // teardown frees TMEM: wait for this thread's last MMAs
+      tc::mma_commit(&r_empty[uq % NU]);
+      if (!tc::mbar_wait(&r_empty[uq % NU], (uq / NU) & 1, abort_flag, kWaitNs))
+        fail(abort_flag, p.status, 27);
     }
   } else if (warp < Cfg::kFirstEpiWarp) {
-    // ---- region producers (128 threads) ------------------------------------
+    // ---- unit producers (256 threads) ---------------------------------------
     const int pt = threadIdx.x - 32 * Cfg::kFirstProducerWarp;
     const T* y = static_cast<const T*>(p.y);
+    const T* gout = static_cast<const T*>(p.gout);
     const int ones_c = Cfg::kBiasInGemm ? C : -1;
-    uint32_t rq = 0;
+    // gradient rows can be bulk-copied when every row start is 16-byte aligned
+    const bool g_bulk = ((size_t)W * sizeof(T)) % 16 == 0 &&
+                        (reinterpret_cast<uintptr_t>(gout) & 15u) == 0;
+    const int items = (Ck / 8) * (kSeg / 8);  // (channel group, 8-pixel block)
+    uint32_t uq = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x) {
       const int per_img = H * p.tiles_w;
       const int n = tile / per_img;
       const int h = (tile % per_img) / p.tiles_w;
       const int w0 = (tile % p.tiles_w) * kTileM;
-      for (int b = 0; b < 3; ++b, ++rq) {
-        const int rb = rq % NR;
-        if (!warp_wait(&r_empty[rb], ((rq / NR) & 1) ^ 1, abort_flag)) {
-          fail(abort_flag, p.status, 23);
-          break;
-        }
-        uint8_t* reg = smem + L.reg + rb * L.reg_bytes;
+      bool failed = false;
+      for (int u = 0; u < kUnits; ++u, ++uq) {
+        const int b = u / KS, ki = u % KS;
         const int d = p.d[b];
-        // item = (channel group kg, segment s, 8-pixel block jb)
-        const int items = (Ck / 8) * KS * (kSeg / 8);
-        for (int item = pt; item < items; item += 128) {
+        const int hr = h - (ki - r) * d;  // image row of this unit
+        const int ub = uq % NU;
+        uint8_t* reg = smem + L.reg + ub * L.reg_bytes;
+        bool waited = false;
+        for (int base = 0; base < items; base += Cfg::kProducers) {
+          // (1) this thread's y item: 8 channels x 8 pixels, loaded before any wait
+          const int item = base + pt;
           const int jb = item % (kSeg / 8);
-          const int s = (item / (kSeg / 8)) % KS;
-          const int kg = item / ((kSeg / 8) * KS);
-          const int hr = h - (s - r) * d;  // image row of segment s
-          Raw8<T> v[8];                    // [channel] x 8 pixels
+          const int kg = item / (kSeg / 8);
+          Raw8<T> v[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const int c = kg * 8 + e;
-            if (c < C)
+            if (item < items && c < C)
               v[e] = load_raw8<T>(y + ((size_t)n * C + c) * P, H, W, hr, w0 - 8 + jb * 8);
+            else if (c == ones_c)
+              v[e].ones();
             else
               v[e].zero();
           }
-#pragma unroll
-          for (int px = 0; px < 8; ++px) {
-            float col[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const int c = kg * 8 + e;
-              col[e] = c < C ? v[e].get(px) : (c == ones_c ? 1.f : 0.f);
+          if (!waited) {
+            if (!warp_wait(&r_empty[ub], ((uq / NU) & 1) ^ 1, abort_flag) ||
+                !warp_wait(&g_empty[ub], ((uq / NU) & 1) ^ 1, abort_flag)) {
+              fail(abort_flag, p.status, 23);
+              failed = true;
+              break;
             }
-            const uint32_t off = ((kg * KS + s) * kSeg + jb * 8 + px) * 16;
-            store8_split<Op, Cfg::kSplit>(reg + off, reg + L.reg_part + off, col);
+            waited = true;
+            // (2) gradient row segment, one channel per thread: columns w0-8 .. w0+135
+            T* gs = reinterpret_cast<T*>(smem + L.gs + ub * L.g_bytes);
+            const int lo = w0 - 8 < 0 ? 0 : w0 - 8;
+            const int hi = w0 + kSeg - 8 > W ? W : w0 + kSeg - 8;
+            const bool row_ok = hr >= 0 && hr < H;
+            if (!row_ok) {
+              // the whole segment is outside the image: vector zero stores over all threads
+              uint4* z = reinterpret_cast<uint4*>(gs);
+              for (int i = pt; i < (int)(L.g_bytes / 16); i += Cfg::kProducers)
+                z[i] = make_uint4(0u, 0u, 0u, 0u);
+            }
+            for (int c = pt; c < Cp && row_ok; c += Cfg::kProducers) {
+              T* dst = gs + (size_t)c * kSeg;
+              const T* src =
+                  gout + ((size_t)n * 4 * C + (size_t)(b + 1) * C + c) * P + (size_t)hr * W;
+              if (c < C && g_bulk) {
+                for (int x = 0; x < lo - (w0 - 8); ++x) dst[x] = T(0.f);
+                for (int x = hi - (w0 - 8); x < kSeg; ++x) dst[x] = T(0.f);
+                const uint32_t bytes = (uint32_t)(hi - lo) * sizeof(T);
+                tc::mbar_expect_tx(&u_full[ub], bytes);  // before the copy can complete
+                tc::bulk_g2s(dst + (lo - (w0 - 8)), src + lo, bytes, &u_full[ub]);
+              } else {
+                for (int x = 0; x < kSeg; ++x) {
+                  const int col = w0 - 8 + x;
+                  dst[x] = (c < C && col >= 0 && col < W) ? src[col] : T(0.f);
+                }
+              }
+            }
           }
+          if (item < items)
+            store_transposed<T, Op, Cfg::kSplit>(reg + (kg * kSeg + jb * 8) * 16, L.reg_part, v);
         }
+        if (failed) break;
         tc::fence_proxy_async_smem();
-        tc::mbar_arrive(&r_full[rb]);
+        tc::mbar_arrive(&u_full[ub]);
       }
+      if (failed) break;
     }
   } else {
     // ---- epilogue: warpgroup wg owns channel blocks wg, wg + 2 ------------
@@ -281,7 +330,7 @@ gencat_bwd_x_kernel(const BxParams p) {
     T* gx = static_cast<T*>(p.gx);
     const float* bias_s = reinterpret_cast<const float*>(smem + L.bias);
     const int nblk = Cp / 16;
-    uint32_t tq = 0;
+    uint32_t tq = 0, uq = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
       const int per_img = H * p.tiles_w;
       const int n = tile / per_img;
@@ -293,13 +342,21 @@ gencat_bwd_x_kernel(const BxParams p) {
 #pragma unroll
       for (int i = 0; i < 16; ++i) acc[0][i] = acc[1][i] = 0.f;
       bool failed = false;
-      for (int b = 0; b < 3 && !failed; ++b) {
+      for (int u = 0; u < kUnits && !failed; ++u, ++uq) {
+        const int b = u / KS, ki = u % KS;
         const int d = p.d[b];
-        for (int tap = 0; tap < KK; ++tap, ++tq) {
-          const int ki = tap / KS, kj = tap % KS;
-          const int dy = (ki - r) * d, dx = (kj - r) * d;
-          const bool ok = px_ok && (unsigned)(h - dy) < (unsigned)H && (unsigned)(w - dx) < (unsigned)W;
-          const size_t src = (size_t)(h - dy) * W + (w - dx);
+        const int ub = uq % NU;
+        if (!warp_wait(&u_full[ub], (uq / NU) & 1, abort_flag)) {
+          fail(abort_flag, p.status, 25);
+          failed = true;
+          break;
+        }
+        const T* gs = reinterpret_cast<const T*>(smem + L.gs + ub * L.g_bytes);
+        for (int kj = 0; kj < KS; ++kj, ++tq) {
+          const int tap = ki * KS + kj;
+          const int dx = (kj - r) * d;
+          // g_b at (h - dy, w - dx): staged column m + 8 - dx (zero off-image)
+          const bool ok = px_ok && (unsigned)(w - dx) < (unsigned)W;
           const int j = tq % NB;
           if (!warp_wait(&t_full[j], (tq / NB) & 1, abort_flag)) {
             fail(abort_flag, p.status, 24);
@@ -314,12 +371,9 @@ gencat_bwd_x_kernel(const BxParams p) {
             float dv[16];
             tc::tmem_ld16(tmem_base + ((uint32_t)(quad * 32) << 16) + j * Cp + blk * 16, dv);
             float gv[16];
+            const T* gcol = gs + (size_t)(blk * 16) * kSeg + (m + 8 - dx);
 #pragma unroll
-            for (int cl = 0; cl < 16; ++cl) {
-              const int c = blk * 16 + cl;
-              gv[cl] = (ok && c < C) ? to_f32<T>(__ldg(gn + (size_t)((b + 1) * C + c) * P + src))
-                                     : 0.f;
-            }
+            for (int cl = 0; cl < 16; ++cl) gv[cl] = ok ? to_f32<T>(gcol[cl * kSeg]) : 0.f;
             tc::tmem_ld_wait();
             if constexpr (!Cfg::kBiasInGemm) {
               const float* bs = bias_s + (b * KK + tap) * Cp + blk * 16;
@@ -333,6 +387,7 @@ gencat_bwd_x_kernel(const BxParams p) {
           tc::tc_fence_before();
           tc::mbar_arrive(&t_empty[j]);
         }
+        if (!failed) tc::mbar_arrive(&g_empty[ub]);
       }
       if (failed) break;
       if (px_ok) {

@@ -44,7 +44,7 @@ constexpr int kDkBytes = kTileM * 128 * 2;  // one dK tile part (bf16 / fp16)
 // is padding (zero rows). gv[b][i] = the pair (g_b[2i], g_b[2i+1]) of this
 // pixel's 16-channel group, packed; products and conversions run on f32x2 /
 // bf16x2 pairs.
-template <typename T, typename Op, bool kSplit, int KS, int OCT>
+template <typename T, typename Op, bool kSplit, int KS, int OCT, int J0 = 0, int JN = 8>
 __device__ __forceinline__ void build_octet(uint8_t* dk, const float4* xc, int xr_plane,
                                             const unsigned long long (&gv)[3][8],
                                             const int (&dil)[3], int m) {
@@ -53,7 +53,7 @@ __device__ __forceinline__ void build_octet(uint8_t* dk, const float4* xc, int x
   const uint32_t base = (m >> 3) * 2048 + (m & 7) * 16;
   const unsigned long long zero2 = 0ull;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
+  for (int j = J0; j < J0 + JN; ++j) {
     const int s = OCT * 8 + j;
     unsigned long long prod[8];
     if (s < 3 * KK) {
@@ -88,6 +88,28 @@ __device__ __forceinline__ void build_dk(uint8_t* dk, int octet, const float4* x
     case 2: build_octet<T, Op, kSplit, KS, 2>(dk, xc, xr_plane, gv, dil, m); break;
     default: build_octet<T, Op, kSplit, KS, 3>(dk, xc, xr_plane, gv, dil, m); break;
   }
+}
+
+// Half of an octet (slots 4*half .. 4*half+3): two builder threads per pixel.
+template <typename T, typename Op, bool kSplit, int KS>
+__device__ __forceinline__ void build_dk_half(uint8_t* dk, int octet, int half, const float4* xc,
+                                              int xr_plane, const unsigned long long (&gv)[3][8],
+                                              const int (&dil)[3], int m) {
+#define DDPM_BUILD_CASE(O, H)                                                           \
+  case O * 2 + H:                                                                       \
+    build_octet<T, Op, kSplit, KS, O, H * 4, 4>(dk, xc, xr_plane, gv, dil, m);          \
+    break;
+  switch (octet * 2 + half) {
+    DDPM_BUILD_CASE(0, 0)
+    DDPM_BUILD_CASE(0, 1)
+    DDPM_BUILD_CASE(1, 0)
+    DDPM_BUILD_CASE(1, 1)
+    DDPM_BUILD_CASE(2, 0)
+    DDPM_BUILD_CASE(2, 1)
+    DDPM_BUILD_CASE(3, 0)
+    default: build_octet<T, Op, kSplit, KS, 3, 4, 4>(dk, xc, xr_plane, gv, dil, m); break;
+  }
+#undef DDPM_BUILD_CASE
 }
 
 // g_b[cg16*16 + cl, pixel] for the three branches (zero off-image / c >= C).
@@ -674,6 +696,389 @@ __global__ void gencat_wreduce_kernel(const float* __restrict__ partial, T* __re
   }
 }
 
+// ========================================================== dY + dW ==========
+// One pass builds every dK tile once and feeds both GEMMs (the separate dY and
+// dW kernels above each build all of dK). CTA = (16-channel group cg, spatial
+// split): D_w of the cg's octets (<= 4 x Nw TMEM columns) accumulates over the
+// split's tiles; per tile, D_y (128 pixels x Cp, double buffered at columns
+// 384 / 448) holds the cg's share of dY and is added into an FP32 dY
+// accumulator with reductions to global memory (the other channel groups'
+// CTAs add theirs). Builders run two threads per pixel (four slots each); one
+// issuer warp per GEMM.
+template <typename T, int KS>
+struct DywCfg {
+  static constexpr bool kSplit = IoTraits<T>::kSplit;
+  static constexpr int kParts = kSplit ? 2 : 1;
+  static constexpr int kDkSlots = kSplit ? 1 : 2;
+  static constexpr int kXBufs = kSplit ? 1 : 2;
+  static constexpr int kYBufs = kSplit ? 1 : 2;
+  static constexpr int kWStages = 2;
+  static constexpr int kProducers = 128;
+  static constexpr int kXItems = (16 * (kTileH + 2 * kMaxHalo) + kProducers - 1) / kProducers;
+  static constexpr int kYItems = (16 * 80 + kProducers - 1) / kProducers;
+  static constexpr int kOct = (3 * KS * KS + 7) / 8;
+  static constexpr int kFirstXWarp = 3, kFirstYWarp = 7, kFirstBuilderWarp = 11;
+  static constexpr int kThreads = 32 * (kFirstBuilderWarp + 8);
+  static constexpr uint32_t kDyCol = 384;
+};
+
+struct DywSmem {
+  uint32_t xr, y, dk, w, bars, total, xr_bytes, y_bytes, dk_bytes, w_bytes;
+};
+
+// C=64, K=3: fp32 37 + 40 + 64 + 2x32 KB = 204 KB; bf16 2x37 + 2x20 + 2x32 + 2x16 KB = 208 KB.
+template <typename T, int KS>
+__host__ __device__ inline DywSmem dyw_smem_layout(int Cp, int Nw, int R) {
+  using Cfg = DywCfg<T, KS>;
+  DywSmem L;
+  L.xr_bytes = (uint32_t)16 * (kTileH + 2 * R) * kHaloCols * 4;
+  L.y_bytes = (uint32_t)Cfg::kParts * kTileM * Nw * 2;
+  L.dk_bytes = (uint32_t)Cfg::kParts * kDkBytes;
+  L.w_bytes = (uint32_t)Cfg::kParts * 128 * Cp * 2;
+  L.xr = 0;
+  L.y = L.xr + Cfg::kXBufs * L.xr_bytes;
+  L.dk = L.y + Cfg::kYBufs * L.y_bytes;
+  L.w = L.dk + Cfg::kDkSlots * L.dk_bytes;
+  L.bars = L.w + Cfg::kWStages * L.w_bytes;
+  L.total = L.bars + 8 * (2 * Cfg::kXBufs + 2 * Cfg::kYBufs + 2 * Cfg::kDkSlots +
+                          2 * Cfg::kWStages + 5);
+  return L;
+}
+
+struct DywParams {
+  const void* x;
+  const void* y;
+  const void* wpack;  // "by" image
+  const void* gout;
+  float* gy_acc;      // FP32 dY accumulator, zeroed before the launch
+  float* partial;     // [splits][NG][128][Nw]
+  int N, C, H, W, Cp, Nw, R;
+  int d[3];
+  int tiles_w, tiles_h, num_tiles;
+  int ngroups, ncg, splits;
+  int* status;
+};
+
+template <typename T, int KS>
+__global__ void __launch_bounds__(DywCfg<T, KS>::kThreads, 1)
+gencat_bwd_dyw_kernel(const DywParams p) {
+  using Cfg = DywCfg<T, KS>;
+  using Op = typename IoTraits<T>::Op;
+  constexpr int NS = Cfg::kDkSlots;
+  constexpr int NX = Cfg::kXBufs;
+  constexpr int NY = Cfg::kYBufs;
+  constexpr int S = Cfg::kWStages;
+  constexpr int NOCT = Cfg::kOct;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ uint32_t tmem_base_s;
+  __shared__ int abort_s;
+
+  const int C = p.C, Cp = p.Cp, H = p.H, W = p.W, R = p.R, Nw = p.Nw;
+  const size_t P = (size_t)H * W;
+  const DywSmem L = dyw_smem_layout<T, KS>(Cp, Nw, R);
+  const int cg = blockIdx.x % p.ncg;
+  const int split = blockIdx.x / p.ncg;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint64_t* x_full = bars;             // [NX]
+  uint64_t* x_empty = x_full + NX;     // [NX]
+  uint64_t* y_full = x_empty + NX;     // [NY]
+  uint64_t* y_empty = y_full + NY;     // [NY]
+  uint64_t* k_full = y_empty + NY;     // [NS]
+  uint64_t* k_empty = k_full + NS;     // [NS]
+  uint64_t* w_full = k_empty + NS;     // [S]
+  uint64_t* w_empty = w_full + S;      // [S]
+  uint64_t* d_full = w_empty + S;      // [2]
+  uint64_t* d_empty = d_full + 2;      // [2]
+  uint64_t* w_done = d_empty + 2;      // [1]
+  const int xr_rows = kTileH + 2 * R;
+  const int xr_plane = xr_rows * kHaloCols;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (warp == 0) {
+    tc::tmem_alloc(&tmem_base_s, 512);
+    tc::tmem_relinquish();
+  }
+  if (threadIdx.x == 32) {
+    for (int i = 0; i < NX; ++i) {
+      tc::mbar_init(&x_full[i], Cfg::kProducers);
+      tc::mbar_init(&x_empty[i], 256);
+    }
+    for (int i = 0; i < NY; ++i) {
+      tc::mbar_init(&y_full[i], Cfg::kProducers);
+      tc::mbar_init(&y_empty[i], 1);
+    }
+    for (int i = 0; i < NS; ++i) {
+      tc::mbar_init(&k_full[i], 256);
+      tc::mbar_init(&k_empty[i], 2);
+    }
+    for (int i = 0; i < S; ++i) {
+      tc::mbar_init(&w_full[i], 1);
+      tc::mbar_init(&w_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(&d_full[i], 1);
+      tc::mbar_init(&d_empty[i], 256);
+    }
+    tc::mbar_init(w_done, 1);
+    tc::fence_mbar_init();
+    abort_s = 0;
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem_base = tmem_base_s;
+  volatile int* abort_flag = &abort_s;
+
+  if (warp == 0) {
+    // ---- the cg's transposed-weight groups, once per tile ---------------------
+    if (lane == 0) {
+      const uint8_t* wsrc = static_cast<const uint8_t*>(p.wpack);
+      uint32_t wq = 0;
+      for (int tile = split; tile < p.num_tiles; tile += p.splits) {
+        for (int oct = 0; oct < NOCT; ++oct, ++wq) {
+          const int s = wq % S;
+          if (!tc::mbar_wait(&w_empty[s], ((wq / S) & 1) ^ 1, abort_flag, kWaitNs)) {
+            fail(abort_flag, p.status, 50);
+            goto done;
+          }
+          tc::mbar_arrive_expect_tx(&w_full[s], L.w_bytes);
+          tc::bulk_g2s(smem + L.w + s * L.w_bytes,
+                       wsrc + (size_t)(cg * NOCT + oct) * L.w_bytes, L.w_bytes, &w_full[s]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---- dY issuer: D_y[tile] = sum over the cg's octets of dK . W -----------
+    if (lane == 0) {
+      const uint32_t idesc = tc::idesc_f16(kTileM, Cp, IoTraits<T>::kBf16, false, false);
+      const uint32_t b_lbo = Cp * 16;
+      const uint64_t b_step = (2 * b_lbo) >> 4;
+      const uint64_t b_lo = (128 * Cp * 2) >> 4;
+      uint32_t wq = 0, kq = 0, it = 0;
+      for (int tile = split; tile < p.num_tiles; tile += p.splits, ++it) {
+        const int tb = it & 1;
+        if (!tc::mbar_wait(&d_empty[tb], ((it >> 1) & 1) ^ 1, abort_flag, kWaitNs)) {
+          fail(abort_flag, p.status, 51);
+          goto done;
+        }
+        tc::tc_fence_after();
+        const uint32_t dt = tmem_base + Cfg::kDyCol + tb * 64;
+        for (int oct = 0; oct < NOCT; ++oct, ++wq, ++kq) {
+          const int s = wq % S, ks_ = kq % NS;
+          if (!tc::mbar_wait(&k_full[ks_], (kq / NS) & 1, abort_flag, kWaitNs) ||
+              !tc::mbar_wait(&w_full[s], (wq / S) & 1, abort_flag, kWaitNs)) {
+            fail(abort_flag, p.status, 52);
+            goto done;
+          }
+          tc::tc_fence_after();
+          // A: dK, K-major (rows are K): row-group stride 128, pixel-group stride 2048
+          const uint64_t ad =
+              tc::smem_desc(tc::smem_u32(smem + L.dk + ks_ * L.dk_bytes), 128, 2048);
+          const uint64_t bd = tc::smem_desc(tc::smem_u32(smem + L.w + s * L.w_bytes), b_lbo, 128);
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks) {
+            const uint64_t a_k = ad + ks * (256 >> 4);
+            const uint64_t b_k = bd + ks * b_step;
+            tc::mma_f16(dt, a_k, b_k, idesc, (oct > 0 || ks > 0) ? 1u : 0u);
+            if constexpr (Cfg::kSplit) {
+              tc::mma_f16(dt, a_k + (kDkBytes >> 4), b_k, idesc, 1u);
+              tc::mma_f16(dt, a_k, b_k + b_lo, idesc, 1u);
+            }
+          }
+          tc::mma_commit(&k_empty[ks_]);
+          tc::mma_commit(&w_empty[s]);
+        }
+        tc::mma_commit(&d_full[tb]);
+      }
+    }
+  } else if (warp == 2) {
+    // ---- dW issuer: D_w[octet] += dK . y over the split's tiles ---------------
+    if (lane == 0) {
+      const uint32_t idesc = tc::idesc_f16(kTileM, Nw, IoTraits<T>::kBf16, true, false);
+      const uint32_t b_lbo = Nw * 16;           // pixel-group stride of the y tile
+      const uint64_t b_step = (2 * b_lbo) >> 4;
+      const uint64_t y_lo = (kTileM * Nw * 2) >> 4;
+      uint32_t kq = 0, it = 0;
+      bool first = true;
+      for (int tile = split; tile < p.num_tiles; tile += p.splits, ++it) {
+        const int yb = it % NY;
+        if (!tc::mbar_wait(&y_full[yb], (it / NY) & 1, abort_flag, kWaitNs)) {
+          fail(abort_flag, p.status, 53);
+          goto done;
+        }
+        tc::tc_fence_after();
+        const uint64_t yd =
+            tc::smem_desc(tc::smem_u32(smem + L.y + yb * L.y_bytes), b_lbo, 128);
+        for (int oct = 0; oct < NOCT; ++oct, ++kq) {
+          const int ks_ = kq % NS;
+          if (!tc::mbar_wait(&k_full[ks_], (kq / NS) & 1, abort_flag, kWaitNs)) {
+            fail(abort_flag, p.status, 54);
+            goto done;
+          }
+          tc::tc_fence_after();
+          // A: dK, MN-major (rows are M, pixels are K): K-group stride 2048, M-group 128
+          const uint64_t ad =
+              tc::smem_desc(tc::smem_u32(smem + L.dk + ks_ * L.dk_bytes), 2048, 128);
+          const uint32_t dt = tmem_base + oct * Nw;
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks) {
+            const uint64_t a_k = ad + ks * ((2 * 2048) >> 4);
+            const uint64_t b_k = yd + ks * b_step;
+            tc::mma_f16(dt, a_k, b_k, idesc, (!first || ks > 0) ? 1u : 0u);
+            if constexpr (Cfg::kSplit) {
+              tc::mma_f16(dt, a_k + (kDkBytes >> 4), b_k, idesc, 1u);
+              tc::mma_f16(dt, a_k, b_k + y_lo, idesc, 1u);
+            }
+          }
+          tc::mma_commit(&k_empty[ks_]);
+        }
+        tc::mma_commit(&y_empty[yb]);
+        first = false;
+      }
+      tc::mma_commit(w_done);
+    }
+  } else if (warp < Cfg::kFirstYWarp) {
+    // ---- x-halo producers (the cg's 16 channels, once per tile) ----------------
+    const int pt = threadIdx.x - 32 * Cfg::kFirstXWarp;
+    const XPlan<Cfg::kXItems> plan = make_xplan<Cfg::kXItems>(xr_rows, pt, Cfg::kProducers);
+    uint32_t xq = 0;
+    for (int tile = split; tile < p.num_tiles && !*abort_flag; tile += p.splits, ++xq) {
+      const int xb = xq % NX;
+      if (!warp_wait(&x_empty[xb], ((xq / NX) & 1) ^ 1, abort_flag)) {
+        fail(abort_flag, p.status, 55);
+        break;
+      }
+      int n, h0, w0;
+      tile_origin(tile, p.tiles_w, p.tiles_h, n, h0, w0);
+      float4* xr = reinterpret_cast<float4*>(smem + L.xr + xb * L.xr_bytes);
+      stage_halo<T, Cfg::kXItems>(plan, static_cast<const T*>(p.x), xr, n, C, H, W, cg * 16,
+                                  h0 - R, w0 - 8, xr_rows);
+      tc::mbar_arrive(&x_full[xb]);
+    }
+  } else if (warp < Cfg::kFirstBuilderWarp) {
+    // ---- y-tile producers (B operand of dW, ones channel at C for db) ---------
+    const int pt = threadIdx.x - 32 * Cfg::kFirstYWarp;
+    const YPlan<Cfg::kYItems> plan = make_yplan<Cfg::kYItems>(Nw, pt, Cfg::kProducers);
+    uint32_t it = 0;
+    for (int tile = split; tile < p.num_tiles && !*abort_flag; tile += p.splits, ++it) {
+      const int yb = it % NY;
+      if (!warp_wait(&y_empty[yb], ((it / NY) & 1) ^ 1, abort_flag)) {
+        fail(abort_flag, p.status, 56);
+        break;
+      }
+      int n, h0, w0;
+      tile_origin(tile, p.tiles_w, p.tiles_h, n, h0, w0);
+      uint8_t* ys = smem + L.y + yb * L.y_bytes;
+      stage_y_mn<T, Op, Cfg::kSplit, Cfg::kYItems>(plan, static_cast<const T*>(p.y), ys,
+                                                   ys + kTileM * Nw * 2, n, C, Nw, C, H, W, h0,
+                                                   w0);
+      tc::fence_proxy_async_smem();
+      tc::mbar_arrive(&y_full[yb]);
+    }
+  } else {
+    // ---- builders (two threads per pixel), D_y and D_w drains ------------------
+    const int half = (warp - Cfg::kFirstBuilderWarp) >> 2;
+    const int quad = warp & 3;               // TMEM lane quadrant
+    const int m = quad * 32 + lane;          // pixel of the tile / weight row of a group
+    const int mr = m >> 4, mc = m & 15;
+    const T* gout = static_cast<const T*>(p.gout);
+    const int dil[3] = {p.d[0], p.d[1], p.d[2]};
+    uint32_t xq = 0, kq = 0, it = 0;
+    bool failed = false;
+    for (int tile = split; tile < p.num_tiles && !failed; tile += p.splits, ++it, ++xq) {
+      int n, h0, w0;
+      tile_origin(tile, p.tiles_w, p.tiles_h, n, h0, w0);
+      const int h = h0 + mr, w = w0 + mc;
+      const bool px_ok = (h < H) && (w < W);
+      const size_t pix = px_ok ? (size_t)h * W + w : 0;
+      const T* gn = gout + (size_t)n * 4 * C * P;
+      unsigned long long gv[3][8];
+      load_gv<T>(gv, gn, C, P, cg, pix, px_ok);
+      const int xb = xq % NX;
+      if (!warp_wait(&x_full[xb], (xq / NX) & 1, abort_flag)) {
+        fail(abort_flag, p.status, 57);
+        failed = true;
+        break;
+      }
+      const float4* xc = reinterpret_cast<const float4*>(smem + L.xr + xb * L.xr_bytes) +
+                         (mr + R) * kHaloCols + (mc + 8);
+      for (int oct = 0; oct < NOCT; ++oct, ++kq) {
+        const int ks_ = kq % NS;
+        if (!warp_wait(&k_empty[ks_], ((kq / NS) & 1) ^ 1, abort_flag)) {
+          fail(abort_flag, p.status, 58);
+          failed = true;
+          break;
+        }
+        build_dk_half<T, Op, Cfg::kSplit, KS>(smem + L.dk + ks_ * L.dk_bytes, oct, half, xc,
+                                              xr_plane, gv, dil, m);
+        tc::fence_proxy_async_smem();
+        tc::mbar_arrive(&k_full[ks_]);
+      }
+      if (failed) break;
+      tc::mbar_arrive(&x_empty[xb]);
+      // D_y of this tile: this thread's 32 output channels of its pixel
+      const int tb = it & 1;
+      if (!warp_wait(&d_full[tb], (it >> 1) & 1, abort_flag)) {
+        fail(abort_flag, p.status, 59);
+        failed = true;
+        break;
+      }
+      tc::tc_fence_after();
+      float dv[2][16];
+      const uint32_t taddr =
+          tmem_base + ((uint32_t)(quad * 32) << 16) + Cfg::kDyCol + tb * 64 + half * 32;
+      tc::tmem_ld16(taddr, dv[0]);
+      tc::tmem_ld16(taddr + 16, dv[1]);
+      tc::tmem_ld_wait();
+      tc::tc_fence_before();
+      tc::mbar_arrive(&d_empty[tb]);
+      if (px_ok) {
+        float* acc = p.gy_acc + (size_t)n * C * P + pix;
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          const int i = half * 32 + k;
+          if (i < C) atomicAdd(acc + (size_t)i * P, dv[k >> 4][k & 15]);
+        }
+      }
+    }
+    // D_w of this CTA's split: lane = weight row, half h drains octets 2h, 2h+1
+    if (!failed && warp_wait(w_done, 0, abort_flag)) {
+      tc::tc_fence_after();
+      for (int oct = 2 * half; oct < 2 * half + 2 && oct < NOCT; ++oct) {
+        const int g = cg * NOCT + oct;
+        float* dst = p.partial + (((size_t)split * p.ngroups + g) * 128 + m) * Nw;
+        for (int c0 = 0; c0 < Nw; c0 += 16) {
+          float dv[16];
+          tc::tmem_ld16(tmem_base + ((uint32_t)(quad * 32) << 16) + oct * Nw + c0, dv);
+          tc::tmem_ld_wait();
+#pragma unroll
+          for (int k = 0; k < 16; k += 4)
+            *reinterpret_cast<float4*>(dst + c0 + k) =
+                make_float4(dv[k], dv[k + 1], dv[k + 2], dv[k + 3]);
+        }
+      }
+    } else if (!failed) {
+      fail(abort_flag, p.status, 49);
+    }
+  }
+done:
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem_base, 512);
+  }
+}
+
+// dY (16-bit) = the FP32 accumulator rounded once.
+template <typename T>
+__global__ void gy_convert_kernel(const float* __restrict__ acc, T* __restrict__ gy, size_t n) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x)
+    gy[i] = from_f32<T>(acc[i]);
+}
+
 // ------------------------------------------------------------- launchers ----
 template <typename T, int KS>
 int launch_y(const ByParams& prm, cudaStream_t st) {
@@ -732,12 +1137,64 @@ WPlan plan_w(int n, int c, int h, int w, int ks) {
   return q;
 }
 
+// Merged dY + dW pass: CTAs = channel groups x splits; workspace = D_w partials,
+// then (16-bit dY only) the FP32 dY accumulator at a 256-byte aligned offset.
+struct DywPlan {
+  int Nw, ncg, splits;
+  size_t partial_bytes, acc_offset, ws_bytes;  // ws_bytes includes the accumulator
+};
+
+DywPlan plan_dyw(int n, int c, int h, int w, int ks) {
+  const gencat::PackLayout pl = gencat::PackLayout::make(c, ks, DDPM_BF16);
+  DywPlan q;
+  q.Nw = gencat::augmented_channels(c);
+  q.ncg = pl.Cp / 16;
+  const int tiles = n * ((h + gencat::kTileH - 1) / gencat::kTileH) *
+                    ((w + gencat::kTileW - 1) / gencat::kTileW);
+  int sp = num_sms() / q.ncg;
+  if (sp < 1) sp = 1;
+  if (sp > tiles) sp = tiles;
+  q.splits = sp;
+  q.partial_bytes = (size_t)sp * pl.NG * 128 * q.Nw * sizeof(float);
+  q.acc_offset = (q.partial_bytes + 255) / 256 * 256;
+  q.ws_bytes = q.acc_offset + (size_t)n * c * h * w * sizeof(float);
+  return q;
+}
+
+template <typename T, int KS>
+int launch_dyw(const DywParams& prm, cudaStream_t st) {
+  using Cfg = DywCfg<T, KS>;
+  const DywSmem L = dyw_smem_layout<T, KS>(prm.Cp, prm.Nw, prm.R);
+  auto fn = gencat_bwd_dyw_kernel<T, KS>;
+  DDPM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total));
+  fn<<<prm.ncg * prm.splits, Cfg::kThreads, L.total, st>>>(prm);
+  DDPM_CHECK_LAUNCH("gencat_bwd_dyw_kernel");
+  return DDPM_OK;
+}
+
+template <typename T>
+int finish_dyw(const DywParams& prm, void* gy, void* gw, void* gb, int c, int ks, int ngroups,
+               cudaStream_t st) {
+  int rc = launch_reduce<T>(prm.partial, gw, gb, c, ks, ngroups, prm.Nw, prm.splits, st);
+  if (rc) return rc;
+  if constexpr (!std::is_same<T, float>::value) {
+    const size_t nel = (size_t)prm.N * c * prm.H * prm.W;
+    const size_t want = (nel + 255) / 256;
+    gy_convert_kernel<T><<<(int)(want < 4096 ? want : 4096), 256, 0, st>>>(
+        prm.gy_acc, static_cast<T*>(gy), nel);
+    DDPM_CHECK_LAUNCH("gy_convert_kernel");
+  }
+  return DDPM_OK;
+}
+
 }  // namespace
 
 size_t gencat_bwd_workspace_bytes(int n, int c, int h, int w, int ks) {
   if (n < 1 || c < 1 || c > gencat::kMaxChannels || h < 1 || w < 1 || (ks != 1 && ks != 3))
     return 0;
-  return plan_w(n, c, h, w, ks).ws_bytes;
+  const size_t a = plan_w(n, c, h, w, ks).ws_bytes;
+  const size_t b = plan_dyw(n, c, h, w, ks).ws_bytes;
+  return a > b ? a : b;
 }
 
 int gencat_bwd_yw(const void* x, const void* y, const void* wpack, const void* gout, void* gy,
@@ -754,6 +1211,56 @@ int gencat_bwd_yw(const void* x, const void* y, const void* wpack, const void* g
   rc = gencat::status_ptr(&status);
   if (rc) return rc;
 
+  if (gy != nullptr && gw != nullptr && gb != nullptr && workspace != nullptr &&
+      (reinterpret_cast<uintptr_t>(workspace) & 255u) == 0) {
+    // merged pass: dK built once for dY and dW
+    const DywPlan q = plan_dyw(n, c, h, w, ks);
+    const size_t need = dt == DDPM_F32 ? q.partial_bytes : q.ws_bytes;
+    if (ws_bytes >= need) {
+      DywParams dp{};
+      dp.x = x;
+      dp.y = y;
+      dp.wpack = static_cast<const uint8_t*>(wpack) + pl.by_offset();
+      dp.gout = gout;
+      dp.partial = static_cast<float*>(workspace);
+      dp.gy_acc = dt == DDPM_F32 ? static_cast<float*>(gy)
+                                 : reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
+                                                            q.acc_offset);
+      dp.N = n;
+      dp.C = c;
+      dp.H = h;
+      dp.W = w;
+      dp.Cp = pl.Cp;
+      dp.Nw = q.Nw;
+      dp.R = R;
+      dp.d[0] = d0;
+      dp.d[1] = d1;
+      dp.d[2] = d2;
+      dp.tiles_w = tiles_w;
+      dp.tiles_h = tiles_h;
+      dp.num_tiles = n * tiles_w * tiles_h;
+      dp.ngroups = pl.NG;
+      dp.ncg = q.ncg;
+      dp.splits = q.splits;
+      dp.status = status;
+      DDPM_CUDA_TRY(cudaMemsetAsync(dp.gy_acc, 0, (size_t)n * c * h * w * sizeof(float), st));
+      switch (dt * 10 + ks) {
+        case DDPM_BF16 * 10 + 1: rc = launch_dyw<__nv_bfloat16, 1>(dp, st); break;
+        case DDPM_BF16 * 10 + 3: rc = launch_dyw<__nv_bfloat16, 3>(dp, st); break;
+        case DDPM_F16 * 10 + 1: rc = launch_dyw<__half, 1>(dp, st); break;
+        case DDPM_F16 * 10 + 3: rc = launch_dyw<__half, 3>(dp, st); break;
+        case DDPM_F32 * 10 + 1: rc = launch_dyw<float, 1>(dp, st); break;
+        case DDPM_F32 * 10 + 3: rc = launch_dyw<float, 3>(dp, st); break;
+        default: rc = set_error(DDPM_ERR_UNSUPPORTED, "unsupported dtype/kernel size");
+      }
+      if (rc) return rc;
+      switch (dt) {
+        case DDPM_BF16: return finish_dyw<__nv_bfloat16>(dp, gy, gw, gb, c, ks, pl.NG, st);
+        case DDPM_F16: return finish_dyw<__half>(dp, gy, gw, gb, c, ks, pl.NG, st);
+        default: return finish_dyw<float>(dp, gy, gw, gb, c, ks, pl.NG, st);
+      }
+    }
+  }
   if (gy != nullptr) {
     ByParams bp{};
     bp.x = x;

@@ -103,6 +103,14 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 
 // 1-D bulk copy global -> shared, completion counted on `bar` (bytes).
 // Both addresses 16-byte aligned, size a multiple of 16.
+// Add `bytes` to the barrier's expected transaction count without arriving
+// (for producers that arrive separately after issuing their copies).
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
                                          uint64_t* bar) {
   asm volatile(

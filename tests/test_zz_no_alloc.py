@@ -2,9 +2,11 @@
 against the workspace entry point (``ddpm_gencat_bwd_yw``), through the C ABI.
 
 The static variant keeps its dW/db partials in a fixed 8 MiB device array and
-caps the spatial split count to fit, so dY must match bit for bit (same
-kernel) while dW/db match to FP32 summation-order rounding. It is called twice
-in a row to show that the shared scratch needs no clearing between calls.
+caps the spatial split count to fit; it computes dY with the separate dY
+kernel while the workspace entry builds dK once for dY and dW and sums the
+channel groups' dY shares with FP32 atomics, so all outputs agree to
+summation-order rounding. It is called twice in a row to show that the
+shared scratch needs no clearing between calls (those two agree exactly).
 """
 
 from __future__ import annotations
@@ -19,7 +21,7 @@ pytestmark = pytest.mark.gpu
 # (n, c, h, w): the last shape needs more than 8 MiB of partials at the
 # workspace path's split count, so the static variant runs with fewer splits.
 SHAPES = [(2, 24, 15, 17), (1, 64, 128, 128)]
-# max |static - workspace| / max |workspace| for dW and db
+# max |static - workspace| / max |workspace| for dY, dW and db
 PARAM_TOL = {torch.float32: 1e-4, torch.bfloat16: 1e-2}
 
 
@@ -69,8 +71,7 @@ def test_static_scratch_matches_workspace_entry(shape, ks, dtype):
     torch.cuda.synchronize()
 
     for gy, gw, gb in results:
-        assert torch.equal(gy, gy_ref)
-        for got, ref in ((gw, gw_ref), (gb, gb_ref)):
+        for got, ref in ((gy, gy_ref), (gw, gw_ref), (gb, gb_ref)):
             assert torch.isfinite(got).all()
             scale = ref.double().abs().max().item() + 1e-12
             err = (got.double() - ref.double()).abs().max().item() / scale
