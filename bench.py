@@ -348,11 +348,22 @@ def library_kernels(model, x, y, dtype, device):
     fgout = torch.randn_like(x)
     fgx = torch.empty_like(out)
     fuse_flops = 2 * (4 * C) * C * 9 * n * H * W
-    keep = (taps, out, gout, gx, gk, packed, out2, gy, gw, gb, ws, fpacked, fout, fgout, fgx)
+    fgw = torch.empty_like(fuse_w)
+    fgb = torch.empty_like(fuse_b)
+    fws_bytes = int(_lib.load().ddpm_fuseconv_bwd_weight_workspace_bytes(n, 4 * C, C, H, W))
+    fws = torch.empty(fws_bytes, dtype=torch.uint8, device=device)
+    keep = (taps, out, gout, gx, gk, packed, out2, gy, gw, gb, ws, fpacked, fout, fgout, fgx,
+            fgw, fgb, fws)
     return keep, {
         "fuseconv_fwd": (
             lambda: _lib.call("ddpm_fuseconv_fwd", out.data_ptr(), fpacked.data_ptr(),
                               fuse_b.data_ptr(), fout.data_ptr(), n, 4 * C, C, H, W, code, sh),
+            "tensor", fuse_flops,
+        ),
+        "fuseconv_wgrad": (
+            lambda: _lib.call("ddpm_fuseconv_bwd_weight", out.data_ptr(), fgout.data_ptr(),
+                              fgw.data_ptr(), fgb.data_ptr(), fws.data_ptr(), fws_bytes,
+                              n, 4 * C, C, H, W, code, sh),
             "tensor", fuse_flops,
         ),
         "fuseconv_dgrad": (
@@ -544,7 +555,7 @@ def main(argv=None):
     # dominant kernel among those the headline step launches
     in_step = {"fused": ("gencat_fwd", "gencat_bwd_x", "gencat_bwd_yw"),
                "materialised": ("dyncat_fwd", "dyncat_bwd")}[headline["path"]]
-    in_step = in_step + ("fuseconv_fwd", "fuseconv_dgrad")
+    in_step = in_step + ("fuseconv_fwd", "fuseconv_dgrad", "fuseconv_wgrad")
     dominant = max((k for k in roof if k in in_step), key=lambda k: roof[k]["ms"])
     if rank == 0:
         px = args.batch * world * H * W

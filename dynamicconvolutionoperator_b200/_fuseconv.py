@@ -9,7 +9,8 @@ on the library's tensor-core kernels instead (``ddpm_fuseconv_*`` in
 FP32 accumulator before a single output rounding. Same parameters, same
 autograd contract as ``nn.Conv2d``.
 
-The weight gradient still goes through ``torch.nn.grad.conv2d_weight``.
+The backward runs on the same library: data gradient (shifted-window GEMM)
+and weight / bias gradient (split spatial reduction into FP32 partials).
 """
 
 from __future__ import annotations
@@ -91,10 +92,18 @@ class _FuseConv(torch.autograd.Function):
             _lib.call("ddpm_fuseconv_bwd_data", g.data_ptr(), ctx.packed.data_ptr(),
                       gx.data_ptr(), n, cin, cout, h, w, _lib.dtype_code(x.dtype),
                       _lib.stream_handle(x.device))
-        if ctx.needs_input_grad[1]:
-            gw = torch.nn.grad.conv2d_weight(x, weight.shape, g, 1, 1)
-        if ctx.has_bias and ctx.needs_input_grad[2]:
-            gb = g.sum(dim=(0, 2, 3))
+        need_b = ctx.has_bias and ctx.needs_input_grad[2]
+        if ctx.needs_input_grad[1] or need_b:
+            gw = torch.empty_like(weight)
+            gb = torch.empty(cout, dtype=x.dtype, device=x.device) if need_b else None
+            nbytes = int(_lib.load().ddpm_fuseconv_bwd_weight_workspace_bytes(n, cin, cout, h, w))
+            ws = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
+            _lib.call("ddpm_fuseconv_bwd_weight", x.data_ptr(), g.data_ptr(), gw.data_ptr(),
+                      gb.data_ptr() if gb is not None else None, ws.data_ptr(), nbytes,
+                      n, cin, cout, h, w, _lib.dtype_code(x.dtype),
+                      _lib.stream_handle(x.device))
+            if not ctx.needs_input_grad[1]:
+                gw = None
         return gx, gw, gb, None
 
 

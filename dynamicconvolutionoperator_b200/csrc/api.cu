@@ -63,6 +63,9 @@ int fuseconv_dgrad(const void* gout, const void* packed, void* gcat, int n, int 
 namespace gencat {
 int read_status(int reset, int* code);
 }
+size_t fuseconv_wgrad_workspace_bytes(int n, int cin, int cout, int h, int w);
+int fuseconv_wgrad(const void* cat, const void* gout, void* gw, void* gb, void* ws, size_t ws_bytes,
+                   int n, int cin, int cout, int h, int w, int dt, cudaStream_t st);
 }  // namespace ddpm
 
 extern "C" {
@@ -175,6 +178,18 @@ int ddpm_fuseconv_bwd_data(const void* grad_out, const void* packed, void* grad_
 int ddpm_device_status(int reset, int* code) {
   ddpm::clear_error();
   return ddpm::gencat::read_status(reset, code);
+}
+
+size_t ddpm_fuseconv_bwd_weight_workspace_bytes(int n, int cin, int cout, int h, int w) {
+  return ddpm::fuseconv_wgrad_workspace_bytes(n, cin, cout, h, w);
+}
+
+int ddpm_fuseconv_bwd_weight(const void* x, const void* grad_out, void* grad_weight,
+                             void* grad_bias, void* workspace, size_t workspace_bytes, int n,
+                             int cin, int cout, int h, int w, int dtype, void* stream) {
+  ddpm::clear_error();
+  return ddpm::fuseconv_wgrad(x, grad_out, grad_weight, grad_bias, workspace, workspace_bytes, n,
+                              cin, cout, h, w, dtype, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -232,6 +232,21 @@ __device__ __forceinline__ Raw8<T> load_raw8(const T* __restrict__ plane, int H,
   return r;
 }
 
+// Eight elements at a 16-byte aligned address, no bounds logic: callers
+// pass a safe address for items they will zero afterwards (so every load of
+// a batch is issued before the first one is waited on).
+template <typename T>
+__device__ __forceinline__ Raw8<T> ldg_raw8(const T* src) {
+  Raw8<T> r;
+  if constexpr (sizeof(T) == 2) {
+    r.u = __ldg(reinterpret_cast<const uint4*>(src));
+  } else {
+    r.a = __ldg(reinterpret_cast<const float4*>(src));
+    r.b = __ldg(reinterpret_cast<const float4*>(src) + 1);
+  }
+  return r;
+}
+
 // Write 8 elements as one 16-byte MMA operand row (bf16/fp16 copy through;
 // fp32 split into a bf16 hi row at `hi` and a bf16 residual row at `lo`).
 template <typename T, typename Op, bool kSplit>
@@ -461,6 +476,29 @@ __device__ __forceinline__ void store8x2_split(uint8_t* dst_hi, uint8_t* dst_lo,
       l[i] = cvt2<Op>(a, b);
     }
     *reinterpret_cast<uint4*>(dst_lo) = make_uint4(l[0], l[1], l[2], l[3]);
+  }
+}
+
+// Eight elements as four 32-bit words of two operand values (element 2i in
+// the low half of word i); with kSplit (FP32) the bf16 hi words and the
+// bf16 residual words (v - hi, exact subtraction).
+template <typename T, typename Op, bool kSplit>
+__device__ __forceinline__ void raw8_words(const Raw8<T>& r, uint32_t (&hi)[4], uint32_t (&lo)[4]) {
+  if constexpr (!kSplit) {
+    hi[0] = r.u.x;
+    hi[1] = r.u.y;
+    hi[2] = r.u.z;
+    hi[3] = r.u.w;
+  } else {
+    const unsigned long long neg1 = f2_pack(-1.f, -1.f);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float a = r.get(2 * i), b = r.get(2 * i + 1);
+      hi[i] = cvt2<Op>(a, b);
+      float ra, rb;
+      f2_unpack(f2_fma(uncvt2<Op>(hi[i]), neg1, f2_pack(a, b)), ra, rb);
+      lo[i] = cvt2<Op>(ra, rb);
+    }
   }
 }
 

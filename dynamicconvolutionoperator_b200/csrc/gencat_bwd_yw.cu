@@ -703,8 +703,9 @@ __global__ void gencat_wreduce_kernel(const float* __restrict__ partial, T* __re
 // split's tiles; per tile, D_y (128 pixels x Cp, double buffered at columns
 // 384 / 448) holds the cg's share of dY and is added into an FP32 dY
 // accumulator with reductions to global memory (the other channel groups'
-// CTAs add theirs). Builders run two threads per pixel (four slots each); one
-// issuer warp per GEMM.
+// CTAs add theirs); the x-halo producer warps do that drain for the previous
+// tile while the builders work on the next. Builders run two threads per
+// pixel (four slots each); one issuer warp per GEMM.
 template <typename T, int KS>
 struct DywCfg {
   static constexpr bool kSplit = IoTraits<T>::kSplit;
@@ -818,7 +819,7 @@ gencat_bwd_dyw_kernel(const DywParams p) {
     }
     for (int i = 0; i < 2; ++i) {
       tc::mbar_init(&d_full[i], 1);
-      tc::mbar_init(&d_empty[i], 256);
+      tc::mbar_init(&d_empty[i], Cfg::kProducers);
     }
     tc::mbar_init(w_done, 1);
     tc::fence_mbar_init();
@@ -939,14 +940,42 @@ gencat_bwd_dyw_kernel(const DywParams p) {
       tc::mma_commit(w_done);
     }
   } else if (warp < Cfg::kFirstYWarp) {
-    // ---- x-halo producers (the cg's 16 channels, once per tile) ----------------
+    // ---- x-halo producers (the cg's 16 channels, once per tile), who also
+    //      drain the previous tile's D_y into the FP32 dY accumulator -----------
     const int pt = threadIdx.x - 32 * Cfg::kFirstXWarp;
+    const int quad = warp & 3;               // TMEM lane quadrant
+    const int m = quad * 32 + lane;          // pixel of the drained tile
     const XPlan<Cfg::kXItems> plan = make_xplan<Cfg::kXItems>(xr_rows, pt, Cfg::kProducers);
+    // D_y of the it-th tile of this split: 64 columns of this thread's pixel
+    auto drain = [&](uint32_t it) -> bool {
+      const int tb = it & 1;
+      if (!warp_wait(&d_full[tb], (it >> 1) & 1, abort_flag)) return false;
+      tc::tc_fence_after();
+      float dv[4][16];
+      const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + Cfg::kDyCol + tb * 64;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) tc::tmem_ld16(taddr + q * 16, dv[q]);
+      tc::tmem_ld_wait();
+      tc::tc_fence_before();
+      tc::mbar_arrive(&d_empty[tb]);
+      int n, h0, w0;
+      tile_origin(split + (int)it * p.splits, p.tiles_w, p.tiles_h, n, h0, w0);
+      const int h = h0 + (m >> 4), w = w0 + (m & 15);
+      if (h < H && w < W) {
+        float* acc = p.gy_acc + (size_t)n * C * P + (size_t)h * W + w;
+#pragma unroll
+        for (int k = 0; k < 64; ++k)
+          if (k < C) atomicAdd(acc + (size_t)k * P, dv[k >> 4][k & 15]);
+      }
+      return true;
+    };
     uint32_t xq = 0;
+    bool failed = false;
     for (int tile = split; tile < p.num_tiles && !*abort_flag; tile += p.splits, ++xq) {
       const int xb = xq % NX;
       if (!warp_wait(&x_empty[xb], ((xq / NX) & 1) ^ 1, abort_flag)) {
         fail(abort_flag, p.status, 55);
+        failed = true;
         break;
       }
       int n, h0, w0;
@@ -955,7 +984,13 @@ gencat_bwd_dyw_kernel(const DywParams p) {
       stage_halo<T, Cfg::kXItems>(plan, static_cast<const T*>(p.x), xr, n, C, H, W, cg * 16,
                                   h0 - R, w0 - 8, xr_rows);
       tc::mbar_arrive(&x_full[xb]);
+      if (xq > 0 && !drain(xq - 1)) {
+        fail(abort_flag, p.status, 59);
+        failed = true;
+        break;
+      }
     }
+    if (!failed && xq > 0 && !drain(xq - 1)) fail(abort_flag, p.status, 59);
   } else if (warp < Cfg::kFirstBuilderWarp) {
     // ---- y-tile producers (B operand of dW, ones channel at C for db) ---------
     const int pt = threadIdx.x - 32 * Cfg::kFirstYWarp;
@@ -984,9 +1019,9 @@ gencat_bwd_dyw_kernel(const DywParams p) {
     const int mr = m >> 4, mc = m & 15;
     const T* gout = static_cast<const T*>(p.gout);
     const int dil[3] = {p.d[0], p.d[1], p.d[2]};
-    uint32_t xq = 0, kq = 0, it = 0;
+    uint32_t xq = 0, kq = 0;
     bool failed = false;
-    for (int tile = split; tile < p.num_tiles && !failed; tile += p.splits, ++it, ++xq) {
+    for (int tile = split; tile < p.num_tiles && !failed; tile += p.splits, ++xq) {
       int n, h0, w0;
       tile_origin(tile, p.tiles_w, p.tiles_h, n, h0, w0);
       const int h = h0 + mr, w = w0 + mc;
@@ -1017,30 +1052,6 @@ gencat_bwd_dyw_kernel(const DywParams p) {
       }
       if (failed) break;
       tc::mbar_arrive(&x_empty[xb]);
-      // D_y of this tile: this thread's 32 output channels of its pixel
-      const int tb = it & 1;
-      if (!warp_wait(&d_full[tb], (it >> 1) & 1, abort_flag)) {
-        fail(abort_flag, p.status, 59);
-        failed = true;
-        break;
-      }
-      tc::tc_fence_after();
-      float dv[2][16];
-      const uint32_t taddr =
-          tmem_base + ((uint32_t)(quad * 32) << 16) + Cfg::kDyCol + tb * 64 + half * 32;
-      tc::tmem_ld16(taddr, dv[0]);
-      tc::tmem_ld16(taddr + 16, dv[1]);
-      tc::tmem_ld_wait();
-      tc::tc_fence_before();
-      tc::mbar_arrive(&d_empty[tb]);
-      if (px_ok) {
-        float* acc = p.gy_acc + (size_t)n * C * P + pix;
-#pragma unroll
-        for (int k = 0; k < 32; ++k) {
-          const int i = half * 32 + k;
-          if (i < C) atomicAdd(acc + (size_t)i * P, dv[k >> 4][k & 15]);
-        }
-      }
     }
     // D_w of this CTA's split: lane = weight row, half h drains octets 2h, 2h+1
     if (!failed && warp_wait(w_done, 0, abort_flag)) {

@@ -101,6 +101,16 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Four 8x8 matrices of 16-bit elements stored transposed (warp-collective).
+// Register i of lane t holds elements (row t/4, columns 2(t%4) and 2(t%4)+1)
+// of matrix i; column r of matrix i (8 elements, 16 bytes) is written to the
+// shared address that lane 8i + r supplies.
+__device__ __forceinline__ void stmatrix_x4_trans(uint32_t addr, uint32_t r0, uint32_t r1,
+                                                  uint32_t r2, uint32_t r3) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.trans.shared.b16 [%0], {%1, %2, %3, %4};"
+               :: "r"(addr), "r"(r0), "r"(r1), "r"(r2), "r"(r3) : "memory");
+}
+
 // 1-D bulk copy global -> shared, completion counted on `bar` (bytes).
 // Both addresses 16-byte aligned, size a multiple of 16.
 // Add `bytes` to the barrier's expected transaction count without arriving

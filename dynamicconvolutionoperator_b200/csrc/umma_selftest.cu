@@ -6,7 +6,10 @@
 //   variant 1: A MN-major, B K-major
 //   variant 2: A K-major, window starting `shift` rows into the staged tile
 //              (any row offset, not only multiples of 8)
-// D[m, n] = sum_k A[shift + m, k] * B[n, k]; A, B row-major bf16 in global,
+//   variant 3: A K-major, B MN-major with its K window starting `shift` rows
+//              into the staged tile (B given as [n, k + shift])
+// D[m, n] = sum_k A[shift + m, k] * B[n, k] (variants 0-2) or
+// sum_k A[m, k] * B[n, shift + k] (variant 3); A, B row-major bf16 in global,
 // D row-major fp32.
 #include "common.cuh"
 #include "tc.cuh"
@@ -27,7 +30,9 @@ umma_selftest_kernel(const __nv_bfloat16* __restrict__ A, const __nv_bfloat16* _
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const int rows_a = kM + shift;
+  const bool b_mn = (variant == 3);
+  const int rows_a = b_mn ? kM : kM + shift;
+  const int kb = b_mn ? K + shift : K;  // staged K extent of B
   uint8_t* sA = smem;
   uint8_t* sB = smem + (size_t)rows_a * K * 2;
 
@@ -52,9 +57,13 @@ umma_selftest_kernel(const __nv_bfloat16* __restrict__ A, const __nv_bfloat16* _
     }
     *reinterpret_cast<__nv_bfloat16*>(sA + off) = A[i];
   }
-  for (int i = tid; i < N * K; i += blockDim.x) {
-    const int r = i / K, k = i - (i / K) * K;
-    const uint32_t off = ((k >> 3) * N + r) * 16 + (k & 7) * 2;  // LBO = N*16, SBO = 128
+  for (int i = tid; i < N * kb; i += blockDim.x) {
+    const int r = i / kb, k = i - (i / kb) * kb;
+    uint32_t off;
+    if (!b_mn)
+      off = ((k >> 3) * N + r) * 16 + (k & 7) * 2;  // LBO = N*16, SBO = 128
+    else
+      off = (r >> 3) * (kb * 16) + k * 16 + (r & 7) * 2;  // LBO = 128, SBO = kb*16
     *reinterpret_cast<__nv_bfloat16*>(sB + off) = B[i];
   }
   tc::fence_proxy_async_smem();
@@ -66,7 +75,7 @@ umma_selftest_kernel(const __nv_bfloat16* __restrict__ A, const __nv_bfloat16* _
   if (tid == 0) {
     const uint32_t a0 = tc::smem_u32(sA);
     const uint32_t b0 = tc::smem_u32(sB);
-    const uint32_t idesc = tc::idesc_f16(kM, N, true, a_mn, false);
+    const uint32_t idesc = tc::idesc_f16(kM, N, true, a_mn, b_mn);
     for (int ks = 0; ks < K / 16; ++ks) {
       uint64_t ad, bd;
       if (!a_mn) {
@@ -75,8 +84,12 @@ umma_selftest_kernel(const __nv_bfloat16* __restrict__ A, const __nv_bfloat16* _
       } else {
         ad = tc::smem_desc(a0 + ks * 2 * 128, 128, K * 16);
       }
-      const uint32_t lbob = N * 16;
-      bd = tc::smem_desc(b0 + ks * 2 * lbob, lbob, 128);
+      if (!b_mn) {
+        const uint32_t lbob = N * 16;
+        bd = tc::smem_desc(b0 + ks * 2 * lbob, lbob, 128);
+      } else {
+        bd = tc::smem_desc(b0 + shift * 16 + ks * 2 * 128, 128, kb * 16);
+      }
       tc::mma_f16(tmem, ad, bd, idesc, ks > 0 ? 1u : 0u);
     }
     tc::mma_commit(&bar);
@@ -110,11 +123,12 @@ __device__ int g_selftest_status;
 int umma_selftest(int variant, const void* a, const void* b, float* d, int n, int k, int shift,
                   cudaStream_t st) {
   DDPM_CHECK_ARG(a && b && d, "null pointer");
-  DDPM_CHECK_ARG(variant >= 0 && variant <= 2, "variant must be 0, 1 or 2");
+  DDPM_CHECK_ARG(variant >= 0 && variant <= 3, "variant must be 0, 1, 2 or 3");
   DDPM_CHECK_ARG(n >= 16 && n <= 256 && n % 16 == 0, "n must be a multiple of 16 in [16, 256]");
   DDPM_CHECK_ARG(k >= 16 && k <= 128 && k % 16 == 0, "k must be a multiple of 16 in [16, 128]");
-  DDPM_CHECK_ARG(shift >= 0 && shift <= 32 && (variant == 2 || shift == 0), "bad shift");
-  const size_t smem = (size_t)(kM + shift) * k * 2 + (size_t)n * k * 2;
+  DDPM_CHECK_ARG(shift >= 0 && shift <= 32 && (variant >= 2 || shift == 0), "bad shift");
+  const size_t smem = variant == 3 ? (size_t)kM * k * 2 + (size_t)n * (k + shift) * 2
+                                   : (size_t)(kM + shift) * k * 2 + (size_t)n * k * 2;
   DDPM_CUDA_TRY(cudaFuncSetAttribute(umma_selftest_kernel,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   int* status = nullptr;

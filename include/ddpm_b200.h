@@ -185,6 +185,16 @@ DDPM_API int ddpm_fuseconv_fwd(const void* x, const void* packed, const void* bi
 DDPM_API int ddpm_fuseconv_bwd_data(const void* grad_out, const void* packed, void* grad_x,
                                     int n, int cin, int cout, int h, int w, int dtype,
                                     void* stream);
+/* grad_weight[o, i, ky, kx] = sum_p grad_out[o, p] * x[i, p + (ky-1, kx-1)] and
+ * grad_bias[o] = sum_p grad_out[o, p] (grad_bias may be NULL): the cuDNN weight
+ * gradient of the same convolution. FP32 split partials in `workspace`
+ * (ddpm_fuseconv_bwd_weight_workspace_bytes() bytes, 16-byte aligned), then a
+ * reduce kernel; weight layout [Cout, Cin, 3, 3]. */
+DDPM_API size_t ddpm_fuseconv_bwd_weight_workspace_bytes(int n, int cin, int cout, int h, int w);
+DDPM_API int ddpm_fuseconv_bwd_weight(const void* x, const void* grad_out, void* grad_weight,
+                                      void* grad_bias, void* workspace, size_t workspace_bytes,
+                                      int n, int cin, int cout, int h, int w, int dtype,
+                                      void* stream);
 
 /*
  * No-allocation variant of ddpm_gencat_bwd_yw (no counterpart in the
@@ -215,7 +225,9 @@ DDPM_API int ddpm_gencat_bwd_yw_static(const void* x, const void* y, const void*
  * on a single CTA with the operand layouts the fused kernels use.
  * a: [128 + shift, k] row-major bf16, b: [n, k] row-major bf16,
  * d: [128, n] row-major fp32, d[m, j] = sum_i a[shift + m, i] * b[j, i].
- * variant 0: K-major A; 1: MN-major A; 2: K-major A read from row `shift`.
+ * variant 0: K-major A; 1: MN-major A; 2: K-major A read from row `shift`;
+ * 3: MN-major B (given as [n, k + shift]) read from K row `shift`,
+ *    d[m, n] = sum_i a[m, i] * b[n, shift + i].
  */
 DDPM_API int ddpm_umma_selftest(int variant, const void* a, const void* b, float* d,
                                 int n, int k, int shift, void* stream);

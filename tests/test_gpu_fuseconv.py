@@ -90,3 +90,30 @@ def test_fuseconv_rejects_unsupported():
     assert lib.ddpm_fuseconv_pack_bytes(257, 64, 0) == 0
     rc = lib.ddpm_fuseconv_fwd(None, None, None, None, 1, 256, 65, 4, 4, 0, None)
     assert rc == -2
+
+
+@pytest.mark.parametrize("shape", SHAPES)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_fuseconv_bwd_weight(shape, dtype):
+    """Weight and bias gradient vs float64 (normalised by the largest gold
+    magnitude: they sum over every pixel)."""
+    from dynamicconvolutionoperator_b200 import _lib
+
+    n, cin, cout, h, w = shape
+    x, wt, _, g = _inputs(shape, dtype, seed=2)
+    xd, gd = x.cuda(), g.cuda()
+    gw = torch.full((cout, cin, 3, 3), float("nan"), dtype=dtype, device="cuda")
+    gb = torch.full((cout,), float("nan"), dtype=dtype, device="cuda")
+    nbytes = int(_lib.load().ddpm_fuseconv_bwd_weight_workspace_bytes(n, cin, cout, h, w))
+    ws = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    _lib.call("ddpm_fuseconv_bwd_weight", xd.data_ptr(), gd.data_ptr(), gw.data_ptr(),
+              gb.data_ptr(), ws.data_ptr(), nbytes, n, cin, cout, h, w, _lib.dtype_code(dtype),
+              _lib.stream_handle(xd.device))
+    torch.cuda.synchronize()
+    gold_w = torch.nn.grad.conv2d_weight(xd.double(), (cout, cin, 3, 3), gd.double(), 1, 1)
+    gold_b = gd.double().sum(dim=(0, 2, 3))
+    tol = 2e-5 if dtype == torch.float32 else 1e-2
+    for got, gold in ((gw, gold_w), (gb, gold_b)):
+        scale = gold.abs().max().item() + 1e-12
+        err = (got.double() - gold).abs().max().item() / scale
+        assert err <= tol, err
