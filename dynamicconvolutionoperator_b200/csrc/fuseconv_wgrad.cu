@@ -20,10 +20,26 @@
 // [split][ic][ky][128][3*Np]; a second kernel sums the splits into dW. While
 // the tiles stream, the drain warps of the (ic 0, ky 1) CTA of every split sum
 // its dout rows per channel into db partials [split][Np].
+//
+// TMA path (W % 8 == 0, 16-byte aligned tensors): a pre-pass writes dout
+// channel-last as operand planes [n][h][o/8][w][8] (bf16 hi + lo planes for
+// FP32) and per-(row, 32-column strip) db partials. The main kernel then has
+// no load warps: one thread issues, per tile and several tiles ahead, the A
+// copy (16-bit: box 64 px x 128 channels, 128-byte swizzle = the canonical
+// K-major SW128 operand) and three B copies, one per kx (box TW px x Np
+// channels of one staged row, x coordinate w0 + 1 - kx px, zero fill outside
+// the image), so the three taps stay one N = 3*Np instruction. (One B copy
+// read through three shifted N = Np windows moves fewer bytes from L2 but
+// re-reads A from shared memory once per tap, and measured slower.) All A
+// stages sit in one shared-memory region and all B stages in another, far
+// apart. FP32 A
+// arrives raw (128-byte swizzled rows of 32 px) in a separate ring and four
+// converter warps split it into the bf16 hi / lo operand.
 #include "common.cuh"
 #include "tc.cuh"
 #include "gencat.cuh"
 #include "fuseconv.cuh"
+#include "tmap.cuh"
 
 namespace ddpm {
 namespace {
@@ -336,37 +352,355 @@ done:
   }
 }
 
-// dW[o, i, ky, kx] = sum over splits of the partials (threads walk the
-// partials' own layout, output channel fastest, so the split-strided reads
-// coalesce; the dW writes scatter), and db[o] = sum over splits of the db
-// partials (items past the dW part).
+// dW[o, i, ky, kx] = sum over splits of the partials. Blocks below `dw_blocks`
+// walk the partials' own layout four columns (output channels) per thread, so
+// the split-strided float4 reads coalesce; the dW writes scatter. Each later
+// block reduces the db partials [parts][Np] of one output channel in a fixed
+// order.
 template <typename T>
-__global__ void fuseconv_wgrad_reduce_kernel(const float* __restrict__ partial,
-                                             const float* __restrict__ db_partial,
-                                             T* __restrict__ dw, T* __restrict__ db, int Cin,
-                                             int Cout, int Np, int nic, int splits) {
-  const long long stride = (long long)nic * 3 * 128 * 3 * Np;
-  const long long total = stride + (db != nullptr ? Cout : 0);
-  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
-       idx += (long long)gridDim.x * blockDim.x) {
-    if (idx >= stride) {
-      const int o = (int)(idx - stride);
-      float acc = 0.f;
-      for (int s = 0; s < splits; ++s) acc += db_partial[(size_t)s * Np + o];
-      db[o] = from_f32<T>(acc);
-      continue;
+__global__ void __launch_bounds__(256) fuseconv_wgrad_reduce_kernel(
+    const float* __restrict__ partial, const float* __restrict__ db_part, T* __restrict__ dw,
+    T* __restrict__ db, int Cin, int Cout, int Np, int nic, int splits, int db_parts,
+    int dw_blocks) {
+  if ((int)blockIdx.x >= dw_blocks) {
+    const int o = blockIdx.x - dw_blocks;
+    float acc = 0.f;
+    for (int k = threadIdx.x; k < db_parts; k += blockDim.x) acc += db_part[(size_t)k * Np + o];
+    __shared__ float red[8];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float t = 0.f;
+      for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += red[i];
+      db[o] = from_f32<T>(t);
     }
+    return;
+  }
+  const long long stride = (long long)nic * 3 * 128 * 3 * Np;  // floats per split
+  const long long quads = stride / 4;
+  for (long long q = blockIdx.x * (long long)blockDim.x + threadIdx.x; q < quads;
+       q += (long long)dw_blocks * blockDim.x) {
+    const long long idx = q * 4;
     const int col = (int)(idx % (3 * Np));
     const long long r = idx / (3 * Np);  // (ic * 3 + ky) * 128 + il
     const int il = (int)(r % 128);
     const int ky = (int)((r / 128) % 3);
     const int ic = (int)(r / (3 * 128));
-    const int kx = col / Np, o = col - kx * Np;
     const int i = ic * 128 + il;
-    if (o >= Cout || i >= Cin) continue;
+    if (i >= Cin) continue;
+    const float4* src = reinterpret_cast<const float4*>(partial + idx);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+    for (int s = 0; s < splits; ++s) {
+      const float4 v = src[(size_t)s * (stride / 4)];
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int kx = (col + e) / Np, o = (col + e) - kx * Np;
+      if (o < Cout) dw[(((size_t)o * Cin + i) * 3 + ky) * 3 + kx] = from_f32<T>(a4[e]);
+    }
+  }
+}
+
+template <typename T>
+int launch_wgrad_reduce(const float* partial, const float* db_part, void* dw, void* db, int cin,
+                        int cout, int Np, int nic, int splits, int db_parts, cudaStream_t st) {
+  const long long quads = (long long)nic * 3 * 128 * 3 * Np / 4;
+  long long blocks = (quads + 255) / 256;
+  if (blocks > 1024) blocks = 1024;
+  const int dw_blocks = (int)blocks;
+  fuseconv_wgrad_reduce_kernel<T><<<dw_blocks + (db != nullptr ? cout : 0), 256, 0, st>>>(
+      partial, db_part, static_cast<T*>(dw), static_cast<T*>(db), cin, cout, Np, nic, splits,
+      db_parts, dw_blocks);
+  DDPM_CHECK_LAUNCH("fuseconv_wgrad_reduce_kernel");
+  return DDPM_OK;
+}
+
+// ------------------------------------------------------------- TMA path ----
+// Pre-pass: dout [N, Cout, H, W] -> operand planes [N][H][Np/8][W][8] of the
+// MMA type (FP32: bf16 hi plane and residual plane), channels >= Cout zero;
+// db partial of the block's 64 columns per channel ->
+// dbp[(n*H + h)*strips + strip][Np]. Block = (image row, 64-column strip):
+// 8 lanes read 8-pixel vectors covering 64 contiguous pixels of one channel,
+// a padded shared tile transposes, and each thread writes 16-byte rows of 8
+// channels (consecutive lanes = consecutive pixels).
+constexpr int kPackCols = 64;
+
+template <typename T>
+__global__ void __launch_bounds__(256) fuseconv_dout_pack_kernel(const T* __restrict__ dout,
+                                                                 uint4* __restrict__ hi,
+                                                                 uint4* __restrict__ lo,
+                                                                 float* __restrict__ dbp, int H,
+                                                                 int W, int Cout, int Np) {
+  using Op = typename IoTraits<T>::Op;
+  constexpr bool kSplit = IoTraits<T>::kSplit;
+  __shared__ float tile[fuseconv::kMaxCout][kPackCols + 1];
+  const int nh = blockIdx.x, n = nh / H, h = nh - n * H;
+  const int w0 = blockIdx.y * kPackCols;
+  const size_t P = (size_t)H * W;
+  const T* src = dout + (size_t)n * Cout * P;
+  // load: item = (channel c, 8-pixel group g)
+  for (int item = threadIdx.x; item < Np * (kPackCols / 8); item += blockDim.x) {
+    const int g = item & 7, c = item >> 3;
+    Raw8<T> v;
+    if (c < Cout)
+      v = load_raw8<T>(src + (size_t)c * P, H, W, h, w0 + g * 8);
+    else
+      v.zero();
+#pragma unroll
+    for (int e = 0; e < 8; ++e) tile[c][g * 8 + e] = v.get(e);
+  }
+  __syncthreads();
+  // db partial: 4 threads per channel, 16 columns each
+  {
+    const int c = threadIdx.x >> 2, q = threadIdx.x & 3;
     float acc = 0.f;
-    for (int s = 0; s < splits; ++s) acc += partial[idx + s * stride];
-    dw[(((size_t)o * Cin + i) * 3 + ky) * 3 + kx] = from_f32<T>(acc);
+    if (c < Np) {
+#pragma unroll
+      for (int x = 0; x < 16; ++x) acc += tile[c][q * 16 + x];
+    }
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    if (c < Np && q == 0) dbp[((size_t)nh * gridDim.y + blockIdx.y) * Np + c] = acc;
+  }
+  const int ng = Np / 8;
+  for (int idx = threadIdx.x; idx < ng * kPackCols; idx += blockDim.x) {
+    const int og = idx / kPackCols, x = idx - og * kPackCols;
+    if (w0 + x >= W) continue;
+    unsigned long long pr[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) pr[e] = f2_pack(tile[og * 8 + 2 * e][x], tile[og * 8 + 2 * e + 1][x]);
+    const size_t dst = ((size_t)nh * ng + og) * W + w0 + x;
+    uint4 vh, vl;
+    store8x2_split<Op, kSplit>(reinterpret_cast<uint8_t*>(&vh), reinterpret_cast<uint8_t*>(&vl), pr);
+    hi[dst] = vh;
+    if constexpr (kSplit) lo[dst] = vl;
+  }
+}
+
+template <typename T>
+struct WtCfg {
+  static constexpr bool kSplit = IoTraits<T>::kSplit;
+  static constexpr int kTW = kSplit ? 32 : 64;  // A row = 128 bytes either way
+  static constexpr int kKSteps = kTW / 16;
+  static constexpr int kStages = kSplit ? 4 : 5;
+  static constexpr int kRaw = 3;                // FP32 raw A ring
+  static constexpr int kConvWarp = 2;           // FP32 converters, then drain: warps 2-5
+  static constexpr int kRawWarp = 6;            // FP32 raw-A copy issuer
+  static constexpr int kThreads = 32 * (kSplit ? 7 : 6);
+  static constexpr uint32_t kAPart = 128 * kTW * 2;            // one bf16/fp16 A image
+  static constexpr uint32_t kABytes = kAPart * (kSplit ? 2 : 1);
+  static constexpr uint32_t kRawBytes = 128 * kTW * 4;         // FP32 raw A tile
+};
+
+struct WtParams {
+  CUtensorMap a;     // cat (16-bit: operand; FP32: raw), box {TW, 1, 128, 1}, SWIZZLE_128B
+  CUtensorMap b_hi;  // dout plane (32-bit view), box {TW*4, Np/8, 1, 1}
+  CUtensorMap b_lo;  // FP32 residual plane
+  float* partial;    // [splits][nic][3][128][3*Np]
+  int H, Np, nic, tiles_w, num_tiles, splits;
+  uint32_t b_copy;       // bytes of one kx copy of B: (Np/8) * TW * 16
+  uint32_t b_stage;      // B images of one stage (3 copies, x2 for FP32), 1024-byte multiple
+  int* status;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(WtCfg<T>::kThreads, 1)
+    fuseconv_wgrad_tma_kernel(const __grid_constant__ WtParams p) {
+  using Cfg = WtCfg<T>;
+  using Op = typename IoTraits<T>::Op;
+  constexpr int S = Cfg::kStages, R = Cfg::kRaw, TW = Cfg::kTW;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint32_t tmem_base_s;
+  __shared__ int abort_s;
+  __shared__ __align__(8) uint64_t bars[2 * S + 2 * R + 1];
+  // 1024-byte aligned operand area (SWIZZLE_128B atoms)
+  uint8_t* base = smem_raw + ((1024u - (tc::smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint8_t* bbase = base + S * Cfg::kABytes;  // B stages
+  uint8_t* raw = bbase + S * p.b_stage;
+  uint64_t* s_full = bars;            // [S] copies (+ FP32 converters)
+  uint64_t* s_empty = bars + S;       // [S] MMA commit
+  uint64_t* r_full = bars + 2 * S;    // [R] raw A copy (FP32)
+  uint64_t* r_empty = r_full + R;     // [R] converters (FP32)
+  uint64_t* d_done = r_empty + R;
+
+  // Loop-invariant parameters in registers: the parameter block's address is
+  // taken (tensor maps), so after every "memory"-clobbering asm statement the
+  // compiler would otherwise reload these through generic loads.
+  const int num_tiles = p.num_tiles, splits = p.splits, H = p.H, tiles_w = p.tiles_w;
+  const uint32_t b_stage = p.b_stage, b_copy = p.b_copy;
+  const int unit = blockIdx.x % (p.nic * 3);
+  const int split = blockIdx.x / (p.nic * 3);
+  const int ic = unit / 3, ky = unit % 3;
+  const int Np = p.Np;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp == 0) {
+    tc::tmem_alloc(&tmem_base_s, 256);
+    tc::tmem_relinquish();
+  }
+  if (threadIdx.x == 32) {
+    for (int i = 0; i < S; ++i) {
+      tc::mbar_init(&s_full[i], Cfg::kSplit ? 1 + 128 : 1);
+      tc::mbar_init(&s_empty[i], 1);
+    }
+    for (int i = 0; i < R; ++i) {
+      tc::mbar_init(&r_full[i], 1);
+      tc::mbar_init(&r_empty[i], 128);
+    }
+    tc::mbar_init(d_done, 1);
+    tc::fence_mbar_init();
+    abort_s = 0;
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem_base = tmem_base_s;
+  volatile int* abort_flag = &abort_s;
+
+  if (warp == 0) {
+    // ---- stage copy issuer ------------------------------------------------------
+    if (lane == 0) {
+      const uint32_t tx = (Cfg::kSplit ? 0u : Cfg::kAPart) + (Cfg::kSplit ? 6u : 3u) * b_copy;
+      uint32_t sq = 0;
+      for (int tile = split; tile < num_tiles; tile += splits, ++sq) {
+        const int per_img = H * tiles_w;
+        const int n = tile / per_img, h = (tile % per_img) / tiles_w;
+        const int w0 = (tile % tiles_w) * TW;
+        const int sb = sq % S;
+        if (!tc::mbar_wait(&s_empty[sb], ((sq / S) & 1) ^ 1, abort_flag, kWaitNs)) {
+          fail(abort_flag, p.status, 73);
+          break;
+        }
+        uint8_t* st = base + sb * Cfg::kABytes;
+        tc::mbar_arrive_expect_tx(&s_full[sb], tx);
+        if constexpr (!Cfg::kSplit) tc::tma_load_4d(st, &p.a, w0, h, ic * 128, n, &s_full[sb]);
+        // B copy kx: dout row h - ky + 1, columns w0 + 1 - kx .. +TW-1 (x in 4-byte units)
+        uint8_t* bst = bbase + sb * b_stage;
+        const int hr = h - ky + 1;
+        for (int kx = 0; kx < 3; ++kx) {
+          tc::tma_load_4d(bst + kx * b_copy, &p.b_hi, (w0 + 1 - kx) * 4, 0, hr, n, &s_full[sb]);
+          if constexpr (Cfg::kSplit)
+            tc::tma_load_4d(bst + (3 + kx) * b_copy, &p.b_lo, (w0 + 1 - kx) * 4, 0, hr, n,
+                            &s_full[sb]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer -------------------------------------------------------------
+    if (lane == 0) {
+      const uint32_t idesc = tc::idesc_f16(128, 3 * Np, IoTraits<T>::kBf16, false, true);
+      constexpr uint64_t b_step = (16 * 16) >> 4;  // 16 pixel rows of B
+      const uint64_t b_lo = (3 * b_copy) >> 4;
+      uint32_t sq = 0;
+      bool first = true;
+      for (int tile = split; tile < num_tiles; tile += splits, ++sq) {
+        const int sb = sq % S;
+        if (!tc::mbar_wait(&s_full[sb], (sq / S) & 1, abort_flag, kWaitNs)) {
+          fail(abort_flag, p.status, 74);
+          goto done;
+        }
+        tc::tc_fence_after();
+        const uint32_t st = tc::smem_u32(base + sb * Cfg::kABytes);
+        const uint64_t bd = tc::smem_desc(tc::smem_u32(bbase + sb * b_stage), 128, TW * 16);
+        if constexpr (!Cfg::kSplit) {
+          const uint64_t ad = tc::smem_desc_sw128(st);
+          for (int ks = 0; ks < Cfg::kKSteps; ++ks)
+            tc::mma_f16(tmem_base, ad + ks * 2, bd + ks * b_step, idesc, (!first || ks > 0) ? 1u : 0u);
+        } else {
+          const uint64_t ad = tc::smem_desc(st, 128 * 16, 128);
+          constexpr uint64_t a_step = (2 * 128 * 16) >> 4;
+          constexpr uint64_t a_lo = Cfg::kAPart >> 4;
+          for (int ks = 0; ks < Cfg::kKSteps; ++ks) {
+            const uint64_t a_k = ad + ks * a_step, b_k = bd + ks * b_step;
+            tc::mma_f16(tmem_base, a_k, b_k, idesc, (!first || ks > 0) ? 1u : 0u);
+            tc::mma_f16(tmem_base, a_k + a_lo, b_k, idesc, 1u);
+            tc::mma_f16(tmem_base, a_k, b_k + b_lo, idesc, 1u);
+          }
+        }
+        tc::mma_commit(&s_empty[sb]);
+        first = false;
+      }
+      tc::mma_commit(d_done);
+    }
+  } else if (Cfg::kSplit && warp == Cfg::kRawWarp) {
+    // ---- FP32 raw A copy issuer ---------------------------------------------------
+    if (lane == 0) {
+      uint32_t sq = 0;
+      for (int tile = split; tile < num_tiles; tile += splits, ++sq) {
+        const int per_img = H * tiles_w;
+        const int n = tile / per_img, h = (tile % per_img) / tiles_w;
+        const int w0 = (tile % tiles_w) * TW;
+        const int rb = sq % R;
+        if (!tc::mbar_wait(&r_empty[rb], ((sq / R) & 1) ^ 1, abort_flag, kWaitNs)) {
+          fail(abort_flag, p.status, 75);
+          break;
+        }
+        tc::mbar_arrive_expect_tx(&r_full[rb], Cfg::kRawBytes);
+        tc::tma_load_4d(raw + rb * Cfg::kRawBytes, &p.a, w0, h, ic * 128, n, &r_full[rb]);
+      }
+    }
+  } else if (warp >= Cfg::kConvWarp && warp < Cfg::kConvWarp + 4) {
+    const int il = (warp - Cfg::kConvWarp) * 32 + lane;  // input channel of the chunk
+    bool ok = true;
+    if constexpr (Cfg::kSplit) {
+      // ---- FP32 converters: raw row il (32 px, 128-byte swizzled) -> A hi / lo ---
+      uint32_t sq = 0;
+      for (int tile = split; tile < num_tiles; tile += splits, ++sq) {
+        const int sb = sq % S, rb = sq % R;
+        if (!warp_wait(&r_full[rb], (sq / R) & 1, abort_flag) ||
+            !warp_wait(&s_empty[sb], ((sq / S) & 1) ^ 1, abort_flag)) {
+          fail(abort_flag, p.status, 76);
+          ok = false;
+          break;
+        }
+        const uint8_t* row = raw + rb * Cfg::kRawBytes + il * 128;
+        uint8_t* a = base + sb * Cfg::kABytes;
+#pragma unroll
+        for (int g = 0; g < TW / 8; ++g) {
+          const float4 u = *reinterpret_cast<const float4*>(row + (((2 * g) ^ (il & 7)) * 16));
+          const float4 v = *reinterpret_cast<const float4*>(row + (((2 * g + 1) ^ (il & 7)) * 16));
+          const unsigned long long pr[4] = {f2_pack(u.x, u.y), f2_pack(u.z, u.w),
+                                            f2_pack(v.x, v.y), f2_pack(v.z, v.w)};
+          const uint32_t off = (g * 128 + il) * 16;
+          store8x2_split<Op, true>(a + off, a + Cfg::kAPart + off, pr);
+        }
+        tc::fence_proxy_async_smem();
+        tc::mbar_arrive(&s_full[sb]);
+        tc::mbar_arrive(&r_empty[rb]);
+      }
+    }
+    // ---- drain: a warp reads TMEM lanes 32 * (warp % 4) .. +31 (channels) ------------
+    const int quad = warp & 3;
+    const int dl = quad * 32 + lane;
+    if (ok && warp_wait(d_done, 0, abort_flag)) {
+      tc::tc_fence_after();
+      float* dst = p.partial + ((((size_t)split * p.nic + ic) * 3 + ky) * 128 + dl) * (3 * Np);
+      for (int c0 = 0; c0 < 3 * Np; c0 += 16) {
+        float v[16];
+        tc::tmem_ld16(tmem_base + ((uint32_t)(quad * 32) << 16) + c0, v);
+        tc::tmem_ld_wait();
+#pragma unroll
+        for (int k = 0; k < 16; k += 4)
+          *reinterpret_cast<float4*>(dst + c0 + k) = make_float4(v[k], v[k + 1], v[k + 2], v[k + 3]);
+      }
+    } else if (ok) {
+      fail(abort_flag, p.status, 77);
+    }
+  }
+done:
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem_base, 256);
   }
 }
 
@@ -390,23 +724,95 @@ WgPlan plan_wgrad(int n, int cin, int cout, int h, int w, int tw) {
   return q;
 }
 
-int wgrad_tile_width(int dt) { return dt == DDPM_F32 ? WgCfg<float>::kTW : WgCfg<__half>::kTW; }
+// TMA path workspace: [partials][db partials][dout plane hi][dout plane lo].
+struct WtPlan {
+  WgPlan g;
+  int strips;  // 64-column pre-pass strips per row (db partials per row)
+  size_t dbp_off, hi_off, lo_off, ws_bytes;
+};
+
+inline size_t round256(size_t v) { return (v + 255) / 256 * 256; }
+
+WtPlan plan_wgrad_tma(int n, int cin, int cout, int h, int w, int tw, bool split) {
+  WtPlan t;
+  t.g = plan_wgrad(n, cin, cout, h, w, tw);
+  t.strips = (w + kPackCols - 1) / kPackCols;
+  const size_t plane = (size_t)n * h * (t.g.Np / 8) * w * 16;
+  t.dbp_off = round256(t.g.partial_bytes);
+  t.hi_off = round256(t.dbp_off + (size_t)n * h * t.strips * t.g.Np * sizeof(float));
+  t.lo_off = round256(t.hi_off + plane);
+  t.ws_bytes = split ? t.lo_off + plane : t.lo_off;
+  return t;
+}
+
+bool wgrad_tma_shape(int w) { return w % 8 == 0; }
 
 template <typename T>
-int run_wgrad(const WgParams& prm, void* dw, void* db, cudaStream_t st) {
+int run_wgrad_reg(const WgParams& prm, void* dw, void* db, cudaStream_t st) {
   using Cfg = WgCfg<T>;
   const WgSmem L = wg_smem_layout(prm, Cfg::kStages);
   auto fn = fuseconv_wgrad_kernel<T>;
   DDPM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total));
   fn<<<prm.nic * 3 * prm.splits, Cfg::kThreads, L.total, st>>>(prm);
   DDPM_CHECK_LAUNCH("fuseconv_wgrad_kernel");
-  const long long total = (long long)prm.nic * 3 * 128 * 3 * prm.Np + prm.Cout;
-  const long long want = (total + 255) / 256;
-  fuseconv_wgrad_reduce_kernel<T><<<(int)(want < 2048 ? want : 2048), 256, 0, st>>>(
-      prm.partial, prm.db_partial, static_cast<T*>(dw), static_cast<T*>(db), prm.Cin, prm.Cout,
-      prm.Np, prm.nic, prm.splits);
-  DDPM_CHECK_LAUNCH("fuseconv_wgrad_reduce_kernel");
-  return DDPM_OK;
+  return launch_wgrad_reduce<T>(prm.partial, prm.db_partial, dw, db, prm.Cin, prm.Cout, prm.Np,
+                                prm.nic, prm.splits, prm.splits, st);
+}
+
+// Returns DDPM_ERR_UNSUPPORTED (nothing launched) when the driver rejects a
+// tensor map, so the caller can take the register path.
+template <typename T>
+int run_wgrad_tma(const void* cat, const void* gout, void* gw, void* gb, uint8_t* ws,
+                  const WtPlan& t, int n, int cin, int cout, int h, int w, int dt, int* status,
+                  cudaStream_t st) {
+  using Cfg = WtCfg<T>;
+  constexpr int TW = Cfg::kTW;
+  const int Np = t.g.Np, ng = Np / 8;
+  const int es = dtype_size(dt);
+  uint4* hi = reinterpret_cast<uint4*>(ws + t.hi_off);
+  uint4* lo = Cfg::kSplit ? reinterpret_cast<uint4*>(ws + t.lo_off) : nullptr;
+  float* dbp = reinterpret_cast<float*>(ws + t.dbp_off);
+  WtParams prm{};
+  const CUtensorMapDataType at = dt == DDPM_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : dt == DDPM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                   : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const uint64_t adims[4] = {(uint64_t)w, (uint64_t)h, (uint64_t)cin, (uint64_t)n};
+  const uint64_t astr[3] = {(uint64_t)w * es, (uint64_t)h * w * es, (uint64_t)cin * h * w * es};
+  const uint32_t abox[4] = {(uint32_t)TW, 1, 128, 1};
+  const uint64_t bdims[4] = {(uint64_t)w * 4, (uint64_t)ng, (uint64_t)h, (uint64_t)n};
+  const uint64_t bstr[3] = {(uint64_t)w * 16, (uint64_t)ng * w * 16, (uint64_t)h * ng * w * 16};
+  const uint32_t bbox[4] = {(uint32_t)TW * 4, (uint32_t)ng, 1, 1};
+  if (encode_tmap(&prm.a, at, 4, cat, adims, astr, abox, CU_TENSOR_MAP_SWIZZLE_128B) != DDPM_OK ||
+      encode_tmap(&prm.b_hi, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, hi, bdims, bstr, bbox,
+                  CU_TENSOR_MAP_SWIZZLE_NONE) != DDPM_OK ||
+      (Cfg::kSplit && encode_tmap(&prm.b_lo, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, lo, bdims, bstr,
+                                  bbox, CU_TENSOR_MAP_SWIZZLE_NONE) != DDPM_OK)) {
+    clear_error();
+    return DDPM_ERR_UNSUPPORTED;
+  }
+  if (!Cfg::kSplit) prm.b_lo = prm.b_hi;
+  prm.partial = reinterpret_cast<float*>(ws);
+  prm.H = h;
+  prm.Np = Np;
+  prm.nic = t.g.nic;
+  prm.tiles_w = t.g.tiles_w;
+  prm.num_tiles = t.g.num_tiles;
+  prm.splits = t.g.splits;
+  prm.b_copy = (uint32_t)ng * TW * 16;
+  prm.b_stage = ((Cfg::kSplit ? 6u : 3u) * prm.b_copy + 1023u) / 1024u * 1024u;
+  prm.status = status;
+
+  fuseconv_dout_pack_kernel<T><<<dim3(n * h, t.strips), 256, 0, st>>>(
+      static_cast<const T*>(gout), hi, lo, dbp, h, w, cout, Np);
+  DDPM_CHECK_LAUNCH("fuseconv_dout_pack_kernel");
+  const size_t smem = (size_t)Cfg::kStages * (Cfg::kABytes + prm.b_stage) +
+                      (Cfg::kSplit ? (size_t)Cfg::kRaw * Cfg::kRawBytes : 0) + 1024;
+  auto fn = fuseconv_wgrad_tma_kernel<T>;
+  DDPM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  fn<<<prm.nic * 3 * prm.splits, Cfg::kThreads, smem, st>>>(prm);
+  DDPM_CHECK_LAUNCH("fuseconv_wgrad_tma_kernel");
+  return launch_wgrad_reduce<T>(prm.partial, dbp, gw, gb, cin, cout, Np, prm.nic, prm.splits,
+                                n * h * t.strips, st);
 }
 
 }  // namespace
@@ -415,10 +821,17 @@ size_t fuseconv_wgrad_workspace_bytes(int n, int cin, int cout, int h, int w) {
   if (n < 1 || h < 1 || w < 1 || cin < 1 || cout < 1 || cin > fuseconv::kMaxCin ||
       cout > fuseconv::kMaxCout)
     return 0;
-  // the larger of the FP32 and 16-bit plans (the split count is shared)
-  const WgPlan a = plan_wgrad(n, cin, cout, h, w, WgCfg<float>::kTW);
-  const WgPlan b = plan_wgrad(n, cin, cout, h, w, WgCfg<__half>::kTW);
-  return a.ws_bytes > b.ws_bytes ? a.ws_bytes : b.ws_bytes;
+  // the largest of the FP32 and 16-bit plans of both paths
+  size_t best = plan_wgrad(n, cin, cout, h, w, WgCfg<float>::kTW).ws_bytes;
+  const size_t b = plan_wgrad(n, cin, cout, h, w, WgCfg<__half>::kTW).ws_bytes;
+  if (b > best) best = b;
+  if (wgrad_tma_shape(w)) {
+    const size_t c = plan_wgrad_tma(n, cin, cout, h, w, WtCfg<float>::kTW, true).ws_bytes;
+    const size_t d = plan_wgrad_tma(n, cin, cout, h, w, WtCfg<__half>::kTW, false).ws_bytes;
+    if (c > best) best = c;
+    if (d > best) best = d;
+  }
+  return best;
 }
 
 int fuseconv_wgrad(const void* cat, const void* gout, void* gw, void* gb, void* ws, size_t ws_bytes,
@@ -429,15 +842,38 @@ int fuseconv_wgrad(const void* cat, const void* gout, void* gw, void* gb, void* 
     return set_error(DDPM_ERR_UNSUPPORTED, "native fuse conv supports Cin <= %d, Cout <= %d",
                      fuseconv::kMaxCin, fuseconv::kMaxCout);
   DDPM_CHECK_ARG(cat && gout && gw, "null pointer");
-  const WgPlan q = plan_wgrad(n, cin, cout, h, w, wgrad_tile_width(dt));
-  if (ws == nullptr || ws_bytes < q.ws_bytes)
-    return set_error(DDPM_ERR_WORKSPACE, "workspace too small (%zu < %zu)", ws_bytes, q.ws_bytes);
-  DDPM_CHECK_ARG((reinterpret_cast<uintptr_t>(ws) & 15u) == 0, "workspace must be 16-byte aligned");
+  const size_t need = fuseconv_wgrad_workspace_bytes(n, cin, cout, h, w);
+  if (ws == nullptr || ws_bytes < need)
+    return set_error(DDPM_ERR_WORKSPACE, "workspace too small (%zu < %zu)", ws_bytes, need);
+  DDPM_CHECK_ARG((reinterpret_cast<uintptr_t>(ws) & 255u) == 0, "workspace must be 256-byte aligned");
   int* status = nullptr;
   int rc = gencat::status_ptr(&status);
   if (rc) return rc;
   const bool split = dt == DDPM_F32;
-  const int tw = wgrad_tile_width(dt);
+  const bool aligned =
+      ((reinterpret_cast<uintptr_t>(cat) | reinterpret_cast<uintptr_t>(gout)) & 15u) == 0;
+  if (aligned && wgrad_tma_shape(w)) {
+    uint8_t* wsb = static_cast<uint8_t*>(ws);
+    switch (dt) {
+      case DDPM_BF16:
+        rc = run_wgrad_tma<__nv_bfloat16>(cat, gout, gw, gb, wsb,
+                                          plan_wgrad_tma(n, cin, cout, h, w, 64, false), n, cin,
+                                          cout, h, w, dt, status, st);
+        break;
+      case DDPM_F16:
+        rc = run_wgrad_tma<__half>(cat, gout, gw, gb, wsb,
+                                   plan_wgrad_tma(n, cin, cout, h, w, 64, false), n, cin, cout, h,
+                                   w, dt, status, st);
+        break;
+      default:
+        rc = run_wgrad_tma<float>(cat, gout, gw, gb, wsb,
+                                  plan_wgrad_tma(n, cin, cout, h, w, 32, true), n, cin, cout, h, w,
+                                  dt, status, st);
+    }
+    if (rc != DDPM_ERR_UNSUPPORTED) return rc;
+  }
+  const int tw = split ? WgCfg<float>::kTW : WgCfg<__half>::kTW;
+  const WgPlan q = plan_wgrad(n, cin, cout, h, w, tw);
   WgParams prm{};
   prm.cat = cat;
   prm.dout = gout;
@@ -455,17 +891,16 @@ int fuseconv_wgrad(const void* cat, const void* gout, void* gw, void* gb, void* 
   prm.tiles_w = q.tiles_w;
   prm.num_tiles = q.num_tiles;
   prm.splits = q.splits;
-  prm.vec = (w % 8) == 0 &&
-            ((reinterpret_cast<uintptr_t>(cat) | reinterpret_cast<uintptr_t>(gout)) & 15u) == 0;
+  prm.vec = (w % 8) == 0 && aligned;
   prm.a_part = (uint32_t)(tw / 8) * 128 * 16;            // pixel groups x 128 channels x 16 B
   prm.a_bytes = prm.a_part * (split ? 2 : 1);
   prm.b_part = (uint32_t)(3 * (q.Np / 8)) * tw * 16;     // [kx][o/8][TW rows][8]
   prm.b_bytes = prm.b_part * (split ? 2 : 1);
   prm.status = status;
   switch (dt) {
-    case DDPM_BF16: return run_wgrad<__nv_bfloat16>(prm, gw, gb, st);
-    case DDPM_F16: return run_wgrad<__half>(prm, gw, gb, st);
-    default: return run_wgrad<float>(prm, gw, gb, st);
+    case DDPM_BF16: return run_wgrad_reg<__nv_bfloat16>(prm, gw, gb, st);
+    case DDPM_F16: return run_wgrad_reg<__half>(prm, gw, gb, st);
+    default: return run_wgrad_reg<float>(prm, gw, gb, st);
   }
 }
 

@@ -10,8 +10,11 @@
 // as a bf16 hi image followed by a bf16 lo (residual) image.
 #include <mutex>
 
+#include <cudaTypedefs.h>
+
 #include "common.cuh"
 #include "gencat.cuh"
+#include "tmap.cuh"
 
 namespace ddpm {
 namespace gencat {
@@ -200,6 +203,36 @@ int gencat_pack(const void* w, const void* bias, int c, int ks, int dt, void* pa
     case DDPM_F32: return launch_pack<float>(w, bias, packed, L, st);
   }
   return set_error(DDPM_ERR_INVALID_ARG, "unknown dtype %d", dt);
+}
+
+int encode_tmap(CUtensorMap* map, CUtensorMapDataType type, int rank, const void* base,
+                const uint64_t* dims, const uint64_t* strides, const uint32_t* box,
+                CUtensorMapSwizzle swizzle) {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (encode == nullptr)
+    return set_error(DDPM_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+  cuuint64_t d[5], s[4];
+  cuuint32_t b[5], e[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1;
+    if (i + 1 < rank) s[i] = strides[i];
+  }
+  const CUresult r = encode(map, type, (cuuint32_t)rank, const_cast<void*>(base), d, s, b, e,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(DDPM_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return DDPM_OK;
 }
 
 }  // namespace ddpm

@@ -130,6 +130,19 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// Tiled tensor copy global -> shared (TMA), 4-D coordinates (innermost
+// first), completion counted on `bar`. `tmap` is the generic address of a
+// CUtensorMap held in kernel parameter space. No cluster multicast.
+__device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, int c0, int c1, int c2,
+                                            int c3, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
+      "r"(smem_u32(bar))
+      : "memory");
+}
+
 // ----------------------------------------------------------------- TMEM ----
 // Allocate `ncols` (power of two >= 32) TMEM columns; the base address is
 // written to `*dst_smem`. Must be executed by one full warp.
@@ -162,6 +175,21 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
   d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
   d |= (uint64_t)1 << 46;  // descriptor version for sm_100
   // base offset 0, lbo mode 0, layout type 0 (SWIZZLE_NONE)
+  return d;
+}
+
+// Descriptor of a K-major operand in the 128-byte swizzled form written by a
+// TMA copy with SWIZZLE_128B: one 128-byte row per M/N index (64 16-bit K
+// elements), 16-byte chunk j of row r stored at chunk j ^ (r % 8), 8-row
+// groups 1024 bytes apart (SBO). The atom base must be 1024-byte aligned; a
+// K step of 16 elements advances the start address by 32 bytes.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1 << 16;            // LBO (unused for swizzled K-major), 16 bytes
+  d |= (uint64_t)(1024 >> 4) << 32;  // SBO
+  d |= (uint64_t)1 << 46;            // descriptor version for sm_100
+  d |= (uint64_t)2 << 61;            // layout type: SWIZZLE_128B
   return d;
 }
 
