@@ -355,8 +355,18 @@ def library_kernels(model, x, y, dtype, device):
     fgb = torch.empty_like(fuse_b)
     fws_bytes = int(_lib.load().ddpm_fuseconv_bwd_weight_workspace_bytes(n, 4 * C, C, H, W))
     fws = torch.empty(fws_bytes, dtype=torch.uint8, device=device)
+    sy_bytes = int(_lib.load().ddpm_gencat_stage_y_bytes(n, C, H, W, K, *DILATIONS, code))
+    sy = torch.empty(sy_bytes, dtype=torch.uint8, device=device)
+
+    def bwd_x():  # as in the training step: stage y, then dX from the staged copy
+        _lib.call("ddpm_gencat_stage_y", y.data_ptr(), sy.data_ptr(), sy_bytes, n, C, H, W, K,
+                  *DILATIONS, code, sh)
+        _lib.call("ddpm_gencat_bwd_x_staged", sy.data_ptr(), sy_bytes, packed.data_ptr(),
+                  gen_b.data_ptr(), gout.data_ptr(), gx.data_ptr(), n, C, H, W, K, *DILATIONS,
+                  code, sh)
+
     keep = (taps, out, gout, gx, gk, packed, out2, gy, gw, gb, ws, fpacked, fout, fgout, fgx,
-            fgw, fgb, fws)
+            fgw, fgb, fws, sy)
     return keep, {
         "fuseconv_fwd": (
             lambda: _lib.call("ddpm_fuseconv_fwd", out.data_ptr(), fpacked.data_ptr(),
@@ -374,12 +384,7 @@ def library_kernels(model, x, y, dtype, device):
                               fgx.data_ptr(), n, 4 * C, C, H, W, code, sh),
             "tensor", fuse_flops,
         ),
-        "gencat_bwd_x": (
-            lambda: _lib.call("ddpm_gencat_bwd_x", y.data_ptr(), packed.data_ptr(),
-                              gen_b.data_ptr(), gout.data_ptr(), gx.data_ptr(), n, C, H, W, K,
-                              *DILATIONS, code, sh),
-            "tensor", gen_flops,
-        ),
+        "gencat_bwd_x": (bwd_x, "tensor", gen_flops),
         "gencat_bwd_yw": (
             lambda: _lib.call("ddpm_gencat_bwd_yw", x.data_ptr(), y.data_ptr(), packed.data_ptr(),
                               gout.data_ptr(), gy.data_ptr(), gw.data_ptr(), gb.data_ptr(),

@@ -235,9 +235,15 @@ class _GeneratorDynamicCat(torch.autograd.Function):
         with torch.cuda.device(x.device):
             stream = _lib.stream_handle(x.device)
             if need_x:
-                _lib.call("ddpm_gencat_bwd_x", y.data_ptr(), packed.data_ptr(), bias.data_ptr(),
-                          grad_out.data_ptr(), grad_x.data_ptr(), n, c, h, w, ks, d0, d1, d2,
-                          code, stream)
+                # y staged once channel-last in the operand type: the dX kernel then
+                # stages its row segments with bulk copies
+                sb = int(_lib.load().ddpm_gencat_stage_y_bytes(n, c, h, w, ks, d0, d1, d2, code))
+                staged = torch.empty(sb, dtype=torch.uint8, device=x.device)
+                _lib.call("ddpm_gencat_stage_y", y.data_ptr(), staged.data_ptr(), sb,
+                          n, c, h, w, ks, d0, d1, d2, code, stream)
+                _lib.call("ddpm_gencat_bwd_x_staged", staged.data_ptr(), sb, packed.data_ptr(),
+                          bias.data_ptr(), grad_out.data_ptr(), grad_x.data_ptr(),
+                          n, c, h, w, ks, d0, d1, d2, code, stream)
             if need_y or grad_w is not None:
                 ws = None
                 ws_bytes = 0

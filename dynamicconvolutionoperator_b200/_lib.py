@@ -51,6 +51,15 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _c_int,
         [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr] + [_c_int] * 4 + [_c_int] * 5 + [_c_ptr],
     ),
+    "ddpm_gencat_stage_y_bytes": (_c_size, [_c_int] * 9),
+    "ddpm_gencat_stage_y": (
+        _c_int,
+        [_c_ptr, _c_ptr, _c_size] + [_c_int] * 4 + [_c_int] * 5 + [_c_ptr],
+    ),
+    "ddpm_gencat_bwd_x_staged": (
+        _c_int,
+        [_c_ptr, _c_size, _c_ptr, _c_ptr, _c_ptr, _c_ptr] + [_c_int] * 4 + [_c_int] * 5 + [_c_ptr],
+    ),
     "ddpm_gencat_bwd_workspace_bytes": (_c_size, [_c_int] * 5),
     "ddpm_gencat_bwd_yw": (
         _c_int,

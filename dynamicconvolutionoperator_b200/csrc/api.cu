@@ -41,9 +41,14 @@ int gencat_fwd(const void* x, const void* y, const void* wpack, const void* bias
                int n, int c, int h, int w, int ks, int d0, int d1, int d2, int dt,
                cudaStream_t st);
 
-int gencat_bwd_x(const void* y, const void* wpack, const void* bias, const void* gout, void* gx,
-                 int n, int c, int h, int w, int ks, int d0, int d1, int d2, int dt,
-                 cudaStream_t st);
+int gencat_bwd_x(const void* y, const void* staged, size_t staged_bytes, const void* wpack,
+                 const void* bias, const void* gout, void* gx, int n, int c, int h, int w, int ks,
+                 int d0, int d1, int d2, int dt, cudaStream_t st);
+namespace gencat {
+size_t stage_y_bytes(int n, int c, int h, int w, int ks, int d0, int d1, int d2, int dt);
+int stage_y(const void* y, void* staged, size_t staged_bytes, int n, int c, int h, int w, int ks,
+            int d0, int d1, int d2, int dt, cudaStream_t st);
+}  // namespace gencat
 
 size_t gencat_bwd_workspace_bytes(int n, int c, int h, int w, int ks);
 int gencat_bwd_yw(const void* x, const void* y, const void* wpack, const void* gout, void* gy,
@@ -122,8 +127,30 @@ int ddpm_gencat_bwd_x(const void* y, const void* packed, const void* bias, const
                       void* grad_x, int n, int c, int h, int w, int ksize, int d0, int d1, int d2,
                       int dtype, void* stream) {
   ddpm::clear_error();
-  return ddpm::gencat_bwd_x(y, packed, bias, grad_out, grad_x, n, c, h, w, ksize, d0, d1, d2,
-                            dtype, static_cast<cudaStream_t>(stream));
+  return ddpm::gencat_bwd_x(y, nullptr, 0, packed, bias, grad_out, grad_x, n, c, h, w, ksize, d0,
+                            d1, d2, dtype, static_cast<cudaStream_t>(stream));
+}
+
+size_t ddpm_gencat_stage_y_bytes(int n, int c, int h, int w, int ksize, int d0, int d1, int d2,
+                                 int dtype) {
+  return ddpm::gencat::stage_y_bytes(n, c, h, w, ksize, d0, d1, d2, dtype);
+}
+
+int ddpm_gencat_stage_y(const void* y, void* staged, size_t staged_bytes, int n, int c, int h,
+                        int w, int ksize, int d0, int d1, int d2, int dtype, void* stream) {
+  ddpm::clear_error();
+  return ddpm::gencat::stage_y(y, staged, staged_bytes, n, c, h, w, ksize, d0, d1, d2, dtype,
+                               static_cast<cudaStream_t>(stream));
+}
+
+int ddpm_gencat_bwd_x_staged(const void* staged_y, size_t staged_bytes, const void* packed,
+                             const void* bias, const void* grad_out, void* grad_x, int n, int c,
+                             int h, int w, int ksize, int d0, int d1, int d2, int dtype,
+                             void* stream) {
+  ddpm::clear_error();
+  DDPM_CHECK_ARG(staged_y != nullptr, "null staged_y");
+  return ddpm::gencat_bwd_x(nullptr, staged_y, staged_bytes, packed, bias, grad_out, grad_x, n, c,
+                            h, w, ksize, d0, d1, d2, dtype, static_cast<cudaStream_t>(stream));
 }
 
 size_t ddpm_gencat_bwd_workspace_bytes(int n, int c, int h, int w, int ksize) {

@@ -568,5 +568,41 @@ int status_ptr(int** out);
 int read_status(int reset, int* code);
 int num_sms();
 
+// Staged y (gencat_stage.cu): y channel-last, zero padded, in the MMA operand
+// type, so every row segment a kernel stages is one contiguous 1-D bulk copy.
+// Layout [part][n][Hp][G][Wp][8]: 16-byte rows of 8 channels, G = round16(C+1)/8
+// groups; channel C is the constant one of the bias / db column (1 at every
+// position), channels above it are zero. Plane row i holds image row i - ph
+// (ph = (K/2) * max dilation), plane column j holds image column j - 8, and
+// Wp = 128 * ceil(W / 128) + 16, so a 144-pixel segment starting 8 columns left
+// of any 128-pixel row tile, at any row within the dilation halo, is in range.
+// FP32 stores a bf16 hi part and a bf16 residual part.
+struct StageLayout {
+  int N, C, H, W, G, ph, Hp, Wp, parts;
+  size_t part_bytes;
+  __host__ __device__ size_t total_bytes() const { return part_bytes * parts; }
+  // byte offset of the 16-byte row (part, n, plane row i, group g, plane column j)
+  __host__ __device__ size_t row_offset(int part, int n, int i, int g, int j) const {
+    return (size_t)part * part_bytes + ((((size_t)n * Hp + i) * G + g) * Wp + j) * 16;
+  }
+  static StageLayout make(int n, int c, int h, int w, int ks, int d0, int d1, int d2, int dt) {
+    StageLayout L;
+    L.N = n;
+    L.C = c;
+    L.H = h;
+    L.W = w;
+    L.G = (c + 1 + 15) / 16 * 2;
+    L.ph = (ks / 2) * max3(d0, d1, d2);
+    L.Hp = h + 2 * L.ph;
+    L.Wp = (w + kTileM - 1) / kTileM * kTileM + 16;
+    L.parts = dt == DDPM_F32 ? 2 : 1;
+    L.part_bytes = (size_t)n * L.Hp * L.G * L.Wp * 16;
+    return L;
+  }
+};
+size_t stage_y_bytes(int n, int c, int h, int w, int ks, int d0, int d1, int d2, int dt);
+int stage_y(const void* y, void* staged, size_t staged_bytes, int n, int c, int h, int w, int ks,
+            int d0, int d1, int d2, int dt, cudaStream_t st);
+
 }  // namespace gencat
 }  // namespace ddpm

@@ -22,15 +22,22 @@
 // instead of gathering it through L1 (27 x 64 scalar loads per pixel and tile
 // bounded the earlier version by memory latency). Units are double buffered.
 //
-// Warp roles (19 warps): w0 = TMEM allocator + weight producer, w1-w2 = MMA
-// issuers (even / odd chunks: one thread issuing N=Cp MMAs back to back
-// leaves the tensor pipe idle ~half the time), w3-w10 = unit producers
-// (operand transpose + gradient bulk copies; each thread issues its global
-// loads before waiting for a free buffer), w11-w18 = two epilogue warpgroups
-// owning the 16-channel blocks {0, 2} and {1, 3} of every chunk.
+// Warp roles: w0 = TMEM allocator + weight producer, w1-w2 = MMA issuers
+// (even / odd chunks: one thread issuing N=Cp MMAs back to back leaves the
+// tensor pipe idle ~half the time), then the unit producers, then two epilogue
+// warpgroups owning the 16-channel blocks {0, 2} and {1, 3} of every chunk.
+// Producers: from y itself, 8 warps load 8-pixel vectors and transpose them
+// into the operand (each thread issues its global loads before waiting for a
+// free buffer) and the gradient rows arrive by one bulk copy per channel; from
+// staged y (gencat_stage.cu, a channel-last operand copy of y), one thread
+// issues one 1-D bulk copy per (part, channel group) and, when the row pitch
+// allows a tensor map, the whole [Cp][144] gradient segment as one TMA copy
+// (zero filled outside the image) — per-channel copies issued by a warp
+// against one mbarrier cost ~3 us per unit.
 #include "common.cuh"
 #include "tc.cuh"
 #include "gencat.cuh"
+#include "tmap.cuh"
 
 namespace ddpm {
 namespace {
@@ -39,7 +46,7 @@ using namespace gencat;
 
 constexpr int kSeg = 144;  // staged pixels per row segment (128 + 8 on each side)
 
-template <typename T, int KS>
+template <typename T, int KS, bool kStaged = false>
 struct BxCfg {
   static constexpr bool kSplit = IoTraits<T>::kSplit;
   static constexpr int kParts = kSplit ? 2 : 1;
@@ -48,7 +55,7 @@ struct BxCfg {
   static constexpr bool kBiasInGemm = !kSplit;
   static constexpr int kIssuers = 2;        // MMA issuer warps (alternate chunks)
   static constexpr int kFirstProducerWarp = 1 + kIssuers;
-  static constexpr int kProducers = 256;
+  static constexpr int kProducers = kStaged ? 32 : 256;
   static constexpr int kFirstEpiWarp = kFirstProducerWarp + kProducers / 32;
   static constexpr int kThreads = 32 * (kFirstEpiWarp + 8);
 };
@@ -87,13 +94,53 @@ struct BxParams {
   int N, C, H, W, Cp, Ck;
   int d[3];
   int tiles_w, num_tiles;
+  const uint8_t* staged;  // staged y, or null (stage from y)
+  StageLayout sl;
+  CUtensorMap gmap;       // grad_out {W, H, 4C, N}, box {kSeg, 1, Cp, 1} (staged path)
+  int g_tma;              // gmap is valid
   int* status;
 };
 
-template <typename T, int KS>
-__global__ void __launch_bounds__(BxCfg<T, KS>::kThreads, 1)
-gencat_bwd_x_kernel(const BxParams p) {
-  using Cfg = BxCfg<T, KS>;
+// Gradient row segment g_b[:, hr, w0-8 .. w0+135] of one unit into `gs`
+// ([Cp][kSeg], I/O dtype): one channel per thread (threads tid, tid + nthr,
+// ...), 1-D bulk copies counted on `bar` when every row start is 16-byte
+// aligned, zero outside the image.
+template <typename T>
+__device__ __forceinline__ void stage_grad_rows(T* gs, const T* gout, uint64_t* bar, int tid,
+                                                int nthr, int n, int b, int hr, int w0, int C,
+                                                int Cp, int H, int W, size_t P, uint32_t g_bytes,
+                                                bool g_bulk) {
+  const int lo = w0 - 8 < 0 ? 0 : w0 - 8;
+  const int hi = w0 + kSeg - 8 > W ? W : w0 + kSeg - 8;
+  const bool row_ok = hr >= 0 && hr < H;
+  if (!row_ok) {
+    // the whole segment is outside the image: vector zero stores over all threads
+    uint4* z = reinterpret_cast<uint4*>(gs);
+    for (int i = tid; i < (int)(g_bytes / 16); i += nthr) z[i] = make_uint4(0u, 0u, 0u, 0u);
+    return;
+  }
+  for (int c = tid; c < Cp; c += nthr) {
+    T* dst = gs + (size_t)c * kSeg;
+    const T* src = gout + ((size_t)n * 4 * C + (size_t)(b + 1) * C + c) * P + (size_t)hr * W;
+    if (c < C && g_bulk) {
+      for (int x = 0; x < lo - (w0 - 8); ++x) dst[x] = T(0.f);
+      for (int x = hi - (w0 - 8); x < kSeg; ++x) dst[x] = T(0.f);
+      const uint32_t bytes = (uint32_t)(hi - lo) * sizeof(T);
+      tc::mbar_expect_tx(bar, bytes);  // before the copy can complete
+      tc::bulk_g2s(dst + (lo - (w0 - 8)), src + lo, bytes, bar);
+    } else {
+      for (int x = 0; x < kSeg; ++x) {
+        const int col = w0 - 8 + x;
+        dst[x] = (c < C && col >= 0 && col < W) ? src[col] : T(0.f);
+      }
+    }
+  }
+}
+
+template <typename T, int KS, bool kStaged>
+__global__ void __launch_bounds__(BxCfg<T, KS, kStaged>::kThreads, 1)
+gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
+  using Cfg = BxCfg<T, KS, kStaged>;
   using Op = typename IoTraits<T>::Op;
   constexpr int S = Cfg::kWStages;
   constexpr int NU = Cfg::kUnitBufs;
@@ -235,7 +282,7 @@ gencat_bwd_x_kernel(const BxParams p) {
         fail(abort_flag, p.status, 27);
     }
   } else if (warp < Cfg::kFirstEpiWarp) {
-    // ---- unit producers (256 threads) ---------------------------------------
+    // ---- unit producers ---------------------------------------------------------
     const int pt = threadIdx.x - 32 * Cfg::kFirstProducerWarp;
     const T* y = static_cast<const T*>(p.y);
     const T* gout = static_cast<const T*>(p.gout);
@@ -257,66 +304,71 @@ gencat_bwd_x_kernel(const BxParams p) {
         const int hr = h - (ki - r) * d;  // image row of this unit
         const int ub = uq % NU;
         uint8_t* reg = smem + L.reg + ub * L.reg_bytes;
-        bool waited = false;
-        for (int base = 0; base < items; base += Cfg::kProducers) {
-          // (1) this thread's y item: 8 channels x 8 pixels, loaded before any wait
-          const int item = base + pt;
-          const int jb = item % (kSeg / 8);
-          const int kg = item / (kSeg / 8);
-          Raw8<T> v[8];
+        T* gs = reinterpret_cast<T*>(smem + L.gs + ub * L.g_bytes);
+        if constexpr (kStaged) {
+          // staged y: one bulk copy per (part, channel group); plane row hr + ph,
+          // plane columns w0 .. w0+143 = image columns w0-8 .. w0+135
+          if (!warp_wait(&r_empty[ub], ((uq / NU) & 1) ^ 1, abort_flag) ||
+              !warp_wait(&g_empty[ub], ((uq / NU) & 1) ^ 1, abort_flag)) {
+            fail(abort_flag, p.status, 23);
+            failed = true;
+            break;
+          }
+          const int ng = Ck / 8;
+          if (pt == 0) {
+            // one arrival carries the unit's whole byte count, then the copies
+            const uint32_t ybytes = (uint32_t)(ng * Cfg::kParts) * kSeg * 16;
+            tc::mbar_arrive_expect_tx(&u_full[ub], ybytes + (p.g_tma ? L.g_bytes : 0u));
+            for (int k = 0; k < ng * Cfg::kParts; ++k) {
+              const int part = k / ng, kg = k - part * ng;
+              const uint8_t* src = p.staged + p.sl.row_offset(part, n, hr + p.sl.ph, kg, w0);
+              tc::bulk_g2s(reg + part * L.reg_part + kg * kSeg * 16, src, kSeg * 16, &u_full[ub]);
+            }
+            if (p.g_tma) tc::tma_load_4d(gs, &p.gmap, w0 - 8, hr, (b + 1) * C, n, &u_full[ub]);
+          }
+          if (!p.g_tma)
+            stage_grad_rows<T>(gs, gout, &u_full[ub], pt, Cfg::kProducers, n, b, hr, w0, C, Cp,
+                               H, W, P, L.g_bytes, g_bulk);
+          __syncwarp();
+          if (pt != 0) tc::mbar_arrive(&u_full[ub]);
+        } else {
+          bool waited = false;
+          for (int base = 0; base < items; base += Cfg::kProducers) {
+            // (1) this thread's y item: 8 channels x 8 pixels, loaded before any wait
+            const int item = base + pt;
+            const int jb = item % (kSeg / 8);
+            const int kg = item / (kSeg / 8);
+            Raw8<T> v[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const int c = kg * 8 + e;
-            if (item < items && c < C)
-              v[e] = load_raw8<T>(y + ((size_t)n * C + c) * P, H, W, hr, w0 - 8 + jb * 8);
-            else if (c == ones_c)
-              v[e].ones();
-            else
-              v[e].zero();
-          }
-          if (!waited) {
-            if (!warp_wait(&r_empty[ub], ((uq / NU) & 1) ^ 1, abort_flag) ||
-                !warp_wait(&g_empty[ub], ((uq / NU) & 1) ^ 1, abort_flag)) {
-              fail(abort_flag, p.status, 23);
-              failed = true;
-              break;
+            for (int e = 0; e < 8; ++e) {
+              const int c = kg * 8 + e;
+              if (item < items && c < C)
+                v[e] = load_raw8<T>(y + ((size_t)n * C + c) * P, H, W, hr, w0 - 8 + jb * 8);
+              else if (c == ones_c)
+                v[e].ones();
+              else
+                v[e].zero();
             }
-            waited = true;
-            // (2) gradient row segment, one channel per thread: columns w0-8 .. w0+135
-            T* gs = reinterpret_cast<T*>(smem + L.gs + ub * L.g_bytes);
-            const int lo = w0 - 8 < 0 ? 0 : w0 - 8;
-            const int hi = w0 + kSeg - 8 > W ? W : w0 + kSeg - 8;
-            const bool row_ok = hr >= 0 && hr < H;
-            if (!row_ok) {
-              // the whole segment is outside the image: vector zero stores over all threads
-              uint4* z = reinterpret_cast<uint4*>(gs);
-              for (int i = pt; i < (int)(L.g_bytes / 16); i += Cfg::kProducers)
-                z[i] = make_uint4(0u, 0u, 0u, 0u);
-            }
-            for (int c = pt; c < Cp && row_ok; c += Cfg::kProducers) {
-              T* dst = gs + (size_t)c * kSeg;
-              const T* src =
-                  gout + ((size_t)n * 4 * C + (size_t)(b + 1) * C + c) * P + (size_t)hr * W;
-              if (c < C && g_bulk) {
-                for (int x = 0; x < lo - (w0 - 8); ++x) dst[x] = T(0.f);
-                for (int x = hi - (w0 - 8); x < kSeg; ++x) dst[x] = T(0.f);
-                const uint32_t bytes = (uint32_t)(hi - lo) * sizeof(T);
-                tc::mbar_expect_tx(&u_full[ub], bytes);  // before the copy can complete
-                tc::bulk_g2s(dst + (lo - (w0 - 8)), src + lo, bytes, &u_full[ub]);
-              } else {
-                for (int x = 0; x < kSeg; ++x) {
-                  const int col = w0 - 8 + x;
-                  dst[x] = (c < C && col >= 0 && col < W) ? src[col] : T(0.f);
-                }
+            if (!waited) {
+              if (!warp_wait(&r_empty[ub], ((uq / NU) & 1) ^ 1, abort_flag) ||
+                  !warp_wait(&g_empty[ub], ((uq / NU) & 1) ^ 1, abort_flag)) {
+                fail(abort_flag, p.status, 23);
+                failed = true;
+                break;
               }
+              waited = true;
+              // (2) gradient row segment, one channel per thread: columns w0-8 .. w0+135
+              stage_grad_rows<T>(gs, gout, &u_full[ub], pt, Cfg::kProducers, n, b, hr, w0, C,
+                                 Cp, H, W, P, L.g_bytes, g_bulk);
             }
+            if (item < items)
+              store_transposed<T, Op, Cfg::kSplit>(reg + (kg * kSeg + jb * 8) * 16, L.reg_part, v);
           }
-          if (item < items)
-            store_transposed<T, Op, Cfg::kSplit>(reg + (kg * kSeg + jb * 8) * 16, L.reg_part, v);
+          if (failed) break;
+          tc::fence_proxy_async_smem();
         }
         if (failed) break;
-        tc::fence_proxy_async_smem();
-        tc::mbar_arrive(&u_full[ub]);
+        if constexpr (!kStaged) tc::mbar_arrive(&u_full[ub]);
       }
       if (failed) break;
     }
@@ -417,16 +469,22 @@ done:
   }
 }
 
-template <typename T, int KS>
-int launch(const BxParams& prm, cudaStream_t st) {
-  using Cfg = BxCfg<T, KS>;
+template <typename T, int KS, bool kStaged>
+int launch_k(const BxParams& prm, cudaStream_t st) {
+  using Cfg = BxCfg<T, KS, kStaged>;
   const BxSmem L = bx_smem_layout<T, KS>(prm.Cp, prm.Ck, prm.C);
-  auto fn = gencat_bwd_x_kernel<T, KS>;
+  auto fn = gencat_bwd_x_kernel<T, KS, kStaged>;
   DDPM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total));
   const int grid = prm.num_tiles < num_sms() ? prm.num_tiles : num_sms();
   fn<<<grid, Cfg::kThreads, L.total, st>>>(prm);
   DDPM_CHECK_LAUNCH("gencat_bwd_x_kernel");
   return DDPM_OK;
+}
+
+template <typename T, int KS>
+int launch(const BxParams& prm, cudaStream_t st) {
+  if (prm.staged != nullptr) return launch_k<T, KS, true>(prm, st);
+  return launch_k<T, KS, false>(prm, st);
 }
 
 template <typename T>
@@ -440,12 +498,14 @@ int dispatch(int ks, const BxParams& prm, cudaStream_t st) {
 
 }  // namespace
 
-int gencat_bwd_x(const void* y, const void* wpack, const void* bias, const void* gout, void* gx,
-                 int n, int c, int h, int w, int ks, int d0, int d1, int d2, int dt,
-                 cudaStream_t st) {
+// `staged`: staged y (gencat::stage_y, at least stage_y_bytes() bytes) or
+// null to stage the operand from y itself.
+int gencat_bwd_x(const void* y, const void* staged, size_t staged_bytes, const void* wpack,
+                 const void* bias, const void* gout, void* gx, int n, int c, int h, int w, int ks,
+                 int d0, int d1, int d2, int dt, cudaStream_t st) {
   int rc = gencat::check_shape(n, c, h, w, ks, d0, d1, d2, dt);
   if (rc) return rc;
-  DDPM_CHECK_ARG(y && wpack && bias && gout && gx, "null pointer");
+  DDPM_CHECK_ARG((y || staged) && wpack && bias && gout && gx, "null pointer");
   const gencat::PackLayout pl = gencat::PackLayout::make(c, ks, dt);
   BxParams prm{};
   prm.y = y;
@@ -464,6 +524,31 @@ int gencat_bwd_x(const void* y, const void* wpack, const void* bias, const void*
   prm.d[2] = d2;
   prm.tiles_w = (w + gencat::kTileM - 1) / gencat::kTileM;
   prm.num_tiles = n * h * prm.tiles_w;
+  prm.staged = static_cast<const uint8_t*>(staged);
+  prm.sl = gencat::StageLayout::make(n, c, h, w, ks, d0, d1, d2, dt);
+  if (staged != nullptr) {
+    if (staged_bytes < prm.sl.total_bytes())
+      return set_error(DDPM_ERR_WORKSPACE, "staged y too small (%zu < %zu)", staged_bytes,
+                       prm.sl.total_bytes());
+    DDPM_CHECK_ARG((reinterpret_cast<uintptr_t>(staged) & 15u) == 0,
+                   "staged y must be 16-byte aligned");
+    // gradient segments by TMA when the row pitch and base allow a tensor map
+    const int es = dtype_size(dt);
+    if (((size_t)w * es) % 16 == 0 && (reinterpret_cast<uintptr_t>(gout) & 15u) == 0) {
+      const CUtensorMapDataType ty = dt == DDPM_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                     : dt == DDPM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                       : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+      const uint64_t dims[4] = {(uint64_t)w, (uint64_t)h, (uint64_t)4 * c, (uint64_t)n};
+      const uint64_t strides[3] = {(uint64_t)w * es, (uint64_t)h * w * es,
+                                   (uint64_t)4 * c * h * w * es};
+      const uint32_t box[4] = {(uint32_t)kSeg, 1, (uint32_t)pl.Cp, 1};
+      if (encode_tmap(&prm.gmap, ty, 4, gout, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE) ==
+          DDPM_OK)
+        prm.g_tma = 1;
+      else
+        clear_error();
+    }
+  }
   rc = gencat::status_ptr(&prm.status);
   if (rc) return rc;
   switch (dt) {

@@ -1,0 +1,103 @@
+// Staged y for the fused generator backward (layout: StageLayout in
+// gencat.cuh). One pass over y writes it channel-last in the MMA operand type,
+// zero padded and with the constant-one bias channel, so the backward kernels
+// stage their y row segments with 1-D bulk copies instead of per-thread loads
+// and register transposes (which bounded them by load latency).
+#include "common.cuh"
+#include "gencat.cuh"
+
+namespace ddpm {
+namespace {
+
+using namespace gencat;
+
+constexpr int kStageCols = 64;               // plane columns per block
+constexpr int kStageChannels = kMaxChannels + 16;  // G*8 <= round16(64 + 1)
+
+// Block = (n, plane row, 64-column strip). Loads: 8 lanes read 8-pixel
+// vectors covering 64 contiguous columns of one channel; a padded shared tile
+// transposes; each thread writes 16-byte rows of 8 channels (consecutive
+// lanes = consecutive columns).
+template <typename T>
+__global__ void __launch_bounds__(256) stage_y_kernel(const T* __restrict__ y,
+                                                      uint4* __restrict__ hi,
+                                                      uint4* __restrict__ lo,
+                                                      const StageLayout L) {
+  using Op = typename IoTraits<T>::Op;
+  constexpr bool kSplit = IoTraits<T>::kSplit;
+  __shared__ float tile[kStageChannels][kStageCols + 1];
+  const int ni = blockIdx.x, n = ni / L.Hp, i = ni - n * L.Hp;
+  const int hr = i - L.ph;                // image row (may be outside the image)
+  const int j0 = blockIdx.y * kStageCols;  // first plane column of the block
+  const int nc = L.G * 8;
+  const size_t P = (size_t)L.H * L.W;
+  for (int item = threadIdx.x; item < nc * (kStageCols / 8); item += blockDim.x) {
+    const int g = item & 7, c = item >> 3;
+    Raw8<T> v;
+    if (c < L.C)
+      v = load_raw8<T>(y + ((size_t)n * L.C + c) * P, L.H, L.W, hr, j0 - 8 + g * 8);
+    else if (c == L.C)
+      v.ones();
+    else
+      v.zero();
+#pragma unroll
+    for (int e = 0; e < 8; ++e) tile[c][g * 8 + e] = v.get(e);
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < L.G * kStageCols; idx += blockDim.x) {
+    const int kg = idx / kStageCols, x = idx - kg * kStageCols;
+    if (j0 + x >= L.Wp) continue;
+    unsigned long long pr[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) pr[e] = f2_pack(tile[kg * 8 + 2 * e][x], tile[kg * 8 + 2 * e + 1][x]);
+    const size_t dst = L.row_offset(0, n, i, kg, j0 + x) / 16;
+    uint4 vh, vl;
+    store8x2_split<Op, kSplit>(reinterpret_cast<uint8_t*>(&vh), reinterpret_cast<uint8_t*>(&vl), pr);
+    hi[dst] = vh;
+    if constexpr (kSplit) lo[dst] = vl;
+  }
+}
+
+template <typename T>
+int launch_stage(const T* y, uint8_t* staged, const StageLayout& L, cudaStream_t st) {
+  uint4* hi = reinterpret_cast<uint4*>(staged);
+  uint4* lo = L.parts > 1 ? reinterpret_cast<uint4*>(staged + L.part_bytes) : nullptr;
+  const dim3 grid((unsigned)(L.N * L.Hp), (unsigned)((L.Wp + kStageCols - 1) / kStageCols));
+  stage_y_kernel<T><<<grid, 256, 0, st>>>(y, hi, lo, L);
+  DDPM_CHECK_LAUNCH("stage_y_kernel");
+  return DDPM_OK;
+}
+
+}  // namespace
+
+namespace gencat {
+
+size_t stage_y_bytes(int n, int c, int h, int w, int ks, int d0, int d1, int d2, int dt) {
+  if (check_shape(n, c, h, w, ks, d0, d1, d2, dt) != DDPM_OK) {
+    clear_error();
+    return 0;
+  }
+  return StageLayout::make(n, c, h, w, ks, d0, d1, d2, dt).total_bytes();
+}
+
+int stage_y(const void* y, void* staged, size_t staged_bytes, int n, int c, int h, int w, int ks,
+            int d0, int d1, int d2, int dt, cudaStream_t st) {
+  int rc = check_shape(n, c, h, w, ks, d0, d1, d2, dt);
+  if (rc) return rc;
+  DDPM_CHECK_ARG(y && staged, "null pointer");
+  const StageLayout L = StageLayout::make(n, c, h, w, ks, d0, d1, d2, dt);
+  if (staged_bytes < L.total_bytes())
+    return set_error(DDPM_ERR_WORKSPACE, "staged buffer too small (%zu < %zu)", staged_bytes,
+                     L.total_bytes());
+  DDPM_CHECK_ARG((reinterpret_cast<uintptr_t>(staged) & 15u) == 0,
+                 "staged buffer must be 16-byte aligned");
+  uint8_t* s = static_cast<uint8_t*>(staged);
+  switch (dt) {
+    case DDPM_BF16: return launch_stage(static_cast<const __nv_bfloat16*>(y), s, L, st);
+    case DDPM_F16: return launch_stage(static_cast<const __half*>(y), s, L, st);
+    default: return launch_stage(static_cast<const float*>(y), s, L, st);
+  }
+}
+
+}  // namespace gencat
+}  // namespace ddpm

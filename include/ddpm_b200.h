@@ -145,6 +145,35 @@ DDPM_API int ddpm_gencat_bwd_x(const void* y, const void* packed, const void* bi
                                void* stream);
 
 /*
+ * Staged y for the fused backward: y written once channel-last, zero padded
+ * by the dilation halo, in the tensor-core operand type (fp32: bf16 hi and
+ * residual parts) with the constant-one bias channel, so the backward kernels
+ * stage every y row segment with one bulk copy. Same role as the per-tile y
+ * loads inside `_generator_dynamic_cat_bwd_x` (reference
+ * `_triton_kernels.py:430-531`), done once per backward instead.
+ * ddpm_gencat_stage_y_bytes() gives the size (0 for unsupported shapes);
+ * `staged` must be 16-byte aligned. The contents depend on y only.
+ */
+DDPM_API size_t ddpm_gencat_stage_y_bytes(int n, int c, int h, int w, int ksize,
+                                          int d0, int d1, int d2, int dtype);
+DDPM_API int ddpm_gencat_stage_y(const void* y, void* staged, size_t staged_bytes,
+                                 int n, int c, int h, int w,
+                                 int ksize, int d0, int d1, int d2, int dtype,
+                                 void* stream);
+
+/*
+ * ddpm_gencat_bwd_x reading y from its staged copy (ddpm_gencat_stage_y with
+ * the same sizes and dtype). Same result as ddpm_gencat_bwd_x; replaces the
+ * same reference kernel (`_triton_kernels.py:430-531`).
+ */
+DDPM_API int ddpm_gencat_bwd_x_staged(const void* staged_y, size_t staged_bytes,
+                                      const void* packed, const void* bias,
+                                      const void* grad_out, void* grad_x,
+                                      int n, int c, int h, int w,
+                                      int ksize, int d0, int d1, int d2, int dtype,
+                                      void* stream);
+
+/*
  * Fused generator backward: dY and dW/db with dK = shifted(x) * grad formed on
  * chip. Replaces `_generator_dynamic_cat_bwd_y` (`_triton_kernels.py:534-623`),
  * `_generator_dynamic_cat_bwd_weight_partial` (`:626-751`) and

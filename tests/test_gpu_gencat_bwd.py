@@ -29,10 +29,25 @@ def _gold_grads(x, y, wt, b, g, ks, dil):
     return torch.autograd.grad(out, (x64, y64, w64, b64), g.double())
 
 
+def _stage_y(yd, ks, dil):
+    """Staged copy of y through the C ABI (ddpm_gencat_stage_y)."""
+    from dynamicconvolutionoperator_b200 import _lib
+
+    n, c, h, w = yd.shape
+    code = _lib.dtype_code(yd.dtype)
+    nb = int(_lib.load().ddpm_gencat_stage_y_bytes(n, c, h, w, ks, *dil, code))
+    assert nb > 0
+    staged = torch.full((nb,), 0xAB, dtype=torch.uint8, device=yd.device)  # no reliance on zeros
+    _lib.call("ddpm_gencat_stage_y", yd.data_ptr(), staged.data_ptr(), nb, n, c, h, w, ks, *dil,
+              code, _lib.stream_handle(yd.device))
+    return staged, nb
+
+
 @pytest.mark.parametrize("shape", SHAPES)
 @pytest.mark.parametrize("ks", [1, 3])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_gencat_bwd_x(shape, ks, dtype):
+@pytest.mark.parametrize("staged", [False, True])
+def test_gencat_bwd_x(shape, ks, dtype, staged):
     from dynamicconvolutionoperator_b200 import _kernels, _lib
 
     x, y, wt, b = _case(shape, ks, dtype)
@@ -41,13 +56,48 @@ def test_gencat_bwd_x(shape, ks, dtype):
     gx_gold, *_ = _gold_grads(x, y, wt, b, g, ks, (1, 3, 5))
     yd, wd, bd, gd = y.cuda(), wt.cuda(), b.cuda(), g.cuda()
     packed = _kernels.pack_generator_weight(wd, bd, c, ks, use_cache=False)
-    gx = torch.empty((n, c, h, w), dtype=dtype, device="cuda")
-    _lib.call("ddpm_gencat_bwd_x", yd.data_ptr(), packed.data_ptr(), bd.data_ptr(), gd.data_ptr(),
-              gx.data_ptr(), n, c, h, w, ks, 1, 3, 5, _lib.dtype_code(dtype),
-              _lib.stream_handle(gx.device))
+    gx = torch.full((n, c, h, w), float("nan"), dtype=dtype, device="cuda")
+    stream = _lib.stream_handle(gx.device)
+    if staged:
+        sy, nb = _stage_y(yd, ks, (1, 3, 5))
+        _lib.call("ddpm_gencat_bwd_x_staged", sy.data_ptr(), nb, packed.data_ptr(), bd.data_ptr(),
+                  gd.data_ptr(), gx.data_ptr(), n, c, h, w, ks, 1, 3, 5, _lib.dtype_code(dtype),
+                  stream)
+    else:
+        _lib.call("ddpm_gencat_bwd_x", yd.data_ptr(), packed.data_ptr(), bd.data_ptr(),
+                  gd.data_ptr(), gx.data_ptr(), n, c, h, w, ks, 1, 3, 5, _lib.dtype_code(dtype),
+                  stream)
     torch.cuda.synchronize()
     rtol, atol = TOL[dtype]
     torch.testing.assert_close(gx.double().cpu(), gx_gold, rtol=rtol, atol=atol)
+
+
+@pytest.mark.parametrize("shape,ks,dil", [((2, 24, 15, 17), 3, (1, 3, 5)), ((1, 64, 9, 130), 3, (2, 1, 4)),
+                                          ((1, 5, 4, 3), 1, (1, 1, 1))])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_stage_y_layout(shape, ks, dil, dtype):
+    """Staged y = y channel-last, zero padded by the halo, ones channel at C,
+    [part][n][Hp][G][Wp][8]; fp32 as bf16 hi + residual (hi + lo == y to
+    within bf16 of the residual)."""
+    n, c, h, w = shape
+    y = torch.randn(shape, generator=torch.Generator().manual_seed(3)).to(dtype)
+    staged, nb = _stage_y(y.cuda(), ks, dil)
+    torch.cuda.synchronize()
+    G = (c + 1 + 15) // 16 * 2
+    ph = (ks // 2) * max(dil)
+    Hp, Wp = h + 2 * ph, (w + 127) // 128 * 128 + 16
+    parts = 2 if dtype == torch.float32 else 1
+    assert nb == parts * n * Hp * G * Wp * 16
+    want = torch.zeros((n, G * 8, Hp, Wp), dtype=torch.float64)
+    want[:, :c, ph:ph + h, 8:8 + w] = y.double()
+    want[:, c] = 1.0
+    # [n][Hp][G][Wp][8] -> [n][G*8][Hp][Wp]
+    planes = staged.cpu().view(torch.bfloat16 if dtype != torch.float16 else torch.float16)
+    planes = planes.view(parts, n, Hp, G, Wp, 8).permute(0, 1, 3, 5, 2, 4).reshape(parts, n, G * 8, Hp, Wp)
+    got = planes[0].double() + (planes[1].double() if parts == 2 else 0.0)
+    # fp32: |y - hi| <= 2^-8 |y| and the residual is rounded to bf16 again
+    tol = 2.0 ** -15 * want.abs().max().item() if dtype == torch.float32 else 0.0
+    assert (got - want).abs().max().item() <= tol
 
 
 @pytest.mark.parametrize("shape", SHAPES)
