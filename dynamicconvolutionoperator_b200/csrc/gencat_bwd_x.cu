@@ -416,25 +416,55 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
             break;
           }
           tc::tc_fence_after();
+          if constexpr (!kStaged) {
+            // 96-register budget: one channel block at a time
+#pragma unroll
+            for (int bi = 0; bi < 2; ++bi) {
+              const int blk = wg + 2 * bi;
+              if (blk >= nblk) break;
+              float dv1[16];
+              tc::tmem_ld16(tmem_base + ((uint32_t)(quad * 32) << 16) + j * Cp + blk * 16, dv1);
+              float gv1[16];
+              const T* gcol = gs + (size_t)(blk * 16) * kSeg + (m + 8 - dx);
+#pragma unroll
+              for (int cl = 0; cl < 16; ++cl) gv1[cl] = ok ? to_f32<T>(gcol[cl * kSeg]) : 0.f;
+              tc::tmem_ld_wait();
+              if constexpr (!Cfg::kBiasInGemm) {
+                const float* bs = bias_s + (b * KK + tap) * Cp + blk * 16;
+#pragma unroll
+                for (int cl = 0; cl < 16; ++cl) dv1[cl] += bs[cl];
+              }
+              round_taps<T>(dv1);
+#pragma unroll
+              for (int cl = 0; cl < 16; ++cl) acc[bi][cl] = fmaf(dv1[cl], gv1[cl], acc[bi][cl]);
+            }
+          } else {
+          // both channel blocks' TMEM loads and gradient reads in flight before one wait
+          float dv[2][16], gv[2][16];
+#pragma unroll
+          for (int bi = 0; bi < 2; ++bi) {
+            const int blk = wg + 2 * bi;
+            if (blk < nblk) {
+              tc::tmem_ld16(tmem_base + ((uint32_t)(quad * 32) << 16) + j * Cp + blk * 16, dv[bi]);
+              const T* gcol = gs + (size_t)(blk * 16) * kSeg + (m + 8 - dx);
+#pragma unroll
+              for (int cl = 0; cl < 16; ++cl) gv[bi][cl] = ok ? to_f32<T>(gcol[cl * kSeg]) : 0.f;
+            }
+          }
+          tc::tmem_ld_wait();
 #pragma unroll
           for (int bi = 0; bi < 2; ++bi) {
             const int blk = wg + 2 * bi;
             if (blk >= nblk) break;
-            float dv[16];
-            tc::tmem_ld16(tmem_base + ((uint32_t)(quad * 32) << 16) + j * Cp + blk * 16, dv);
-            float gv[16];
-            const T* gcol = gs + (size_t)(blk * 16) * kSeg + (m + 8 - dx);
-#pragma unroll
-            for (int cl = 0; cl < 16; ++cl) gv[cl] = ok ? to_f32<T>(gcol[cl * kSeg]) : 0.f;
-            tc::tmem_ld_wait();
             if constexpr (!Cfg::kBiasInGemm) {
               const float* bs = bias_s + (b * KK + tap) * Cp + blk * 16;
 #pragma unroll
-              for (int cl = 0; cl < 16; ++cl) dv[cl] += bs[cl];
+              for (int cl = 0; cl < 16; ++cl) dv[bi][cl] += bs[cl];
             }
-            round_taps<T>(dv);
+            round_taps<T>(dv[bi]);
 #pragma unroll
-            for (int cl = 0; cl < 16; ++cl) acc[bi][cl] = fmaf(dv[cl], gv[cl], acc[bi][cl]);
+            for (int cl = 0; cl < 16; ++cl) acc[bi][cl] = fmaf(dv[bi][cl], gv[bi][cl], acc[bi][cl]);
+          }
           }
           tc::tc_fence_before();
           tc::mbar_arrive(&t_empty[j]);
@@ -443,7 +473,20 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
       }
       if (failed) break;
       if (px_ok) {
+        // all loads of the x-branch gradient before the first store (gx may
+        // alias nothing, but the compiler cannot know; interleaved, every load
+        // waited for the previous store: 32 serial load latencies per tile)
         const size_t q = (size_t)h * W + w;
+        float g0[2][16];
+#pragma unroll
+        for (int bi = 0; bi < 2; ++bi) {
+          const int blk = wg + 2 * bi;
+#pragma unroll
+          for (int cl = 0; cl < 16; ++cl) {
+            const int c = blk * 16 + cl;
+            g0[bi][cl] = (blk < nblk && c < C) ? to_f32<T>(__ldg(gn + (size_t)c * P + q)) : 0.f;
+          }
+        }
 #pragma unroll
         for (int bi = 0; bi < 2; ++bi) {
           const int blk = wg + 2 * bi;
@@ -451,10 +494,7 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
 #pragma unroll
           for (int cl = 0; cl < 16; ++cl) {
             const int c = blk * 16 + cl;
-            if (c < C) {
-              const float g0 = to_f32<T>(gn[(size_t)c * P + q]);
-              gx[((size_t)n * C + c) * P + q] = from_f32<T>(acc[bi][cl] + g0);
-            }
+            if (c < C) gx[((size_t)n * C + c) * P + q] = from_f32<T>(acc[bi][cl] + g0[bi][cl]);
           }
         }
       }
