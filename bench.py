@@ -355,15 +355,25 @@ def library_kernels(model, x, y, dtype, device):
     fgb = torch.empty_like(fuse_b)
     fws_bytes = int(_lib.load().ddpm_fuseconv_bwd_weight_workspace_bytes(n, 4 * C, C, H, W))
     fws = torch.empty(fws_bytes, dtype=torch.uint8, device=device)
-    sy_bytes = int(_lib.load().ddpm_gencat_stage_y_bytes(n, C, H, W, K, *DILATIONS, code))
+    sy_bytes = int(_lib.load().ddpm_gencat_stage_bytes(n, C, H, W, K, *DILATIONS, code))
     sy = torch.empty(sy_bytes, dtype=torch.uint8, device=device)
 
-    def bwd_x():  # as in the training step: stage y, then dX from the staged copy
-        _lib.call("ddpm_gencat_stage_y", y.data_ptr(), sy.data_ptr(), sy_bytes, n, C, H, W, K,
-                  *DILATIONS, code, sh)
+    # as in the training step: one staging call (x and y), then dX and dY + dW read
+    # the staged operands; the staging is timed with dX
+    _lib.call("ddpm_gencat_stage", x.data_ptr(), y.data_ptr(), sy.data_ptr(), sy_bytes, n, C, H,
+              W, K, *DILATIONS, code, sh)
+
+    def bwd_x():
+        _lib.call("ddpm_gencat_stage", x.data_ptr(), y.data_ptr(), sy.data_ptr(), sy_bytes, n, C,
+                  H, W, K, *DILATIONS, code, sh)
         _lib.call("ddpm_gencat_bwd_x_staged", sy.data_ptr(), sy_bytes, packed.data_ptr(),
                   gen_b.data_ptr(), gout.data_ptr(), gx.data_ptr(), n, C, H, W, K, *DILATIONS,
                   code, sh)
+
+    def bwd_yw():
+        _lib.call("ddpm_gencat_bwd_yw_staged", sy.data_ptr(), sy_bytes, packed.data_ptr(),
+                  gout.data_ptr(), gy.data_ptr(), gw.data_ptr(), gb.data_ptr(), ws.data_ptr(),
+                  ws_bytes, n, C, H, W, K, *DILATIONS, code, sh)
 
     keep = (taps, out, gout, gx, gk, packed, out2, gy, gw, gb, ws, fpacked, fout, fgout, fgx,
             fgw, fgb, fws, sy)
@@ -385,12 +395,7 @@ def library_kernels(model, x, y, dtype, device):
             "tensor", fuse_flops,
         ),
         "gencat_bwd_x": (bwd_x, "tensor", gen_flops),
-        "gencat_bwd_yw": (
-            lambda: _lib.call("ddpm_gencat_bwd_yw", x.data_ptr(), y.data_ptr(), packed.data_ptr(),
-                              gout.data_ptr(), gy.data_ptr(), gw.data_ptr(), gb.data_ptr(),
-                              ws.data_ptr(), ws_bytes, n, C, H, W, K, *DILATIONS, code, sh),
-            "tensor", 2 * gen_flops,
-        ),
+        "gencat_bwd_yw": (bwd_yw, "tensor", 2 * gen_flops),
         "gencat_fwd": (
             lambda: _lib.call("ddpm_gencat_fwd", x.data_ptr(), y.data_ptr(), packed.data_ptr(),
                               gen_b.data_ptr(), out2.data_ptr(), n, C, H, W, K, *DILATIONS,

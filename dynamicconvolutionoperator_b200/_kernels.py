@@ -234,17 +234,28 @@ class _GeneratorDynamicCat(torch.autograd.Function):
             grad_b = torch.empty(3 * c * ks * ks, dtype=x.dtype, device=x.device)
         with torch.cuda.device(x.device):
             stream = _lib.stream_handle(x.device)
-            if need_x:
-                # y staged once channel-last in the operand type: the dX kernel then
-                # stages its row segments with bulk copies
-                sb = int(_lib.load().ddpm_gencat_stage_y_bytes(n, c, h, w, ks, d0, d1, d2, code))
+            # x and y staged once (channel-last operand copies): the backward
+            # kernels then stage their tiles with bulk / TMA copies
+            full = need_y and grad_w is not None
+            staged = None
+            sb = 0
+            if need_x or full:
+                sb = int(_lib.load().ddpm_gencat_stage_bytes(n, c, h, w, ks, d0, d1, d2, code))
                 staged = torch.empty(sb, dtype=torch.uint8, device=x.device)
-                _lib.call("ddpm_gencat_stage_y", y.data_ptr(), staged.data_ptr(), sb,
-                          n, c, h, w, ks, d0, d1, d2, code, stream)
+                _lib.call("ddpm_gencat_stage", x.data_ptr() if full else None, y.data_ptr(),
+                          staged.data_ptr(), sb, n, c, h, w, ks, d0, d1, d2, code, stream)
+            if need_x:
                 _lib.call("ddpm_gencat_bwd_x_staged", staged.data_ptr(), sb, packed.data_ptr(),
                           bias.data_ptr(), grad_out.data_ptr(), grad_x.data_ptr(),
                           n, c, h, w, ks, d0, d1, d2, code, stream)
-            if need_y or grad_w is not None:
+            if full:
+                ws_bytes = int(_lib.load().ddpm_gencat_bwd_workspace_bytes(n, c, h, w, ks))
+                ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
+                _lib.call("ddpm_gencat_bwd_yw_staged", staged.data_ptr(), sb, packed.data_ptr(),
+                          grad_out.data_ptr(), grad_y.data_ptr(), grad_w.data_ptr(),
+                          grad_b.data_ptr(), ws.data_ptr(), ws_bytes,
+                          n, c, h, w, ks, d0, d1, d2, code, stream)
+            elif need_y or grad_w is not None:
                 ws = None
                 ws_bytes = 0
                 if grad_w is not None:

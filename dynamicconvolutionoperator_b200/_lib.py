@@ -51,10 +51,10 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _c_int,
         [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr] + [_c_int] * 4 + [_c_int] * 5 + [_c_ptr],
     ),
-    "ddpm_gencat_stage_y_bytes": (_c_size, [_c_int] * 9),
-    "ddpm_gencat_stage_y": (
+    "ddpm_gencat_stage_bytes": (_c_size, [_c_int] * 9),
+    "ddpm_gencat_stage": (
         _c_int,
-        [_c_ptr, _c_ptr, _c_size] + [_c_int] * 4 + [_c_int] * 5 + [_c_ptr],
+        [_c_ptr, _c_ptr, _c_ptr, _c_size] + [_c_int] * 4 + [_c_int] * 5 + [_c_ptr],
     ),
     "ddpm_gencat_bwd_x_staged": (
         _c_int,
@@ -64,6 +64,10 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ddpm_gencat_bwd_yw": (
         _c_int,
         [_c_ptr] * 8 + [_c_size] + [_c_int] * 4 + [_c_int] * 5 + [_c_ptr],
+    ),
+    "ddpm_gencat_bwd_yw_staged": (
+        _c_int,
+        [_c_ptr, _c_size] + [_c_ptr] * 6 + [_c_size] + [_c_int] * 4 + [_c_int] * 5 + [_c_ptr],
     ),
     "ddpm_gencat_bwd_yw_static": (
         _c_int,

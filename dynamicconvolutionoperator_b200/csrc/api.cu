@@ -45,15 +45,16 @@ int gencat_bwd_x(const void* y, const void* staged, size_t staged_bytes, const v
                  const void* bias, const void* gout, void* gx, int n, int c, int h, int w, int ks,
                  int d0, int d1, int d2, int dt, cudaStream_t st);
 namespace gencat {
-size_t stage_y_bytes(int n, int c, int h, int w, int ks, int d0, int d1, int d2, int dt);
-int stage_y(const void* y, void* staged, size_t staged_bytes, int n, int c, int h, int w, int ks,
-            int d0, int d1, int d2, int dt, cudaStream_t st);
+size_t stage_bytes(int n, int c, int h, int w, int ks, int d0, int d1, int d2, int dt);
+int stage(const void* x, const void* y, void* staged, size_t staged_bytes, int n, int c, int h,
+          int w, int ks, int d0, int d1, int d2, int dt, cudaStream_t st);
 }  // namespace gencat
 
 size_t gencat_bwd_workspace_bytes(int n, int c, int h, int w, int ks);
-int gencat_bwd_yw(const void* x, const void* y, const void* wpack, const void* gout, void* gy,
-                  void* gw, void* gb, void* workspace, size_t ws_bytes, int n, int c, int h, int w,
-                  int ks, int d0, int d1, int d2, int dt, cudaStream_t st);
+int gencat_bwd_yw(const void* x, const void* y, const void* staged, size_t staged_bytes,
+                  const void* wpack, const void* gout, void* gy, void* gw, void* gb,
+                  void* workspace, size_t ws_bytes, int n, int c, int h, int w, int ks, int d0,
+                  int d1, int d2, int dt, cudaStream_t st);
 
 int gencat_bwd_yw_static(const void* x, const void* y, const void* wpack, const void* gout,
                          void* gy, void* gw, void* gb, int n, int c, int h, int w, int ks, int d0,
@@ -131,16 +132,17 @@ int ddpm_gencat_bwd_x(const void* y, const void* packed, const void* bias, const
                             d1, d2, dtype, static_cast<cudaStream_t>(stream));
 }
 
-size_t ddpm_gencat_stage_y_bytes(int n, int c, int h, int w, int ksize, int d0, int d1, int d2,
-                                 int dtype) {
-  return ddpm::gencat::stage_y_bytes(n, c, h, w, ksize, d0, d1, d2, dtype);
+size_t ddpm_gencat_stage_bytes(int n, int c, int h, int w, int ksize, int d0, int d1, int d2,
+                               int dtype) {
+  return ddpm::gencat::stage_bytes(n, c, h, w, ksize, d0, d1, d2, dtype);
 }
 
-int ddpm_gencat_stage_y(const void* y, void* staged, size_t staged_bytes, int n, int c, int h,
-                        int w, int ksize, int d0, int d1, int d2, int dtype, void* stream) {
+int ddpm_gencat_stage(const void* x, const void* y, void* staged, size_t staged_bytes, int n,
+                      int c, int h, int w, int ksize, int d0, int d1, int d2, int dtype,
+                      void* stream) {
   ddpm::clear_error();
-  return ddpm::gencat::stage_y(y, staged, staged_bytes, n, c, h, w, ksize, d0, d1, d2, dtype,
-                               static_cast<cudaStream_t>(stream));
+  return ddpm::gencat::stage(x, y, staged, staged_bytes, n, c, h, w, ksize, d0, d1, d2, dtype,
+                             static_cast<cudaStream_t>(stream));
 }
 
 int ddpm_gencat_bwd_x_staged(const void* staged_y, size_t staged_bytes, const void* packed,
@@ -162,9 +164,21 @@ int ddpm_gencat_bwd_yw(const void* x, const void* y, const void* packed, const v
                        size_t workspace_bytes, int n, int c, int h, int w, int ksize, int d0,
                        int d1, int d2, int dtype, void* stream) {
   ddpm::clear_error();
-  return ddpm::gencat_bwd_yw(x, y, packed, grad_out, grad_y, grad_weight, grad_bias, workspace,
-                             workspace_bytes, n, c, h, w, ksize, d0, d1, d2, dtype,
+  return ddpm::gencat_bwd_yw(x, y, nullptr, 0, packed, grad_out, grad_y, grad_weight, grad_bias,
+                             workspace, workspace_bytes, n, c, h, w, ksize, d0, d1, d2, dtype,
                              static_cast<cudaStream_t>(stream));
+}
+
+int ddpm_gencat_bwd_yw_staged(const void* staged, size_t staged_bytes, const void* packed,
+                              const void* grad_out, void* grad_y, void* grad_weight,
+                              void* grad_bias, void* workspace, size_t ws_bytes, int n, int c,
+                              int h, int w, int ksize, int d0, int d1, int d2, int dtype,
+                              void* stream) {
+  ddpm::clear_error();
+  DDPM_CHECK_ARG(staged != nullptr, "null staged");
+  return ddpm::gencat_bwd_yw(nullptr, nullptr, staged, staged_bytes, packed, grad_out, grad_y,
+                             grad_weight, grad_bias, workspace, ws_bytes, n, c, h, w, ksize, d0,
+                             d1, d2, dtype, static_cast<cudaStream_t>(stream));
 }
 
 int ddpm_gencat_bwd_yw_static(const void* x, const void* y, const void* packed,

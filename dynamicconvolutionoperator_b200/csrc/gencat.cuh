@@ -568,22 +568,30 @@ int status_ptr(int** out);
 int read_status(int reset, int* code);
 int num_sms();
 
-// Staged y (gencat_stage.cu): y channel-last, zero padded, in the MMA operand
-// type, so every row segment a kernel stages is one contiguous 1-D bulk copy.
-// Layout [part][n][Hp][G][Wp][8]: 16-byte rows of 8 channels, G = round16(C+1)/8
+// Staged operands of the fused backward (gencat_stage.cu), written once per
+// backward so the kernels stage tiles with bulk / TMA copies instead of
+// per-thread loads and register transposes.
+//
+// y plane: y channel-last, zero padded, in the MMA operand type; layout
+// [part][n][G][Hp][Wp][8]: 16-byte rows of 8 channels, G = round16(C+1)/8
 // groups; channel C is the constant one of the bias / db column (1 at every
 // position), channels above it are zero. Plane row i holds image row i - ph
 // (ph = (K/2) * max dilation), plane column j holds image column j - 8, and
 // Wp = 128 * ceil(W / 128) + 16, so a 144-pixel segment starting 8 columns left
 // of any 128-pixel row tile, at any row within the dilation halo, is in range.
 // FP32 stores a bf16 hi part and a bf16 residual part.
+//
+// x plane (after the y plane, 256-byte aligned): x in FP32, 4 channels per
+// 16-byte cell, [n][Cq][H][W][4] with Cq = ceil(C/4) (channels >= C zero); not
+// padded: it is read by TMA, which zero-fills outside the image.
 struct StageLayout {
-  int N, C, H, W, G, ph, Hp, Wp, parts;
-  size_t part_bytes;
-  __host__ __device__ size_t total_bytes() const { return part_bytes * parts; }
-  // byte offset of the 16-byte row (part, n, plane row i, group g, plane column j)
+  int N, C, H, W, G, ph, Hp, Wp, parts, Cq;
+  size_t part_bytes, x_offset, x_bytes;
+  __host__ __device__ size_t y_bytes() const { return part_bytes * parts; }
+  __host__ __device__ size_t total_bytes() const { return x_offset + x_bytes; }
+  // byte offset of the y-plane row (part, n, group g, plane row i, plane column j)
   __host__ __device__ size_t row_offset(int part, int n, int i, int g, int j) const {
-    return (size_t)part * part_bytes + ((((size_t)n * Hp + i) * G + g) * Wp + j) * 16;
+    return (size_t)part * part_bytes + ((((size_t)n * G + g) * Hp + i) * Wp + j) * 16;
   }
   static StageLayout make(int n, int c, int h, int w, int ks, int d0, int d1, int d2, int dt) {
     StageLayout L;
@@ -596,13 +604,17 @@ struct StageLayout {
     L.Hp = h + 2 * L.ph;
     L.Wp = (w + kTileM - 1) / kTileM * kTileM + 16;
     L.parts = dt == DDPM_F32 ? 2 : 1;
-    L.part_bytes = (size_t)n * L.Hp * L.G * L.Wp * 16;
+    L.part_bytes = (size_t)n * L.G * L.Hp * L.Wp * 16;
+    L.Cq = (c + 3) / 4;
+    L.x_offset = (L.y_bytes() + 255) / 256 * 256;
+    L.x_bytes = (size_t)n * L.Cq * h * w * 16;
     return L;
   }
 };
-size_t stage_y_bytes(int n, int c, int h, int w, int ks, int d0, int d1, int d2, int dt);
-int stage_y(const void* y, void* staged, size_t staged_bytes, int n, int c, int h, int w, int ks,
-            int d0, int d1, int d2, int dt, cudaStream_t st);
+size_t stage_bytes(int n, int c, int h, int w, int ks, int d0, int d1, int d2, int dt);
+// x may be null: only the y plane is written (enough for dX).
+int stage(const void* x, const void* y, void* staged, size_t staged_bytes, int n, int c, int h,
+          int w, int ks, int d0, int d1, int d2, int dt, cudaStream_t st);
 
 }  // namespace gencat
 }  // namespace ddpm

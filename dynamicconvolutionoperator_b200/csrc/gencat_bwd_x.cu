@@ -538,8 +538,8 @@ int dispatch(int ks, const BxParams& prm, cudaStream_t st) {
 
 }  // namespace
 
-// `staged`: staged y (gencat::stage_y, at least stage_y_bytes() bytes) or
-// null to stage the operand from y itself.
+// `staged`: staged operands (gencat::stage; the y plane is used) or null to
+// stage the operand from y itself.
 int gencat_bwd_x(const void* y, const void* staged, size_t staged_bytes, const void* wpack,
                  const void* bias, const void* gout, void* gx, int n, int c, int h, int w, int ks,
                  int d0, int d1, int d2, int dt, cudaStream_t st) {
@@ -567,9 +567,9 @@ int gencat_bwd_x(const void* y, const void* staged, size_t staged_bytes, const v
   prm.staged = static_cast<const uint8_t*>(staged);
   prm.sl = gencat::StageLayout::make(n, c, h, w, ks, d0, d1, d2, dt);
   if (staged != nullptr) {
-    if (staged_bytes < prm.sl.total_bytes())
+    if (staged_bytes < prm.sl.y_bytes())
       return set_error(DDPM_ERR_WORKSPACE, "staged y too small (%zu < %zu)", staged_bytes,
-                       prm.sl.total_bytes());
+                       prm.sl.y_bytes());
     DDPM_CHECK_ARG((reinterpret_cast<uintptr_t>(staged) & 15u) == 0,
                    "staged y must be 16-byte aligned");
     // gradient segments by TMA when the row pitch and base allow a tensor map

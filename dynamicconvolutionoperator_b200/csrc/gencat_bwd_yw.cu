@@ -31,6 +31,7 @@
 #include "common.cuh"
 #include "tc.cuh"
 #include "gencat.cuh"
+#include "tmap.cuh"
 
 namespace ddpm {
 namespace {
@@ -705,8 +706,13 @@ __global__ void gencat_wreduce_kernel(const float* __restrict__ partial, T* __re
 // accumulator with reductions to global memory (the other channel groups'
 // CTAs add theirs); the x-halo producer warps do that drain for the previous
 // tile while the builders work on the next. Builders run two threads per
-// pixel (four slots each); one issuer warp per GEMM.
-template <typename T, int KS>
+// pixel (four slots each); one issuer warp per GEMM. With staged operands
+// (gencat_stage.cu) one thread per producer group issues one TMA copy per tile
+// instead: the x halo from the FP32 cell plane (box 32 px x halo rows x 4
+// channel quads, zero filled outside the image) and the y tile from the y
+// plane (box 16 px x 8 rows x all channel groups), which makes the dW GEMM's B
+// operand MN-major ([channel group][pixel][8 channels]).
+template <typename T, int KS, bool kStaged = false>
 struct DywCfg {
   static constexpr bool kSplit = IoTraits<T>::kSplit;
   static constexpr int kParts = kSplit ? 2 : 1;
@@ -760,10 +766,18 @@ struct DywParams {
   int* status;
 };
 
-template <typename T, int KS>
-__global__ void __launch_bounds__(DywCfg<T, KS>::kThreads, 1)
-gencat_bwd_dyw_kernel(const DywParams p) {
-  using Cfg = DywCfg<T, KS>;
+// Tensor maps of the staged operands (a separate grid-constant parameter so the
+// non-staged kernel's parameter block keeps its register allocation).
+struct DywMaps {
+  CUtensorMap xmap;  // staged x plane (64-bit view) {W*2, H, Cq, N}, box {64, 8+2R, 4, 1}
+  CUtensorMap ymap;  // staged y plane (64-bit view) {Wp*2, Hp, G, parts*N}, box {32, 8, G, 1}
+  int ph;            // y-plane row offset
+};
+
+template <typename T, int KS, bool kStaged>
+__global__ void __launch_bounds__(DywCfg<T, KS, kStaged>::kThreads, 1)
+gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
+  using Cfg = DywCfg<T, KS, kStaged>;
   using Op = typename IoTraits<T>::Op;
   constexpr int NS = Cfg::kDkSlots;
   constexpr int NX = Cfg::kXBufs;
@@ -896,9 +910,12 @@ gencat_bwd_dyw_kernel(const DywParams p) {
   } else if (warp == 2) {
     // ---- dW issuer: D_w[octet] += dK . y over the split's tiles ---------------
     if (lane == 0) {
-      const uint32_t idesc = tc::idesc_f16(kTileM, Nw, IoTraits<T>::kBf16, true, false);
-      const uint32_t b_lbo = Nw * 16;           // pixel-group stride of the y tile
-      const uint64_t b_step = (2 * b_lbo) >> 4;
+      // y tile: K-major [pixel group][channel][8 px] (staged from y), or MN-major
+      // [channel group][pixel][8 ch] (copied from the y plane)
+      const uint32_t idesc = tc::idesc_f16(kTileM, Nw, IoTraits<T>::kBf16, true, kStaged);
+      const uint32_t b_lbo = kStaged ? 128u : (uint32_t)Nw * 16;
+      const uint32_t b_sbo = kStaged ? (uint32_t)kTileM * 16 : 128u;
+      const uint64_t b_step = kStaged ? (uint64_t)(256 >> 4) : (uint64_t)((2 * b_lbo) >> 4);
       const uint64_t y_lo = (kTileM * Nw * 2) >> 4;
       uint32_t kq = 0, it = 0;
       bool first = true;
@@ -910,7 +927,7 @@ gencat_bwd_dyw_kernel(const DywParams p) {
         }
         tc::tc_fence_after();
         const uint64_t yd =
-            tc::smem_desc(tc::smem_u32(smem + L.y + yb * L.y_bytes), b_lbo, 128);
+            tc::smem_desc(tc::smem_u32(smem + L.y + yb * L.y_bytes), b_lbo, b_sbo);
         for (int oct = 0; oct < NOCT; ++oct, ++kq) {
           const int ks_ = kq % NS;
           if (!tc::mbar_wait(&k_full[ks_], (kq / NS) & 1, abort_flag, kWaitNs)) {
@@ -981,9 +998,19 @@ gencat_bwd_dyw_kernel(const DywParams p) {
       int n, h0, w0;
       tile_origin(tile, p.tiles_w, p.tiles_h, n, h0, w0);
       float4* xr = reinterpret_cast<float4*>(smem + L.xr + xb * L.xr_bytes);
-      stage_halo<T, Cfg::kXItems>(plan, static_cast<const T*>(p.x), xr, n, C, H, W, cg * 16,
-                                  h0 - R, w0 - 8, xr_rows);
-      tc::mbar_arrive(&x_full[xb]);
+      if constexpr (kStaged) {
+        // columns w0-8 .. w0+23 (x in 8-byte units), rows h0-R .., quads 4cg .. 4cg+3
+        if (pt == 0) {
+          tc::mbar_arrive_expect_tx(&x_full[xb], L.xr_bytes);
+          tc::tma_load_4d(xr, &maps.xmap, (w0 - 8) * 2, h0 - R, cg * 4, n, &x_full[xb]);
+        } else {
+          tc::mbar_arrive(&x_full[xb]);
+        }
+      } else {
+        stage_halo<T, Cfg::kXItems>(plan, static_cast<const T*>(p.x), xr, n, C, H, W, cg * 16,
+                                    h0 - R, w0 - 8, xr_rows);
+        tc::mbar_arrive(&x_full[xb]);
+      }
       if (xq > 0 && !drain(xq - 1)) {
         fail(abort_flag, p.status, 59);
         failed = true;
@@ -1005,11 +1032,24 @@ gencat_bwd_dyw_kernel(const DywParams p) {
       int n, h0, w0;
       tile_origin(tile, p.tiles_w, p.tiles_h, n, h0, w0);
       uint8_t* ys = smem + L.y + yb * L.y_bytes;
-      stage_y_mn<T, Op, Cfg::kSplit, Cfg::kYItems>(plan, static_cast<const T*>(p.y), ys,
-                                                   ys + kTileM * Nw * 2, n, C, Nw, C, H, W, h0,
-                                                   w0);
-      tc::fence_proxy_async_smem();
-      tc::mbar_arrive(&y_full[yb]);
+      if constexpr (kStaged) {
+        // y plane rows h0+ph .. +7, columns w0+8 .. w0+23, every channel group
+        if (pt == 0) {
+          tc::mbar_arrive_expect_tx(&y_full[yb], L.y_bytes);
+          tc::tma_load_4d(ys, &maps.ymap, (w0 + 8) * 2, h0 + maps.ph, 0, n, &y_full[yb]);
+          if constexpr (Cfg::kSplit)
+            tc::tma_load_4d(ys + kTileM * Nw * 2, &maps.ymap, (w0 + 8) * 2, h0 + maps.ph, 0,
+                            p.N + n, &y_full[yb]);
+        } else {
+          tc::mbar_arrive(&y_full[yb]);
+        }
+      } else {
+        stage_y_mn<T, Op, Cfg::kSplit, Cfg::kYItems>(plan, static_cast<const T*>(p.y), ys,
+                                                     ys + kTileM * Nw * 2, n, C, Nw, C, H, W, h0,
+                                                     w0);
+        tc::fence_proxy_async_smem();
+        tc::mbar_arrive(&y_full[yb]);
+      }
     }
   } else {
     // ---- builders (two threads per pixel), D_y and D_w drains ------------------
@@ -1172,15 +1212,44 @@ DywPlan plan_dyw(int n, int c, int h, int w, int ks) {
   return q;
 }
 
-template <typename T, int KS>
-int launch_dyw(const DywParams& prm, cudaStream_t st) {
-  using Cfg = DywCfg<T, KS>;
+template <typename T, int KS, bool kStaged>
+int launch_dyw_k(const DywParams& prm, const DywMaps& maps, cudaStream_t st) {
+  using Cfg = DywCfg<T, KS, kStaged>;
   const DywSmem L = dyw_smem_layout<T, KS>(prm.Cp, prm.Nw, prm.R);
-  auto fn = gencat_bwd_dyw_kernel<T, KS>;
+  auto fn = gencat_bwd_dyw_kernel<T, KS, kStaged>;
   DDPM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total));
-  fn<<<prm.ncg * prm.splits, Cfg::kThreads, L.total, st>>>(prm);
+  fn<<<prm.ncg * prm.splits, Cfg::kThreads, L.total, st>>>(prm, maps);
   DDPM_CHECK_LAUNCH("gencat_bwd_dyw_kernel");
   return DDPM_OK;
+}
+
+template <typename T, int KS>
+int launch_dyw(const DywParams& prm, const DywMaps& maps, bool staged, cudaStream_t st) {
+  return staged ? launch_dyw_k<T, KS, true>(prm, maps, st)
+                : launch_dyw_k<T, KS, false>(prm, maps, st);
+}
+
+// Tensor maps of the staged x and y planes for the merged kernel; false when
+// the driver rejects one (the caller then stages from x and y).
+bool encode_stage_maps(DywMaps& dp, int R, const uint8_t* staged, const gencat::StageLayout& sl) {
+  const uint64_t xd[4] = {(uint64_t)sl.W * 2, (uint64_t)sl.H, (uint64_t)sl.Cq, (uint64_t)sl.N};
+  const uint64_t xs[3] = {(uint64_t)sl.W * 16, (uint64_t)sl.H * sl.W * 16,
+                          (uint64_t)sl.Cq * sl.H * sl.W * 16};
+  const uint32_t xb[4] = {2 * gencat::kHaloCols, (uint32_t)(gencat::kTileH + 2 * R), 4, 1};
+  const uint64_t yd[4] = {(uint64_t)sl.Wp * 2, (uint64_t)sl.Hp, (uint64_t)sl.G,
+                          (uint64_t)sl.parts * sl.N};
+  const uint64_t ys[3] = {(uint64_t)sl.Wp * 16, (uint64_t)sl.Hp * sl.Wp * 16,
+                          (uint64_t)sl.G * sl.Hp * sl.Wp * 16};
+  const uint32_t yb[4] = {2 * gencat::kTileW, (uint32_t)gencat::kTileH, (uint32_t)sl.G, 1};
+  if (encode_tmap(&dp.xmap, CU_TENSOR_MAP_DATA_TYPE_UINT64, 4, staged + sl.x_offset, xd, xs, xb,
+                  CU_TENSOR_MAP_SWIZZLE_NONE) != DDPM_OK ||
+      encode_tmap(&dp.ymap, CU_TENSOR_MAP_DATA_TYPE_UINT64, 4, staged, yd, ys, yb,
+                  CU_TENSOR_MAP_SWIZZLE_NONE) != DDPM_OK) {
+    clear_error();
+    return false;
+  }
+  dp.ph = sl.ph;
+  return true;
 }
 
 template <typename T>
@@ -1208,12 +1277,25 @@ size_t gencat_bwd_workspace_bytes(int n, int c, int h, int w, int ks) {
   return a > b ? a : b;
 }
 
-int gencat_bwd_yw(const void* x, const void* y, const void* wpack, const void* gout, void* gy,
-                  void* gw, void* gb, void* workspace, size_t ws_bytes, int n, int c, int h, int w,
-                  int ks, int d0, int d1, int d2, int dt, cudaStream_t st) {
+// `staged`: staged operands (gencat::stage with x) for the merged pass, or null
+// to stage tiles from x and y.
+int gencat_bwd_yw(const void* x, const void* y, const void* staged, size_t staged_bytes,
+                  const void* wpack, const void* gout, void* gy, void* gw, void* gb,
+                  void* workspace, size_t ws_bytes, int n, int c, int h, int w, int ks, int d0,
+                  int d1, int d2, int dt, cudaStream_t st) {
   int rc = gencat::check_shape(n, c, h, w, ks, d0, d1, d2, dt);
   if (rc) return rc;
-  DDPM_CHECK_ARG(x && y && wpack && gout, "null pointer");
+  DDPM_CHECK_ARG(((x && y) || staged) && wpack && gout, "null pointer");
+  if (staged != nullptr) {
+    const gencat::StageLayout sl = gencat::StageLayout::make(n, c, h, w, ks, d0, d1, d2, dt);
+    if (staged_bytes < sl.total_bytes())
+      return set_error(DDPM_ERR_WORKSPACE, "staged operands too small (%zu < %zu)", staged_bytes,
+                       sl.total_bytes());
+    DDPM_CHECK_ARG((reinterpret_cast<uintptr_t>(staged) & 255u) == 0,
+                   "staged operands must be 256-byte aligned");
+    DDPM_CHECK_ARG(gy && gw && gb && workspace,
+                   "the staged pass computes grad_y, grad_weight and grad_bias together");
+  }
   const gencat::PackLayout pl = gencat::PackLayout::make(c, ks, dt);
   const int R = (ks / 2) * max3(d0, d1, d2);
   const int tiles_w = (w + gencat::kTileW - 1) / gencat::kTileW;
@@ -1254,14 +1336,21 @@ int gencat_bwd_yw(const void* x, const void* y, const void* wpack, const void* g
       dp.ncg = q.ncg;
       dp.splits = q.splits;
       dp.status = status;
+      bool use_staged = false;
+      DywMaps maps{};
+      if (staged != nullptr)
+        use_staged = encode_stage_maps(
+            maps, R, static_cast<const uint8_t*>(staged),
+            gencat::StageLayout::make(n, c, h, w, ks, d0, d1, d2, dt));
+      DDPM_CHECK_ARG(use_staged || (x && y), "tensor maps unavailable: x and y are needed");
       DDPM_CUDA_TRY(cudaMemsetAsync(dp.gy_acc, 0, (size_t)n * c * h * w * sizeof(float), st));
       switch (dt * 10 + ks) {
-        case DDPM_BF16 * 10 + 1: rc = launch_dyw<__nv_bfloat16, 1>(dp, st); break;
-        case DDPM_BF16 * 10 + 3: rc = launch_dyw<__nv_bfloat16, 3>(dp, st); break;
-        case DDPM_F16 * 10 + 1: rc = launch_dyw<__half, 1>(dp, st); break;
-        case DDPM_F16 * 10 + 3: rc = launch_dyw<__half, 3>(dp, st); break;
-        case DDPM_F32 * 10 + 1: rc = launch_dyw<float, 1>(dp, st); break;
-        case DDPM_F32 * 10 + 3: rc = launch_dyw<float, 3>(dp, st); break;
+        case DDPM_BF16 * 10 + 1: rc = launch_dyw<__nv_bfloat16, 1>(dp, maps, use_staged, st); break;
+        case DDPM_BF16 * 10 + 3: rc = launch_dyw<__nv_bfloat16, 3>(dp, maps, use_staged, st); break;
+        case DDPM_F16 * 10 + 1: rc = launch_dyw<__half, 1>(dp, maps, use_staged, st); break;
+        case DDPM_F16 * 10 + 3: rc = launch_dyw<__half, 3>(dp, maps, use_staged, st); break;
+        case DDPM_F32 * 10 + 1: rc = launch_dyw<float, 1>(dp, maps, use_staged, st); break;
+        case DDPM_F32 * 10 + 3: rc = launch_dyw<float, 3>(dp, maps, use_staged, st); break;
         default: rc = set_error(DDPM_ERR_UNSUPPORTED, "unsupported dtype/kernel size");
       }
       if (rc) return rc;
@@ -1272,6 +1361,8 @@ int gencat_bwd_yw(const void* x, const void* y, const void* wpack, const void* g
       }
     }
   }
+  // separate dY and dW passes (no merged-pass workspace): they stage from x and y
+  DDPM_CHECK_ARG(x && y, "x and y are needed without a merged-pass workspace");
   if (gy != nullptr) {
     ByParams bp{};
     bp.x = x;
@@ -1424,8 +1515,8 @@ int gencat_bwd_yw_static(const void* x, const void* y, const void* wpack, const 
   if (rc) return rc;
   // dY needs no scratch: the workspace path's dY launch is used as is.
   if (gy != nullptr) {
-    rc = gencat_bwd_yw(x, y, wpack, gout, gy, nullptr, nullptr, nullptr, 0, n, c, h, w, ks, d0,
-                       d1, d2, dt, st);
+    rc = gencat_bwd_yw(x, y, nullptr, 0, wpack, gout, gy, nullptr, nullptr, nullptr, 0, n, c, h,
+                       w, ks, d0, d1, d2, dt, st);
     if (rc) return rc;
   }
   if (gw == nullptr) return DDPM_OK;

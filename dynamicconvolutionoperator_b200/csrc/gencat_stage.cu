@@ -1,8 +1,9 @@
-// Staged y for the fused generator backward (layout: StageLayout in
+// Staged operands of the fused generator backward (layout: StageLayout in
 // gencat.cuh). One pass over y writes it channel-last in the MMA operand type,
-// zero padded and with the constant-one bias channel, so the backward kernels
-// stage their y row segments with 1-D bulk copies instead of per-thread loads
-// and register transposes (which bounded them by load latency).
+// zero padded and with the constant-one bias channel; one pass over x writes
+// it as FP32 4-channel cells. The backward kernels then stage their tiles with
+// 1-D bulk / TMA copies instead of per-thread loads and register transposes
+// (which bounded them by load latency).
 #include "common.cuh"
 #include "gencat.cuh"
 
@@ -58,13 +59,44 @@ __global__ void __launch_bounds__(256) stage_y_kernel(const T* __restrict__ y,
   }
 }
 
+// x plane: thread = one 16-byte cell (n, channel quad q, h, w) = x[n, 4q .. 4q+3, h, w]
+// in FP32 (channels >= C zero); consecutive threads = consecutive columns.
 template <typename T>
-int launch_stage(const T* y, uint8_t* staged, const StageLayout& L, cudaStream_t st) {
+__global__ void __launch_bounds__(256) stage_x_kernel(const T* __restrict__ x,
+                                                      float4* __restrict__ xp,
+                                                      const StageLayout L) {
+  const size_t P = (size_t)L.H * L.W;
+  const size_t cells = (size_t)L.N * L.Cq * P;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < cells;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const size_t pix = i % P;
+    const size_t nq = i / P;
+    const int q = (int)(nq % L.Cq), n = (int)(nq / L.Cq);
+    float v[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int c = 4 * q + k;
+      v[k] = c < L.C ? to_f32<T>(__ldg(x + ((size_t)n * L.C + c) * P + pix)) : 0.f;
+    }
+    xp[i] = make_float4(v[0], v[1], v[2], v[3]);
+  }
+}
+
+template <typename T>
+int launch_stage(const T* x, const T* y, uint8_t* staged, const StageLayout& L, cudaStream_t st) {
   uint4* hi = reinterpret_cast<uint4*>(staged);
   uint4* lo = L.parts > 1 ? reinterpret_cast<uint4*>(staged + L.part_bytes) : nullptr;
   const dim3 grid((unsigned)(L.N * L.Hp), (unsigned)((L.Wp + kStageCols - 1) / kStageCols));
   stage_y_kernel<T><<<grid, 256, 0, st>>>(y, hi, lo, L);
   DDPM_CHECK_LAUNCH("stage_y_kernel");
+  if (x != nullptr) {
+    const size_t cells = (size_t)L.N * L.Cq * L.H * L.W;
+    size_t blocks = (cells + 255) / 256;
+    if (blocks > 65535u * 8u) blocks = 65535u * 8u;
+    stage_x_kernel<T><<<(unsigned)blocks, 256, 0, st>>>(
+        x, reinterpret_cast<float4*>(staged + L.x_offset), L);
+    DDPM_CHECK_LAUNCH("stage_x_kernel");
+  }
   return DDPM_OK;
 }
 
@@ -72,7 +104,7 @@ int launch_stage(const T* y, uint8_t* staged, const StageLayout& L, cudaStream_t
 
 namespace gencat {
 
-size_t stage_y_bytes(int n, int c, int h, int w, int ks, int d0, int d1, int d2, int dt) {
+size_t stage_bytes(int n, int c, int h, int w, int ks, int d0, int d1, int d2, int dt) {
   if (check_shape(n, c, h, w, ks, d0, d1, d2, dt) != DDPM_OK) {
     clear_error();
     return 0;
@@ -80,22 +112,27 @@ size_t stage_y_bytes(int n, int c, int h, int w, int ks, int d0, int d1, int d2,
   return StageLayout::make(n, c, h, w, ks, d0, d1, d2, dt).total_bytes();
 }
 
-int stage_y(const void* y, void* staged, size_t staged_bytes, int n, int c, int h, int w, int ks,
-            int d0, int d1, int d2, int dt, cudaStream_t st) {
+int stage(const void* x, const void* y, void* staged, size_t staged_bytes, int n, int c, int h,
+          int w, int ks, int d0, int d1, int d2, int dt, cudaStream_t st) {
   int rc = check_shape(n, c, h, w, ks, d0, d1, d2, dt);
   if (rc) return rc;
   DDPM_CHECK_ARG(y && staged, "null pointer");
   const StageLayout L = StageLayout::make(n, c, h, w, ks, d0, d1, d2, dt);
-  if (staged_bytes < L.total_bytes())
+  const size_t need = x != nullptr ? L.total_bytes() : L.y_bytes();
+  if (staged_bytes < need)
     return set_error(DDPM_ERR_WORKSPACE, "staged buffer too small (%zu < %zu)", staged_bytes,
-                     L.total_bytes());
-  DDPM_CHECK_ARG((reinterpret_cast<uintptr_t>(staged) & 15u) == 0,
-                 "staged buffer must be 16-byte aligned");
+                     need);
+  DDPM_CHECK_ARG((reinterpret_cast<uintptr_t>(staged) & 255u) == 0,
+                 "staged buffer must be 256-byte aligned");
   uint8_t* s = static_cast<uint8_t*>(staged);
   switch (dt) {
-    case DDPM_BF16: return launch_stage(static_cast<const __nv_bfloat16*>(y), s, L, st);
-    case DDPM_F16: return launch_stage(static_cast<const __half*>(y), s, L, st);
-    default: return launch_stage(static_cast<const float*>(y), s, L, st);
+    case DDPM_BF16:
+      return launch_stage(static_cast<const __nv_bfloat16*>(x),
+                          static_cast<const __nv_bfloat16*>(y), s, L, st);
+    case DDPM_F16:
+      return launch_stage(static_cast<const __half*>(x), static_cast<const __half*>(y), s, L, st);
+    default:
+      return launch_stage(static_cast<const float*>(x), static_cast<const float*>(y), s, L, st);
   }
 }
 

@@ -145,25 +145,29 @@ DDPM_API int ddpm_gencat_bwd_x(const void* y, const void* packed, const void* bi
                                void* stream);
 
 /*
- * Staged y for the fused backward: y written once channel-last, zero padded
- * by the dilation halo, in the tensor-core operand type (fp32: bf16 hi and
- * residual parts) with the constant-one bias channel, so the backward kernels
- * stage every y row segment with one bulk copy. Same role as the per-tile y
- * loads inside `_generator_dynamic_cat_bwd_x` (reference
- * `_triton_kernels.py:430-531`), done once per backward instead.
- * ddpm_gencat_stage_y_bytes() gives the size (0 for unsupported shapes);
- * `staged` must be 16-byte aligned. The contents depend on y only.
+ * Staged operands for the fused backward, written once per backward:
+ * y channel-last, zero padded by the dilation halo, in the tensor-core operand
+ * type (fp32: bf16 hi and residual parts) with the constant-one bias channel,
+ * and (when x is given) x as FP32 cells of 4 channels. The backward kernels
+ * then stage every tile with bulk / TMA copies. Same role as the per-tile x
+ * and y loads inside `_generator_dynamic_cat_bwd_x` and
+ * `_generator_dynamic_cat_bwd_y` / `_bwd_weight_partial` (reference
+ * `_triton_kernels.py:430-751`), done once per backward instead.
+ * ddpm_gencat_stage_bytes() gives the size with the x part (0 for unsupported
+ * shapes); with x == NULL only the leading y part is written (enough for
+ * ddpm_gencat_bwd_x_staged). `staged` must be 256-byte aligned. The contents
+ * depend on x and y only.
  */
-DDPM_API size_t ddpm_gencat_stage_y_bytes(int n, int c, int h, int w, int ksize,
-                                          int d0, int d1, int d2, int dtype);
-DDPM_API int ddpm_gencat_stage_y(const void* y, void* staged, size_t staged_bytes,
-                                 int n, int c, int h, int w,
-                                 int ksize, int d0, int d1, int d2, int dtype,
-                                 void* stream);
+DDPM_API size_t ddpm_gencat_stage_bytes(int n, int c, int h, int w, int ksize,
+                                        int d0, int d1, int d2, int dtype);
+DDPM_API int ddpm_gencat_stage(const void* x, const void* y, void* staged, size_t staged_bytes,
+                               int n, int c, int h, int w,
+                               int ksize, int d0, int d1, int d2, int dtype,
+                               void* stream);
 
 /*
- * ddpm_gencat_bwd_x reading y from its staged copy (ddpm_gencat_stage_y with
- * the same sizes and dtype). Same result as ddpm_gencat_bwd_x; replaces the
+ * ddpm_gencat_bwd_x reading y from the staged operands (ddpm_gencat_stage with
+ * the same sizes and dtype; x may have been NULL there). Same result as ddpm_gencat_bwd_x; replaces the
  * same reference kernel (`_triton_kernels.py:430-531`).
  */
 DDPM_API int ddpm_gencat_bwd_x_staged(const void* staged_y, size_t staged_bytes,
@@ -194,6 +198,20 @@ DDPM_API int ddpm_gencat_bwd_yw(const void* x, const void* y, const void* packed
                                 int n, int c, int h, int w,
                                 int ksize, int d0, int d1, int d2, int dtype,
                                 void* stream);
+
+/*
+ * ddpm_gencat_bwd_yw reading x and y from the staged operands
+ * (ddpm_gencat_stage with x and y, same sizes and dtype). grad_y, grad_weight,
+ * grad_bias and the workspace are all required. Same results; replaces the
+ * same reference kernels (`_triton_kernels.py:534-811`).
+ */
+DDPM_API int ddpm_gencat_bwd_yw_staged(const void* staged, size_t staged_bytes,
+                                       const void* packed, const void* grad_out,
+                                       void* grad_y, void* grad_weight, void* grad_bias,
+                                       void* workspace, size_t workspace_bytes,
+                                       int n, int c, int h, int w,
+                                       int ksize, int d0, int d1, int d2, int dtype,
+                                       void* stream);
 
 /*
  * Native 3x3 fuse convolution (stride 1, zero padding 1, Cin <= 256,

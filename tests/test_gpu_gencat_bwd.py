@@ -29,17 +29,17 @@ def _gold_grads(x, y, wt, b, g, ks, dil):
     return torch.autograd.grad(out, (x64, y64, w64, b64), g.double())
 
 
-def _stage_y(yd, ks, dil):
-    """Staged copy of y through the C ABI (ddpm_gencat_stage_y)."""
+def _stage(xd, yd, ks, dil):
+    """Staged operands through the C ABI (ddpm_gencat_stage); xd may be None."""
     from dynamicconvolutionoperator_b200 import _lib
 
     n, c, h, w = yd.shape
     code = _lib.dtype_code(yd.dtype)
-    nb = int(_lib.load().ddpm_gencat_stage_y_bytes(n, c, h, w, ks, *dil, code))
+    nb = int(_lib.load().ddpm_gencat_stage_bytes(n, c, h, w, ks, *dil, code))
     assert nb > 0
     staged = torch.full((nb,), 0xAB, dtype=torch.uint8, device=yd.device)  # no reliance on zeros
-    _lib.call("ddpm_gencat_stage_y", yd.data_ptr(), staged.data_ptr(), nb, n, c, h, w, ks, *dil,
-              code, _lib.stream_handle(yd.device))
+    _lib.call("ddpm_gencat_stage", xd.data_ptr() if xd is not None else None, yd.data_ptr(),
+              staged.data_ptr(), nb, n, c, h, w, ks, *dil, code, _lib.stream_handle(yd.device))
     return staged, nb
 
 
@@ -59,7 +59,7 @@ def test_gencat_bwd_x(shape, ks, dtype, staged):
     gx = torch.full((n, c, h, w), float("nan"), dtype=dtype, device="cuda")
     stream = _lib.stream_handle(gx.device)
     if staged:
-        sy, nb = _stage_y(yd, ks, (1, 3, 5))
+        sy, nb = _stage(None, yd, ks, (1, 3, 5))
         _lib.call("ddpm_gencat_bwd_x_staged", sy.data_ptr(), nb, packed.data_ptr(), bd.data_ptr(),
                   gd.data_ptr(), gx.data_ptr(), n, c, h, w, ks, 1, 3, 5, _lib.dtype_code(dtype),
                   stream)
@@ -75,36 +75,48 @@ def test_gencat_bwd_x(shape, ks, dtype, staged):
 @pytest.mark.parametrize("shape,ks,dil", [((2, 24, 15, 17), 3, (1, 3, 5)), ((1, 64, 9, 130), 3, (2, 1, 4)),
                                           ((1, 5, 4, 3), 1, (1, 1, 1))])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_stage_y_layout(shape, ks, dil, dtype):
-    """Staged y = y channel-last, zero padded by the halo, ones channel at C,
-    [part][n][Hp][G][Wp][8]; fp32 as bf16 hi + residual (hi + lo == y to
-    within bf16 of the residual)."""
+def test_stage_layout(shape, ks, dil, dtype):
+    """y plane = y channel-last, zero padded by the halo, ones channel at C,
+    [part][n][G][Hp][Wp][8]; fp32 as bf16 hi + residual (hi + lo == y to
+    within bf16 of the residual). x plane = x in FP32, [n][ceil(C/4)][H][W][4]."""
     n, c, h, w = shape
-    y = torch.randn(shape, generator=torch.Generator().manual_seed(3)).to(dtype)
-    staged, nb = _stage_y(y.cuda(), ks, dil)
+    gen = torch.Generator().manual_seed(3)
+    y = torch.randn(shape, generator=gen).to(dtype)
+    x = torch.randn(shape, generator=gen).to(dtype)
+    staged, nb = _stage(x.cuda(), y.cuda(), ks, dil)
     torch.cuda.synchronize()
     G = (c + 1 + 15) // 16 * 2
     ph = (ks // 2) * max(dil)
     Hp, Wp = h + 2 * ph, (w + 127) // 128 * 128 + 16
     parts = 2 if dtype == torch.float32 else 1
-    assert nb == parts * n * Hp * G * Wp * 16
+    part_bytes = n * G * Hp * Wp * 16
+    x_off = (parts * part_bytes + 255) // 256 * 256
+    cq = (c + 3) // 4
+    assert nb == x_off + n * cq * h * w * 16
     want = torch.zeros((n, G * 8, Hp, Wp), dtype=torch.float64)
     want[:, :c, ph:ph + h, 8:8 + w] = y.double()
     want[:, c] = 1.0
-    # [n][Hp][G][Wp][8] -> [n][G*8][Hp][Wp]
-    planes = staged.cpu().view(torch.bfloat16 if dtype != torch.float16 else torch.float16)
-    planes = planes.view(parts, n, Hp, G, Wp, 8).permute(0, 1, 3, 5, 2, 4).reshape(parts, n, G * 8, Hp, Wp)
+    # [part][n][G][Hp][Wp][8] -> [part][n][G*8][Hp][Wp]
+    raw = staged.cpu()
+    planes = raw[:parts * part_bytes].view(torch.bfloat16)
+    planes = planes.view(parts, n, G, Hp, Wp, 8).permute(0, 1, 2, 5, 3, 4).reshape(parts, n, G * 8, Hp, Wp)
     got = planes[0].double() + (planes[1].double() if parts == 2 else 0.0)
     # fp32: |y - hi| <= 2^-8 |y| and the residual is rounded to bf16 again
     tol = 2.0 ** -15 * want.abs().max().item() if dtype == torch.float32 else 0.0
     assert (got - want).abs().max().item() <= tol
+    xp = raw[x_off:x_off + n * cq * h * w * 16].view(torch.float32).view(n, cq, h, w, 4)
+    xp = xp.permute(0, 1, 4, 2, 3).reshape(n, cq * 4, h, w)
+    assert torch.equal(xp[:, :c], x.float())
+    assert not xp[:, c:].any()
 
 
 @pytest.mark.parametrize("shape", SHAPES)
 @pytest.mark.parametrize("ks", [1, 3])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_gencat_bwd_yw(shape, ks, dtype):
-    """dY, dW and db from the on-chip dK (split partials + reduce)."""
+@pytest.mark.parametrize("staged", [False, True])
+def test_gencat_bwd_yw(shape, ks, dtype, staged):
+    """dY, dW and db from the on-chip dK (split partials + reduce); staged: x
+    and y read from the staged operands by TMA."""
     from dynamicconvolutionoperator_b200 import _kernels, _lib
 
     x, y, wt, b = _case(shape, ks, dtype)
@@ -113,14 +125,21 @@ def test_gencat_bwd_yw(shape, ks, dtype):
     _, gy_gold, gw_gold, gb_gold = _gold_grads(x, y, wt, b, g, ks, (1, 3, 5))
     xd, yd, wd, bd, gd = x.cuda(), y.cuda(), wt.cuda(), b.cuda(), g.cuda()
     packed = _kernels.pack_generator_weight(wd, bd, c, ks, use_cache=False)
-    gy = torch.empty_like(yd)
-    gw = torch.empty((3 * c * ks * ks, c), dtype=dtype, device="cuda")
-    gb = torch.empty(3 * c * ks * ks, dtype=dtype, device="cuda")
+    gy = torch.full_like(yd, float("nan"))
+    gw = torch.full((3 * c * ks * ks, c), float("nan"), dtype=dtype, device="cuda")
+    gb = torch.full((3 * c * ks * ks,), float("nan"), dtype=dtype, device="cuda")
     ws_bytes = int(_lib.load().ddpm_gencat_bwd_workspace_bytes(n, c, h, w, ks))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
-    _lib.call("ddpm_gencat_bwd_yw", xd.data_ptr(), yd.data_ptr(), packed.data_ptr(), gd.data_ptr(),
-              gy.data_ptr(), gw.data_ptr(), gb.data_ptr(), ws.data_ptr(), ws_bytes,
-              n, c, h, w, ks, 1, 3, 5, _lib.dtype_code(dtype), _lib.stream_handle(gy.device))
+    stream = _lib.stream_handle(gy.device)
+    if staged:
+        st, nb = _stage(xd, yd, ks, (1, 3, 5))
+        _lib.call("ddpm_gencat_bwd_yw_staged", st.data_ptr(), nb, packed.data_ptr(),
+                  gd.data_ptr(), gy.data_ptr(), gw.data_ptr(), gb.data_ptr(), ws.data_ptr(),
+                  ws_bytes, n, c, h, w, ks, 1, 3, 5, _lib.dtype_code(dtype), stream)
+    else:
+        _lib.call("ddpm_gencat_bwd_yw", xd.data_ptr(), yd.data_ptr(), packed.data_ptr(),
+                  gd.data_ptr(), gy.data_ptr(), gw.data_ptr(), gb.data_ptr(), ws.data_ptr(),
+                  ws_bytes, n, c, h, w, ks, 1, 3, 5, _lib.dtype_code(dtype), stream)
     torch.cuda.synchronize()
     rtol, atol = TOL[dtype]
     torch.testing.assert_close(gy.double().cpu(), gy_gold, rtol=rtol, atol=atol)
