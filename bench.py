@@ -358,14 +358,18 @@ def library_kernels(model, x, y, dtype, device):
     sy_bytes = int(_lib.load().ddpm_gencat_stage_bytes(n, C, H, W, K, *DILATIONS, code))
     sy = torch.empty(sy_bytes, dtype=torch.uint8, device=device)
 
-    # as in the training step: one staging call (x and y), then dX and dY + dW read
-    # the staged operands; the staging is timed with dX
+    # as in the training step: one staging call (x and y) in the forward, timed with
+    # it; the forward, dX and dY + dW read the staged operands
     _lib.call("ddpm_gencat_stage", x.data_ptr(), y.data_ptr(), sy.data_ptr(), sy_bytes, n, C, H,
               W, K, *DILATIONS, code, sh)
 
-    def bwd_x():
+    def fwd():
         _lib.call("ddpm_gencat_stage", x.data_ptr(), y.data_ptr(), sy.data_ptr(), sy_bytes, n, C,
                   H, W, K, *DILATIONS, code, sh)
+        _lib.call("ddpm_gencat_fwd_staged", sy.data_ptr(), sy_bytes, packed.data_ptr(),
+                  gen_b.data_ptr(), out2.data_ptr(), n, C, H, W, K, *DILATIONS, code, sh)
+
+    def bwd_x():
         _lib.call("ddpm_gencat_bwd_x_staged", sy.data_ptr(), sy_bytes, packed.data_ptr(),
                   gen_b.data_ptr(), gout.data_ptr(), gx.data_ptr(), n, C, H, W, K, *DILATIONS,
                   code, sh)
@@ -396,12 +400,7 @@ def library_kernels(model, x, y, dtype, device):
         ),
         "gencat_bwd_x": (bwd_x, "tensor", gen_flops),
         "gencat_bwd_yw": (bwd_yw, "tensor", 2 * gen_flops),
-        "gencat_fwd": (
-            lambda: _lib.call("ddpm_gencat_fwd", x.data_ptr(), y.data_ptr(), packed.data_ptr(),
-                              gen_b.data_ptr(), out2.data_ptr(), n, C, H, W, K, *DILATIONS,
-                              code, sh),
-            "tensor", 2 * (3 * C * K * K) * C * n * H * W,
-        ),
+        "gencat_fwd": (fwd, "tensor", 2 * (3 * C * K * K) * C * n * H * W),
         "dyncat_fwd": (
             lambda: _lib.call("ddpm_dyncat_fwd", x.data_ptr(), code, taps.data_ptr(), code,
                               out.data_ptr(), n, C, H, W, K, *DILATIONS, sh),

@@ -169,13 +169,28 @@ def pack_generator_weight(weight: torch.Tensor, bias: torch.Tensor, channels: in
     return packed
 
 
-def _launch_gencat_fwd(x, y, packed, bias, kernel_size, dilations):
+def _stage_operands(x, y, kernel_size, dilations):
+    """x and y staged once as the tensor-core operand copies the fused kernels
+    read by TMA (``ddpm_gencat_stage``); valid while x and y are unchanged."""
+    n, c, h, w = x.shape
+    d0, d1, d2 = _dil(dilations)
+    code = _lib.dtype_code(x.dtype)
+    nb = int(_lib.load().ddpm_gencat_stage_bytes(n, c, h, w, int(kernel_size), d0, d1, d2, code))
+    staged = torch.empty(nb, dtype=torch.uint8, device=x.device)
+    _lib.call("ddpm_gencat_stage", x.data_ptr(), y.data_ptr(), staged.data_ptr(), nb,
+              n, c, h, w, int(kernel_size), d0, d1, d2, code, _lib.stream_handle(x.device))
+    return staged
+
+
+def _launch_gencat_fwd(x, y, packed, bias, kernel_size, dilations, staged=None):
     n, c, h, w = x.shape
     out = torch.empty((n, 4 * c, h, w), dtype=x.dtype, device=x.device)
     d0, d1, d2 = _dil(dilations)
+    if staged is None:
+        staged = _stage_operands(x, y, kernel_size, dilations)
     _lib.call(
-        "ddpm_gencat_fwd",
-        x.data_ptr(), y.data_ptr(), packed.data_ptr(), bias.data_ptr(), out.data_ptr(),
+        "ddpm_gencat_fwd_staged",
+        staged.data_ptr(), staged.numel(), packed.data_ptr(), bias.data_ptr(), out.data_ptr(),
         n, c, h, w, int(kernel_size), d0, d1, d2, _lib.dtype_code(x.dtype),
         _lib.stream_handle(x.device),
     )
@@ -209,9 +224,11 @@ class _GeneratorDynamicCat(torch.autograd.Function):
         x, y, bias = _prepare(x, y, weight, bias, kernel_size, dilations)
         with torch.cuda.device(x.device):
             packed = pack_generator_weight(weight, bias, x.shape[1], kernel_size, use_cache=False)
-            out = _launch_gencat_fwd(x, y, packed, bias, kernel_size, dilations)
+            staged = _stage_operands(x, y, kernel_size, dilations)
+            out = _launch_gencat_fwd(x, y, packed, bias, kernel_size, dilations, staged)
         ctx.save_for_backward(x, y, weight, bias)
         ctx.packed = packed
+        ctx.staged = staged  # reused by the backward (depends on x and y only)
         ctx.kernel_size = int(kernel_size)
         ctx.dilations = _dil(dilations)
         return out
@@ -234,16 +251,11 @@ class _GeneratorDynamicCat(torch.autograd.Function):
             grad_b = torch.empty(3 * c * ks * ks, dtype=x.dtype, device=x.device)
         with torch.cuda.device(x.device):
             stream = _lib.stream_handle(x.device)
-            # x and y staged once (channel-last operand copies): the backward
-            # kernels then stage their tiles with bulk / TMA copies
+            # the operands staged by the forward (x and y, channel-last operand
+            # copies): the backward kernels stage their tiles with bulk / TMA copies
             full = need_y and grad_w is not None
-            staged = None
-            sb = 0
-            if need_x or full:
-                sb = int(_lib.load().ddpm_gencat_stage_bytes(n, c, h, w, ks, d0, d1, d2, code))
-                staged = torch.empty(sb, dtype=torch.uint8, device=x.device)
-                _lib.call("ddpm_gencat_stage", x.data_ptr() if full else None, y.data_ptr(),
-                          staged.data_ptr(), sb, n, c, h, w, ks, d0, d1, d2, code, stream)
+            staged = ctx.staged
+            sb = staged.numel()
             if need_x:
                 _lib.call("ddpm_gencat_bwd_x_staged", staged.data_ptr(), sb, packed.data_ptr(),
                           bias.data_ptr(), grad_out.data_ptr(), grad_x.data_ptr(),

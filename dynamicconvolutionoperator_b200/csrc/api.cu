@@ -37,9 +37,9 @@ int umma_selftest(int variant, const void* a, const void* b, float* d, int n, in
 size_t gencat_pack_bytes(int c, int ks, int dt);
 int gencat_pack(const void* w, const void* bias, int c, int ks, int dt, void* packed,
                 size_t packed_bytes, cudaStream_t st);
-int gencat_fwd(const void* x, const void* y, const void* wpack, const void* bias, void* out,
-               int n, int c, int h, int w, int ks, int d0, int d1, int d2, int dt,
-               cudaStream_t st);
+int gencat_fwd(const void* x, const void* y, const void* staged, size_t staged_bytes,
+               const void* wpack, const void* bias, void* out, int n, int c, int h, int w,
+               int ks, int d0, int d1, int d2, int dt, cudaStream_t st);
 
 int gencat_bwd_x(const void* y, const void* staged, size_t staged_bytes, const void* wpack,
                  const void* bias, const void* gout, void* gx, int n, int c, int h, int w, int ks,
@@ -120,8 +120,17 @@ int ddpm_gencat_fwd(const void* x, const void* y, const void* packed, const void
                     int n, int c, int h, int w, int ksize, int d0, int d1, int d2, int dtype,
                     void* stream) {
   ddpm::clear_error();
-  return ddpm::gencat_fwd(x, y, packed, bias, out, n, c, h, w, ksize, d0, d1, d2, dtype,
-                          static_cast<cudaStream_t>(stream));
+  return ddpm::gencat_fwd(x, y, nullptr, 0, packed, bias, out, n, c, h, w, ksize, d0, d1, d2,
+                          dtype, static_cast<cudaStream_t>(stream));
+}
+
+int ddpm_gencat_fwd_staged(const void* staged, size_t staged_bytes, const void* packed,
+                           const void* bias, void* out, int n, int c, int h, int w, int ksize,
+                           int d0, int d1, int d2, int dtype, void* stream) {
+  ddpm::clear_error();
+  DDPM_CHECK_ARG(staged != nullptr, "null staged");
+  return ddpm::gencat_fwd(nullptr, nullptr, staged, staged_bytes, packed, bias, out, n, c, h, w,
+                          ksize, d0, d1, d2, dtype, static_cast<cudaStream_t>(stream));
 }
 
 int ddpm_gencat_bwd_x(const void* y, const void* packed, const void* bias, const void* grad_out,

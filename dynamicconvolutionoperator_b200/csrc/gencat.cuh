@@ -6,6 +6,7 @@
 
 #include "common.cuh"
 #include "tc.cuh"
+#include "tmap.cuh"
 
 namespace ddpm {
 namespace gencat {
@@ -615,6 +616,13 @@ size_t stage_bytes(int n, int c, int h, int w, int ks, int d0, int d1, int d2, i
 // x may be null: only the y plane is written (enough for dX).
 int stage(const void* x, const void* y, void* staged, size_t staged_bytes, int n, int c, int h,
           int w, int ks, int d0, int d1, int d2, int dt, cudaStream_t st);
+// TMA descriptors of the staged planes for 8 x 16 pixel tiles (64-bit element
+// views): x halo box {32 px, 8 + 2R rows, 4 channel quads}, coordinates
+// ((w0 - 8) * 2, h0 - R, 4 * cg, n); y tile box {16 px, 8 rows, ygroups
+// channel groups}, coordinates ((w0 + 8) * 2, h0 + ph, 0, part * N + n).
+// False when the driver rejects one (callers then stage from x and y).
+bool encode_stage_maps(CUtensorMap* xmap, CUtensorMap* ymap, int R, int ygroups,
+                       const uint8_t* staged, const StageLayout& sl);
 
 }  // namespace gencat
 }  // namespace ddpm

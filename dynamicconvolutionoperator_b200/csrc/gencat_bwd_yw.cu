@@ -1229,29 +1229,6 @@ int launch_dyw(const DywParams& prm, const DywMaps& maps, bool staged, cudaStrea
                 : launch_dyw_k<T, KS, false>(prm, maps, st);
 }
 
-// Tensor maps of the staged x and y planes for the merged kernel; false when
-// the driver rejects one (the caller then stages from x and y).
-bool encode_stage_maps(DywMaps& dp, int R, const uint8_t* staged, const gencat::StageLayout& sl) {
-  const uint64_t xd[4] = {(uint64_t)sl.W * 2, (uint64_t)sl.H, (uint64_t)sl.Cq, (uint64_t)sl.N};
-  const uint64_t xs[3] = {(uint64_t)sl.W * 16, (uint64_t)sl.H * sl.W * 16,
-                          (uint64_t)sl.Cq * sl.H * sl.W * 16};
-  const uint32_t xb[4] = {2 * gencat::kHaloCols, (uint32_t)(gencat::kTileH + 2 * R), 4, 1};
-  const uint64_t yd[4] = {(uint64_t)sl.Wp * 2, (uint64_t)sl.Hp, (uint64_t)sl.G,
-                          (uint64_t)sl.parts * sl.N};
-  const uint64_t ys[3] = {(uint64_t)sl.Wp * 16, (uint64_t)sl.Hp * sl.Wp * 16,
-                          (uint64_t)sl.G * sl.Hp * sl.Wp * 16};
-  const uint32_t yb[4] = {2 * gencat::kTileW, (uint32_t)gencat::kTileH, (uint32_t)sl.G, 1};
-  if (encode_tmap(&dp.xmap, CU_TENSOR_MAP_DATA_TYPE_UINT64, 4, staged + sl.x_offset, xd, xs, xb,
-                  CU_TENSOR_MAP_SWIZZLE_NONE) != DDPM_OK ||
-      encode_tmap(&dp.ymap, CU_TENSOR_MAP_DATA_TYPE_UINT64, 4, staged, yd, ys, yb,
-                  CU_TENSOR_MAP_SWIZZLE_NONE) != DDPM_OK) {
-    clear_error();
-    return false;
-  }
-  dp.ph = sl.ph;
-  return true;
-}
-
 template <typename T>
 int finish_dyw(const DywParams& prm, void* gy, void* gw, void* gb, int c, int ks, int ngroups,
                cudaStream_t st) {
@@ -1338,10 +1315,12 @@ int gencat_bwd_yw(const void* x, const void* y, const void* staged, size_t stage
       dp.status = status;
       bool use_staged = false;
       DywMaps maps{};
-      if (staged != nullptr)
-        use_staged = encode_stage_maps(
-            maps, R, static_cast<const uint8_t*>(staged),
-            gencat::StageLayout::make(n, c, h, w, ks, d0, d1, d2, dt));
+      if (staged != nullptr) {
+        const gencat::StageLayout sl = gencat::StageLayout::make(n, c, h, w, ks, d0, d1, d2, dt);
+        use_staged = gencat::encode_stage_maps(&maps.xmap, &maps.ymap, R, sl.G,
+                                               static_cast<const uint8_t*>(staged), sl);
+        maps.ph = sl.ph;
+      }
       DDPM_CHECK_ARG(use_staged || (x && y), "tensor maps unavailable: x and y are needed");
       DDPM_CUDA_TRY(cudaMemsetAsync(dp.gy_acc, 0, (size_t)n * c * h * w * sizeof(float), st));
       switch (dt * 10 + ks) {

@@ -50,7 +50,10 @@
 // TMEM buffers. Each producer thread issues all of its loads for a tile before
 // its first shared-memory store, so a tile costs one memory latency, not
 // several; each epilogue thread issues the three TMEM loads of a chunk before
-// a single wait.
+// a single wait. With staged operands (gencat_stage.cu) one thread per
+// producer role issues one TMA copy per tile instead: the y tile from the y
+// plane (then a K-major A operand, [channel group][pixel][8 channels]) and the
+// x halo from the FP32 cell plane, both zero filled outside the image.
 #include "common.cuh"
 #include "tc.cuh"
 #include "gencat.cuh"
@@ -60,7 +63,7 @@ namespace {
 
 using namespace gencat;
 
-template <typename T, int KS>
+template <typename T, int KS, bool kStaged = false>
 struct FwdCfg {
   static constexpr bool kSplit = IoTraits<T>::kSplit;
   static constexpr int kParts = kSplit ? 2 : 1;
@@ -122,10 +125,16 @@ struct FwdParams {
   int* status;
 };
 
-template <typename T, int KS>
-__global__ void __launch_bounds__(FwdCfg<T, KS>::kThreads, 1)
-gencat_fwd_kernel(const FwdParams p) {
-  using Cfg = FwdCfg<T, KS>;
+// Tensor maps of the staged operands (separate grid-constant parameter).
+struct FwdMaps {
+  CUtensorMap xmap, ymap;  // see gencat::encode_stage_maps
+  int ph;
+};
+
+template <typename T, int KS, bool kStaged>
+__global__ void __launch_bounds__(FwdCfg<T, KS, kStaged>::kThreads, 1)
+gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
+  using Cfg = FwdCfg<T, KS, kStaged>;
   using Op = typename IoTraits<T>::Op;
   constexpr int kN = Cfg::kN;
   constexpr int NB = Cfg::kNumBuf;
@@ -205,9 +214,11 @@ gencat_fwd_kernel(const FwdParams p) {
   } else if (warp == 1) {
     // ---- MMA issuer --------------------------------------------------------
     if (lane == 0) {
-      const uint32_t idesc = tc::idesc_f16(kTileM, kN, IoTraits<T>::kBf16, true, false);
+      // y tile: MN-major [pixel group][channel][8 px] (staged from y) or K-major
+      // [channel group][pixel][8 channels] (copied from the y plane)
+      const uint32_t idesc = tc::idesc_f16(kTileM, kN, IoTraits<T>::kBf16, !kStaged, false);
       const uint32_t b_lbo = Cfg::kRows * 16;   // 8-channel groups of the weight image
-      const uint64_t a_step = 256 >> 4;         // descriptor advance per K step
+      const uint64_t a_step = kStaged ? (uint64_t)(2 * kTileM * 16 >> 4) : (uint64_t)(256 >> 4);
       const uint64_t b_step = (2 * b_lbo) >> 4;
       const uint64_t a_lo = (kTileM * Ck * 2) >> 4;        // hi -> lo part of the y tile
       const uint64_t b_lo = (Cfg::kRows * Ck * 2) >> 4;    // hi -> lo part of the weights
@@ -226,7 +237,8 @@ gencat_fwd_kernel(const FwdParams p) {
         }
         tc::tc_fence_after();
         const uint64_t y_desc =
-            tc::smem_desc(tc::smem_u32(smem + L.y + yb * L.y_bytes), 128, Ck * 16);
+            kStaged ? tc::smem_desc(tc::smem_u32(smem + L.y + yb * L.y_bytes), kTileM * 16, 128)
+                    : tc::smem_desc(tc::smem_u32(smem + L.y + yb * L.y_bytes), 128, Ck * 16);
         for (int q = 0; q < Cfg::kSlots; ++q, ++tq) {
           // slot tq belongs to epilogue warpgroup tq % 2 (its (tq / 2)-th slot)
           const uint32_t own = tq >> 1;
@@ -274,13 +286,26 @@ gencat_fwd_kernel(const FwdParams p) {
       int n, h0, w0;
       tile_origin(tile, p.tiles_w, p.tiles_h, n, h0, w0);
       uint8_t* ys = smem + L.y + yb * L.y_bytes;
-      // 16 eight-pixel groups x Ck channels; one 16-byte smem row each.
-      // MN-major interleaved: group g at g*Ck*16, channel c at (c/8)*128 + (c%8)*16.
-      stage_y_mn<T, Op, Cfg::kSplit, Cfg::kYItems>(plan, static_cast<const T*>(p.y), ys,
-                                                   ys + kTileM * Ck * 2, n, C, Ck,
-                                                   Cfg::kBiasInGemm ? C : -1, H, W, h0, w0);
-      tc::fence_proxy_async_smem();
-      tc::mbar_arrive(&y_full[yb]);
+      if constexpr (kStaged) {
+        // y plane rows h0+ph .. +7, columns w0+8 .. w0+23, channel groups 0 .. Ck/8-1
+        if (pt == 0) {
+          tc::mbar_arrive_expect_tx(&y_full[yb], L.y_bytes);
+          tc::tma_load_4d(ys, &maps.ymap, (w0 + 8) * 2, h0 + maps.ph, 0, n, &y_full[yb]);
+          if constexpr (Cfg::kSplit)
+            tc::tma_load_4d(ys + kTileM * Ck * 2, &maps.ymap, (w0 + 8) * 2, h0 + maps.ph, 0,
+                            p.N + n, &y_full[yb]);
+        } else {
+          tc::mbar_arrive(&y_full[yb]);
+        }
+      } else {
+        // 16 eight-pixel groups x Ck channels; one 16-byte smem row each.
+        // MN-major interleaved: group g at g*Ck*16, channel c at (c/8)*128 + (c%8)*16.
+        stage_y_mn<T, Op, Cfg::kSplit, Cfg::kYItems>(plan, static_cast<const T*>(p.y), ys,
+                                                     ys + kTileM * Ck * 2, n, C, Ck,
+                                                     Cfg::kBiasInGemm ? C : -1, H, W, h0, w0);
+        tc::fence_proxy_async_smem();
+        tc::mbar_arrive(&y_full[yb]);
+      }
     }
   } else if (warp < Cfg::kFirstEpiWarp) {
     // ---- x-halo producers ----------------------------------------------------
@@ -296,9 +321,18 @@ gencat_fwd_kernel(const FwdParams p) {
       int n, h0, w0;
       tile_origin(tile, p.tiles_w, p.tiles_h, n, h0, w0);
       float4* xr = reinterpret_cast<float4*>(smem + L.xr + xb * L.xr_bytes);
-      stage_halo<T, Cfg::kXItems>(plan, static_cast<const T*>(p.x), xr, n, C, H, W, cg * 16,
-                                  h0 - R, w0 - 8, xr_rows);
-      tc::mbar_arrive(&x_full[xb]);
+      if constexpr (kStaged) {
+        if (pt == 0) {
+          tc::mbar_arrive_expect_tx(&x_full[xb], L.xr_bytes);
+          tc::tma_load_4d(xr, &maps.xmap, (w0 - 8) * 2, h0 - R, cg * 4, n, &x_full[xb]);
+        } else {
+          tc::mbar_arrive(&x_full[xb]);
+        }
+      } else {
+        stage_halo<T, Cfg::kXItems>(plan, static_cast<const T*>(p.x), xr, n, C, H, W, cg * 16,
+                                    h0 - R, w0 - 8, xr_rows);
+        tc::mbar_arrive(&x_full[xb]);
+      }
     }
   } else {
     // ---- epilogue warpgroups -----------------------------------------------
@@ -415,38 +449,45 @@ done:
   }
 }
 
-template <typename T, int KS>
-int launch(const FwdParams& prm, cudaStream_t st) {
-  using Cfg = FwdCfg<T, KS>;
+template <typename T, int KS, bool kStaged>
+int launch_k(const FwdParams& prm, const FwdMaps& maps, cudaStream_t st) {
+  using Cfg = FwdCfg<T, KS, kStaged>;
   const FwdSmem L = fwd_smem_layout<T, KS>(prm.Ck, prm.R);
-  auto fn = gencat_fwd_kernel<T, KS>;
+  auto fn = gencat_fwd_kernel<T, KS, kStaged>;
   DDPM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total));
   FwdParams q = prm;
   const int per_cg = num_sms() / q.ncg;
   q.per_cg = q.num_tiles < per_cg ? q.num_tiles : per_cg;
   const int grid = q.ncg * q.per_cg;
-  fn<<<grid, Cfg::kThreads, L.total, st>>>(q);
+  fn<<<grid, Cfg::kThreads, L.total, st>>>(q, maps);
   DDPM_CHECK_LAUNCH("gencat_fwd_kernel");
   return DDPM_OK;
 }
 
+template <typename T, int KS>
+int launch(const FwdParams& prm, const FwdMaps& maps, bool staged, cudaStream_t st) {
+  return staged ? launch_k<T, KS, true>(prm, maps, st) : launch_k<T, KS, false>(prm, maps, st);
+}
+
 template <typename T>
-int dispatch(int ks, const FwdParams& prm, cudaStream_t st) {
+int dispatch(int ks, const FwdParams& prm, const FwdMaps& maps, bool staged, cudaStream_t st) {
   switch (ks) {
-    case 1: return launch<T, 1>(prm, st);
-    case 3: return launch<T, 3>(prm, st);
+    case 1: return launch<T, 1>(prm, maps, staged, st);
+    case 3: return launch<T, 3>(prm, maps, staged, st);
   }
   return set_error(DDPM_ERR_UNSUPPORTED, "fused generator: kernel_size %d not supported", ks);
 }
 
 }  // namespace
 
-int gencat_fwd(const void* x, const void* y, const void* wpack, const void* bias, void* out,
-               int n, int c, int h, int w, int ks, int d0, int d1, int d2, int dt,
-               cudaStream_t st) {
+// `staged`: staged operands (gencat::stage with x and y) or null to stage
+// tiles from x and y.
+int gencat_fwd(const void* x, const void* y, const void* staged, size_t staged_bytes,
+               const void* wpack, const void* bias, void* out, int n, int c, int h, int w,
+               int ks, int d0, int d1, int d2, int dt, cudaStream_t st) {
   int rc = gencat::check_shape(n, c, h, w, ks, d0, d1, d2, dt);
   if (rc) return rc;
-  DDPM_CHECK_ARG(x && y && wpack && bias && out, "null pointer");
+  DDPM_CHECK_ARG(((x && y) || staged) && wpack && bias && out, "null pointer");
   FwdParams prm{};
   prm.x = x;
   prm.y = y;
@@ -470,10 +511,24 @@ int gencat_fwd(const void* x, const void* y, const void* wpack, const void* bias
   prm.num_tiles = n * prm.tiles_w * prm.tiles_h;
   rc = gencat::status_ptr(&prm.status);
   if (rc) return rc;
+  FwdMaps maps{};
+  bool use_staged = false;
+  if (staged != nullptr) {
+    const gencat::StageLayout sl = gencat::StageLayout::make(n, c, h, w, ks, d0, d1, d2, dt);
+    if (staged_bytes < sl.total_bytes())
+      return set_error(DDPM_ERR_WORKSPACE, "staged operands too small (%zu < %zu)", staged_bytes,
+                       sl.total_bytes());
+    DDPM_CHECK_ARG((reinterpret_cast<uintptr_t>(staged) & 255u) == 0,
+                   "staged operands must be 256-byte aligned");
+    use_staged = gencat::encode_stage_maps(&maps.xmap, &maps.ymap, prm.R, pl.Ck / 8,
+                                           static_cast<const uint8_t*>(staged), sl);
+    maps.ph = sl.ph;
+  }
+  DDPM_CHECK_ARG(use_staged || (x && y), "tensor maps unavailable: x and y are needed");
   switch (dt) {
-    case DDPM_BF16: return dispatch<__nv_bfloat16>(ks, prm, st);
-    case DDPM_F16: return dispatch<__half>(ks, prm, st);
-    case DDPM_F32: return dispatch<float>(ks, prm, st);
+    case DDPM_BF16: return dispatch<__nv_bfloat16>(ks, prm, maps, use_staged, st);
+    case DDPM_F16: return dispatch<__half>(ks, prm, maps, use_staged, st);
+    case DDPM_F32: return dispatch<float>(ks, prm, maps, use_staged, st);
   }
   return set_error(DDPM_ERR_INVALID_ARG, "unknown dtype %d", dt);
 }

@@ -131,6 +131,18 @@ DDPM_API int ddpm_gencat_fwd(const void* x, const void* y, const void* packed,
                              void* stream);
 
 /*
+ * ddpm_gencat_fwd reading x and y from the staged operands (ddpm_gencat_stage
+ * with x and y, same sizes and dtype): tiles arrive by TMA copies. Same
+ * result; replaces the same reference kernel (`_triton_kernels.py:268-420`).
+ * The staged buffer can then be reused by the backward of the same x and y.
+ */
+DDPM_API int ddpm_gencat_fwd_staged(const void* staged, size_t staged_bytes,
+                                    const void* packed, const void* bias, void* out,
+                                    int n, int c, int h, int w,
+                                    int ksize, int d0, int d1, int d2, int dtype,
+                                    void* stream);
+
+/*
  * Fused generator backward: input gradient dX, recomputing the taps.
  * Replaces `_generator_dynamic_cat_bwd_x` (reference `_triton_kernels.py:430-531`):
  *   grad_x[c,q] = grad_out[c,q]

@@ -52,6 +52,28 @@ def test_gencat_forward(shape, ks, dtype):
     torch.testing.assert_close(out.float().cpu(), gold.float(), rtol=rtol, atol=atol)
 
 
+@pytest.mark.parametrize("shape", [(2, 24, 15, 17), (1, 64, 48, 48), (3, 40, 33, 30)])
+@pytest.mark.parametrize("ks", [1, 3])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_gencat_forward_unstaged_abi(shape, ks, dtype):
+    """ddpm_gencat_fwd staging tiles from x and y itself (the public module
+    path stages the operands once and calls ddpm_gencat_fwd_staged)."""
+    from dynamicconvolutionoperator_b200 import _kernels, _lib
+
+    x, y, wt, b = _case(shape, ks, dtype)
+    n, c, h, w = shape
+    xd, yd, wd, bd = x.cuda(), y.cuda(), wt.cuda(), b.cuda()
+    packed = _kernels.pack_generator_weight(wd, bd, c, ks, use_cache=False)
+    out = torch.full((n, 4 * c, h, w), float("nan"), dtype=dtype, device="cuda")
+    _lib.call("ddpm_gencat_fwd", xd.data_ptr(), yd.data_ptr(), packed.data_ptr(), bd.data_ptr(),
+              out.data_ptr(), n, c, h, w, ks, 1, 3, 5, _lib.dtype_code(dtype),
+              _lib.stream_handle(out.device))
+    torch.cuda.synchronize()
+    gold = orc.fused_generator_cat(x, y, wt, b, ks, quantize=True)
+    rtol, atol = TOL[dtype]
+    torch.testing.assert_close(out.float().cpu(), gold.float(), rtol=rtol, atol=atol)
+
+
 def test_gencat_custom_dilations_and_repeat_calls():
     """Custom dilations; repeated calls reuse the cached packed weight and an
     in-place weight update invalidates it."""
