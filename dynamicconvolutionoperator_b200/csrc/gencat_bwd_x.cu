@@ -50,7 +50,9 @@ template <typename T, int KS, bool kStaged = false>
 struct BxCfg {
   static constexpr bool kSplit = IoTraits<T>::kSplit;
   static constexpr int kParts = kSplit ? 2 : 1;
-  static constexpr int kUnitBufs = 2;                 // staged units in flight
+  // units in flight (16-bit staged: a third unit buffer fits and keeps one
+  // more unit's copies outstanding)
+  static constexpr int kUnitBufs = (kStaged && !kSplit) ? 3 : 2;
   static constexpr int kWStages = kSplit ? 4 : 6;
   static constexpr bool kBiasInGemm = !kSplit;
   static constexpr int kIssuers = 2;        // MMA issuer warps (alternate chunks)
@@ -66,10 +68,11 @@ struct BxSmem {
 };
 
 // One unit buffer = the y row segment (both parts) + the gradient row segment.
-// C=64: fp32 2x36 + 2x36 + 4x16 + 7 KB = 215 KB; bf16 2x23 + 2x18 + 6x10 KB = 143 KB.
-template <typename T, int KS>
+// C=64: fp32 2x36 + 2x36 + 4x16 + 7 KB = 215 KB; bf16 2x23 + 2x18 + 6x10 KB = 143 KB
+// (3 unit buffers when staged: 184 KB).
+template <typename T, int KS, bool kStaged>
 __host__ __device__ inline BxSmem bx_smem_layout(int Cp, int Ck, int C) {
-  using Cfg = BxCfg<T, KS>;
+  using Cfg = BxCfg<T, KS, kStaged>;
   BxSmem L;
   L.reg_part = (uint32_t)Ck * kSeg * 2;
   L.reg_bytes = Cfg::kParts * L.reg_part;
@@ -152,7 +155,7 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
 
   const int C = p.C, Cp = p.Cp, Ck = p.Ck, H = p.H, W = p.W;
   const size_t P = (size_t)H * W;
-  const BxSmem L = bx_smem_layout<T, KS>(Cp, Ck, C);
+  const BxSmem L = bx_smem_layout<T, KS, kStaged>(Cp, Ck, C);
   const int NB = 512 / Cp > 8 ? 8 : 512 / Cp;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint64_t* u_full = bars;              // [NU] producers (128 arrivals) + gradient bytes
@@ -512,7 +515,7 @@ done:
 template <typename T, int KS, bool kStaged>
 int launch_k(const BxParams& prm, cudaStream_t st) {
   using Cfg = BxCfg<T, KS, kStaged>;
-  const BxSmem L = bx_smem_layout<T, KS>(prm.Cp, prm.Ck, prm.C);
+  const BxSmem L = bx_smem_layout<T, KS, kStaged>(prm.Cp, prm.Ck, prm.C);
   auto fn = gencat_bwd_x_kernel<T, KS, kStaged>;
   DDPM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total));
   const int grid = prm.num_tiles < num_sms() ? prm.num_tiles : num_sms();

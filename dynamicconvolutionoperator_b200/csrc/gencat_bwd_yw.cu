@@ -705,8 +705,10 @@ __global__ void gencat_wreduce_kernel(const float* __restrict__ partial, T* __re
 // 384 / 448) holds the cg's share of dY and is added into an FP32 dY
 // accumulator with reductions to global memory (the other channel groups'
 // CTAs add theirs); the x-halo producer warps do that drain for the previous
-// tile while the builders work on the next. Builders run two threads per
-// pixel (four slots each); one issuer warp per GEMM. With staged operands
+// tile while the builders work on the next (with staged operands the
+// y-tile producer warps do it, so that the x-halo copies never wait behind a
+// drain). Builders run two threads per pixel (four slots each); one issuer
+// warp per GEMM. With staged operands
 // (gencat_stage.cu) one thread per producer group issues one TMA copy per tile
 // instead: the x halo from the FP32 cell plane (box 32 px x halo rows x 4
 // channel quads, zero filled outside the image) and the y tile from the y
@@ -773,6 +775,37 @@ struct DywMaps {
   CUtensorMap ymap;  // staged y plane (64-bit view) {Wp*2, Hp, G, parts*N}, box {32, 8, G, 1}
   int ph;            // y-plane row offset
 };
+
+// D_y of the it-th tile of a split (64 columns at `dy_col`, double buffered)
+// into the FP32 dY accumulator: the calling warp reads TMEM lane quadrant
+// `quad`, thread = pixel m of the tile. False when the bounded wait gives up.
+__device__ __forceinline__ bool drain_dy(const DywParams& p, uint32_t it, int split, int quad,
+                                         int lane, uint32_t tmem_base, uint32_t dy_col,
+                                         uint64_t* d_full, uint64_t* d_empty,
+                                         volatile int* abort_flag) {
+  const int tb = it & 1;
+  if (!warp_wait(&d_full[tb], (it >> 1) & 1, abort_flag)) return false;
+  tc::tc_fence_after();
+  float dv[4][16];
+  const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + dy_col + tb * 64;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) tc::tmem_ld16(taddr + q * 16, dv[q]);
+  tc::tmem_ld_wait();
+  tc::tc_fence_before();
+  tc::mbar_arrive(&d_empty[tb]);
+  int n, h0, w0;
+  tile_origin(split + (int)it * p.splits, p.tiles_w, p.tiles_h, n, h0, w0);
+  const int m = quad * 32 + lane;
+  const int h = h0 + (m >> 4), w = w0 + (m & 15);
+  if (h < p.H && w < p.W) {
+    const size_t P = (size_t)p.H * p.W;
+    float* acc = p.gy_acc + (size_t)n * p.C * P + (size_t)h * p.W + w;
+#pragma unroll
+    for (int k = 0; k < 64; ++k)
+      if (k < p.C) atomicAdd(acc + (size_t)k * P, dv[k >> 4][k & 15]);
+  }
+  return true;
+}
 
 template <typename T, int KS, bool kStaged>
 __global__ void __launch_bounds__(DywCfg<T, KS, kStaged>::kThreads, 1)
@@ -957,34 +990,14 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
       tc::mma_commit(w_done);
     }
   } else if (warp < Cfg::kFirstYWarp) {
-    // ---- x-halo producers (the cg's 16 channels, once per tile), who also
-    //      drain the previous tile's D_y into the FP32 dY accumulator -----------
+    // ---- x-halo producers (the cg's 16 channels, once per tile); without
+    //      staged operands they also drain the previous tile's D_y ------------
     const int pt = threadIdx.x - 32 * Cfg::kFirstXWarp;
     const int quad = warp & 3;               // TMEM lane quadrant
-    const int m = quad * 32 + lane;          // pixel of the drained tile
     const XPlan<Cfg::kXItems> plan = make_xplan<Cfg::kXItems>(xr_rows, pt, Cfg::kProducers);
-    // D_y of the it-th tile of this split: 64 columns of this thread's pixel
     auto drain = [&](uint32_t it) -> bool {
-      const int tb = it & 1;
-      if (!warp_wait(&d_full[tb], (it >> 1) & 1, abort_flag)) return false;
-      tc::tc_fence_after();
-      float dv[4][16];
-      const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + Cfg::kDyCol + tb * 64;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) tc::tmem_ld16(taddr + q * 16, dv[q]);
-      tc::tmem_ld_wait();
-      tc::tc_fence_before();
-      tc::mbar_arrive(&d_empty[tb]);
-      int n, h0, w0;
-      tile_origin(split + (int)it * p.splits, p.tiles_w, p.tiles_h, n, h0, w0);
-      const int h = h0 + (m >> 4), w = w0 + (m & 15);
-      if (h < H && w < W) {
-        float* acc = p.gy_acc + (size_t)n * C * P + (size_t)h * W + w;
-#pragma unroll
-        for (int k = 0; k < 64; ++k)
-          if (k < C) atomicAdd(acc + (size_t)k * P, dv[k >> 4][k & 15]);
-      }
-      return true;
+      return drain_dy(p, it, split, quad, lane, tmem_base, Cfg::kDyCol, d_full, d_empty,
+                      abort_flag);
     };
     uint32_t xq = 0;
     bool failed = false;
@@ -1011,22 +1024,25 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
                                     h0 - R, w0 - 8, xr_rows);
         tc::mbar_arrive(&x_full[xb]);
       }
-      if (xq > 0 && !drain(xq - 1)) {
+      if (!kStaged && xq > 0 && !drain(xq - 1)) {
         fail(abort_flag, p.status, 59);
         failed = true;
         break;
       }
     }
-    if (!failed && xq > 0 && !drain(xq - 1)) fail(abort_flag, p.status, 59);
+    if (!kStaged && !failed && xq > 0 && !drain(xq - 1)) fail(abort_flag, p.status, 59);
   } else if (warp < Cfg::kFirstBuilderWarp) {
     // ---- y-tile producers (B operand of dW, ones channel at C for db) ---------
     const int pt = threadIdx.x - 32 * Cfg::kFirstYWarp;
     const YPlan<Cfg::kYItems> plan = make_yplan<Cfg::kYItems>(Nw, pt, Cfg::kProducers);
+    const int quad = warp & 3;  // TMEM lane quadrant (staged: these warps drain D_y)
     uint32_t it = 0;
+    bool failed = false;
     for (int tile = split; tile < p.num_tiles && !*abort_flag; tile += p.splits, ++it) {
       const int yb = it % NY;
       if (!warp_wait(&y_empty[yb], ((it / NY) & 1) ^ 1, abort_flag)) {
         fail(abort_flag, p.status, 56);
+        failed = true;
         break;
       }
       int n, h0, w0;
@@ -1050,7 +1066,18 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
         tc::fence_proxy_async_smem();
         tc::mbar_arrive(&y_full[yb]);
       }
+      if (kStaged && it > 0 &&
+          !drain_dy(p, it - 1, split, quad, lane, tmem_base, Cfg::kDyCol, d_full, d_empty,
+                    abort_flag)) {
+        fail(abort_flag, p.status, 59);
+        failed = true;
+        break;
+      }
     }
+    if (kStaged && !failed && it > 0 &&
+        !drain_dy(p, it - 1, split, quad, lane, tmem_base, Cfg::kDyCol, d_full, d_empty,
+                  abort_flag))
+      fail(abort_flag, p.status, 59);
   } else {
     // ---- builders (two threads per pixel), D_y and D_w drains ------------------
     const int half = (warp - Cfg::kFirstBuilderWarp) >> 2;
