@@ -568,6 +568,8 @@ int check_shape(int n, int c, int h, int w, int ks, int d0, int d1, int d2, int 
 int status_ptr(int** out);
 int read_status(int reset, int* code);
 int num_sms();
+// Dynamic shared memory a block may opt in to on the current device (bytes).
+int max_smem_optin();
 
 // Staged operands of the fused backward (gencat_stage.cu), written once per
 // backward so the kernels stage tiles with bulk / TMA copies instead of

@@ -713,13 +713,18 @@ __global__ void gencat_wreduce_kernel(const float* __restrict__ partial, T* __re
 // instead: the x halo from the FP32 cell plane (box 32 px x halo rows x 4
 // channel quads, zero filled outside the image) and the y tile from the y
 // plane (box 16 px x 8 rows x all channel groups), which makes the dW GEMM's B
-// operand MN-major ([channel group][pixel][8 channels]).
-template <typename T, int KS, bool kStaged = false>
+// operand MN-major ([channel group][pixel][8 channels]). With kGTma (16-bit,
+// staged) the gradient values of the cg's 16 channels x 3 branches also come
+// by one TMA copy per tile, one tile ahead, into a single buffer the builders
+// release as soon as they hold the values in registers; otherwise each builder
+// loads its pixel's 48 values from global memory at the start of the tile.
+template <typename T, int KS, bool kStaged = false, bool kGTmaArg = false>
 struct DywCfg {
   static constexpr bool kSplit = IoTraits<T>::kSplit;
+  static constexpr bool kGTma = kGTmaArg;
   static constexpr int kParts = kSplit ? 2 : 1;
   static constexpr int kDkSlots = kSplit ? 1 : 2;
-  static constexpr int kXBufs = kSplit ? 1 : 2;
+  static constexpr int kXBufs = kSplit ? 1 : 2;  // at most; DywParams::nx is the count used
   static constexpr int kYBufs = kSplit ? 1 : 2;
   static constexpr int kWStages = 2;
   static constexpr int kProducers = 128;
@@ -732,25 +737,29 @@ struct DywCfg {
 };
 
 struct DywSmem {
-  uint32_t xr, y, dk, w, bars, total, xr_bytes, y_bytes, dk_bytes, w_bytes;
+  uint32_t xr, y, dk, w, g, bars, total, xr_bytes, y_bytes, dk_bytes, w_bytes, g_bytes;
 };
 
-// C=64, K=3: fp32 37 + 40 + 64 + 2x32 KB = 204 KB; bf16 2x37 + 2x20 + 2x32 + 2x16 KB = 208 KB.
-template <typename T, int KS>
-__host__ __device__ inline DywSmem dyw_smem_layout(int Cp, int Nw, int R) {
+// `nx` x-halo buffers (2, or 1 where two do not fit), then y, dK, weight ring
+// and (kGTma) the gradient tile [branch][channel][8 rows][16 px].
+// C=64, K=3, halo 5: fp32 36 + 40 + 64 + 2x32 KB = 204 KB;
+// bf16 2x36 + 2x20 + 2x32 + 2x16 (+ 12) KB = 208 (220) KB.
+template <typename T, int KS, bool kGTma = false>
+__host__ __device__ inline DywSmem dyw_smem_layout(int Cp, int Nw, int R, int nx) {
   using Cfg = DywCfg<T, KS>;
   DywSmem L;
   L.xr_bytes = (uint32_t)16 * (kTileH + 2 * R) * kHaloCols * 4;
   L.y_bytes = (uint32_t)Cfg::kParts * kTileM * Nw * 2;
   L.dk_bytes = (uint32_t)Cfg::kParts * kDkBytes;
   L.w_bytes = (uint32_t)Cfg::kParts * 128 * Cp * 2;
+  L.g_bytes = kGTma ? (uint32_t)(3 * 16 * kTileM * sizeof(T)) : 0u;
   L.xr = 0;
-  L.y = L.xr + Cfg::kXBufs * L.xr_bytes;
+  L.y = L.xr + nx * L.xr_bytes;
   L.dk = L.y + Cfg::kYBufs * L.y_bytes;
   L.w = L.dk + Cfg::kDkSlots * L.dk_bytes;
-  L.bars = L.w + Cfg::kWStages * L.w_bytes;
-  L.total = L.bars + 8 * (2 * Cfg::kXBufs + 2 * Cfg::kYBufs + 2 * Cfg::kDkSlots +
-                          2 * Cfg::kWStages + 5);
+  L.g = L.w + Cfg::kWStages * L.w_bytes;
+  L.bars = L.g + L.g_bytes;
+  L.total = L.bars + 8 * (4 + 2 * Cfg::kYBufs + 2 * Cfg::kDkSlots + 2 * Cfg::kWStages + 7);
   return L;
 }
 
@@ -765,6 +774,7 @@ struct DywParams {
   int d[3];
   int tiles_w, tiles_h, num_tiles;
   int ngroups, ncg, splits;
+  int nx;             // x-halo buffers (1 or 2)
   int* status;
 };
 
@@ -773,6 +783,7 @@ struct DywParams {
 struct DywMaps {
   CUtensorMap xmap;  // staged x plane (64-bit view) {W*2, H, Cq, N}, box {64, 8+2R, 4, 1}
   CUtensorMap ymap;  // staged y plane (64-bit view) {Wp*2, Hp, G, parts*N}, box {32, 8, G, 1}
+  CUtensorMap gmap;  // grad_out {W, H, C, 4, N}, box {16, 8, 16, 3, 1} (kGTma only)
   int ph;            // y-plane row offset
 };
 
@@ -807,13 +818,14 @@ __device__ __forceinline__ bool drain_dy(const DywParams& p, uint32_t it, int sp
   return true;
 }
 
-template <typename T, int KS, bool kStaged>
-__global__ void __launch_bounds__(DywCfg<T, KS, kStaged>::kThreads, 1)
+template <typename T, int KS, bool kStaged, bool kGTma>
+__global__ void __launch_bounds__(DywCfg<T, KS, kStaged, kGTma>::kThreads, 1)
 gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
-  using Cfg = DywCfg<T, KS, kStaged>;
+  using Cfg = DywCfg<T, KS, kStaged, kGTma>;
   using Op = typename IoTraits<T>::Op;
   constexpr int NS = Cfg::kDkSlots;
-  constexpr int NX = Cfg::kXBufs;
+  const int NX = Cfg::kXBufs == 1 ? 1 : p.nx;  // 1 or 2: index = xq & (NX-1), lap = xq >> (NX-1)
+  const int nx_sh = NX - 1;
   constexpr int NY = Cfg::kYBufs;
   constexpr int S = Cfg::kWStages;
   constexpr int NOCT = Cfg::kOct;
@@ -823,13 +835,13 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
 
   const int C = p.C, Cp = p.Cp, H = p.H, W = p.W, R = p.R, Nw = p.Nw;
   const size_t P = (size_t)H * W;
-  const DywSmem L = dyw_smem_layout<T, KS>(Cp, Nw, R);
+  const DywSmem L = dyw_smem_layout<T, KS, kGTma>(Cp, Nw, R, NX);
   const int cg = blockIdx.x % p.ncg;
   const int split = blockIdx.x / p.ncg;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
-  uint64_t* x_full = bars;             // [NX]
-  uint64_t* x_empty = x_full + NX;     // [NX]
-  uint64_t* y_full = x_empty + NX;     // [NY]
+  uint64_t* x_full = bars;             // [2] (NX used)
+  uint64_t* x_empty = x_full + 2;      // [2]
+  uint64_t* y_full = x_empty + 2;      // [NY]
   uint64_t* y_empty = y_full + NY;     // [NY]
   uint64_t* k_full = y_empty + NY;     // [NS]
   uint64_t* k_empty = k_full + NS;     // [NS]
@@ -838,6 +850,8 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
   uint64_t* d_full = w_empty + S;      // [2]
   uint64_t* d_empty = d_full + 2;      // [2]
   uint64_t* w_done = d_empty + 2;      // [1]
+  uint64_t* g_full = w_done + 1;       // [1] (kGTma)
+  uint64_t* g_empty = g_full + 1;      // [1] (kGTma)
   const int xr_rows = kTileH + 2 * R;
   const int xr_plane = xr_rows * kHaloCols;
   const int warp = threadIdx.x >> 5;
@@ -848,7 +862,7 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
     tc::tmem_relinquish();
   }
   if (threadIdx.x == 32) {
-    for (int i = 0; i < NX; ++i) {
+    for (int i = 0; i < 2; ++i) {
       tc::mbar_init(&x_full[i], Cfg::kProducers);
       tc::mbar_init(&x_empty[i], 256);
     }
@@ -869,6 +883,8 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
       tc::mbar_init(&d_empty[i], Cfg::kProducers);
     }
     tc::mbar_init(w_done, 1);
+    tc::mbar_init(g_full, 1);
+    tc::mbar_init(g_empty, 8);
     tc::fence_mbar_init();
     abort_s = 0;
   }
@@ -1002,8 +1018,8 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
     uint32_t xq = 0;
     bool failed = false;
     for (int tile = split; tile < p.num_tiles && !*abort_flag; tile += p.splits, ++xq) {
-      const int xb = xq % NX;
-      if (!warp_wait(&x_empty[xb], ((xq / NX) & 1) ^ 1, abort_flag)) {
+      const int xb = xq & nx_sh;
+      if (!warp_wait(&x_empty[xb], ((xq >> nx_sh) & 1) ^ 1, abort_flag)) {
         fail(abort_flag, p.status, 55);
         failed = true;
         break;
@@ -1018,6 +1034,25 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
           tc::tma_load_4d(xr, &maps.xmap, (w0 - 8) * 2, h0 - R, cg * 4, n, &x_full[xb]);
         } else {
           tc::mbar_arrive(&x_full[xb]);
+        }
+        if constexpr (kGTma) {
+          // gradient tile (branches 1..3, the cg's 16 channels) once the builders
+          // hold the previous one in registers; zero filled outside the image
+          if (warp == Cfg::kFirstXWarp + 1) {
+            bool ok = true;
+            if (lane == 0) {
+              ok = tc::mbar_wait(g_empty, (xq & 1) ^ 1, abort_flag, kWaitNs);
+              if (ok) {
+                tc::mbar_arrive_expect_tx(g_full, L.g_bytes);
+                tc::tma_load_5d(smem + L.g, &maps.gmap, w0, h0, cg * 16, 1, n, g_full);
+              }
+            }
+            if (!__all_sync(0xffffffffu, ok)) {
+              fail(abort_flag, p.status, 48);
+              failed = true;
+              break;
+            }
+          }
         }
       } else {
         stage_halo<T, Cfg::kXItems>(plan, static_cast<const T*>(p.x), xr, n, C, H, W, cg * 16,
@@ -1096,9 +1131,26 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
       const size_t pix = px_ok ? (size_t)h * W + w : 0;
       const T* gn = gout + (size_t)n * 4 * C * P;
       unsigned long long gv[3][8];
-      load_gv<T>(gv, gn, C, P, cg, pix, px_ok);
-      const int xb = xq % NX;
-      if (!warp_wait(&x_full[xb], (xq / NX) & 1, abort_flag)) {
+      if constexpr (kGTma) {
+        if (!warp_wait(g_full, xq & 1, abort_flag)) {
+          fail(abort_flag, p.status, 47);
+          failed = true;
+          break;
+        }
+        const T* gs = reinterpret_cast<const T*>(smem + L.g) + m;
+#pragma unroll
+        for (int b = 0; b < 3; ++b)
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            gv[b][i] = f2_pack(to_f32<T>(gs[(b * 16 + 2 * i) * kTileM]),
+                               to_f32<T>(gs[(b * 16 + 2 * i + 1) * kTileM]));
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(g_empty);
+      } else {
+        load_gv<T>(gv, gn, C, P, cg, pix, px_ok);
+      }
+      const int xb = xq & nx_sh;
+      if (!warp_wait(&x_full[xb], (xq >> nx_sh) & 1, abort_flag)) {
         fail(abort_flag, p.status, 57);
         failed = true;
         break;
@@ -1239,21 +1291,38 @@ DywPlan plan_dyw(int n, int c, int h, int w, int ks) {
   return q;
 }
 
-template <typename T, int KS, bool kStaged>
+template <typename T, int KS, bool kStaged, bool kGTma>
 int launch_dyw_k(const DywParams& prm, const DywMaps& maps, cudaStream_t st) {
-  using Cfg = DywCfg<T, KS, kStaged>;
-  const DywSmem L = dyw_smem_layout<T, KS>(prm.Cp, prm.Nw, prm.R);
-  auto fn = gencat_bwd_dyw_kernel<T, KS, kStaged>;
+  using Cfg = DywCfg<T, KS, kStaged, kGTma>;
+  const DywSmem L = dyw_smem_layout<T, KS, kGTma>(prm.Cp, prm.Nw, prm.R, prm.nx);
+  auto fn = gencat_bwd_dyw_kernel<T, KS, kStaged, kGTma>;
   DDPM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total));
   fn<<<prm.ncg * prm.splits, Cfg::kThreads, L.total, st>>>(prm, maps);
   DDPM_CHECK_LAUNCH("gencat_bwd_dyw_kernel");
   return DDPM_OK;
 }
 
+// Picks the variant and the x-buffer count: the gradient tile by TMA where the
+// caller could encode its map (16-bit, staged), two x buffers where they fit.
 template <typename T, int KS>
-int launch_dyw(const DywParams& prm, const DywMaps& maps, bool staged, cudaStream_t st) {
-  return staged ? launch_dyw_k<T, KS, true>(prm, maps, st)
-                : launch_dyw_k<T, KS, false>(prm, maps, st);
+int launch_dyw(DywParams prm, const DywMaps& maps, bool staged, bool g_tma, cudaStream_t st) {
+  const int lim = max_smem_optin();
+  constexpr int kMaxX = DywCfg<T, KS>::kXBufs;
+  if constexpr (!IoTraits<T>::kSplit) {
+    if (staged && g_tma)
+      for (int nx = kMaxX; nx >= 1; --nx)
+        if ((int)dyw_smem_layout<T, KS, true>(prm.Cp, prm.Nw, prm.R, nx).total <= lim) {
+          prm.nx = nx;
+          return launch_dyw_k<T, KS, true, true>(prm, maps, st);
+        }
+  }
+  for (int nx = kMaxX; nx >= 1; --nx)
+    if ((int)dyw_smem_layout<T, KS>(prm.Cp, prm.Nw, prm.R, nx).total <= lim) {
+      prm.nx = nx;
+      return staged ? launch_dyw_k<T, KS, true, false>(prm, maps, st)
+                    : launch_dyw_k<T, KS, false, false>(prm, maps, st);
+    }
+  return set_error(DDPM_ERR_UNSUPPORTED, "dY+dW tile does not fit in shared memory");
 }
 
 template <typename T>
@@ -1340,23 +1409,39 @@ int gencat_bwd_yw(const void* x, const void* y, const void* staged, size_t stage
       dp.ncg = q.ncg;
       dp.splits = q.splits;
       dp.status = status;
-      bool use_staged = false;
+      bool use_staged = false, g_tma = false;
       DywMaps maps{};
       if (staged != nullptr) {
         const gencat::StageLayout sl = gencat::StageLayout::make(n, c, h, w, ks, d0, d1, d2, dt);
         use_staged = gencat::encode_stage_maps(&maps.xmap, &maps.ymap, R, sl.G,
                                                static_cast<const uint8_t*>(staged), sl);
         maps.ph = sl.ph;
+        // gradient tiles by TMA (16-bit) when the row pitch and base allow a map
+        const size_t es = (size_t)dtype_size(dt);
+        if (use_staged && dt != DDPM_F32 && ((size_t)w * es) % 16 == 0 &&
+            (reinterpret_cast<uintptr_t>(gout) & 15u) == 0) {
+          const uint64_t gd[5] = {(uint64_t)w, (uint64_t)h, (uint64_t)c, 4, (uint64_t)n};
+          const uint64_t gs[4] = {w * es, (uint64_t)h * w * es, (uint64_t)c * h * w * es,
+                                  (uint64_t)4 * c * h * w * es};
+          const uint32_t gb_[5] = {(uint32_t)gencat::kTileW, (uint32_t)gencat::kTileH, 16, 3, 1};
+          const CUtensorMapDataType ty = dt == DDPM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                         : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+          if (encode_tmap(&maps.gmap, ty, 5, gout, gd, gs, gb_, CU_TENSOR_MAP_SWIZZLE_NONE) ==
+              DDPM_OK)
+            g_tma = true;
+          else
+            clear_error();
+        }
       }
       DDPM_CHECK_ARG(use_staged || (x && y), "tensor maps unavailable: x and y are needed");
       DDPM_CUDA_TRY(cudaMemsetAsync(dp.gy_acc, 0, (size_t)n * c * h * w * sizeof(float), st));
       switch (dt * 10 + ks) {
-        case DDPM_BF16 * 10 + 1: rc = launch_dyw<__nv_bfloat16, 1>(dp, maps, use_staged, st); break;
-        case DDPM_BF16 * 10 + 3: rc = launch_dyw<__nv_bfloat16, 3>(dp, maps, use_staged, st); break;
-        case DDPM_F16 * 10 + 1: rc = launch_dyw<__half, 1>(dp, maps, use_staged, st); break;
-        case DDPM_F16 * 10 + 3: rc = launch_dyw<__half, 3>(dp, maps, use_staged, st); break;
-        case DDPM_F32 * 10 + 1: rc = launch_dyw<float, 1>(dp, maps, use_staged, st); break;
-        case DDPM_F32 * 10 + 3: rc = launch_dyw<float, 3>(dp, maps, use_staged, st); break;
+        case DDPM_BF16 * 10 + 1: rc = launch_dyw<__nv_bfloat16, 1>(dp, maps, use_staged, g_tma, st); break;
+        case DDPM_BF16 * 10 + 3: rc = launch_dyw<__nv_bfloat16, 3>(dp, maps, use_staged, g_tma, st); break;
+        case DDPM_F16 * 10 + 1: rc = launch_dyw<__half, 1>(dp, maps, use_staged, g_tma, st); break;
+        case DDPM_F16 * 10 + 3: rc = launch_dyw<__half, 3>(dp, maps, use_staged, g_tma, st); break;
+        case DDPM_F32 * 10 + 1: rc = launch_dyw<float, 1>(dp, maps, use_staged, g_tma, st); break;
+        case DDPM_F32 * 10 + 3: rc = launch_dyw<float, 3>(dp, maps, use_staged, g_tma, st); break;
         default: rc = set_error(DDPM_ERR_UNSUPPORTED, "unsupported dtype/kernel size");
       }
       if (rc) return rc;

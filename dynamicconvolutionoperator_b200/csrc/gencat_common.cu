@@ -74,6 +74,22 @@ int num_sms() {
   return cache[dev];
 }
 
+int max_smem_optin() {
+  static std::mutex mu;
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 232448;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[dev] == 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
+        v <= 0)
+      v = 232448;
+    cache[dev] = v;
+  }
+  return cache[dev];
+}
+
 }  // namespace gencat
 
 namespace {

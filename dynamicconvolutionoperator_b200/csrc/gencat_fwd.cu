@@ -94,10 +94,11 @@ struct FwdSmem {
   uint32_t y_bytes, w_bytes, xr_bytes;
 };
 
-// Resident weights of one channel group + y tile(s) + two x-halo buffers.
-// C=64, K=3: bf16 69 + 2x20 + 2x36 KB = 181 KB; fp32 108 + 32 + 72 KB = 214 KB.
+// Resident weights of one channel group + y tile(s) + `nxb` (2, or 1 where two
+// do not fit: FP32 with halos >= 7) x-halo buffers.
+// C=64, K=3, halo 5: bf16 69 + 2x20 + 2x36 KB = 181 KB; fp32 108 + 32 + 72 KB = 214 KB.
 template <typename T, int KS>
-__host__ __device__ inline FwdSmem fwd_smem_layout(int Ck, int R) {
+__host__ __device__ inline FwdSmem fwd_smem_layout(int Ck, int R, int nxb) {
   using Cfg = FwdCfg<T, KS>;
   FwdSmem L;
   L.y_bytes = (uint32_t)Cfg::kParts * kTileM * Ck * 2;
@@ -106,7 +107,7 @@ __host__ __device__ inline FwdSmem fwd_smem_layout(int Ck, int R) {
   L.y = 0;
   L.w = L.y + Cfg::kYBufs * L.y_bytes;
   L.xr = L.w + L.w_bytes;
-  L.bias = L.xr + 2 * L.xr_bytes;
+  L.bias = L.xr + nxb * L.xr_bytes;
   L.bars = L.bias + (Cfg::kBiasInGemm ? 0u : (uint32_t)(3 * 16 * KS * KS * 4));
   L.total = L.bars + 8 * (9 + 2 * Cfg::kNumBuf);
   return L;
@@ -122,6 +123,7 @@ struct FwdParams {
   int d[3];
   int tiles_w, tiles_h, num_tiles;
   int ncg, per_cg;    // channel groups; CTAs per channel group
+  int nxb;            // x-halo buffers (1 or 2)
   int* status;
 };
 
@@ -147,7 +149,8 @@ gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
 
   const int C = p.C, Ck = p.Ck, H = p.H, W = p.W, R = p.R;
   const size_t P = (size_t)H * W;
-  const FwdSmem L = fwd_smem_layout<T, KS>(Ck, R);
+  const FwdSmem L = fwd_smem_layout<T, KS>(Ck, R, p.nxb);
+  const int nx_sh = p.nxb - 1;  // 1 or 2 buffers: index = it & nx_sh, lap = it >> nx_sh
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint64_t* y_full = bars;           // [2]
   uint64_t* y_empty = bars + 2;      // [2]
@@ -313,8 +316,8 @@ gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
     const XPlan<Cfg::kXItems> plan = make_xplan<Cfg::kXItems>(xr_rows, pt, Cfg::kProducers);
     uint32_t it = 0;
     for (int tile = first_tile; tile < p.num_tiles; tile += tile_step, ++it) {
-      const int xb = it & 1;
-      if (!warp_wait(&x_empty[xb], ((it >> 1) & 1) ^ 1, abort_flag)) {
+      const int xb = it & nx_sh;
+      if (!warp_wait(&x_empty[xb], ((it >> nx_sh) & 1) ^ 1, abort_flag)) {
         fail(abort_flag, p.status, 15);
         break;
       }
@@ -352,8 +355,8 @@ gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
       const bool px_ok = (h < H) && (w < W);
       const size_t pix = (size_t)h * W + w;
       T* on = out + (size_t)n * 4 * C * P;
-      const int xb = it & 1;
-      if (!warp_wait(&x_full[xb], (it >> 1) & 1, abort_flag)) {
+      const int xb = it & nx_sh;
+      if (!warp_wait(&x_full[xb], (it >> nx_sh) & 1, abort_flag)) {
         fail(abort_flag, p.status, 16);
         break;
       }
@@ -452,10 +455,15 @@ done:
 template <typename T, int KS, bool kStaged>
 int launch_k(const FwdParams& prm, const FwdMaps& maps, cudaStream_t st) {
   using Cfg = FwdCfg<T, KS, kStaged>;
-  const FwdSmem L = fwd_smem_layout<T, KS>(prm.Ck, prm.R);
+  FwdParams q = prm;
+  q.nxb = 2;
+  if ((int)fwd_smem_layout<T, KS>(q.Ck, q.R, 2).total > max_smem_optin()) q.nxb = 1;
+  const FwdSmem L = fwd_smem_layout<T, KS>(q.Ck, q.R, q.nxb);
+  if ((int)L.total > max_smem_optin())
+    return set_error(DDPM_ERR_UNSUPPORTED, "forward tile needs %u bytes of shared memory",
+                     L.total);
   auto fn = gencat_fwd_kernel<T, KS, kStaged>;
   DDPM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total));
-  FwdParams q = prm;
   const int per_cg = num_sms() / q.ncg;
   q.per_cg = q.num_tiles < per_cg ? q.num_tiles : per_cg;
   const int grid = q.ncg * q.per_cg;

@@ -112,7 +112,7 @@ def test_stage_layout(shape, ks, dil, dtype):
 
 @pytest.mark.parametrize("shape", SHAPES)
 @pytest.mark.parametrize("ks", [1, 3])
-@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("staged", [False, True])
 def test_gencat_bwd_yw(shape, ks, dtype, staged):
     """dY, dW and db from the on-chip dK (split partials + reduce); staged: x
@@ -165,3 +165,42 @@ def test_fused_autograd_matches_oracle_all_grads():
     for got, ref in zip(grads, gold):
         scale = max(ref.abs().max().item(), 1.0)
         assert (got.double().cpu() - ref).abs().max().item() <= 2e-4 * scale
+
+
+@pytest.mark.parametrize("shape", [(1, 64, 20, 24), (2, 40, 19, 24)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_max_halo_and_ragged_gradient_tiles(shape, dtype):
+    """Dilation halo 8, the largest supported (C=64 needs single-buffered x
+    halos in the fp32 forward and the 16-bit dY+dW pass to fit shared
+    memory), and 16-bit gradient tiles copied by TMA with ragged rows, columns
+    and channel groups (C=40): forward and every gradient through autograd,
+    plus the unstaged forward entry point."""
+    from dynamicconvolutionoperator_b200 import _kernels, _lib, fused_generator_dynamic_cat
+
+    ks, dil = 3, (8, 1, 8)
+    x, y, wt, b = _case(shape, ks, dtype, seed=21)
+    n, c, h, w = shape
+    g = torch.randn((n, 4 * c, h, w), generator=torch.Generator().manual_seed(22)).to(dtype)
+    gold_out = orc.fused_generator_cat(x, y, wt, b, ks, dil, quantize=True)
+    gold = _gold_grads(x, y, wt, b, g, ks, dil)
+    ts = [t.cuda().requires_grad_(True) for t in (x, y, wt, b)]
+    out = fused_generator_dynamic_cat(*ts, ks, dil)
+    grads = torch.autograd.grad(out, ts, g.cuda())
+    rtol, atol = TOL[dtype]
+    torch.testing.assert_close(out.detach().float().cpu(), gold_out.float(), rtol=rtol, atol=atol)
+    for got, ref in zip(grads[:2], gold[:2]):
+        torch.testing.assert_close(got.double().cpu(), ref, rtol=rtol, atol=atol)
+    for got, ref in zip(grads[2:], gold[2:]):
+        scale = ref.abs().max().item() + 1e-12
+        err = (got.double().cpu() - ref).abs().max().item() / scale
+        assert err <= (2e-4 if dtype == torch.float32 else 1e-2), err
+
+    with torch.no_grad():
+        xd, yd, wd, bd = (t.detach() for t in ts)
+        packed = _kernels.pack_generator_weight(wd, bd, c, ks, use_cache=False)
+        o2 = torch.full((n, 4 * c, h, w), float("nan"), dtype=dtype, device="cuda")
+        _lib.call("ddpm_gencat_fwd", xd.data_ptr(), yd.data_ptr(), packed.data_ptr(),
+                  bd.data_ptr(), o2.data_ptr(), n, c, h, w, ks, *dil, _lib.dtype_code(dtype),
+                  _lib.stream_handle(o2.device))
+        torch.cuda.synchronize()
+    torch.testing.assert_close(o2.float().cpu(), gold_out.float(), rtol=rtol, atol=atol)
