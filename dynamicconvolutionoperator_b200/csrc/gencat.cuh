@@ -625,6 +625,11 @@ int stage(const void* x, const void* y, void* staged, size_t staged_bytes, int n
 // False when the driver rejects one (callers then stage from x and y).
 bool encode_stage_maps(CUtensorMap* xmap, CUtensorMap* ymap, int R, int ygroups,
                        const uint8_t* staged, const StageLayout& sl);
+// Tensor map reading a 144-pixel row segment of the y plane ([group][pixel][8
+// channels], all `ngroups` channel groups of one part) as one 5-D box:
+// coordinates (0, first plane column / 16, plane row, 0, part * N + n).
+bool encode_stage_segment_map(CUtensorMap* map, int ngroups, const uint8_t* staged,
+                              const StageLayout& sl);
 
 }  // namespace gencat
 }  // namespace ddpm

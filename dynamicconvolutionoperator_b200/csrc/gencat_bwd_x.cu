@@ -59,7 +59,12 @@ struct BxCfg {
   static constexpr int kFirstProducerWarp = 1 + kIssuers;
   static constexpr int kProducers = kStaged ? 32 : 256;
   static constexpr int kFirstEpiWarp = kFirstProducerWarp + kProducers / 32;
-  static constexpr int kThreads = 32 * (kFirstEpiWarp + 8);
+  // epilogue warpgroups: the staged variant (one light producer warp) has the
+  // registers for four, one 16-channel block each, which hides twice the TMEM
+  // and shared-memory load latency of two warpgroups with two blocks each
+  static constexpr int kEpiWG = kStaged ? 4 : 2;
+  static constexpr int kBlkPerWG = 4 / kEpiWG;
+  static constexpr int kThreads = 32 * (kFirstEpiWarp + 4 * kEpiWG);
 };
 
 struct BxSmem {
@@ -83,8 +88,7 @@ __host__ __device__ inline BxSmem bx_smem_layout(int Cp, int Ck, int C) {
   L.w = L.gs + Cfg::kUnitBufs * L.g_bytes;
   L.bias = L.w + Cfg::kWStages * L.w_bytes;
   L.bars = L.bias + (Cfg::kBiasInGemm ? 0u : (uint32_t)(3 * KS * KS * Cp * 4));
-  const int nb = 512 / Cp > 8 ? 8 : 512 / Cp;
-  L.total = L.bars + 8 * (3 * Cfg::kUnitBufs + 2 * Cfg::kWStages + 2 * nb);
+  L.total = L.bars + 8 * (3 * Cfg::kUnitBufs + 2 * Cfg::kWStages + 2 * 8);
   return L;
 }
 
@@ -100,7 +104,9 @@ struct BxParams {
   const uint8_t* staged;  // staged y, or null (stage from y)
   StageLayout sl;
   CUtensorMap gmap;       // grad_out {W, H, 4C, N}, box {kSeg, 1, Cp, 1} (staged path)
+  CUtensorMap ymap;       // y-plane row segment, box of 9 16-px blocks x Ck/8 groups
   int g_tma;              // gmap is valid
+  int y_tma;              // ymap is valid
   int* status;
 };
 
@@ -156,7 +162,7 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
   const int C = p.C, Cp = p.Cp, Ck = p.Ck, H = p.H, W = p.W;
   const size_t P = (size_t)H * W;
   const BxSmem L = bx_smem_layout<T, KS, kStaged>(Cp, Ck, C);
-  const int NB = 512 / Cp > 8 ? 8 : 512 / Cp;
+  constexpr int NB = 8;  // TMEM chunk accumulators: 512 / Cp >= 8 for every Cp <= 64
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint64_t* u_full = bars;              // [NU] producers (128 arrivals) + gradient bytes
   uint64_t* r_empty = bars + NU;        // [NU] MMAs done with the y segment
@@ -177,7 +183,7 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
     for (int i = 0; i < NU; ++i) {
       tc::mbar_init(&u_full[i], Cfg::kProducers);
       tc::mbar_init(&r_empty[i], Cfg::kIssuers);
-      tc::mbar_init(&g_empty[i], 256);
+      tc::mbar_init(&g_empty[i], 128 * Cfg::kEpiWG);
     }
     for (int i = 0; i < S; ++i) {
       tc::mbar_init(&w_full[i], 1);
@@ -185,7 +191,7 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
     }
     for (int i = 0; i < NB; ++i) {
       tc::mbar_init(&t_full[i], 1);
-      tc::mbar_init(&t_empty[i], 256);
+      tc::mbar_init(&t_empty[i], 128 * Cfg::kEpiWG);
     }
     tc::fence_mbar_init();
     abort_s = 0;
@@ -322,10 +328,19 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
             // one arrival carries the unit's whole byte count, then the copies
             const uint32_t ybytes = (uint32_t)(ng * Cfg::kParts) * kSeg * 16;
             tc::mbar_arrive_expect_tx(&u_full[ub], ybytes + (p.g_tma ? L.g_bytes : 0u));
-            for (int k = 0; k < ng * Cfg::kParts; ++k) {
-              const int part = k / ng, kg = k - part * ng;
-              const uint8_t* src = p.staged + p.sl.row_offset(part, n, hr + p.sl.ph, kg, w0);
-              tc::bulk_g2s(reg + part * L.reg_part + kg * kSeg * 16, src, kSeg * 16, &u_full[ub]);
+            if (p.y_tma) {
+              // one box per part (the 1-D copies below cost ~60 ns each to issue)
+#pragma unroll
+              for (int part = 0; part < Cfg::kParts; ++part)
+                tc::tma_load_5d(reg + part * L.reg_part, &p.ymap, 0, w0 / 16, hr + p.sl.ph, 0,
+                                part * p.N + n, &u_full[ub]);
+            } else {
+              for (int k = 0; k < ng * Cfg::kParts; ++k) {
+                const int part = k / ng, kg = k - part * ng;
+                const uint8_t* src = p.staged + p.sl.row_offset(part, n, hr + p.sl.ph, kg, w0);
+                tc::bulk_g2s(reg + part * L.reg_part + kg * kSeg * 16, src, kSeg * 16,
+                             &u_full[ub]);
+              }
             }
             if (p.g_tma) tc::tma_load_4d(gs, &p.gmap, w0 - 8, hr, (b + 1) * C, n, &u_full[ub]);
           }
@@ -376,7 +391,7 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
       if (failed) break;
     }
   } else {
-    // ---- epilogue: warpgroup wg owns channel blocks wg, wg + 2 ------------
+    // ---- epilogue: warpgroup wg owns channel blocks wg, wg + kEpiWG --------
     const int ew = warp - Cfg::kFirstEpiWarp;
     const int wg = ew >> 2;
     const int quad = warp & 3;
@@ -393,37 +408,100 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
       const int w = (tile % p.tiles_w) * kTileM + m;
       const bool px_ok = w < W;
       const T* gn = gout + (size_t)n * 4 * C * P;
-      float acc[2][16];
+      float acc[Cfg::kBlkPerWG][16];
+      float g0[Cfg::kBlkPerWG][16];  // x-branch gradient
+      T g0raw[16];  // staged: loaded during the last unit, converted at the tile end
 #pragma unroll
-      for (int i = 0; i < 16; ++i) acc[0][i] = acc[1][i] = 0.f;
+      for (int bi = 0; bi < Cfg::kBlkPerWG; ++bi)
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[bi][i] = 0.f;
       bool failed = false;
       for (int u = 0; u < kUnits && !failed; ++u, ++uq) {
         const int b = u / KS, ki = u % KS;
         const int d = p.d[b];
         const int ub = uq % NU;
+        if constexpr (kStaged) {
+          // global loads issued here land while the last unit is computed (at
+          // the tile end they took ~3 us under the kernel's own copy traffic)
+          // (kept in the I/O type: a conversion right after the load waited for it)
+          if (u == kUnits - 1) {
+            const T* g0p = gn + (size_t)(wg * 16) * P + (size_t)h * W + w;
+#pragma unroll
+            for (int cl = 0; cl < 16; ++cl)
+              g0raw[cl] = (px_ok && wg < nblk && wg * 16 + cl < C) ? __ldg(g0p + cl * P) : T(0.f);
+          }
+        }
         if (!warp_wait(&u_full[ub], (uq / NU) & 1, abort_flag)) {
           fail(abort_flag, p.status, 25);
           failed = true;
           break;
         }
         const T* gs = reinterpret_cast<const T*>(smem + L.gs + ub * L.g_bytes);
-        for (int kj = 0; kj < KS; ++kj, ++tq) {
-          const int tap = ki * KS + kj;
-          const int dx = (kj - r) * d;
-          // g_b at (h - dy, w - dx): staged column m + 8 - dx (zero off-image)
-          const bool ok = px_ok && (unsigned)(w - dx) < (unsigned)W;
-          const int j = tq % NB;
-          if (!warp_wait(&t_full[j], (tq / NB) & 1, abort_flag)) {
+        if constexpr (kStaged) {
+          // One channel block per warpgroup. The next chunk's wait and TMEM load
+          // are issued before the current chunk is computed, so each chunk's
+          // wait / load latency overlaps the previous chunk's math. The staged
+          // gradient segment is zero outside the image.
+          static_assert(Cfg::kBlkPerWG == 1, "staged epilogue: one block per warpgroup");
+          const bool blk_ok = wg < nblk;
+          const T* gcol = gs + (size_t)(wg * 16) * kSeg + (m + 8);
+          const uint32_t tcol = tmem_base + ((uint32_t)(quad * 32) << 16) + wg * 16;
+          float dv[2][16];
+          if (!warp_wait(&t_full[tq % NB], (tq / NB) & 1, abort_flag)) {
             fail(abort_flag, p.status, 24);
             failed = true;
             break;
           }
           tc::tc_fence_after();
-          if constexpr (!kStaged) {
+          if (blk_ok) tc::tmem_ld16(tcol + (tq % NB) * Cp, dv[0]);
+#pragma unroll
+          for (int kj = 0; kj < KS; ++kj, ++tq) {
+            const int cur = kj & 1;
+            tc::tmem_ld_wait();
+            if (kj + 1 < KS) {
+              const uint32_t tn = tq + 1;
+              if (!warp_wait(&t_full[tn % NB], (tn / NB) & 1, abort_flag)) {
+                fail(abort_flag, p.status, 24);
+                failed = true;
+                break;
+              }
+              tc::tc_fence_after();
+              if (blk_ok) tc::tmem_ld16(tcol + (tn % NB) * Cp, dv[cur ^ 1]);
+            }
+            if (blk_ok) {
+              const int dx = (kj - r) * d;
+              float gv[16];
+#pragma unroll
+              for (int cl = 0; cl < 16; ++cl) gv[cl] = to_f32<T>(gcol[cl * kSeg - dx]);
+              if constexpr (!Cfg::kBiasInGemm) {
+                const float* bs = bias_s + (b * KK + ki * KS + kj) * Cp + wg * 16;
+#pragma unroll
+                for (int cl = 0; cl < 16; ++cl) dv[cur][cl] += bs[cl];
+              }
+              round_taps<T>(dv[cur]);
+#pragma unroll
+              for (int cl = 0; cl < 16; ++cl) acc[0][cl] = fmaf(dv[cur][cl], gv[cl], acc[0][cl]);
+            }
+            tc::tc_fence_before();
+            tc::mbar_arrive(&t_empty[tq % NB]);
+          }
+        } else {
+          for (int kj = 0; kj < KS; ++kj, ++tq) {
+            const int tap = ki * KS + kj;
+            const int dx = (kj - r) * d;
+            // g_b at (h - dy, w - dx): staged column m + 8 - dx (zero off-image)
+            const bool ok = px_ok && (unsigned)(w - dx) < (unsigned)W;
+            const int j = tq % NB;
+            if (!warp_wait(&t_full[j], (tq / NB) & 1, abort_flag)) {
+              fail(abort_flag, p.status, 24);
+              failed = true;
+              break;
+            }
+            tc::tc_fence_after();
             // 96-register budget: one channel block at a time
 #pragma unroll
-            for (int bi = 0; bi < 2; ++bi) {
-              const int blk = wg + 2 * bi;
+            for (int bi = 0; bi < Cfg::kBlkPerWG; ++bi) {
+              const int blk = wg + Cfg::kEpiWG * bi;
               if (blk >= nblk) break;
               float dv1[16];
               tc::tmem_ld16(tmem_base + ((uint32_t)(quad * 32) << 16) + j * Cp + blk * 16, dv1);
@@ -441,36 +519,9 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
 #pragma unroll
               for (int cl = 0; cl < 16; ++cl) acc[bi][cl] = fmaf(dv1[cl], gv1[cl], acc[bi][cl]);
             }
-          } else {
-          // both channel blocks' TMEM loads and gradient reads in flight before one wait
-          float dv[2][16], gv[2][16];
-#pragma unroll
-          for (int bi = 0; bi < 2; ++bi) {
-            const int blk = wg + 2 * bi;
-            if (blk < nblk) {
-              tc::tmem_ld16(tmem_base + ((uint32_t)(quad * 32) << 16) + j * Cp + blk * 16, dv[bi]);
-              const T* gcol = gs + (size_t)(blk * 16) * kSeg + (m + 8 - dx);
-#pragma unroll
-              for (int cl = 0; cl < 16; ++cl) gv[bi][cl] = ok ? to_f32<T>(gcol[cl * kSeg]) : 0.f;
-            }
+            tc::tc_fence_before();
+            tc::mbar_arrive(&t_empty[j]);
           }
-          tc::tmem_ld_wait();
-#pragma unroll
-          for (int bi = 0; bi < 2; ++bi) {
-            const int blk = wg + 2 * bi;
-            if (blk >= nblk) break;
-            if constexpr (!Cfg::kBiasInGemm) {
-              const float* bs = bias_s + (b * KK + tap) * Cp + blk * 16;
-#pragma unroll
-              for (int cl = 0; cl < 16; ++cl) dv[bi][cl] += bs[cl];
-            }
-            round_taps<T>(dv[bi]);
-#pragma unroll
-            for (int cl = 0; cl < 16; ++cl) acc[bi][cl] = fmaf(dv[bi][cl], gv[bi][cl], acc[bi][cl]);
-          }
-          }
-          tc::tc_fence_before();
-          tc::mbar_arrive(&t_empty[j]);
         }
         if (!failed) tc::mbar_arrive(&g_empty[ub]);
       }
@@ -480,19 +531,23 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
         // alias nothing, but the compiler cannot know; interleaved, every load
         // waited for the previous store: 32 serial load latencies per tile)
         const size_t q = (size_t)h * W + w;
-        float g0[2][16];
+        if constexpr (kStaged) {
 #pragma unroll
-        for (int bi = 0; bi < 2; ++bi) {
-          const int blk = wg + 2 * bi;
+          for (int cl = 0; cl < 16; ++cl) g0[0][cl] = to_f32<T>(g0raw[cl]);
+        } else {
 #pragma unroll
-          for (int cl = 0; cl < 16; ++cl) {
-            const int c = blk * 16 + cl;
-            g0[bi][cl] = (blk < nblk && c < C) ? to_f32<T>(__ldg(gn + (size_t)c * P + q)) : 0.f;
+          for (int bi = 0; bi < Cfg::kBlkPerWG; ++bi) {
+            const int blk = wg + Cfg::kEpiWG * bi;
+#pragma unroll
+            for (int cl = 0; cl < 16; ++cl) {
+              const int c = blk * 16 + cl;
+              g0[bi][cl] = (blk < nblk && c < C) ? to_f32<T>(__ldg(gn + (size_t)c * P + q)) : 0.f;
+            }
           }
         }
 #pragma unroll
-        for (int bi = 0; bi < 2; ++bi) {
-          const int blk = wg + 2 * bi;
+        for (int bi = 0; bi < Cfg::kBlkPerWG; ++bi) {
+          const int blk = wg + Cfg::kEpiWG * bi;
           if (blk >= nblk) break;
 #pragma unroll
           for (int cl = 0; cl < 16; ++cl) {
@@ -575,6 +630,7 @@ int gencat_bwd_x(const void* y, const void* staged, size_t staged_bytes, const v
                        prm.sl.y_bytes());
     DDPM_CHECK_ARG((reinterpret_cast<uintptr_t>(staged) & 15u) == 0,
                    "staged y must be 16-byte aligned");
+    prm.y_tma = gencat::encode_stage_segment_map(&prm.ymap, pl.Ck / 8, prm.staged, prm.sl) ? 1 : 0;
     // gradient segments by TMA when the row pitch and base allow a tensor map
     const int es = dtype_size(dt);
     if (((size_t)w * es) % 16 == 0 && (reinterpret_cast<uintptr_t>(gout) & 15u) == 0) {

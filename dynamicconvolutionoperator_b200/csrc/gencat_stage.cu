@@ -157,5 +157,22 @@ bool encode_stage_maps(CUtensorMap* xmap, CUtensorMap* ymap, int R, int ygroups,
   return true;
 }
 
+bool encode_stage_segment_map(CUtensorMap* map, int ngroups, const uint8_t* staged,
+                              const StageLayout& sl) {
+  // 16-pixel blocks of 256 bytes as the two inner dimensions, so one box of
+  // 9 blocks x ngroups lands as [group][144 px][16 B] (group stride 2304 B)
+  const uint64_t d[5] = {32, (uint64_t)sl.Wp / 16, (uint64_t)sl.Hp, (uint64_t)sl.G,
+                         (uint64_t)sl.parts * sl.N};
+  const uint64_t s[4] = {256, (uint64_t)sl.Wp * 16, (uint64_t)sl.Hp * sl.Wp * 16,
+                         (uint64_t)sl.G * sl.Hp * sl.Wp * 16};
+  const uint32_t box[5] = {32, 9, 1, (uint32_t)ngroups, 1};
+  if (encode_tmap(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 5, staged, d, s, box,
+                  CU_TENSOR_MAP_SWIZZLE_NONE) != DDPM_OK) {
+    clear_error();
+    return false;
+  }
+  return true;
+}
+
 }  // namespace gencat
 }  // namespace ddpm
