@@ -369,6 +369,25 @@ def library_kernels(model, x, y, dtype, device):
         _lib.call("ddpm_gencat_fwd_staged", sy.data_ptr(), sy_bytes, packed.data_ptr(),
                   gen_b.data_ptr(), out2.data_ptr(), n, C, H, W, K, *DILATIONS, code, sh)
 
+    # fuse conv as in the step: the source staged as operand planes, then the
+    # staged kernel (both timed together)
+    fp_bytes = int(_lib.load().ddpm_fuseconv_stage_bytes(n, 4 * C, H, W, code))
+    fplanes = torch.empty(fp_bytes, dtype=torch.uint8, device=device)
+    gp_bytes = int(_lib.load().ddpm_fuseconv_stage_bytes(n, C, H, W, code))
+    gplanes = torch.empty(gp_bytes, dtype=torch.uint8, device=device)
+
+    def fuse_fwd():
+        _lib.call("ddpm_fuseconv_stage", out.data_ptr(), fplanes.data_ptr(), fp_bytes, n, 4 * C,
+                  H, W, code, sh)
+        _lib.call("ddpm_fuseconv_fwd_staged", fplanes.data_ptr(), fp_bytes, fpacked.data_ptr(),
+                  fuse_b.data_ptr(), fout.data_ptr(), n, 4 * C, C, H, W, code, sh)
+
+    def fuse_dgrad():
+        _lib.call("ddpm_fuseconv_stage", fgout.data_ptr(), gplanes.data_ptr(), gp_bytes, n, C, H,
+                  W, code, sh)
+        _lib.call("ddpm_fuseconv_bwd_data_staged", gplanes.data_ptr(), gp_bytes,
+                  fpacked.data_ptr(), fgx.data_ptr(), n, 4 * C, C, H, W, code, sh)
+
     def bwd_x():
         _lib.call("ddpm_gencat_bwd_x_staged", sy.data_ptr(), sy_bytes, packed.data_ptr(),
                   gen_b.data_ptr(), gout.data_ptr(), gx.data_ptr(), n, C, H, W, K, *DILATIONS,
@@ -380,24 +399,16 @@ def library_kernels(model, x, y, dtype, device):
                   ws_bytes, n, C, H, W, K, *DILATIONS, code, sh)
 
     keep = (taps, out, gout, gx, gk, packed, out2, gy, gw, gb, ws, fpacked, fout, fgout, fgx,
-            fgw, fgb, fws, sy)
+            fgw, fgb, fws, sy, fplanes, gplanes)
     return keep, {
-        "fuseconv_fwd": (
-            lambda: _lib.call("ddpm_fuseconv_fwd", out.data_ptr(), fpacked.data_ptr(),
-                              fuse_b.data_ptr(), fout.data_ptr(), n, 4 * C, C, H, W, code, sh),
-            "tensor", fuse_flops,
-        ),
+        "fuseconv_fwd": (fuse_fwd, "tensor", fuse_flops),
         "fuseconv_wgrad": (
             lambda: _lib.call("ddpm_fuseconv_bwd_weight", out.data_ptr(), fgout.data_ptr(),
                               fgw.data_ptr(), fgb.data_ptr(), fws.data_ptr(), fws_bytes,
                               n, 4 * C, C, H, W, code, sh),
             "tensor", fuse_flops,
         ),
-        "fuseconv_dgrad": (
-            lambda: _lib.call("ddpm_fuseconv_bwd_data", fgout.data_ptr(), fpacked.data_ptr(),
-                              fgx.data_ptr(), n, 4 * C, C, H, W, code, sh),
-            "tensor", fuse_flops,
-        ),
+        "fuseconv_dgrad": (fuse_dgrad, "tensor", fuse_flops),
         "gencat_bwd_x": (bwd_x, "tensor", gen_flops),
         "gencat_bwd_yw": (bwd_yw, "tensor", 2 * gen_flops),
         "gencat_fwd": (fwd, "tensor", 2 * (3 * C * K * K) * C * n * H * W),

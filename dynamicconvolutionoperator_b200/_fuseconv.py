@@ -11,6 +11,11 @@ autograd contract as ``nn.Conv2d``.
 
 The backward runs on the same library: data gradient (shifted-window GEMM)
 and weight / bias gradient (split spatial reduction into FP32 partials).
+
+The forward and the data gradient first stage their source tensor (x, resp.
+grad_out) once as zero-padded channel-group planes (``ddpm_fuseconv_stage``),
+which the staged kernels read with one TMA copy per K slab; the results equal
+the unstaged entry points bit for bit.
 """
 
 from __future__ import annotations
@@ -63,6 +68,17 @@ def pack_fuse_weight(weight: torch.Tensor, use_cache: bool) -> torch.Tensor:
     return packed
 
 
+def _stage_planes(src: torch.Tensor) -> tuple[torch.Tensor, int]:
+    """``src`` [N, C, H, W] as the staged operand planes (``ddpm_fuseconv_stage``)."""
+    n, c, h, w = src.shape
+    code = _lib.dtype_code(src.dtype)
+    nbytes = int(_lib.load().ddpm_fuseconv_stage_bytes(n, c, h, w, code))
+    planes = torch.empty(nbytes, dtype=torch.uint8, device=src.device)
+    _lib.call("ddpm_fuseconv_stage", src.data_ptr(), planes.data_ptr(), nbytes, n, c, h, w, code,
+              _lib.stream_handle(src.device))
+    return planes, nbytes
+
+
 class _FuseConv(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, weight, bias, use_cache):
@@ -72,7 +88,8 @@ class _FuseConv(torch.autograd.Function):
         packed = pack_fuse_weight(weight, use_cache)
         out = torch.empty((n, cout, h, w), dtype=x.dtype, device=x.device)
         b = bias.contiguous() if bias is not None else None
-        _lib.call("ddpm_fuseconv_fwd", x.data_ptr(), packed.data_ptr(),
+        planes, nbytes = _stage_planes(x)
+        _lib.call("ddpm_fuseconv_fwd_staged", planes.data_ptr(), nbytes, packed.data_ptr(),
                   b.data_ptr() if b is not None else None, out.data_ptr(),
                   n, cin, cout, h, w, _lib.dtype_code(x.dtype), _lib.stream_handle(x.device))
         ctx.save_for_backward(x, weight)
@@ -89,9 +106,10 @@ class _FuseConv(torch.autograd.Function):
         gx = gw = gb = None
         if ctx.needs_input_grad[0]:
             gx = torch.empty_like(x)
-            _lib.call("ddpm_fuseconv_bwd_data", g.data_ptr(), ctx.packed.data_ptr(),
-                      gx.data_ptr(), n, cin, cout, h, w, _lib.dtype_code(x.dtype),
-                      _lib.stream_handle(x.device))
+            planes, nbytes = _stage_planes(g)
+            _lib.call("ddpm_fuseconv_bwd_data_staged", planes.data_ptr(), nbytes,
+                      ctx.packed.data_ptr(), gx.data_ptr(), n, cin, cout, h, w,
+                      _lib.dtype_code(x.dtype), _lib.stream_handle(x.device))
         need_b = ctx.has_bias and ctx.needs_input_grad[2]
         if ctx.needs_input_grad[1] or need_b:
             gw = torch.empty_like(weight)

@@ -81,6 +81,14 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ddpm_fuseconv_pack": (_c_int, [_c_ptr, _c_int, _c_int, _c_int, _c_ptr, _c_size, _c_ptr]),
     "ddpm_fuseconv_fwd": (_c_int, [_c_ptr] * 4 + [_c_int] * 6 + [_c_ptr]),
     "ddpm_fuseconv_bwd_data": (_c_int, [_c_ptr] * 3 + [_c_int] * 6 + [_c_ptr]),
+    "ddpm_fuseconv_stage_bytes": (_c_size, [_c_int] * 5),
+    "ddpm_fuseconv_stage": (_c_int, [_c_ptr, _c_ptr, _c_size] + [_c_int] * 5 + [_c_ptr]),
+    "ddpm_fuseconv_fwd_staged": (
+        _c_int, [_c_ptr, _c_size] + [_c_ptr] * 3 + [_c_int] * 6 + [_c_ptr]
+    ),
+    "ddpm_fuseconv_bwd_data_staged": (
+        _c_int, [_c_ptr, _c_size] + [_c_ptr] * 2 + [_c_int] * 6 + [_c_ptr]
+    ),
     "ddpm_fuseconv_bwd_weight_workspace_bytes": (_c_size, [_c_int] * 5),
     "ddpm_fuseconv_bwd_weight": (
         _c_int, [_c_ptr] * 5 + [_c_size] + [_c_int] * 6 + [_c_ptr]

@@ -66,6 +66,14 @@ int fuseconv_fwd(const void* cat, const void* packed, const void* bias, void* ou
                  int cout, int h, int w, int dt, cudaStream_t st);
 int fuseconv_dgrad(const void* gout, const void* packed, void* gcat, int n, int cin, int cout,
                    int h, int w, int dt, cudaStream_t st);
+size_t fuseconv_stage_bytes(int n, int c, int h, int w, int dt);
+int fuseconv_stage(const void* src, void* planes, size_t bytes, int n, int c, int h, int w, int dt,
+                   cudaStream_t st);
+int fuseconv_fwd_staged(const void* planes, size_t planes_bytes, const void* packed,
+                        const void* bias, void* out, int n, int cin, int cout, int h, int w, int dt,
+                        cudaStream_t st);
+int fuseconv_dgrad_staged(const void* planes, size_t planes_bytes, const void* packed, void* gcat,
+                          int n, int cin, int cout, int h, int w, int dt, cudaStream_t st);
 namespace gencat {
 int read_status(int reset, int* code);
 }
@@ -223,6 +231,33 @@ int ddpm_fuseconv_bwd_data(const void* grad_out, const void* packed, void* grad_
   ddpm::clear_error();
   return ddpm::fuseconv_dgrad(grad_out, packed, grad_x, n, cin, cout, h, w, dtype,
                               static_cast<cudaStream_t>(stream));
+}
+
+size_t ddpm_fuseconv_stage_bytes(int n, int c, int h, int w, int dtype) {
+  return ddpm::fuseconv_stage_bytes(n, c, h, w, dtype);
+}
+
+int ddpm_fuseconv_stage(const void* src, void* planes, size_t planes_bytes, int n, int c, int h,
+                        int w, int dtype, void* stream) {
+  ddpm::clear_error();
+  return ddpm::fuseconv_stage(src, planes, planes_bytes, n, c, h, w, dtype,
+                              static_cast<cudaStream_t>(stream));
+}
+
+int ddpm_fuseconv_fwd_staged(const void* planes, size_t planes_bytes, const void* packed,
+                             const void* bias, void* out, int n, int cin, int cout, int h, int w,
+                             int dtype, void* stream) {
+  ddpm::clear_error();
+  return ddpm::fuseconv_fwd_staged(planes, planes_bytes, packed, bias, out, n, cin, cout, h, w,
+                                   dtype, static_cast<cudaStream_t>(stream));
+}
+
+int ddpm_fuseconv_bwd_data_staged(const void* planes, size_t planes_bytes, const void* packed,
+                                  void* grad_x, int n, int cin, int cout, int h, int w, int dtype,
+                                  void* stream) {
+  ddpm::clear_error();
+  return ddpm::fuseconv_dgrad_staged(planes, planes_bytes, packed, grad_x, n, cin, cout, h, w,
+                                     dtype, static_cast<cudaStream_t>(stream));
 }
 
 int ddpm_device_status(int reset, int* code) {

@@ -32,6 +32,7 @@
 #include "tc.cuh"
 #include "gencat.cuh"
 #include "fuseconv.cuh"
+#include "tmap.cuh"
 
 namespace ddpm {
 namespace {
@@ -56,8 +57,17 @@ struct FcParams {
   int nhalf;            // dst channel blocks of Nn (data gradient: ceil(Cin / 128))
   int tiles_w, hpairs, num_units;
   int reg_bufs, w_stages;
-  uint32_t reg_part, reg_bytes, w_chunk;
+  uint32_t reg_part, reg_bytes;
+  uint32_t w_chunk;     // bytes per streamed weight chunk (FcCfg::kTapsPerChunk taps)
+  uint32_t w_tap;       // bytes of one (slab, tap) B image within a chunk
   int* status;
+};
+
+// Tensor map of the staged source planes (separate grid-constant parameter):
+// dims {32 x 64-bit (16 px), Wp/16, Hp, G, parts*N}, box {32, 9, 4, KC/8, 1},
+// which lands as the slab operand [KC/8][4 rows][144 px][8 channels].
+struct FcMaps {
+  CUtensorMap smap;
 };
 
 struct FcSmem {
@@ -74,13 +84,18 @@ __host__ __device__ inline FcSmem fc_smem_layout(const FcParams& p) {
   return L;
 }
 
-template <typename T, bool kDgrad>
+template <typename T, bool kDgrad, bool kStaged = false>
 struct FcCfg {
   static constexpr bool kSplit = IoTraits<T>::kSplit;
   // K slab: input channels (forward) or output channels (data gradient)
   static constexpr int KC = kDgrad ? (kSplit ? 32 : 64) : (kSplit ? 16 : 32);
   static constexpr int kSteps = KC / 16;
-  static constexpr int kProducers = 256;
+  // staged planes: one warp (one thread issues the TMA boxes)
+  static constexpr int kProducers = kStaged ? 32 : 256;
+  // taps per streamed weight chunk: the forward streams a slab's 9 tap images
+  // (4 KB each) as one chunk, so the issuers wait, and commit, once per slab
+  // instead of once per 1-3 MMAs; the data gradient's tap images are 16-32 KB
+  static constexpr int kTapsPerChunk = kDgrad ? 1 : 9;
   static constexpr int kItems = (KC / 8) * kRows * (kSeg / 8);  // 8 channels x 8 pixels each
   static constexpr int kItemsMax = sizeof(T) == 4 ? 1 : 2;      // per thread and round
   static constexpr int kRounds = (kItems + kProducers * kItemsMax - 1) / (kProducers * kItemsMax);
@@ -97,10 +112,10 @@ struct FcCfg {
 // thread ~55 cycles, so with N <= 128 a single issuer would leave the tensor
 // pipe idle between instructions. Their inner loops are unrolled over taps
 // and K steps with descriptors advanced by constants.
-template <typename T, bool kDgrad>
-__global__ void __launch_bounds__(FcCfg<T, kDgrad>::kThreads, 1)
-fuseconv_kernel(const FcParams p) {
-  using Cfg = FcCfg<T, kDgrad>;
+template <typename T, bool kDgrad, bool kStaged>
+__global__ void __launch_bounds__(FcCfg<T, kDgrad, kStaged>::kThreads, 1)
+fuseconv_kernel(const FcParams p, const __grid_constant__ FcMaps maps) {
+  using Cfg = FcCfg<T, kDgrad, kStaged>;
   using Op = typename IoTraits<T>::Op;
   constexpr bool kSplit = Cfg::kSplit;
   constexpr int KC = Cfg::KC;
@@ -154,7 +169,7 @@ fuseconv_kernel(const FcParams p) {
   tc::tc_fence_after();
   const uint32_t tmem_base = tmem_base_s;
   volatile int* abort_flag = &abort_s;
-  const int chunks = p.nslab * 9;  // weight chunks per unit
+  const int chunks = p.nslab * (9 / Cfg::kTapsPerChunk);  // weight chunks per unit
 
   if (warp == 0) {
     // ---- weight producer ------------------------------------------------------
@@ -205,31 +220,38 @@ fuseconv_kernel(const FcParams p) {
           tc::tc_fence_after();
           const uint64_t a_base =
               tc::smem_desc(tc::smem_u32(smem + L.reg + rb * p.reg_bytes), a_lbo, 128);
+          constexpr int TPC = Cfg::kTapsPerChunk;
+          const uint64_t b_tap = p.w_tap >> 4;  // descriptor advance per tap image
 #pragma unroll
-          for (int t = 0; t < 9; ++t) {
-            const int s = (wq + t) % S;
-            if (!tc::mbar_wait(&w_full[s], ((wq + t) / S) & 1, abort_flag, kWaitNs)) {
+          for (int tcg = 0; tcg < 9 / TPC; ++tcg, ++wq) {
+            const int s = wq % S;
+            if (!tc::mbar_wait(&w_full[s], (wq / S) & 1, abort_flag, kWaitNs)) {
               fail(abort_flag, p.status, 63);
               goto done;
             }
             tc::tc_fence_after();
-            const int ky = t / 3, kx = t % 3;
-            const int seg = kDgrad ? (mh - ky + 2) : (mh + ky);
-            const int col = kDgrad ? (9 - kx) : (7 + kx);
-            const uint64_t ad = a_base + (uint64_t)(seg * kSeg + col);
-            const uint64_t bd = tc::smem_desc(tc::smem_u32(smem + L.w + s * p.w_chunk), b_lbo, 128);
+            const uint64_t bstage =
+                tc::smem_desc(tc::smem_u32(smem + L.w + s * p.w_chunk), b_lbo, 128);
 #pragma unroll
-            for (int ks = 0; ks < Cfg::kSteps; ++ks) {
-              const uint32_t acc = (sl > 0 || t > 0 || ks > 0) ? 1u : 0u;
-              tc::mma_f16(d, ad + ks * a_step, bd + ks * b_step, idesc, acc);
-              if constexpr (kSplit) {
-                tc::mma_f16(d, ad + a_lo + ks * a_step, bd + ks * b_step, idesc, 1u);
-                tc::mma_f16(d, ad + ks * a_step, bd + b_lo + ks * b_step, idesc, 1u);
+            for (int tt = 0; tt < TPC; ++tt) {
+              const int t = tcg * TPC + tt;
+              const int ky = t / 3, kx = t % 3;
+              const int seg = kDgrad ? (mh - ky + 2) : (mh + ky);
+              const int col = kDgrad ? (9 - kx) : (7 + kx);
+              const uint64_t ad = a_base + (uint64_t)(seg * kSeg + col);
+              const uint64_t bd = bstage + tt * b_tap;
+#pragma unroll
+              for (int ks = 0; ks < Cfg::kSteps; ++ks) {
+                const uint32_t acc = (sl > 0 || t > 0 || ks > 0) ? 1u : 0u;
+                tc::mma_f16(d, ad + ks * a_step, bd + ks * b_step, idesc, acc);
+                if constexpr (kSplit) {
+                  tc::mma_f16(d, ad + a_lo + ks * a_step, bd + ks * b_step, idesc, 1u);
+                  tc::mma_f16(d, ad + ks * a_step, bd + b_lo + ks * b_step, idesc, 1u);
+                }
               }
             }
             tc::mma_commit(&w_empty[s]);
           }
-          wq += 9;
           tc::mma_commit(&r_empty[rb]);
         }
         tc::mma_commit(&t_full[tb]);
@@ -251,6 +273,24 @@ fuseconv_kernel(const FcParams p) {
         const int rb = rq % NR;
         uint8_t* reg = smem + L.reg + rb * p.reg_bytes;
         bool failed = false;
+        if constexpr (kStaged) {
+          // plane rows h0 .. h0+3 = image rows h0-1 .. h0+2; plane columns
+          // w0 .. w0+143 = image columns w0-8 .. w0+135; one box per part
+          if (!warp_wait(&r_empty[rb], ((rq / NR) & 1) ^ 1, abort_flag)) {
+            fail(abort_flag, p.status, 64);
+            break;
+          }
+          if (pt == 0) {
+            tc::mbar_arrive_expect_tx(&r_full[rb], p.reg_bytes);
+#pragma unroll
+            for (int part = 0; part < (kSplit ? 2 : 1); ++part)
+              tc::tma_load_5d(reg + part * p.reg_part, &maps.smap, 0, w0 / 16, h0,
+                              sl * (KC / 8), part * p.N + n, &r_full[rb]);
+          } else {
+            tc::mbar_arrive(&r_full[rb]);
+          }
+          continue;
+        }
 #pragma unroll 1
         for (int round = 0; round < Cfg::kRounds; ++round) {
           const int base = round * Cfg::kProducers * Cfg::kItemsMax;
@@ -409,20 +449,98 @@ __global__ void fuseconv_pack_kernel(const T* __restrict__ w, typename IoTraits<
   }
 }
 
-template <typename T, bool kDgrad>
-int launch_conv(FcParams prm, cudaStream_t st) {
+template <typename T, bool kDgrad, bool kStaged>
+int launch_conv(FcParams prm, const FcMaps& maps, cudaStream_t st) {
   const FcSmem L = fc_smem_layout(prm);
-  auto fn = fuseconv_kernel<T, kDgrad>;
+  auto fn = fuseconv_kernel<T, kDgrad, kStaged>;
   DDPM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total));
   const int grid = prm.num_units < num_sms() ? prm.num_units : num_sms();
-  fn<<<grid, FcCfg<T, kDgrad>::kThreads, L.total, st>>>(prm);
+  fn<<<grid, FcCfg<T, kDgrad, kStaged>::kThreads, L.total, st>>>(prm, maps);
   DDPM_CHECK_LAUNCH(kDgrad ? "fuseconv_dgrad_kernel" : "fuseconv_fwd_kernel");
   return DDPM_OK;
 }
 
 template <typename T>
-int dispatch_conv(bool dgrad, const FcParams& prm, cudaStream_t st) {
-  return dgrad ? launch_conv<T, true>(prm, st) : launch_conv<T, false>(prm, st);
+int dispatch_conv(bool dgrad, bool staged, const FcParams& prm, const FcMaps& maps,
+                  cudaStream_t st) {
+  if (staged)
+    return dgrad ? launch_conv<T, true, true>(prm, maps, st)
+                 : launch_conv<T, false, true>(prm, maps, st);
+  return dgrad ? launch_conv<T, true, false>(prm, maps, st)
+               : launch_conv<T, false, false>(prm, maps, st);
+}
+
+// ------------------------------------------------------------ plane staging ----
+constexpr int kPlaneCols = 64;   // plane columns per block
+constexpr int kPlaneChans = 64;  // channels per block
+
+// Block = (n, plane row, 64-column strip, 64-channel chunk): 8-pixel vector
+// loads of one channel, a padded shared tile transposes, each thread writes
+// 16-byte rows of 8 channels (consecutive threads = consecutive columns).
+template <typename T>
+__global__ void __launch_bounds__(256) stage_planes_kernel(const T* __restrict__ src,
+                                                           uint4* __restrict__ hi,
+                                                           uint4* __restrict__ lo,
+                                                           const fuseconv::PlaneLayout L) {
+  using Op = typename IoTraits<T>::Op;
+  constexpr bool kSplit = IoTraits<T>::kSplit;
+  __shared__ float tile[kPlaneChans][kPlaneCols + 1];
+  const int ni = blockIdx.x, n = ni / L.Hp, i = ni - n * L.Hp;
+  const int hr = i - 1;                      // image row (may be outside the image)
+  const int j0 = blockIdx.y * kPlaneCols;    // first plane column
+  const int c0 = blockIdx.z * kPlaneChans;   // first channel
+  const size_t P = (size_t)L.H * L.W;
+  for (int item = threadIdx.x; item < kPlaneChans * (kPlaneCols / 8); item += blockDim.x) {
+    const int g = item & 7, cl = item >> 3, c = c0 + cl;
+    Raw8<T> v;
+    if (c < L.C)
+      v = load_raw8<T>(src + ((size_t)n * L.C + c) * P, L.H, L.W, hr, j0 - 8 + g * 8);
+    else
+      v.zero();
+#pragma unroll
+    for (int e = 0; e < 8; ++e) tile[cl][g * 8 + e] = v.get(e);
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < (kPlaneChans / 8) * kPlaneCols; idx += blockDim.x) {
+    const int kg = idx / kPlaneCols, x = idx - kg * kPlaneCols;
+    const int g = c0 / 8 + kg;
+    if (j0 + x >= L.Wp || g >= L.G) continue;
+    unsigned long long pr[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) pr[e] = f2_pack(tile[kg * 8 + 2 * e][x], tile[kg * 8 + 2 * e + 1][x]);
+    const size_t dst = (((size_t)n * L.G + g) * L.Hp + i) * L.Wp + j0 + x;
+    uint4 vh, vl;
+    store8x2_split<Op, kSplit>(reinterpret_cast<uint8_t*>(&vh), reinterpret_cast<uint8_t*>(&vl), pr);
+    hi[dst] = vh;
+    if constexpr (kSplit) lo[dst] = vl;
+  }
+}
+
+template <typename T>
+int launch_stage_planes(const T* src, uint8_t* planes, const fuseconv::PlaneLayout& L,
+                        cudaStream_t st) {
+  uint4* hi = reinterpret_cast<uint4*>(planes);
+  uint4* lo = L.parts > 1 ? reinterpret_cast<uint4*>(planes + L.part_bytes) : nullptr;
+  const dim3 grid((unsigned)(L.N * L.Hp), (unsigned)((L.Wp + kPlaneCols - 1) / kPlaneCols),
+                  (unsigned)((L.G * 8 + kPlaneChans - 1) / kPlaneChans));
+  stage_planes_kernel<T><<<grid, 256, 0, st>>>(src, hi, lo, L);
+  DDPM_CHECK_LAUNCH("fuseconv_stage_planes_kernel");
+  return DDPM_OK;
+}
+
+bool encode_plane_map(CUtensorMap* map, const uint8_t* planes, const fuseconv::PlaneLayout& L,
+                      int KC) {
+  const uint64_t d[5] = {32, (uint64_t)L.Wp / 16, (uint64_t)L.Hp, (uint64_t)L.G,
+                         (uint64_t)L.parts * L.N};
+  const uint64_t s4[4] = {256, (uint64_t)L.Wp * 16, (uint64_t)L.Hp * L.Wp * 16,
+                          (uint64_t)L.G * L.Hp * L.Wp * 16};
+  const uint32_t box[5] = {32, 9, (uint32_t)kRows, (uint32_t)(KC / 8), 1};
+  if (encode_tmap(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 5, planes, d, s4, box,
+                  CU_TENSOR_MAP_SWIZZLE_NONE) != DDPM_OK) {
+    clear_error();
+    return false;
+  }
+  return true;
 }
 
 int check_conv(int n, int cin, int cout, int h, int w, int dt) {
@@ -449,18 +567,46 @@ FcParams common_params(int n, int h, int w, int nhalf, int* status) {
   return q;
 }
 
-int dispatch_dt(int dt, bool dgrad, const FcParams& prm, cudaStream_t st) {
+int dispatch_dt(int dt, bool dgrad, bool staged, const FcParams& prm, const FcMaps& maps,
+                cudaStream_t st) {
   switch (dt) {
-    case DDPM_BF16: return dispatch_conv<__nv_bfloat16>(dgrad, prm, st);
-    case DDPM_F16: return dispatch_conv<__half>(dgrad, prm, st);
-    case DDPM_F32: return dispatch_conv<float>(dgrad, prm, st);
+    case DDPM_BF16: return dispatch_conv<__nv_bfloat16>(dgrad, staged, prm, maps, st);
+    case DDPM_F16: return dispatch_conv<__half>(dgrad, staged, prm, maps, st);
+    case DDPM_F32: return dispatch_conv<float>(dgrad, staged, prm, maps, st);
   }
   return set_error(DDPM_ERR_INVALID_ARG, "unknown dtype %d", dt);
+}
+
+// Staged planes argument check and tensor map (KC = the pass's K slab).
+int plane_map(FcMaps* maps, const void* planes, size_t bytes, int n, int c, int h, int w,
+              int dt, int KC) {
+  const fuseconv::PlaneLayout L = fuseconv::PlaneLayout::make(n, c, h, w, dt);
+  if (bytes < L.bytes())
+    return set_error(DDPM_ERR_WORKSPACE, "staged planes too small (%zu < %zu)", bytes, L.bytes());
+  DDPM_CHECK_ARG((reinterpret_cast<uintptr_t>(planes) & 255u) == 0,
+                 "staged planes must be 256-byte aligned");
+  if (!encode_plane_map(&maps->smap, static_cast<const uint8_t*>(planes), L, KC))
+    return set_error(DDPM_ERR_CUDA, "tensor map of the staged planes could not be encoded");
+  return DDPM_OK;
 }
 
 }  // namespace
 
 namespace fuseconv {
+
+PlaneLayout PlaneLayout::make(int n, int c, int h, int w, int dt) {
+  PlaneLayout L{};
+  L.N = n;
+  L.C = c;
+  L.H = h;
+  L.W = w;
+  L.G = (c + 63) / 64 * 8;
+  L.Hp = h + 2;
+  L.Wp = (w + 127) / 128 * 128 + 16;
+  L.parts = dt == DDPM_F32 ? 2 : 1;
+  L.part_bytes = (size_t)n * L.G * L.Hp * L.Wp * 16;
+  return L;
+}
 
 Layout Layout::make(int cin, int cout, int dt) {
   Layout L{};
@@ -523,11 +669,38 @@ int fuseconv_pack(const void* w, int cin, int cout, int dt, void* packed, size_t
   return DDPM_OK;
 }
 
-int fuseconv_fwd(const void* cat, const void* packed, const void* bias, void* out, int n, int cin,
-                 int cout, int h, int w, int dt, cudaStream_t st) {
+size_t fuseconv_stage_bytes(int n, int c, int h, int w, int dt) {
+  if (n < 1 || c < 1 || h < 1 || w < 1 || c > fuseconv::kMaxCin || dtype_size(dt) == 0) return 0;
+  return fuseconv::PlaneLayout::make(n, c, h, w, dt).bytes();
+}
+
+int fuseconv_stage(const void* src, void* planes, size_t bytes, int n, int c, int h, int w, int dt,
+                   cudaStream_t st) {
+  DDPM_CHECK_ARG(n >= 1 && c >= 1 && h >= 1 && w >= 1, "sizes must be positive");
+  DDPM_CHECK_ARG(dtype_size(dt) > 0, "unknown dtype code %d", dt);
+  if (c > fuseconv::kMaxCin)
+    return set_error(DDPM_ERR_UNSUPPORTED, "staged planes support C <= %d", fuseconv::kMaxCin);
+  DDPM_CHECK_ARG(src && planes, "null pointer");
+  const fuseconv::PlaneLayout L = fuseconv::PlaneLayout::make(n, c, h, w, dt);
+  if (bytes < L.bytes())
+    return set_error(DDPM_ERR_WORKSPACE, "staged planes too small (%zu < %zu)", bytes, L.bytes());
+  DDPM_CHECK_ARG((reinterpret_cast<uintptr_t>(planes) & 255u) == 0,
+                 "staged planes must be 256-byte aligned");
+  uint8_t* pl = static_cast<uint8_t*>(planes);
+  switch (dt) {
+    case DDPM_BF16: return launch_stage_planes(static_cast<const __nv_bfloat16*>(src), pl, L, st);
+    case DDPM_F16: return launch_stage_planes(static_cast<const __half*>(src), pl, L, st);
+    default: return launch_stage_planes(static_cast<const float*>(src), pl, L, st);
+  }
+}
+
+// `cat` (NCHW) or, when `planes` is set, its staged planes (fuseconv_stage).
+int fuseconv_fwd_any(const void* cat, const void* planes, size_t planes_bytes, const void* packed,
+                     const void* bias, void* out, int n, int cin, int cout, int h, int w, int dt,
+                     cudaStream_t st) {
   int rc = check_conv(n, cin, cout, h, w, dt);
   if (rc) return rc;
-  DDPM_CHECK_ARG(cat && packed && out, "null pointer");
+  DDPM_CHECK_ARG((cat || planes) && packed && out, "null pointer");
   int* status = nullptr;
   rc = gencat::status_ptr(&status);
   if (rc) return rc;
@@ -545,16 +718,37 @@ int fuseconv_fwd(const void* cat, const void* packed, const void* bias, void* ou
   q.reg_part = (uint32_t)L.KC * kRows * kSeg * 2;
   q.reg_bytes = q.reg_part * L.parts;
   q.reg_bufs = 3;
-  q.w_chunk = (uint32_t)L.fwd_chunk;
-  q.w_stages = 16;
-  return dispatch_dt(dt, false, q, st);
+  q.w_chunk = (uint32_t)(9 * L.fwd_chunk);  // a slab's 9 tap images per chunk
+  q.w_tap = (uint32_t)L.fwd_chunk;
+  q.w_stages = 3;
+  FcMaps maps{};
+  if (planes != nullptr) {
+    rc = plane_map(&maps, planes, planes_bytes, n, cin, h, w, dt, L.KC);
+    if (rc) return rc;
+  }
+  return dispatch_dt(dt, false, planes != nullptr, q, maps, st);
 }
 
-int fuseconv_dgrad(const void* gout, const void* packed, void* gcat, int n, int cin, int cout,
-                   int h, int w, int dt, cudaStream_t st) {
+int fuseconv_fwd(const void* cat, const void* packed, const void* bias, void* out, int n, int cin,
+                 int cout, int h, int w, int dt, cudaStream_t st) {
+  return fuseconv_fwd_any(cat, nullptr, 0, packed, bias, out, n, cin, cout, h, w, dt, st);
+}
+
+int fuseconv_fwd_staged(const void* planes, size_t planes_bytes, const void* packed,
+                        const void* bias, void* out, int n, int cin, int cout, int h, int w, int dt,
+                        cudaStream_t st) {
+  DDPM_CHECK_ARG(planes, "null pointer");
+  return fuseconv_fwd_any(nullptr, planes, planes_bytes, packed, bias, out, n, cin, cout, h, w, dt,
+                          st);
+}
+
+// `gout` (NCHW) or, when `planes` is set, its staged planes (fuseconv_stage).
+int fuseconv_dgrad_any(const void* gout, const void* planes, size_t planes_bytes,
+                       const void* packed, void* gcat, int n, int cin, int cout, int h, int w,
+                       int dt, cudaStream_t st) {
   int rc = check_conv(n, cin, cout, h, w, dt);
   if (rc) return rc;
-  DDPM_CHECK_ARG(gout && packed && gcat, "null pointer");
+  DDPM_CHECK_ARG((gout || planes) && packed && gcat, "null pointer");
   int* status = nullptr;
   rc = gencat::status_ptr(&status);
   if (rc) return rc;
@@ -573,8 +767,26 @@ int fuseconv_dgrad(const void* gout, const void* packed, void* gcat, int n, int 
   q.reg_bytes = q.reg_part * L.parts;
   q.reg_bufs = 2;
   q.w_chunk = (uint32_t)L.dg_chunk;
+  q.w_tap = (uint32_t)L.dg_chunk;
   q.w_stages = 4;
-  return dispatch_dt(dt, true, q, st);
+  FcMaps maps{};
+  if (planes != nullptr) {
+    rc = plane_map(&maps, planes, planes_bytes, n, cout, h, w, dt, L.KD);
+    if (rc) return rc;
+  }
+  return dispatch_dt(dt, true, planes != nullptr, q, maps, st);
+}
+
+int fuseconv_dgrad(const void* gout, const void* packed, void* gcat, int n, int cin, int cout,
+                   int h, int w, int dt, cudaStream_t st) {
+  return fuseconv_dgrad_any(gout, nullptr, 0, packed, gcat, n, cin, cout, h, w, dt, st);
+}
+
+int fuseconv_dgrad_staged(const void* planes, size_t planes_bytes, const void* packed, void* gcat,
+                          int n, int cin, int cout, int h, int w, int dt, cudaStream_t st) {
+  DDPM_CHECK_ARG(planes, "null pointer");
+  return fuseconv_dgrad_any(nullptr, planes, planes_bytes, packed, gcat, n, cin, cout, h, w, dt,
+                            st);
 }
 
 }  // namespace ddpm

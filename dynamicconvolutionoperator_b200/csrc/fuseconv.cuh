@@ -25,6 +25,20 @@ struct Layout {
   static Layout make(int cin, int cout, int dt);
 };
 
+// Staged source planes of the fuse convolution (input of the forward, output
+// gradient of the data gradient): [part][n][G][Hp][Wp][8 channels] in the MMA
+// operand type (bf16 hi + residual lo parts for FP32), zero padded: plane row
+// i = image row i - 1, plane column j = image column j - 8, channels >= C zero.
+// G covers the channels rounded up to 64, so every K slab of either pass is a
+// whole number of groups. A unit's 4 rows x 144 columns of one slab are then
+// one TMA box per part.
+struct PlaneLayout {
+  int N, C, H, W, G, Hp, Wp, parts;
+  size_t part_bytes;
+  size_t bytes() const { return part_bytes * parts; }
+  static PlaneLayout make(int n, int c, int h, int w, int dt);
+};
+
 }  // namespace fuseconv
 
 size_t fuseconv_pack_bytes(int cin, int cout, int dt);

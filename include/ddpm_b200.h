@@ -244,6 +244,26 @@ DDPM_API int ddpm_fuseconv_fwd(const void* x, const void* packed, const void* bi
 DDPM_API int ddpm_fuseconv_bwd_data(const void* grad_out, const void* packed, void* grad_x,
                                     int n, int cin, int cout, int h, int w, int dtype,
                                     void* stream);
+/*
+ * Staged source planes of the fuse convolution (no counterpart in the
+ * reference, whose cuDNN call reads NCHW directly): ddpm_fuseconv_stage
+ * writes src [N, C, H, W] once as zero-padded channel-group planes in the
+ * tensor-core operand type (ddpm_fuseconv_stage_bytes() bytes, 256-byte
+ * aligned), which the staged entry points then read with one TMA copy per
+ * K slab instead of per-thread loads and register transposes. The forward
+ * stages x (C = cin), the data gradient stages grad_out (C = cout); the
+ * results equal ddpm_fuseconv_fwd / ddpm_fuseconv_bwd_data on the same
+ * inputs bit for bit. The planes are valid while src is unchanged.
+ */
+DDPM_API size_t ddpm_fuseconv_stage_bytes(int n, int c, int h, int w, int dtype);
+DDPM_API int ddpm_fuseconv_stage(const void* src, void* planes, size_t planes_bytes, int n, int c,
+                                 int h, int w, int dtype, void* stream);
+DDPM_API int ddpm_fuseconv_fwd_staged(const void* planes, size_t planes_bytes, const void* packed,
+                                      const void* bias, void* out, int n, int cin, int cout, int h,
+                                      int w, int dtype, void* stream);
+DDPM_API int ddpm_fuseconv_bwd_data_staged(const void* planes, size_t planes_bytes,
+                                           const void* packed, void* grad_x, int n, int cin,
+                                           int cout, int h, int w, int dtype, void* stream);
 /* grad_weight[o, i, ky, kx] = sum_p grad_out[o, p] * x[i, p + (ky-1, kx-1)] and
  * grad_bias[o] = sum_p grad_out[o, p] (grad_bias may be NULL): the cuDNN weight
  * gradient of the same convolution. FP32 split partials in `workspace`

@@ -46,9 +46,26 @@ def _pack(wt, cin, cout, dtype):
     return packed
 
 
+def _stage(src):
+    """src as staged planes (ddpm_fuseconv_stage); filler bytes, so nothing
+    relies on the buffer starting at zero."""
+    from dynamicconvolutionoperator_b200 import _lib
+
+    n, c, h, w = src.shape
+    code = _lib.dtype_code(src.dtype)
+    nbytes = int(_lib.load().ddpm_fuseconv_stage_bytes(n, c, h, w, code))
+    assert nbytes > 0
+    planes = torch.full((nbytes,), 0x5A, dtype=torch.uint8, device="cuda")
+    _lib.call("ddpm_fuseconv_stage", src.data_ptr(), planes.data_ptr(), nbytes, n, c, h, w, code,
+              _lib.stream_handle(planes.device))
+    return planes, nbytes
+
+
 @pytest.mark.parametrize("shape", SHAPES)
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 def test_fuseconv_forward(shape, dtype):
+    """Unstaged and staged-plane forward: both within tolerance of float64,
+    and equal to each other bit for bit (same operands, same MMA order)."""
     from dynamicconvolutionoperator_b200 import _lib
 
     n, cin, cout, h, w = shape
@@ -59,10 +76,16 @@ def test_fuseconv_forward(shape, dtype):
     _lib.call("ddpm_fuseconv_fwd", xd.data_ptr(), packed.data_ptr(), bd.data_ptr(),
               out.data_ptr(), n, cin, cout, h, w, _lib.dtype_code(dtype),
               _lib.stream_handle(out.device))
+    planes, nbytes = _stage(xd)
+    out_s = torch.full_like(out, float("nan"))
+    _lib.call("ddpm_fuseconv_fwd_staged", planes.data_ptr(), nbytes, packed.data_ptr(),
+              bd.data_ptr(), out_s.data_ptr(), n, cin, cout, h, w, _lib.dtype_code(dtype),
+              _lib.stream_handle(out.device))
     torch.cuda.synchronize()
     gold = F.conv2d(xd.double(), wd.double(), bd.double(), 1, 1)
     rtol, atol = TOL[dtype]
     torch.testing.assert_close(out.double(), gold, rtol=rtol, atol=atol)
+    torch.testing.assert_close(out_s, out, rtol=0, atol=0)
 
 
 @pytest.mark.parametrize("shape", SHAPES)
@@ -77,10 +100,16 @@ def test_fuseconv_bwd_data(shape, dtype):
     gx = torch.full((n, cin, h, w), float("nan"), dtype=dtype, device="cuda")
     _lib.call("ddpm_fuseconv_bwd_data", gd.data_ptr(), packed.data_ptr(), gx.data_ptr(),
               n, cin, cout, h, w, _lib.dtype_code(dtype), _lib.stream_handle(gx.device))
+    planes, nbytes = _stage(gd)
+    gx_s = torch.full_like(gx, float("nan"))
+    _lib.call("ddpm_fuseconv_bwd_data_staged", planes.data_ptr(), nbytes, packed.data_ptr(),
+              gx_s.data_ptr(), n, cin, cout, h, w, _lib.dtype_code(dtype),
+              _lib.stream_handle(gx.device))
     torch.cuda.synchronize()
     gold = torch.nn.grad.conv2d_input((n, cin, h, w), wd.double(), gd.double(), 1, 1)
     rtol, atol = TOL[dtype]
     torch.testing.assert_close(gx.double(), gold, rtol=rtol, atol=atol)
+    torch.testing.assert_close(gx_s, gx, rtol=0, atol=0)
 
 
 def test_fuseconv_rejects_unsupported():
