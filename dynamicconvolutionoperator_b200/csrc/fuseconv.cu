@@ -101,7 +101,10 @@ struct FcCfg {
   static constexpr int kRounds = (kItems + kProducers * kItemsMax - 1) / (kProducers * kItemsMax);
   static constexpr int kFirstProducerWarp = 3;
   static constexpr int kFirstEpiWarp = kFirstProducerWarp + kProducers / 32;
-  static constexpr int kThreads = 32 * (kFirstEpiWarp + 4);
+  // epilogue warpgroups: the staged variant has the threads for one per output
+  // row (half the stores per thread); otherwise one warpgroup drains both rows
+  static constexpr int kEpiWG = kStaged ? 2 : 1;
+  static constexpr int kThreads = 32 * (kFirstEpiWarp + 4 * kEpiWG);
 };
 
 // kDgrad = false: forward (window of tap (ky, kx) for output row h0 + mh starts
@@ -153,7 +156,7 @@ fuseconv_kernel(const FcParams p, const __grid_constant__ FcMaps maps) {
     }
     for (int i = 0; i < 2; ++i) {
       tc::mbar_init(&t_full[i], 2);
-      tc::mbar_init(&t_empty[i], 128);
+      tc::mbar_init(&t_empty[i], 128 * Cfg::kEpiWG);
     }
     tc::fence_mbar_init();
     abort_s = 0;
@@ -334,7 +337,8 @@ fuseconv_kernel(const FcParams p, const __grid_constant__ FcMaps maps) {
       }
     }
   } else {
-    // ---- epilogue (128 threads): both output rows of a unit ------------------
+    // ---- epilogue: warpgroup ewg drains output rows ewg, ewg + kEpiWG ---------
+    const int ewg = (warp - Cfg::kFirstEpiWarp) >> 2;
     const int quad = warp & 3;
     const int m = quad * 32 + lane;
     const float* bias_s = reinterpret_cast<const float*>(smem + L.bias);
@@ -355,7 +359,7 @@ fuseconv_kernel(const FcParams p, const __grid_constant__ FcMaps maps) {
       tc::tc_fence_after();
       const int c0 = half * Nn;
 #pragma unroll 1
-      for (int mh = 0; mh < 2; ++mh) {
+      for (int mh = ewg; mh < 2; mh += Cfg::kEpiWG) {
         const int h = 2 * hp + mh;
         const bool ok = h < H && w < W;
         const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + tb * 256 + mh * 128;
