@@ -48,7 +48,8 @@ constexpr int kDkBytes = kTileM * 128 * 2;  // one dK tile part (bf16 / fp16)
 template <typename T, typename Op, bool kSplit, int KS, int OCT, int J0 = 0, int JN = 8>
 __device__ __forceinline__ void build_octet(uint8_t* dk, const float4* xc, int xr_plane,
                                             const unsigned long long (&gv)[3][8],
-                                            const int (&dil)[3], int m) {
+                                            const int (&dil)[3], int m,
+                                            uint32_t lo_off = kDkBytes) {
   constexpr int KK = KS * KS;
   constexpr int r = KS / 2;
   const uint32_t base = (m >> 3) * 2048 + (m & 7) * 16;
@@ -74,8 +75,8 @@ __device__ __forceinline__ void build_octet(uint8_t* dk, const float4* xc, int x
     const unsigned long long lo8[4] = {prod[0], prod[1], prod[2], prod[3]};
     const unsigned long long hi8[4] = {prod[4], prod[5], prod[6], prod[7]};
     const uint32_t off = base + (j * 2) * 128;
-    store8x2_split<Op, kSplit>(dk + off, dk + kDkBytes + off, lo8);
-    store8x2_split<Op, kSplit>(dk + off + 128, dk + kDkBytes + off + 128, hi8);
+    store8x2_split<Op, kSplit>(dk + off, dk + lo_off + off, lo8);
+    store8x2_split<Op, kSplit>(dk + off + 128, dk + lo_off + off + 128, hi8);
   }
 }
 
@@ -92,13 +93,15 @@ __device__ __forceinline__ void build_dk(uint8_t* dk, int octet, const float4* x
 }
 
 // Half of an octet (slots 4*half .. 4*half+3): two builder threads per pixel.
+// lo_off: bytes from a slot's hi part to its lo part (FP32).
 template <typename T, typename Op, bool kSplit, int KS>
 __device__ __forceinline__ void build_dk_half(uint8_t* dk, int octet, int half, const float4* xc,
                                               int xr_plane, const unsigned long long (&gv)[3][8],
-                                              const int (&dil)[3], int m) {
+                                              const int (&dil)[3], int m,
+                                              uint32_t lo_off = kDkBytes) {
 #define DDPM_BUILD_CASE(O, H)                                                           \
   case O * 2 + H:                                                                       \
-    build_octet<T, Op, kSplit, KS, O, H * 4, 4>(dk, xc, xr_plane, gv, dil, m);          \
+    build_octet<T, Op, kSplit, KS, O, H * 4, 4>(dk, xc, xr_plane, gv, dil, m, lo_off);  \
     break;
   switch (octet * 2 + half) {
     DDPM_BUILD_CASE(0, 0)
@@ -108,7 +111,7 @@ __device__ __forceinline__ void build_dk_half(uint8_t* dk, int octet, int half, 
     DDPM_BUILD_CASE(2, 0)
     DDPM_BUILD_CASE(2, 1)
     DDPM_BUILD_CASE(3, 0)
-    default: build_octet<T, Op, kSplit, KS, 3, 4, 4>(dk, xc, xr_plane, gv, dil, m); break;
+    default: build_octet<T, Op, kSplit, KS, 3, 4, 4>(dk, xc, xr_plane, gv, dil, m, lo_off); break;
   }
 #undef DDPM_BUILD_CASE
 }
@@ -718,15 +721,25 @@ __global__ void gencat_wreduce_kernel(const float* __restrict__ partial, T* __re
 // by one TMA copy per tile, one tile ahead, into a single buffer the builders
 // release as soon as they hold the values in registers; otherwise each builder
 // loads its pixel's 48 values from global memory at the start of the tile.
-template <typename T, int KS, bool kStaged = false, bool kGTmaArg = false>
+//
+// FP32 with kLoRing: the dK hi part is double buffered and the lo part single
+// buffered; both issuers run an octet's MMAs with the lo operand first and
+// release the lo buffer then, so the next octet's build starts after a third
+// of the current octet's MMAs instead of after all of them (with one 64 KB
+// slot, build and MMAs alternated). The weight ring holds one part (16 KB)
+// per stage, 3 stages, to pay for the extra 32 KB.
+template <typename T, int KS, bool kStaged = false, bool kGTmaArg = false,
+          bool kLoRingArg = false>
 struct DywCfg {
   static constexpr bool kSplit = IoTraits<T>::kSplit;
   static constexpr bool kGTma = kGTmaArg;
+  static constexpr bool kLoRing = kLoRingArg;
+  static_assert(!kLoRing || kSplit, "the lo ring is for the FP32 split operands");
   static constexpr int kParts = kSplit ? 2 : 1;
-  static constexpr int kDkSlots = kSplit ? 1 : 2;
+  static constexpr int kDkSlots = kSplit ? (kLoRing ? 2 : 1) : 2;  // lo ring: hi slots
   static constexpr int kXBufs = kSplit ? 1 : 2;  // at most; DywParams::nx is the count used
   static constexpr int kYBufs = kSplit ? 1 : 2;
-  static constexpr int kWStages = 2;
+  static constexpr int kWStages = kLoRing ? 3 : 2;
   static constexpr int kProducers = 128;
   static constexpr int kXItems = (16 * (kTileH + 2 * kMaxHalo) + kProducers - 1) / kProducers;
   static constexpr int kYItems = (16 * 80 + kProducers - 1) / kProducers;
@@ -744,22 +757,23 @@ struct DywSmem {
 // and (kGTma) the gradient tile [branch][channel][8 rows][16 px].
 // C=64, K=3, halo 5: fp32 36 + 40 + 64 + 2x32 KB = 204 KB;
 // bf16 2x36 + 2x20 + 2x32 + 2x16 (+ 12) KB = 208 (220) KB.
-template <typename T, int KS, bool kGTma = false>
+template <typename T, int KS, bool kGTma = false, bool kLoRing = false>
 __host__ __device__ inline DywSmem dyw_smem_layout(int Cp, int Nw, int R, int nx) {
-  using Cfg = DywCfg<T, KS>;
+  using Cfg = DywCfg<T, KS, false, kGTma, kLoRing>;
   DywSmem L;
   L.xr_bytes = (uint32_t)16 * (kTileH + 2 * R) * kHaloCols * 4;
   L.y_bytes = (uint32_t)Cfg::kParts * kTileM * Nw * 2;
-  L.dk_bytes = (uint32_t)Cfg::kParts * kDkBytes;
-  L.w_bytes = (uint32_t)Cfg::kParts * 128 * Cp * 2;
+  // lo ring: dk_bytes / w_bytes are one part; the lo buffer follows the hi slots
+  L.dk_bytes = (uint32_t)(kLoRing ? 1 : Cfg::kParts) * kDkBytes;
+  L.w_bytes = (uint32_t)(kLoRing ? 1 : Cfg::kParts) * 128 * Cp * 2;
   L.g_bytes = kGTma ? (uint32_t)(3 * 16 * kTileM * sizeof(T)) : 0u;
   L.xr = 0;
   L.y = L.xr + nx * L.xr_bytes;
   L.dk = L.y + Cfg::kYBufs * L.y_bytes;
-  L.w = L.dk + Cfg::kDkSlots * L.dk_bytes;
+  L.w = L.dk + (Cfg::kDkSlots + (kLoRing ? 1 : 0)) * L.dk_bytes;
   L.g = L.w + Cfg::kWStages * L.w_bytes;
   L.bars = L.g + L.g_bytes;
-  L.total = L.bars + 8 * (4 + 2 * Cfg::kYBufs + 2 * Cfg::kDkSlots + 2 * Cfg::kWStages + 7);
+  L.total = L.bars + 8 * (4 + 2 * Cfg::kYBufs + 2 * Cfg::kDkSlots + 2 * Cfg::kWStages + 9);
   return L;
 }
 
@@ -818,10 +832,10 @@ __device__ __forceinline__ bool drain_dy(const DywParams& p, uint32_t it, int sp
   return true;
 }
 
-template <typename T, int KS, bool kStaged, bool kGTma>
-__global__ void __launch_bounds__(DywCfg<T, KS, kStaged, kGTma>::kThreads, 1)
+template <typename T, int KS, bool kStaged, bool kGTma, bool kLoRing>
+__global__ void __launch_bounds__(DywCfg<T, KS, kStaged, kGTma, kLoRing>::kThreads, 1)
 gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
-  using Cfg = DywCfg<T, KS, kStaged, kGTma>;
+  using Cfg = DywCfg<T, KS, kStaged, kGTma, kLoRing>;
   using Op = typename IoTraits<T>::Op;
   constexpr int NS = Cfg::kDkSlots;
   const int NX = Cfg::kXBufs == 1 ? 1 : p.nx;  // 1 or 2: index = xq & (NX-1), lap = xq >> (NX-1)
@@ -835,7 +849,7 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
 
   const int C = p.C, Cp = p.Cp, H = p.H, W = p.W, R = p.R, Nw = p.Nw;
   const size_t P = (size_t)H * W;
-  const DywSmem L = dyw_smem_layout<T, KS, kGTma>(Cp, Nw, R, NX);
+  const DywSmem L = dyw_smem_layout<T, KS, kGTma, kLoRing>(Cp, Nw, R, NX);
   const int cg = blockIdx.x % p.ncg;
   const int split = blockIdx.x / p.ncg;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
@@ -852,6 +866,8 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
   uint64_t* w_done = d_empty + 2;      // [1]
   uint64_t* g_full = w_done + 1;       // [1] (kGTma)
   uint64_t* g_empty = g_full + 1;      // [1] (kGTma)
+  uint64_t* lo_full = g_empty + 1;     // [1] (kLoRing: the lo buffer)
+  uint64_t* lo_empty = lo_full + 1;    // [1]
   const int xr_rows = kTileH + 2 * R;
   const int xr_plane = xr_rows * kHaloCols;
   const int warp = threadIdx.x >> 5;
@@ -885,6 +901,8 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
     tc::mbar_init(w_done, 1);
     tc::mbar_init(g_full, 1);
     tc::mbar_init(g_empty, 8);
+    tc::mbar_init(lo_full, 256);
+    tc::mbar_init(lo_empty, 2);
     tc::fence_mbar_init();
     abort_s = 0;
   }
@@ -899,16 +917,23 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
     if (lane == 0) {
       const uint8_t* wsrc = static_cast<const uint8_t*>(p.wpack);
       uint32_t wq = 0;
+      // a group's image is both parts back to back; the lo ring streams them
+      // as separate stages (hi, then lo)
+      constexpr int kLoads = kLoRing ? 2 : 1;
+      const size_t w_group = (size_t)Cfg::kParts * 128 * Cp * 2;
       for (int tile = split; tile < p.num_tiles; tile += p.splits) {
-        for (int oct = 0; oct < NOCT; ++oct, ++wq) {
-          const int s = wq % S;
-          if (!tc::mbar_wait(&w_empty[s], ((wq / S) & 1) ^ 1, abort_flag, kWaitNs)) {
-            fail(abort_flag, p.status, 50);
-            goto done;
+        for (int oct = 0; oct < NOCT; ++oct) {
+          for (int part = 0; part < kLoads; ++part, ++wq) {
+            const int s = wq % S;
+            if (!tc::mbar_wait(&w_empty[s], ((wq / S) & 1) ^ 1, abort_flag, kWaitNs)) {
+              fail(abort_flag, p.status, 50);
+              goto done;
+            }
+            tc::mbar_arrive_expect_tx(&w_full[s], L.w_bytes);
+            tc::bulk_g2s(smem + L.w + s * L.w_bytes,
+                         wsrc + (size_t)(cg * NOCT + oct) * w_group + (size_t)part * L.w_bytes,
+                         L.w_bytes, &w_full[s]);
           }
-          tc::mbar_arrive_expect_tx(&w_full[s], L.w_bytes);
-          tc::bulk_g2s(smem + L.w + s * L.w_bytes,
-                       wsrc + (size_t)(cg * NOCT + oct) * L.w_bytes, L.w_bytes, &w_full[s]);
         }
       }
     }
@@ -928,6 +953,50 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
         }
         tc::tc_fence_after();
         const uint32_t dt = tmem_base + Cfg::kDyCol + tb * 64;
+        if constexpr (kLoRing) {
+          // per octet: lo * W_hi, release lo; hi * W_hi; hi * W_lo
+          const uint64_t lo_d =
+              tc::smem_desc(tc::smem_u32(smem + L.dk + 2 * kDkBytes), 128, 2048);
+          for (int oct = 0; oct < NOCT; ++oct, ++kq) {
+            const int hb = kq & 1;
+            const int s_hi = wq % S;
+            if (!tc::mbar_wait(&k_full[hb], (kq >> 1) & 1, abort_flag, kWaitNs) ||
+                !tc::mbar_wait(lo_full, kq & 1, abort_flag, kWaitNs) ||
+                !tc::mbar_wait(&w_full[s_hi], (wq / S) & 1, abort_flag, kWaitNs)) {
+              fail(abort_flag, p.status, 52);
+              goto done;
+            }
+            tc::tc_fence_after();
+            const uint64_t hi_d =
+                tc::smem_desc(tc::smem_u32(smem + L.dk + hb * kDkBytes), 128, 2048);
+            const uint64_t bh = tc::smem_desc(tc::smem_u32(smem + L.w + s_hi * L.w_bytes), b_lbo, 128);
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks)
+              tc::mma_f16(dt, lo_d + ks * (256 >> 4), bh + ks * b_step, idesc,
+                          (oct > 0 || ks > 0) ? 1u : 0u);
+            tc::mma_commit(lo_empty);
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks)
+              tc::mma_f16(dt, hi_d + ks * (256 >> 4), bh + ks * b_step, idesc, 1u);
+            tc::mma_commit(&w_empty[s_hi]);
+            ++wq;
+            const int s_lo = wq % S;
+            if (!tc::mbar_wait(&w_full[s_lo], (wq / S) & 1, abort_flag, kWaitNs)) {
+              fail(abort_flag, p.status, 52);
+              goto done;
+            }
+            tc::tc_fence_after();
+            const uint64_t bl = tc::smem_desc(tc::smem_u32(smem + L.w + s_lo * L.w_bytes), b_lbo, 128);
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks)
+              tc::mma_f16(dt, hi_d + ks * (256 >> 4), bl + ks * b_step, idesc, 1u);
+            tc::mma_commit(&w_empty[s_lo]);
+            ++wq;
+            tc::mma_commit(&k_empty[hb]);
+          }
+          tc::mma_commit(&d_full[tb]);
+          continue;
+        }
         for (int oct = 0; oct < NOCT; ++oct, ++wq, ++kq) {
           const int s = wq % S, ks_ = kq % NS;
           if (!tc::mbar_wait(&k_full[ks_], (kq / NS) & 1, abort_flag, kWaitNs) ||
@@ -977,6 +1046,39 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
         tc::tc_fence_after();
         const uint64_t yd =
             tc::smem_desc(tc::smem_u32(smem + L.y + yb * L.y_bytes), b_lbo, b_sbo);
+        if constexpr (kLoRing) {
+          // per octet: lo * y_hi, release lo; hi * y_hi + hi * y_lo
+          const uint64_t lo_d =
+              tc::smem_desc(tc::smem_u32(smem + L.dk + 2 * kDkBytes), 2048, 128);
+          for (int oct = 0; oct < NOCT; ++oct, ++kq) {
+            const int hb = kq & 1;
+            if (!tc::mbar_wait(&k_full[hb], (kq >> 1) & 1, abort_flag, kWaitNs) ||
+                !tc::mbar_wait(lo_full, kq & 1, abort_flag, kWaitNs)) {
+              fail(abort_flag, p.status, 54);
+              goto done;
+            }
+            tc::tc_fence_after();
+            const uint64_t hi_d =
+                tc::smem_desc(tc::smem_u32(smem + L.dk + hb * kDkBytes), 2048, 128);
+            const uint32_t dt = tmem_base + oct * Nw;
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks)
+              tc::mma_f16(dt, lo_d + ks * ((2 * 2048) >> 4), yd + ks * b_step, idesc,
+                          (!first || ks > 0) ? 1u : 0u);
+            tc::mma_commit(lo_empty);
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks) {
+              const uint64_t a_k = hi_d + ks * ((2 * 2048) >> 4);
+              const uint64_t b_k = yd + ks * b_step;
+              tc::mma_f16(dt, a_k, b_k, idesc, 1u);
+              tc::mma_f16(dt, a_k, b_k + y_lo, idesc, 1u);
+            }
+            tc::mma_commit(&k_empty[hb]);
+          }
+          tc::mma_commit(&y_empty[yb]);
+          first = false;
+          continue;
+        }
         for (int oct = 0; oct < NOCT; ++oct, ++kq) {
           const int ks_ = kq % NS;
           if (!tc::mbar_wait(&k_full[ks_], (kq / NS) & 1, abort_flag, kWaitNs)) {
@@ -1159,15 +1261,19 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
                          (mr + R) * kHaloCols + (mc + 8);
       for (int oct = 0; oct < NOCT; ++oct, ++kq) {
         const int ks_ = kq % NS;
-        if (!warp_wait(&k_empty[ks_], ((kq / NS) & 1) ^ 1, abort_flag)) {
+        if (!warp_wait(&k_empty[ks_], ((kq / NS) & 1) ^ 1, abort_flag) ||
+            (kLoRing && !warp_wait(lo_empty, (kq & 1) ^ 1, abort_flag))) {
           fail(abort_flag, p.status, 58);
           failed = true;
           break;
         }
+        // lo ring: hi part in slot ks_, lo part in the buffer after both slots
+        const uint32_t lo_off = kLoRing ? (uint32_t)(2 - ks_) * kDkBytes : (uint32_t)kDkBytes;
         build_dk_half<T, Op, Cfg::kSplit, KS>(smem + L.dk + ks_ * L.dk_bytes, oct, half, xc,
-                                              xr_plane, gv, dil, m);
+                                              xr_plane, gv, dil, m, lo_off);
         tc::fence_proxy_async_smem();
         tc::mbar_arrive(&k_full[ks_]);
+        if constexpr (kLoRing) tc::mbar_arrive(lo_full);
       }
       if (failed) break;
       tc::mbar_arrive(&x_empty[xb]);
@@ -1291,11 +1397,11 @@ DywPlan plan_dyw(int n, int c, int h, int w, int ks) {
   return q;
 }
 
-template <typename T, int KS, bool kStaged, bool kGTma>
+template <typename T, int KS, bool kStaged, bool kGTma, bool kLoRing = false>
 int launch_dyw_k(const DywParams& prm, const DywMaps& maps, cudaStream_t st) {
-  using Cfg = DywCfg<T, KS, kStaged, kGTma>;
-  const DywSmem L = dyw_smem_layout<T, KS, kGTma>(prm.Cp, prm.Nw, prm.R, prm.nx);
-  auto fn = gencat_bwd_dyw_kernel<T, KS, kStaged, kGTma>;
+  using Cfg = DywCfg<T, KS, kStaged, kGTma, kLoRing>;
+  const DywSmem L = dyw_smem_layout<T, KS, kGTma, kLoRing>(prm.Cp, prm.Nw, prm.R, prm.nx);
+  auto fn = gencat_bwd_dyw_kernel<T, KS, kStaged, kGTma, kLoRing>;
   DDPM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total));
   fn<<<prm.ncg * prm.splits, Cfg::kThreads, L.total, st>>>(prm, maps);
   DDPM_CHECK_LAUNCH("gencat_bwd_dyw_kernel");
@@ -1315,6 +1421,12 @@ int launch_dyw(DywParams prm, const DywMaps& maps, bool staged, bool g_tma, cuda
           prm.nx = nx;
           return launch_dyw_k<T, KS, true, true>(prm, maps, st);
         }
+  } else {
+    // FP32: the lo ring where it fits (halos up to 5 at C = 64)
+    if (staged && (int)dyw_smem_layout<T, KS, false, true>(prm.Cp, prm.Nw, prm.R, 1).total <= lim) {
+      prm.nx = 1;
+      return launch_dyw_k<T, KS, true, false, true>(prm, maps, st);
+    }
   }
   for (int nx = kMaxX; nx >= 1; --nx)
     if ((int)dyw_smem_layout<T, KS>(prm.Cp, prm.Nw, prm.R, nx).total <= lim) {
