@@ -295,16 +295,18 @@ def load_peaks():
 # None where no capture exists. Outputs still resident in L2 when a captured
 # launch ends are not counted as writes.
 NCU_TRAFFIC_BYTES: dict[tuple[str, str], float] = {
-    ("gencat_fwd", "torch.float32"): 68869376,
-    ("gencat_fwd", "torch.bfloat16"): 20539648,
-    ("gencat_bwd_x", "torch.float32"): 98812928,
-    ("gencat_bwd_x", "torch.bfloat16"): 43686400,
-    ("gencat_bwd_yw", "torch.float32"): 112307456,
-    ("gencat_bwd_yw", "torch.bfloat16"): 63030272,
-    ("fuseconv_fwd", "torch.float32"): 70899456,
-    ("fuseconv_fwd", "torch.bfloat16"): 33924096,
-    ("fuseconv_dgrad", "torch.float32"): 26112512,
-    ("fuseconv_dgrad", "torch.bfloat16"): 8797184,
+    # staged paths: the main kernel only (the staging copies are HBM-bound
+    # passes of their own, profiles/staging_256.md)
+    ("gencat_fwd", "torch.float32"): 63058944,
+    ("gencat_fwd", "torch.bfloat16"): 32418048,
+    ("gencat_bwd_x", "torch.float32"): 91352320,
+    ("gencat_bwd_x", "torch.bfloat16"): 45780224,
+    ("gencat_bwd_yw", "torch.float32"): 114652928,
+    ("gencat_bwd_yw", "torch.bfloat16"): 73122816,
+    ("fuseconv_fwd", "torch.float32"): 75615744,
+    ("fuseconv_fwd", "torch.bfloat16"): 36270848,
+    ("fuseconv_dgrad", "torch.float32"): 27409920,
+    ("fuseconv_dgrad", "torch.bfloat16"): 9356288,
     # dout pre-pass + TMA main kernel (the split reduction is not captured)
     ("fuseconv_wgrad", "torch.float32"): 16783872 + 89954560,
     ("fuseconv_wgrad", "torch.bfloat16"): 8395264 + 42037760,
