@@ -479,8 +479,9 @@ constexpr int kPlaneCols = 64;   // plane columns per block
 constexpr int kPlaneChans = 64;  // channels per block
 
 // Block = (n, plane row, 64-column strip, 64-channel chunk): 8-pixel vector
-// loads of one channel, a padded shared tile transposes, each thread writes
-// 16-byte rows of 8 channels (consecutive threads = consecutive columns).
+// loads of one channel, a shared tile (68-float rows: 16-byte aligned vector
+// stores, conflict-free column reads) transposes, each thread writes 16-byte
+// rows of 8 channels (consecutive threads = consecutive columns).
 template <typename T>
 __global__ void __launch_bounds__(256) stage_planes_kernel(const T* __restrict__ src,
                                                            uint4* __restrict__ hi,
@@ -488,7 +489,7 @@ __global__ void __launch_bounds__(256) stage_planes_kernel(const T* __restrict__
                                                            const fuseconv::PlaneLayout L) {
   using Op = typename IoTraits<T>::Op;
   constexpr bool kSplit = IoTraits<T>::kSplit;
-  __shared__ float tile[kPlaneChans][kPlaneCols + 1];
+  __shared__ __align__(16) float tile[kPlaneChans][kPlaneCols + 4];
   const int ni = blockIdx.x, n = ni / L.Hp, i = ni - n * L.Hp;
   const int hr = i - 1;                      // image row (may be outside the image)
   const int j0 = blockIdx.y * kPlaneCols;    // first plane column
@@ -501,8 +502,9 @@ __global__ void __launch_bounds__(256) stage_planes_kernel(const T* __restrict__
       v = load_raw8<T>(src + ((size_t)n * L.C + c) * P, L.H, L.W, hr, j0 - 8 + g * 8);
     else
       v.zero();
-#pragma unroll
-    for (int e = 0; e < 8; ++e) tile[cl][g * 8 + e] = v.get(e);
+    float4* row = reinterpret_cast<float4*>(&tile[cl][g * 8]);
+    row[0] = make_float4(v.get(0), v.get(1), v.get(2), v.get(3));
+    row[1] = make_float4(v.get(4), v.get(5), v.get(6), v.get(7));
   }
   __syncthreads();
   for (int idx = threadIdx.x; idx < (kPlaneChans / 8) * kPlaneCols; idx += blockDim.x) {

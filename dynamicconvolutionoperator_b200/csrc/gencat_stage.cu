@@ -16,9 +16,10 @@ constexpr int kStageCols = 64;               // plane columns per block
 constexpr int kStageChannels = kMaxChannels + 16;  // G*8 <= round16(64 + 1)
 
 // Block = (n, plane row, 64-column strip). Loads: 8 lanes read 8-pixel
-// vectors covering 64 contiguous columns of one channel; a padded shared tile
-// transposes; each thread writes 16-byte rows of 8 channels (consecutive
-// lanes = consecutive columns).
+// vectors covering 64 contiguous columns of one channel; a shared tile with a
+// 68-float row pitch (16-byte aligned rows for the vector stores, column
+// reads still conflict-free) transposes; each thread writes 16-byte rows of
+// 8 channels (consecutive lanes = consecutive columns).
 template <typename T>
 __global__ void __launch_bounds__(256) stage_y_kernel(const T* __restrict__ y,
                                                       uint4* __restrict__ hi,
@@ -26,7 +27,7 @@ __global__ void __launch_bounds__(256) stage_y_kernel(const T* __restrict__ y,
                                                       const StageLayout L) {
   using Op = typename IoTraits<T>::Op;
   constexpr bool kSplit = IoTraits<T>::kSplit;
-  __shared__ float tile[kStageChannels][kStageCols + 1];
+  __shared__ __align__(16) float tile[kStageChannels][kStageCols + 4];
   const int ni = blockIdx.x, n = ni / L.Hp, i = ni - n * L.Hp;
   const int hr = i - L.ph;                // image row (may be outside the image)
   const int j0 = blockIdx.y * kStageCols;  // first plane column of the block
@@ -41,8 +42,9 @@ __global__ void __launch_bounds__(256) stage_y_kernel(const T* __restrict__ y,
       v.ones();
     else
       v.zero();
-#pragma unroll
-    for (int e = 0; e < 8; ++e) tile[c][g * 8 + e] = v.get(e);
+    float4* row = reinterpret_cast<float4*>(&tile[c][g * 8]);
+    row[0] = make_float4(v.get(0), v.get(1), v.get(2), v.get(3));
+    row[1] = make_float4(v.get(4), v.get(5), v.get(6), v.get(7));
   }
   __syncthreads();
   for (int idx = threadIdx.x; idx < L.G * kStageCols; idx += blockDim.x) {
@@ -67,18 +69,28 @@ __global__ void __launch_bounds__(256) stage_x_kernel(const T* __restrict__ x,
                                                       const StageLayout L) {
   const size_t P = (size_t)L.H * L.W;
   const size_t cells = (size_t)L.N * L.Cq * P;
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < cells;
-       i += (size_t)gridDim.x * blockDim.x) {
-    const size_t pix = i % P;
-    const size_t nq = i / P;
-    const int q = (int)(nq % L.Cq), n = (int)(nq / L.Cq);
-    float v[4];
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  // four cells per thread per round, all loads issued before the stores
+  for (size_t i0 = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i0 < cells; i0 += 4 * stride) {
+    float v[4][4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int c = 4 * q + k;
-      v[k] = c < L.C ? to_f32<T>(__ldg(x + ((size_t)n * L.C + c) * P + pix)) : 0.f;
+    for (int r = 0; r < 4; ++r) {
+      const size_t i = i0 + r * stride;
+      const size_t pix = i % P;
+      const size_t nq = i / P;
+      const int q = (int)(nq % L.Cq), n = (int)(nq / L.Cq);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int c = 4 * q + k;
+        v[r][k] = (i < cells && c < L.C) ? to_f32<T>(__ldg(x + ((size_t)n * L.C + c) * P + pix))
+                                         : 0.f;
+      }
     }
-    xp[i] = make_float4(v[0], v[1], v[2], v[3]);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const size_t i = i0 + r * stride;
+      if (i < cells) xp[i] = make_float4(v[r][0], v[r][1], v[r][2], v[r][3]);
+    }
   }
 }
 
@@ -91,7 +103,7 @@ int launch_stage(const T* x, const T* y, uint8_t* staged, const StageLayout& L, 
   DDPM_CHECK_LAUNCH("stage_y_kernel");
   if (x != nullptr) {
     const size_t cells = (size_t)L.N * L.Cq * L.H * L.W;
-    size_t blocks = (cells + 255) / 256;
+    size_t blocks = (cells + 4 * 256 - 1) / (4 * 256);  // four cells per thread
     if (blocks > 65535u * 8u) blocks = 65535u * 8u;
     stage_x_kernel<T><<<(unsigned)blocks, 256, 0, st>>>(
         x, reinterpret_cast<float4*>(staged + L.x_offset), L);
