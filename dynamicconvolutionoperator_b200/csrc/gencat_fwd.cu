@@ -47,7 +47,8 @@
 // issuer, w2-w5 = y-tile producers, w6-w9 = x-halo producers, w10-w17 = two
 // epilogue warpgroups; slot number s (counted over the CTA's tiles) belongs
 // to warpgroup s % 2, which consumes its slots in order from its own ring of
-// TMEM buffers. Each producer thread issues all of its loads for a tile before
+// TMEM buffers. With staged operands (16 warps): one warp per producer role
+// and three epilogue warpgroups (slot s -> warpgroup s % 3). Each producer thread issues all of its loads for a tile before
 // its first shared-memory store, so a tile costs one memory latency, not
 // several; each epilogue thread issues the three TMEM loads of a chunk before
 // a single wait. With staged operands (gencat_stage.cu) one thread per
@@ -72,14 +73,17 @@ struct FwdCfg {
   static constexpr int kN = kBr * KS * KS * 16;               // accumulator columns per slot
   static constexpr int kRows = 3 * KS * KS * 16;              // weight rows of a channel group
   static constexpr int kNumBuf = (512 / kN) > 8 ? 8 : (512 / kN);
-  // Each epilogue warpgroup owns kNumBuf / 2 TMEM buffers: every buffer has a
-  // single consumer that sees all of its phases in order.
-  static constexpr int kBufPerWG = kNumBuf / 2;
-  static_assert(kBufPerWG >= 1, "two TMEM slots must fit");
+  // Epilogue warpgroups: slot s belongs to warpgroup s % kEpiWG. With staged
+  // operands each producer role is one warp, which leaves the threads for a
+  // third warpgroup: the epilogue (the bound of this kernel) then drains three
+  // slots at once. Each warpgroup owns kNumBuf / kEpiWG TMEM buffers: every
+  // buffer has a single consumer that sees all of its phases in order.
+  static constexpr int kEpiWG = kStaged ? 3 : 2;
+  static constexpr int kBufPerWG = kNumBuf / kEpiWG;
+  static_assert(kBufPerWG >= 1, "a TMEM slot per epilogue warpgroup must fit");
   static constexpr int kYBufs = kSplit ? 1 : 2;               // smem budget (see layout)
   static constexpr bool kBiasInGemm = !kSplit;
-  static constexpr int kEpiWG = 2;
-  static constexpr int kProducers = 128;                      // threads per producer role
+  static constexpr int kProducers = kStaged ? 32 : 128;       // threads per producer role
   static constexpr int kFirstEpiWarp = 2 + 2 * (kProducers / 32);
   static constexpr int kThreads = 32 * (kFirstEpiWarp + 4 * kEpiWG);
   // loads per producer thread and tile (whole tile in one batch)
@@ -243,9 +247,9 @@ gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
             kStaged ? tc::smem_desc(tc::smem_u32(smem + L.y + yb * L.y_bytes), kTileM * 16, 128)
                     : tc::smem_desc(tc::smem_u32(smem + L.y + yb * L.y_bytes), 128, Ck * 16);
         for (int q = 0; q < Cfg::kSlots; ++q, ++tq) {
-          // slot tq belongs to epilogue warpgroup tq % 2 (its (tq / 2)-th slot)
-          const uint32_t own = tq >> 1;
-          const int j = (tq & 1) * Cfg::kBufPerWG + own % Cfg::kBufPerWG;
+          // slot tq belongs to epilogue warpgroup tq % kEpiWG (its own-th slot)
+          const uint32_t own = tq / Cfg::kEpiWG;
+          const int j = (int)(tq % Cfg::kEpiWG) * Cfg::kBufPerWG + own % Cfg::kBufPerWG;
           if (!tc::mbar_wait(&t_empty[j], ((own / Cfg::kBufPerWG) & 1) ^ 1, abort_flag,
                              kWaitNs)) {
             fail(abort_flag, p.status, 12);
@@ -365,8 +369,8 @@ gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
       const float4* xc = xr + (mr + R) * kHaloCols + (mc + 8);
       bool failed = false;
       for (int q = 0; q < Cfg::kSlots && !failed; ++q, ++tq) {
-        if ((tq & 1) != (uint32_t)wg) continue;  // the other warpgroup's slot
-        const uint32_t own = tq >> 1;
+        if (tq % Cfg::kEpiWG != (uint32_t)wg) continue;  // another warpgroup's slot
+        const uint32_t own = tq / Cfg::kEpiWG;
         const int j = wg * Cfg::kBufPerWG + own % Cfg::kBufPerWG;
         if (!warp_wait(&t_full[j], (own / Cfg::kBufPerWG) & 1, abort_flag)) {
           fail(abort_flag, p.status, 14);
