@@ -243,20 +243,21 @@ def measure_dtype(args, dtype, device, rank, world, dist, timed_clocks=False):
 
     # ---- end to end through the public API: H2D inputs, fwd+bwd, D2H loss ----
     # x and y are copied on the compute stream (the forward starts with them);
-    # the upstream gradient g is copied on a side stream that starts after the
-    # step's first event and overlaps the forward, as a training loop's input
-    # pipeline would; the compute stream waits for it before the loss, so every
-    # copy lies inside the timed region.
+    # the upstream gradient g is copied on a side stream that starts once those
+    # two copies are done (sharing the PCIe link with them would only delay the
+    # forward) and overlaps the forward, as a training loop's input pipeline
+    # would; the compute stream waits for it before the loss, so every copy
+    # lies inside the timed region.
     host_loss = torch.empty((), dtype=torch.float32).pin_memory()
     copy_stream = torch.cuda.Stream(device)
 
     def e2e_step():
         zero()
+        xe = hx.to(device, non_blocking=True)
+        ye = hy.to(device, non_blocking=True)
         copy_stream.wait_stream(stream)
         with torch.cuda.stream(copy_stream):
             ge = hg.to(device, non_blocking=True)
-        xe = hx.to(device, non_blocking=True)
-        ye = hy.to(device, non_blocking=True)
         x_ = xe.detach().requires_grad_(True)
         y_ = ye.detach().requires_grad_(True)
         out = model(x_, y_)
