@@ -151,14 +151,17 @@ def make_inputs(batch, dtype, rank):
 def step_fn(model, x, y, g, allreduce):
     # x and y take part in autograd (dX and dY are computed), as in the
     # reference's training benchmarks (gpu_bench.py:275-300).
+    # g is the upstream gradient of the module output (d loss / d out for
+    # loss = <out, g>): backward starts from it directly, and the loss value
+    # read back to the host is the one dot product
     x = x.detach().requires_grad_(True)
     y = y.detach().requires_grad_(True)
     out = model(x, y)
-    loss = (out.float() * g.float()).sum()
-    loss.backward()
+    out.backward(g)
     if allreduce is not None:
         allreduce()
-    return loss
+    with torch.no_grad():
+        return torch.dot(out.reshape(-1), g.reshape(-1)).float()
 
 
 def time_steps(run, steps, flush, stream):
@@ -263,11 +266,12 @@ def measure_dtype(args, dtype, device, rank, world, dist, timed_clocks=False):
         out = model(x_, y_)
         stream.wait_stream(copy_stream)
         ge.record_stream(stream)
-        loss = (out.float() * ge.float()).sum()
-        loss.backward()
+        out.backward(ge)
         if allreduce is not None:
             allreduce()
-        host_loss.copy_(loss.detach(), non_blocking=True)
+        with torch.no_grad():
+            loss = torch.dot(out.reshape(-1), ge.reshape(-1)).float()
+        host_loss.copy_(loss, non_blocking=True)
 
     for _ in range(3):
         e2e_step()
