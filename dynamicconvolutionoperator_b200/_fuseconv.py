@@ -128,10 +128,9 @@ class _FuseConv(torch.autograd.Function):
 def fuse_conv(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None) -> torch.Tensor:
     """``F.conv2d(x, weight, bias, 1, 1)`` for a 3x3 weight on the native kernels."""
     _lib.load()
-    grad = torch.is_grad_enabled() and (
-        x.requires_grad or weight.requires_grad or (bias is not None and bias.requires_grad)
-    )
-    return _FuseConv.apply(x, weight, bias, not grad)
+    # the packed weight is cached per weight version, except while a CUDA
+    # graph is captured (a cache hit would leave the pack out of the graph)
+    return _FuseConv.apply(x, weight, bias, not torch.cuda.is_current_stream_capturing())
 
 
 __all__ = ["fuse_conv", "fuse_conv_supported", "pack_fuse_weight"]

@@ -143,9 +143,10 @@ def pack_generator_weight(weight: torch.Tensor, bias: torch.Tensor, channels: in
     operand layout (all three images: forward, dX and dY).
 
     With ``use_cache`` the packed copy is reused while ``weight`` and ``bias``
-    (same tensor objects, same in-place version counters) are unchanged;
-    autograd and CUDA-graph paths pack on every call so a captured step repacks
-    updated weights.
+    (same tensor objects, same in-place version counters) are unchanged, so an
+    optimizer's in-place update repacks on the next call. Calls made while a
+    CUDA graph is being captured pack every time: a cache hit there would leave
+    the pack out of the graph, and its replays would keep the old weights.
     """
     w2 = weight.reshape(weight.shape[0], -1).contiguous()
     b1 = bias.contiguous()
@@ -223,7 +224,8 @@ class _GeneratorDynamicCat(torch.autograd.Function):
     def forward(ctx, x, y, weight, bias, kernel_size, dilations):
         x, y, bias = _prepare(x, y, weight, bias, kernel_size, dilations)
         with torch.cuda.device(x.device):
-            packed = pack_generator_weight(weight, bias, x.shape[1], kernel_size, use_cache=False)
+            packed = pack_generator_weight(weight, bias, x.shape[1], kernel_size,
+                                           use_cache=not torch.cuda.is_current_stream_capturing())
             staged = _stage_operands(x, y, kernel_size, dilations)
             out = _launch_gencat_fwd(x, y, packed, bias, kernel_size, dilations, staged)
         ctx.save_for_backward(x, y, weight, bias)

@@ -98,3 +98,85 @@ def test_cudnn_fuse_path_training(dtype, ks):
     stats, fails = ddpm_parity((2, 24, 15, 17), ks, dtype, seed=7, input_seed=8,
                                native_fuse=False)
     _assert_ok(stats, fails)
+
+
+def _training_step(model, x, y, g):
+    for p in model.parameters():
+        p.grad = None
+    xi = x.detach().requires_grad_(True)
+    yi = y.detach().requires_grad_(True)
+    out = model(xi, yi)
+    out.backward(g)
+    return [out.detach().clone(), xi.grad.clone(), yi.grad.clone()] + [
+        p.grad.clone() for p in model.parameters()]
+
+
+def _update_in_place(model):
+    with torch.no_grad():
+        for p in model.parameters():
+            p.mul_(0.75).add_(0.01)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_weight_update_between_steps_repacks(dtype):
+    """The packed weight copies are cached per weight version: after an
+    in-place update (what an optimizer step does) the next training step must
+    use the new weights, exactly like a module built with them."""
+    from dynamicconvolutionoperator_b200 import DDPM
+
+    torch.manual_seed(3)
+    a = DDPM(32, 3, fused_generator_training=True).cuda().to(dtype)
+    b = DDPM(32, 3, fused_generator_training=True).cuda().to(dtype)
+    b.load_state_dict(a.state_dict())
+    gen = torch.Generator().manual_seed(4)
+    x, y, g = (torch.randn((1, 32, 24, 40), generator=gen).to(dtype).cuda() for _ in range(3))
+    _training_step(a, x, y, g)
+    _update_in_place(a)
+    _update_in_place(b)
+    got = _training_step(a, x, y, g)
+    ref = _training_step(b, x, y, g)
+    # dY is summed across CTAs with FP32 atomics (order not fixed), hence a small
+    # tolerance; stale weights (scaled by 0.75) would be far outside it
+    tol = 1e-5 if dtype == torch.float32 else 1.6e-2
+    for u, v in zip(got, ref):
+        torch.testing.assert_close(u.float(), v.float(), rtol=tol, atol=tol)
+
+
+def test_graph_replay_sees_weight_updates():
+    """A training step captured in a CUDA graph repacks the weights on every
+    replay (nothing packed is cached at capture), so a replay after an
+    in-place weight update matches an eager step with the new weights."""
+    from dynamicconvolutionoperator_b200 import DDPM
+
+    torch.manual_seed(5)
+    model = DDPM(32, 3, fused_generator_training=True).cuda()
+    fresh = DDPM(32, 3, fused_generator_training=True).cuda()
+    gen = torch.Generator().manual_seed(6)
+    x, y, g = (torch.randn((1, 32, 24, 40), generator=gen).cuda() for _ in range(3))
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            _training_step(model, x, y, g)
+    torch.cuda.current_stream().wait_stream(side)
+    for p in model.parameters():
+        p.grad = None
+    graph = torch.cuda.CUDAGraph()
+    xi = x.detach().requires_grad_(True)
+    yi = y.detach().requires_grad_(True)
+    with torch.cuda.graph(graph):
+        out = model(xi, yi)
+        out.backward(g)
+    _update_in_place(model)
+    fresh.load_state_dict(model.state_dict())
+    for p in model.parameters():
+        p.grad.zero_()
+    xi.grad.zero_()
+    yi.grad.zero_()
+    graph.replay()
+    torch.cuda.synchronize()
+    got = [out.detach(), xi.grad, yi.grad] + [p.grad for p in model.parameters()]
+    ref = _training_step(fresh, x, y, g)
+    for u, v in zip(got, ref):
+        torch.testing.assert_close(u, v, rtol=1e-5, atol=1e-5)
+    del graph
