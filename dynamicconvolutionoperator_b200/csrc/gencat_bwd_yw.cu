@@ -1310,9 +1310,29 @@ done:
 // dY (16-bit) = the FP32 accumulator rounded once.
 template <typename T>
 __global__ void gy_convert_kernel(const float* __restrict__ acc, T* __restrict__ gy, size_t n) {
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
-       i += (size_t)gridDim.x * blockDim.x)
-    gy[i] = from_f32<T>(acc[i]);
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  const size_t i0 = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  size_t done = 0;
+  if ((reinterpret_cast<uintptr_t>(gy) & 7u) == 0) {
+    // four elements per step: one 16-byte load, one 8-byte store
+    const size_t n4 = n / 4;
+    const float4* a4 = reinterpret_cast<const float4*>(acc);
+    uint2* g4 = reinterpret_cast<uint2*>(gy);
+    for (size_t i = i0; i < n4; i += stride) {
+      const float4 v = a4[i];
+      union {
+        uint2 u;
+        T e[4];
+      } o;
+      o.e[0] = from_f32<T>(v.x);
+      o.e[1] = from_f32<T>(v.y);
+      o.e[2] = from_f32<T>(v.z);
+      o.e[3] = from_f32<T>(v.w);
+      g4[i] = o.u;
+    }
+    done = n4 * 4;
+  }
+  for (size_t i = done + i0; i < n; i += stride) gy[i] = from_f32<T>(acc[i]);
 }
 
 // ------------------------------------------------------------- launchers ----
@@ -1444,7 +1464,7 @@ int finish_dyw(const DywParams& prm, void* gy, void* gw, void* gb, int c, int ks
   if (rc) return rc;
   if constexpr (!std::is_same<T, float>::value) {
     const size_t nel = (size_t)prm.N * c * prm.H * prm.W;
-    const size_t want = (nel + 255) / 256;
+    const size_t want = (nel / 4 + 255) / 256 + 1;
     gy_convert_kernel<T><<<(int)(want < 4096 ? want : 4096), 256, 0, st>>>(
         prm.gy_acc, static_cast<T*>(gy), nel);
     DDPM_CHECK_LAUNCH("gy_convert_kernel");
