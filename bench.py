@@ -395,22 +395,25 @@ def library_kernels(model, x, y, dtype, device):
     _lib.call("ddpm_gencat_stage", x.data_ptr(), y.data_ptr(), sy.data_ptr(), sy_bytes, n, C, H,
               W, K, *DILATIONS, code, sh)
 
+    # as in the step: the generator forward also writes the fuse conv's staged
+    # planes of its output (C % 8 == 0), so the fuse forward needs no staging
+    fp_bytes = int(_lib.load().ddpm_fuseconv_stage_bytes(n, 4 * C, H, W, code))
+    fplanes = torch.empty(fp_bytes, dtype=torch.uint8, device=device)
+
     def fwd():
         _lib.call("ddpm_gencat_stage", x.data_ptr(), y.data_ptr(), sy.data_ptr(), sy_bytes, n, C,
                   H, W, K, *DILATIONS, code, sh)
-        _lib.call("ddpm_gencat_fwd_staged", sy.data_ptr(), sy_bytes, packed.data_ptr(),
-                  gen_b.data_ptr(), out2.data_ptr(), n, C, H, W, K, *DILATIONS, code, sh)
+        _lib.call("ddpm_gencat_fwd_staged_planes", sy.data_ptr(), sy_bytes, packed.data_ptr(),
+                  gen_b.data_ptr(), out2.data_ptr(), fplanes.data_ptr(), fp_bytes,
+                  n, C, H, W, K, *DILATIONS, code, sh)
 
-    # fuse conv as in the step: the source staged as operand planes, then the
-    # staged kernel (both timed together)
-    fp_bytes = int(_lib.load().ddpm_fuseconv_stage_bytes(n, 4 * C, H, W, code))
-    fplanes = torch.empty(fp_bytes, dtype=torch.uint8, device=device)
+    # fuse conv as in the step: the data gradient stages grad_out as operand
+    # planes (timed with it); the forward reads the planes the generator wrote
+    fwd()
     gp_bytes = int(_lib.load().ddpm_fuseconv_stage_bytes(n, C, H, W, code))
     gplanes = torch.empty(gp_bytes, dtype=torch.uint8, device=device)
 
     def fuse_fwd():
-        _lib.call("ddpm_fuseconv_stage", out.data_ptr(), fplanes.data_ptr(), fp_bytes, n, 4 * C,
-                  H, W, code, sh)
         _lib.call("ddpm_fuseconv_fwd_staged", fplanes.data_ptr(), fp_bytes, fpacked.data_ptr(),
                   fuse_b.data_ptr(), fout.data_ptr(), n, 4 * C, C, H, W, code, sh)
 

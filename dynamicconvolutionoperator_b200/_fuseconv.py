@@ -25,6 +25,7 @@ import weakref
 import torch
 
 from . import _lib
+from ._kernels import FUSE_PLANES_ATTR
 
 FUSE_MAX_CIN = 256
 FUSE_MAX_COUT = 64
@@ -81,14 +82,15 @@ def _stage_planes(src: torch.Tensor) -> tuple[torch.Tensor, int]:
 
 class _FuseConv(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, weight, bias, use_cache):
+    def forward(ctx, x, weight, bias, use_cache, planes_in):
         x = x.contiguous()
         n, cin, h, w = x.shape
         cout = weight.shape[0]
         packed = pack_fuse_weight(weight, use_cache)
         out = torch.empty((n, cout, h, w), dtype=x.dtype, device=x.device)
         b = bias.contiguous() if bias is not None else None
-        planes, nbytes = _stage_planes(x)
+        # the producer's own planes of x when it wrote them, else one staging pass
+        planes, nbytes = planes_in if planes_in is not None else _stage_planes(x)
         _lib.call("ddpm_fuseconv_fwd_staged", planes.data_ptr(), nbytes, packed.data_ptr(),
                   b.data_ptr() if b is not None else None, out.data_ptr(),
                   n, cin, cout, h, w, _lib.dtype_code(x.dtype), _lib.stream_handle(x.device))
@@ -122,15 +124,24 @@ class _FuseConv(torch.autograd.Function):
                       _lib.stream_handle(x.device))
             if not ctx.needs_input_grad[1]:
                 gw = None
-        return gx, gw, gb, None
+        return gx, gw, gb, None, None
 
 
 def fuse_conv(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None) -> torch.Tensor:
     """``F.conv2d(x, weight, bias, 1, 1)`` for a 3x3 weight on the native kernels."""
     _lib.load()
+    # Staged planes written by the producer of x (the fused generator forward),
+    # valid while x is unmodified; taken off x so they are freed after use.
+    planes_in = None
+    held = getattr(x, FUSE_PLANES_ATTR, None)
+    if held is not None:
+        delattr(x, FUSE_PLANES_ATTR)
+        if held[2] == x._version and x.is_contiguous():
+            planes_in = (held[0], held[1])
     # the packed weight is cached per weight version, except while a CUDA
     # graph is captured (a cache hit would leave the pack out of the graph)
-    return _FuseConv.apply(x, weight, bias, not torch.cuda.is_current_stream_capturing())
+    return _FuseConv.apply(x, weight, bias, not torch.cuda.is_current_stream_capturing(),
+                           planes_in)
 
 
 __all__ = ["fuse_conv", "fuse_conv_supported", "pack_fuse_weight"]

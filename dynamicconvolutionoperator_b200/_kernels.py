@@ -183,17 +183,38 @@ def _stage_operands(x, y, kernel_size, dilations):
     return staged
 
 
-def _launch_gencat_fwd(x, y, packed, bias, kernel_size, dilations, staged=None):
+# Attribute of a cat output that carries its fuse-conv staged planes (written by
+# the forward itself) to the fuse conv: (planes, nbytes, output version).
+FUSE_PLANES_ATTR = "_ddpm_fuse_planes"
+
+
+def _launch_gencat_fwd(x, y, packed, bias, kernel_size, dilations, staged=None,
+                       fuse_planes=False):
+    """The forward output; with ``fuse_planes`` (C % 8 == 0) the forward also
+    writes the output as the fuse conv's staged planes and attaches them to it
+    (``FUSE_PLANES_ATTR``), which saves the fuse conv its staging pass."""
     n, c, h, w = x.shape
     out = torch.empty((n, 4 * c, h, w), dtype=x.dtype, device=x.device)
     d0, d1, d2 = _dil(dilations)
     if staged is None:
         staged = _stage_operands(x, y, kernel_size, dilations)
+    code = _lib.dtype_code(x.dtype)
+    stream = _lib.stream_handle(x.device)
+    if fuse_planes and c % 8 == 0:
+        nbytes = int(_lib.load().ddpm_fuseconv_stage_bytes(n, 4 * c, h, w, code))
+        planes = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
+        _lib.call(
+            "ddpm_gencat_fwd_staged_planes",
+            staged.data_ptr(), staged.numel(), packed.data_ptr(), bias.data_ptr(),
+            out.data_ptr(), planes.data_ptr(), nbytes,
+            n, c, h, w, int(kernel_size), d0, d1, d2, code, stream,
+        )
+        setattr(out, FUSE_PLANES_ATTR, (planes, nbytes, out._version))
+        return out
     _lib.call(
         "ddpm_gencat_fwd_staged",
         staged.data_ptr(), staged.numel(), packed.data_ptr(), bias.data_ptr(), out.data_ptr(),
-        n, c, h, w, int(kernel_size), d0, d1, d2, _lib.dtype_code(x.dtype),
-        _lib.stream_handle(x.device),
+        n, c, h, w, int(kernel_size), d0, d1, d2, code, stream,
     )
     return out
 
@@ -221,13 +242,14 @@ class _GeneratorDynamicCat(torch.autograd.Function):
     ``_triton_kernels.py:911-1053``): saves only ``(x, y, weight, bias)``."""
 
     @staticmethod
-    def forward(ctx, x, y, weight, bias, kernel_size, dilations):
+    def forward(ctx, x, y, weight, bias, kernel_size, dilations, fuse_planes=False):
         x, y, bias = _prepare(x, y, weight, bias, kernel_size, dilations)
         with torch.cuda.device(x.device):
             packed = pack_generator_weight(weight, bias, x.shape[1], kernel_size,
                                            use_cache=not torch.cuda.is_current_stream_capturing())
             staged = _stage_operands(x, y, kernel_size, dilations)
-            out = _launch_gencat_fwd(x, y, packed, bias, kernel_size, dilations, staged)
+            out = _launch_gencat_fwd(x, y, packed, bias, kernel_size, dilations, staged,
+                                     fuse_planes)
         ctx.save_for_backward(x, y, weight, bias)
         ctx.packed = packed
         ctx.staged = staged  # reused by the backward (depends on x and y only)
@@ -283,23 +305,28 @@ class _GeneratorDynamicCat(torch.autograd.Function):
                           n, c, h, w, ks, d0, d1, d2, code, stream)
         gw = grad_w.view_as(weight) if (grad_w is not None and need_w) else None
         gb = grad_b if need_b else None
-        return grad_x, grad_y, gw, gb, None, None
+        return grad_x, grad_y, gw, gb, None, None, None
 
 
-def fused_generator_dynamic_cat(x, y, weight, bias, kernel_size, dilations):
+def fused_generator_dynamic_cat(x, y, weight, bias, kernel_size, dilations, *,
+                                _fuse_planes=False):
     """Fused 1x1 generator + dynamic filter (reference ``_triton_kernels.py:1056-1065``).
 
     Differentiable w.r.t. x, y, weight and bias; without gradients it is a
-    single launch (plus a cached weight packing).
+    single launch (plus a cached weight packing). ``_fuse_planes`` (used by
+    the DDPM module when its native fuse conv consumes the output) has the
+    forward also write the fuse conv's staged planes.
     """
     if torch.is_grad_enabled() and any(t.requires_grad for t in (x, y, weight, bias)):
-        return _GeneratorDynamicCat.apply(x, y, weight, bias, kernel_size, dilations)
+        return _GeneratorDynamicCat.apply(x, y, weight, bias, kernel_size, dilations,
+                                          _fuse_planes)
     x, y, bias = _prepare(x, y, weight, bias, kernel_size, dilations)
     with torch.cuda.device(x.device):
         capturing = torch.cuda.is_current_stream_capturing()
         packed = pack_generator_weight(weight, bias, x.shape[1], kernel_size,
                                        use_cache=not capturing)
-        return _launch_gencat_fwd(x, y, packed, bias, kernel_size, dilations)
+        return _launch_gencat_fwd(x, y, packed, bias, kernel_size, dilations,
+                                  fuse_planes=_fuse_planes)
 
 
 __all__ = ["fused_dynamic_cat", "fused_generator_dynamic_cat"]

@@ -51,6 +51,10 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _c_int,
         [_c_ptr, _c_size, _c_ptr, _c_ptr, _c_ptr] + [_c_int] * 4 + [_c_int] * 5 + [_c_ptr],
     ),
+    "ddpm_gencat_fwd_staged_planes": (
+        _c_int,
+        [_c_ptr, _c_size] + [_c_ptr] * 4 + [_c_size] + [_c_int] * 4 + [_c_int] * 5 + [_c_ptr],
+    ),
     "ddpm_gencat_bwd_x": (
         _c_int,
         [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr] + [_c_int] * 4 + [_c_int] * 5 + [_c_ptr],

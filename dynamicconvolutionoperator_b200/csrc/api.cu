@@ -40,6 +40,10 @@ int gencat_pack(const void* w, const void* bias, int c, int ks, int dt, void* pa
 int gencat_fwd(const void* x, const void* y, const void* staged, size_t staged_bytes,
                const void* wpack, const void* bias, void* out, int n, int c, int h, int w,
                int ks, int d0, int d1, int d2, int dt, cudaStream_t st);
+int gencat_fwd_ex(const void* x, const void* y, const void* staged, size_t staged_bytes,
+                  const void* wpack, const void* bias, void* out, void* planes,
+                  size_t planes_bytes, int n, int c, int h, int w, int ks, int d0, int d1,
+                  int d2, int dt, cudaStream_t st);
 
 int gencat_bwd_x(const void* y, const void* staged, size_t staged_bytes, const void* wpack,
                  const void* bias, const void* gout, void* gx, int n, int c, int h, int w, int ks,
@@ -130,6 +134,17 @@ int ddpm_gencat_fwd(const void* x, const void* y, const void* packed, const void
   ddpm::clear_error();
   return ddpm::gencat_fwd(x, y, nullptr, 0, packed, bias, out, n, c, h, w, ksize, d0, d1, d2,
                           dtype, static_cast<cudaStream_t>(stream));
+}
+
+int ddpm_gencat_fwd_staged_planes(const void* staged, size_t staged_bytes, const void* packed,
+                                  const void* bias, void* out, void* planes, size_t planes_bytes,
+                                  int n, int c, int h, int w, int ksize, int d0, int d1, int d2,
+                                  int dtype, void* stream) {
+  ddpm::clear_error();
+  DDPM_CHECK_ARG(staged && planes, "null pointer");
+  return ddpm::gencat_fwd_ex(nullptr, nullptr, staged, staged_bytes, packed, bias, out, planes,
+                             planes_bytes, n, c, h, w, ksize, d0, d1, d2, dtype,
+                             static_cast<cudaStream_t>(stream));
 }
 
 int ddpm_gencat_fwd_staged(const void* staged, size_t staged_bytes, const void* packed,

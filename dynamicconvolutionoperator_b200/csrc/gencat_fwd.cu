@@ -58,6 +58,7 @@
 #include "common.cuh"
 #include "tc.cuh"
 #include "gencat.cuh"
+#include "fuseconv.cuh"
 
 namespace ddpm {
 namespace {
@@ -128,8 +129,21 @@ struct FwdParams {
   int tiles_w, tiles_h, num_tiles;
   int ncg, per_cg;    // channel groups; CTAs per channel group
   int nxb;            // x-halo buffers (1 or 2)
+  // optional: the output also written as the fuse convolution's staged planes
+  // (fuseconv::PlaneLayout of 4C channels; null = off; needs C % 8 == 0)
+  uint8_t* planes;
+  size_t pl_part;     // bytes per part (FP32: bf16 hi part, then lo part)
+  int pl_G, pl_Hp, pl_Wp;
   int* status;
 };
+
+// One 8-channel, 16-byte plane cell (and the lo cell for FP32) of pixel (h, w).
+template <typename Op, bool kSplit>
+__device__ __forceinline__ void store_plane_cell(const FwdParams& p, int n, int g, int h, int w,
+                                                 const unsigned long long (&pr)[4]) {
+  const size_t off = ((((size_t)n * p.pl_G + g) * p.pl_Hp + (h + 1)) * p.pl_Wp + (w + 8)) * 16;
+  store8x2_split<Op, kSplit>(p.planes + off, p.planes + p.pl_part + off, pr);
+}
 
 // Tensor maps of the staged operands (separate grid-constant parameter).
 struct FwdMaps {
@@ -427,6 +441,17 @@ gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
               if (c < C) on[(size_t)((b + 1) * C + c) * P + pix] = from_f32<T>(a0);
               if (c + 1 < C) on[(size_t)((b + 1) * C + c + 1) * P + pix] = from_f32<T>(a1);
             }
+            if (p.planes != nullptr) {
+              // cat channels (b+1)C + cg*16 .. : whole 8-channel groups (C % 8 == 0)
+#pragma unroll
+              for (int k8 = 0; k8 < 2; ++k8) {
+                if (cg * 16 + 8 * k8 + 8 > C) break;
+                const unsigned long long pr[4] = {acc[4 * k8], acc[4 * k8 + 1], acc[4 * k8 + 2],
+                                                  acc[4 * k8 + 3]};
+                store_plane_cell<Op, Cfg::kSplit>(p, n, ((b + 1) * C + cg * 16) / 8 + k8, h, w,
+                                                  pr);
+              }
+            }
           }
         }
       }
@@ -441,6 +466,16 @@ gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
           for (int k = 0; k < 4; ++k) {
             const int c = cg * 16 + q4 * 4 + k;
             if (c < C) on[(size_t)c * P + pix] = from_f32<T>(e[k]);
+          }
+        }
+        if (p.planes != nullptr) {
+#pragma unroll
+          for (int k8 = 0; k8 < 2; ++k8) {
+            if (cg * 16 + 8 * k8 + 8 > C) break;
+            const float4 v0 = xc[(2 * k8) * xr_plane], v1 = xc[(2 * k8 + 1) * xr_plane];
+            const unsigned long long pr[4] = {f2_pack(v0.x, v0.y), f2_pack(v0.z, v0.w),
+                                              f2_pack(v1.x, v1.y), f2_pack(v1.z, v1.w)};
+            store_plane_cell<Op, Cfg::kSplit>(p, n, 2 * cg + k8, h, w, pr);
           }
         }
       }
@@ -494,13 +529,57 @@ int dispatch(int ks, const FwdParams& prm, const FwdMaps& maps, bool staged, cud
 
 // `staged`: staged operands (gencat::stage with x and y) or null to stage
 // tiles from x and y.
-int gencat_fwd(const void* x, const void* y, const void* staged, size_t staged_bytes,
-               const void* wpack, const void* bias, void* out, int n, int c, int h, int w,
-               int ks, int d0, int d1, int d2, int dt, cudaStream_t st) {
+namespace {
+
+// Zero frame of staged fuse planes whose interior the forward writes: plane
+// rows 0 and Hp-1, plane columns 0..7 and W+8..Wp-1, and channel groups at or
+// beyond `gvalid`. Block = one plane row (part, n, group, row).
+__global__ void __launch_bounds__(128) plane_frame_zero_kernel(uint4* __restrict__ planes,
+                                                               int G, int Hp, int Wp, int W,
+                                                               int gvalid) {
+  const int i = blockIdx.x % Hp;
+  const int g = (blockIdx.x / Hp) % G;
+  uint4* row = planes + (size_t)blockIdx.x * Wp;
+  const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+  if (i == 0 || i == Hp - 1 || g >= gvalid) {
+    for (int j = threadIdx.x; j < Wp; j += blockDim.x) row[j] = z;
+  } else {
+    const int tail = Wp - (W + 8);
+    for (int j = threadIdx.x; j < 8 + tail; j += blockDim.x) row[j < 8 ? j : W + j] = z;
+  }
+}
+
+}  // namespace
+
+// `planes`: optional fuse-conv planes of the output (see FwdParams), or null.
+int gencat_fwd_ex(const void* x, const void* y, const void* staged, size_t staged_bytes,
+                  const void* wpack, const void* bias, void* out, void* planes,
+                  size_t planes_bytes, int n, int c, int h, int w, int ks, int d0, int d1,
+                  int d2, int dt, cudaStream_t st) {
   int rc = gencat::check_shape(n, c, h, w, ks, d0, d1, d2, dt);
   if (rc) return rc;
   DDPM_CHECK_ARG(((x && y) || staged) && wpack && bias && out, "null pointer");
   FwdParams prm{};
+  if (planes != nullptr) {
+    if (c % 8 != 0)
+      return set_error(DDPM_ERR_UNSUPPORTED,
+                       "fuse planes from the forward need C %% 8 == 0 (got %d)", c);
+    const fuseconv::PlaneLayout pl4 = fuseconv::PlaneLayout::make(n, 4 * c, h, w, dt);
+    if (planes_bytes < pl4.bytes())
+      return set_error(DDPM_ERR_WORKSPACE, "fuse planes too small (%zu < %zu)", planes_bytes,
+                       pl4.bytes());
+    DDPM_CHECK_ARG((reinterpret_cast<uintptr_t>(planes) & 255u) == 0,
+                   "fuse planes must be 256-byte aligned");
+    prm.planes = static_cast<uint8_t*>(planes);
+    prm.pl_part = pl4.part_bytes;
+    prm.pl_G = pl4.G;
+    prm.pl_Hp = pl4.Hp;
+    prm.pl_Wp = pl4.Wp;
+    const unsigned rows = (unsigned)(pl4.parts * pl4.N * pl4.G * pl4.Hp);
+    plane_frame_zero_kernel<<<rows, 128, 0, st>>>(static_cast<uint4*>(planes), pl4.G, pl4.Hp,
+                                                  pl4.Wp, w, (4 * c) / 8);
+    DDPM_CHECK_LAUNCH("plane_frame_zero_kernel");
+  }
   prm.x = x;
   prm.y = y;
   prm.wpack = wpack;
@@ -543,6 +622,13 @@ int gencat_fwd(const void* x, const void* y, const void* staged, size_t staged_b
     case DDPM_F32: return dispatch<float>(ks, prm, maps, use_staged, st);
   }
   return set_error(DDPM_ERR_INVALID_ARG, "unknown dtype %d", dt);
+}
+
+int gencat_fwd(const void* x, const void* y, const void* staged, size_t staged_bytes,
+               const void* wpack, const void* bias, void* out, int n, int c, int h, int w,
+               int ks, int d0, int d1, int d2, int dt, cudaStream_t st) {
+  return gencat_fwd_ex(x, y, staged, staged_bytes, wpack, bias, out, nullptr, 0, n, c, h, w, ks,
+                       d0, d1, d2, dt, st);
 }
 
 }  // namespace ddpm

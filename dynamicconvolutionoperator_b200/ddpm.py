@@ -118,8 +118,10 @@ class DDPM(nn.Module):
             )
         return bool(requested) and _kernels.fused_training_supported(self.kernel_size)
 
-    def _cuda_cat(self, x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
-        """GPU path selection (replaces ``DDPM._cuda_cat``, ``triton_impl.py:305-348``)."""
+    def _cuda_cat(self, x: torch.Tensor, y: torch.Tensor, fuse_planes: bool = False) -> torch.Tensor:
+        """GPU path selection (replaces ``DDPM._cuda_cat``, ``triton_impl.py:305-348``).
+        ``fuse_planes``: the native fuse conv will consume the output, so the
+        fused forward may also write it as the fuse conv's staged planes."""
         grad = torch.is_grad_enabled()
         fuse_training = grad and self._use_fused_training(x)
         want_fused = (self.fused_generator_inference and not grad) or fuse_training
@@ -131,6 +133,7 @@ class DDPM(nn.Module):
                 self.generator.bias,
                 self.kernel_size,
                 self.dilations,
+                _fuse_planes=fuse_planes,
             )
         kernels = self.generator(y).reshape(
             x.shape[0],
@@ -149,13 +152,10 @@ class DDPM(nn.Module):
                 "DDPM (B200 build) runs on CUDA tensors only; got tensors on "
                 f"{x.device}. The reference's CPU paths are not part of this build."
             )
-        cat_out = self._cuda_cat(x, y)
         fuse = self.fuse
-        if (
-            self.native_fuse
-            and not _autocast_enabled()
-            and _fuseconv.fuse_conv_supported(cat_out, fuse.weight, fuse.bias)
-        ):
+        native = self.native_fuse and not _autocast_enabled()
+        cat_out = self._cuda_cat(x, y, fuse_planes=native and fuse.weight.dtype == x.dtype)
+        if native and _fuseconv.fuse_conv_supported(cat_out, fuse.weight, fuse.bias):
             return _fuseconv.fuse_conv(cat_out, fuse.weight, fuse.bias)
         if (
             cat_out.dtype in (torch.bfloat16, torch.float16)

@@ -143,6 +143,22 @@ DDPM_API int ddpm_gencat_fwd_staged(const void* staged, size_t staged_bytes,
                                     void* stream);
 
 /*
+ * ddpm_gencat_fwd_staged that also writes its output as the staged planes of
+ * the fuse convolution that consumes it (no counterpart in the reference,
+ * whose cuDNN conv reads the NCHW output): `planes` is laid out as
+ * ddpm_fuseconv_stage would write it for src = out (C = 4c channels,
+ * ddpm_fuseconv_stage_bytes(n, 4c, h, w, dtype) bytes, 256-byte aligned) and
+ * holds the same bytes, so ddpm_fuseconv_fwd_staged can use it directly and
+ * the separate staging pass over the output is saved. `out` is written as
+ * well. Requires c % 8 == 0 (-2 otherwise).
+ */
+DDPM_API int ddpm_gencat_fwd_staged_planes(const void* staged, size_t staged_bytes,
+                                           const void* packed, const void* bias, void* out,
+                                           void* planes, size_t planes_bytes, int n, int c,
+                                           int h, int w, int ksize, int d0, int d1, int d2,
+                                           int dtype, void* stream);
+
+/*
  * Fused generator backward: input gradient dX, recomputing the taps.
  * Replaces `_generator_dynamic_cat_bwd_x` (reference `_triton_kernels.py:430-531`):
  *   grad_x[c,q] = grad_out[c,q]

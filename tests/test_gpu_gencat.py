@@ -105,3 +105,49 @@ def test_gencat_multiple_tiles_per_cta():
     gold = orc.fused_generator_cat(x, y, wt, b, 3, quantize=True)
     rtol, atol = TOL[torch.bfloat16]
     torch.testing.assert_close(out.float().cpu(), gold.float(), rtol=rtol, atol=atol)
+
+
+@pytest.mark.parametrize("shape", [(2, 24, 15, 17), (1, 64, 48, 48), (3, 40, 33, 30),
+                                   (1, 8, 1, 1), (1, 16, 9, 130)])
+@pytest.mark.parametrize("ks", [1, 3])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_gencat_forward_writes_fuse_planes(shape, ks, dtype):
+    """ddpm_gencat_fwd_staged_planes: the same output as ddpm_gencat_fwd_staged,
+    and planes byte-identical to ddpm_fuseconv_stage of that output (padding
+    frame included: both buffers start as filler bytes)."""
+    from dynamicconvolutionoperator_b200 import _kernels, _lib
+
+    x, y, wt, b = _case(shape, ks, dtype, seed=9)
+    n, c, h, w = shape
+    xd, yd, wd, bd = x.cuda(), y.cuda(), wt.cuda(), b.cuda()
+    lib = _lib.load()
+    code = _lib.dtype_code(dtype)
+    st = _lib.stream_handle(xd.device)
+    packed = _kernels.pack_generator_weight(wd, bd, c, ks, use_cache=False)
+    sb = int(lib.ddpm_gencat_stage_bytes(n, c, h, w, ks, 1, 3, 5, code))
+    staged = torch.empty(sb, dtype=torch.uint8, device="cuda")
+    _lib.call("ddpm_gencat_stage", xd.data_ptr(), yd.data_ptr(), staged.data_ptr(), sb,
+              n, c, h, w, ks, 1, 3, 5, code, st)
+    ref = torch.full((n, 4 * c, h, w), float("nan"), dtype=dtype, device="cuda")
+    _lib.call("ddpm_gencat_fwd_staged", staged.data_ptr(), sb, packed.data_ptr(), bd.data_ptr(),
+              ref.data_ptr(), n, c, h, w, ks, 1, 3, 5, code, st)
+    pb = int(lib.ddpm_fuseconv_stage_bytes(n, 4 * c, h, w, code))
+    planes = torch.full((pb,), 0x5A, dtype=torch.uint8, device="cuda")
+    out = torch.full_like(ref, float("nan"))
+    _lib.call("ddpm_gencat_fwd_staged_planes", staged.data_ptr(), sb, packed.data_ptr(),
+              bd.data_ptr(), out.data_ptr(), planes.data_ptr(), pb,
+              n, c, h, w, ks, 1, 3, 5, code, st)
+    gold = torch.full((pb,), 0xA5, dtype=torch.uint8, device="cuda")
+    _lib.call("ddpm_fuseconv_stage", ref.data_ptr(), gold.data_ptr(), pb, n, 4 * c, h, w, code, st)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(out, ref, rtol=0, atol=0, equal_nan=True)
+    assert torch.equal(planes, gold)
+
+
+def test_gencat_forward_fuse_planes_rejects_ragged_channels():
+    """The planes variant needs whole 8-channel groups per branch (C % 8 == 0)."""
+    from dynamicconvolutionoperator_b200 import _lib
+
+    rc = _lib.load().ddpm_gencat_fwd_staged_planes(1, 1, 1, 1, 1, 256, 1 << 20, 1, 3, 8, 8, 3,
+                                                    1, 3, 5, 0, None)
+    assert rc == -2
