@@ -106,13 +106,26 @@ class _FuseConv(torch.autograd.Function):
         n, cin, h, w = x.shape
         cout = weight.shape[0]
         gx = gw = gb = None
+        need_b = ctx.has_bias and ctx.needs_input_grad[2]
+        if ctx.needs_input_grad[0] and (ctx.needs_input_grad[1] or need_b):
+            # both in one call: the data gradient reads grad_out from the
+            # channel-last copy the weight gradient makes anyway
+            gx = torch.empty_like(x)
+            gw = torch.empty_like(weight)
+            gb = torch.empty(cout, dtype=x.dtype, device=x.device) if need_b else None
+            nbytes = int(_lib.load().ddpm_fuseconv_bwd_weight_workspace_bytes(n, cin, cout, h, w))
+            ws = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
+            _lib.call("ddpm_fuseconv_bwd", x.data_ptr(), g.data_ptr(), ctx.packed.data_ptr(),
+                      gx.data_ptr(), gw.data_ptr(), gb.data_ptr() if gb is not None else None,
+                      ws.data_ptr(), nbytes, n, cin, cout, h, w, _lib.dtype_code(x.dtype),
+                      _lib.stream_handle(x.device))
+            return gx, (gw if ctx.needs_input_grad[1] else None), gb, None, None
         if ctx.needs_input_grad[0]:
             gx = torch.empty_like(x)
             planes, nbytes = _stage_planes(g)
             _lib.call("ddpm_fuseconv_bwd_data_staged", planes.data_ptr(), nbytes,
                       ctx.packed.data_ptr(), gx.data_ptr(), n, cin, cout, h, w,
                       _lib.dtype_code(x.dtype), _lib.stream_handle(x.device))
-        need_b = ctx.has_bias and ctx.needs_input_grad[2]
         if ctx.needs_input_grad[1] or need_b:
             gw = torch.empty_like(weight)
             gb = torch.empty(cout, dtype=x.dtype, device=x.device) if need_b else None

@@ -93,6 +93,9 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ddpm_fuseconv_bwd_data_staged": (
         _c_int, [_c_ptr, _c_size] + [_c_ptr] * 2 + [_c_int] * 6 + [_c_ptr]
     ),
+    "ddpm_fuseconv_bwd": (
+        _c_int, [_c_ptr] * 7 + [_c_size] + [_c_int] * 6 + [_c_ptr]
+    ),
     "ddpm_fuseconv_bwd_weight_workspace_bytes": (_c_size, [_c_int] * 5),
     "ddpm_fuseconv_bwd_weight": (
         _c_int, [_c_ptr] * 5 + [_c_size] + [_c_int] * 6 + [_c_ptr]

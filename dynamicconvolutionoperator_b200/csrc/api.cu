@@ -70,6 +70,9 @@ int fuseconv_fwd(const void* cat, const void* packed, const void* bias, void* ou
                  int cout, int h, int w, int dt, cudaStream_t st);
 int fuseconv_dgrad(const void* gout, const void* packed, void* gcat, int n, int cin, int cout,
                    int h, int w, int dt, cudaStream_t st);
+int fuseconv_bwd(const void* cat, const void* gout, const void* packed, void* gcat, void* gw,
+                 void* gb, void* ws, size_t ws_bytes, int n, int cin, int cout, int h, int w,
+                 int dt, cudaStream_t st);
 size_t fuseconv_stage_bytes(int n, int c, int h, int w, int dt);
 int fuseconv_stage(const void* src, void* planes, size_t bytes, int n, int c, int h, int w, int dt,
                    cudaStream_t st);
@@ -246,6 +249,15 @@ int ddpm_fuseconv_bwd_data(const void* grad_out, const void* packed, void* grad_
   ddpm::clear_error();
   return ddpm::fuseconv_dgrad(grad_out, packed, grad_x, n, cin, cout, h, w, dtype,
                               static_cast<cudaStream_t>(stream));
+}
+
+int ddpm_fuseconv_bwd(const void* x, const void* grad_out, const void* packed, void* grad_x,
+                      void* grad_weight, void* grad_bias, void* workspace, size_t workspace_bytes,
+                      int n, int cin, int cout, int h, int w, int dtype, void* stream) {
+  ddpm::clear_error();
+  return ddpm::fuseconv_bwd(x, grad_out, packed, grad_x, grad_weight, grad_bias, workspace,
+                            workspace_bytes, n, cin, cout, h, w, dtype,
+                            static_cast<cudaStream_t>(stream));
 }
 
 size_t ddpm_fuseconv_stage_bytes(int n, int c, int h, int w, int dtype) {

@@ -57,6 +57,7 @@ struct FcParams {
   int nhalf;            // dst channel blocks of Nn (data gradient: ceil(Cin / 128))
   int tiles_w, hpairs, num_units;
   int reg_bufs, w_stages;
+  int row_major;        // staged slab order [row][group][px][8] (else [group][row][px][8])
   uint32_t reg_part, reg_bytes;
   uint32_t w_chunk;     // bytes per streamed weight chunk (FcCfg::kTapsPerChunk taps)
   uint32_t w_tap;       // bytes of one (slab, tap) B image within a chunk
@@ -68,6 +69,11 @@ struct FcParams {
 // which lands as the slab operand [KC/8][4 rows][144 px][8 channels].
 struct FcMaps {
   CUtensorMap smap;
+  // row-major slabs (FcParams::row_major): the weight gradient's grad_out
+  // planes [n][h][Cout/8][w][8], one map per part (smap = hi, smap_lo = lo),
+  // dims {16 x 64-bit (8 px), W/8, Cout/8, H, N}, box {16, 18, KC/8, 4, 1},
+  // which lands as [4 rows][KC/8][144 px][8 channels]
+  CUtensorMap smap_lo;
 };
 
 struct FcSmem {
@@ -198,10 +204,12 @@ fuseconv_kernel(const FcParams p, const __grid_constant__ FcMaps maps) {
     if (lane == 0) {
       const int mh = warp - 1;
       const uint32_t idesc = tc::idesc_f16(128, Nn, IoTraits<T>::kBf16, false, false);
-      constexpr uint32_t a_lbo = kRows * kSeg * 16;  // channel-group stride of a slab
+      // channel-group stride of a slab, and the row stride (16-byte units)
+      const uint32_t a_lbo = p.row_major ? kSeg * 16 : kRows * kSeg * 16;
+      const int a_row = p.row_major ? (KC / 8) * kSeg : kSeg;
       const uint32_t b_lbo = Nn * 16;                // channel-group stride of a weight chunk
       // descriptor increments (units of 16 bytes)
-      constexpr uint64_t a_step = (2 * a_lbo) >> 4;  // one K step (16 channels)
+      const uint64_t a_step = (2 * a_lbo) >> 4;      // one K step (16 channels)
       const uint64_t b_step = (2 * b_lbo) >> 4;
       const uint64_t a_lo = p.reg_part >> 4;          // hi -> lo part of the slab
       const uint64_t b_lo = (Nn * KC * 2) >> 4;       // hi -> lo part of a weight chunk
@@ -241,7 +249,7 @@ fuseconv_kernel(const FcParams p, const __grid_constant__ FcMaps maps) {
               const int ky = t / 3, kx = t % 3;
               const int seg = kDgrad ? (mh - ky + 2) : (mh + ky);
               const int col = kDgrad ? (9 - kx) : (7 + kx);
-              const uint64_t ad = a_base + (uint64_t)(seg * kSeg + col);
+              const uint64_t ad = a_base + (uint64_t)(seg * a_row + col);
               const uint64_t bd = bstage + tt * b_tap;
 #pragma unroll
               for (int ks = 0; ks < Cfg::kSteps; ++ks) {
@@ -286,9 +294,14 @@ fuseconv_kernel(const FcParams p, const __grid_constant__ FcMaps maps) {
           if (pt == 0) {
             tc::mbar_arrive_expect_tx(&r_full[rb], p.reg_bytes);
 #pragma unroll
-            for (int part = 0; part < (kSplit ? 2 : 1); ++part)
-              tc::tma_load_5d(reg + part * p.reg_part, &maps.smap, 0, w0 / 16, h0,
-                              sl * (KC / 8), part * p.N + n, &r_full[rb]);
+            for (int part = 0; part < (kSplit ? 2 : 1); ++part) {
+              if (p.row_major)  // 8-px blocks from w0-8, rows from h0-1 (zero outside)
+                tc::tma_load_5d(reg + part * p.reg_part, part ? &maps.smap_lo : &maps.smap, 0,
+                                w0 / 8 - 1, sl * (KC / 8), h0 - 1, n, &r_full[rb]);
+              else
+                tc::tma_load_5d(reg + part * p.reg_part, &maps.smap, 0, w0 / 16, h0,
+                                sl * (KC / 8), part * p.N + n, &r_full[rb]);
+            }
           } else {
             tc::mbar_arrive(&r_full[rb]);
           }
@@ -786,6 +799,51 @@ int fuseconv_dgrad_any(const void* gout, const void* planes, size_t planes_bytes
 int fuseconv_dgrad(const void* gout, const void* packed, void* gcat, int n, int cin, int cout,
                    int h, int w, int dt, cudaStream_t st) {
   return fuseconv_dgrad_any(gout, nullptr, 0, packed, gcat, n, cin, cout, h, w, dt, st);
+}
+
+// Data gradient reading grad_out from the weight gradient's channel-last
+// planes [n][h][Np/8][w][8] (hi, and lo for FP32; W % 8 == 0, 16-byte aligned):
+// one box per slab and part over those planes, so grad_out is not staged a
+// second time. Returns DDPM_ERR_UNSUPPORTED, nothing launched, if a tensor map
+// is rejected.
+int fuseconv_dgrad_rowmajor(const void* hi, const void* lo, const void* packed, void* gcat, int n,
+                            int cin, int cout, int h, int w, int dt, cudaStream_t st) {
+  int rc = check_conv(n, cin, cout, h, w, dt);
+  if (rc) return rc;
+  DDPM_CHECK_ARG(hi && packed && gcat && (dt != DDPM_F32 || lo), "null pointer");
+  DDPM_CHECK_ARG(w % 8 == 0, "row-major grad_out planes need W %% 8 == 0");
+  int* status = nullptr;
+  rc = gencat::status_ptr(&status);
+  if (rc) return rc;
+  const fuseconv::Layout L = fuseconv::Layout::make(cin, cout, dt);
+  FcParams q = common_params(n, h, w, L.nhalf, status);
+  q.wimg = static_cast<const uint8_t*>(packed) + L.fwd_bytes;
+  q.dst = gcat;
+  q.Csrc = cout;
+  q.Cdst = cin;
+  q.KC = L.KD;
+  q.nslab = L.nslabD;
+  q.Nn = 128;
+  q.reg_part = (uint32_t)L.KD * kRows * kSeg * 2;
+  q.reg_bytes = q.reg_part * L.parts;
+  q.reg_bufs = 2;
+  q.w_chunk = (uint32_t)L.dg_chunk;
+  q.w_tap = (uint32_t)L.dg_chunk;
+  q.w_stages = 4;
+  q.row_major = 1;
+  const uint64_t ng = (uint64_t)L.Np / 8;
+  const uint64_t d[5] = {16, (uint64_t)w / 8, ng, (uint64_t)h, (uint64_t)n};
+  const uint64_t s4[4] = {128, (uint64_t)w * 16, ng * w * 16, (uint64_t)h * ng * w * 16};
+  const uint32_t box[5] = {16, 18, (uint32_t)(L.KD / 8), (uint32_t)kRows, 1};
+  FcMaps maps{};
+  for (int part = 0; part < L.parts; ++part) {
+    if (encode_tmap(part ? &maps.smap_lo : &maps.smap, CU_TENSOR_MAP_DATA_TYPE_UINT64, 5,
+                    part ? lo : hi, d, s4, box, CU_TENSOR_MAP_SWIZZLE_NONE) != DDPM_OK) {
+      clear_error();
+      return DDPM_ERR_UNSUPPORTED;
+    }
+  }
+  return dispatch_dt(dt, true, true, q, maps, st);
 }
 
 int fuseconv_dgrad_staged(const void* planes, size_t planes_bytes, const void* packed, void* gcat,

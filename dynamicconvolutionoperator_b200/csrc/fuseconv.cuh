@@ -4,6 +4,8 @@
 #include <cstddef>
 #include <cstdint>
 
+#include <cuda_runtime.h>
+
 namespace ddpm {
 namespace fuseconv {
 
@@ -42,5 +44,9 @@ struct PlaneLayout {
 }  // namespace fuseconv
 
 size_t fuseconv_pack_bytes(int cin, int cout, int dt);
+int fuseconv_dgrad(const void* gout, const void* packed, void* gcat, int n, int cin, int cout,
+                   int h, int w, int dt, cudaStream_t st);
+int fuseconv_dgrad_rowmajor(const void* hi, const void* lo, const void* packed, void* gcat, int n,
+                            int cin, int cout, int h, int w, int dt, cudaStream_t st);
 
 }  // namespace ddpm

@@ -761,10 +761,12 @@ int run_wgrad_reg(const WgParams& prm, void* dw, void* db, cudaStream_t st) {
 
 // Returns DDPM_ERR_UNSUPPORTED (nothing launched) when the driver rejects a
 // tensor map, so the caller can take the register path.
+// With `gcat` set, the data gradient runs between the pre-pass and the main
+// kernel, reading grad_out from the pre-pass's planes (fuseconv_dgrad_rowmajor).
 template <typename T>
 int run_wgrad_tma(const void* cat, const void* gout, void* gw, void* gb, uint8_t* ws,
                   const WtPlan& t, int n, int cin, int cout, int h, int w, int dt, int* status,
-                  cudaStream_t st) {
+                  cudaStream_t st, const void* packed = nullptr, void* gcat = nullptr) {
   using Cfg = WtCfg<T>;
   constexpr int TW = Cfg::kTW;
   const int Np = t.g.Np, ng = Np / 8;
@@ -805,6 +807,12 @@ int run_wgrad_tma(const void* cat, const void* gout, void* gw, void* gb, uint8_t
   fuseconv_dout_pack_kernel<T><<<dim3(n * h, t.strips), 256, 0, st>>>(
       static_cast<const T*>(gout), hi, lo, dbp, h, w, cout, Np);
   DDPM_CHECK_LAUNCH("fuseconv_dout_pack_kernel");
+  if (gcat != nullptr) {
+    int rc = fuseconv_dgrad_rowmajor(hi, lo, packed, gcat, n, cin, cout, h, w, dt, st);
+    if (rc == DDPM_ERR_UNSUPPORTED) rc = fuseconv_dgrad(gout, packed, gcat, n, cin, cout, h, w,
+                                                        dt, st);
+    if (rc) return rc;
+  }
   const size_t smem = (size_t)Cfg::kStages * (Cfg::kABytes + prm.b_stage) +
                       (Cfg::kSplit ? (size_t)Cfg::kRaw * Cfg::kRawBytes : 0) + 1024;
   auto fn = fuseconv_wgrad_tma_kernel<T>;
@@ -832,6 +840,55 @@ size_t fuseconv_wgrad_workspace_bytes(int n, int cin, int cout, int h, int w) {
     if (d > best) best = d;
   }
   return best;
+}
+
+int fuseconv_wgrad(const void* cat, const void* gout, void* gw, void* gb, void* ws, size_t ws_bytes,
+                   int n, int cin, int cout, int h, int w, int dt, cudaStream_t st);
+
+// Data and weight / bias gradient together: with the TMA weight-gradient path
+// the data gradient reads grad_out from the planes the weight gradient's
+// pre-pass writes anyway, instead of staging it separately.
+int fuseconv_bwd(const void* cat, const void* gout, const void* packed, void* gcat, void* gw,
+                 void* gb, void* ws, size_t ws_bytes, int n, int cin, int cout, int h, int w,
+                 int dt, cudaStream_t st) {
+  DDPM_CHECK_ARG(n >= 1 && h >= 1 && w >= 1 && cin >= 1 && cout >= 1, "sizes must be positive");
+  DDPM_CHECK_ARG(dtype_size(dt) > 0, "unknown dtype code %d", dt);
+  if (cin > fuseconv::kMaxCin || cout > fuseconv::kMaxCout)
+    return set_error(DDPM_ERR_UNSUPPORTED, "native fuse conv supports Cin <= %d, Cout <= %d",
+                     fuseconv::kMaxCin, fuseconv::kMaxCout);
+  DDPM_CHECK_ARG(cat && gout && packed && gcat && gw, "null pointer");
+  const size_t need = fuseconv_wgrad_workspace_bytes(n, cin, cout, h, w);
+  if (ws == nullptr || ws_bytes < need)
+    return set_error(DDPM_ERR_WORKSPACE, "workspace too small (%zu < %zu)", ws_bytes, need);
+  DDPM_CHECK_ARG((reinterpret_cast<uintptr_t>(ws) & 255u) == 0, "workspace must be 256-byte aligned");
+  int* status = nullptr;
+  int rc = gencat::status_ptr(&status);
+  if (rc) return rc;
+  const bool aligned =
+      ((reinterpret_cast<uintptr_t>(cat) | reinterpret_cast<uintptr_t>(gout)) & 15u) == 0;
+  if (aligned && wgrad_tma_shape(w)) {
+    uint8_t* wsb = static_cast<uint8_t*>(ws);
+    switch (dt) {
+      case DDPM_BF16:
+        rc = run_wgrad_tma<__nv_bfloat16>(cat, gout, gw, gb, wsb,
+                                          plan_wgrad_tma(n, cin, cout, h, w, 64, false), n, cin,
+                                          cout, h, w, dt, status, st, packed, gcat);
+        break;
+      case DDPM_F16:
+        rc = run_wgrad_tma<__half>(cat, gout, gw, gb, wsb,
+                                   plan_wgrad_tma(n, cin, cout, h, w, 64, false), n, cin, cout, h,
+                                   w, dt, status, st, packed, gcat);
+        break;
+      default:
+        rc = run_wgrad_tma<float>(cat, gout, gw, gb, wsb,
+                                  plan_wgrad_tma(n, cin, cout, h, w, 32, true), n, cin, cout, h, w,
+                                  dt, status, st, packed, gcat);
+    }
+    if (rc != DDPM_ERR_UNSUPPORTED) return rc;
+  }
+  rc = fuseconv_dgrad(gout, packed, gcat, n, cin, cout, h, w, dt, st);
+  if (rc) return rc;
+  return fuseconv_wgrad(cat, gout, gw, gb, ws, ws_bytes, n, cin, cout, h, w, dt, st);
 }
 
 int fuseconv_wgrad(const void* cat, const void* gout, void* gw, void* gb, void* ws, size_t ws_bytes,

@@ -292,6 +292,20 @@ DDPM_API int ddpm_fuseconv_bwd_weight(const void* x, const void* grad_out, void*
                                       void* stream);
 
 /*
+ * Data gradient and weight / bias gradient of the fuse convolution in one call
+ * (no counterpart in the reference, whose cuDNN backward runs them separately):
+ * the results of ddpm_fuseconv_bwd_data and ddpm_fuseconv_bwd_weight with the
+ * same arguments (bit for bit for grad_x). For widths that are a multiple of 8
+ * the data gradient reads grad_out from the channel-last copy the weight
+ * gradient writes into `workspace` anyway, instead of staging it a second
+ * time. Workspace as ddpm_fuseconv_bwd_weight.
+ */
+DDPM_API int ddpm_fuseconv_bwd(const void* x, const void* grad_out, const void* packed,
+                               void* grad_x, void* grad_weight, void* grad_bias, void* workspace,
+                               size_t workspace_bytes, int n, int cin, int cout, int h, int w,
+                               int dtype, void* stream);
+
+/*
  * No-allocation variant of ddpm_gencat_bwd_yw (no counterpart in the
  * reference, whose Triton backward allocates its partials with torch).
  * Same arguments and results minus the workspace: the FP32 dW/db partials

@@ -146,3 +146,39 @@ def test_fuseconv_bwd_weight(shape, dtype):
         scale = gold.abs().max().item() + 1e-12
         err = (got.double() - gold).abs().max().item() / scale
         assert err <= tol, err
+
+
+@pytest.mark.parametrize("shape", SHAPES)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_fuseconv_bwd_combined(shape, dtype):
+    """ddpm_fuseconv_bwd (data + weight/bias gradient in one call; for widths
+    that are a multiple of 8 the data gradient reads grad_out from the weight
+    gradient's channel-last copy) equals ddpm_fuseconv_bwd_data and
+    ddpm_fuseconv_bwd_weight bit for bit."""
+    from dynamicconvolutionoperator_b200 import _lib
+
+    n, cin, cout, h, w = shape
+    x, wt, b, g = _inputs(shape, dtype, seed=2)
+    xd, wd, gd = x.cuda(), wt.cuda(), g.cuda()
+    packed = _pack(wd, cin, cout, dtype)
+    code = _lib.dtype_code(dtype)
+    st = _lib.stream_handle(xd.device)
+    nb = int(_lib.load().ddpm_fuseconv_bwd_weight_workspace_bytes(n, cin, cout, h, w))
+    ws = torch.empty(nb, dtype=torch.uint8, device="cuda")
+    gx_ref = torch.full_like(xd, float("nan"))
+    gw_ref = torch.full_like(wd, float("nan"))
+    gb_ref = torch.full((cout,), float("nan"), dtype=dtype, device="cuda")
+    _lib.call("ddpm_fuseconv_bwd_data", gd.data_ptr(), packed.data_ptr(), gx_ref.data_ptr(),
+              n, cin, cout, h, w, code, st)
+    _lib.call("ddpm_fuseconv_bwd_weight", xd.data_ptr(), gd.data_ptr(), gw_ref.data_ptr(),
+              gb_ref.data_ptr(), ws.data_ptr(), nb, n, cin, cout, h, w, code, st)
+    gx = torch.full_like(gx_ref, float("nan"))
+    gw = torch.full_like(gw_ref, float("nan"))
+    gb = torch.full_like(gb_ref, float("nan"))
+    ws.fill_(0x5A)
+    _lib.call("ddpm_fuseconv_bwd", xd.data_ptr(), gd.data_ptr(), packed.data_ptr(), gx.data_ptr(),
+              gw.data_ptr(), gb.data_ptr(), ws.data_ptr(), nb, n, cin, cout, h, w, code, st)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(gx, gx_ref, rtol=0, atol=0)
+    torch.testing.assert_close(gw, gw_ref, rtol=0, atol=0)
+    torch.testing.assert_close(gb, gb_ref, rtol=0, atol=0)
