@@ -327,8 +327,8 @@ def load_peaks():
 NCU_TRAFFIC_BYTES: dict[tuple[str, str], float] = {
     # staged paths: the main kernel only (the staging copies are HBM-bound
     # passes of their own, profiles/staging_256.md)
-    ("gencat_fwd", "torch.float32"): 61278464,
-    ("gencat_fwd", "torch.bfloat16"): 32018688,
+    ("gencat_fwd", "torch.float32"): 115258624,
+    ("gencat_fwd", "torch.bfloat16"): 42377472,
     ("gencat_bwd_x", "torch.float32"): 91352320,
     ("gencat_bwd_x", "torch.bfloat16"): 45780224,
     ("gencat_bwd_yw", "torch.float32"): 114652928,
