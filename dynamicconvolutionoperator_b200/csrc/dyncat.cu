@@ -19,9 +19,12 @@
 // The staged plane is "column-interleaved" (column cc of a row is stored at
 // (cc % VEC) * (row_words / VEC) + cc / VEC): for any tap shift the 32 lanes of
 // a warp then read 32 consecutive words, i.e. no bank conflicts.
-// dX gathers K at shifted (unaligned) positions, so it keeps one pixel per
-// thread per step, with a small register footprint for high occupancy.
+// dX gathers K at shifted (unaligned) positions. Its vector kernel keeps the
+// same layout and builds each shifted VEC-window from the two aligned 16-byte
+// chunks that cover it; the scalar kernel (one pixel per thread per step)
+// serves rows that are not 16-byte aligned and very large halos.
 #include <initializer_list>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -107,21 +110,96 @@ __host__ __device__ __forceinline__ int stage_sub(int R) {
   return (kThreadsX * VEC + 2 * R + VEC - 1) / VEC;
 }
 
+// Staging issues kStageBatch independent loads per thread before the first
+// shared-memory store: a load-then-store loop would leave one global load in
+// flight per thread and make the staging phase latency-bound. Every load reads
+// a clamped in-image address and is zeroed afterwards when the staged position
+// lies in the padding, so no load is predicated away.
+constexpr int kStageBatch = 8;
+
+__device__ __forceinline__ int clampi(int v, int lo, int hi) { return min(max(v, lo), hi); }
+
 template <typename T, int VEC>
 __device__ __forceinline__ void stage_plane(float* __restrict__ s, const Stage<VEC>& st,
                                             const T* __restrict__ plane, int H, int W, int h0,
                                             int w0) {
   const int rows = kTileH + 2 * st.R;
   const int cols = st.row_words;
+  const int total = rows * cols;
   const int tid = threadIdx.y * kThreadsX + threadIdx.x;
-  for (int i = tid; i < rows * cols; i += kThreads) {
-    const int rr = i / cols;
-    const int cc = i - rr * cols;
-    const int gh = h0 - st.R + rr;
-    const int gw = w0 - st.R + cc;
-    float v = 0.f;
-    if (gh >= 0 && gh < H && gw >= 0 && gw < W) v = ldg_f32<T>(plane + (size_t)gh * W + gw);
-    s[st.idx(rr, cc)] = v;
+  for (int base = tid; base < total; base += kThreads * kStageBatch) {
+    float v[kStageBatch];
+    int dst[kStageBatch];
+#pragma unroll
+    for (int u = 0; u < kStageBatch; ++u) {
+      const int i = min(base + u * kThreads, total - 1);
+      const int rr = i / cols;
+      const int cc = i - rr * cols;
+      const int gh = h0 - st.R + rr;
+      const int gw = w0 - st.R + cc;
+      const float t = ldg_f32<T>(plane + (size_t)clampi(gh, 0, H - 1) * W + clampi(gw, 0, W - 1));
+      v[u] = (gh >= 0 && gh < H && gw >= 0 && gw < W) ? t : 0.f;
+      dst[u] = st.idx(rr, cc);
+    }
+#pragma unroll
+    for (int u = 0; u < kStageBatch; ++u)
+      if (base + u * kThreads < total) s[dst[u]] = v[u];
+  }
+}
+
+// NPL planes (plane i at plane0 + i * plane_stride) staged with 16-byte loads,
+// for rows that are a whole number of aligned VEC-chunks (W % VEC == 0, 16-byte
+// aligned base): a chunk then lies wholly inside or wholly outside the image,
+// and a tile needs about VEC times fewer loads, so all of a thread's loads
+// fit in one or two batches. For a fixed element of the chunk the lanes of a
+// warp store consecutive words of one interleave sub-row: no bank conflicts.
+template <typename T, int VEC, int NPL>
+__device__ __forceinline__ void stage_planes_vec(float* __restrict__ s, int plane_words,
+                                                 const Stage<VEC>& st, const T* __restrict__ plane0,
+                                                 size_t plane_stride, int H, int W, int h0,
+                                                 int w0) {
+  using U = typename Vec<T, VEC>::U;
+  const int rows = kTileH + 2 * st.R;
+  const int x0 = w0 - st.R;  // global column of staged column 0
+  const int k0 = x0 >= 0 ? x0 / VEC : -((VEC - 1 - x0) / VEC);  // floor(x0 / VEC)
+  const int nk = (x0 + st.row_words - 1) / VEC - k0 + 1;        // chunks per staged row
+  const int nchunk = W / VEC;
+  const int per_plane = rows * nk;
+  const int total = NPL * per_plane;
+  const int tid = threadIdx.y * kThreadsX + threadIdx.x;
+  for (int base = tid; base < total; base += kThreads * kStageBatch) {
+    U u[kStageBatch];
+    bool ok[kStageBatch];
+#pragma unroll
+    for (int q = 0; q < kStageBatch; ++q) {
+      const int i = min(base + q * kThreads, total - 1);
+      const int pl = i / per_plane;
+      const int rem = i - pl * per_plane;
+      const int rr = rem / nk;
+      const int kc = k0 + rem - rr * nk;
+      const int gh = h0 - st.R + rr;
+      ok[q] = gh >= 0 && gh < H && kc >= 0 && kc < nchunk;
+      const U* row = reinterpret_cast<const U*>(plane0 + pl * plane_stride +
+                                                (size_t)clampi(gh, 0, H - 1) * W);
+      u[q] = __ldg(row + clampi(kc, 0, nchunk - 1));
+    }
+#pragma unroll
+    for (int q = 0; q < kStageBatch; ++q) {
+      const int i = base + q * kThreads;
+      if (i >= total) break;
+      const int pl = i / per_plane;
+      const int rem = i - pl * per_plane;
+      const int rr = rem / nk;
+      const int cc0 = (k0 + rem - rr * nk) * VEC - x0;
+      float v[VEC];
+      Vec<T, VEC>::unpack(u[q], v);
+      float* dst = s + pl * plane_words;
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) {
+        const int cc = cc0 + e;
+        if (cc >= 0 && cc < st.row_words) dst[st.idx(rr, cc)] = ok[q] ? v[e] : 0.f;
+      }
+    }
   }
 }
 
@@ -255,13 +333,20 @@ dyncat_bwd_k_kernel(const TX* __restrict__ x, const TK* __restrict__ gout, TK* _
 // gradients of the tile + halo are staged in smem (plain row-major, VEC = 1).
 constexpr int kDxTileW = kThreadsX * 4;  // 4 pixel columns per thread, 32 apart
 
-template <typename TX, typename TK, int KS>
+// D0 > 0 fixes the dilations (D0, D1, D2) at compile time, as for the vector
+// kernel below: tap shifts, the halo and every shared-memory offset are then
+// constants. D0 == 0 takes them from `dil` and `R_rt` at run time.
+template <typename TX, typename TK, int KS, int D0, int D1, int D2>
 __global__ void __launch_bounds__(kThreads, 3)
 dyncat_bwd_x_kernel(const TK* __restrict__ kern, const TK* __restrict__ gout, TX* __restrict__ gx,
-                    int C, int H, int W, Dil dil, int R) {
+                    int C, int H, int W, Dil dil, int R_rt) {
   extern __shared__ float smem[];
   constexpr int KK = KS * KS;
   constexpr int r = KS / 2;
+  constexpr bool kFixed = D0 > 0;
+  constexpr int kDil[3] = {D0, D1, D2};
+  constexpr int kR = r * (D0 > D1 ? (D0 > D2 ? D0 : D2) : (D1 > D2 ? D1 : D2));
+  const int R = kFixed ? kR : R_rt;
   const int nc = blockIdx.x;
   const int n = nc / C;
   const int c = nc - n * C;
@@ -276,17 +361,25 @@ dyncat_bwd_x_kernel(const TK* __restrict__ kern, const TK* __restrict__ gout, TX
   const size_t gbranch = (size_t)C * P;
   {
     const int tid = threadIdx.y * kThreadsX + threadIdx.x;
-    for (int i = tid; i < 3 * plane_sz; i += kThreads) {
-      const int b = i / plane_sz;
-      const int k = i - b * plane_sz;
-      const int rr = k / pitch;
-      const int cc = k - rr * pitch;
-      const int gh = h0 - R + rr;
-      const int gw = w0 - R + cc;
-      float v = 0.f;
-      if (gh >= 0 && gh < H && gw >= 0 && gw < W)
-        v = ldg_f32<TK>(gbase + (b + 1) * gbranch + (size_t)gh * W + gw);
-      smem[i] = v;
+    const int total = 3 * plane_sz;
+    for (int base = tid; base < total; base += kThreads * kStageBatch) {
+      float v[kStageBatch];
+#pragma unroll
+      for (int u = 0; u < kStageBatch; ++u) {
+        const int i = min(base + u * kThreads, total - 1);
+        const int b = i / plane_sz;
+        const int k = i - b * plane_sz;
+        const int rr = k / pitch;
+        const int cc = k - rr * pitch;
+        const int gh = h0 - R + rr;
+        const int gw = w0 - R + cc;
+        const float t = ldg_f32<TK>(gbase + (b + 1) * gbranch +
+                                    (size_t)clampi(gh, 0, H - 1) * W + clampi(gw, 0, W - 1));
+        v[u] = (gh >= 0 && gh < H && gw >= 0 && gw < W) ? t : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < kStageBatch; ++u)
+        if (base + u * kThreads < total) smem[base + u * kThreads] = v[u];
     }
   }
   __syncthreads();
@@ -308,25 +401,183 @@ dyncat_bwd_x_kernel(const TK* __restrict__ kern, const TK* __restrict__ gout, TX
       float acc = to_f32<TK>(gbase[p]);
 #pragma unroll
       for (int b = 0; b < 3; ++b) {
-        const int d = dil.d[b];
+        const int d = kFixed ? kDil[b] : dil.d[b];
         const TK* kp = kern + kbase + b * kbranch;
         const float* gs = smem + b * plane_sz + sidx;
+        // A tap whose source pixel q - off lies outside the image (zero
+        // padding) contributes nothing. Its load still goes out, from a
+        // clamped in-image address, so that a group's loads are all issued
+        // before the first FMA; the value is zeroed (a non-finite tap there
+        // never reaches the sum) and meets the staged zero of the padding.
+        constexpr int RG = KS <= 3 ? KS : 1;
 #pragma unroll
-        for (int ki = 0; ki < KS; ++ki) {
-          const int dy = (ki - r) * d;
-          const bool row_ok = (unsigned)(h - dy) < (unsigned)H;
+        for (int k0 = 0; k0 < KS; k0 += RG) {
+          float kv[RG * KS];
 #pragma unroll
-          for (int kj = 0; kj < KS; ++kj) {
-            const int dx = (kj - r) * d;
-            // Source pixel q - off must lie inside the image (zero padding).
-            if (row_ok && (unsigned)(w - dx) < (unsigned)W) {
-              const float kv = ldcs_f32<TK>(kp + (size_t)(ki * KS + kj) * P + (p - (ptrdiff_t)dy * W - dx));
-              acc = fmaf(kv, gs[-dy * pitch - dx], acc);
+          for (int ki = k0; ki < k0 + RG; ++ki) {
+            const int dy = (ki - r) * d;
+            const bool row_ok = (unsigned)(h - dy) < (unsigned)H;
+            const size_t srow = (size_t)clampi(h - dy, 0, H - 1) * W;
+#pragma unroll
+            for (int kj = 0; kj < KS; ++kj) {
+              const int dx = (kj - r) * d;
+              const float t =
+                  ldcs_f32<TK>(kp + (size_t)(ki * KS + kj) * P + srow + clampi(w - dx, 0, W - 1));
+              kv[(ki - k0) * KS + kj] = (row_ok && (unsigned)(w - dx) < (unsigned)W) ? t : 0.f;
             }
+          }
+#pragma unroll
+          for (int ki = k0; ki < k0 + RG; ++ki) {
+            const int dy = (ki - r) * d;
+#pragma unroll
+            for (int kj = 0; kj < KS; ++kj)
+              acc = fmaf(kv[(ki - k0) * KS + kj], gs[-dy * pitch - (kj - r) * d], acc);
           }
         }
       }
       gx[(size_t)nc * P + p] = from_f32<TX>(acc);
+    }
+  }
+}
+
+// ------------------------------------------------------- dX (vector) --------
+// The same sum as dyncat_bwd_x_kernel, in the same order, with the forward's
+// thread layout: a thread owns VEC consecutive pixels, so a warp reads each
+// tap plane as one contiguous 32 x 16-byte row segment instead of VEC
+// separate 4- or 2-byte gathers spread over time. The tap a pixel q needs
+// sits at q - off, which is not VEC-aligned for odd shifts: the thread loads
+// the two aligned 16-byte chunks that cover its shifted window (the second
+// one is mostly an L1 hit on the neighbour's first) and picks the window out
+// of them. The window offset m = (-dx) mod VEC is the same for every thread of
+// the CTA, so the pick is a uniform branch over compile-time cases.
+template <int VEC, int M = 0, typename F>
+__device__ __forceinline__ void with_window(int m, F&& f) {
+  if constexpr (M < VEC) {
+    if (m == M)
+      f(std::integral_constant<int, M>{});
+    else
+      with_window<VEC, M + 1>(m, f);
+  }
+}
+
+// D0 > 0 fixes the dilations (D0, D1, D2) at compile time (the module's
+// (1, 3, 5)): every tap shift, window offset and shared-memory offset is then a
+// constant, and the per-tap work is the loads, the reads and the FMAs.
+// D0 == 0 takes them from `dil` at run time.
+template <typename TX, typename TK, int KS, int VEC, int D0, int D1, int D2>
+__global__ void __launch_bounds__(kThreads, 2)
+dyncat_bwd_x_vec_kernel(const TK* __restrict__ kern, const TK* __restrict__ gout,
+                        TX* __restrict__ gx, int C, int H, int W, Dil dil, int R_rt) {
+  extern __shared__ float smem[];
+  constexpr int KK = KS * KS;
+  constexpr int r = KS / 2;
+  constexpr bool kFixed = D0 > 0;
+  constexpr int kDil[3] = {D0, D1, D2};
+  constexpr int kR = r * (D0 > D1 ? (D0 > D2 ? D0 : D2) : (D1 > D2 ? D1 : D2));
+  using U = typename Vec<TK, VEC>::U;
+  const int R = kFixed ? kR : R_rt;
+  const int nc = blockIdx.x;
+  const int n = nc / C;
+  const int c = nc - n * C;
+  const int h0 = blockIdx.y * kTileH;
+  const int w0 = blockIdx.z * (kThreadsX * VEC);
+  const size_t P = (size_t)H * W;
+  const Stage<VEC> st{R, stage_sub<VEC>(R), VEC * stage_sub<VEC>(R)};
+  const int plane_words = st.row_words * (kTileH + 2 * R);
+
+  const TK* gbase = gout + ((size_t)n * 4 * C + c) * P;
+  const size_t gbranch = (size_t)C * P;
+  stage_planes_vec<TK, VEC, 3>(smem, plane_words, st, gbase + gbranch, gbranch, H, W, h0, w0);
+  __syncthreads();
+
+  const int tx = threadIdx.x;
+  const int w = w0 + tx * VEC;
+  if (w >= W) return;
+  const int nchunk = W / VEC;
+  const size_t kbase = ((size_t)n * 3 * C + c) * KK * P;
+  const size_t kbranch = (size_t)C * KK * P;
+
+#pragma unroll 1
+  for (int j = 0; j < kRowsPerThread; ++j) {
+    const int ly = threadIdx.y + j * kThreadsY;
+    const int h = h0 + ly;
+    if (h >= H) break;
+    const size_t p = (size_t)h * W + w;
+    // Staged word of (row ly + R - dy, column VEC*tx + R + v - dx): with
+    // e = R + v - dx >= 0 it is ly*row_words + tx + [(R - dy)*row_words +
+    // (e % VEC)*sub + e / VEC], the bracket being a constant per tap and v.
+    const float* gthr = smem + ly * st.row_words + tx;
+    float acc[VEC];
+    vload<TK, VEC>(gbase + p, acc);  // the x passthrough's gradient g[n, c, q]
+    auto branch = [&](int b, int d) {
+      const TK* kp = kern + kbase + b * kbranch;
+      const float* gs = gthr + b * plane_words;
+      // With fixed dilations the second chunk is only loaded for the shifted
+      // taps (known at compile time), and a K = 3 branch's chunks all fit in
+      // registers: all nine taps' loads go out before the first FMA.
+      constexpr int RG = (kFixed && KS <= 3) ? KS : 1;
+#pragma unroll
+      for (int k0 = 0; k0 < KS; k0 += RG) {
+        U ua[RG][KS], ub[RG][KS];
+#pragma unroll
+        for (int ki = k0; ki < k0 + RG; ++ki) {
+          const int dy = (ki - r) * d;
+          const TK* krow = kp + (size_t)clampi(h - dy, 0, H - 1) * W;
+#pragma unroll
+          for (int kj = 0; kj < KS; ++kj) {
+            const int dx = (kj - r) * d;
+            const int m = ((-dx) % VEC + VEC) % VEC;
+            const int c0 = w / VEC + (-dx - m) / VEC;  // exact: -dx - m is a multiple of VEC
+            const U* tp = reinterpret_cast<const U*>(krow + (size_t)(ki * KS + kj) * P);
+            // Chunks outside the row are clamped; every element they supply
+            // has its source outside the image and is zeroed below.
+            ua[ki - k0][kj] = __ldg(tp + clampi(c0, 0, nchunk - 1));
+            if (m != 0) ub[ki - k0][kj] = __ldg(tp + clampi(c0 + 1, 0, nchunk - 1));
+          }
+        }
+#pragma unroll
+      for (int ki = k0; ki < k0 + RG; ++ki) {
+        const int dy = (ki - r) * d;
+        const bool row_ok = (unsigned)(h - dy) < (unsigned)H;
+        const float* grow = gs + (R - dy) * st.row_words;
+#pragma unroll
+        for (int kj = 0; kj < KS; ++kj) {
+          const int dx = (kj - r) * d;
+          const int m = ((-dx) % VEC + VEC) % VEC;
+          const bool inside = row_ok && w - dx >= 0 && w + VEC - 1 - dx < W;
+          float za[VEC], zb[VEC];
+          Vec<TK, VEC>::unpack(ua[ki - k0][kj], za);
+          if (m != 0) Vec<TK, VEC>::unpack(ub[ki - k0][kj], zb);
+          with_window<VEC>(m, [&](auto mc) {
+            constexpr int M = decltype(mc)::value;
+#pragma unroll
+            for (int v = 0; v < VEC; ++v) {
+              float t = (M + v < VEC) ? za[(M + v) % VEC] : zb[(M + v) % VEC];
+              // A source pixel outside the image contributes nothing (and a
+              // non-finite tap there never reaches the sum).
+              if (!inside) t = (row_ok && (unsigned)(w + v - dx) < (unsigned)W) ? t : 0.f;
+              const int e = R + v - dx;
+              acc[v] = fmaf(t, grow[(e % VEC) * st.sub + e / VEC], acc[v]);
+            }
+          });
+        }
+      }
+      }
+    };
+    if constexpr (kFixed) {  // constant shifts and offsets after inlining
+      branch(0, kDil[0]);
+      branch(1, kDil[1]);
+      branch(2, kDil[2]);
+    } else {
+#pragma unroll 1
+      for (int b = 0; b < 3; ++b) branch(b, dil.d[b]);
+    }
+    if constexpr (sizeof(TX) == sizeof(TK)) {
+      vstore_cs<TX, VEC>(gx + (size_t)nc * P + p, acc);
+    } else {  // FP32 x with a 16-bit taps tensor: VEC = 8 floats, two 16-byte stores
+      float4* o = reinterpret_cast<float4*>(gx + (size_t)nc * P + p);
+      __stcs(o, make_float4(acc[0], acc[1], acc[2], acc[3]));
+      __stcs(o + 1, make_float4(acc[4], acc[5], acc[6], acc[7]));
     }
   }
 }
@@ -372,17 +623,36 @@ int launch_bwd_k(const void* x, const void* g, void* gk, int n, int c, int h, in
   return DDPM_OK;
 }
 
-template <typename TX, typename TK, int KS>
+template <typename TX, typename TK, int KS, int D0, int D1, int D2>
 int launch_bwd_x(const void* k, const void* g, void* gx, int n, int c, int h, int w, Dil dil,
                  int R, cudaStream_t st) {
   const size_t smem = sizeof(float) * 3 * (size_t)(kDxTileW + 2 * R) * (kTileH + 2 * R);
-  auto fn = dyncat_bwd_x_kernel<TX, TK, KS>;
+  auto fn = dyncat_bwd_x_kernel<TX, TK, KS, D0, D1, D2>;
   if (int rc = set_smem(fn, smem)) return rc;
   dim3 grid(n * c, (h + kTileH - 1) / kTileH, (w + kDxTileW - 1) / kDxTileW);
   fn<<<grid, dim3(kThreadsX, kThreadsY), smem, st>>>(static_cast<const TK*>(k),
                                                        static_cast<const TK*>(g),
                                                        static_cast<TX*>(gx), c, h, w, dil, R);
   DDPM_CHECK_LAUNCH("dyncat_bwd_x_kernel");
+  return DDPM_OK;
+}
+
+// The vector dX kernel stages the three branch planes at the wider vector
+// tile; beyond this size (large K x dilation halos) two CTAs no longer fit on
+// an SM and the scalar kernel is used.
+constexpr size_t kDxVecSmemMax = 113 * 1024;
+
+template <typename TX, typename TK, int KS, int VEC, int D0, int D1, int D2>
+int launch_bwd_x_vec(const void* k, const void* g, void* gx, int n, int c, int h, int w, Dil dil,
+                     int R, cudaStream_t st) {
+  const size_t smem = 3 * stage_bytes<VEC>(R);
+  auto fn = dyncat_bwd_x_vec_kernel<TX, TK, KS, VEC, D0, D1, D2>;
+  if (int rc = set_smem(fn, smem)) return rc;
+  dim3 grid(n * c, (h + kTileH - 1) / kTileH, (w + kThreadsX * VEC - 1) / (kThreadsX * VEC));
+  fn<<<grid, dim3(kThreadsX, kThreadsY), smem, st>>>(static_cast<const TK*>(k),
+                                                       static_cast<const TK*>(g),
+                                                       static_cast<TX*>(gx), c, h, w, dil, R);
+  DDPM_CHECK_LAUNCH("dyncat_bwd_x_vec_kernel");
   return DDPM_OK;
 }
 
@@ -428,7 +698,22 @@ int bwd_ks(const void* x, const void* k, const void* g, void* gx, void* gk, int 
                        : launch_bwd_k<TX, TK, KS, 1>(x, g, gk, n, c, h, w, dil, R, st);
     if (rc) return rc;
   }
-  if (gx != nullptr) return launch_bwd_x<TX, TK, KS>(k, g, gx, n, c, h, w, dil, R, st);
+  if (gx != nullptr) {
+    // The vector dX kernel serves 16-bit taps with K <= 3 (its chunk pairs fit
+    // in registers without spilling). For FP32 taps the scalar kernel, at
+    // three CTAs per SM, is the faster one (162 against 184 us at B1 C64 256^2
+    // K3 on B200).
+    if constexpr (V == 8 && KS <= 3) {
+      if (vec_ok(w, V, {k, g, gx}) && 3 * stage_bytes<V>(R) <= kDxVecSmemMax) {
+        if (dil.d[0] == 1 && dil.d[1] == 3 && dil.d[2] == 5)
+          return launch_bwd_x_vec<TX, TK, KS, V, 1, 3, 5>(k, g, gx, n, c, h, w, dil, R, st);
+        return launch_bwd_x_vec<TX, TK, KS, V, 0, 0, 0>(k, g, gx, n, c, h, w, dil, R, st);
+      }
+    }
+    if (dil.d[0] == 1 && dil.d[1] == 3 && dil.d[2] == 5)
+      return launch_bwd_x<TX, TK, KS, 1, 3, 5>(k, g, gx, n, c, h, w, dil, R, st);
+    return launch_bwd_x<TX, TK, KS, 0, 0, 0>(k, g, gx, n, c, h, w, dil, R, st);
+  }
   return DDPM_OK;
 }
 

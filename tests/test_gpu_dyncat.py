@@ -97,3 +97,70 @@ def test_dyncat_large_plane_bf16():
     ggx, ggk = orc.dynamic_cat_backward(x.double(), k.double(), g.double(), 3)
     _check(gx, ggx, torch.bfloat16)
     _check(gk, ggk, torch.bfloat16)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("width", [20, 24])
+def test_dyncat_backward_ignores_taps_that_feed_padding(dtype, width):
+    """A tap value at pixel p whose source p + off lies outside the image only
+    meets the zero padding, so it never reaches grad_x, even when it is not
+    finite (the reference folds its products into the discarded border)."""
+    from dynamicconvolutionoperator_b200 import fused_dynamic_cat
+
+    ks, dil = 3, (1, 3, 5)
+    x, k, g = _inputs((1, 3, 12, width), ks, dtype, dtype, seed=7)
+    n, c, h, w = x.shape
+    rows = torch.arange(h).view(h, 1)
+    cols = torch.arange(w).view(1, w)
+    for b, d in enumerate(dil):
+        for ki in range(ks):
+            for kj in range(ks):
+                dy, dx = (ki - ks // 2) * d, (kj - ks // 2) * d
+                outside = ((rows + dy < 0) | (rows + dy >= h) | (cols + dx < 0) | (cols + dx >= w))
+                k[:, b, :, ki * ks + kj][:, :, outside] = float("inf")
+    xd = x.cuda().requires_grad_(True)
+    out = fused_dynamic_cat(xd, k.cuda(), ks, dil)
+    (gx,) = torch.autograd.grad(out, (xd,), g.cuda())
+    gold_gx, _ = orc.dynamic_cat_backward(x.double(), k.double(), g.double(), ks, dil)
+    assert torch.isfinite(gold_gx).all()
+    assert torch.isfinite(gx).all()
+    _check(gx, gold_gx, dtype)
+
+
+def _misaligned(t):
+    """The same values one element past a 16-byte boundary: the library's
+    vector kernels need 16-byte aligned rows, so this selects the scalar ones."""
+    buf = torch.empty(t.numel() + 1, dtype=t.dtype, device=t.device)
+    out = buf[1:].view(t.shape)
+    out.copy_(t)
+    assert out.data_ptr() % 16 != 0
+    return out
+
+
+@pytest.mark.parametrize("shape", [(1, 3, 21, 136), (2, 2, 9, 264), (1, 4, 16, 8), (1, 2, 5, 40)])
+@pytest.mark.parametrize("ks", [1, 3, 5])
+@pytest.mark.parametrize("dil", [(1, 3, 5), (7, 2, 4)])
+@pytest.mark.parametrize(
+    "xdt,kdt",
+    [(torch.float32, torch.float32), (torch.bfloat16, torch.bfloat16),
+     (torch.float16, torch.float16), (torch.float32, torch.bfloat16)],
+)
+def test_dyncat_grad_x_vector_kernel_matches_scalar(shape, ks, dil, xdt, kdt):
+    """grad_x from aligned tensors (the vector kernel for 16-bit taps, rows a
+    multiple of 16 bytes) is bit-identical to the scalar kernel's (same sum,
+    same order) and matches the oracle; shapes cover ragged column tiles,
+    8-wide images and tap shifts wider than one vector, for the dilations with
+    a compile-time instance (1, 3, 5) and for run-time ones."""
+    from dynamicconvolutionoperator_b200 import fused_dynamic_cat
+
+    x, k, g = _inputs(shape, ks, xdt, kdt, seed=11)
+    kc, gc = k.cuda(), g.cuda()
+    grads = []
+    for kk in (kc, _misaligned(kc)):
+        xd = x.cuda().requires_grad_(True)
+        out = fused_dynamic_cat(xd, kk, ks, dil)
+        (gx,) = torch.autograd.grad(out, (xd,), gc)
+        grads.append(gx)
+    assert torch.equal(grads[0], grads[1])
+    gold_gx, _ = orc.dynamic_cat_backward(x.double(), k.double(), g.double(), ks, dil)
+    _check(grads[0], gold_gx, xdt if xdt != torch.float32 else kdt)
