@@ -204,13 +204,32 @@ __device__ __forceinline__ void stage_planes_vec(float* __restrict__ s, int plan
 }
 
 // ------------------------------------------------------------- forward ------
-template <typename TX, typename TK, int KS, int VEC>
+// Forward, dK and dX each have a compile-time instance for the dilations the
+// module uses, (1, 3, 5) (template arguments D0 > 0): every tap shift, the halo
+// and every shared-memory offset are then constants, and the per-tap work is
+// the load or store, the reads and the arithmetic. D0 == 0 takes the
+// dilations and the halo from the arguments at run time.
+#define DDPM_DIL_CONSTANTS                                                      \
+  constexpr bool kFixed = D0 > 0;                                              \
+  constexpr int kDil[3] = {D0, D1, D2};                                        \
+  constexpr int kR = (KS / 2) * (D0 > D1 ? (D0 > D2 ? D0 : D2) : (D1 > D2 ? D1 : D2)); \
+  const int R = kFixed ? kR : R_rt;
+
+// Staged word of (row ly + R + dy, column VEC*tx + e), e = R + dx + v >= 0:
+// ly*row_words + tx + [(R + dy)*row_words + (e % VEC)*sub + e / VEC].
+template <int VEC>
+__device__ __forceinline__ int stage_off(const Stage<VEC>& st, int row, int e) {
+  return row * st.row_words + (e % VEC) * st.sub + e / VEC;
+}
+
+template <typename TX, typename TK, int KS, int VEC, int D0, int D1, int D2>
 __global__ void __launch_bounds__(kThreads, 2)
 dyncat_fwd_kernel(const TX* __restrict__ x, const TK* __restrict__ kern, TK* __restrict__ out,
-                  int C, int H, int W, Dil dil, int R) {
+                  int C, int H, int W, Dil dil, int R_rt) {
   extern __shared__ float smem[];
   constexpr int KK = KS * KS;
   constexpr int r = KS / 2;
+  DDPM_DIL_CONSTANTS
   const int nc = blockIdx.x;
   const int n = nc / C;
   const int c = nc - n * C;
@@ -226,8 +245,8 @@ dyncat_fwd_kernel(const TX* __restrict__ x, const TK* __restrict__ kern, TK* __r
   const size_t kbranch = (size_t)C * KK * P;
   TK* obase = out + ((size_t)n * 4 * C + c) * P;
   const size_t obranch = (size_t)C * P;
-  const int lx = threadIdx.x * VEC;
-  const int w = w0 + lx;
+  const int tx = threadIdx.x;
+  const int w = w0 + tx * VEC;
   if (w >= W) return;
 
 #pragma unroll 1
@@ -236,13 +255,12 @@ dyncat_fwd_kernel(const TX* __restrict__ x, const TK* __restrict__ kern, TK* __r
     const int h = h0 + ly;
     if (h >= H) break;
     const size_t p = (size_t)h * W + w;
+    const float* sthr = smem + ly * st.row_words + tx;
     float center[VEC];
 #pragma unroll
-    for (int v = 0; v < VEC; ++v) center[v] = smem[st.idx(ly + R, lx + R + v)];
+    for (int v = 0; v < VEC; ++v) center[v] = sthr[stage_off(st, R, R + v)];
     vstore_cs<TK, VEC>(obase + p, center);
-#pragma unroll 1
-    for (int b = 0; b < 3; ++b) {
-      const int d = dil.d[b];
+    auto branch = [&](int b, int d) {
       const TK* kp = kern + kbase + b * kbranch + p;
       float acc[VEC];
 #pragma unroll
@@ -258,29 +276,38 @@ dyncat_fwd_kernel(const TX* __restrict__ x, const TK* __restrict__ kern, TK* __r
           vload_cs<TK, VEC>(kp + (size_t)(k0 * KS + t) * P, kv[t]);
 #pragma unroll
         for (int ki = k0; ki < k0 + RG; ++ki) {
-          const int row = ly + R + (ki - r) * d;
+          const int row = R + (ki - r) * d;
 #pragma unroll
           for (int kj = 0; kj < KS; ++kj) {
-            const int col = lx + R + (kj - r) * d;
 #pragma unroll
             for (int v = 0; v < VEC; ++v)
-              acc[v] = fmaf(smem[st.idx(row, col + v)], kv[(ki - k0) * KS + kj][v], acc[v]);
+              acc[v] = fmaf(sthr[stage_off(st, row, R + (kj - r) * d + v)],
+                            kv[(ki - k0) * KS + kj][v], acc[v]);
           }
         }
       }
       vstore_cs<TK, VEC>(obase + (b + 1) * obranch + p, acc);
+    };
+    if constexpr (kFixed) {
+      branch(0, kDil[0]);
+      branch(1, kDil[1]);
+      branch(2, kDil[2]);
+    } else {
+#pragma unroll 1
+      for (int b = 0; b < 3; ++b) branch(b, dil.d[b]);
     }
   }
 }
 
 // ---------------------------------------------------------------- dK --------
-template <typename TX, typename TK, int KS, int VEC>
+template <typename TX, typename TK, int KS, int VEC, int D0, int D1, int D2>
 __global__ void __launch_bounds__(kThreads, 2)
 dyncat_bwd_k_kernel(const TX* __restrict__ x, const TK* __restrict__ gout, TK* __restrict__ gk,
-                    int C, int H, int W, Dil dil, int R) {
+                    int C, int H, int W, Dil dil, int R_rt) {
   extern __shared__ float smem[];
   constexpr int KK = KS * KS;
   constexpr int r = KS / 2;
+  DDPM_DIL_CONSTANTS
   const int nc = blockIdx.x;
   const int n = nc / C;
   const int c = nc - n * C;
@@ -296,8 +323,8 @@ dyncat_bwd_k_kernel(const TX* __restrict__ x, const TK* __restrict__ gout, TK* _
   const size_t gbranch = (size_t)C * P;
   const size_t kbase = ((size_t)n * 3 * C + c) * KK * P;
   const size_t kbranch = (size_t)C * KK * P;
-  const int lx = threadIdx.x * VEC;
-  const int w = w0 + lx;
+  const int tx = threadIdx.x;
+  const int w = w0 + tx * VEC;
   if (w >= W) return;
 
 #pragma unroll 1
@@ -306,24 +333,30 @@ dyncat_bwd_k_kernel(const TX* __restrict__ x, const TK* __restrict__ gout, TK* _
     const int h = h0 + ly;
     if (h >= H) break;
     const size_t p = (size_t)h * W + w;
-#pragma unroll 1
-    for (int b = 0; b < 3; ++b) {
-      const int d = dil.d[b];
+    const float* sthr = smem + ly * st.row_words + tx;
+    auto branch = [&](int b, int d) {
       float g[VEC];
       vload<TK, VEC>(gbase + (b + 1) * gbranch + p, g);
       TK* kp = gk + kbase + b * kbranch + p;
 #pragma unroll
       for (int ki = 0; ki < KS; ++ki) {
-        const int row = ly + R + (ki - r) * d;
+        const int row = R + (ki - r) * d;
 #pragma unroll
         for (int kj = 0; kj < KS; ++kj) {
-          const int col = lx + R + (kj - r) * d;
           float o[VEC];
 #pragma unroll
-          for (int v = 0; v < VEC; ++v) o[v] = smem[st.idx(row, col + v)] * g[v];
+          for (int v = 0; v < VEC; ++v) o[v] = sthr[stage_off(st, row, R + (kj - r) * d + v)] * g[v];
           vstore_cs<TK, VEC>(kp + (size_t)(ki * KS + kj) * P, o);
         }
       }
+    };
+    if constexpr (kFixed) {
+      branch(0, kDil[0]);
+      branch(1, kDil[1]);
+      branch(2, kDil[2]);
+    } else {
+#pragma unroll 1
+      for (int b = 0; b < 3; ++b) branch(b, dil.d[b]);
     }
   }
 }
@@ -588,6 +621,11 @@ size_t stage_bytes(int R) {
   return sizeof(float) * (size_t)VEC * stage_sub<VEC>(R) * (kTileH + 2 * R);
 }
 
+// The dilations with compile-time kernel instances (the module's default).
+inline bool is_default_dil(const Dil& dil) {
+  return dil.d[0] == 1 && dil.d[1] == 3 && dil.d[2] == 5;
+}
+
 template <typename F>
 int set_smem(F fn, size_t smem) {
   if (smem > 48 * 1024)
@@ -599,7 +637,8 @@ template <typename TX, typename TK, int KS, int VEC>
 int launch_fwd(const void* x, const void* k, void* out, int n, int c, int h, int w, Dil dil, int R,
                cudaStream_t st) {
   const size_t smem = stage_bytes<VEC>(R);
-  auto fn = dyncat_fwd_kernel<TX, TK, KS, VEC>;
+  auto fn = is_default_dil(dil) ? dyncat_fwd_kernel<TX, TK, KS, VEC, 1, 3, 5>
+                                : dyncat_fwd_kernel<TX, TK, KS, VEC, 0, 0, 0>;
   if (int rc = set_smem(fn, smem)) return rc;
   dim3 grid(n * c, (h + kTileH - 1) / kTileH, (w + kThreadsX * VEC - 1) / (kThreadsX * VEC));
   fn<<<grid, dim3(kThreadsX, kThreadsY), smem, st>>>(static_cast<const TX*>(x),
@@ -613,7 +652,8 @@ template <typename TX, typename TK, int KS, int VEC>
 int launch_bwd_k(const void* x, const void* g, void* gk, int n, int c, int h, int w, Dil dil,
                  int R, cudaStream_t st) {
   const size_t smem = stage_bytes<VEC>(R);
-  auto fn = dyncat_bwd_k_kernel<TX, TK, KS, VEC>;
+  auto fn = is_default_dil(dil) ? dyncat_bwd_k_kernel<TX, TK, KS, VEC, 1, 3, 5>
+                                : dyncat_bwd_k_kernel<TX, TK, KS, VEC, 0, 0, 0>;
   if (int rc = set_smem(fn, smem)) return rc;
   dim3 grid(n * c, (h + kTileH - 1) / kTileH, (w + kThreadsX * VEC - 1) / (kThreadsX * VEC));
   fn<<<grid, dim3(kThreadsX, kThreadsY), smem, st>>>(static_cast<const TX*>(x),
@@ -705,12 +745,12 @@ int bwd_ks(const void* x, const void* k, const void* g, void* gx, void* gk, int 
     // K3 on B200).
     if constexpr (V == 8 && KS <= 3) {
       if (vec_ok(w, V, {k, g, gx}) && 3 * stage_bytes<V>(R) <= kDxVecSmemMax) {
-        if (dil.d[0] == 1 && dil.d[1] == 3 && dil.d[2] == 5)
+        if (is_default_dil(dil))
           return launch_bwd_x_vec<TX, TK, KS, V, 1, 3, 5>(k, g, gx, n, c, h, w, dil, R, st);
         return launch_bwd_x_vec<TX, TK, KS, V, 0, 0, 0>(k, g, gx, n, c, h, w, dil, R, st);
       }
     }
-    if (dil.d[0] == 1 && dil.d[1] == 3 && dil.d[2] == 5)
+    if (is_default_dil(dil))
       return launch_bwd_x<TX, TK, KS, 1, 3, 5>(k, g, gx, n, c, h, w, dil, R, st);
     return launch_bwd_x<TX, TK, KS, 0, 0, 0>(k, g, gx, n, c, h, w, dil, R, st);
   }
