@@ -340,8 +340,8 @@ NCU_TRAFFIC_BYTES: dict[tuple[str, str], float] = {
     # dout pre-pass + TMA main kernel (the split reduction is not captured)
     ("fuseconv_wgrad", "torch.float32"): 16783872 + 89954560,
     ("fuseconv_wgrad", "torch.bfloat16"): 8395264 + 42037760,
-    ("dyncat_fwd", "torch.float32"): 491238400,
-    ("dyncat_bwd", "torch.float32"): 464840192 + 594088448,
+    ("dyncat_fwd", "torch.float32"): 491269632,
+    ("dyncat_bwd", "torch.float32"): 466273536 + 593169408,
     ("dyncat_bwd", "torch.bfloat16"): 201383936 + 271141376,
 }
 
