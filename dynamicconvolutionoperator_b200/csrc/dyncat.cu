@@ -663,10 +663,22 @@ int launch_bwd_k(const void* x, const void* g, void* gk, int n, int c, int h, in
   return DDPM_OK;
 }
 
+// Shared memory of the scalar dX kernel: the three branch-gradient planes of
+// its tile with the halo. The largest halo that fits the 227 KB a CTA may opt
+// into is 39 ((128 + 78) x (16 + 78) x 3 x 4 bytes = 232,368).
+constexpr size_t kMaxSmemPerCta = 227 * 1024;
+constexpr size_t dx_stage_bytes(int R) {
+  return sizeof(float) * 3 * (size_t)(kDxTileW + 2 * R) * (kTileH + 2 * R);
+}
+constexpr int kMaxDxHalo = 39;
+static_assert(dx_stage_bytes(kMaxDxHalo) <= kMaxSmemPerCta &&
+                  dx_stage_bytes(kMaxDxHalo + 1) > kMaxSmemPerCta,
+              "kMaxDxHalo out of step with the dX tile");
+
 template <typename TX, typename TK, int KS, int D0, int D1, int D2>
 int launch_bwd_x(const void* k, const void* g, void* gx, int n, int c, int h, int w, Dil dil,
                  int R, cudaStream_t st) {
-  const size_t smem = sizeof(float) * 3 * (size_t)(kDxTileW + 2 * R) * (kTileH + 2 * R);
+  const size_t smem = dx_stage_bytes(R);
   auto fn = dyncat_bwd_x_kernel<TX, TK, KS, D0, D1, D2>;
   if (int rc = set_smem(fn, smem)) return rc;
   dim3 grid(n * c, (h + kTileH - 1) / kTileH, (w + kDxTileW - 1) / kDxTileW);
@@ -814,6 +826,12 @@ int dyncat_bwd(const void* x, int xdt, const void* k, const void* g, int kdt, vo
   if (gx == nullptr && gk == nullptr) return DDPM_OK;
   Dil dil{{d0, d1, d2}};
   const int R = (ks / 2) * max3(d0, d1, d2);
+  // The data gradient stages three zero-padded gradient planes of its tile:
+  // (128 + 2R) x (16 + 2R) floats each must fit one CTA's shared memory.
+  if (gx != nullptr && dx_stage_bytes(R) > kMaxSmemPerCta)
+    return set_error(DDPM_ERR_UNSUPPORTED,
+                     "dilation halo %d too large for the data gradient (at most %d)", R,
+                     kMaxDxHalo);
   DDPM_DYNCAT_DISPATCH(dispatch_bwd, ks, x, k, g, gx, gk, n, c, h, w, dil, R, st)
 }
 

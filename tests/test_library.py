@@ -11,6 +11,7 @@ import re
 from pathlib import Path
 
 import pytest
+import torch
 
 from dynamicconvolutionoperator_b200 import _lib
 
@@ -47,3 +48,16 @@ def test_argument_errors_return_codes_without_gpu():
     assert rc == -1
     with pytest.raises(RuntimeError, match="dtype"):
         _lib.call("ddpm_dyncat_bwd", 1, 9, 1, 1, 0, 1, 1, 1, 1, 1, 1, 3, 1, 3, 5, None)
+
+
+def test_dyncat_bwd_rejects_halos_the_data_gradient_cannot_stage():
+    """The data gradient stages its tile's three gradient planes with the
+    dilation halo; halos above 39 do not fit a CTA and are refused up front
+    (the tap gradient alone, and the forward, go to 64)."""
+    lib = _lib.load()
+    f32 = _lib.dtype_code(torch.float32)
+    args = (1, f32, 1, 1, f32)
+    rc = lib.ddpm_dyncat_bwd(*args, 1, 1, 1, 1, 8, 8, 3, 1, 40, 5, None)
+    assert rc != 0 and b"halo 40" in lib.ddpm_last_error()
+    rc = lib.ddpm_dyncat_bwd(*args, 1, None, 1, 1, 8, 8, 3, 1, 65, 5, None)
+    assert rc != 0 and b"halo" in lib.ddpm_last_error()
