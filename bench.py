@@ -42,6 +42,7 @@ REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
 METRIC = "DDPM fwd+bwd ms @B1 C64 256² K3; dyn-filter HBM TB/s vs ~8 TB/s peak"
+WORKLOAD = "configs[3] DDPM training step (fwd+bwd)"  # both arms, same workload
 C, H, W, K = 64, 256, 256, 3
 DILATIONS = (1, 3, 5)
 # 256^2 K3 FP32 fused training step, RTX 5090 (README.md:161-162).
@@ -549,8 +550,8 @@ def run_reference_arm(args):
         "n_gpus": args.gpus, "steps": n, "warmup": min(args.warmup, 1), "ms_per_step": round(ms, 3),
         "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
         "dtype": DTYPE_TAG[args.dtype], "data": "synthetic",
-        "config": {"workload": "configs[3] DDPM training step", "batch_per_gpu": args.batch,
-                   "channels": C, "height": H, "width": W, "kernel_size": K,
+        "config": {"workload": WORKLOAD, "batch_per_gpu": args.batch,
+                   "global_batch": args.batch, "channels": C, "height": H, "width": W, "kernel_size": K,
                    "dilations": list(DILATIONS), "parallelism": "cpu"},
         "cpu_baseline": {"value": round(ms, 3), "unit": "ms", "cores": cores, "kind": "port",
                          "sample": sample},
@@ -632,7 +633,7 @@ def main(argv=None):
             "dtype": DTYPE_TAG[args.dtype],
             "data": "synthetic",
             "config": {
-                "workload": "configs[3] DDPM training step (fwd+bwd)",
+                "workload": WORKLOAD,
                 "batch_per_gpu": args.batch, "global_batch": args.batch * world,
                 "channels": C, "height": H, "width": W, "kernel_size": K,
                 "dilations": list(DILATIONS), "path": headline["path"],
