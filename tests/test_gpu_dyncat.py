@@ -164,3 +164,21 @@ def test_dyncat_grad_x_vector_kernel_matches_scalar(shape, ks, dil, xdt, kdt):
     assert torch.equal(grads[0], grads[1])
     gold_gx, _ = orc.dynamic_cat_backward(x.double(), k.double(), g.double(), ks, dil)
     _check(grads[0], gold_gx, xdt if xdt != torch.float32 else kdt)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_dyncat_largest_accepted_data_gradient_halo(dtype):
+    """Halo 39, the largest the data gradient stages (232,368 bytes of shared
+    memory for its three planes), runs and matches the oracle."""
+    from dynamicconvolutionoperator_b200 import fused_dynamic_cat
+
+    ks, dil = 3, (1, 39, 5)
+    x, k, g = _inputs((1, 2, 20, 24), ks, dtype, dtype, seed=13)
+    xd = x.cuda().requires_grad_(True)
+    kd = k.cuda().requires_grad_(True)
+    out = fused_dynamic_cat(xd, kd, ks, dil)
+    gx, gk = torch.autograd.grad(out, (xd, kd), g.cuda())
+    _check(out, orc.dynamic_cat(x.double(), k.double(), ks, dil), dtype)
+    ggx, ggk = orc.dynamic_cat_backward(x.double(), k.double(), g.double(), ks, dil)
+    _check(gx, ggx, dtype)
+    _check(gk, ggk, dtype)
