@@ -91,3 +91,41 @@ def test_fuse_bias_fold_matches_conv2d():
     for a, e in zip(torch.autograd.grad(got, (cat, wt, b), g),
                     torch.autograd.grad(ref, (cat, wt, b), g)):
         torch.testing.assert_close(a, e, rtol=1e-12, atol=1e-12)
+
+
+def test_training_crossover_matches_reference_rule():
+    """Fused training above 16384 spatial tokens, and at exactly 16384 only in
+    FP32 (reference ``triton_impl.py:313-316``)."""
+    from dynamicconvolutionoperator_b200 import _kernels
+
+    for dt in (torch.float32, torch.bfloat16, torch.float16):
+        assert _kernels.auto_fuse_training(16385, 64, 3, dt)
+        assert not _kernels.auto_fuse_training(16383, 64, 3, dt)
+    assert _kernels.auto_fuse_training(16384, 64, 3, torch.float32)
+    assert not _kernels.auto_fuse_training(16384, 64, 3, torch.bfloat16)
+
+
+def test_fused_kernel_limits():
+    """C <= 64, K in {1, 3}, halo (K/2) * max(dilation) <= 8; the recompute
+    backward covers the same K (reference ``triton_impl.py:320``: K <= 3)."""
+    from dynamicconvolutionoperator_b200 import _kernels
+
+    ok = _kernels.fused_generator_supported
+    assert ok(64, 3, torch.float32) and ok(1, 1, torch.bfloat16, (1, 1, 1))
+    assert not ok(65, 3, torch.float32)
+    assert not ok(64, 5, torch.float32)
+    assert ok(64, 3, torch.float16, (1, 3, 8)) and not ok(64, 3, torch.float16, (1, 3, 9))
+    assert not ok(64, 3, torch.float64)
+    assert [k for k in (1, 3, 5, 7) if _kernels.fused_training_supported(k)] == [1, 3]
+
+
+@pytest.mark.parametrize(
+    "hw,ks,requested,expect",
+    [((128, 128), 3, None, True), ((128, 127), 3, None, False), ((256, 256), 5, None, False),
+     ((256, 256), 3, False, False), ((8, 8), 3, True, True), ((8, 8), 7, True, False)],
+)
+def test_module_training_path_choice(hw, ks, requested, expect):
+    """``fused_generator_training``: None follows the crossover, True / False
+    force the path, and K > 3 always materialises."""
+    m = DDPM(4, ks, fused_generator_training=requested)
+    assert m._use_fused_training(torch.empty(1, 4, *hw)) is expect
