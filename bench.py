@@ -1,30 +1,41 @@
 #!/usr/bin/env python
 """DDPM hot-path benchmark (driver contract: one JSON line on rank 0).
 
-Workload: DDPM forward+backward at B=1 per GPU,
-C=64, 256x256, K=3, dilations (1,3,5), seeded default init, x, y and the
-upstream gradient ~ N(0,1), synthetic data. One "step" = forward + backward of
-the whole module (generator/filter kernels and the 3x3 fuse conv, all on this
-library's kernels), plus, for N>1 GPUs, the NCCL gradient all-reduce of the
-batch-sharded data-parallel step (per-GPU batch fixed => weak scaling).
+Headline workload: batch-sharded DDPM training,
+global batch 64 split over the N ranks (64/N samples per GPU: strong
+scaling), C=64, 256x256, K=3, dilations (1,3,5), bf16, seeded default init
+replicated on every rank, x, y and the upstream gradient ~ N(0,1), synthetic
+data. One "step" = forward + backward of the whole module on the rank's shard
+(generator/filter kernels and the 3x3 fuse conv, all on this library's
+kernels) plus, for N>1, the NCCL all-reduce (average) of the parameter
+gradients, launched from the backward so it overlaps the generator backward.
+
+Also measured and reported under ``extra``: configs[3] (B=1 per GPU, fp32 and
+bf16; weak scaling at N>1) with the same step structure, and the per-kernel
+rooflines at B=1 in both dtypes (``kernels``, ``kernels_bf16``).
 
 Timing: W warm-up steps, then exactly K timed steps bracketed by barrier +
 synchronize; each step is timed with CUDA events on the launching stream and
 an L2 flush (a 256 MiB write) runs between steps outside the events. The
-device-time ``value`` replays the step as one CUDA graph with inputs resident
-in HBM; ``e2e`` runs the public API eagerly with the H2D copy of x, y and the
-upstream gradient from pinned host memory and the D2H read of the loss inside
-the timed region (the gradient's copy on a side stream overlapping the
-forward; the Python collector paused while timing). The max over ranks is
-reported.
+device-time ``value`` replays the step (all-reduce included) as one CUDA graph
+with inputs resident in HBM; ``e2e`` runs the public API eagerly with the H2D
+copy of x, y and the upstream gradient from pinned host memory and the D2H read
+of the loss inside the timed region (micro-batches of the shard: the copy of
+micro-batch i+1 overlaps the compute of micro-batch i, gradients accumulate,
+the all-reduce runs once; the Python collector paused while timing). The max
+over ranks is reported.
 
 ``--impl reference`` times the reference's CPU algorithm (the oracle port of
-``unfold_impl.DDPM`` in oracle/) on this host's cores for the same config.
+``unfold_impl.DDPM`` in oracle/) on this host's cores for the same config: a
+bounded sample of one-sample steps, scaled to the global batch.
+``--memory`` prints the temporary peak memory of one training step (the
+reference's ``gpu_memory_bench.py`` measurement).
 """
 
 from __future__ import annotations
 
 import argparse
+import contextlib
 import gc
 import json
 import os
@@ -42,10 +53,15 @@ REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
 METRIC = "DDPM fwd+bwd ms @B1 C64 256² K3; dyn-filter HBM TB/s vs ~8 TB/s peak"
-WORKLOAD = "configs[3] DDPM training step (fwd+bwd)"  # both arms, same workload
+WORKLOADS = {
+    "sharded": "configs[4] batch-sharded DDPM training step (fwd+bwd + gradient all-reduce)",
+    "b1": "configs[3] DDPM training step (fwd+bwd)",
+}
 C, H, W, K = 64, 256, 256, 3
 DILATIONS = (1, 3, 5)
-# 256^2 K3 FP32 fused training step, RTX 5090 (README.md:161-162).
+GLOBAL_BATCH = 64
+# Published absolute number for the configs[3] fp32 step: 256^2 K3 FP32 fused
+# training, RTX 5090 (reference README.md:161-162).
 PUBLISHED_FP32_MS = 3.66
 L2_FLUSH_BYTES = 256 * 1024**2
 DTYPES = {"fp32": torch.float32, "bf16": torch.bfloat16}
@@ -58,17 +74,26 @@ def parse_args(argv=None):
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--dtype", choices=list(DTYPES), default="fp32",
-                    help="headline dtype (the other one is reported under 'extra')")
-    ap.add_argument("--batch", type=int, default=1, help="per-GPU batch")
+    ap.add_argument("--workload", choices=list(WORKLOADS), default="sharded",
+                    help="headline: configs[4] (sharded, default) or configs[3] (b1)")
+    ap.add_argument("--global-batch", type=int, default=GLOBAL_BATCH,
+                    help="configs[4] global batch (split over the ranks)")
+    ap.add_argument("--dtype", choices=list(DTYPES), default=None,
+                    help="headline dtype (default: bf16 for sharded, fp32 for b1)")
     ap.add_argument("--path", choices=["auto", "fused", "materialised"], default="auto")
     ap.add_argument("--no-graph", action="store_true", help="time eager steps for 'value'")
-    ap.add_argument("--skip-extra", action="store_true", help="headline dtype only")
+    ap.add_argument("--skip-extra", action="store_true", help="headline workload only")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU oracle baseline leg")
+    ap.add_argument("--memory", action="store_true",
+                    help="print the temporary peak memory of one training step and exit")
     ap.add_argument("--profile-kernel", default=None,
                     help="only launch this library kernel (ncu capture target)")
     ap.add_argument("--profile-iters", type=int, default=3)
-    return ap.parse_args(argv)
+    ap.add_argument("--batch", type=int, default=1, help="per-GPU batch of --profile-kernel")
+    args = ap.parse_args(argv)
+    if args.dtype is None:
+        args.dtype = "bf16" if args.workload == "sharded" else "fp32"
+    return args
 
 
 # ------------------------------------------------------------------ clocks --
@@ -144,9 +169,11 @@ def build_model(dtype, path, device):
 
 
 def make_inputs(batch, dtype, rank):
+    """x, y and the upstream gradient of this rank's shard, seeded per rank
+    (the shards of one global batch), generated on the host."""
     gen = torch.Generator().manual_seed(1000 + rank)
     shape = (batch, C, H, W)
-    return [torch.randn(shape, generator=gen).to(dtype) for _ in range(3)]  # x, y, upstream
+    return [torch.randn(shape, generator=gen).to(dtype) for _ in range(3)]
 
 
 def step_fn(model, x, y, g, allreduce):
@@ -180,14 +207,18 @@ def time_steps(run, steps, flush, stream):
     return [a.elapsed_time(b) for a, b in times]
 
 
-def measure_dtype(args, dtype, device, rank, world, dist, timed_clocks=False):
+def measure(args, dtype, batch, device, rank, world, dist, timed_clocks=False, micro=None):
+    """Device-timed step (CUDA graph, inputs in HBM) and end-to-end step
+    (public API, host buffers) of ``batch`` samples on this rank, with the
+    gradient all-reduce at world > 1. ``micro``: the end-to-end step's
+    micro-batch size (copies of the next micro-batch overlap the compute)."""
     from dynamicconvolutionoperator_b200 import _lib
     from dynamicconvolutionoperator_b200.data_parallel import GradAllReducer
 
     model, taken = build_model(dtype, args.path, device)
-    hx, hy, hg = [t.pin_memory() for t in make_inputs(args.batch, dtype, rank)]
+    hx, hy, hg = [t.pin_memory() for t in make_inputs(batch, dtype, rank)]
     x, y, g = [t.to(device) for t in (hx, hy, hg)]
-    reducer = GradAllReducer(model) if world > 1 else None
+    reducer = GradAllReducer(model, overlap=True) if world > 1 else None
     allreduce = reducer.all_reduce if reducer is not None else None
     stream = torch.cuda.current_stream(device)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
@@ -208,23 +239,26 @@ def measure_dtype(args, dtype, device, rank, world, dist, timed_clocks=False):
     launches_per_step = _lib.launch_count() - n0
 
     use_graph = not args.no_graph
+    graph = None
+    allreduce_in_graph = False
     if use_graph:
         side = torch.cuda.Stream(device)
         side.wait_stream(stream)
         with torch.cuda.stream(side):
             for _ in range(3):
                 zero()
-                step_fn(model, x, y, g, None)
+                step_fn(model, x, y, g, allreduce)
         stream.wait_stream(side)
+        torch.cuda.synchronize()
         zero()
         graph = torch.cuda.CUDAGraph()
+        # the whole step, the overlapped NCCL all-reduce included, as one graph
         with torch.cuda.graph(graph):
-            step_fn(model, x, y, g, None)
+            step_fn(model, x, y, g, allreduce)
+        allreduce_in_graph = allreduce is not None
 
         def run():
             graph.replay()
-            if allreduce is not None:
-                allreduce()
     else:
         def run():
             zero()
@@ -244,34 +278,51 @@ def measure_dtype(args, dtype, device, rank, world, dist, timed_clocks=False):
     if dist is not None:
         dist.barrier()
     ms = sum(times) / len(times)
+    if graph is not None:
+        del graph  # before any later destroy_process_group: it holds NCCL calls
+        graph = None
+        zero()
 
     # ---- end to end through the public API: H2D inputs, fwd+bwd, D2H loss ----
-    # x and y are copied on the compute stream (the forward starts with them);
-    # the upstream gradient g is copied on a side stream that starts once those
-    # two copies are done (sharing the PCIe link with them would only delay the
-    # forward) and overlaps the forward, as a training loop's input pipeline
-    # would; the compute stream waits for it before the loss, so every copy
-    # lies inside the timed region.
+    # All H2D copies of the step are queued on a copy stream at the start of
+    # the timed region, micro-batch by micro-batch; the compute stream starts
+    # micro-batch i once its three copies are done, so the copies of i+1
+    # overlap the compute of i. Gradients accumulate over the micro-batches
+    # (every one but the last under no_sync), the all-reduce runs once, and
+    # the summed loss is read back. Every copy lies inside the timed region.
+    mb = micro or batch
+    if batch % mb:
+        mb = batch
+    bounds = [(i, i + mb) for i in range(0, batch, mb)]
     host_loss = torch.empty((), dtype=torch.float32).pin_memory()
     copy_stream = torch.cuda.Stream(device)
 
     def e2e_step():
         zero()
-        xe = hx.to(device, non_blocking=True)
-        ye = hy.to(device, non_blocking=True)
         copy_stream.wait_stream(stream)
+        ready = []
         with torch.cuda.stream(copy_stream):
-            ge = hg.to(device, non_blocking=True)
-        x_ = xe.detach().requires_grad_(True)
-        y_ = ye.detach().requires_grad_(True)
-        out = model(x_, y_)
-        stream.wait_stream(copy_stream)
-        ge.record_stream(stream)
-        out.backward(ge)
+            for a, b in bounds:
+                x[a:b].copy_(hx[a:b], non_blocking=True)
+                y[a:b].copy_(hy[a:b], non_blocking=True)
+                g[a:b].copy_(hg[a:b], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(copy_stream)
+                ready.append(ev)
+        loss = torch.zeros((), dtype=torch.float32, device=device)
+        for i, (a, b) in enumerate(bounds):
+            stream.wait_event(ready[i])
+            last = i == len(bounds) - 1
+            ctx = reducer.no_sync() if (reducer is not None and not last) else contextlib.nullcontext()
+            with ctx:
+                xe = x[a:b].detach().requires_grad_(True)
+                ye = y[a:b].detach().requires_grad_(True)
+                out = model(xe, ye)
+                out.backward(g[a:b])
+            with torch.no_grad():
+                loss += torch.dot(out.reshape(-1), g[a:b].reshape(-1)).float()
         if allreduce is not None:
             allreduce()
-        with torch.no_grad():
-            loss = torch.dot(out.reshape(-1), ge.reshape(-1)).float()
         host_loss.copy_(loss, non_blocking=True)
 
     for _ in range(3):
@@ -296,9 +347,9 @@ def measure_dtype(args, dtype, device, rank, world, dist, timed_clocks=False):
     if dist is not None:
         dist.barrier()
     e2e_ms = sum(e2e_times) / len(e2e_times)
-    if use_graph:
-        del graph
     in_bytes = sum(t.numel() * t.element_size() for t in (hx, hy, hg))
+    if reducer is not None:
+        reducer.remove_hooks()
     return {
         "ms": ms,
         "e2e_ms": e2e_ms,
@@ -309,6 +360,8 @@ def measure_dtype(args, dtype, device, rank, world, dist, timed_clocks=False):
         "clocks": clocks,
         "model": model,
         "inputs": (x, y),
+        "micro_batch": mb,
+        "allreduce_in_graph": allreduce_in_graph,
     }
 
 
@@ -321,7 +374,7 @@ def load_peaks():
     return 6650.0, 1590.0, "fallback"
 
 
-# DRAM bytes (read + write) per launch at this configuration, from the ncu
+# DRAM bytes (read + write) per launch at B=1 C=64 256x256 K=3, from the ncu
 # captures summarised in profiles/<kernel>_256.md, keyed by (kernel, dtype);
 # None where no capture exists. Outputs still resident in L2 when a captured
 # launch ends are not counted as writes.
@@ -347,28 +400,33 @@ NCU_TRAFFIC_BYTES: dict[tuple[str, str], float] = {
 }
 
 
-def library_kernels(model, x, y, dtype, device):
+def library_kernels(model, x, y, dtype, device, materialised=True):
     """Thunks launching each library kernel of the step on its own, with the
     operands it sees inside the step, and each kernel's roofline work unit:
-    (thunk, bound, algorithmic bytes or FLOPs per launch)."""
+    (thunk, bound, algorithmic bytes or FLOPs per launch). ``materialised``
+    adds the materialised-path filter kernels (their taps tensor is 27 C
+    planes per sample)."""
     from dynamicconvolutionoperator_b200 import _lib
 
     n = x.shape[0]
     elt = x.element_size()
     ncp = n * C * H * W
-    with torch.no_grad():
-        taps = model.generator(y).reshape(n, 3, C, K * K, H, W).contiguous()
+    if materialised:
+        with torch.no_grad():
+            taps = model.generator(y).reshape(n, 3, C, K * K, H, W).contiguous()
+        gk = torch.empty_like(taps)
+    else:
+        taps = gk = None
     out = torch.empty((n, 4 * C, H, W), dtype=dtype, device=device)
     gout = torch.randn((n, 4 * C, H, W), device=device).to(dtype)
     gx = torch.empty_like(x)
-    gk = torch.empty_like(taps)
     code = _lib.dtype_code(dtype)
     sh = _lib.stream_handle(device)
     from dynamicconvolutionoperator_b200 import _kernels
 
     gen_w = model.generator.weight.detach()
     gen_b = model.generator.bias.detach()
-    packed = _kernels.pack_generator_weight(gen_w, gen_b, C, K, use_cache=False)
+    packed = _kernels.pack_generator_weight(gen_w, gen_b, C, K)
     out2 = torch.empty_like(out)
     gy = torch.empty_like(y)
     gw = torch.empty((3 * C * K * K, C), dtype=dtype, device=device)
@@ -380,7 +438,7 @@ def library_kernels(model, x, y, dtype, device):
 
     fuse_w = model.fuse.weight.detach()
     fuse_b = model.fuse.bias.detach()
-    fpacked = _fuseconv.pack_fuse_weight(fuse_w, use_cache=False)
+    fpacked = _fuseconv.pack_fuse_weight(fuse_w)
     fout = torch.empty_like(x)
     fgout = torch.randn_like(x)
     fgx = torch.empty_like(out)
@@ -437,7 +495,7 @@ def library_kernels(model, x, y, dtype, device):
 
     keep = (taps, out, gout, gx, gk, packed, out2, gy, gw, gb, ws, fpacked, fout, fgout, fgx,
             fgw, fgb, fws, sy, fplanes, gplanes)
-    return keep, {
+    kernels = {
         "fuseconv_fwd": (fuse_fwd, "tensor", fuse_flops),
         "fuseconv_wgrad": (
             lambda: _lib.call("ddpm_fuseconv_bwd_weight", out.data_ptr(), fgout.data_ptr(),
@@ -461,15 +519,21 @@ def library_kernels(model, x, y, dtype, device):
             "hbm", (6 * K * K + 9) * ncp * elt,
         ),
     }
+    if not materialised:
+        del kernels["dyncat_fwd"], kernels["dyncat_bwd"]
+    return keep, kernels
 
 
-def kernel_roofline(model, x, y, dtype, steps, device):
+def kernel_roofline(model, x, y, dtype, steps, device, materialised=True):
     """Time the library's kernels of the step in isolation (CUDA events, L2
-    flushed before every launch) and return per-kernel roofline entries."""
+    flushed before every launch) and return per-kernel roofline entries.
+    ``traffic`` is the DRAM bytes of the B=1 ncu capture times the batch
+    (every kernel's traffic grows in proportion to the samples processed)."""
     hbm, tflops, src = load_peaks()
     stream = torch.cuda.current_stream(device)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
-    keep, kernels = library_kernels(model, x, y, dtype, device)
+    n = x.shape[0]
+    keep, kernels = library_kernels(model, x, y, dtype, device, materialised)
     res = {}
     for name, (fn, bound, work) in kernels.items():
         for _ in range(3):
@@ -481,6 +545,8 @@ def kernel_roofline(model, x, y, dtype, steps, device):
         else:
             achieved, peak, unit = work / (t * 1e-3) / 1e12, tflops, "TFLOP/s"
         traffic = NCU_TRAFFIC_BYTES.get((name, str(dtype)))
+        if traffic is not None:
+            traffic = int(traffic * n)
         res[name] = {
             "bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
             "frac": round(achieved / peak, 4), "traffic": traffic, "work": work,
@@ -491,14 +557,16 @@ def kernel_roofline(model, x, y, dtype, steps, device):
 
 
 def profile_kernel(args):
-    """Launch one library kernel ``--profile-iters`` times at the bench config
-    (the target of the committed ncu captures; prints nothing but 'ok')."""
+    """Launch one library kernel ``--profile-iters`` times at B=``--batch``
+    C=64 256x256 K=3 (the target of the committed ncu captures; prints
+    nothing but 'ok')."""
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
     dtype = DTYPES[args.dtype]
     model, _ = build_model(dtype, args.path, device)
     x, y, _ = [t.to(device) for t in make_inputs(args.batch, dtype, 0)]
-    keep, kernels = library_kernels(model, x, y, dtype, device)
+    keep, kernels = library_kernels(model, x, y, dtype, device,
+                                    materialised=args.profile_kernel.startswith("dyncat"))
     fn = kernels[args.profile_kernel][0]
     for _ in range(args.profile_iters):
         fn()
@@ -509,50 +577,68 @@ def profile_kernel(args):
 
 
 # -------------------------------------------------------------- CPU legs --
-def cpu_step_time(dtype, batch, budget_s=15.0, max_steps=10, warmup=1):
-    """Oracle (reference CPU algorithm) fwd+bwd ms per full step on host cores."""
+def cpu_sample_time(dtype, steps, warmup, budget_s=None):
+    """Median ms of one-sample forward+backward steps of the oracle port of
+    ``unfold_impl.DDPM`` (the reference's CPU algorithm) on all host cores."""
     from oracle import ddpm_oracle as orc
 
     cores = len(os.sched_getaffinity(0))
     torch.set_num_threads(cores)
     model = orc.make_model(C, K, dtype=dtype, seed=0)
-    x, y, g = orc.make_inputs((batch, C, H, W), dtype=dtype, seed=1000)
+    x, y, g = orc.make_inputs((1, C, H, W), dtype=dtype, seed=1000)
 
     def one():
         xr = x.clone().requires_grad_(True)
         yr = y.clone().requires_grad_(True)
         model.zero_grad(set_to_none=True)
         out = model(xr, yr)
-        (out.float() * g.float()).sum().backward()
+        out.backward(g)
 
     for _ in range(warmup):
         one()
     times, t_start = [], time.perf_counter()
-    while len(times) < max_steps and (time.perf_counter() - t_start) < budget_s:
+    while len(times) < max(steps, 1):
+        if budget_s is not None and times and time.perf_counter() - t_start > budget_s:
+            break
         t0 = time.perf_counter()
         one()
         times.append((time.perf_counter() - t0) * 1e3)
     return statistics.median(times), cores, len(times)
 
 
+def workload_config(args, world):
+    """The ``config`` object both arms print: the workload, not how it ran."""
+    if args.workload == "sharded":
+        glob, per = args.global_batch, args.global_batch // world
+        scaling = "strong"
+    else:
+        glob, per = world, 1
+        scaling = "weak"
+    return {
+        "workload": WORKLOADS[args.workload] + f", {args.dtype}",
+        "global_batch": glob, "batch_per_gpu": per,
+        "channels": C, "height": H, "width": W, "kernel_size": K,
+        "dilations": list(DILATIONS), "parallelism": f"dp{world}",
+        "l2": "flushed between steps (256 MiB write)",
+    }, scaling
+
+
 def run_reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     if rank != 0:
         return 0
-    dtype = DTYPES[args.dtype]
-    ms, cores, n = cpu_step_time(dtype, args.batch, budget_s=120.0,
-                                 max_steps=max(1, min(args.steps, 10)),
-                                 warmup=max(0, min(args.warmup, 1)))
-    sample = (f"{n} full fwd+bwd steps (median) of B={args.batch} C={C} {H}x{W} K={K} "
-              f"{args.dtype}, oracle port of unfold_impl.DDPM on {cores} host threads")
+    cfg, scaling = workload_config(args, world)
+    per_ms, cores, n = cpu_sample_time(DTYPES[args.dtype], args.steps, args.warmup)
+    ms = per_ms * cfg["global_batch"]
+    sample = (f"{n} timed one-sample fwd+bwd steps (median {per_ms:.1f} ms, after {args.warmup} "
+              f"warm-up) of C={C} {H}x{W} K={K} {args.dtype}, oracle port of unfold_impl.DDPM "
+              f"on {cores} host threads, x {cfg['global_batch']} samples of the global batch")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(ms, 3), "unit": "ms",
-        "n_gpus": args.gpus, "steps": n, "warmup": min(args.warmup, 1), "ms_per_step": round(ms, 3),
-        "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
-        "dtype": DTYPE_TAG[args.dtype], "data": "synthetic",
-        "config": {"workload": WORKLOAD, "batch_per_gpu": args.batch,
-                   "global_batch": args.batch, "channels": C, "height": H, "width": W, "kernel_size": K,
-                   "dilations": list(DILATIONS), "parallelism": "cpu"},
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+        "higher_is_better": False, "scaling": scaling, "vs_baseline": None,
+        "dtype": DTYPE_TAG[args.dtype], "data": "synthetic", "config": cfg,
         "cpu_baseline": {"value": round(ms, 3), "unit": "ms", "cores": cores, "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(ms, 3), "unit": "ms", "h2d_bytes_per_step": 0,
@@ -560,6 +646,50 @@ def run_reference_arm(args):
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+# ------------------------------------------------------------------ memory --
+def memory_peaks(device, resolution=H):
+    """Temporary peak memory of one B=1 C=64 K=3 training step, measured like
+    the reference's ``gpu_memory_bench.py:54-73`` (``max_memory_allocated``
+    minus the allocation before the step; loss = out.square().mean())."""
+    from dynamicconvolutionoperator_b200 import DDPM
+
+    res = []
+    for dname in ("fp32", "bf16"):
+        dtype = DTYPES[dname]
+        for path in ("fused", "materialised"):
+            torch.manual_seed(0)
+            module = DDPM(C, K, fused_generator_training=path == "fused")
+            module = module.to(device=device, dtype=dtype).train()
+            x = torch.randn(1, C, resolution, resolution, device=device, dtype=dtype,
+                            requires_grad=True)
+            y = torch.randn_like(x, requires_grad=True)
+
+            def step():
+                module.zero_grad(set_to_none=True)
+                x.grad = None
+                y.grad = None
+                module(x, y).square().mean().backward()
+
+            for _ in range(2):
+                step()
+            torch.cuda.synchronize()
+            module.zero_grad(set_to_none=True)
+            x.grad = None
+            y.grad = None
+            torch.cuda.empty_cache()
+            torch.cuda.reset_peak_memory_stats(device)
+            base = torch.cuda.memory_allocated(device)
+            step()
+            torch.cuda.synchronize()
+            peak = torch.cuda.max_memory_allocated(device)
+            res.append({"dtype": dname, "path": path, "resolution": resolution,
+                        "baseline_mib": round(base / 2**20, 1),
+                        "temporary_peak_mib": round((peak - base) / 2**20, 1)})
+            del module, x, y
+            torch.cuda.empty_cache()
+    return res
 
 
 # -------------------------------------------------------------------- main --
@@ -570,7 +700,7 @@ def main(argv=None):
     if args.profile_kernel:
         return profile_kernel(args)
 
-    # The fuse conv runs in true FP32 for the fp32 step: TF32 would put the
+    # The fuse conv runs without TF32 for the fp32 step: TF32 would put the
     # output outside the FP32 parity tolerance, which is measured the same way.
     torch.backends.cudnn.allow_tf32 = False
     torch.backends.cuda.matmul.allow_tf32 = False
@@ -579,23 +709,14 @@ def main(argv=None):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    if args.memory:
+        print(json.dumps({"memory": memory_peaks(device)}), flush=True)
+        return 0
     dist = None
     if world > 1:
         import torch.distributed as dist
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
-
-    headline = measure_dtype(args, DTYPES[args.dtype], device, rank, world, dist,
-                             timed_clocks=True)
-    extra = {}
-    if not args.skip_extra:
-        other = "bf16" if args.dtype == "fp32" else "fp32"
-        m = measure_dtype(args, DTYPES[other], device, rank, world, dist)
-        extra[other] = {"ms_per_step": round(m["ms"], 4), "e2e_ms": round(m["e2e_ms"], 4),
-                        "path": m["path"]}
-        del m
-    roof = kernel_roofline(headline["model"], *headline["inputs"], DTYPES[args.dtype],
-                           args.steps, device)
 
     def gather_max(v):
         if dist is None:
@@ -604,21 +725,63 @@ def main(argv=None):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return t.item()
 
+    memory = memory_peaks(device) if (world == 1 and not args.skip_extra) else None
+    cfg, scaling = workload_config(args, world)
+    if args.workload == "sharded" and args.global_batch % world:
+        raise SystemExit(f"global batch {args.global_batch} does not split over {world} GPUs")
+    per = cfg["batch_per_gpu"]
+    dtype = DTYPES[args.dtype]
+    headline = measure(args, dtype, per, device, rank, world, dist, timed_clocks=True,
+                       micro=4 if per >= 8 else None)
+    head_roof = kernel_roofline(headline["model"], *headline["inputs"], dtype, args.steps, device,
+                                materialised=(headline["path"] == "materialised"
+                                              or args.workload == "b1"))
     ms = gather_max(headline["ms"])
     e2e_ms = gather_max(headline["e2e_ms"])
+    head_info = {k: headline[k] for k in ("h2d_bytes", "d2h_bytes", "launches_per_step", "path",
+                                          "clocks", "micro_batch", "allreduce_in_graph")}
+    del headline
+    torch.cuda.empty_cache()
+
+    # configs[3] (B=1 per GPU) in both dtypes, with the per-kernel rooflines
+    extra, kernels = {}, {}
+    if args.workload == "b1":
+        kernels[args.dtype] = head_roof
+    if not args.skip_extra:
+        for dname in ("fp32", "bf16"):
+            if args.workload == "b1" and dname == args.dtype:
+                continue
+            m = measure(args, DTYPES[dname], 1, device, rank, world, dist)
+            kernels[dname] = kernel_roofline(m["model"], *m["inputs"], DTYPES[dname], args.steps,
+                                             device)
+            entry = {"workload": WORKLOADS["b1"] + f", {dname}", "batch_per_gpu": 1,
+                     "global_batch": world, "scaling": "weak",
+                     "ms_per_step": round(gather_max(m["ms"]), 4),
+                     "e2e_ms": round(gather_max(m["e2e_ms"]), 4), "path": m["path"],
+                     "h2d_bytes_per_step": m["h2d_bytes"]}
+            if dname == "fp32":
+                entry["vs_published_rtx5090_fp32_ms"] = round(entry["ms_per_step"] /
+                                                              PUBLISHED_FP32_MS, 4)
+            extra[f"configs[3]_{dname}"] = entry
+            del m
+            torch.cuda.empty_cache()
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        cms, cores, n = cpu_step_time(DTYPES[args.dtype], args.batch)
-        cpu = {"value": round(cms, 3), "unit": "ms", "cores": cores, "kind": "port",
-               "sample": f"{n} full fwd+bwd steps (median) of the same workload, oracle port "
-                         f"of unfold_impl.DDPM, {args.dtype}"}
+        steps = 10 if args.workload == "sharded" else 5
+        per_ms, cores, n = cpu_sample_time(dtype, steps, 1, budget_s=20.0)
+        cpu = {"value": round(per_ms * cfg["global_batch"], 3), "unit": "ms", "cores": cores,
+               "kind": "port",
+               "sample": f"{n} one-sample fwd+bwd steps (median {per_ms:.1f} ms) of the same "
+                         f"workload, oracle port of unfold_impl.DDPM, {args.dtype}, "
+                         f"x {cfg['global_batch']} samples"}
     # dominant kernel among those the headline step launches
     in_step = {"fused": ("gencat_fwd", "gencat_bwd_x", "gencat_bwd_yw"),
-               "materialised": ("dyncat_fwd", "dyncat_bwd")}[headline["path"]]
+               "materialised": ("dyncat_fwd", "dyncat_bwd")}[head_info["path"]]
     in_step = in_step + ("fuseconv_fwd", "fuseconv_dgrad", "fuseconv_wgrad")
-    dominant = max((k for k in roof if k in in_step), key=lambda k: roof[k]["ms"])
+    dominant = max((k for k in head_roof if k in in_step), key=lambda k: head_roof[k]["ms"])
     if rank == 0:
-        px = args.batch * world * H * W
+        px = cfg["global_batch"] * H * W
         line = {
             "metric": METRIC,
             "value": round(ms, 4),
@@ -628,29 +791,32 @@ def main(argv=None):
             "warmup": args.warmup,
             "ms_per_step": round(ms, 4),
             "higher_is_better": False,
-            "scaling": "weak",
-            "vs_baseline": round(ms / PUBLISHED_FP32_MS, 4) if args.dtype == "fp32" else None,
+            "scaling": scaling,
+            # a published number exists for the configs[3] fp32 step only
+            "vs_baseline": (round(ms / PUBLISHED_FP32_MS, 4)
+                            if (args.workload == "b1" and args.dtype == "fp32") else None),
             "dtype": DTYPE_TAG[args.dtype],
             "data": "synthetic",
-            "config": {
-                "workload": WORKLOAD,
-                "batch_per_gpu": args.batch, "global_batch": args.batch * world,
-                "channels": C, "height": H, "width": W, "kernel_size": K,
-                "dilations": list(DILATIONS), "path": headline["path"],
-                "parallelism": f"dp{world}", "cuda_graph": not args.no_graph,
-                "l2": "flushed between steps (256 MiB write)",
-                "cudnn_tf32": bool(torch.backends.cudnn.allow_tf32),
-            },
+            "config": cfg,
+            "run": {"path": head_info["path"], "cuda_graph": not args.no_graph,
+                    "allreduce_in_graph": head_info["allreduce_in_graph"],
+                    "allreduce": ("NCCL average over 2 flat buckets (fuse, generator), "
+                                  "launched from the backward" if world > 1 else None),
+                    "e2e_micro_batch": head_info["micro_batch"],
+                    "cudnn_tf32": bool(torch.backends.cudnn.allow_tf32)},
             "mpixel_per_s": round(px / (ms * 1e-3) / 1e6, 2),
             "e2e": {"value": round(e2e_ms, 4), "unit": "ms",
-                    "h2d_bytes_per_step": headline["h2d_bytes"],
-                    "d2h_bytes_per_step": headline["d2h_bytes"]},
-            "gpu_launches": int(headline["launches_per_step"] * args.steps),
-            "roofline": {k: v for k, v in roof[dominant].items() if k != "work"}
-            | {"kernel": dominant},
-            "kernels": roof,
-            "clocks": headline["clocks"],
+                    "h2d_bytes_per_step": head_info["h2d_bytes"],
+                    "d2h_bytes_per_step": head_info["d2h_bytes"]},
+            "gpu_launches": int(head_info["launches_per_step"] * args.steps),
+            "roofline": {k: v for k, v in head_roof[dominant].items() if k != "work"}
+            | {"kernel": dominant, "batch": per},
+            "kernels_headline": head_roof,
+            "kernels": kernels.get("fp32"),
+            "kernels_bf16": kernels.get("bf16"),
+            "clocks": head_info["clocks"],
             "cpu_baseline": cpu,
+            "memory": memory,
             "extra": extra,
         }
         print(json.dumps(line), flush=True)

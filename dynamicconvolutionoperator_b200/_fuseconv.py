@@ -20,27 +20,37 @@ the unstaged entry points bit for bit.
 
 from __future__ import annotations
 
-import weakref
-
 import torch
 
 from . import _lib
+from ._gradbuf import grad_buffer
 from ._kernels import FUSE_PLANES_ATTR
 
 FUSE_MAX_CIN = 256
 FUSE_MAX_COUT = 64
 
-_cache: dict[tuple, tuple] = {}
 
-
-def fuse_conv_supported(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None) -> bool:
-    """Shapes and dtypes the native kernels cover (stride 1, padding 1, 3x3)."""
+def fuse_conv_supported(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None,
+                        conv: torch.nn.Conv2d | None = None) -> bool:
+    """Shapes and dtypes the native kernels cover: a 3x3 convolution with
+    stride 1, padding 1 (zeros), dilation 1 and one group. With ``conv`` its
+    configuration is checked too, so a replaced ``fuse`` module of another
+    configuration goes to its own forward instead."""
+    if conv is not None and not (
+        tuple(conv.stride) == (1, 1)
+        and tuple(conv.padding) == (1, 1)
+        and tuple(conv.dilation) == (1, 1)
+        and conv.groups == 1
+        and conv.padding_mode == "zeros"
+    ):
+        return False
     return (
         x.is_cuda
         and x.ndim == 4
         and x.dtype in _lib.DTYPE_CODE
         and weight.dtype == x.dtype
         and (bias is None or bias.dtype == x.dtype)
+        and weight.ndim == 4
         and tuple(weight.shape[2:]) == (3, 3)
         and weight.shape[1] == x.shape[1]
         and weight.shape[0] <= FUSE_MAX_COUT
@@ -48,14 +58,11 @@ def fuse_conv_supported(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tenso
     )
 
 
-def pack_fuse_weight(weight: torch.Tensor, use_cache: bool) -> torch.Tensor:
+def pack_fuse_weight(weight: torch.Tensor) -> torch.Tensor:
     """The weight in the kernels' shared-memory operand layout (forward and
-    data-gradient images), reused while the same tensor is unchanged."""
-    key = (weight.data_ptr(), weight.device, weight.dtype, tuple(weight.shape))
-    if use_cache:
-        hit = _cache.get(key)
-        if hit is not None and hit[0]() is weight and hit[1] == weight._version:
-            return hit[2]
+    data-gradient images). Packed on every forward (one small launch): a copy
+    cached across calls would miss writes through ``param.data``, which leave
+    the version counter untouched."""
     cout, cin = weight.shape[0], weight.shape[1]
     code = _lib.dtype_code(weight.dtype)
     nbytes = int(_lib.load().ddpm_fuseconv_pack_bytes(cin, cout, code))
@@ -63,9 +70,6 @@ def pack_fuse_weight(weight: torch.Tensor, use_cache: bool) -> torch.Tensor:
     w = weight.contiguous()
     _lib.call("ddpm_fuseconv_pack", w.data_ptr(), cin, cout, code, packed.data_ptr(), nbytes,
               _lib.stream_handle(weight.device))
-    if use_cache:
-        _cache.clear()
-        _cache[key] = (weakref.ref(weight), weight._version, packed)
     return packed
 
 
@@ -82,11 +86,11 @@ def _stage_planes(src: torch.Tensor) -> tuple[torch.Tensor, int]:
 
 class _FuseConv(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, weight, bias, use_cache, planes_in):
+    def forward(ctx, x, weight, bias, planes_in):
         x = x.contiguous()
         n, cin, h, w = x.shape
         cout = weight.shape[0]
-        packed = pack_fuse_weight(weight, use_cache)
+        packed = pack_fuse_weight(weight)
         out = torch.empty((n, cout, h, w), dtype=x.dtype, device=x.device)
         b = bias.contiguous() if bias is not None else None
         # the producer's own planes of x when it wrote them, else one staging pass
@@ -95,6 +99,7 @@ class _FuseConv(torch.autograd.Function):
                   b.data_ptr() if b is not None else None, out.data_ptr(),
                   n, cin, cout, h, w, _lib.dtype_code(x.dtype), _lib.stream_handle(x.device))
         ctx.save_for_backward(x, weight)
+        ctx.bias = bias  # the parameter itself (its gradient buffer is looked up by identity)
         ctx.packed = packed
         ctx.has_bias = bias is not None
         return out
@@ -111,15 +116,16 @@ class _FuseConv(torch.autograd.Function):
             # both in one call: the data gradient reads grad_out from the
             # channel-last copy the weight gradient makes anyway
             gx = torch.empty_like(x)
-            gw = torch.empty_like(weight)
-            gb = torch.empty(cout, dtype=x.dtype, device=x.device) if need_b else None
+            gw = (grad_buffer(weight, weight.shape, x.dtype, x.device)
+                  if ctx.needs_input_grad[1] else torch.empty_like(weight))
+            gb = grad_buffer(ctx.bias, (cout,), x.dtype, x.device) if need_b else None
             nbytes = int(_lib.load().ddpm_fuseconv_bwd_weight_workspace_bytes(n, cin, cout, h, w))
             ws = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
             _lib.call("ddpm_fuseconv_bwd", x.data_ptr(), g.data_ptr(), ctx.packed.data_ptr(),
                       gx.data_ptr(), gw.data_ptr(), gb.data_ptr() if gb is not None else None,
                       ws.data_ptr(), nbytes, n, cin, cout, h, w, _lib.dtype_code(x.dtype),
                       _lib.stream_handle(x.device))
-            return gx, (gw if ctx.needs_input_grad[1] else None), gb, None, None
+            return gx, (gw if ctx.needs_input_grad[1] else None), gb, None
         if ctx.needs_input_grad[0]:
             gx = torch.empty_like(x)
             planes, nbytes = _stage_planes(g)
@@ -127,8 +133,9 @@ class _FuseConv(torch.autograd.Function):
                       ctx.packed.data_ptr(), gx.data_ptr(), n, cin, cout, h, w,
                       _lib.dtype_code(x.dtype), _lib.stream_handle(x.device))
         if ctx.needs_input_grad[1] or need_b:
-            gw = torch.empty_like(weight)
-            gb = torch.empty(cout, dtype=x.dtype, device=x.device) if need_b else None
+            gw = (grad_buffer(weight, weight.shape, x.dtype, x.device)
+                  if ctx.needs_input_grad[1] else torch.empty_like(weight))
+            gb = grad_buffer(ctx.bias, (cout,), x.dtype, x.device) if need_b else None
             nbytes = int(_lib.load().ddpm_fuseconv_bwd_weight_workspace_bytes(n, cin, cout, h, w))
             ws = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
             _lib.call("ddpm_fuseconv_bwd_weight", x.data_ptr(), g.data_ptr(), gw.data_ptr(),
@@ -137,7 +144,7 @@ class _FuseConv(torch.autograd.Function):
                       _lib.stream_handle(x.device))
             if not ctx.needs_input_grad[1]:
                 gw = None
-        return gx, gw, gb, None, None
+        return gx, gw, gb, None
 
 
 def fuse_conv(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None) -> torch.Tensor:
@@ -151,10 +158,7 @@ def fuse_conv(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None) 
         delattr(x, FUSE_PLANES_ATTR)
         if held[2] == x._version and x.is_contiguous():
             planes_in = (held[0], held[1])
-    # the packed weight is cached per weight version, except while a CUDA
-    # graph is captured (a cache hit would leave the pack out of the graph)
-    return _FuseConv.apply(x, weight, bias, not torch.cuda.is_current_stream_capturing(),
-                           planes_in)
+    return _FuseConv.apply(x, weight, bias, planes_in)
 
 
 __all__ = ["fuse_conv", "fuse_conv_supported", "pack_fuse_weight"]

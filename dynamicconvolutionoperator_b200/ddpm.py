@@ -13,12 +13,15 @@ sm_100a kernels of ``libddpm_b200.so``. CUDA tensors always take the native
 path; CPU tensors raise (the reference's CPU branches are not part of this
 build). The final 3x3 ``fuse`` convolution (a cuDNN call in the reference,
 ``triton_impl.py:294, 392``) runs on the library's own tensor-core kernels for
-C <= 64 (``native_fuse=True``, the default) and on cuDNN otherwise.
+C <= 64 (``native_fuse=True``, the default) and on cuDNN otherwise. Under
+autocast the module runs on the same native kernels in the autocast dtype
+(inputs and parameters cast once, differentiably).
 """
 
 from __future__ import annotations
 
 import torch
+import torch.nn.functional as F
 from torch import nn
 
 from . import _fuseconv, _kernels
@@ -97,15 +100,14 @@ class DDPM(nn.Module):
         self.fuse = nn.Conv2d(4 * dim, dim, 3, 1, 1)
 
     # ------------------------------------------------------------ dispatch --
-    def _fused_generator_ok(self, x: torch.Tensor, y: torch.Tensor) -> bool:
-        """Dtype/bias/autocast preconditions of the fused generator path
-        (reference ``triton_impl.py:322-329``) plus this build's kernel limits."""
-        gen = self.generator
+    def _fused_generator_ok(self, x: torch.Tensor, y: torch.Tensor,
+                            weight: torch.Tensor, bias: torch.Tensor | None) -> bool:
+        """Dtype/bias preconditions of the fused generator path (reference
+        ``triton_impl.py:322-329``) plus this build's kernel limits."""
         return (
-            not _autocast_enabled()
-            and x.dtype == y.dtype == gen.weight.dtype
-            and gen.bias is not None
-            and gen.bias.dtype == x.dtype
+            x.dtype == y.dtype == weight.dtype
+            and bias is not None
+            and bias.dtype == x.dtype
             and _kernels.fused_generator_supported(self.dim, self.kernel_size, x.dtype,
                                                    self.dilations)
         )
@@ -118,24 +120,21 @@ class DDPM(nn.Module):
             )
         return bool(requested) and _kernels.fused_training_supported(self.kernel_size)
 
-    def _cuda_cat(self, x: torch.Tensor, y: torch.Tensor, fuse_planes: bool = False) -> torch.Tensor:
-        """GPU path selection (replaces ``DDPM._cuda_cat``, ``triton_impl.py:305-348``).
-        ``fuse_planes``: the native fuse conv will consume the output, so the
-        fused forward may also write it as the fuse conv's staged planes."""
+    def _cuda_cat(self, x: torch.Tensor, y: torch.Tensor, weight: torch.Tensor,
+                  bias: torch.Tensor | None, fuse_planes: bool = False) -> torch.Tensor:
+        """GPU path selection (replaces ``DDPM._cuda_cat``, ``triton_impl.py:305-348``)
+        with the generator's ``weight`` and ``bias`` (the parameters, or their
+        autocast copies). ``fuse_planes``: the native fuse conv will consume the
+        output, so the fused forward may also write it as the fuse conv's
+        staged planes."""
         grad = torch.is_grad_enabled()
         fuse_training = grad and self._use_fused_training(x)
         want_fused = (self.fused_generator_inference and not grad) or fuse_training
-        if want_fused and self._fused_generator_ok(x, y):
+        if want_fused and self._fused_generator_ok(x, y, weight, bias):
             return _kernels.fused_generator_dynamic_cat(
-                x,
-                y,
-                self.generator.weight,
-                self.generator.bias,
-                self.kernel_size,
-                self.dilations,
-                _fuse_planes=fuse_planes,
+                x, y, weight, bias, self.kernel_size, self.dilations, _fuse_planes=fuse_planes,
             )
-        kernels = self.generator(y).reshape(
+        kernels = F.conv2d(y, weight, bias).reshape(
             x.shape[0],
             len(self.dilations),
             self.dim,
@@ -152,19 +151,57 @@ class DDPM(nn.Module):
                 "DDPM (B200 build) runs on CUDA tensors only; got tensors on "
                 f"{x.device}. The reference's CPU paths are not part of this build."
             )
+        gen, fuse = self.generator, self.fuse
+        params = (gen.weight, gen.bias, fuse.weight, fuse.bias)
+        if _autocast_enabled():
+            # Under autocast both convolutions of the module run in the autocast
+            # dtype (as nn.Conv2d does under autocast), so the whole module runs
+            # on the native kernels in that dtype: inputs and parameters are
+            # cast once (differentiably: gradients reach the FP32 parameters)
+            # and autocast is off inside. The reference instead declines its
+            # fused path under autocast (``triton_impl.py:325``); the output
+            # dtype is the autocast dtype on both.
+            ac = torch.get_autocast_dtype("cuda")
+            with torch.autocast("cuda", enabled=False):
+                x, y, *params = (t.to(ac) if t is not None and t.is_floating_point() else t
+                                 for t in (x, y, *params))
+                return self._forward_cuda(x, y, *params, autocast_dtype=ac)
+        return self._forward_cuda(x, y, *params)
+
+    def _forward_cuda(self, x, y, gen_w, gen_b, fuse_w, fuse_b, autocast_dtype=None):
         fuse = self.fuse
-        native = self.native_fuse and not _autocast_enabled()
-        cat_out = self._cuda_cat(x, y, fuse_planes=native and fuse.weight.dtype == x.dtype)
-        if native and _fuseconv.fuse_conv_supported(cat_out, fuse.weight, fuse.bias):
-            return _fuseconv.fuse_conv(cat_out, fuse.weight, fuse.bias)
+        if not _is_standard_fuse(fuse):
+            # a replaced fuse module of another kind or configuration runs its
+            # own forward (under the caller's autocast, if there was one)
+            cat_out = self._cuda_cat(x, y, gen_w, gen_b)
+            with torch.autocast("cuda", enabled=autocast_dtype is not None,
+                                dtype=autocast_dtype or torch.bfloat16):
+                return fuse(cat_out)
+        native = self.native_fuse and fuse_w.dtype == x.dtype
+        cat_out = self._cuda_cat(x, y, gen_w, gen_b, fuse_planes=native)
+        if native and _fuseconv.fuse_conv_supported(cat_out, fuse_w, fuse_b, fuse):
+            return _fuseconv.fuse_conv(cat_out, fuse_w, fuse_b)
         if (
             cat_out.dtype in (torch.bfloat16, torch.float16)
-            and fuse.weight.dtype == cat_out.dtype
-            and fuse.bias is not None
-            and not _autocast_enabled()
+            and fuse_w.dtype == cat_out.dtype
+            and fuse_b is not None
         ):
-            return _fuse_single_rounding(cat_out, fuse.weight, fuse.bias)
-        return fuse(cat_out)
+            return _fuse_single_rounding(cat_out, fuse_w, fuse_b)
+        return F.conv2d(cat_out, fuse_w, fuse_b, 1, 1)
+
+
+def _is_standard_fuse(fuse: nn.Module) -> bool:
+    """``fuse`` is the module's own kind of layer: a 3x3 ``nn.Conv2d`` with
+    stride 1, padding 1 (zeros), dilation 1 and one group."""
+    return (
+        type(fuse) is nn.Conv2d
+        and tuple(fuse.kernel_size) == (3, 3)
+        and tuple(fuse.stride) == (1, 1)
+        and tuple(fuse.padding) == (1, 1)
+        and tuple(fuse.dilation) == (1, 1)
+        and fuse.groups == 1
+        and fuse.padding_mode == "zeros"
+    )
 
 
 _BIAS_LANES = 8  # extra input channels carrying the folded bias (keeps Cin % 8 == 0)

@@ -34,7 +34,27 @@ def test_reference_arm_prints_one_contract_line():
     assert d["e2e"] == {"value": d["value"], "unit": "ms", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}
     assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["cores"] >= 1
-    assert d["config"]["workload"].startswith("configs[3]")
+    # the repo arm's default workload (configs[4], global batch 64, bf16), and
+    # the driver's --steps / --warmup honoured
+    assert d["config"]["workload"].startswith("configs[4]")
+    assert d["config"]["global_batch"] == 64 and d["dtype"] == "bf16"
+    assert d["steps"] == 1 and d["warmup"] == 0 and d["scaling"] == "strong"
+
+
+def test_both_arms_print_the_same_config():
+    import bench
+
+    for world in (1, 2, 8):
+        for argv in ([], ["--workload", "b1"]):
+            args = bench.parse_args(argv)
+            cfg, scaling = bench.workload_config(args, world)
+            assert cfg["parallelism"] == f"dp{world}"
+            if args.workload == "sharded":
+                assert (cfg["global_batch"], cfg["batch_per_gpu"]) == (64, 64 // world)
+                assert scaling == "strong"
+            else:
+                assert (cfg["global_batch"], cfg["batch_per_gpu"]) == (world, 1)
+                assert scaling == "weak"
 
 
 def test_reference_arm_other_ranks_exit_quietly():

@@ -12,7 +12,7 @@ import pytest
 import torch
 
 from tests import _golden as gold
-from tests._parity import ddpm_parity
+from tests._parity import compare, ddpm_parity, run_device
 
 pytestmark = pytest.mark.gpu
 
@@ -23,7 +23,7 @@ def _assert_ok(stats, fails):
     assert not fails, "\n".join(fails) + f"\n{stats}"
 
 
-@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("dtype", DTYPES + [torch.float16])
 @pytest.mark.parametrize("ks", [1, 3, 5])
 @pytest.mark.parametrize("fused", [False, True])
 def test_cfg2_regression_training(dtype, ks, fused):
@@ -71,7 +71,7 @@ def test_cfg1_inference_matches_golden():
         assert (out - gold.tensor(rec, "out")).abs().max().item() <= 2e-3
 
 
-@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("dtype", DTYPES + [torch.float16])
 @pytest.mark.parametrize("ks", [3, 5])
 @pytest.mark.parametrize("fused", [True, False])
 def test_cfg3_inference_128(dtype, ks, fused):
@@ -81,7 +81,7 @@ def test_cfg3_inference_128(dtype, ks, fused):
     _assert_ok(stats, fails)
 
 
-@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("dtype", DTYPES + [torch.float16])
 @pytest.mark.parametrize("fused", [True, False])
 def test_cfg4_training_256(dtype, fused):
     """B=1 C=64 256x256 K=3, fwd+bwd, every gradient."""
@@ -119,9 +119,8 @@ def _update_in_place(model):
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_weight_update_between_steps_repacks(dtype):
-    """The packed weight copies are cached per weight version: after an
-    in-place update (what an optimizer step does) the next training step must
-    use the new weights, exactly like a module built with them."""
+    """After an in-place update (what an optimizer step does) the next training
+    step must use the new weights, exactly like a module built with them."""
     from dynamicconvolutionoperator_b200 import DDPM
 
     torch.manual_seed(3)
@@ -180,3 +179,63 @@ def test_graph_replay_sees_weight_updates():
     for u, v in zip(got, ref):
         torch.testing.assert_close(u, v, rtol=1e-5, atol=1e-5)
     del graph
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_weight_write_through_data_is_seen(dtype):
+    """Writes through ``param.data`` leave the version counter untouched (what
+    ``dist.broadcast(p.data)``, EMA or legacy optimizer code do): the next
+    forward must still use the new weights, against the float64 oracle."""
+    from dynamicconvolutionoperator_b200 import DDPM
+    from oracle import ddpm_oracle as orc
+
+    shape = (1, 32, 24, 40)
+    first = orc.make_model(32, 3, dtype=dtype, seed=11)
+    second = orc.make_model(32, 3, dtype=dtype, seed=12)
+    dev = DDPM(32, 3, fused_generator_training=True).cuda().to(dtype)
+    dev.load_state_dict(first.state_dict())
+    x, y, g = orc.make_inputs(shape, dtype=dtype, seed=13, grad_seed=14)
+    run_device(dev, x, y, g)  # a forward + backward with the first weights
+    versions = [p._version for p in dev.parameters()]
+    for p, q in zip(dev.parameters(), second.parameters()):
+        p.data.copy_(q.detach().cuda())
+    assert [p._version for p in dev.parameters()] == versions
+    for grad in (None, g):
+        out, grads = run_device(dev, x, y, grad)
+        gold_out, gold_grads = orc.run_reference(second, x, y, grad=grad, dtype=torch.float64)
+        stats, fails = compare(out, grads, gold_out, gold_grads, dtype)
+        _assert_ok(stats, fails)
+
+
+@pytest.mark.parametrize("ac_dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("fused", [True, False])
+def test_autocast_runs_the_native_kernels(ac_dtype, fused):
+    """Under autocast the FP32 module runs in the autocast dtype on the native
+    kernels (fused or materialised), returns that dtype, and its output and
+    every gradient (x, y and the FP32 parameters) sit within the 16-bit
+    tolerance of the float64 oracle. Inputs and weights are exactly
+    representable in the autocast dtype, so the comparison measures the
+    kernels, not the cast."""
+    from dynamicconvolutionoperator_b200 import DDPM, _lib
+    from oracle import ddpm_oracle as orc
+
+    shape = (2, 24, 15, 17)
+    ref = orc.make_model(24, 3, dtype=ac_dtype, seed=15)
+    dev = DDPM(24, 3, fused_generator_training=fused, fused_generator_inference=fused).cuda()
+    dev.load_state_dict({k: v.float() for k, v in ref.state_dict().items()})
+    x, y, g = orc.make_inputs(shape, dtype=ac_dtype, seed=16, grad_seed=17)
+    xd = x.float().cuda().requires_grad_(True)
+    yd = y.float().cuda().requires_grad_(True)
+    n0 = _lib.launch_count()
+    with torch.autocast("cuda", dtype=ac_dtype):
+        out = dev(xd, yd)
+    assert out.dtype == ac_dtype
+    names = ["x", "y"] + [n for n, _ in dev.named_parameters()]
+    grads = torch.autograd.grad(out, [xd, yd, *dev.parameters()], g.cuda())
+    torch.cuda.synchronize()
+    assert _lib.launch_count() - n0 >= 4  # filter/generator and fuse kernels of the library
+    assert all(gr.dtype == torch.float32 for gr in grads)
+    gold_out, gold_grads = orc.run_reference(ref, x, y, grad=g, dtype=torch.float64)
+    stats, fails = compare(out.detach().cpu(), {k: v.cpu() for k, v in zip(names, grads)},
+                           gold_out, gold_grads, ac_dtype)
+    _assert_ok(stats, fails)

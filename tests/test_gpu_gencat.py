@@ -63,7 +63,7 @@ def test_gencat_forward_unstaged_abi(shape, ks, dtype):
     x, y, wt, b = _case(shape, ks, dtype)
     n, c, h, w = shape
     xd, yd, wd, bd = x.cuda(), y.cuda(), wt.cuda(), b.cuda()
-    packed = _kernels.pack_generator_weight(wd, bd, c, ks, use_cache=False)
+    packed = _kernels.pack_generator_weight(wd, bd, c, ks)
     out = torch.full((n, 4 * c, h, w), float("nan"), dtype=dtype, device="cuda")
     _lib.call("ddpm_gencat_fwd", xd.data_ptr(), yd.data_ptr(), packed.data_ptr(), bd.data_ptr(),
               out.data_ptr(), n, c, h, w, ks, 1, 3, 5, _lib.dtype_code(dtype),
@@ -123,7 +123,7 @@ def test_gencat_forward_writes_fuse_planes(shape, ks, dtype):
     lib = _lib.load()
     code = _lib.dtype_code(dtype)
     st = _lib.stream_handle(xd.device)
-    packed = _kernels.pack_generator_weight(wd, bd, c, ks, use_cache=False)
+    packed = _kernels.pack_generator_weight(wd, bd, c, ks)
     sb = int(lib.ddpm_gencat_stage_bytes(n, c, h, w, ks, 1, 3, 5, code))
     staged = torch.empty(sb, dtype=torch.uint8, device="cuda")
     _lib.call("ddpm_gencat_stage", xd.data_ptr(), yd.data_ptr(), staged.data_ptr(), sb,

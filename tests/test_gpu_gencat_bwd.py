@@ -55,7 +55,7 @@ def test_gencat_bwd_x(shape, ks, dtype, staged):
     g = torch.randn((n, 4 * c, h, w), generator=torch.Generator().manual_seed(5)).to(dtype)
     gx_gold, *_ = _gold_grads(x, y, wt, b, g, ks, (1, 3, 5))
     yd, wd, bd, gd = y.cuda(), wt.cuda(), b.cuda(), g.cuda()
-    packed = _kernels.pack_generator_weight(wd, bd, c, ks, use_cache=False)
+    packed = _kernels.pack_generator_weight(wd, bd, c, ks)
     gx = torch.full((n, c, h, w), float("nan"), dtype=dtype, device="cuda")
     stream = _lib.stream_handle(gx.device)
     if staged:
@@ -124,7 +124,7 @@ def test_gencat_bwd_yw(shape, ks, dtype, staged):
     g = torch.randn((n, 4 * c, h, w), generator=torch.Generator().manual_seed(6)).to(dtype)
     _, gy_gold, gw_gold, gb_gold = _gold_grads(x, y, wt, b, g, ks, (1, 3, 5))
     xd, yd, wd, bd, gd = x.cuda(), y.cuda(), wt.cuda(), b.cuda(), g.cuda()
-    packed = _kernels.pack_generator_weight(wd, bd, c, ks, use_cache=False)
+    packed = _kernels.pack_generator_weight(wd, bd, c, ks)
     gy = torch.full_like(yd, float("nan"))
     gw = torch.full((3 * c * ks * ks, c), float("nan"), dtype=dtype, device="cuda")
     gb = torch.full((3 * c * ks * ks,), float("nan"), dtype=dtype, device="cuda")
@@ -197,7 +197,7 @@ def test_max_halo_and_ragged_gradient_tiles(shape, dtype):
 
     with torch.no_grad():
         xd, yd, wd, bd = (t.detach() for t in ts)
-        packed = _kernels.pack_generator_weight(wd, bd, c, ks, use_cache=False)
+        packed = _kernels.pack_generator_weight(wd, bd, c, ks)
         o2 = torch.full((n, 4 * c, h, w), float("nan"), dtype=dtype, device="cuda")
         _lib.call("ddpm_gencat_fwd", xd.data_ptr(), yd.data_ptr(), packed.data_ptr(),
                   bd.data_ptr(), o2.data_ptr(), n, c, h, w, ks, *dil, _lib.dtype_code(dtype),

@@ -32,7 +32,7 @@ def _inputs(shape, ks, dtype):
     n, c, h, w = shape
     g = torch.randn((n, 4 * c, h, w), generator=torch.Generator().manual_seed(7)).to(dtype)
     xd, yd, wd, bd, gd = x.cuda(), y.cuda(), wt.cuda(), b.cuda(), g.cuda()
-    packed = _kernels.pack_generator_weight(wd, bd, c, ks, use_cache=False)
+    packed = _kernels.pack_generator_weight(wd, bd, c, ks)
     return xd, yd, packed, gd
 
 
