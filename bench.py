@@ -84,8 +84,18 @@ def parse_args(argv=None):
     ap.add_argument("--no-graph", action="store_true", help="time eager steps for 'value'")
     ap.add_argument("--skip-extra", action="store_true", help="headline workload only")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU oracle baseline leg")
+    ap.add_argument("--no-triton", action="store_true",
+                    help="skip timing the reference's Triton path on the GPU")
     ap.add_argument("--memory", action="store_true",
                     help="print the temporary peak memory of one training step and exit")
+    ap.add_argument("--launch-list", action="store_true",
+                    help="one eager step of the workload inside cudaProfilerStart/Stop (for "
+                         "ncu --profile-from-start off) and exit")
+    ap.add_argument("--triton-ref", action="store_true",
+                    help="time the reference's own Triton path (baseline/_ref) on cuda:0 for "
+                         "--workload/--dtype and exit (run by the main bench as a subprocess)")
+    ap.add_argument("--crossover", action="store_true",
+                    help="time fused vs materialised training steps over image sizes and exit")
     ap.add_argument("--profile-kernel", default=None,
                     help="only launch this library kernel (ncu capture target)")
     ap.add_argument("--profile-iters", type=int, default=3)
@@ -692,6 +702,118 @@ def memory_peaks(device, resolution=H):
     return res
 
 
+# ------------------------------------------------- reference Triton on GPU --
+REF_DIR = REPO / "baseline" / "_ref"
+
+
+def triton_reference_leg(args, device):
+    """The reference's stock CUDA path, ``triton_impl.DDPM`` on CUDA tensors
+    (its Triton kernels and cuDNN, ``triton_impl.py:305-392``), on this GPU for
+    the same workload: the "existing kernel" comparison. Eager forward +
+    backward from the upstream gradient, CUDA events, L2 flushed between steps;
+    Triton's JIT and autotuning happen in the warm-up. Returns a dict."""
+    if not (REF_DIR / "triton_impl.py").is_file():
+        return {"unavailable": "the reference is not installed in baseline/_ref"}
+    sys.path.insert(0, str(REF_DIR))
+    import triton_impl  # the reference's module, unmodified
+
+    if triton_impl._load_triton_ops() is None:
+        return {"unavailable": "the reference's Triton kernels do not import on this box"}
+    cfg, _ = workload_config(args, 1)
+    dtype = DTYPES[args.dtype]
+    torch.manual_seed(0)
+    model = triton_impl.DDPM(C, K).to(device=device, dtype=dtype)
+    x, y, g = [t.to(device) for t in make_inputs(cfg["batch_per_gpu"], dtype, 0)]
+    stream = torch.cuda.current_stream(device)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
+
+    def run():
+        for p in model.parameters():
+            p.grad = None
+        step_fn(model, x, y, g, None)
+
+    for _ in range(max(args.warmup, 2)):
+        run()
+    torch.cuda.synchronize()
+    ts = time_steps(run, args.steps, flush, stream)
+    return {"ms_per_step": round(sum(ts) / len(ts), 4), "batch": cfg["batch_per_gpu"],
+            "dtype": args.dtype, "workload": cfg["workload"],
+            "cudnn_tf32": bool(torch.backends.cudnn.allow_tf32),
+            "timing": "eager fwd+bwd, CUDA events, L2 flushed between steps"}
+
+
+def run_triton_legs(args, legs, timeout_s=420):
+    """Each reference Triton measurement in its own process (a failure there
+    cannot touch this process's CUDA context)."""
+    out = {}
+    for name, extra in legs:
+        cmd = [sys.executable, str(REPO / "bench.py"), "--triton-ref", "--steps", str(args.steps),
+               "--warmup", str(args.warmup)] + extra
+        try:
+            res = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout_s,
+                                 env=dict(os.environ, WORLD_SIZE="1", RANK="0", LOCAL_RANK="0"))
+            lines = [ln for ln in res.stdout.splitlines() if ln.startswith("{")]
+            if res.returncode == 0 and lines:
+                out[name] = json.loads(lines[-1])["triton_ref"]
+            else:
+                tail = (res.stderr or res.stdout).strip().splitlines()[-1:] or ["no output"]
+                out[name] = {"unavailable": f"exit {res.returncode}: {tail[0][:300]}"}
+        except subprocess.TimeoutExpired:
+            out[name] = {"unavailable": f"did not finish within {timeout_s} s"}
+    return out
+
+
+# --------------------------------------------------------------- crossover --
+CROSSOVER_SIZES = (32, 48, 64, 96, 128, 192, 256)
+
+
+def crossover(args, device):
+    """Fused vs materialised training step (B=1, C=64, K=3) at square image
+    sizes, both dtypes: graph-replayed device time, L2 flushed between steps.
+    The measurement behind the module's automatic training-path choice."""
+    from dynamicconvolutionoperator_b200 import DDPM
+
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
+    stream = torch.cuda.current_stream(device)
+    rows = []
+    for dname in ("fp32", "bf16"):
+        dtype = DTYPES[dname]
+        for hw in CROSSOVER_SIZES:
+            row = {"dtype": dname, "hw": hw, "tokens": hw * hw}
+            for path in ("fused", "materialised"):
+                torch.manual_seed(0)
+                model = DDPM(C, K, fused_generator_training=path == "fused")
+                model = model.to(device=device, dtype=dtype)
+                gen = torch.Generator().manual_seed(7)
+                x, y, g = (torch.randn((1, C, hw, hw), generator=gen).to(dtype).to(device)
+                           for _ in range(3))
+
+                def zero():
+                    for p in model.parameters():
+                        p.grad = None
+
+                side = torch.cuda.Stream(device)
+                side.wait_stream(stream)
+                with torch.cuda.stream(side):
+                    for _ in range(3):
+                        zero()
+                        step_fn(model, x, y, g, None)
+                stream.wait_stream(side)
+                torch.cuda.synchronize()
+                zero()
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    step_fn(model, x, y, g, None)
+                for _ in range(args.warmup):
+                    graph.replay()
+                ts = time_steps(graph.replay, max(args.steps, 10), flush, stream)
+                row[path + "_ms"] = round(statistics.median(ts), 4)
+                del graph, model
+            row["fused_faster"] = row["fused_ms"] < row["materialised_ms"]
+            rows.append(row)
+    return rows
+
+
 # -------------------------------------------------------------------- main --
 def main(argv=None):
     args = parse_args(argv)
@@ -700,6 +822,13 @@ def main(argv=None):
     if args.profile_kernel:
         return profile_kernel(args)
 
+    if args.triton_ref:
+        # the reference's stock path with PyTorch's defaults (cuDNN may use
+        # TF32, the faster setting for its fuse conv)
+        device = torch.device("cuda", 0)
+        torch.cuda.set_device(device)
+        print(json.dumps({"triton_ref": triton_reference_leg(args, device)}), flush=True)
+        return 0
     # The fuse conv runs without TF32 for the fp32 step: TF32 would put the
     # output outside the FP32 parity tolerance, which is measured the same way.
     torch.backends.cudnn.allow_tf32 = False
@@ -711,6 +840,28 @@ def main(argv=None):
     torch.cuda.set_device(device)
     if args.memory:
         print(json.dumps({"memory": memory_peaks(device)}), flush=True)
+        return 0
+    if args.crossover:
+        print(json.dumps({"crossover": crossover(args, device)}), flush=True)
+        return 0
+
+    if args.launch_list:
+        cfg, _ = workload_config(args, world)
+        dtype = DTYPES[args.dtype]
+        model, _ = build_model(dtype, args.path, device)
+        x, y, g = [t.to(device) for t in make_inputs(cfg["batch_per_gpu"], dtype, rank)]
+        for _ in range(max(args.warmup, 1)):
+            for p in model.parameters():
+                p.grad = None
+            step_fn(model, x, y, g, None)
+        torch.cuda.synchronize()
+        for p in model.parameters():
+            p.grad = None
+        torch.cuda.profiler.start()
+        step_fn(model, x, y, g, None)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        print("ok")
         return 0
     dist = None
     if world > 1:
@@ -775,6 +926,13 @@ def main(argv=None):
                "sample": f"{n} one-sample fwd+bwd steps (median {per_ms:.1f} ms) of the same "
                          f"workload, oracle port of unfold_impl.DDPM, {args.dtype}, "
                          f"x {cfg['global_batch']} samples"}
+    triton = None
+    if rank == 0 and world == 1 and not args.skip_extra and not args.no_triton:
+        legs = [(f"{args.workload}_{args.dtype}", ["--workload", args.workload, "--dtype",
+                                                   args.dtype])]
+        legs += [(f"configs[3]_{d}", ["--workload", "b1", "--dtype", d]) for d in ("fp32", "bf16")
+                 if not (args.workload == "b1" and d == args.dtype)]
+        triton = run_triton_legs(args, legs)
     # dominant kernel among those the headline step launches
     in_step = {"fused": ("gencat_fwd", "gencat_bwd_x", "gencat_bwd_yw"),
                "materialised": ("dyncat_fwd", "dyncat_bwd")}[head_info["path"]]
@@ -816,6 +974,7 @@ def main(argv=None):
             "kernels_bf16": kernels.get("bf16"),
             "clocks": head_info["clocks"],
             "cpu_baseline": cpu,
+            "triton_b200": triton,
             "memory": memory,
             "extra": extra,
         }

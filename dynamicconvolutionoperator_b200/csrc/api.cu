@@ -31,6 +31,7 @@ int dyncat_fwd(const void* x, int xdt, const void* k, int kdt, void* out, int n,
 int dyncat_bwd(const void* x, int xdt, const void* k, const void* g, int kdt, void* gx, void* gk,
                int n, int c, int h, int w, int ks, int d0, int d1, int d2, cudaStream_t st);
 
+int gencat_fwd_test_skip_arrive(int enable);
 int umma_selftest(int variant, const void* a, const void* b, float* d, int n, int k, int shift,
                   cudaStream_t st);
 
@@ -112,6 +113,11 @@ int ddpm_dyncat_bwd(const void* x, int x_dtype, const void* kernels, const void*
   ddpm::clear_error();
   return ddpm::dyncat_bwd(x, x_dtype, kernels, grad_out, k_dtype, grad_x, grad_k, n, c, h, w,
                           ksize, d0, d1, d2, static_cast<cudaStream_t>(stream));
+}
+
+int ddpm_test_skip_arrive(int enable) {
+  ddpm::clear_error();
+  return ddpm::gencat_fwd_test_skip_arrive(enable);
 }
 
 int ddpm_umma_selftest(int variant, const void* a, const void* b, float* d, int n, int k,

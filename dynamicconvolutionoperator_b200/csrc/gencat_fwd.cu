@@ -65,6 +65,14 @@ namespace {
 
 using namespace gencat;
 
+// Test hook (ddpm_test_skip_arrive): when set, one y-tile producer thread of
+// CTA 0 withholds its arrival for the CTA's first tile, so that CTA's MMA
+// issuer waits on a phase that never completes. The bounded wait gives up
+// after kWaitNs, records its code in the device status word, and every role
+// unwinds (TMEM is freed): the failure path of the kernels, exercised without
+// a fault. Zero in normal operation.
+__device__ int g_test_skip_arrive;
+
 template <typename T, int KS, bool kStaged = false>
 struct FwdCfg {
   static constexpr bool kSplit = IoTraits<T>::kSplit;
@@ -297,6 +305,8 @@ gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
     // ---- y-tile producers ----------------------------------------------------
     const int pt = threadIdx.x - 64;
     const YPlan<Cfg::kYItems> plan = make_yplan<Cfg::kYItems>(Ck, pt, Cfg::kProducers);
+    // the test hook: this thread withholds its first arrival (see g_test_skip_arrive)
+    const bool withhold = pt == 1 && blockIdx.x == 0 && *(volatile int*)&g_test_skip_arrive;
     uint32_t it = 0;
     for (int tile = first_tile; tile < p.num_tiles; tile += tile_step, ++it) {
       const int yb = it % NY;
@@ -315,7 +325,7 @@ gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
           if constexpr (Cfg::kSplit)
             tc::tma_load_4d(ys + kTileM * Ck * 2, &maps.ymap, (w0 + 8) * 2, h0 + maps.ph, 0,
                             p.N + n, &y_full[yb]);
-        } else {
+        } else if (!(withhold && it == 0)) {
           tc::mbar_arrive(&y_full[yb]);
         }
       } else {
@@ -325,7 +335,7 @@ gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
                                                      ys + kTileM * Ck * 2, n, C, Ck,
                                                      Cfg::kBiasInGemm ? C : -1, H, W, h0, w0);
         tc::fence_proxy_async_smem();
-        tc::mbar_arrive(&y_full[yb]);
+        if (!(withhold && it == 0)) tc::mbar_arrive(&y_full[yb]);
       }
     }
   } else if (warp < Cfg::kFirstEpiWarp) {
@@ -622,6 +632,12 @@ int gencat_fwd_ex(const void* x, const void* y, const void* staged, size_t stage
     case DDPM_F32: return dispatch<float>(ks, prm, maps, use_staged, st);
   }
   return set_error(DDPM_ERR_INVALID_ARG, "unknown dtype %d", dt);
+}
+
+int gencat_fwd_test_skip_arrive(int enable) {
+  const int v = enable ? 1 : 0;
+  DDPM_CUDA_TRY(cudaMemcpyToSymbol(g_test_skip_arrive, &v, sizeof(int)));
+  return DDPM_OK;
 }
 
 int gencat_fwd(const void* x, const void* y, const void* staged, size_t staged_bytes,

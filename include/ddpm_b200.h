@@ -329,8 +329,24 @@ DDPM_API int ddpm_gencat_bwd_yw_static(const void* x, const void* y, const void*
                                        int ksize, int d0, int d1, int d2, int dtype,
                                        void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Test-only exports (no reference counterpart). They exist for this
+ * library's own tests; production callers never need them.
+ * ------------------------------------------------------------------------- */
+
 /*
- * Diagnostic (no reference counterpart): one 128 x n x k bf16 tcgen05 UMMA
+ * Test hook of the bounded waits: with `enable` != 0, the next fused generator
+ * forwards (ddpm_gencat_fwd*) on the current device have one producer thread
+ * of CTA 0 withhold an mbarrier arrival, so a wait in that CTA runs out after
+ * its limit (2 s): the kernel records a nonzero code (ddpm_device_status),
+ * unwinds, frees its tensor memory and returns; its outputs are invalid.
+ * No fault and no hang: the context stays usable. Call again with 0 to
+ * restore normal operation.
+ */
+DDPM_API int ddpm_test_skip_arrive(int enable);
+
+/*
+ * Diagnostic (test-only; no reference counterpart): one 128 x n x k bf16 tcgen05 UMMA
  * on a single CTA with the operand layouts the fused kernels use.
  * a: [128 + shift, k] row-major bf16, b: [n, k] row-major bf16,
  * d: [128, n] row-major fp32, d[m, j] = sum_i a[shift + m, i] * b[j, i].

@@ -1,6 +1,6 @@
 """Parity harness: the CUDA DDPM against the CPU oracle (float64 gold).
 
-Tolerance policy (survey "tolerance realism"):
+Tolerance policy:
   * fp32: output, dX, dY max-abs <= 2e-3; parameter gradients max-abs
     normalised by max|gold| <= 2e-3 (parameter grads reach |g| ~ 2e3 at 256^2,
     where even the fp32 reference differs from float64 by ~4e-3 absolute).
