@@ -186,18 +186,21 @@ def make_inputs(batch, dtype, rank):
     return [torch.randn(shape, generator=gen).to(dtype) for _ in range(3)]
 
 
-def step_fn(model, x, y, g, allreduce):
+def step_fn(model, x, y, g, allreduce, loss=True):
     # x and y take part in autograd (dX and dY are computed), as in the
     # reference's training benchmarks (gpu_bench.py:275-300).
     # g is the upstream gradient of the module output (d loss / d out for
-    # loss = <out, g>): backward starts from it directly, and the loss value
-    # read back to the host is the one dot product
+    # loss = <out, g>): backward starts from it directly. With ``loss`` the
+    # loss value (the one dot product) is formed for a read-back to the host;
+    # the training step itself never needs it.
     x = x.detach().requires_grad_(True)
     y = y.detach().requires_grad_(True)
     out = model(x, y)
     out.backward(g)
     if allreduce is not None:
         allreduce()
+    if not loss:
+        return None
     with torch.no_grad():
         return torch.dot(out.reshape(-1), g.reshape(-1)).float()
 
@@ -263,8 +266,9 @@ def measure(args, dtype, batch, device, rank, world, dist, timed_clocks=False, m
         zero()
         graph = torch.cuda.CUDAGraph()
         # the whole step, the overlapped NCCL all-reduce included, as one graph
+        # (the loss read-back belongs to the end-to-end step below)
         with torch.cuda.graph(graph):
-            step_fn(model, x, y, g, allreduce)
+            step_fn(model, x, y, g, allreduce, loss=False)
         allreduce_in_graph = allreduce is not None
 
         def run():
@@ -272,7 +276,7 @@ def measure(args, dtype, batch, device, rank, world, dist, timed_clocks=False, m
     else:
         def run():
             zero()
-            step_fn(model, x, y, g, allreduce)
+            step_fn(model, x, y, g, allreduce, loss=False)
 
     for _ in range(args.warmup):
         run()
@@ -956,7 +960,10 @@ def main(argv=None):
             "dtype": DTYPE_TAG[args.dtype],
             "data": "synthetic",
             "config": cfg,
-            "run": {"path": head_info["path"], "cuda_graph": not args.no_graph,
+            "run": {"value_step": "forward + backward of the module on the shard (+ the "
+                                  "gradient all-reduce at N > 1) as one CUDA graph; the loss "
+                                  "read-back is part of e2e",
+                    "path": head_info["path"], "cuda_graph": not args.no_graph,
                     "allreduce_in_graph": head_info["allreduce_in_graph"],
                     "allreduce": ("NCCL average over 2 flat buckets (fuse, generator), "
                                   "launched from the backward" if world > 1 else None),

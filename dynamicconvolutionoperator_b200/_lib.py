@@ -101,6 +101,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _c_int, [_c_ptr] * 5 + [_c_size] + [_c_int] * 6 + [_c_ptr]
     ),
     "ddpm_test_skip_arrive": (_c_int, [_c_int]),
+    "ddpm_test_disable_tma": (_c_int, [_c_int]),
     "ddpm_umma_selftest": (
         _c_int, [_c_int, _c_ptr, _c_ptr, _c_ptr, _c_int, _c_int, _c_int, _c_ptr]
     ),

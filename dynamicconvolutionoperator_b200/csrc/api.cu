@@ -32,6 +32,7 @@ int dyncat_bwd(const void* x, int xdt, const void* k, const void* g, int kdt, vo
                int n, int c, int h, int w, int ks, int d0, int d1, int d2, cudaStream_t st);
 
 int gencat_fwd_test_skip_arrive(int enable);
+int dyncat_set_tma_disabled(int disabled);
 int umma_selftest(int variant, const void* a, const void* b, float* d, int n, int k, int shift,
                   cudaStream_t st);
 
@@ -113,6 +114,11 @@ int ddpm_dyncat_bwd(const void* x, int x_dtype, const void* kernels, const void*
   ddpm::clear_error();
   return ddpm::dyncat_bwd(x, x_dtype, kernels, grad_out, k_dtype, grad_x, grad_k, n, c, h, w,
                           ksize, d0, d1, d2, static_cast<cudaStream_t>(stream));
+}
+
+int ddpm_test_disable_tma(int disabled) {
+  ddpm::clear_error();
+  return ddpm::dyncat_set_tma_disabled(disabled);
 }
 
 int ddpm_test_skip_arrive(int enable) {

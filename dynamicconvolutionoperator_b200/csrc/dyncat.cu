@@ -808,11 +808,36 @@ int check_common(const void* x, int xdt, const void* k, int kdt, int n, int c, i
   if (xdt == DDPM_F32 && kdt == DDPM_F16) return FN<float, __half>(__VA_ARGS__);              \
   return set_error(DDPM_ERR_UNSUPPORTED, "dtype pair (x=%d, kernels=%d) not supported", xdt, kdt);
 
+// TMA-fed kernels (dyncat_tma.cu) for K = 3, dilations (1, 3, 5), one dtype
+// and 16-byte aligned rows; the kernels above serve every other case.
+bool dyncat_tma_eligible(int xdt, int kdt, int w, int ks, int d0, int d1, int d2,
+                         std::initializer_list<const void*> ptrs);
+int dyncat_fwd_tma(const void* x, const void* k, void* out, int n, int c, int h, int w, int dt,
+                   cudaStream_t st);
+int dyncat_bwdk_tma(const void* x, const void* g, void* gk, int n, int c, int h, int w, int dt,
+                    cudaStream_t st);
+int dyncat_bwdx_tma(const void* k, const void* g, void* gx, int n, int c, int h, int w, int dt,
+                    cudaStream_t st);
+
+namespace {
+bool g_tma_disabled = false;  // test hook: ddpm_test_disable_tma
+}
+
+int dyncat_set_tma_disabled(int disabled) {
+  g_tma_disabled = disabled != 0;
+  return DDPM_OK;
+}
+
 int dyncat_fwd(const void* x, int xdt, const void* k, int kdt, void* out, int n, int c, int h,
                int w, int ks, int d0, int d1, int d2, cudaStream_t st) {
   int rc = check_common(x, xdt, k, kdt, n, c, h, w, ks, d0, d1, d2);
   if (rc) return rc;
   DDPM_CHECK_ARG(out != nullptr, "null output pointer");
+  if (!g_tma_disabled && dyncat_tma_eligible(xdt, kdt, w, ks, d0, d1, d2, {x, k, out})) {
+    rc = dyncat_fwd_tma(x, k, out, n, c, h, w, xdt, st);
+    if (rc != DDPM_ERR_UNSUPPORTED) return rc;
+    clear_error();  // a tensor map the driver rejected: the kernels above
+  }
   Dil dil{{d0, d1, d2}};
   const int R = (ks / 2) * max3(d0, d1, d2);
   DDPM_DYNCAT_DISPATCH(dispatch_fwd, ks, x, k, out, n, c, h, w, dil, R, st)
@@ -832,6 +857,25 @@ int dyncat_bwd(const void* x, int xdt, const void* k, const void* g, int kdt, vo
     return set_error(DDPM_ERR_UNSUPPORTED,
                      "dilation halo %d too large for the data gradient (at most %d)", R,
                      kMaxDxHalo);
+  if (!g_tma_disabled && dyncat_tma_eligible(xdt, kdt, w, ks, d0, d1, d2, {x, k, g, gx, gk})) {
+    if (gk != nullptr) {
+      rc = dyncat_bwdk_tma(x, g, gk, n, c, h, w, xdt, st);
+      if (rc == DDPM_OK)
+        gk = nullptr;  // done
+      else if (rc != DDPM_ERR_UNSUPPORTED)
+        return rc;
+      clear_error();
+    }
+    if (gx != nullptr) {
+      rc = dyncat_bwdx_tma(k, g, gx, n, c, h, w, xdt, st);
+      if (rc == DDPM_OK)
+        gx = nullptr;
+      else if (rc != DDPM_ERR_UNSUPPORTED)
+        return rc;
+      clear_error();
+    }
+    if (gx == nullptr && gk == nullptr) return DDPM_OK;
+  }
   DDPM_DYNCAT_DISPATCH(dispatch_bwd, ks, x, k, g, gx, gk, n, c, h, w, dil, R, st)
 }
 

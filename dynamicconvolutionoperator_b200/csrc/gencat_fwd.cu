@@ -543,19 +543,25 @@ namespace {
 
 // Zero frame of staged fuse planes whose interior the forward writes: plane
 // rows 0 and Hp-1, plane columns 0..7 and W+8..Wp-1, and channel groups at or
-// beyond `gvalid`. Block = one plane row (part, n, group, row).
-__global__ void __launch_bounds__(128) plane_frame_zero_kernel(uint4* __restrict__ planes,
-                                                               int G, int Hp, int Wp, int W,
-                                                               int gvalid) {
-  const int i = blockIdx.x % Hp;
-  const int g = (blockIdx.x / Hp) % G;
-  uint4* row = planes + (size_t)blockIdx.x * Wp;
+// beyond `gvalid`. One warp per plane row (part, n, group, row), rows strided
+// over a grid of a few blocks per SM: an interior row is two short runs of
+// 16-byte cells, one store instruction each.
+__global__ void __launch_bounds__(256) plane_frame_zero_kernel(uint4* __restrict__ planes,
+                                                               int rows, int G, int Hp, int Wp,
+                                                               int W, int gvalid) {
+  const int lane = threadIdx.x & 31;
+  const int nwarps = (gridDim.x * blockDim.x) >> 5;
+  const int tail = Wp - (W + 8);
   const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-  if (i == 0 || i == Hp - 1 || g >= gvalid) {
-    for (int j = threadIdx.x; j < Wp; j += blockDim.x) row[j] = z;
-  } else {
-    const int tail = Wp - (W + 8);
-    for (int j = threadIdx.x; j < 8 + tail; j += blockDim.x) row[j < 8 ? j : W + j] = z;
+  for (int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows; r += nwarps) {
+    const int i = r % Hp;
+    const int g = (r / Hp) % G;
+    uint4* row = planes + (size_t)r * Wp;
+    if (i == 0 || i == Hp - 1 || g >= gvalid) {
+      for (int j = lane; j < Wp; j += 32) row[j] = z;
+    } else {
+      for (int j = lane; j < 8 + tail; j += 32) row[j < 8 ? j : W + j] = z;
+    }
   }
 }
 
@@ -585,9 +591,12 @@ int gencat_fwd_ex(const void* x, const void* y, const void* staged, size_t stage
     prm.pl_G = pl4.G;
     prm.pl_Hp = pl4.Hp;
     prm.pl_Wp = pl4.Wp;
-    const unsigned rows = (unsigned)(pl4.parts * pl4.N * pl4.G * pl4.Hp);
-    plane_frame_zero_kernel<<<rows, 128, 0, st>>>(static_cast<uint4*>(planes), pl4.G, pl4.Hp,
-                                                  pl4.Wp, w, (4 * c) / 8);
+    const long long rows = (long long)pl4.parts * pl4.N * pl4.G * pl4.Hp;
+    DDPM_CHECK_ARG(rows < (1LL << 31), "too many plane rows");
+    const long long blocks = (rows + 7) / 8;
+    const int grid = (int)(blocks < 8LL * gencat::num_sms() ? blocks : 8LL * gencat::num_sms());
+    plane_frame_zero_kernel<<<grid, 256, 0, st>>>(static_cast<uint4*>(planes), (int)rows, pl4.G,
+                                                  pl4.Hp, pl4.Wp, w, (4 * c) / 8);
     DDPM_CHECK_LAUNCH("plane_frame_zero_kernel");
   }
   prm.x = x;

@@ -346,6 +346,13 @@ DDPM_API int ddpm_gencat_bwd_yw_static(const void* x, const void* y, const void*
 DDPM_API int ddpm_test_skip_arrive(int enable);
 
 /*
+ * Test hook of the materialised filter: with `disabled` != 0 (this process,
+ * all devices) ddpm_dyncat_fwd / ddpm_dyncat_bwd skip their TMA-fed kernels
+ * and run the register-fed ones, so tests can compare the two bit for bit.
+ */
+DDPM_API int ddpm_test_disable_tma(int disabled);
+
+/*
  * Diagnostic (test-only; no reference counterpart): one 128 x n x k bf16 tcgen05 UMMA
  * on a single CTA with the operand layouts the fused kernels use.
  * a: [128 + shift, k] row-major bf16, b: [n, k] row-major bf16,
