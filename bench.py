@@ -408,9 +408,11 @@ NCU_TRAFFIC_BYTES: dict[tuple[str, str], float] = {
     # dout pre-pass + TMA main kernel (the split reduction is not captured)
     ("fuseconv_wgrad", "torch.float32"): 16783872 + 89954560,
     ("fuseconv_wgrad", "torch.bfloat16"): 8395264 + 42037760,
-    ("dyncat_fwd", "torch.float32"): 491269632,
-    ("dyncat_bwd", "torch.float32"): 466273536 + 593169408,
-    ("dyncat_bwd", "torch.bfloat16"): 201383936 + 271141376,
+    # the TMA-fed filter kernels (dyncat_tma.cu): forward; dK + dX
+    ("dyncat_fwd", "torch.float32"): 469865984 + 57570304,
+    ("dyncat_fwd", "torch.bfloat16"): 234918144 + 22441472,
+    ("dyncat_bwd", "torch.float32"): 67156992 + 394124544 + 516594944 + 16864000,
+    ("dyncat_bwd", "torch.bfloat16"): 33578496 + 167493632 + 258332928 + 7923456,
 }
 
 
@@ -862,7 +864,7 @@ def main(argv=None):
         for p in model.parameters():
             p.grad = None
         torch.cuda.profiler.start()
-        step_fn(model, x, y, g, None)
+        step_fn(model, x, y, g, None, loss=False)  # the device-timed step
         torch.cuda.synchronize()
         torch.cuda.profiler.stop()
         print("ok")

@@ -67,6 +67,7 @@ struct WgParams {
   const void* dout;  // [N, Cout, H, W]
   float* partial;    // [splits][nic][3][128][3*Np]
   float* db_partial; // [splits][Np] or null
+  float* db_mid;     // level-2 rows of the db reduction
   int N, H, W, Cin, Cout, Np, nic;
   int tiles_w, num_tiles, splits;
   int vec;  // W % 8 == 0 and 16-byte aligned tensors: branch-free vector loads
@@ -354,28 +355,33 @@ done:
 
 // dW[o, i, ky, kx] = sum over splits of the partials. Blocks below `dw_blocks`
 // walk the partials' own layout four columns (output channels) per thread, so
-// the split-strided float4 reads coalesce; the dW writes scatter. Each later
-// block reduces the db partials [parts][Np] of one output channel in a fixed
-// order.
+// the split-strided float4 reads coalesce; the dW writes scatter. The
+// `db_blocks` blocks after them reduce the db partials [parts][Np] in two
+// levels: block j sums a contiguous range of parts for every output channel
+// (64 consecutive threads read one 64-channel row, so the reads coalesce; four
+// row lanes are combined in a fixed order) into db_mid[j][Np]; the final
+// kernel sums db_mid over j in order. Deterministic, like the dW sum.
+constexpr int kDbMidBlocks = 128;  // most level-1 db blocks (db_mid rows)
+
 template <typename T>
 __global__ void __launch_bounds__(256) fuseconv_wgrad_reduce_kernel(
-    const float* __restrict__ partial, const float* __restrict__ db_part, T* __restrict__ dw,
-    T* __restrict__ db, int Cin, int Cout, int Np, int nic, int splits, int db_parts,
-    int dw_blocks) {
+    const float* __restrict__ partial, const float* __restrict__ db_part,
+    float* __restrict__ db_mid, T* __restrict__ dw, int Cin, int Cout, int Np, int nic,
+    int splits, int db_parts, int dw_blocks, int db_blocks) {
   if ((int)blockIdx.x >= dw_blocks) {
-    const int o = blockIdx.x - dw_blocks;
+    const int j = blockIdx.x - dw_blocks;
+    const int per = (db_parts + db_blocks - 1) / db_blocks;
+    const int k0 = j * per, k1 = min(db_parts, k0 + per);
+    const int o = threadIdx.x & 63, lane4 = threadIdx.x >> 6;  // Np <= 64
     float acc = 0.f;
-    for (int k = threadIdx.x; k < db_parts; k += blockDim.x) acc += db_part[(size_t)k * Np + o];
-    __shared__ float red[8];
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+    if (o < Np)
+      for (int k = k0 + lane4; k < k1; k += 4) acc += db_part[(size_t)k * Np + o];
+    __shared__ float red[4][64];
+    red[lane4][o] = acc;
     __syncthreads();
-    if (threadIdx.x == 0) {
-      float t = 0.f;
-      for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += red[i];
-      db[o] = from_f32<T>(t);
-    }
+    if (threadIdx.x < Np)
+      db_mid[(size_t)j * Np + threadIdx.x] =
+          ((red[0][threadIdx.x] + red[1][threadIdx.x]) + red[2][threadIdx.x]) + red[3][threadIdx.x];
     return;
   }
   const long long stride = (long long)nic * 3 * 128 * 3 * Np;  // floats per split
@@ -410,16 +416,38 @@ __global__ void __launch_bounds__(256) fuseconv_wgrad_reduce_kernel(
 }
 
 template <typename T>
-int launch_wgrad_reduce(const float* partial, const float* db_part, void* dw, void* db, int cin,
-                        int cout, int Np, int nic, int splits, int db_parts, cudaStream_t st) {
+__global__ void __launch_bounds__(64) fuseconv_db_final_kernel(const float* __restrict__ db_mid,
+                                                               T* __restrict__ db, int Cout,
+                                                               int Np, int rows) {
+  const int o = threadIdx.x;
+  if (o >= Cout) return;
+  float acc = 0.f;
+  for (int j = 0; j < rows; ++j) acc += db_mid[(size_t)j * Np + o];
+  db[o] = from_f32<T>(acc);
+}
+
+template <typename T>
+int launch_wgrad_reduce(const float* partial, const float* db_part, float* db_mid, void* dw,
+                        void* db, int cin, int cout, int Np, int nic, int splits, int db_parts,
+                        cudaStream_t st) {
   const long long quads = (long long)nic * 3 * 128 * 3 * Np / 4;
   long long blocks = (quads + 255) / 256;
   if (blocks > 1024) blocks = 1024;
   const int dw_blocks = (int)blocks;
-  fuseconv_wgrad_reduce_kernel<T><<<dw_blocks + (db != nullptr ? cout : 0), 256, 0, st>>>(
-      partial, db_part, static_cast<T*>(dw), static_cast<T*>(db), cin, cout, Np, nic, splits,
-      db_parts, dw_blocks);
+  int db_blocks = 0;
+  if (db != nullptr) {
+    db_blocks = (db_parts + 255) / 256;
+    if (db_blocks > kDbMidBlocks) db_blocks = kDbMidBlocks;
+  }
+  fuseconv_wgrad_reduce_kernel<T><<<dw_blocks + db_blocks, 256, 0, st>>>(
+      partial, db_part, db_mid, static_cast<T*>(dw), cin, cout, Np, nic, splits, db_parts,
+      dw_blocks, db_blocks);
   DDPM_CHECK_LAUNCH("fuseconv_wgrad_reduce_kernel");
+  if (db != nullptr) {
+    fuseconv_db_final_kernel<T><<<1, 64, 0, st>>>(db_mid, static_cast<T*>(db), cout, Np,
+                                                  db_blocks);
+    DDPM_CHECK_LAUNCH("fuseconv_db_final_kernel");
+  }
   return DDPM_OK;
 }
 
@@ -706,7 +734,7 @@ done:
 
 struct WgPlan {
   int Np, nic, splits, tiles_w, num_tiles;
-  size_t partial_bytes, ws_bytes;
+  size_t partial_bytes, mid_off, ws_bytes;  // mid_off: the db reduction's level-2 rows
 };
 
 WgPlan plan_wgrad(int n, int cin, int cout, int h, int w, int tw) {
@@ -720,7 +748,8 @@ WgPlan plan_wgrad(int n, int cin, int cout, int h, int w, int tw) {
   if (sp > q.num_tiles) sp = q.num_tiles;
   q.splits = sp;
   q.partial_bytes = (size_t)sp * q.nic * 3 * 128 * 3 * q.Np * sizeof(float);
-  q.ws_bytes = q.partial_bytes + (size_t)sp * q.Np * sizeof(float);
+  q.mid_off = (q.partial_bytes + (size_t)sp * q.Np * sizeof(float) + 255) / 256 * 256;
+  q.ws_bytes = q.mid_off + (size_t)kDbMidBlocks * q.Np * sizeof(float);
   return q;
 }
 
@@ -728,7 +757,7 @@ WgPlan plan_wgrad(int n, int cin, int cout, int h, int w, int tw) {
 struct WtPlan {
   WgPlan g;
   int strips;  // 64-column pre-pass strips per row (db partials per row)
-  size_t dbp_off, hi_off, lo_off, ws_bytes;
+  size_t dbp_off, hi_off, lo_off, mid_off, ws_bytes;
 };
 
 inline size_t round256(size_t v) { return (v + 255) / 256 * 256; }
@@ -741,7 +770,8 @@ WtPlan plan_wgrad_tma(int n, int cin, int cout, int h, int w, int tw, bool split
   t.dbp_off = round256(t.g.partial_bytes);
   t.hi_off = round256(t.dbp_off + (size_t)n * h * t.strips * t.g.Np * sizeof(float));
   t.lo_off = round256(t.hi_off + plane);
-  t.ws_bytes = split ? t.lo_off + plane : t.lo_off;
+  t.mid_off = round256(split ? t.lo_off + plane : t.lo_off);
+  t.ws_bytes = t.mid_off + (size_t)kDbMidBlocks * t.g.Np * sizeof(float);
   return t;
 }
 
@@ -755,7 +785,8 @@ int run_wgrad_reg(const WgParams& prm, void* dw, void* db, cudaStream_t st) {
   DDPM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total));
   fn<<<prm.nic * 3 * prm.splits, Cfg::kThreads, L.total, st>>>(prm);
   DDPM_CHECK_LAUNCH("fuseconv_wgrad_kernel");
-  return launch_wgrad_reduce<T>(prm.partial, prm.db_partial, dw, db, prm.Cin, prm.Cout, prm.Np,
+  return launch_wgrad_reduce<T>(prm.partial, prm.db_partial, prm.db_mid, dw, db, prm.Cin,
+                                prm.Cout, prm.Np,
                                 prm.nic, prm.splits, prm.splits, st);
 }
 
@@ -819,8 +850,8 @@ int run_wgrad_tma(const void* cat, const void* gout, void* gw, void* gb, uint8_t
   DDPM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   fn<<<prm.nic * 3 * prm.splits, Cfg::kThreads, smem, st>>>(prm);
   DDPM_CHECK_LAUNCH("fuseconv_wgrad_tma_kernel");
-  return launch_wgrad_reduce<T>(prm.partial, dbp, gw, gb, cin, cout, Np, prm.nic, prm.splits,
-                                n * h * t.strips, st);
+  return launch_wgrad_reduce<T>(prm.partial, dbp, reinterpret_cast<float*>(ws + t.mid_off), gw,
+                                gb, cin, cout, Np, prm.nic, prm.splits, n * h * t.strips, st);
 }
 
 }  // namespace
@@ -938,6 +969,7 @@ int fuseconv_wgrad(const void* cat, const void* gout, void* gw, void* gb, void* 
   prm.db_partial = gb != nullptr
                        ? reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + q.partial_bytes)
                        : nullptr;
+  prm.db_mid = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + q.mid_off);
   prm.N = n;
   prm.H = h;
   prm.W = w;

@@ -409,6 +409,9 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
       const bool px_ok = w < W;
       const T* gn = gout + (size_t)n * 4 * C * P;
       float acc[Cfg::kBlkPerWG][16];
+      unsigned long long acc2[8];    // staged path: channel pairs (2c, 2c+1) of acc[0]
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc2[i] = 0ull;
       float g0[Cfg::kBlkPerWG][16];  // x-branch gradient
       T g0raw[16];  // staged: loaded during the last unit, converted at the tile end
 #pragma unroll
@@ -478,9 +481,12 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
 #pragma unroll
                 for (int cl = 0; cl < 16; ++cl) dv[cur][cl] += bs[cl];
               }
-              round_taps<T>(dv[cur]);
+              // taps rounded to the I/O type a pair per conversion, then two
+              // FMAs per instruction (same products and sums as fmaf per value)
 #pragma unroll
-              for (int cl = 0; cl < 16; ++cl) acc[0][cl] = fmaf(dv[cur][cl], gv[cl], acc[0][cl]);
+              for (int i = 0; i < 8; ++i)
+                acc2[i] = f2_fma(tap_pair<T>(dv[cur][2 * i], dv[cur][2 * i + 1]),
+                                 f2_pack(gv[2 * i], gv[2 * i + 1]), acc2[i]);
             }
             tc::tc_fence_before();
             tc::mbar_arrive(&t_empty[tq % NB]);
@@ -534,6 +540,8 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
         if constexpr (kStaged) {
 #pragma unroll
           for (int cl = 0; cl < 16; ++cl) g0[0][cl] = to_f32<T>(g0raw[cl]);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) f2_unpack(acc2[i], acc[0][2 * i], acc[0][2 * i + 1]);
         } else {
 #pragma unroll
           for (int bi = 0; bi < Cfg::kBlkPerWG; ++bi) {

@@ -36,6 +36,24 @@ def _inputs(shape, ks, dtype):
     return xd, yd, packed, gd
 
 
+STATIC_SCRATCH_BYTES = 8 << 20
+
+
+def _partials_bytes(n, c, h, w, ks):
+    """Bytes of dW/db partials the workspace entry's split plan uses (its
+    split count, uncapped): channel-group batches of at most 512 accumulator
+    columns share the SMs, the rest of the SMs split the spatial tiles."""
+    cp = (c + 15) // 16 * 16
+    nw = (c + 1 + 15) // 16 * 16
+    ng = (cp // 16) * ((3 * ks * ks + 7) // 8)
+    gb = min(512 // nw, ng)
+    nbatches = (ng + gb - 1) // gb
+    tiles = n * ((h + 7) // 8) * ((w + 15) // 16)
+    splits = min(max(torch.cuda.get_device_properties(0).multi_processor_count // nbatches, 1),
+                 tiles)
+    return splits * ng * 128 * nw * 4
+
+
 def _outputs(yd, c, ks):
     kk = 3 * c * ks * ks
     return (torch.full_like(yd, float("nan")),
@@ -56,6 +74,11 @@ def test_static_scratch_matches_workspace_entry(shape, ks, dtype):
 
     gy_ref, gw_ref, gb_ref = _outputs(yd, c, ks)
     ws_bytes = int(_lib.load().ddpm_gencat_bwd_workspace_bytes(n, c, h, w, ks))
+    need = _partials_bytes(n, c, h, w, ks)
+    assert need <= ws_bytes  # the workspace covers the plan's partials
+    if shape == SHAPES[-1]:
+        # the case that must run the static entry with a capped split count
+        assert need > STATIC_SCRATCH_BYTES
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
     _lib.call("ddpm_gencat_bwd_yw", xd.data_ptr(), yd.data_ptr(), packed.data_ptr(),
               gd.data_ptr(), gy_ref.data_ptr(), gw_ref.data_ptr(), gb_ref.data_ptr(),
