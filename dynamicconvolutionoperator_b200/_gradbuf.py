@@ -24,6 +24,8 @@ import torch
 
 # id(param) -> [weakref to param, view, armed]
 _views: dict[int, list] = {}
+# callables (params, buffers) told when a backward has written gradients
+_listeners: list = []
 
 
 def attach(param: torch.Tensor, view: torch.Tensor) -> None:
@@ -67,4 +69,26 @@ def grad_buffer(param: torch.Tensor | None, shape, dtype: torch.dtype,
     return torch.empty(shape, dtype=dtype, device=device)
 
 
-__all__ = ["arm", "attach", "detach", "grad_buffer", "view_of"]
+def add_listener(fn) -> None:
+    """Have ``fn(params, buffers)`` called whenever the library's backward has
+    written the gradients of ``params`` into ``buffers`` (on the current
+    stream, before the backward returns and before autograd stores them as
+    ``param.grad``)."""
+    _listeners.append(fn)
+
+
+def remove_listener(fn) -> None:
+    if fn in _listeners:
+        _listeners.remove(fn)
+
+
+def grads_written(params, buffers) -> None:
+    """Called by a backward once the gradient kernels of ``params`` have been
+    launched into ``buffers`` (the work that follows in the same backward may
+    then overlap with whatever a listener starts)."""
+    for fn in list(_listeners):
+        fn(tuple(params), tuple(buffers))
+
+
+__all__ = ["add_listener", "arm", "attach", "detach", "grad_buffer", "grads_written",
+           "remove_listener", "view_of"]

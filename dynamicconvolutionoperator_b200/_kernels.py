@@ -13,7 +13,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from ._gradbuf import grad_buffer
+from ._gradbuf import grad_buffer, grads_written
 
 
 def _require_cuda(*tensors: torch.Tensor) -> None:
@@ -280,10 +280,9 @@ class _GeneratorDynamicCat(torch.autograd.Function):
             full = need_y and grad_w is not None
             staged = ctx.staged
             sb = staged.numel()
-            if need_x:
-                _lib.call("ddpm_gencat_bwd_x_staged", staged.data_ptr(), sb, packed.data_ptr(),
-                          bias.data_ptr(), grad_out.data_ptr(), grad_x.data_ptr(),
-                          n, c, h, w, ks, d0, d1, d2, code, stream)
+            # dY + dW/db first: once the weight gradients are written, a
+            # listener (the data-parallel reducer) may start their all-reduce,
+            # which then runs while dX computes
             if full:
                 ws_bytes = int(_lib.load().ddpm_gencat_bwd_workspace_bytes(n, c, h, w, ks))
                 ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
@@ -303,6 +302,12 @@ class _GeneratorDynamicCat(torch.autograd.Function):
                           grad_b.data_ptr() if grad_b is not None else None,
                           ws.data_ptr() if ws is not None else None, ws_bytes,
                           n, c, h, w, ks, d0, d1, d2, code, stream)
+            if need_w and need_b:
+                grads_written((weight, ctx.bias), (grad_w, grad_b))
+            if need_x:
+                _lib.call("ddpm_gencat_bwd_x_staged", staged.data_ptr(), sb, packed.data_ptr(),
+                          bias.data_ptr(), grad_out.data_ptr(), grad_x.data_ptr(),
+                          n, c, h, w, ks, d0, d1, d2, code, stream)
         gw = grad_w.view_as(weight) if (grad_w is not None and need_w) else None
         gb = grad_b if need_b else None
         return grad_x, grad_y, gw, gb, None, None, None
@@ -313,7 +318,7 @@ def fused_generator_dynamic_cat(x, y, weight, bias, kernel_size, dilations, *,
     """Fused 1x1 generator + dynamic filter (reference ``_triton_kernels.py:1056-1065``).
 
     Differentiable w.r.t. x, y, weight and bias; without gradients it is a
-    single launch (plus a cached weight packing). ``_fuse_planes`` (used by
+    single launch (plus the weight packing). ``_fuse_planes`` (used by
     the DDPM module when its native fuse conv consumes the output) has the
     forward also write the fuse conv's staged planes.
     """

@@ -94,6 +94,45 @@ __global__ void __launch_bounds__(256) stage_x_kernel(const T* __restrict__ x,
   }
 }
 
+// The same x plane from 16-byte vectors: block = (pixel range, (n, quad)),
+// thread = 8 consecutive pixels of the quad's four channels (four vector
+// loads), written as 8 consecutive cells (128 contiguous bytes); no index
+// division per cell. Needs H*W % 8 == 0 and a 16-byte aligned x.
+template <typename T>
+__global__ void __launch_bounds__(256) stage_x_vec_kernel(const T* __restrict__ x,
+                                                          float4* __restrict__ xp,
+                                                          const StageLayout L) {
+  const size_t P = (size_t)L.H * L.W;
+  const int nq = blockIdx.y, n = nq / L.Cq, q = nq - n * L.Cq;
+  const size_t p0 = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (p0 >= P) return;
+  float v[4][8];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int c = 4 * q + k;
+    if (c < L.C) {
+      const T* src = x + ((size_t)n * L.C + c) * P + p0;
+      if constexpr (sizeof(T) == 4) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(src));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(src) + 1);
+        v[k][0] = a.x; v[k][1] = a.y; v[k][2] = a.z; v[k][3] = a.w;
+        v[k][4] = b.x; v[k][5] = b.y; v[k][6] = b.z; v[k][7] = b.w;
+      } else {
+        const uint4 u = __ldg(reinterpret_cast<const uint4*>(src));
+        const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[k][i] = to_f32<T>(e[i]);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[k][i] = 0.f;
+    }
+  }
+  float4* dst = xp + ((size_t)n * L.Cq + q) * P + p0;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) dst[e] = make_float4(v[0][e], v[1][e], v[2][e], v[3][e]);
+}
+
 template <typename T>
 int launch_stage(const T* x, const T* y, uint8_t* staged, const StageLayout& L, cudaStream_t st) {
   uint4* hi = reinterpret_cast<uint4*>(staged);
@@ -101,7 +140,14 @@ int launch_stage(const T* x, const T* y, uint8_t* staged, const StageLayout& L, 
   const dim3 grid((unsigned)(L.N * L.Hp), (unsigned)((L.Wp + kStageCols - 1) / kStageCols));
   stage_y_kernel<T><<<grid, 256, 0, st>>>(y, hi, lo, L);
   DDPM_CHECK_LAUNCH("stage_y_kernel");
-  if (x != nullptr) {
+  const size_t P = (size_t)L.H * L.W;
+  if (x != nullptr && P % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15u) == 0 &&
+      (size_t)L.N * L.Cq <= 65535u) {
+    const dim3 grid((unsigned)((P / 8 + 255) / 256), (unsigned)(L.N * L.Cq));
+    stage_x_vec_kernel<T><<<grid, 256, 0, st>>>(
+        x, reinterpret_cast<float4*>(staged + L.x_offset), L);
+    DDPM_CHECK_LAUNCH("stage_x_vec_kernel");
+  } else if (x != nullptr) {
     const size_t cells = (size_t)L.N * L.Cq * L.H * L.W;
     size_t blocks = (cells + 4 * 256 - 1) / (4 * 256);  // four cells per thread
     if (blocks > 65535u * 8u) blocks = 65535u * 8u;

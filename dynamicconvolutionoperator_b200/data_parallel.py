@@ -15,8 +15,10 @@ of the flat buffer and the all-reduce needs no gather or scatter copy. With
 ``overlap=True`` (the default) a bucket's all-reduce is launched from a
 post-accumulate-grad hook as soon as its last gradient exists, so the fuse
 bucket's all-reduce runs on NCCL's stream while the generator backward is
-still computing. The whole step, collectives included, can be captured in one
-CUDA graph.
+still computing; with ``early=True`` the generator bucket's all-reduce starts
+inside the generator backward, right after its weight-gradient kernel and
+before its data-gradient kernel, so that one overlaps too. The whole step,
+collectives included, can be captured in one CUDA graph.
 """
 
 from __future__ import annotations
@@ -78,10 +80,18 @@ class GradAllReducer:
     one flat gradient buffer that the library's backward writes into; when a
     gradient did not land there (another autograd function produced it) the
     bucket falls back to gathering into the flat buffer and copying back.
+
+    ``early=True`` (with ``overlap`` and ``flat``) launches a bucket's
+    all-reduce as soon as the library's backward reports that it has written
+    all of the bucket's gradients into the flat buffer (``_gradbuf``), before
+    the rest of that backward runs. It requires that each of the bucket's
+    parameters gets its gradient from one use in the backward: a second
+    contribution would be added after the all-reduce started.
     """
 
     def __init__(self, module: nn.Module, group=None, overlap: bool = True,
-                 buckets: list[list[nn.Parameter]] | None = None, flat: bool = True):
+                 buckets: list[list[nn.Parameter]] | None = None, flat: bool = True,
+                 early: bool = False):
         self.group = group
         self.world = dist.get_world_size(group)
         self.buckets = buckets if buckets is not None else default_buckets(module)
@@ -91,8 +101,10 @@ class GradAllReducer:
         self.overlap = overlap
         self._pending: dict[int, tuple[object, torch.Tensor, bool]] = {}
         self._ready: dict[int, int] = {}
+        self._early: set[int] = set()
         self._sync = True
         self._hooks = []
+        self._listener = None
         self.flat: list[torch.Tensor | None] = []
         for bucket in self.buckets:
             buf = None
@@ -108,6 +120,9 @@ class GradAllReducer:
             for bi, bucket in enumerate(self.buckets):
                 for p in bucket:
                     self._hooks.append(p.register_post_accumulate_grad_hook(self._make_hook(bi)))
+            if early and flat:
+                self._listener = self._on_written
+                _gradbuf.add_listener(self._listener)
 
     @contextlib.contextmanager
     def no_sync(self):
@@ -118,9 +133,31 @@ class GradAllReducer:
         finally:
             self._sync = prev
 
+    def _on_written(self, params, buffers):
+        """``early``: the backward wrote ``params``' gradients into ``buffers``;
+        launch the matching bucket now if they are its flat-buffer views."""
+        if not self._sync:
+            return
+        ids = sorted(id(p) for p in params)
+        for bi, bucket in enumerate(self.buckets):
+            if self.flat[bi] is None or bi in self._pending or sorted(id(p) for p in bucket) != ids:
+                continue
+            for p, buf in zip(params, buffers):
+                view = _gradbuf.view_of(p)
+                if (buf is None or view is None or buf.data_ptr() != view.data_ptr()
+                        or buf.numel() != view.numel()):
+                    return
+            work = dist.all_reduce(self.flat[bi], op=self.op, group=self.group, async_op=True)
+            self._pending[bi] = (work, self.flat[bi], True)
+            self._early.add(bi)
+            return
+
     def _make_hook(self, bi: int):
         def hook(_p):
             if not self._sync:
+                return
+            if bi in self._early:  # launched from inside the backward
+                self._ready[bi] = self._ready.get(bi, 0) + 1
                 return
             if bi in self._pending:
                 raise RuntimeError(
@@ -163,7 +200,17 @@ class GradAllReducer:
                 work.wait()
             if self.divide:
                 flat.div_(self.world)
-            if not in_place:
+            if bi in self._early:
+                # launched before autograd stored the gradients: each must now
+                # be the flat-buffer view (or, if autograd copied it, get the
+                # averaged values copied in)
+                for p in self.buckets[bi]:
+                    view = _gradbuf.view_of(p)
+                    if p.grad is None:
+                        raise RuntimeError("a parameter in the bucket has no gradient")
+                    if p.grad.data_ptr() != view.data_ptr():
+                        p.grad.copy_(view.view_as(p.grad))
+            elif not in_place:
                 off = 0
                 for p in self.buckets[bi]:
                     n = p.grad.numel()
@@ -171,6 +218,7 @@ class GradAllReducer:
                     off += n
         self._pending.clear()
         self._ready.clear()
+        self._early.clear()
         for bucket in self.buckets:
             for p in bucket:
                 _gradbuf.arm(p)
@@ -179,6 +227,9 @@ class GradAllReducer:
         for h in self._hooks:
             h.remove()
         self._hooks.clear()
+        if self._listener is not None:
+            _gradbuf.remove_listener(self._listener)
+            self._listener = None
         for bucket in self.buckets:
             for p in bucket:
                 _gradbuf.detach(p)

@@ -143,6 +143,7 @@ class _AffineFn(torch.autograd.Function):
         torch.matmul(g.t(), x, out=gw)
         gb = _gradbuf.grad_buffer(ctx.bias, ctx.bias.shape, w.dtype, w.device)
         torch.sum(g, 0, out=gb)
+        _gradbuf.grads_written((w, ctx.bias), (gw, gb))  # before the input gradient, as the library
         return g @ w, gw, gb
 
 
@@ -186,7 +187,7 @@ def _toy_rank_main(rank, port, mode, out_dir):
     dist.init_process_group("gloo", rank=rank, world_size=WORLD)
     try:
         model = _Toy(0)
-        reducer = GradAllReducer(model, overlap=mode != "sync")
+        reducer = GradAllReducer(model, overlap=mode != "sync", early=mode == "early")
         x, g = _toy_data()
         xs, gs = shard_batch(x, rank, WORLD), shard_batch(g, rank, WORLD)
         per = xs.shape[0]
@@ -200,6 +201,9 @@ def _toy_rank_main(rank, port, mode, out_dir):
                 ((model(xs[half:]) * gs[half:]).sum() / per).backward()
             else:
                 ((model(xs) * gs).sum() / per).backward()
+            if mode == "early":
+                # both buckets were launched from inside the backward
+                result.setdefault("early", []).append(sorted(reducer._early))
             if mode == "double":
                 try:
                     ((model(xs) * gs).sum() / per).backward()
@@ -221,7 +225,7 @@ def _toy_rank_main(rank, port, mode, out_dir):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["sync", "overlap", "accumulate"])
+@pytest.mark.parametrize("mode", ["sync", "overlap", "accumulate", "early"])
 def test_flat_buffers_hold_the_averaged_gradients(tmp_path, mode):
     """The backward writes each bucket's gradients into its flat buffer
     (param.grad is a view of it, no gather or scatter copy), the all-reduce
@@ -232,6 +236,8 @@ def test_flat_buffers_hold_the_averaged_gradients(tmp_path, mode):
     for r in range(WORLD):
         res = torch.load(tmp_path / f"rank{r}.pt")
         assert all(res["in_flat"].values()), res["in_flat"]
+        if mode == "early":
+            assert res["early"] == [[0, 1], [0, 1]], res["early"]
         for name, grad in res["grads"].items():
             torch.testing.assert_close(grad, gold[name], rtol=1e-12, atol=1e-12)
 
