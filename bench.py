@@ -231,7 +231,7 @@ def measure(args, dtype, batch, device, rank, world, dist, timed_clocks=False, m
     model, taken = build_model(dtype, args.path, device)
     hx, hy, hg = [t.pin_memory() for t in make_inputs(batch, dtype, rank)]
     x, y, g = [t.to(device) for t in (hx, hy, hg)]
-    reducer = GradAllReducer(model, overlap=True, early=True) if world > 1 else None
+    reducer = GradAllReducer(model, overlap=True) if world > 1 else None
     allreduce = reducer.all_reduce if reducer is not None else None
     stream = torch.cuda.current_stream(device)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
