@@ -58,6 +58,12 @@ def fuse_conv_supported(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tenso
     )
 
 
+def nhwc_grad_ok(cat: torch.Tensor) -> bool:
+    """Whether the gradient of a fused generator output ``cat`` [N, 4C, H, W]
+    can travel channel-last to the generator's backward (16-bit, C == 64)."""
+    return cat.dtype in (torch.bfloat16, torch.float16) and cat.shape[1] == 256
+
+
 def pack_fuse_weight(weight: torch.Tensor) -> torch.Tensor:
     """The weight in the kernels' shared-memory operand layout (forward and
     data-gradient images). Packed on every forward (one small launch): a copy
@@ -102,6 +108,9 @@ class _FuseConv(torch.autograd.Function):
         ctx.bias = bias  # the parameter itself (its gradient buffer is looked up by identity)
         ctx.packed = packed
         ctx.has_bias = bias is not None
+        # x came from the fused generator forward (its planes): the gradient of x
+        # goes to that generator's backward, which reads it channel-last
+        ctx.grad_nhwc = planes_in is not None and nhwc_grad_ok(x)
         return out
 
     @staticmethod
@@ -115,13 +124,15 @@ class _FuseConv(torch.autograd.Function):
         if ctx.needs_input_grad[0] and (ctx.needs_input_grad[1] or need_b):
             # both in one call: the data gradient reads grad_out from the
             # channel-last copy the weight gradient makes anyway
-            gx = torch.empty_like(x)
+            nhwc = ctx.grad_nhwc
+            gx = (torch.empty_like(x, memory_format=torch.channels_last) if nhwc
+                  else torch.empty_like(x))
             gw = (grad_buffer(weight, weight.shape, x.dtype, x.device)
                   if ctx.needs_input_grad[1] else torch.empty_like(weight))
             gb = grad_buffer(ctx.bias, (cout,), x.dtype, x.device) if need_b else None
             nbytes = int(_lib.load().ddpm_fuseconv_bwd_weight_workspace_bytes(n, cin, cout, h, w))
             ws = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
-            _lib.call("ddpm_fuseconv_bwd", x.data_ptr(), g.data_ptr(), ctx.packed.data_ptr(),
+            _lib.call("ddpm_fuseconv_bwd_nhwc" if nhwc else "ddpm_fuseconv_bwd", x.data_ptr(), g.data_ptr(), ctx.packed.data_ptr(),
                       gx.data_ptr(), gw.data_ptr(), gb.data_ptr() if gb is not None else None,
                       ws.data_ptr(), nbytes, n, cin, cout, h, w, _lib.dtype_code(x.dtype),
                       _lib.stream_handle(x.device))

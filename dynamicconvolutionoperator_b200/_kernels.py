@@ -256,7 +256,6 @@ class _GeneratorDynamicCat(torch.autograd.Function):
     def backward(ctx, grad_out):
         x, y, weight, bias = ctx.saved_tensors
         packed = ctx.packed
-        grad_out = grad_out.to(x.dtype).contiguous()
         n, c, h, w = x.shape
         ks = ctx.kernel_size
         d0, d1, d2 = ctx.dilations
@@ -273,11 +272,20 @@ class _GeneratorDynamicCat(torch.autograd.Function):
                       else torch.empty((rows, c), dtype=x.dtype, device=x.device))
             grad_b = (grad_buffer(ctx.bias, (rows,), x.dtype, x.device) if need_b
                       else torch.empty(rows, dtype=x.dtype, device=x.device))
+        full = need_y and grad_w is not None
+        # a channel-last grad_out (the module's fuse conv writes it so for a
+        # 16-bit C = 64 generator output) is read as is; anything else as NCHW
+        nhwc = (grad_out.dtype == x.dtype and x.dtype != torch.float32 and c == 64
+                and not grad_out.is_contiguous()
+                and grad_out.is_contiguous(memory_format=torch.channels_last)
+                and (full or not (need_y or grad_w is not None)))
+        if not nhwc:
+            grad_out = grad_out.to(x.dtype).contiguous()
+        sfx = "_nhwc" if nhwc else ""
         with torch.cuda.device(x.device):
             stream = _lib.stream_handle(x.device)
             # the operands staged by the forward (x and y, channel-last operand
             # copies): the backward kernels stage their tiles with bulk / TMA copies
-            full = need_y and grad_w is not None
             staged = ctx.staged
             sb = staged.numel()
             # dY + dW/db first: once the weight gradients are written, a
@@ -286,7 +294,8 @@ class _GeneratorDynamicCat(torch.autograd.Function):
             if full:
                 ws_bytes = int(_lib.load().ddpm_gencat_bwd_workspace_bytes(n, c, h, w, ks))
                 ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
-                _lib.call("ddpm_gencat_bwd_yw_staged", staged.data_ptr(), sb, packed.data_ptr(),
+                _lib.call("ddpm_gencat_bwd_yw_staged" + sfx, staged.data_ptr(), sb,
+                          packed.data_ptr(),
                           grad_out.data_ptr(), grad_y.data_ptr(), grad_w.data_ptr(),
                           grad_b.data_ptr(), ws.data_ptr(), ws_bytes,
                           n, c, h, w, ks, d0, d1, d2, code, stream)
@@ -305,7 +314,8 @@ class _GeneratorDynamicCat(torch.autograd.Function):
             if need_w and need_b:
                 grads_written((weight, ctx.bias), (grad_w, grad_b))
             if need_x:
-                _lib.call("ddpm_gencat_bwd_x_staged", staged.data_ptr(), sb, packed.data_ptr(),
+                _lib.call("ddpm_gencat_bwd_x_staged" + sfx, staged.data_ptr(), sb,
+                          packed.data_ptr(),
                           bias.data_ptr(), grad_out.data_ptr(), grad_x.data_ptr(),
                           n, c, h, w, ks, d0, d1, d2, code, stream)
         gw = grad_w.view_as(weight) if (grad_w is not None and need_w) else None

@@ -68,6 +68,14 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _c_int,
         [_c_ptr, _c_size, _c_ptr, _c_ptr, _c_ptr, _c_ptr] + [_c_int] * 4 + [_c_int] * 5 + [_c_ptr],
     ),
+    "ddpm_gencat_bwd_x_staged_nhwc": (
+        _c_int,
+        [_c_ptr, _c_size, _c_ptr, _c_ptr, _c_ptr, _c_ptr] + [_c_int] * 4 + [_c_int] * 5 + [_c_ptr],
+    ),
+    "ddpm_gencat_bwd_yw_staged_nhwc": (
+        _c_int,
+        [_c_ptr, _c_size] + [_c_ptr] * 6 + [_c_size] + [_c_int] * 4 + [_c_int] * 5 + [_c_ptr],
+    ),
     "ddpm_gencat_bwd_workspace_bytes": (_c_size, [_c_int] * 5),
     "ddpm_gencat_bwd_yw": (
         _c_int,
@@ -94,6 +102,9 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _c_int, [_c_ptr, _c_size] + [_c_ptr] * 2 + [_c_int] * 6 + [_c_ptr]
     ),
     "ddpm_fuseconv_bwd": (
+        _c_int, [_c_ptr] * 7 + [_c_size] + [_c_int] * 6 + [_c_ptr]
+    ),
+    "ddpm_fuseconv_bwd_nhwc": (
         _c_int, [_c_ptr] * 7 + [_c_size] + [_c_int] * 6 + [_c_ptr]
     ),
     "ddpm_fuseconv_bwd_weight_workspace_bytes": (_c_size, [_c_int] * 5),

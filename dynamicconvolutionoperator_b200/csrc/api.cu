@@ -49,7 +49,7 @@ int gencat_fwd_ex(const void* x, const void* y, const void* staged, size_t stage
 
 int gencat_bwd_x(const void* y, const void* staged, size_t staged_bytes, const void* wpack,
                  const void* bias, const void* gout, void* gx, int n, int c, int h, int w, int ks,
-                 int d0, int d1, int d2, int dt, cudaStream_t st);
+                 int d0, int d1, int d2, int dt, cudaStream_t st, int g_nhwc);
 namespace gencat {
 size_t stage_bytes(int n, int c, int h, int w, int ks, int d0, int d1, int d2, int dt);
 int stage(const void* x, const void* y, void* staged, size_t staged_bytes, int n, int c, int h,
@@ -60,7 +60,7 @@ size_t gencat_bwd_workspace_bytes(int n, int c, int h, int w, int ks);
 int gencat_bwd_yw(const void* x, const void* y, const void* staged, size_t staged_bytes,
                   const void* wpack, const void* gout, void* gy, void* gw, void* gb,
                   void* workspace, size_t ws_bytes, int n, int c, int h, int w, int ks, int d0,
-                  int d1, int d2, int dt, cudaStream_t st);
+                  int d1, int d2, int dt, cudaStream_t st, int g_nhwc);
 
 int gencat_bwd_yw_static(const void* x, const void* y, const void* wpack, const void* gout,
                          void* gy, void* gw, void* gb, int n, int c, int h, int w, int ks, int d0,
@@ -71,10 +71,10 @@ int fuseconv_pack(const void* w, int cin, int cout, int dt, void* packed, size_t
 int fuseconv_fwd(const void* cat, const void* packed, const void* bias, void* out, int n, int cin,
                  int cout, int h, int w, int dt, cudaStream_t st);
 int fuseconv_dgrad(const void* gout, const void* packed, void* gcat, int n, int cin, int cout,
-                   int h, int w, int dt, cudaStream_t st);
+                   int h, int w, int dt, cudaStream_t st, int gcat_nhwc);
 int fuseconv_bwd(const void* cat, const void* gout, const void* packed, void* gcat, void* gw,
                  void* gb, void* ws, size_t ws_bytes, int n, int cin, int cout, int h, int w,
-                 int dt, cudaStream_t st);
+                 int dt, cudaStream_t st, int gcat_nhwc);
 size_t fuseconv_stage_bytes(int n, int c, int h, int w, int dt);
 int fuseconv_stage(const void* src, void* planes, size_t bytes, int n, int c, int h, int w, int dt,
                    cudaStream_t st);
@@ -176,7 +176,7 @@ int ddpm_gencat_bwd_x(const void* y, const void* packed, const void* bias, const
                       int dtype, void* stream) {
   ddpm::clear_error();
   return ddpm::gencat_bwd_x(y, nullptr, 0, packed, bias, grad_out, grad_x, n, c, h, w, ksize, d0,
-                            d1, d2, dtype, static_cast<cudaStream_t>(stream));
+                            d1, d2, dtype, static_cast<cudaStream_t>(stream), 0);
 }
 
 size_t ddpm_gencat_stage_bytes(int n, int c, int h, int w, int ksize, int d0, int d1, int d2,
@@ -199,7 +199,17 @@ int ddpm_gencat_bwd_x_staged(const void* staged_y, size_t staged_bytes, const vo
   ddpm::clear_error();
   DDPM_CHECK_ARG(staged_y != nullptr, "null staged_y");
   return ddpm::gencat_bwd_x(nullptr, staged_y, staged_bytes, packed, bias, grad_out, grad_x, n, c,
-                            h, w, ksize, d0, d1, d2, dtype, static_cast<cudaStream_t>(stream));
+                            h, w, ksize, d0, d1, d2, dtype, static_cast<cudaStream_t>(stream), 0);
+}
+
+int ddpm_gencat_bwd_x_staged_nhwc(const void* staged_y, size_t staged_bytes, const void* packed,
+                                  const void* bias, const void* grad_out, void* grad_x, int n,
+                                  int c, int h, int w, int ksize, int d0, int d1, int d2,
+                                  int dtype, void* stream) {
+  ddpm::clear_error();
+  DDPM_CHECK_ARG(staged_y != nullptr, "null staged_y");
+  return ddpm::gencat_bwd_x(nullptr, staged_y, staged_bytes, packed, bias, grad_out, grad_x, n, c,
+                            h, w, ksize, d0, d1, d2, dtype, static_cast<cudaStream_t>(stream), 1);
 }
 
 size_t ddpm_gencat_bwd_workspace_bytes(int n, int c, int h, int w, int ksize) {
@@ -213,7 +223,7 @@ int ddpm_gencat_bwd_yw(const void* x, const void* y, const void* packed, const v
   ddpm::clear_error();
   return ddpm::gencat_bwd_yw(x, y, nullptr, 0, packed, grad_out, grad_y, grad_weight, grad_bias,
                              workspace, workspace_bytes, n, c, h, w, ksize, d0, d1, d2, dtype,
-                             static_cast<cudaStream_t>(stream));
+                             static_cast<cudaStream_t>(stream), 0);
 }
 
 int ddpm_gencat_bwd_yw_staged(const void* staged, size_t staged_bytes, const void* packed,
@@ -225,7 +235,19 @@ int ddpm_gencat_bwd_yw_staged(const void* staged, size_t staged_bytes, const voi
   DDPM_CHECK_ARG(staged != nullptr, "null staged");
   return ddpm::gencat_bwd_yw(nullptr, nullptr, staged, staged_bytes, packed, grad_out, grad_y,
                              grad_weight, grad_bias, workspace, ws_bytes, n, c, h, w, ksize, d0,
-                             d1, d2, dtype, static_cast<cudaStream_t>(stream));
+                             d1, d2, dtype, static_cast<cudaStream_t>(stream), 0);
+}
+
+int ddpm_gencat_bwd_yw_staged_nhwc(const void* staged, size_t staged_bytes, const void* packed,
+                                   const void* grad_out, void* grad_y, void* grad_weight,
+                                   void* grad_bias, void* workspace, size_t ws_bytes, int n,
+                                   int c, int h, int w, int ksize, int d0, int d1, int d2,
+                                   int dtype, void* stream) {
+  ddpm::clear_error();
+  DDPM_CHECK_ARG(staged != nullptr, "null staged");
+  return ddpm::gencat_bwd_yw(nullptr, nullptr, staged, staged_bytes, packed, grad_out, grad_y,
+                             grad_weight, grad_bias, workspace, ws_bytes, n, c, h, w, ksize, d0,
+                             d1, d2, dtype, static_cast<cudaStream_t>(stream), 1);
 }
 
 int ddpm_gencat_bwd_yw_static(const void* x, const void* y, const void* packed,
@@ -260,7 +282,7 @@ int ddpm_fuseconv_bwd_data(const void* grad_out, const void* packed, void* grad_
                            int cin, int cout, int h, int w, int dtype, void* stream) {
   ddpm::clear_error();
   return ddpm::fuseconv_dgrad(grad_out, packed, grad_x, n, cin, cout, h, w, dtype,
-                              static_cast<cudaStream_t>(stream));
+                              static_cast<cudaStream_t>(stream), 0);
 }
 
 int ddpm_fuseconv_bwd(const void* x, const void* grad_out, const void* packed, void* grad_x,
@@ -269,7 +291,17 @@ int ddpm_fuseconv_bwd(const void* x, const void* grad_out, const void* packed, v
   ddpm::clear_error();
   return ddpm::fuseconv_bwd(x, grad_out, packed, grad_x, grad_weight, grad_bias, workspace,
                             workspace_bytes, n, cin, cout, h, w, dtype,
-                            static_cast<cudaStream_t>(stream));
+                            static_cast<cudaStream_t>(stream), 0);
+}
+
+int ddpm_fuseconv_bwd_nhwc(const void* x, const void* grad_out, const void* packed, void* grad_x,
+                           void* grad_weight, void* grad_bias, void* workspace,
+                           size_t workspace_bytes, int n, int cin, int cout, int h, int w,
+                           int dtype, void* stream) {
+  ddpm::clear_error();
+  return ddpm::fuseconv_bwd(x, grad_out, packed, grad_x, grad_weight, grad_bias, workspace,
+                            workspace_bytes, n, cin, cout, h, w, dtype,
+                            static_cast<cudaStream_t>(stream), 1);
 }
 
 size_t ddpm_fuseconv_stage_bytes(int n, int c, int h, int w, int dtype) {

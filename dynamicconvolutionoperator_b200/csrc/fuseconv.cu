@@ -58,6 +58,7 @@ struct FcParams {
   int tiles_w, hpairs, num_units;
   int reg_bufs, w_stages;
   int row_major;        // staged slab order [row][group][px][8] (else [group][row][px][8])
+  int dst_nhwc;         // dst channel-last [N][H][W][Cdst] (Cdst % 16 == 0), else NCHW
   uint32_t reg_part, reg_bytes;
   uint32_t w_chunk;     // bytes per streamed weight chunk (FcCfg::kTapsPerChunk taps)
   uint32_t w_tap;       // bytes of one (slab, tap) B image within a chunk
@@ -121,6 +122,25 @@ struct FcCfg {
 // thread ~55 cycles, so with N <= 128 a single issuer would leave the tensor
 // pipe idle between instructions. Their inner loops are unrolled over taps
 // and K steps with descriptors advanced by constants.
+// Sixteen FP32 accumulators -> sixteen consecutive channel-last elements of
+// dst (16-byte aligned): FP32 as four 16-byte stores, 16-bit types rounded a
+// pair per conversion (round to nearest even, as from_f32) into two.
+template <typename T>
+__device__ __forceinline__ void store16_cl(T* dst, const float (&v)[16]) {
+  if constexpr (sizeof(T) == 4) {
+    float4* d = reinterpret_cast<float4*>(dst);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) d[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  } else {
+    uint32_t w[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) w[i] = cvt2<T>(v[2 * i], v[2 * i + 1]);
+    uint4* d = reinterpret_cast<uint4*>(dst);
+    d[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    d[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  }
+}
+
 template <typename T, bool kDgrad, bool kStaged>
 __global__ void __launch_bounds__(FcCfg<T, kDgrad, kStaged>::kThreads, 1)
 fuseconv_kernel(const FcParams p, const __grid_constant__ FcMaps maps) {
@@ -377,12 +397,25 @@ fuseconv_kernel(const FcParams p, const __grid_constant__ FcMaps maps) {
         const bool ok = h < H && w < W;
         const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + tb * 256 + mh * 128;
         T* out = dst + ((size_t)n * p.Cdst + c0) * P + (size_t)h * W + w;
+        // channel-last: the pixel's channels are contiguous, 16 per vector store
+        T* out_cl = dst + (((size_t)n * H + h) * W + w) * p.Cdst + c0;
         for (int blk = 0; blk < Nn; blk += 32) {
           float a[2][16];
           tc::tmem_ld16(taddr + blk, a[0]);
           tc::tmem_ld16(taddr + blk + 16, a[1]);
           tc::tmem_ld_wait();
-          if (ok) {
+          if (ok && p.dst_nhwc) {
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              const int cb = blk + hh * 16;
+              if (c0 + cb >= p.Cdst) break;
+              if constexpr (!kDgrad) {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) a[hh][e] += bias_s[cb + e];
+              }
+              store16_cl<T>(out_cl + cb, a[hh]);
+            }
+          } else if (ok) {
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh)
 #pragma unroll
@@ -764,10 +797,12 @@ int fuseconv_fwd_staged(const void* planes, size_t planes_bytes, const void* pac
 // `gout` (NCHW) or, when `planes` is set, its staged planes (fuseconv_stage).
 int fuseconv_dgrad_any(const void* gout, const void* planes, size_t planes_bytes,
                        const void* packed, void* gcat, int n, int cin, int cout, int h, int w,
-                       int dt, cudaStream_t st) {
+                       int dt, cudaStream_t st, int gcat_nhwc = 0) {
   int rc = check_conv(n, cin, cout, h, w, dt);
   if (rc) return rc;
   DDPM_CHECK_ARG((gout || planes) && packed && gcat, "null pointer");
+  DDPM_CHECK_ARG(!gcat_nhwc || (cin % 16 == 0 && (reinterpret_cast<uintptr_t>(gcat) & 15u) == 0),
+                 "a channel-last gradient needs Cin %% 16 == 0 and a 16-byte aligned buffer");
   int* status = nullptr;
   rc = gencat::status_ptr(&status);
   if (rc) return rc;
@@ -777,6 +812,7 @@ int fuseconv_dgrad_any(const void* gout, const void* planes, size_t planes_bytes
   q.wimg = static_cast<const uint8_t*>(packed) + L.fwd_bytes;
   q.bias = nullptr;
   q.dst = gcat;
+  q.dst_nhwc = gcat_nhwc;
   q.Csrc = cout;
   q.Cdst = cin;
   q.KC = L.KD;
@@ -797,8 +833,9 @@ int fuseconv_dgrad_any(const void* gout, const void* planes, size_t planes_bytes
 }
 
 int fuseconv_dgrad(const void* gout, const void* packed, void* gcat, int n, int cin, int cout,
-                   int h, int w, int dt, cudaStream_t st) {
-  return fuseconv_dgrad_any(gout, nullptr, 0, packed, gcat, n, cin, cout, h, w, dt, st);
+                   int h, int w, int dt, cudaStream_t st, int gcat_nhwc) {
+  return fuseconv_dgrad_any(gout, nullptr, 0, packed, gcat, n, cin, cout, h, w, dt, st,
+                            gcat_nhwc);
 }
 
 // Data gradient reading grad_out from the weight gradient's channel-last
@@ -807,9 +844,12 @@ int fuseconv_dgrad(const void* gout, const void* packed, void* gcat, int n, int 
 // second time. Returns DDPM_ERR_UNSUPPORTED, nothing launched, if a tensor map
 // is rejected.
 int fuseconv_dgrad_rowmajor(const void* hi, const void* lo, const void* packed, void* gcat, int n,
-                            int cin, int cout, int h, int w, int dt, cudaStream_t st) {
+                            int cin, int cout, int h, int w, int dt, cudaStream_t st,
+                            int gcat_nhwc) {
   int rc = check_conv(n, cin, cout, h, w, dt);
   if (rc) return rc;
+  DDPM_CHECK_ARG(!gcat_nhwc || (cin % 16 == 0 && (reinterpret_cast<uintptr_t>(gcat) & 15u) == 0),
+                 "a channel-last gradient needs Cin %% 16 == 0 and a 16-byte aligned buffer");
   DDPM_CHECK_ARG(hi && packed && gcat && (dt != DDPM_F32 || lo), "null pointer");
   DDPM_CHECK_ARG(w % 8 == 0, "row-major grad_out planes need W %% 8 == 0");
   int* status = nullptr;
@@ -819,6 +859,7 @@ int fuseconv_dgrad_rowmajor(const void* hi, const void* lo, const void* packed, 
   FcParams q = common_params(n, h, w, L.nhalf, status);
   q.wimg = static_cast<const uint8_t*>(packed) + L.fwd_bytes;
   q.dst = gcat;
+  q.dst_nhwc = gcat_nhwc;
   q.Csrc = cout;
   q.Cdst = cin;
   q.KC = L.KD;

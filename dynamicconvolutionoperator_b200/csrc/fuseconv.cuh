@@ -44,9 +44,11 @@ struct PlaneLayout {
 }  // namespace fuseconv
 
 size_t fuseconv_pack_bytes(int cin, int cout, int dt);
+// gcat_nhwc: write the gradient channel-last [N][H][W][Cin] (Cin % 16 == 0)
 int fuseconv_dgrad(const void* gout, const void* packed, void* gcat, int n, int cin, int cout,
-                   int h, int w, int dt, cudaStream_t st);
+                   int h, int w, int dt, cudaStream_t st, int gcat_nhwc = 0);
 int fuseconv_dgrad_rowmajor(const void* hi, const void* lo, const void* packed, void* gcat, int n,
-                            int cin, int cout, int h, int w, int dt, cudaStream_t st);
+                            int cin, int cout, int h, int w, int dt, cudaStream_t st,
+                            int gcat_nhwc = 0);
 
 }  // namespace ddpm

@@ -797,7 +797,8 @@ int run_wgrad_reg(const WgParams& prm, void* dw, void* db, cudaStream_t st) {
 template <typename T>
 int run_wgrad_tma(const void* cat, const void* gout, void* gw, void* gb, uint8_t* ws,
                   const WtPlan& t, int n, int cin, int cout, int h, int w, int dt, int* status,
-                  cudaStream_t st, const void* packed = nullptr, void* gcat = nullptr) {
+                  cudaStream_t st, const void* packed = nullptr, void* gcat = nullptr,
+                  int gcat_nhwc = 0) {
   using Cfg = WtCfg<T>;
   constexpr int TW = Cfg::kTW;
   const int Np = t.g.Np, ng = Np / 8;
@@ -839,9 +840,9 @@ int run_wgrad_tma(const void* cat, const void* gout, void* gw, void* gb, uint8_t
       static_cast<const T*>(gout), hi, lo, dbp, h, w, cout, Np);
   DDPM_CHECK_LAUNCH("fuseconv_dout_pack_kernel");
   if (gcat != nullptr) {
-    int rc = fuseconv_dgrad_rowmajor(hi, lo, packed, gcat, n, cin, cout, h, w, dt, st);
+    int rc = fuseconv_dgrad_rowmajor(hi, lo, packed, gcat, n, cin, cout, h, w, dt, st, gcat_nhwc);
     if (rc == DDPM_ERR_UNSUPPORTED) rc = fuseconv_dgrad(gout, packed, gcat, n, cin, cout, h, w,
-                                                        dt, st);
+                                                        dt, st, gcat_nhwc);
     if (rc) return rc;
   }
   const size_t smem = (size_t)Cfg::kStages * (Cfg::kABytes + prm.b_stage) +
@@ -881,7 +882,7 @@ int fuseconv_wgrad(const void* cat, const void* gout, void* gw, void* gb, void* 
 // pre-pass writes anyway, instead of staging it separately.
 int fuseconv_bwd(const void* cat, const void* gout, const void* packed, void* gcat, void* gw,
                  void* gb, void* ws, size_t ws_bytes, int n, int cin, int cout, int h, int w,
-                 int dt, cudaStream_t st) {
+                 int dt, cudaStream_t st, int gcat_nhwc) {
   DDPM_CHECK_ARG(n >= 1 && h >= 1 && w >= 1 && cin >= 1 && cout >= 1, "sizes must be positive");
   DDPM_CHECK_ARG(dtype_size(dt) > 0, "unknown dtype code %d", dt);
   if (cin > fuseconv::kMaxCin || cout > fuseconv::kMaxCout)
@@ -903,21 +904,21 @@ int fuseconv_bwd(const void* cat, const void* gout, const void* packed, void* gc
       case DDPM_BF16:
         rc = run_wgrad_tma<__nv_bfloat16>(cat, gout, gw, gb, wsb,
                                           plan_wgrad_tma(n, cin, cout, h, w, 64, false), n, cin,
-                                          cout, h, w, dt, status, st, packed, gcat);
+                                          cout, h, w, dt, status, st, packed, gcat, gcat_nhwc);
         break;
       case DDPM_F16:
         rc = run_wgrad_tma<__half>(cat, gout, gw, gb, wsb,
                                    plan_wgrad_tma(n, cin, cout, h, w, 64, false), n, cin, cout, h,
-                                   w, dt, status, st, packed, gcat);
+                                   w, dt, status, st, packed, gcat, gcat_nhwc);
         break;
       default:
         rc = run_wgrad_tma<float>(cat, gout, gw, gb, wsb,
                                   plan_wgrad_tma(n, cin, cout, h, w, 32, true), n, cin, cout, h, w,
-                                  dt, status, st, packed, gcat);
+                                  dt, status, st, packed, gcat, gcat_nhwc);
     }
     if (rc != DDPM_ERR_UNSUPPORTED) return rc;
   }
-  rc = fuseconv_dgrad(gout, packed, gcat, n, cin, cout, h, w, dt, st);
+  rc = fuseconv_dgrad(gout, packed, gcat, n, cin, cout, h, w, dt, st, gcat_nhwc);
   if (rc) return rc;
   return fuseconv_wgrad(cat, gout, gw, gb, ws, ws_bytes, n, cin, cout, h, w, dt, st);
 }

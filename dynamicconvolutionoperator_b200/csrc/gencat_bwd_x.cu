@@ -34,6 +34,9 @@
 // allows a tensor map, the whole [Cp][144] gradient segment as one TMA copy
 // (zero filled outside the image) — per-channel copies issued by a warp
 // against one mbarrier cost ~3 us per unit.
+#include <cstring>
+#include <type_traits>
+
 #include "common.cuh"
 #include "tc.cuh"
 #include "gencat.cuh"
@@ -45,6 +48,29 @@ namespace {
 using namespace gencat;
 
 constexpr int kSeg = 144;  // staged pixels per row segment (128 + 8 on each side)
+
+// Sixteen 16-bit values (two 16-byte vectors, element 0 in the low half of the
+// first word) as floats; FP32 instances never take this path.
+template <typename T>
+__device__ __forceinline__ void unpack16(const uint4& a, const uint4& b, float (&v)[16]) {
+  if constexpr (sizeof(T) == 2) {
+    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+        v[2 * i] = __uint_as_float(w[i] << 16);
+        v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+      } else {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = 0.f;
+  }
+}
 
 template <typename T, int KS, bool kStaged = false>
 struct BxCfg {
@@ -84,7 +110,8 @@ __host__ __device__ inline BxSmem bx_smem_layout(int Cp, int Ck, int C) {
   L.g_bytes = (uint32_t)Cp * kSeg * sizeof(T);
   L.w_bytes = (uint32_t)Cfg::kParts * Cp * Ck * 2;
   L.reg = 0;
-  L.gs = L.reg + Cfg::kUnitBufs * L.reg_bytes;
+  // 1024-byte aligned: a 128-byte-swizzled TMA destination (channel-last grad_out)
+  L.gs = (L.reg + Cfg::kUnitBufs * L.reg_bytes + 1023u) / 1024u * 1024u;
   L.w = L.gs + Cfg::kUnitBufs * L.g_bytes;
   L.bias = L.w + Cfg::kWStages * L.w_bytes;
   L.bars = L.bias + (Cfg::kBiasInGemm ? 0u : (uint32_t)(3 * KS * KS * Cp * 4));
@@ -107,6 +134,10 @@ struct BxParams {
   CUtensorMap ymap;       // y-plane row segment, box of 9 16-px blocks x Ck/8 groups
   int g_tma;              // gmap is valid
   int y_tma;              // ymap is valid
+  // grad_out channel-last [N][H][W][4C] (16-bit, C == 64, staged): gmap is then
+  // {C, 4, W, H, N}, box {64, 1, kSeg, 1, 1} with 128-byte swizzle, landing as
+  // [kSeg px][64 channels], 16-byte chunk j of pixel row r at chunk j ^ (r & 7)
+  int g_nhwc;
   int* status;
 };
 
@@ -146,7 +177,7 @@ __device__ __forceinline__ void stage_grad_rows(T* gs, const T* gout, uint64_t* 
   }
 }
 
-template <typename T, int KS, bool kStaged>
+template <typename T, int KS, bool kStaged, bool kNhwc = false>
 __global__ void __launch_bounds__(BxCfg<T, KS, kStaged>::kThreads, 1)
 gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
   using Cfg = BxCfg<T, KS, kStaged>;
@@ -342,7 +373,12 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
                              &u_full[ub]);
               }
             }
-            if (p.g_tma) tc::tma_load_4d(gs, &p.gmap, w0 - 8, hr, (b + 1) * C, n, &u_full[ub]);
+            if (p.g_tma) {
+              if constexpr (kNhwc)
+                tc::tma_load_5d(gs, &p.gmap, 0, b + 1, w0 - 8, hr, n, &u_full[ub]);
+              else
+                tc::tma_load_4d(gs, &p.gmap, w0 - 8, hr, (b + 1) * C, n, &u_full[ub]);
+            }
           }
           if (!p.g_tma)
             stage_grad_rows<T>(gs, gout, &u_full[ub], pt, Cfg::kProducers, n, b, hr, w0, C, Cp,
@@ -428,10 +464,24 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
           // the tile end they took ~3 us under the kernel's own copy traffic)
           // (kept in the I/O type: a conversion right after the load waited for it)
           if (u == kUnits - 1) {
-            const T* g0p = gn + (size_t)(wg * 16) * P + (size_t)h * W + w;
+            if constexpr (kNhwc) {
+              // channel-last: the pixel's 16 channels are two 16-byte vectors
+              const uint4* g0v = reinterpret_cast<const uint4*>(
+                  gout + (((size_t)n * H + h) * W + w) * 4 * C + wg * 16);
+              uint4 v0 = make_uint4(0u, 0u, 0u, 0u), v1 = v0;
+              if (px_ok && wg < nblk) {
+                v0 = __ldg(g0v);
+                v1 = __ldg(g0v + 1);
+              }
+              memcpy(&g0raw[0], &v0, 16);
+              memcpy(&g0raw[8], &v1, 16);
+            } else {
+              const T* g0p = gn + (size_t)(wg * 16) * P + (size_t)h * W + w;
 #pragma unroll
-            for (int cl = 0; cl < 16; ++cl)
-              g0raw[cl] = (px_ok && wg < nblk && wg * 16 + cl < C) ? __ldg(g0p + cl * P) : T(0.f);
+              for (int cl = 0; cl < 16; ++cl)
+                g0raw[cl] =
+                    (px_ok && wg < nblk && wg * 16 + cl < C) ? __ldg(g0p + cl * P) : T(0.f);
+            }
           }
         }
         if (!warp_wait(&u_full[ub], (uq / NU) & 1, abort_flag)) {
@@ -474,8 +524,19 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
             if (blk_ok) {
               const int dx = (kj - r) * d;
               float gv[16];
+              if constexpr (kNhwc) {
+                // pixel row m + 8 - dx of the swizzled [kSeg][64] segment:
+                // channel chunks 2wg and 2wg+1 (8 channels each)
+                const int pr = m + 8 - dx;
+                const uint8_t* row = reinterpret_cast<const uint8_t*>(gs) + pr * 128;
+                const uint4 v0 = *reinterpret_cast<const uint4*>(row + (((2 * wg) ^ (pr & 7)) * 16));
+                const uint4 v1 =
+                    *reinterpret_cast<const uint4*>(row + (((2 * wg + 1) ^ (pr & 7)) * 16));
+                unpack16<T>(v0, v1, gv);
+              } else {
 #pragma unroll
-              for (int cl = 0; cl < 16; ++cl) gv[cl] = to_f32<T>(gcol[cl * kSeg - dx]);
+                for (int cl = 0; cl < 16; ++cl) gv[cl] = to_f32<T>(gcol[cl * kSeg - dx]);
+              }
               if constexpr (!Cfg::kBiasInGemm) {
                 const float* bs = bias_s + (b * KK + ki * KS + kj) * Cp + wg * 16;
 #pragma unroll
@@ -575,11 +636,11 @@ done:
   }
 }
 
-template <typename T, int KS, bool kStaged>
+template <typename T, int KS, bool kStaged, bool kNhwc = false>
 int launch_k(const BxParams& prm, cudaStream_t st) {
   using Cfg = BxCfg<T, KS, kStaged>;
   const BxSmem L = bx_smem_layout<T, KS, kStaged>(prm.Cp, prm.Ck, prm.C);
-  auto fn = gencat_bwd_x_kernel<T, KS, kStaged>;
+  auto fn = gencat_bwd_x_kernel<T, KS, kStaged, kNhwc>;
   DDPM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total));
   const int grid = prm.num_tiles < num_sms() ? prm.num_tiles : num_sms();
   fn<<<grid, Cfg::kThreads, L.total, st>>>(prm);
@@ -589,6 +650,9 @@ int launch_k(const BxParams& prm, cudaStream_t st) {
 
 template <typename T, int KS>
 int launch(const BxParams& prm, cudaStream_t st) {
+  if constexpr (sizeof(T) == 2) {
+    if (prm.g_nhwc) return launch_k<T, KS, true, true>(prm, st);
+  }
   if (prm.staged != nullptr) return launch_k<T, KS, true>(prm, st);
   return launch_k<T, KS, false>(prm, st);
 }
@@ -608,10 +672,13 @@ int dispatch(int ks, const BxParams& prm, cudaStream_t st) {
 // stage the operand from y itself.
 int gencat_bwd_x(const void* y, const void* staged, size_t staged_bytes, const void* wpack,
                  const void* bias, const void* gout, void* gx, int n, int c, int h, int w, int ks,
-                 int d0, int d1, int d2, int dt, cudaStream_t st) {
+                 int d0, int d1, int d2, int dt, cudaStream_t st, int g_nhwc) {
   int rc = gencat::check_shape(n, c, h, w, ks, d0, d1, d2, dt);
   if (rc) return rc;
   DDPM_CHECK_ARG((y || staged) && wpack && bias && gout && gx, "null pointer");
+  if (g_nhwc && (dt == DDPM_F32 || c != 64 || staged == nullptr))
+    return set_error(DDPM_ERR_UNSUPPORTED,
+                     "a channel-last grad_out needs 16-bit data, C == 64 and staged operands");
   const gencat::PackLayout pl = gencat::PackLayout::make(c, ks, dt);
   BxParams prm{};
   prm.y = y;
@@ -641,7 +708,21 @@ int gencat_bwd_x(const void* y, const void* staged, size_t staged_bytes, const v
     prm.y_tma = gencat::encode_stage_segment_map(&prm.ymap, pl.Ck / 8, prm.staged, prm.sl) ? 1 : 0;
     // gradient segments by TMA when the row pitch and base allow a tensor map
     const int es = dtype_size(dt);
-    if (((size_t)w * es) % 16 == 0 && (reinterpret_cast<uintptr_t>(gout) & 15u) == 0) {
+    if (g_nhwc) {
+      DDPM_CHECK_ARG((reinterpret_cast<uintptr_t>(gout) & 15u) == 0,
+                     "grad_out must be 16-byte aligned");
+      const CUtensorMapDataType ty =
+          dt == DDPM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+      const uint64_t dims[5] = {(uint64_t)c, 4, (uint64_t)w, (uint64_t)h, (uint64_t)n};
+      const uint64_t strides[4] = {(uint64_t)c * es, (uint64_t)4 * c * es,
+                                   (uint64_t)4 * c * w * es, (uint64_t)4 * c * w * h * es};
+      const uint32_t box[5] = {64, 1, (uint32_t)kSeg, 1, 1};
+      if (encode_tmap(&prm.gmap, ty, 5, gout, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B) !=
+          DDPM_OK)
+        return DDPM_ERR_CUDA;  // the message is set
+      prm.g_tma = 1;
+      prm.g_nhwc = 1;
+    } else if (((size_t)w * es) % 16 == 0 && (reinterpret_cast<uintptr_t>(gout) & 15u) == 0) {
       const CUtensorMapDataType ty = dt == DDPM_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                      : dt == DDPM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                        : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;

@@ -789,6 +789,9 @@ struct DywParams {
   int tiles_w, tiles_h, num_tiles;
   int ngroups, ncg, splits;
   int nx;             // x-halo buffers (1 or 2)
+  // grad_out channel-last [N][H][W][4C] (kGTma only): gmap {C, 4, W, H, N}, box
+  // {16, 3, 16, 8, 1}, landing as [8 rows][16 px][3 branches][16 channels]
+  int g_nhwc;
   int* status;
 };
 
@@ -1146,7 +1149,10 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
               ok = tc::mbar_wait(g_empty, (xq & 1) ^ 1, abort_flag, kWaitNs);
               if (ok) {
                 tc::mbar_arrive_expect_tx(g_full, L.g_bytes);
-                tc::tma_load_5d(smem + L.g, &maps.gmap, w0, h0, cg * 16, 1, n, g_full);
+                if (p.g_nhwc)
+                  tc::tma_load_5d(smem + L.g, &maps.gmap, cg * 16, 1, w0, h0, n, g_full);
+                else
+                  tc::tma_load_5d(smem + L.g, &maps.gmap, w0, h0, cg * 16, 1, n, g_full);
               }
             }
             if (!__all_sync(0xffffffffu, ok)) {
@@ -1239,13 +1245,25 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
           failed = true;
           break;
         }
-        const T* gs = reinterpret_cast<const T*>(smem + L.g) + m;
+        if (p.g_nhwc) {
+          // [pixel][branch][16 channels]: two 16-byte vectors per branch
+          const uint4* gq = reinterpret_cast<const uint4*>(smem + L.g) + m * 6;
 #pragma unroll
-        for (int b = 0; b < 3; ++b)
+          for (int b = 0; b < 3; ++b) {
+            const uint4 v0 = gq[2 * b], v1 = gq[2 * b + 1];
+            const uint32_t wv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
 #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            gv[b][i] = f2_pack(to_f32<T>(gs[(b * 16 + 2 * i) * kTileM]),
-                               to_f32<T>(gs[(b * 16 + 2 * i + 1) * kTileM]));
+            for (int i = 0; i < 8; ++i) gv[b][i] = uncvt2<T>(wv[i]);
+          }
+        } else {
+          const T* gs = reinterpret_cast<const T*>(smem + L.g) + m;
+#pragma unroll
+          for (int b = 0; b < 3; ++b)
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              gv[b][i] = f2_pack(to_f32<T>(gs[(b * 16 + 2 * i) * kTileM]),
+                                 to_f32<T>(gs[(b * 16 + 2 * i + 1) * kTileM]));
+        }
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(g_empty);
       } else {
@@ -1487,10 +1505,13 @@ size_t gencat_bwd_workspace_bytes(int n, int c, int h, int w, int ks) {
 int gencat_bwd_yw(const void* x, const void* y, const void* staged, size_t staged_bytes,
                   const void* wpack, const void* gout, void* gy, void* gw, void* gb,
                   void* workspace, size_t ws_bytes, int n, int c, int h, int w, int ks, int d0,
-                  int d1, int d2, int dt, cudaStream_t st) {
+                  int d1, int d2, int dt, cudaStream_t st, int g_nhwc) {
   int rc = gencat::check_shape(n, c, h, w, ks, d0, d1, d2, dt);
   if (rc) return rc;
   DDPM_CHECK_ARG(((x && y) || staged) && wpack && gout, "null pointer");
+  if (g_nhwc && (dt == DDPM_F32 || c != 64 || staged == nullptr))
+    return set_error(DDPM_ERR_UNSUPPORTED,
+                     "a channel-last grad_out needs 16-bit data, C == 64 and staged operands");
   if (staged != nullptr) {
     const gencat::StageLayout sl = gencat::StageLayout::make(n, c, h, w, ks, d0, d1, d2, dt);
     if (staged_bytes < sl.total_bytes())
@@ -1550,8 +1571,22 @@ int gencat_bwd_yw(const void* x, const void* y, const void* staged, size_t stage
         maps.ph = sl.ph;
         // gradient tiles by TMA (16-bit) when the row pitch and base allow a map
         const size_t es = (size_t)dtype_size(dt);
-        if (use_staged && dt != DDPM_F32 && ((size_t)w * es) % 16 == 0 &&
-            (reinterpret_cast<uintptr_t>(gout) & 15u) == 0) {
+        if (g_nhwc) {
+          const uint64_t gd[5] = {(uint64_t)c, 4, (uint64_t)w, (uint64_t)h, (uint64_t)n};
+          const uint64_t gs[4] = {(uint64_t)c * es, (uint64_t)4 * c * es,
+                                  (uint64_t)4 * c * w * es, (uint64_t)4 * c * w * h * es};
+          const uint32_t gb_[5] = {16, 3, (uint32_t)gencat::kTileW, (uint32_t)gencat::kTileH, 1};
+          const CUtensorMapDataType ty = dt == DDPM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                         : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+          if (!use_staged || (reinterpret_cast<uintptr_t>(gout) & 15u) != 0 ||
+              encode_tmap(&maps.gmap, ty, 5, gout, gd, gs, gb_, CU_TENSOR_MAP_SWIZZLE_NONE) !=
+                  DDPM_OK)
+            return set_error(DDPM_ERR_UNSUPPORTED,
+                             "channel-last grad_out: the gradient tensor map is unavailable");
+          g_tma = true;
+          dp.g_nhwc = 1;
+        } else if (use_staged && dt != DDPM_F32 && ((size_t)w * es) % 16 == 0 &&
+                   (reinterpret_cast<uintptr_t>(gout) & 15u) == 0) {
           const uint64_t gd[5] = {(uint64_t)w, (uint64_t)h, (uint64_t)c, 4, (uint64_t)n};
           const uint64_t gs[4] = {w * es, (uint64_t)h * w * es, (uint64_t)c * h * w * es,
                                   (uint64_t)4 * c * h * w * es};
@@ -1585,6 +1620,10 @@ int gencat_bwd_yw(const void* x, const void* y, const void* staged, size_t stage
     }
   }
   // separate dY and dW passes (no merged-pass workspace): they stage from x and y
+  if (g_nhwc)
+    return set_error(DDPM_ERR_UNSUPPORTED,
+                     "a channel-last grad_out needs the merged pass (grad_y, grad_weight, "
+                     "grad_bias and the workspace)");
   DDPM_CHECK_ARG(x && y, "x and y are needed without a merged-pass workspace");
   if (gy != nullptr) {
     ByParams bp{};
@@ -1739,7 +1778,7 @@ int gencat_bwd_yw_static(const void* x, const void* y, const void* wpack, const 
   // dY needs no scratch: the workspace path's dY launch is used as is.
   if (gy != nullptr) {
     rc = gencat_bwd_yw(x, y, nullptr, 0, wpack, gout, gy, nullptr, nullptr, nullptr, 0, n, c, h,
-                       w, ks, d0, d1, d2, dt, st);
+                       w, ks, d0, d1, d2, dt, st, 0);
     if (rc) return rc;
   }
   if (gw == nullptr) return DDPM_OK;

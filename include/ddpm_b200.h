@@ -306,6 +306,39 @@ DDPM_API int ddpm_fuseconv_bwd(const void* x, const void* grad_out, const void* 
                                int dtype, void* stream);
 
 /*
+ * ddpm_fuseconv_bwd with grad_x written channel-last ([N][H][W][Cin],
+ * Cin % 16 == 0, 16-byte aligned) instead of NCHW (no reference
+ * counterpart). Same values bit for bit. In the DDPM module grad_x is the
+ * gradient of the generator forward's output, and the fused generator's
+ * backward (the *_nhwc entry points below) reads it channel-last: a pixel's
+ * channels are one contiguous run, loaded with 16-byte vectors.
+ */
+DDPM_API int ddpm_fuseconv_bwd_nhwc(const void* x, const void* grad_out, const void* packed,
+                                    void* grad_x, void* grad_weight, void* grad_bias,
+                                    void* workspace, size_t workspace_bytes, int n, int cin,
+                                    int cout, int h, int w, int dtype, void* stream);
+
+/*
+ * ddpm_gencat_bwd_x_staged / ddpm_gencat_bwd_yw_staged reading grad_out
+ * channel-last ([N][H][W][4C], as ddpm_fuseconv_bwd_nhwc writes it; no
+ * reference counterpart). bf16 / fp16 with C == 64 (DDPM_ERR_UNSUPPORTED
+ * otherwise); same results as the NCHW entry points (dX bit for bit, dY and
+ * dW/db to the FP32 summation order of dY's reductions). The kernels load a
+ * pixel's 16 channels as two 16-byte vectors instead of 16 strided elements.
+ */
+DDPM_API int ddpm_gencat_bwd_x_staged_nhwc(const void* staged_y, size_t staged_bytes,
+                                           const void* packed, const void* bias,
+                                           const void* grad_out, void* grad_x, int n, int c,
+                                           int h, int w, int ksize, int d0, int d1, int d2,
+                                           int dtype, void* stream);
+DDPM_API int ddpm_gencat_bwd_yw_staged_nhwc(const void* staged, size_t staged_bytes,
+                                            const void* packed, const void* grad_out,
+                                            void* grad_y, void* grad_weight, void* grad_bias,
+                                            void* workspace, size_t workspace_bytes, int n,
+                                            int c, int h, int w, int ksize, int d0, int d1,
+                                            int d2, int dtype, void* stream);
+
+/*
  * No-allocation variant of ddpm_gencat_bwd_yw (no counterpart in the
  * reference, whose Triton backward allocates its partials with torch).
  * Same arguments and results minus the workspace: the FP32 dW/db partials

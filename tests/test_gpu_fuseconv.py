@@ -182,3 +182,35 @@ def test_fuseconv_bwd_combined(shape, dtype):
     torch.testing.assert_close(gx, gx_ref, rtol=0, atol=0)
     torch.testing.assert_close(gw, gw_ref, rtol=0, atol=0)
     torch.testing.assert_close(gb, gb_ref, rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("shape", [(2, 256, 64, 15, 24), (1, 256, 64, 32, 136), (1, 32, 16, 9, 40)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_fuseconv_bwd_nhwc_matches_nchw(shape, dtype):
+    """ddpm_fuseconv_bwd_nhwc writes grad_x channel-last with the values of
+    ddpm_fuseconv_bwd bit for bit (and the same weight / bias gradients)."""
+    from dynamicconvolutionoperator_b200 import _lib
+
+    n, cin, cout, h, w = shape
+    x, wt, b, g = _inputs(shape, dtype, seed=9)
+    xd, wd, gd = x.cuda(), wt.cuda(), g.cuda()
+    packed = _pack(wd, cin, cout, dtype)
+    code = _lib.dtype_code(dtype)
+    st = _lib.stream_handle(xd.device)
+    nb = int(_lib.load().ddpm_fuseconv_bwd_weight_workspace_bytes(n, cin, cout, h, w))
+    ws = torch.empty(nb, dtype=torch.uint8, device="cuda")
+    outs = {}
+    for name in ("ddpm_fuseconv_bwd", "ddpm_fuseconv_bwd_nhwc"):
+        cl = name.endswith("nhwc")
+        gx = torch.full_like(xd, float("nan"),
+                             memory_format=torch.channels_last if cl else torch.contiguous_format)
+        gw = torch.full_like(wd, float("nan"))
+        gb = torch.full((cout,), float("nan"), dtype=dtype, device="cuda")
+        _lib.call(name, xd.data_ptr(), gd.data_ptr(), packed.data_ptr(), gx.data_ptr(),
+                  gw.data_ptr(), gb.data_ptr(), ws.data_ptr(), nb, n, cin, cout, h, w, code, st)
+        outs[name] = (gx, gw, gb)
+    torch.cuda.synchronize()
+    ref, got = outs["ddpm_fuseconv_bwd"], outs["ddpm_fuseconv_bwd_nhwc"]
+    assert got[0].is_contiguous(memory_format=torch.channels_last)
+    for a, r in zip(got, ref):
+        assert torch.equal(a, r)  # value comparison, layout-independent

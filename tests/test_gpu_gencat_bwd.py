@@ -204,3 +204,60 @@ def test_max_halo_and_ragged_gradient_tiles(shape, dtype):
                   _lib.stream_handle(o2.device))
         torch.cuda.synchronize()
     torch.testing.assert_close(o2.float().cpu(), gold_out.float(), rtol=rtol, atol=atol)
+
+
+@pytest.mark.parametrize("shape", [(2, 64, 15, 40), (1, 64, 33, 136)])
+@pytest.mark.parametrize("ks", [1, 3])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_channel_last_grad_out_matches_nchw(shape, ks, dtype):
+    """The *_staged_nhwc backward entry points read grad_out channel-last
+    ([N][H][W][4C], C = 64) and give dX bit for bit and dY, dW, db to FP32
+    summation order of the NCHW entry points."""
+    from dynamicconvolutionoperator_b200 import _kernels, _lib
+
+    x, y, wt, b = _case(shape, ks, dtype)
+    n, c, h, w = shape
+    g = torch.randn((n, 4 * c, h, w), generator=torch.Generator().manual_seed(8)).to(dtype)
+    xd, yd, wd, bd = x.cuda(), y.cuda(), wt.cuda(), b.cuda()
+    gd = g.cuda()
+    gd_cl = gd.contiguous(memory_format=torch.channels_last)
+    packed = _kernels.pack_generator_weight(wd, bd, c, ks)
+    st, nb = _stage(xd, yd, ks, (1, 3, 5))
+    code = _lib.dtype_code(dtype)
+    stream = _lib.stream_handle(xd.device)
+    ws_bytes = int(_lib.load().ddpm_gencat_bwd_workspace_bytes(n, c, h, w, ks))
+    res = {}
+    for sfx, gg in (("", gd), ("_nhwc", gd_cl)):
+        gx = torch.full_like(xd, float("nan"))
+        gy = torch.full_like(yd, float("nan"))
+        gw = torch.full((3 * c * ks * ks, c), float("nan"), dtype=dtype, device="cuda")
+        gb = torch.full((3 * c * ks * ks,), float("nan"), dtype=dtype, device="cuda")
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+        _lib.call("ddpm_gencat_bwd_x_staged" + sfx, st.data_ptr(), nb, packed.data_ptr(),
+                  bd.data_ptr(), gg.data_ptr(), gx.data_ptr(), n, c, h, w, ks, 1, 3, 5, code,
+                  stream)
+        _lib.call("ddpm_gencat_bwd_yw_staged" + sfx, st.data_ptr(), nb, packed.data_ptr(),
+                  gg.data_ptr(), gy.data_ptr(), gw.data_ptr(), gb.data_ptr(), ws.data_ptr(),
+                  ws_bytes, n, c, h, w, ks, 1, 3, 5, code, stream)
+        res[sfx] = (gx, gy, gw, gb)
+    torch.cuda.synchronize()
+    ref, got = res[""], res["_nhwc"]
+    assert torch.equal(got[0], ref[0]), "dX differs"
+    for a, r in zip(got[1:], ref[1:]):
+        assert torch.isfinite(a).all()
+        scale = r.double().abs().max().item() + 1e-12
+        assert (a.double() - r.double()).abs().max().item() / scale <= 1e-2
+
+
+def test_channel_last_grad_out_rejected_outside_its_limits():
+    """fp32, C != 64 and the unstaged path return DDPM_ERR_UNSUPPORTED."""
+    from dynamicconvolutionoperator_b200 import _lib
+
+    lib = _lib.load()
+    t = torch.zeros(16, dtype=torch.uint8, device="cuda")
+    p = t.data_ptr()
+    stream = _lib.stream_handle(t.device)
+    for c, code in ((64, 0), (32, 1)):
+        rc = lib.ddpm_gencat_bwd_x_staged_nhwc(p, 16, p, p, p, p, 1, c, 8, 16, 3, 1, 3, 5, code,
+                                               stream)
+        assert rc == -2, (c, code, rc)
