@@ -398,9 +398,9 @@ NCU_TRAFFIC_BYTES: dict[tuple[str, str], float] = {
     ("gencat_fwd", "torch.float32"): 115258624,
     ("gencat_fwd", "torch.bfloat16"): 42377472,
     ("gencat_bwd_x", "torch.float32"): 91352320,
-    ("gencat_bwd_x", "torch.bfloat16"): 45780224,
+    ("gencat_bwd_x", "torch.bfloat16"): 45458944 + 896000,  # channel-last grad_out
     ("gencat_bwd_yw", "torch.float32"): 114652928,
-    ("gencat_bwd_yw", "torch.bfloat16"): 73122816,
+    ("gencat_bwd_yw", "torch.bfloat16"): 69589504 + 3247104,  # channel-last grad_out
     ("fuseconv_fwd", "torch.float32"): 75615744,
     ("fuseconv_fwd", "torch.bfloat16"): 36270848,
     ("fuseconv_dgrad", "torch.float32"): 27409920,
@@ -499,18 +499,24 @@ def library_kernels(model, x, y, dtype, device, materialised=True):
         _lib.call("ddpm_fuseconv_bwd_data_staged", gplanes.data_ptr(), gp_bytes,
                   fpacked.data_ptr(), fgx.data_ptr(), n, 4 * C, C, H, W, code, sh)
 
+    # as in the step: for 16-bit data at C=64 the fuse conv hands the generator
+    # backward its gradient channel-last, and the *_nhwc entry points read it so
+    nhwc = dtype != torch.float32 and C == 64
+    gout_g = gout.contiguous(memory_format=torch.channels_last) if nhwc else gout
+    sfx = "_nhwc" if nhwc else ""
+
     def bwd_x():
-        _lib.call("ddpm_gencat_bwd_x_staged", sy.data_ptr(), sy_bytes, packed.data_ptr(),
-                  gen_b.data_ptr(), gout.data_ptr(), gx.data_ptr(), n, C, H, W, K, *DILATIONS,
+        _lib.call("ddpm_gencat_bwd_x_staged" + sfx, sy.data_ptr(), sy_bytes, packed.data_ptr(),
+                  gen_b.data_ptr(), gout_g.data_ptr(), gx.data_ptr(), n, C, H, W, K, *DILATIONS,
                   code, sh)
 
     def bwd_yw():
-        _lib.call("ddpm_gencat_bwd_yw_staged", sy.data_ptr(), sy_bytes, packed.data_ptr(),
-                  gout.data_ptr(), gy.data_ptr(), gw.data_ptr(), gb.data_ptr(), ws.data_ptr(),
+        _lib.call("ddpm_gencat_bwd_yw_staged" + sfx, sy.data_ptr(), sy_bytes, packed.data_ptr(),
+                  gout_g.data_ptr(), gy.data_ptr(), gw.data_ptr(), gb.data_ptr(), ws.data_ptr(),
                   ws_bytes, n, C, H, W, K, *DILATIONS, code, sh)
 
-    keep = (taps, out, gout, gx, gk, packed, out2, gy, gw, gb, ws, fpacked, fout, fgout, fgx,
-            fgw, fgb, fws, sy, fplanes, gplanes)
+    keep = (taps, out, gout, gout_g, gx, gk, packed, out2, gy, gw, gb, ws, fpacked, fout, fgout,
+            fgx, fgw, fgb, fws, sy, fplanes, gplanes)
     kernels = {
         "fuseconv_fwd": (fuse_fwd, "tensor", fuse_flops),
         "fuseconv_wgrad": (
