@@ -239,3 +239,30 @@ def test_autocast_runs_the_native_kernels(ac_dtype, fused):
     stats, fails = compare(out.detach().cpu(), {k: v.cpu() for k, v in zip(names, grads)},
                            gold_out, gold_grads, ac_dtype)
     _assert_ok(stats, fails)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_training_step_hands_the_generator_a_channel_last_gradient(dtype, monkeypatch):
+    """For 16-bit data at C=64 the fuse conv writes the gradient of the
+    generator output channel-last and the generator backward reads it so
+    (the *_nhwc entry points); FP32 keeps NCHW. Both within the oracle's
+    tolerance (the cfg4 parity test covers the values at 256^2)."""
+    from dynamicconvolutionoperator_b200 import _lib
+
+    calls = []
+    real = _lib.call
+
+    def spy(name, *args):
+        calls.append(name)
+        return real(name, *args)
+
+    monkeypatch.setattr(_lib, "call", spy)
+    stats, fails = ddpm_parity((1, 64, 24, 40), 3, dtype, seed=60, input_seed=61,
+                               fused_generator_training=True)
+    _assert_ok(stats, fails)
+    nhwc = {n for n in calls if n.endswith("_nhwc")}
+    if dtype == torch.bfloat16:
+        assert nhwc == {"ddpm_fuseconv_bwd_nhwc", "ddpm_gencat_bwd_x_staged_nhwc",
+                        "ddpm_gencat_bwd_yw_staged_nhwc"}, calls
+    else:
+        assert not nhwc, calls
