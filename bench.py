@@ -754,11 +754,18 @@ def triton_reference_leg(args, device):
             "timing": "eager fwd+bwd, CUDA events, L2 flushed between steps"}
 
 
-def run_triton_legs(args, legs, timeout_s=420):
+def run_triton_legs(args, legs, timeout_s=180, budget_s=360):
     """Each reference Triton measurement in its own process (a failure there
-    cannot touch this process's CUDA context)."""
+    cannot touch this process's CUDA context), each bounded in time and all of
+    them together too, so the bench line always comes out."""
     out = {}
+    t_start = time.monotonic()
     for name, extra in legs:
+        left = budget_s - (time.monotonic() - t_start)
+        if left < 30:
+            out[name] = {"unavailable": f"skipped: the {budget_s} s budget of these legs ran out"}
+            continue
+        timeout_s = min(timeout_s, left)
         cmd = [sys.executable, str(REPO / "bench.py"), "--triton-ref", "--steps", str(args.steps),
                "--warmup", str(args.warmup)] + extra
         try:
@@ -771,7 +778,7 @@ def run_triton_legs(args, legs, timeout_s=420):
                 tail = (res.stderr or res.stdout).strip().splitlines()[-1:] or ["no output"]
                 out[name] = {"unavailable": f"exit {res.returncode}: {tail[0][:300]}"}
         except subprocess.TimeoutExpired:
-            out[name] = {"unavailable": f"did not finish within {timeout_s} s"}
+            out[name] = {"unavailable": f"did not finish within {timeout_s:.0f} s"}
     return out
 
 
