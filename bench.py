@@ -300,8 +300,9 @@ def measure(args, dtype, batch, device, rank, world, dist, timed_clocks=False, m
     # ---- end to end through the public API: H2D inputs, fwd+bwd, D2H loss ----
     # All H2D copies of the step are queued on a copy stream at the start of
     # the timed region, micro-batch by micro-batch; the compute stream starts
-    # micro-batch i once its three copies are done, so the copies of i+1
-    # overlap the compute of i. Gradients accumulate over the micro-batches
+    # micro-batch i's forward once its x and y copies are done and its
+    # backward once its upstream-gradient copy is, so the copies overlap the
+    # compute. Gradients accumulate over the micro-batches
     # (every one but the last under no_sync), the all-reduce runs once, and
     # the summed loss is read back. Every copy lies inside the timed region.
     mb = micro or batch
@@ -314,24 +315,30 @@ def measure(args, dtype, batch, device, rank, world, dist, timed_clocks=False, m
     def e2e_step():
         zero()
         copy_stream.wait_stream(stream)
-        ready = []
+        ready_xy, ready_g = [], []
         with torch.cuda.stream(copy_stream):
             for a, b in bounds:
                 x[a:b].copy_(hx[a:b], non_blocking=True)
                 y[a:b].copy_(hy[a:b], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(copy_stream)
+                ready_xy.append(ev)
+                # the upstream gradient is needed only by the backward: its copy
+                # overlaps the micro-batch's forward
                 g[a:b].copy_(hg[a:b], non_blocking=True)
                 ev = torch.cuda.Event()
                 ev.record(copy_stream)
-                ready.append(ev)
+                ready_g.append(ev)
         loss = torch.zeros((), dtype=torch.float32, device=device)
         for i, (a, b) in enumerate(bounds):
-            stream.wait_event(ready[i])
+            stream.wait_event(ready_xy[i])
             last = i == len(bounds) - 1
             ctx = reducer.no_sync() if (reducer is not None and not last) else contextlib.nullcontext()
             with ctx:
                 xe = x[a:b].detach().requires_grad_(True)
                 ye = y[a:b].detach().requires_grad_(True)
                 out = model(xe, ye)
+                stream.wait_event(ready_g[i])
                 out.backward(g[a:b])
             with torch.no_grad():
                 loss += torch.dot(out.reshape(-1), g[a:b].reshape(-1)).float()
@@ -782,6 +789,45 @@ def run_triton_legs(args, legs, timeout_s=180, budget_s=360):
     return out
 
 
+# ------------------------------------------------------ inference (cfg[2]) --
+def inference_lines(args, device):
+    """DDPM inference (forward only, no autograd), B=1, C=64,
+    128x128, K=3 (fused generator path) and K=5 (materialised path: the 1x1
+    generator on cuDNN, then this library's filter kernels), fp32 and bf16;
+    graph-replayed device time, L2 flushed between steps."""
+    from dynamicconvolutionoperator_b200 import DDPM
+
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
+    stream = torch.cuda.current_stream(device)
+    out = {}
+    for ks in (3, 5):
+        for dname in ("fp32", "bf16"):
+            dtype = DTYPES[dname]
+            torch.manual_seed(0)
+            model = DDPM(C, ks).to(device=device, dtype=dtype).eval()
+            gen = torch.Generator().manual_seed(9)
+            x, y = (torch.randn((1, C, 128, 128), generator=gen).to(dtype).to(device)
+                    for _ in range(2))
+            with torch.no_grad():
+                side = torch.cuda.Stream(device)
+                side.wait_stream(stream)
+                with torch.cuda.stream(side):
+                    for _ in range(3):
+                        model(x, y)
+                stream.wait_stream(side)
+                torch.cuda.synchronize()
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    model(x, y)
+            for _ in range(args.warmup):
+                graph.replay()
+            ts = time_steps(graph.replay, max(args.steps, 10), flush, stream)
+            out[f"K{ks}_{dname}"] = {"ms": round(statistics.median(ts), 4),
+                                     "path": "fused" if ks == 3 else "materialised"}
+            del graph, model
+    return {"workload": "configs[2] DDPM inference, B=1, C=64, 128x128", **out}
+
+
 # --------------------------------------------------------------- crossover --
 CROSSOVER_SIZES = (32, 48, 64, 96, 128, 192, 256)
 
@@ -935,6 +981,10 @@ def main(argv=None):
             extra[f"configs[3]_{dname}"] = entry
             del m
             torch.cuda.empty_cache()
+
+    if world == 1 and not args.skip_extra:
+        extra["configs[2]_inference"] = inference_lines(args, device)
+        torch.cuda.empty_cache()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
