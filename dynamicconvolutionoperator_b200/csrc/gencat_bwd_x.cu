@@ -374,10 +374,16 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
               }
             }
             if (p.g_tma) {
-              if constexpr (kNhwc)
-                tc::tma_load_5d(gs, &p.gmap, 0, b + 1, w0 - 8, hr, n, &u_full[ub]);
-              else
+              if constexpr (kNhwc) {
+                // one 128-byte-wide box per 128 bytes of channels (FP32: two)
+                constexpr int kBoxes = (int)sizeof(T) / 2;
+#pragma unroll
+                for (int bx = 0; bx < kBoxes; ++bx)
+                  tc::tma_load_5d(reinterpret_cast<uint8_t*>(gs) + bx * kSeg * 128, &p.gmap,
+                                  bx * (64 / kBoxes), b + 1, w0 - 8, hr, n, &u_full[ub]);
+              } else {
                 tc::tma_load_4d(gs, &p.gmap, w0 - 8, hr, (b + 1) * C, n, &u_full[ub]);
+              }
             }
           }
           if (!p.g_tma)
@@ -465,16 +471,16 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
           // (kept in the I/O type: a conversion right after the load waited for it)
           if (u == kUnits - 1) {
             if constexpr (kNhwc) {
-              // channel-last: the pixel's 16 channels are two 16-byte vectors
+              // channel-last: the pixel's 16 channels are 16-byte vectors
+              constexpr int kVecs = 16 * (int)sizeof(T) / 16;
               const uint4* g0v = reinterpret_cast<const uint4*>(
                   gout + (((size_t)n * H + h) * W + w) * 4 * C + wg * 16);
-              uint4 v0 = make_uint4(0u, 0u, 0u, 0u), v1 = v0;
-              if (px_ok && wg < nblk) {
-                v0 = __ldg(g0v);
-                v1 = __ldg(g0v + 1);
+#pragma unroll
+              for (int k = 0; k < kVecs; ++k) {
+                uint4 v = make_uint4(0u, 0u, 0u, 0u);
+                if (px_ok && wg < nblk) v = __ldg(g0v + k);
+                memcpy(reinterpret_cast<uint8_t*>(g0raw) + 16 * k, &v, 16);
               }
-              memcpy(&g0raw[0], &v0, 16);
-              memcpy(&g0raw[8], &v1, 16);
             } else {
               const T* g0p = gn + (size_t)(wg * 16) * P + (size_t)h * W + w;
 #pragma unroll
@@ -525,14 +531,33 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
               const int dx = (kj - r) * d;
               float gv[16];
               if constexpr (kNhwc) {
-                // pixel row m + 8 - dx of the swizzled [kSeg][64] segment:
-                // channel chunks 2wg and 2wg+1 (8 channels each)
+                // pixel row m + 8 - dx of the swizzled [kSeg][128 bytes]
+                // segment(s): this block's channel chunks, chunk j of row r at
+                // j ^ (r & 7)
                 const int pr = m + 8 - dx;
-                const uint8_t* row = reinterpret_cast<const uint8_t*>(gs) + pr * 128;
-                const uint4 v0 = *reinterpret_cast<const uint4*>(row + (((2 * wg) ^ (pr & 7)) * 16));
-                const uint4 v1 =
-                    *reinterpret_cast<const uint4*>(row + (((2 * wg + 1) ^ (pr & 7)) * 16));
-                unpack16<T>(v0, v1, gv);
+                if constexpr (sizeof(T) == 4) {
+                  // FP32: box wg / 2 holds channels 32 (wg / 2) .. +31; the
+                  // block's 16 channels are chunks 4 (wg % 2) .. +3
+                  const uint8_t* row = reinterpret_cast<const uint8_t*>(gs) +
+                                       (wg >> 1) * kSeg * 128 + pr * 128;
+#pragma unroll
+                  for (int k = 0; k < 4; ++k) {
+                    const float4 v = *reinterpret_cast<const float4*>(
+                        row + ((((wg & 1) * 4 + k) ^ (pr & 7)) * 16));
+                    gv[4 * k] = v.x;
+                    gv[4 * k + 1] = v.y;
+                    gv[4 * k + 2] = v.z;
+                    gv[4 * k + 3] = v.w;
+                  }
+                } else {
+                  // 16-bit: chunks 2wg and 2wg+1 (8 channels each)
+                  const uint8_t* row = reinterpret_cast<const uint8_t*>(gs) + pr * 128;
+                  const uint4 v0 =
+                      *reinterpret_cast<const uint4*>(row + (((2 * wg) ^ (pr & 7)) * 16));
+                  const uint4 v1 =
+                      *reinterpret_cast<const uint4*>(row + (((2 * wg + 1) ^ (pr & 7)) * 16));
+                  unpack16<T>(v0, v1, gv);
+                }
               } else {
 #pragma unroll
                 for (int cl = 0; cl < 16; ++cl) gv[cl] = to_f32<T>(gcol[cl * kSeg - dx]);
@@ -650,9 +675,7 @@ int launch_k(const BxParams& prm, cudaStream_t st) {
 
 template <typename T, int KS>
 int launch(const BxParams& prm, cudaStream_t st) {
-  if constexpr (sizeof(T) == 2) {
-    if (prm.g_nhwc) return launch_k<T, KS, true, true>(prm, st);
-  }
+  if (prm.g_nhwc) return launch_k<T, KS, true, true>(prm, st);
   if (prm.staged != nullptr) return launch_k<T, KS, true>(prm, st);
   return launch_k<T, KS, false>(prm, st);
 }
@@ -676,9 +699,9 @@ int gencat_bwd_x(const void* y, const void* staged, size_t staged_bytes, const v
   int rc = gencat::check_shape(n, c, h, w, ks, d0, d1, d2, dt);
   if (rc) return rc;
   DDPM_CHECK_ARG((y || staged) && wpack && bias && gout && gx, "null pointer");
-  if (g_nhwc && (dt == DDPM_F32 || c != 64 || staged == nullptr))
+  if (g_nhwc && (c != 64 || staged == nullptr))
     return set_error(DDPM_ERR_UNSUPPORTED,
-                     "a channel-last grad_out needs 16-bit data, C == 64 and staged operands");
+                     "a channel-last grad_out needs C == 64 and staged operands");
   const gencat::PackLayout pl = gencat::PackLayout::make(c, ks, dt);
   BxParams prm{};
   prm.y = y;
@@ -711,12 +734,15 @@ int gencat_bwd_x(const void* y, const void* staged, size_t staged_bytes, const v
     if (g_nhwc) {
       DDPM_CHECK_ARG((reinterpret_cast<uintptr_t>(gout) & 15u) == 0,
                      "grad_out must be 16-byte aligned");
-      const CUtensorMapDataType ty =
-          dt == DDPM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+      const CUtensorMapDataType ty = dt == DDPM_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                     : dt == DDPM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                       : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
       const uint64_t dims[5] = {(uint64_t)c, 4, (uint64_t)w, (uint64_t)h, (uint64_t)n};
       const uint64_t strides[4] = {(uint64_t)c * es, (uint64_t)4 * c * es,
                                    (uint64_t)4 * c * w * es, (uint64_t)4 * c * w * h * es};
-      const uint32_t box[5] = {64, 1, (uint32_t)kSeg, 1, 1};
+      // 128 bytes of channels per box (the 128-byte swizzle span): 64 16-bit
+      // or 32 FP32 channels; FP32 takes two boxes per unit
+      const uint32_t box[5] = {(uint32_t)(128 / es), 1, (uint32_t)kSeg, 1, 1};
       if (encode_tmap(&prm.gmap, ty, 5, gout, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B) !=
           DDPM_OK)
         return DDPM_ERR_CUDA;  // the message is set

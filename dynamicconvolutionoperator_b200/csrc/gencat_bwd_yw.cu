@@ -135,6 +135,32 @@ __device__ __forceinline__ void load_gv(unsigned long long (&gv)[3][8], const T*
     for (int i = 0; i < 8; ++i) gv[b][i] = f2_pack(v[b][2 * i], v[b][2 * i + 1]);
 }
 
+// The same from a channel-last grad_out [N][H][W][4C]: per branch the 16
+// channels are one contiguous run (16-byte vector loads).
+template <typename T>
+__device__ __forceinline__ void load_gv_nhwc(unsigned long long (&gv)[3][8], const T* gout, int n,
+                                             int H, int W, int C, int cg16, int h, int w,
+                                             bool px_ok) {
+  constexpr int kVecs = 16 * (int)sizeof(T) / 16;  // vectors per 16 channels
+  constexpr int kPer = 16 / (int)sizeof(T);        // elements per vector
+#pragma unroll
+  for (int b = 0; b < 3; ++b) {
+    float v[16];
+    const uint4* src = reinterpret_cast<const uint4*>(
+        gout + (((size_t)n * H + h) * W + w) * 4 * C + (b + 1) * C + cg16 * 16);
+#pragma unroll
+    for (int k = 0; k < kVecs; ++k) {
+      uint4 u = make_uint4(0u, 0u, 0u, 0u);
+      if (px_ok) u = __ldg(src + k);
+      const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) v[k * kPer + i] = to_f32<T>(e[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) gv[b][i] = f2_pack(v[2 * i], v[2 * i + 1]);
+  }
+}
+
 // =============================================================== dY =========
 template <typename T, int KS>
 struct ByCfg {
@@ -1266,6 +1292,8 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
         }
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(g_empty);
+      } else if (p.g_nhwc) {
+        load_gv_nhwc<T>(gv, gout, n, H, W, C, cg, h, w, px_ok);
       } else {
         load_gv<T>(gv, gn, C, P, cg, pix, px_ok);
       }
@@ -1509,9 +1537,9 @@ int gencat_bwd_yw(const void* x, const void* y, const void* staged, size_t stage
   int rc = gencat::check_shape(n, c, h, w, ks, d0, d1, d2, dt);
   if (rc) return rc;
   DDPM_CHECK_ARG(((x && y) || staged) && wpack && gout, "null pointer");
-  if (g_nhwc && (dt == DDPM_F32 || c != 64 || staged == nullptr))
+  if (g_nhwc && (c != 64 || staged == nullptr))
     return set_error(DDPM_ERR_UNSUPPORTED,
-                     "a channel-last grad_out needs 16-bit data, C == 64 and staged operands");
+                     "a channel-last grad_out needs C == 64 and staged operands");
   if (staged != nullptr) {
     const gencat::StageLayout sl = gencat::StageLayout::make(n, c, h, w, ks, d0, d1, d2, dt);
     if (staged_bytes < sl.total_bytes())
@@ -1571,7 +1599,12 @@ int gencat_bwd_yw(const void* x, const void* y, const void* staged, size_t stage
         maps.ph = sl.ph;
         // gradient tiles by TMA (16-bit) when the row pitch and base allow a map
         const size_t es = (size_t)dtype_size(dt);
-        if (g_nhwc) {
+        if (g_nhwc && dt == DDPM_F32) {
+          // FP32 builders load their gradient values themselves (channel-last)
+          DDPM_CHECK_ARG((reinterpret_cast<uintptr_t>(gout) & 15u) == 0,
+                         "grad_out must be 16-byte aligned");
+          dp.g_nhwc = 1;
+        } else if (g_nhwc) {
           const uint64_t gd[5] = {(uint64_t)c, 4, (uint64_t)w, (uint64_t)h, (uint64_t)n};
           const uint64_t gs[4] = {(uint64_t)c * es, (uint64_t)4 * c * es,
                                   (uint64_t)4 * c * w * es, (uint64_t)4 * c * w * h * es};
