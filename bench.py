@@ -94,6 +94,8 @@ def parse_args(argv=None):
     ap.add_argument("--triton-ref", action="store_true",
                     help="time the reference's own Triton path (baseline/_ref) on cuda:0 for "
                          "--workload/--dtype and exit (run by the main bench as a subprocess)")
+    ap.add_argument("--inference", action="store_true",
+                    help="print the configs[2] inference lines (fused and materialised) only")
     ap.add_argument("--crossover", action="store_true",
                     help="time fused vs materialised training steps over image sizes and exit")
     ap.add_argument("--profile-kernel", default=None,
@@ -792,8 +794,9 @@ def run_triton_legs(args, legs, timeout_s=180, budget_s=360):
 # ------------------------------------------------------ inference (cfg[2]) --
 def inference_lines(args, device):
     """DDPM inference (forward only, no autograd), B=1, C=64,
-    128x128, K=3 (fused generator path) and K=5 (materialised path: the 1x1
-    generator on cuDNN, then this library's filter kernels), fp32 and bf16;
+    128x128, K=3 and K=5, fp32 and bf16, through the fused generator path
+    (``fused_generator_inference=True``, the default) and the materialised
+    path (the 1x1 generator on cuDNN, then this library's filter kernels);
     graph-replayed device time, L2 flushed between steps."""
     from dynamicconvolutionoperator_b200 import DDPM
 
@@ -803,28 +806,31 @@ def inference_lines(args, device):
     for ks in (3, 5):
         for dname in ("fp32", "bf16"):
             dtype = DTYPES[dname]
-            torch.manual_seed(0)
-            model = DDPM(C, ks).to(device=device, dtype=dtype).eval()
-            gen = torch.Generator().manual_seed(9)
-            x, y = (torch.randn((1, C, 128, 128), generator=gen).to(dtype).to(device)
-                    for _ in range(2))
-            with torch.no_grad():
-                side = torch.cuda.Stream(device)
-                side.wait_stream(stream)
-                with torch.cuda.stream(side):
-                    for _ in range(3):
+            line = {}
+            for path in ("fused", "materialised"):
+                torch.manual_seed(0)
+                model = DDPM(C, ks, fused_generator_inference=path == "fused")
+                model = model.to(device=device, dtype=dtype).eval()
+                gen = torch.Generator().manual_seed(9)
+                x, y = (torch.randn((1, C, 128, 128), generator=gen).to(dtype).to(device)
+                        for _ in range(2))
+                with torch.no_grad():
+                    side = torch.cuda.Stream(device)
+                    side.wait_stream(stream)
+                    with torch.cuda.stream(side):
+                        for _ in range(3):
+                            model(x, y)
+                    stream.wait_stream(side)
+                    torch.cuda.synchronize()
+                    graph = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(graph):
                         model(x, y)
-                stream.wait_stream(side)
-                torch.cuda.synchronize()
-                graph = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(graph):
-                    model(x, y)
-            for _ in range(args.warmup):
-                graph.replay()
-            ts = time_steps(graph.replay, max(args.steps, 10), flush, stream)
-            out[f"K{ks}_{dname}"] = {"ms": round(statistics.median(ts), 4),
-                                     "path": "fused" if ks == 3 else "materialised"}
-            del graph, model
+                for _ in range(args.warmup):
+                    graph.replay()
+                ts = time_steps(graph.replay, max(args.steps, 10), flush, stream)
+                line[f"{path}_ms"] = round(statistics.median(ts), 4)
+                del graph, model
+            out[f"K{ks}_{dname}"] = line
     return {"workload": "configs[2] DDPM inference, B=1, C=64, 128x128", **out}
 
 
@@ -908,6 +914,9 @@ def main(argv=None):
         return 0
     if args.crossover:
         print(json.dumps({"crossover": crossover(args, device)}), flush=True)
+        return 0
+    if args.inference:
+        print(json.dumps({"configs[2]_inference": inference_lines(args, device)}), flush=True)
         return 0
 
     if args.launch_list:

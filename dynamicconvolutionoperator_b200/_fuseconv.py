@@ -60,8 +60,8 @@ def fuse_conv_supported(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tenso
 
 def nhwc_grad_ok(cat: torch.Tensor) -> bool:
     """Whether the gradient of a fused generator output ``cat`` [N, 4C, H, W]
-    can travel channel-last to the generator's backward (16-bit, C == 64)."""
-    return cat.dtype in (torch.bfloat16, torch.float16) and cat.shape[1] == 256
+    can travel channel-last to the generator's backward (C == 64)."""
+    return cat.shape[1] == 256
 
 
 def pack_fuse_weight(weight: torch.Tensor) -> torch.Tensor:

@@ -11,6 +11,7 @@ Triton and no CPU or eager-PyTorch fallback: non-CUDA tensors raise.
 from __future__ import annotations
 
 import torch
+import torch.nn.functional as F
 
 from . import _lib
 from ._gradbuf import grad_buffer, grads_written
@@ -71,24 +72,30 @@ class _DynamicCat(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad_out):
         x, kernels = ctx.saved_tensors
-        grad_out = grad_out.to(kernels.dtype).contiguous()
-        n, c, h, w = x.shape
-        need_x, need_k = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
-        grad_x = torch.empty_like(x) if need_x else None
-        grad_k = torch.empty_like(kernels) if need_k else None
-        if need_x or need_k:
-            d0, d1, d2 = ctx.dilations
-            with torch.cuda.device(x.device):
-                _lib.call(
-                    "ddpm_dyncat_bwd",
-                    x.data_ptr(), _lib.dtype_code(x.dtype),
-                    kernels.data_ptr(), grad_out.data_ptr(), _lib.dtype_code(kernels.dtype),
-                    grad_x.data_ptr() if need_x else None,
-                    grad_k.data_ptr() if need_k else None,
-                    n, c, h, w, ctx.kernel_size, d0, d1, d2,
-                    _lib.stream_handle(x.device),
-                )
+        grad_x, grad_k = _dyncat_backward(x, kernels, grad_out, ctx.kernel_size, ctx.dilations,
+                                          ctx.needs_input_grad[0], ctx.needs_input_grad[1])
         return grad_x, grad_k, None, None
+
+
+def _dyncat_backward(x, kernels, grad_out, ks, dilations, need_x, need_k):
+    """(grad_x, grad_kernels) of the materialised filter (``ddpm_dyncat_bwd``)."""
+    grad_out = grad_out.to(kernels.dtype).contiguous()
+    n, c, h, w = x.shape
+    grad_x = torch.empty_like(x) if need_x else None
+    grad_k = torch.empty_like(kernels) if need_k else None
+    if need_x or need_k:
+        d0, d1, d2 = dilations
+        with torch.cuda.device(x.device):
+            _lib.call(
+                "ddpm_dyncat_bwd",
+                x.data_ptr(), _lib.dtype_code(x.dtype),
+                kernels.data_ptr(), grad_out.data_ptr(), _lib.dtype_code(kernels.dtype),
+                grad_x.data_ptr() if need_x else None,
+                grad_k.data_ptr() if need_k else None,
+                n, c, h, w, ks, d0, d1, d2,
+                _lib.stream_handle(x.device),
+            )
+    return grad_x, grad_k
 
 
 def fused_dynamic_cat(x, kernels, kernel_size, dilations):
@@ -100,29 +107,32 @@ def fused_dynamic_cat(x, kernels, kernel_size, dilations):
 # Limits of the fused generator kernels of this build (tcgen05 tiles hold the
 # padded channel count in shared memory and TMEM).
 FUSED_MAX_CHANNELS = 64
-FUSED_KERNEL_SIZES = (1, 3)
-# The flash-style recompute backward kernels.
+# Kernel sizes of the fused forward, and of the flash-style recompute backward
+# kernels (K <= 3, like the reference's fused training, ``triton_impl.py:320``).
+FUSED_KERNEL_SIZES = (1, 3, 5)
+FUSED_TRAINING_KERNEL_SIZES = (1, 3)
 FUSED_BACKWARD_AVAILABLE = True
 
-
-FUSED_MAX_HALO = 8
+# Largest dilation halo (K // 2) * max(dilations) of the fused forward per K:
+# the x halo tile spans 8 (K <= 3) or 16 (K = 5) pixels beyond the tile.
+FUSED_MAX_HALO = {1: 8, 3: 8, 5: 16}
 
 
 def fused_generator_supported(channels: int, kernel_size: int, dtype: torch.dtype,
                               dilations=(1, 3, 5)) -> bool:
-    """Whether the fused generator+filter kernels cover this configuration."""
+    """Whether the fused generator+filter forward covers this configuration."""
     return (
         channels <= FUSED_MAX_CHANNELS
         and kernel_size in FUSED_KERNEL_SIZES
         and dtype in _lib.DTYPE_CODE
-        and (kernel_size // 2) * max(dilations) <= FUSED_MAX_HALO
+        and (kernel_size // 2) * max(dilations) <= FUSED_MAX_HALO[kernel_size]
     )
 
 
 def fused_training_supported(kernel_size: int) -> bool:
     """The flash-style recompute backward covers K <= 3, like the reference
     (``triton_impl.py:320``)."""
-    return FUSED_BACKWARD_AVAILABLE and kernel_size in FUSED_KERNEL_SIZES
+    return FUSED_BACKWARD_AVAILABLE and kernel_size in FUSED_TRAINING_KERNEL_SIZES
 
 
 def auto_fuse_training(tokens: int, channels: int, kernel_size: int, dtype: torch.dtype) -> bool:
@@ -225,8 +235,8 @@ def _prepare(x, y, weight, bias, kernel_size, dilations):
     if not fused_generator_supported(c, kernel_size, x.dtype, _dil(dilations)):
         raise RuntimeError(
             f"fused generator kernels support C <= {FUSED_MAX_CHANNELS}, K in "
-            f"{FUSED_KERNEL_SIZES} and a dilation halo <= {FUSED_MAX_HALO}; got C={c}, "
-            f"K={kernel_size}, dilations={tuple(dilations)}"
+            f"{FUSED_KERNEL_SIZES} and a dilation halo <= {FUSED_MAX_HALO} (per K); got "
+            f"C={c}, K={kernel_size}, dilations={tuple(dilations)}"
         )
     return x, y, bias
 
@@ -254,6 +264,8 @@ class _GeneratorDynamicCat(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_out):
+        if ctx.kernel_size not in FUSED_TRAINING_KERNEL_SIZES:
+            return _recompute_backward(ctx, grad_out)
         x, y, weight, bias = ctx.saved_tensors
         packed = ctx.packed
         n, c, h, w = x.shape
@@ -274,8 +286,8 @@ class _GeneratorDynamicCat(torch.autograd.Function):
                       else torch.empty(rows, dtype=x.dtype, device=x.device))
         full = need_y and grad_w is not None
         # a channel-last grad_out (the module's fuse conv writes it so for a
-        # 16-bit C = 64 generator output) is read as is; anything else as NCHW
-        nhwc = (grad_out.dtype == x.dtype and x.dtype != torch.float32 and c == 64
+        # C = 64 generator output) is read as is; anything else as NCHW
+        nhwc = (grad_out.dtype == x.dtype and c == 64
                 and not grad_out.is_contiguous()
                 and grad_out.is_contiguous(memory_format=torch.channels_last)
                 and (full or not (need_y or grad_w is not None)))
@@ -321,6 +333,34 @@ class _GeneratorDynamicCat(torch.autograd.Function):
         gw = grad_w.view_as(weight) if (grad_w is not None and need_w) else None
         gb = grad_b if need_b else None
         return grad_x, grad_y, gw, gb, None, None, None
+
+
+def _recompute_backward(ctx, grad_out):
+    """Backward of the fused forward for kernel sizes the fused backward kernels
+    do not cover (K = 5): the taps are recomputed by the 1x1 generator
+    convolution (a library GEMM, as the reference's materialised path,
+    ``triton_impl.py:340-347``), the filter's gradients come from this library's
+    ``ddpm_dyncat_bwd``, and the generator's gradients from the convolution's
+    autograd. Only (x, y, weight, bias) were saved, as in the fused path."""
+    x, y, weight, bias = ctx.saved_tensors
+    n, c, h, w = x.shape
+    ks = ctx.kernel_size
+    need_x, need_y, need_w, need_b = ctx.needs_input_grad[:4]
+    with torch.enable_grad():
+        y_ = y.detach().requires_grad_(need_y)
+        w_ = weight.detach().reshape(3 * c * ks * ks, c, 1, 1).requires_grad_(need_w)
+        b_ = bias.detach().requires_grad_(need_b)
+        taps = F.conv2d(y_, w_, b_)
+    kernels = taps.detach().reshape(n, 3, c, ks * ks, h, w)
+    grad_x, grad_k = _dyncat_backward(x, kernels, grad_out, ks, ctx.dilations, need_x,
+                                      need_y or need_w or need_b)
+    wanted = [t for t, need in ((y_, need_y), (w_, need_w), (b_, need_b)) if need]
+    grads = iter(torch.autograd.grad(taps, wanted, grad_k.reshape(taps.shape)) if wanted else ())
+    del taps, kernels
+    gy = next(grads) if need_y else None
+    gw = next(grads).view_as(weight) if need_w else None
+    gb = next(grads) if need_b else None
+    return grad_x if need_x else None, gy, gw, gb, None, None, None
 
 
 def fused_generator_dynamic_cat(x, y, weight, bias, kernel_size, dilations, *,

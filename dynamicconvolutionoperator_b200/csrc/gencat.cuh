@@ -21,6 +21,24 @@ constexpr int kMaxChannels = 64;
 // aligned with the tile origin.
 constexpr int kHaloCols = 32;
 constexpr int kMaxHalo = 8;
+// K = 5 (forward only): dilation halos up to 16, a 48-column halo tile whose
+// first column is 16 left of the tile origin.
+constexpr int kMaxHalo5 = 16;
+
+// Forward geometry per kernel size. A CTA owns `fwd_cg` output channels:
+// 16 for K <= 3; for K = 5 the group's resident weights (3 * 25 taps per
+// channel) would not fit shared memory at 16, so 8 (bf16 / fp16) or 4 (FP32,
+// hi + lo images). One branch's accumulator columns (taps x channels, tap
+// major) are padded to the MMA's N step of 16: 25 x 8 = 200 -> 208.
+__host__ __device__ constexpr int fwd_cg(int ks, bool split) {
+  return ks <= 3 ? 16 : (split ? 4 : 8);
+}
+__host__ __device__ constexpr int fwd_branch_cols(int ks, bool split) {
+  return (ks * ks * fwd_cg(ks, split) + 15) / 16 * 16;
+}
+__host__ __device__ constexpr int fwd_halo_cols(int ks) { return ks <= 3 ? kHaloCols : 48; }
+__host__ __device__ constexpr int fwd_halo_off(int ks) { return ks <= 3 ? 8 : 16; }
+__host__ __device__ constexpr int fwd_max_halo(int ks) { return ks <= 3 ? kMaxHalo : kMaxHalo5; }
 // Upper bound for any single mbarrier wait before the kernel gives up, records
 // an error and unwinds (no legitimate wait in these kernels lasts this long).
 constexpr uint64_t kWaitNs = 2000000000ull;
@@ -59,9 +77,10 @@ inline int padded_channels(int c) { return (c + 15) / 16 * 16; }
 inline int augmented_channels(int c) { return (c + 1 + 15) / 16 * 16; }
 
 // Layout of the packed generator weight (three operand images back to back).
-//   fwd : chunks q = (cg*3 + b)*K + ki, each [part][Ck/8][16*K rows][8];
-//         row kj*16 + cl <-> weight row (b*C + cg*16 + cl)*K^2 + ki*K + kj,
-//         K dimension = augmented input channels (bias at index C).
+//   fwd : per channel group cg of G = fwd_cg(K) channels, [part][Ck/8][3*BC
+//         rows][8] with BC = fwd_branch_cols(K); row b*BC + tap*G + cl <->
+//         weight row (b*C + cg*G + cl)*K^2 + tap (rows past K^2*G of a branch
+//         are zero), K dimension = augmented input channels (bias at index C).
 //   bx  : chunks q = b*K^2 + tap, each [part][Ck/8][Cp rows (c)][8].
 //   by  : groups g = (cg16, slot octet) of 128 weight rows, row j*16 + cl <->
 //         slot s = octet*8 + j = b*K^2 + tap, channel cg16*16 + cl; each group
@@ -90,7 +109,8 @@ struct PackLayout {
     L.Cq = 16;
     L.spg = 8;
     L.NG = (L.Cp / 16) * ((3 * ks * ks + 7) / 8);
-    L.fwd_rows = (long long)(L.Cp / 16) * 3 * ks * L.parts * (L.Ck / 8) * 16 * ks;
+    L.fwd_rows = (long long)(L.Cp / fwd_cg(ks, L.parts == 2)) * L.parts * (L.Ck / 8) * 3 *
+                 fwd_branch_cols(ks, L.parts == 2);
     L.bx_rows = (long long)3 * ks * ks * L.parts * (L.Ck / 8) * L.Cp;
     L.by_rows = (long long)L.NG * L.parts * 16 * L.Cp;
     return L;
@@ -333,11 +353,12 @@ __device__ __forceinline__ void stage_y_mn(const YPlan<N>& pl, const T* __restri
   }
 }
 
-// Stage the x halo of one 16-channel group: rows hs .. hs+rows-1, columns
-// ws .. ws+31 of channels c0 .. c0+15, as FP32 float4 cells holding four
-// consecutive channels: cell (q4, row, col) = xr[(q4*rows + row)*32 + col].
-// Zero outside the image and for channels >= C. Items = (q4, row, 8-column
-// block); the mapping is precomputed per thread (XPlan).
+// Stage the x halo of one group of 4*Q channels (Q = 4 unless given): rows
+// hs .. hs+rows-1, columns ws .. ws+8*CB-1 of channels c0 .. c0+4Q-1, as FP32
+// float4 cells holding four consecutive channels: cell (q4, row, col) =
+// xr[(q4*rows + row)*8*CB + col]. Zero outside the image and for channels
+// >= C. Items = (q4, row, 8-column block); the mapping is precomputed per
+// thread (XPlan).
 template <int N>
 struct XPlan {
   int q4[N];   // 4-channel group, or -1
@@ -345,27 +366,27 @@ struct XPlan {
   int blk[N];
 };
 
-template <int N>
+template <int N, int Q = 4, int CB = kHaloCols / 8>
 __device__ __forceinline__ XPlan<N> make_xplan(int rows, int tid, int nthreads) {
   XPlan<N> pl;
 #pragma unroll
   for (int u = 0; u < N; ++u) {
     const int item = tid + u * nthreads;
-    pl.blk[u] = item & 3;
-    pl.row[u] = (item >> 2) % rows;
-    pl.q4[u] = item < 16 * rows ? (item >> 2) / rows : -1;
+    pl.blk[u] = item % CB;
+    pl.row[u] = (item / CB) % rows;
+    pl.q4[u] = item < Q * CB * rows ? (item / CB) / rows : -1;
   }
   return pl;
 }
 
-template <typename T, int N>
+template <typename T, int N, int Q = 4, int CB = kHaloCols / 8>
 __device__ __forceinline__ void stage_halo(const XPlan<N>& pl, const T* __restrict__ x, float4* xr,
                                            int n, int C, int H, int W, int c0, int hs, int ws,
                                            int rows) {
   const size_t P = (size_t)H * W;
   const T* xbase = x + ((size_t)n * C + c0) * P;
-  const bool interior = hs >= 0 && hs + rows <= H && ws >= 0 && ws + kHaloCols <= W &&
-                        c0 + 16 <= C && (((size_t)W * sizeof(T)) % 16 == 0) &&
+  const bool interior = hs >= 0 && hs + rows <= H && ws >= 0 && ws + 8 * CB <= W &&
+                        c0 + 4 * Q <= C && (((size_t)W * sizeof(T)) % 16 == 0) &&
                         (P * sizeof(T)) % 16 == 0 &&
                         ((reinterpret_cast<uintptr_t>(xbase + (size_t)hs * W + ws) & 15u) == 0);
   Raw8<T> v[N][4];
@@ -393,7 +414,7 @@ __device__ __forceinline__ void stage_halo(const XPlan<N>& pl, const T* __restri
 #pragma unroll
   for (int u = 0; u < N; ++u) {
     if (pl.q4[u] < 0) continue;
-    float4* dst = xr + (pl.q4[u] * rows + pl.row[u]) * kHaloCols + pl.blk[u] * 8;
+    float4* dst = xr + (pl.q4[u] * rows + pl.row[u]) * (8 * CB) + pl.blk[u] * 8;
 #pragma unroll
     for (int i = 0; i < 8; ++i)
       dst[i] = make_float4(v[u][0].get(i), v[u][1].get(i), v[u][2].get(i), v[u][3].get(i));
@@ -477,6 +498,32 @@ __device__ __forceinline__ void store8x2_split(uint8_t* dst_hi, uint8_t* dst_lo,
       l[i] = cvt2<Op>(a, b);
     }
     *reinterpret_cast<uint4*>(dst_lo) = make_uint4(l[0], l[1], l[2], l[3]);
+  }
+}
+
+// Four channels (two f32x2 pairs) as one 8-byte cell half: the 4-channel
+// counterpart of store8x2_split.
+template <typename Op, bool kSplit>
+__device__ __forceinline__ void store4x2_split(uint8_t* dst_hi, uint8_t* dst_lo,
+                                               const unsigned long long (&v)[2]) {
+  uint32_t h[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    float a, b;
+    f2_unpack(v[i], a, b);
+    h[i] = cvt2<Op>(a, b);
+  }
+  *reinterpret_cast<uint2*>(dst_hi) = make_uint2(h[0], h[1]);
+  if constexpr (kSplit) {
+    const unsigned long long neg1 = f2_pack(-1.f, -1.f);
+    uint32_t l[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      float a, b;
+      f2_unpack(f2_fma(uncvt2<Op>(h[i]), neg1, v[i]), a, b);
+      l[i] = cvt2<Op>(a, b);
+    }
+    *reinterpret_cast<uint2*>(dst_lo) = make_uint2(l[0], l[1]);
   }
 }
 
@@ -565,6 +612,8 @@ __device__ __forceinline__ void round_taps(float (&v)[16]) {
 
 // Host helpers (gencat_common.cu).
 int check_shape(int n, int c, int h, int w, int ks, int d0, int d1, int d2, int dt);
+// check_shape plus the backward kernels' limit K <= 3.
+int check_shape_bwd(int n, int c, int h, int w, int ks, int d0, int d1, int d2, int dt);
 int status_ptr(int** out);
 int read_status(int reset, int* code);
 int num_sms();
@@ -623,8 +672,11 @@ int stage(const void* x, const void* y, void* staged, size_t staged_bytes, int n
 // ((w0 - 8) * 2, h0 - R, 4 * cg, n); y tile box {16 px, 8 rows, ygroups
 // channel groups}, coordinates ((w0 + 8) * 2, h0 + ph, 0, part * N + n).
 // False when the driver rejects one (callers then stage from x and y).
+// `halo_cols` and `quads` (4-channel cells per box) set the x box for other
+// tile geometries (the K = 5 forward: 48 columns from w0 - 16, 2 or 1 quads).
 bool encode_stage_maps(CUtensorMap* xmap, CUtensorMap* ymap, int R, int ygroups,
-                       const uint8_t* staged, const StageLayout& sl);
+                       const uint8_t* staged, const StageLayout& sl, int halo_cols = kHaloCols,
+                       int quads = 4);
 // Tensor map reading a 144-pixel row segment of the y plane ([group][pixel][8
 // channels], all `ngroups` channel groups of one part) as one 5-D box:
 // coordinates (0, first plane column / 16, plane row, 0, part * N + n).

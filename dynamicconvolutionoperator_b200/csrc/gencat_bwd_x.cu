@@ -696,7 +696,7 @@ int dispatch(int ks, const BxParams& prm, cudaStream_t st) {
 int gencat_bwd_x(const void* y, const void* staged, size_t staged_bytes, const void* wpack,
                  const void* bias, const void* gout, void* gx, int n, int c, int h, int w, int ks,
                  int d0, int d1, int d2, int dt, cudaStream_t st, int g_nhwc) {
-  int rc = gencat::check_shape(n, c, h, w, ks, d0, d1, d2, dt);
+  int rc = gencat::check_shape_bwd(n, c, h, w, ks, d0, d1, d2, dt);
   if (rc) return rc;
   DDPM_CHECK_ARG((y || staged) && wpack && bias && gout && gx, "null pointer");
   if (g_nhwc && (c != 64 || staged == nullptr))

@@ -1534,7 +1534,7 @@ int gencat_bwd_yw(const void* x, const void* y, const void* staged, size_t stage
                   const void* wpack, const void* gout, void* gy, void* gw, void* gb,
                   void* workspace, size_t ws_bytes, int n, int c, int h, int w, int ks, int d0,
                   int d1, int d2, int dt, cudaStream_t st, int g_nhwc) {
-  int rc = gencat::check_shape(n, c, h, w, ks, d0, d1, d2, dt);
+  int rc = gencat::check_shape_bwd(n, c, h, w, ks, d0, d1, d2, dt);
   if (rc) return rc;
   DDPM_CHECK_ARG(((x && y) || staged) && wpack && gout, "null pointer");
   if (g_nhwc && (c != 64 || staged == nullptr))
@@ -1800,7 +1800,7 @@ int static_scratch(void** out) {
 int gencat_bwd_yw_static(const void* x, const void* y, const void* wpack, const void* gout,
                          void* gy, void* gw, void* gb, int n, int c, int h, int w, int ks, int d0,
                          int d1, int d2, int dt, cudaStream_t st) {
-  int rc = gencat::check_shape(n, c, h, w, ks, d0, d1, d2, dt);
+  int rc = gencat::check_shape_bwd(n, c, h, w, ks, d0, d1, d2, dt);
   if (rc) return rc;
   DDPM_CHECK_ARG(x && y && wpack && gout, "null pointer");
   DDPM_CHECK_ARG((gw == nullptr) == (gb == nullptr),

@@ -31,12 +31,23 @@ int check_shape(int n, int c, int h, int w, int ks, int d0, int d1, int d2, int 
   if (c > kMaxChannels)
     return set_error(DDPM_ERR_UNSUPPORTED, "fused generator supports C <= %d (got %d)",
                      kMaxChannels, c);
-  if (ks != 1 && ks != 3)
-    return set_error(DDPM_ERR_UNSUPPORTED, "fused generator supports K in {1, 3} (got %d)", ks);
-  if ((ks / 2) * max3(d0, d1, d2) > kMaxHalo)
-    return set_error(DDPM_ERR_UNSUPPORTED, "fused generator supports dilation halos <= %d",
-                     kMaxHalo);
+  if (ks != 1 && ks != 3 && ks != 5)
+    return set_error(DDPM_ERR_UNSUPPORTED, "fused generator supports K in {1, 3, 5} (got %d)",
+                     ks);
+  if ((ks / 2) * max3(d0, d1, d2) > fwd_max_halo(ks))
+    return set_error(DDPM_ERR_UNSUPPORTED,
+                     "fused generator supports dilation halos <= %d at K = %d", fwd_max_halo(ks),
+                     ks);
   DDPM_CHECK_ARG((long long)n * h * ((w + 127) / 128) < (1LL << 31), "too many tiles");
+  return DDPM_OK;
+}
+
+int check_shape_bwd(int n, int c, int h, int w, int ks, int d0, int d1, int d2, int dt) {
+  const int rc = check_shape(n, c, h, w, ks, d0, d1, d2, dt);
+  if (rc) return rc;
+  if (ks > 3)
+    return set_error(DDPM_ERR_UNSUPPORTED, "fused generator backward supports K in {1, 3} (got %d)",
+                     ks);
   return DDPM_OK;
 }
 
@@ -112,8 +123,10 @@ __global__ void pack_kernel(const T* __restrict__ W, const T* __restrict__ bias,
     bool kdim_is_row = false;  // dY image: the K dimension runs over weight rows
     int i_col = 0;             // dY image: the weight column (input channel)
     if (idx < L.fwd_rows) {
-      // [cg][part][Ck/8][3*K^2*16][8]; row = (b*K^2 + tap)*16 + cl
-      const int nrow = 48 * KK;
+      // [cg][part][Ck/8][3*BC][8]; row = b*BC + tap*G + cl (zero past K^2*G)
+      const int G = gencat::fwd_cg(KS, L.parts == 2);
+      const int BC = gencat::fwd_branch_cols(KS, L.parts == 2);
+      const int nrow = 3 * BC;
       const long long per_cg = (long long)L.parts * (L.Ck / 8) * nrow;
       const int cg = (int)(idx / per_cg);
       int rem = (int)(idx - cg * per_cg);
@@ -121,8 +134,8 @@ __global__ void pack_kernel(const T* __restrict__ W, const T* __restrict__ bias,
       rem -= part * (L.Ck / 8) * nrow;
       const int kg = rem / nrow;
       const int row = rem - kg * nrow;
-      const int b = row / (16 * KK), tap = (row / 16) % KK, c = cg * 16 + row % 16;
-      if (c < C) m = (long long)(b * C + c) * KK + tap;
+      const int b = row / BC, tap = (row % BC) / G, c = cg * G + row % G;
+      if (c < C && tap < KK) m = (long long)(b * C + c) * KK + tap;
       k0 = kg * 8;
     } else if (idx < L.fwd_rows + L.bx_rows) {
       // [q][part][Ck/8][Cp][8]; q = b*K^2 + tap; row = c

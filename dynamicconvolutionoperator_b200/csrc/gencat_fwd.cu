@@ -77,17 +77,22 @@ template <typename T, int KS, bool kStaged = false>
 struct FwdCfg {
   static constexpr bool kSplit = IoTraits<T>::kSplit;
   static constexpr int kParts = kSplit ? 2 : 1;
+  static constexpr int kCG = fwd_cg(KS, kSplit);              // output channels of a CTA
+  static constexpr int kQ4 = kCG / 4;                         // 4-channel x cells per pixel
+  static constexpr int kBrN = fwd_branch_cols(KS, kSplit);    // accumulator columns per branch
   static constexpr int kBr = KS == 1 ? 3 : 1;                 // branches per slot
   static constexpr int kSlots = 3 / kBr;                      // slots per tile
-  static constexpr int kN = kBr * KS * KS * 16;               // accumulator columns per slot
-  static constexpr int kRows = 3 * KS * KS * 16;              // weight rows of a channel group
+  static constexpr int kN = kBr * kBrN;                       // accumulator columns per slot
+  static constexpr int kRows = 3 * kBrN;                      // weight rows of a channel group
   static constexpr int kNumBuf = (512 / kN) > 8 ? 8 : (512 / kN);
   // Epilogue warpgroups: slot s belongs to warpgroup s % kEpiWG. With staged
   // operands each producer role is one warp, which leaves the threads for a
   // third warpgroup: the epilogue (the bound of this kernel) then drains three
-  // slots at once. Each warpgroup owns kNumBuf / kEpiWG TMEM buffers: every
-  // buffer has a single consumer that sees all of its phases in order.
-  static constexpr int kEpiWG = kStaged ? 3 : 2;
+  // slots at once (where TMEM holds a buffer for each: not at K = 5 bf16, whose
+  // 208-column slots fit twice). Each warpgroup owns kNumBuf / kEpiWG TMEM
+  // buffers: every buffer has a single consumer that sees all of its phases in
+  // order.
+  static constexpr int kEpiWG = (kStaged && kNumBuf >= 3) ? 3 : 2;
   static constexpr int kBufPerWG = kNumBuf / kEpiWG;
   static_assert(kBufPerWG >= 1, "a TMEM slot per epilogue warpgroup must fit");
   static constexpr int kYBufs = kSplit ? 1 : 2;               // smem budget (see layout)
@@ -95,10 +100,15 @@ struct FwdCfg {
   static constexpr int kProducers = kStaged ? 32 : 128;       // threads per producer role
   static constexpr int kFirstEpiWarp = 2 + 2 * (kProducers / 32);
   static constexpr int kThreads = 32 * (kFirstEpiWarp + 4 * kEpiWG);
+  // x halo tile: kHaloW columns from w0 - kHaloOff, up to kMaxR rows above and below
+  static constexpr int kHaloW = fwd_halo_cols(KS);
+  static constexpr int kHaloOff = fwd_halo_off(KS);
+  static constexpr int kMaxR = fwd_max_halo(KS);
   // loads per producer thread and tile (whole tile in one batch)
   // y items per thread: 16 pixel groups x Ck (<= 80 for bf16/fp16, = Cp <= 64 for fp32)
   static constexpr int kYItems = (16 * (kSplit ? 64 : 80) + kProducers - 1) / kProducers;
-  static constexpr int kXItems = (16 * (kTileH + 2 * kMaxHalo) + kProducers - 1) / kProducers;
+  static constexpr int kXItems =
+      (kQ4 * (kHaloW / 8) * (kTileH + 2 * kMaxR) + kProducers - 1) / kProducers;
 };
 
 struct FwdSmem {
@@ -110,18 +120,20 @@ struct FwdSmem {
 // Resident weights of one channel group + y tile(s) + `nxb` (2, or 1 where two
 // do not fit: FP32 with halos >= 7) x-halo buffers.
 // C=64, K=3, halo 5: bf16 69 + 2x20 + 2x36 KB = 181 KB; fp32 108 + 32 + 72 KB = 214 KB.
+// C=64, K=5, halo 10 (8 / 4 channels): bf16 97.5 + 2x20 + 2x42 KB = 221.5 KB;
+// fp32 84 + 32 + 2x21 KB + 1.2 KB bias = 159 KB.
 template <typename T, int KS>
 __host__ __device__ inline FwdSmem fwd_smem_layout(int Ck, int R, int nxb) {
   using Cfg = FwdCfg<T, KS>;
   FwdSmem L;
   L.y_bytes = (uint32_t)Cfg::kParts * kTileM * Ck * 2;
   L.w_bytes = (uint32_t)Cfg::kParts * Cfg::kRows * Ck * 2;  // the group's whole image
-  L.xr_bytes = (uint32_t)16 * (kTileH + 2 * R) * kHaloCols * 4;
+  L.xr_bytes = (uint32_t)Cfg::kCG * (kTileH + 2 * R) * Cfg::kHaloW * 4;
   L.y = 0;
   L.w = L.y + Cfg::kYBufs * L.y_bytes;
   L.xr = L.w + L.w_bytes;
   L.bias = L.xr + nxb * L.xr_bytes;
-  L.bars = L.bias + (Cfg::kBiasInGemm ? 0u : (uint32_t)(3 * 16 * KS * KS * 4));
+  L.bars = L.bias + (Cfg::kBiasInGemm ? 0u : (uint32_t)(3 * Cfg::kCG * KS * KS * 4));
   L.total = L.bars + 8 * (9 + 2 * Cfg::kNumBuf);
   return L;
 }
@@ -151,6 +163,35 @@ __device__ __forceinline__ void store_plane_cell(const FwdParams& p, int n, int 
                                                  const unsigned long long (&pr)[4]) {
   const size_t off = ((((size_t)n * p.pl_G + g) * p.pl_Hp + (h + 1)) * p.pl_Wp + (w + 8)) * 16;
   store8x2_split<Op, kSplit>(p.planes + off, p.planes + p.pl_part + off, pr);
+}
+// Half `half` (channels 4*half .. +3) of that cell.
+template <typename Op, bool kSplit>
+__device__ __forceinline__ void store_plane_half(const FwdParams& p, int n, int g, int half, int h,
+                                                 int w, const unsigned long long (&pr)[2]) {
+  const size_t off =
+      ((((size_t)n * p.pl_G + g) * p.pl_Hp + (h + 1)) * p.pl_Wp + (w + 8)) * 16 + half * 8;
+  store4x2_split<Op, kSplit>(p.planes + off, p.planes + p.pl_part + off, pr);
+}
+// The group's kCG channels (pairs pr[0 .. kCG/2)) of pixel (h, w) starting at
+// cat channel c0 (a multiple of kCG): whole cells, or one half cell at kCG = 4.
+// `cvalid`: channels of the group below C (cells past it are not written;
+// C % 8 == 0, so a valid cell is whole).
+template <typename Op, bool kSplit, int kCG>
+__device__ __forceinline__ void store_plane_group(const FwdParams& p, int n, int c0, int cvalid,
+                                                  int h, int w, const unsigned long long* pr) {
+  if constexpr (kCG == 4) {
+    if (cvalid < 4) return;
+    const unsigned long long q[2] = {pr[0], pr[1]};
+    store_plane_half<Op, kSplit>(p, n, c0 / 8, (c0 / 4) & 1, h, w, q);
+  } else {
+#pragma unroll
+    for (int k8 = 0; k8 < kCG / 8; ++k8) {
+      if (8 * k8 + 8 > cvalid) break;
+      const unsigned long long q[4] = {pr[4 * k8], pr[4 * k8 + 1], pr[4 * k8 + 2],
+                                       pr[4 * k8 + 3]};
+      store_plane_cell<Op, kSplit>(p, n, c0 / 8 + k8, h, w, q);
+    }
+  }
 }
 
 // Tensor maps of the staged operands (separate grid-constant parameter).
@@ -185,8 +226,11 @@ gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
   uint64_t* w_full = bars + 8;       // [1]
   uint64_t* t_full = bars + 9;       // [NB]
   uint64_t* t_empty = t_full + NB;   // [NB]
+  constexpr int kCG = Cfg::kCG;
+  constexpr int kQ4 = Cfg::kQ4;
+  constexpr int kHW = Cfg::kHaloW;
   const int xr_rows = kTileH + 2 * R;
-  const int xr_plane = xr_rows * kHaloCols;  // 16-byte cells per 4-channel group
+  const int xr_plane = xr_rows * kHW;  // 16-byte cells per 4-channel group
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -217,9 +261,9 @@ gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
   if constexpr (!Cfg::kBiasInGemm) {
     float* bias_s = reinterpret_cast<float*>(smem + L.bias);
     const T* bias = static_cast<const T*>(p.bias);
-    for (int i = threadIdx.x; i < 3 * 16 * KK; i += blockDim.x) {
-      const int b = i / (16 * KK), cl = (i / KK) % 16, tap = i % KK;
-      const int c = cg * 16 + cl;
+    for (int i = threadIdx.x; i < 3 * kCG * KK; i += blockDim.x) {
+      const int b = i / (kCG * KK), cl = (i / KK) % kCG, tap = i % KK;
+      const int c = cg * kCG + cl;
       bias_s[i] = c < C ? to_f32<T>(bias[(b * C + c) * KK + tap]) : 0.f;
     }
   }
@@ -278,7 +322,7 @@ gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
             goto done;
           }
           tc::tc_fence_after();
-          // rows of branch q (K = 3) or of all branches (K = 1): (q * kN) * 16 bytes in
+          // rows of branch q (K = 3, 5) or of all branches (K = 1): (q * kN) * 16 bytes in
           const uint64_t bd = w_desc + (uint64_t)(q * kN);
           const uint32_t d = tmem_base + j * kN;
           // A plain runtime loop: an MMA under a per-step condition inside an
@@ -341,7 +385,8 @@ gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
   } else if (warp < Cfg::kFirstEpiWarp) {
     // ---- x-halo producers ----------------------------------------------------
     const int pt = threadIdx.x - 64 - Cfg::kProducers;
-    const XPlan<Cfg::kXItems> plan = make_xplan<Cfg::kXItems>(xr_rows, pt, Cfg::kProducers);
+    const XPlan<Cfg::kXItems> plan =
+        make_xplan<Cfg::kXItems, kQ4, kHW / 8>(xr_rows, pt, Cfg::kProducers);
     uint32_t it = 0;
     for (int tile = first_tile; tile < p.num_tiles; tile += tile_step, ++it) {
       const int xb = it & nx_sh;
@@ -355,13 +400,15 @@ gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
       if constexpr (kStaged) {
         if (pt == 0) {
           tc::mbar_arrive_expect_tx(&x_full[xb], L.xr_bytes);
-          tc::tma_load_4d(xr, &maps.xmap, (w0 - 8) * 2, h0 - R, cg * 4, n, &x_full[xb]);
+          tc::tma_load_4d(xr, &maps.xmap, (w0 - Cfg::kHaloOff) * 2, h0 - R, cg * kQ4, n,
+                          &x_full[xb]);
         } else {
           tc::mbar_arrive(&x_full[xb]);
         }
       } else {
-        stage_halo<T, Cfg::kXItems>(plan, static_cast<const T*>(p.x), xr, n, C, H, W, cg * 16,
-                                    h0 - R, w0 - 8, xr_rows);
+        stage_halo<T, Cfg::kXItems, kQ4, kHW / 8>(plan, static_cast<const T*>(p.x), xr, n, C, H,
+                                                  W, cg * kCG, h0 - R, w0 - Cfg::kHaloOff,
+                                                  xr_rows);
         tc::mbar_arrive(&x_full[xb]);
       }
     }
@@ -390,7 +437,7 @@ gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
       }
       const float4* xr = reinterpret_cast<const float4*>(smem + L.xr + xb * L.xr_bytes);
       // this pixel's cell in the halo tile; a tap shifts it by (dy, dx)
-      const float4* xc = xr + (mr + R) * kHaloCols + (mc + 8);
+      const float4* xc = xr + (mr + R) * kHW + (mc + Cfg::kHaloOff);
       bool failed = false;
       for (int q = 0; q < Cfg::kSlots && !failed; ++q, ++tq) {
         if (tq % Cfg::kEpiWG != (uint32_t)wg) continue;  // another warpgroup's slot
@@ -407,16 +454,16 @@ gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
         for (int bb = 0; bb < Cfg::kBr; ++bb) {
           const int b = q * Cfg::kBr + bb;
           const int d = p.d[b];
-          unsigned long long acc[8];
+          unsigned long long acc[kCG / 2];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) acc[i] = 0ull;
+          for (int i = 0; i < kCG / 2; ++i) acc[i] = 0ull;
 #pragma unroll
           for (int ki = 0; ki < KS; ++ki) {
-            const uint32_t taddr = slot_addr + (bb * KK + ki * KS) * 16;
-            const float4* xrow = xc + (ki - r) * d * kHaloCols;
-            float dv[KS][16];
+            const uint32_t taddr = slot_addr + bb * Cfg::kBrN + ki * KS * kCG;
+            const float4* xrow = xc + (ki - r) * d * kHW;
+            float dv[KS][kCG];
 #pragma unroll
-            for (int kj = 0; kj < KS; ++kj) tc::tmem_ld16(taddr + kj * 16, dv[kj]);
+            for (int kj = 0; kj < KS; ++kj) tc::tmem_ld_cols<kCG>(taddr + kj * kCG, dv[kj]);
             tc::tmem_ld_wait();
             if (bb == Cfg::kBr - 1 && ki == KS - 1) {
               tc::tc_fence_before();
@@ -426,12 +473,12 @@ gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
             for (int kj = 0; kj < KS; ++kj) {
               const float4* cell = xrow + (kj - r) * d;
 #pragma unroll
-              for (int q4 = 0; q4 < 4; ++q4) {
+              for (int q4 = 0; q4 < kQ4; ++q4) {
                 const float4 v = cell[q4 * xr_plane];
                 float g0 = dv[kj][q4 * 4 + 0], g1 = dv[kj][q4 * 4 + 1];
                 float g2 = dv[kj][q4 * 4 + 2], g3 = dv[kj][q4 * 4 + 3];
                 if constexpr (!Cfg::kBiasInGemm) {
-                  const float* bs = bias_s + (b * 16 + q4 * 4) * KK + ki * KS + kj;
+                  const float* bs = bias_s + (b * kCG + q4 * 4) * KK + ki * KS + kj;
                   g0 += bs[0];
                   g1 += bs[KK];
                   g2 += bs[2 * KK];
@@ -444,50 +491,37 @@ gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
           }
           if (px_ok) {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
+            for (int i = 0; i < kCG / 2; ++i) {
               float a0, a1;
               f2_unpack(acc[i], a0, a1);
-              const int c = cg * 16 + 2 * i;
+              const int c = cg * kCG + 2 * i;
               if (c < C) on[(size_t)((b + 1) * C + c) * P + pix] = from_f32<T>(a0);
               if (c + 1 < C) on[(size_t)((b + 1) * C + c + 1) * P + pix] = from_f32<T>(a1);
             }
-            if (p.planes != nullptr) {
-              // cat channels (b+1)C + cg*16 .. : whole 8-channel groups (C % 8 == 0)
-#pragma unroll
-              for (int k8 = 0; k8 < 2; ++k8) {
-                if (cg * 16 + 8 * k8 + 8 > C) break;
-                const unsigned long long pr[4] = {acc[4 * k8], acc[4 * k8 + 1], acc[4 * k8 + 2],
-                                                  acc[4 * k8 + 3]};
-                store_plane_cell<Op, Cfg::kSplit>(p, n, ((b + 1) * C + cg * 16) / 8 + k8, h, w,
-                                                  pr);
-              }
-            }
+            if (p.planes != nullptr)  // cat channels (b+1)C + cg*kCG .. (C % 8 == 0)
+              store_plane_group<Op, Cfg::kSplit, kCG>(p, n, (b + 1) * C + cg * kCG,
+                                                      C - cg * kCG, h, w, acc);
           }
         }
       }
       if (failed) break;
-      // passthrough out[:, cg*16 : cg*16+16] = x, written from the halo tile
+      // passthrough out[:, cg*kCG : (cg+1)*kCG] = x, written from the halo tile
       if (px_ok && (it % Cfg::kEpiWG) == (uint32_t)wg) {
+        unsigned long long xp[kCG / 2];
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
+        for (int q4 = 0; q4 < kQ4; ++q4) {
           const float4 v = xc[q4 * xr_plane];
           const float e[4] = {v.x, v.y, v.z, v.w};
+          xp[2 * q4] = f2_pack(v.x, v.y);
+          xp[2 * q4 + 1] = f2_pack(v.z, v.w);
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            const int c = cg * 16 + q4 * 4 + k;
+            const int c = cg * kCG + q4 * 4 + k;
             if (c < C) on[(size_t)c * P + pix] = from_f32<T>(e[k]);
           }
         }
-        if (p.planes != nullptr) {
-#pragma unroll
-          for (int k8 = 0; k8 < 2; ++k8) {
-            if (cg * 16 + 8 * k8 + 8 > C) break;
-            const float4 v0 = xc[(2 * k8) * xr_plane], v1 = xc[(2 * k8 + 1) * xr_plane];
-            const unsigned long long pr[4] = {f2_pack(v0.x, v0.y), f2_pack(v0.z, v0.w),
-                                              f2_pack(v1.x, v1.y), f2_pack(v1.z, v1.w)};
-            store_plane_cell<Op, Cfg::kSplit>(p, n, 2 * cg + k8, h, w, pr);
-          }
-        }
+        if (p.planes != nullptr)
+          store_plane_group<Op, Cfg::kSplit, kCG>(p, n, cg * kCG, C - cg * kCG, h, w, xp);
       }
       tc::mbar_arrive(&x_empty[xb]);
     }
@@ -531,6 +565,7 @@ int dispatch(int ks, const FwdParams& prm, const FwdMaps& maps, bool staged, cud
   switch (ks) {
     case 1: return launch<T, 1>(prm, maps, staged, st);
     case 3: return launch<T, 3>(prm, maps, staged, st);
+    case 5: return launch<T, 5>(prm, maps, staged, st);
   }
   return set_error(DDPM_ERR_UNSUPPORTED, "fused generator: kernel_size %d not supported", ks);
 }
@@ -611,7 +646,8 @@ int gencat_fwd_ex(const void* x, const void* y, const void* staged, size_t stage
   const gencat::PackLayout pl = gencat::PackLayout::make(c, ks, dt);
   prm.Cp = pl.Cp;
   prm.Ck = pl.Ck;
-  prm.ncg = pl.Cp / 16;
+  const int cgw = gencat::fwd_cg(ks, dt == DDPM_F32);
+  prm.ncg = pl.Cp / cgw;
   prm.R = (ks / 2) * max3(d0, d1, d2);
   prm.d[0] = d0;
   prm.d[1] = d1;
@@ -631,7 +667,8 @@ int gencat_fwd_ex(const void* x, const void* y, const void* staged, size_t stage
     DDPM_CHECK_ARG((reinterpret_cast<uintptr_t>(staged) & 255u) == 0,
                    "staged operands must be 256-byte aligned");
     use_staged = gencat::encode_stage_maps(&maps.xmap, &maps.ymap, prm.R, pl.Ck / 8,
-                                           static_cast<const uint8_t*>(staged), sl);
+                                           static_cast<const uint8_t*>(staged), sl,
+                                           gencat::fwd_halo_cols(ks), cgw / 4);
     maps.ph = sl.ph;
   }
   DDPM_CHECK_ARG(use_staged || (x && y), "tensor maps unavailable: x and y are needed");

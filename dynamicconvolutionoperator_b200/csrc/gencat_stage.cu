@@ -195,11 +195,12 @@ int stage(const void* x, const void* y, void* staged, size_t staged_bytes, int n
 }
 
 bool encode_stage_maps(CUtensorMap* xmap, CUtensorMap* ymap, int R, int ygroups,
-                       const uint8_t* staged, const StageLayout& sl) {
+                       const uint8_t* staged, const StageLayout& sl, int halo_cols, int quads) {
   const uint64_t xd[4] = {(uint64_t)sl.W * 2, (uint64_t)sl.H, (uint64_t)sl.Cq, (uint64_t)sl.N};
   const uint64_t xs[3] = {(uint64_t)sl.W * 16, (uint64_t)sl.H * sl.W * 16,
                           (uint64_t)sl.Cq * sl.H * sl.W * 16};
-  const uint32_t xb[4] = {2 * kHaloCols, (uint32_t)(kTileH + 2 * R), 4, 1};
+  const uint32_t xb[4] = {(uint32_t)(2 * halo_cols), (uint32_t)(kTileH + 2 * R),
+                          (uint32_t)quads, 1};
   const uint64_t yd[4] = {(uint64_t)sl.Wp * 2, (uint64_t)sl.Hp, (uint64_t)sl.G,
                           (uint64_t)sl.parts * sl.N};
   const uint64_t ys[3] = {(uint64_t)sl.Wp * 16, (uint64_t)sl.Hp * sl.Wp * 16,

@@ -106,7 +106,9 @@ DDPM_API int ddpm_dyncat_bwd(const void* x, int x_dtype,
  * MMAs (fp32 weights are split into bf16 hi + lo parts). Callers pack once per
  * weight version into a buffer of ddpm_gencat_pack_bytes() bytes (16-byte
  * aligned) and pass it to every fused launch that uses that weight.
- * Limits of this build: C <= 64, K in {1, 3}; other sizes return
+ * Limits of this build: C <= 64; K in {1, 3} with dilation halos
+ * (K/2)*max(d) <= 8, or K = 5 with halos <= 16 (forward entry points only:
+ * the fused backward entry points cover K in {1, 3}); other sizes return
  * DDPM_ERR_UNSUPPORTED (callers then take the materialised path).
  */
 DDPM_API size_t ddpm_gencat_pack_bytes(int c, int ksize, int dtype);
@@ -321,10 +323,10 @@ DDPM_API int ddpm_fuseconv_bwd_nhwc(const void* x, const void* grad_out, const v
 /*
  * ddpm_gencat_bwd_x_staged / ddpm_gencat_bwd_yw_staged reading grad_out
  * channel-last ([N][H][W][4C], as ddpm_fuseconv_bwd_nhwc writes it; no
- * reference counterpart). bf16 / fp16 with C == 64 (DDPM_ERR_UNSUPPORTED
- * otherwise); same results as the NCHW entry points (dX bit for bit, dY and
- * dW/db to the FP32 summation order of dY's reductions). The kernels load a
- * pixel's 16 channels as two 16-byte vectors instead of 16 strided elements.
+ * reference counterpart). C == 64 (DDPM_ERR_UNSUPPORTED otherwise); same
+ * results as the NCHW entry points (dX bit for bit, dY and dW/db to the FP32
+ * summation order of dY's reductions). The kernels load a pixel's 16 channels
+ * as 16-byte vectors instead of 16 strided elements.
  */
 DDPM_API int ddpm_gencat_bwd_x_staged_nhwc(const void* staged_y, size_t staged_bytes,
                                            const void* packed, const void* bias,

@@ -108,14 +108,16 @@ def test_training_crossover_follows_the_b200_measurement():
 
 
 def test_fused_kernel_limits():
-    """C <= 64, K in {1, 3}, halo (K/2) * max(dilation) <= 8; the recompute
-    backward covers the same K (reference ``triton_impl.py:320``: K <= 3)."""
+    """Forward: C <= 64, K in {1, 3} with halo (K/2) * max(dilation) <= 8 or
+    K = 5 with halo <= 16; the recompute backward kernels cover K <= 3
+    (reference ``triton_impl.py:320``)."""
     from dynamicconvolutionoperator_b200 import _kernels
 
     ok = _kernels.fused_generator_supported
     assert ok(64, 3, torch.float32) and ok(1, 1, torch.bfloat16, (1, 1, 1))
     assert not ok(65, 3, torch.float32)
-    assert not ok(64, 5, torch.float32)
+    assert ok(64, 5, torch.float32) and ok(64, 5, torch.bfloat16, (1, 8, 4))
+    assert not ok(64, 5, torch.float32, (1, 9, 4)) and not ok(64, 7, torch.bfloat16)
     assert ok(64, 3, torch.float16, (1, 3, 8)) and not ok(64, 3, torch.float16, (1, 3, 9))
     assert not ok(64, 3, torch.float64)
     assert [k for k in (1, 3, 5, 7) if _kernels.fused_training_supported(k)] == [1, 3]

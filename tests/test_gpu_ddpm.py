@@ -243,10 +243,10 @@ def test_autocast_runs_the_native_kernels(ac_dtype, fused):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 def test_training_step_hands_the_generator_a_channel_last_gradient(dtype, monkeypatch):
-    """For 16-bit data at C=64 the fuse conv writes the gradient of the
-    generator output channel-last and the generator backward reads it so
-    (the *_nhwc entry points); FP32 keeps NCHW. Both within the oracle's
-    tolerance (the cfg4 parity test covers the values at 256^2)."""
+    """At C=64 the fuse conv writes the gradient of the generator output
+    channel-last and the generator backward reads it so (the *_nhwc entry
+    points), within the oracle's tolerance (the cfg4 parity test covers the
+    values at 256^2)."""
     from dynamicconvolutionoperator_b200 import _lib
 
     calls = []
@@ -261,8 +261,5 @@ def test_training_step_hands_the_generator_a_channel_last_gradient(dtype, monkey
                                fused_generator_training=True)
     _assert_ok(stats, fails)
     nhwc = {n for n in calls if n.endswith("_nhwc")}
-    if dtype == torch.bfloat16:
-        assert nhwc == {"ddpm_fuseconv_bwd_nhwc", "ddpm_gencat_bwd_x_staged_nhwc",
-                        "ddpm_gencat_bwd_yw_staged_nhwc"}, calls
-    else:
-        assert not nhwc, calls
+    assert nhwc == {"ddpm_fuseconv_bwd_nhwc", "ddpm_gencat_bwd_x_staged_nhwc",
+                    "ddpm_gencat_bwd_yw_staged_nhwc"}, calls

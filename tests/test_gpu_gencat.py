@@ -36,7 +36,7 @@ def _case(shape, ks, dtype, seed=0):
 
 
 @pytest.mark.parametrize("shape", SHAPES)
-@pytest.mark.parametrize("ks", [1, 3])
+@pytest.mark.parametrize("ks", [1, 3, 5])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 def test_gencat_forward(shape, ks, dtype):
     from dynamicconvolutionoperator_b200 import fused_generator_dynamic_cat
@@ -53,7 +53,7 @@ def test_gencat_forward(shape, ks, dtype):
 
 
 @pytest.mark.parametrize("shape", [(2, 24, 15, 17), (1, 64, 48, 48), (3, 40, 33, 30)])
-@pytest.mark.parametrize("ks", [1, 3])
+@pytest.mark.parametrize("ks", [1, 3, 5])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_gencat_forward_unstaged_abi(shape, ks, dtype):
     """ddpm_gencat_fwd staging tiles from x and y itself (the public module
@@ -108,8 +108,8 @@ def test_gencat_multiple_tiles_per_cta():
 
 
 @pytest.mark.parametrize("shape", [(2, 24, 15, 17), (1, 64, 48, 48), (3, 40, 33, 30),
-                                   (1, 8, 1, 1), (1, 16, 9, 130)])
-@pytest.mark.parametrize("ks", [1, 3])
+                                   (1, 8, 1, 1), (1, 16, 9, 130), (1, 32, 19, 21)])
+@pytest.mark.parametrize("ks", [1, 3, 5])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 def test_gencat_forward_writes_fuse_planes(shape, ks, dtype):
     """ddpm_gencat_fwd_staged_planes: the same output as ddpm_gencat_fwd_staged,
@@ -142,6 +142,26 @@ def test_gencat_forward_writes_fuse_planes(shape, ks, dtype):
     torch.cuda.synchronize()
     torch.testing.assert_close(out, ref, rtol=0, atol=0, equal_nan=True)
     assert torch.equal(planes, gold)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_gencat_k5_halo_limits_and_tiles(dtype):
+    """K = 5: the largest halo the forward covers ((K/2) * 8 = 16, dilations
+    (1, 8, 4)) against the oracle on a shape with more tiles than SMs, and a
+    halo of 18 rejected as unsupported before anything is launched."""
+    from dynamicconvolutionoperator_b200 import _kernels, _lib, fused_generator_dynamic_cat
+
+    x, y, wt, b = _case((2, 64, 40, 72), 5, dtype, seed=4)
+    dil = (1, 8, 4)
+    with torch.no_grad():
+        out = fused_generator_dynamic_cat(x.cuda(), y.cuda(), wt.cuda(), b.cuda(), 5, dil)
+    gold = orc.fused_generator_cat(x, y, wt, b, 5, dil, quantize=True)
+    rtol, atol = TOL[dtype]
+    torch.testing.assert_close(out.float().cpu(), gold.float(), rtol=rtol, atol=atol)
+    assert not _kernels.fused_generator_supported(64, 5, dtype, (1, 9, 4))
+    rc = _lib.load().ddpm_gencat_fwd_staged(1, 1, 1, 1, 1, 1, 64, 8, 8, 5, 1, 9, 4,
+                                            _lib.dtype_code(dtype), None)
+    assert rc == -2
 
 
 def test_gencat_forward_fuse_planes_rejects_ragged_channels():

@@ -208,11 +208,12 @@ def test_max_halo_and_ragged_gradient_tiles(shape, dtype):
 
 @pytest.mark.parametrize("shape", [(2, 64, 15, 40), (1, 64, 33, 136)])
 @pytest.mark.parametrize("ks", [1, 3])
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 def test_channel_last_grad_out_matches_nchw(shape, ks, dtype):
     """The *_staged_nhwc backward entry points read grad_out channel-last
     ([N][H][W][4C], C = 64) and give dX bit for bit and dY, dW, db to FP32
-    summation order of the NCHW entry points."""
+    summation order of the NCHW entry points (FP32 included: two 128-byte
+    channel boxes per dX unit, vector loads in the dY+dW builders)."""
     from dynamicconvolutionoperator_b200 import _kernels, _lib
 
     x, y, wt, b = _case(shape, ks, dtype)
@@ -250,14 +251,14 @@ def test_channel_last_grad_out_matches_nchw(shape, ks, dtype):
 
 
 def test_channel_last_grad_out_rejected_outside_its_limits():
-    """fp32, C != 64 and the unstaged path return DDPM_ERR_UNSUPPORTED."""
+    """C != 64 returns DDPM_ERR_UNSUPPORTED before anything is launched."""
     from dynamicconvolutionoperator_b200 import _lib
 
     lib = _lib.load()
     t = torch.zeros(16, dtype=torch.uint8, device="cuda")
     p = t.data_ptr()
     stream = _lib.stream_handle(t.device)
-    for c, code in ((64, 0), (32, 1)):
+    for c, code in ((32, 0), (48, 1)):
         rc = lib.ddpm_gencat_bwd_x_staged_nhwc(p, 16, p, p, p, p, 1, c, 8, 16, 3, 1, 3, 5, code,
                                                stream)
         assert rc == -2, (c, code, rc)
