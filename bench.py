@@ -835,53 +835,53 @@ def inference_lines(args, device):
 
 
 # --------------------------------------------------------------- crossover --
-CROSSOVER_SIZES = (32, 48, 64, 96, 128, 192, 256)
+CROSSOVER_SIZES = {3: (32, 48, 64, 96, 128, 192, 256), 5: (32, 64, 128, 256)}
 
 
 def crossover(args, device):
-    """Fused vs materialised training step (B=1, C=64, K=3) at square image
-    sizes, both dtypes: graph-replayed device time, L2 flushed between steps.
-    The measurement behind the module's automatic training-path choice."""
+    """Fused vs materialised training step (B=1, C=64, K=3 and K=5) at square
+    image sizes, both dtypes: graph-replayed device time, L2 flushed between
+    steps. The measurement behind the module's automatic training-path choice."""
     from dynamicconvolutionoperator_b200 import DDPM
 
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
     stream = torch.cuda.current_stream(device)
     rows = []
-    for dname in ("fp32", "bf16"):
+    for ks, dname, hw in ((k, d, s) for k in CROSSOVER_SIZES for d in ("fp32", "bf16")
+                          for s in CROSSOVER_SIZES[k]):
         dtype = DTYPES[dname]
-        for hw in CROSSOVER_SIZES:
-            row = {"dtype": dname, "hw": hw, "tokens": hw * hw}
-            for path in ("fused", "materialised"):
-                torch.manual_seed(0)
-                model = DDPM(C, K, fused_generator_training=path == "fused")
-                model = model.to(device=device, dtype=dtype)
-                gen = torch.Generator().manual_seed(7)
-                x, y, g = (torch.randn((1, C, hw, hw), generator=gen).to(dtype).to(device)
-                           for _ in range(3))
+        row = {"ks": ks, "dtype": dname, "hw": hw, "tokens": hw * hw}
+        for path in ("fused", "materialised"):
+            torch.manual_seed(0)
+            model = DDPM(C, ks, fused_generator_training=path == "fused")
+            model = model.to(device=device, dtype=dtype)
+            gen = torch.Generator().manual_seed(7)
+            x, y, g = (torch.randn((1, C, hw, hw), generator=gen).to(dtype).to(device)
+                       for _ in range(3))
 
-                def zero():
-                    for p in model.parameters():
-                        p.grad = None
+            def zero():
+                for p in model.parameters():
+                    p.grad = None
 
-                side = torch.cuda.Stream(device)
-                side.wait_stream(stream)
-                with torch.cuda.stream(side):
-                    for _ in range(3):
-                        zero()
-                        step_fn(model, x, y, g, None)
-                stream.wait_stream(side)
-                torch.cuda.synchronize()
-                zero()
-                graph = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(graph):
+            side = torch.cuda.Stream(device)
+            side.wait_stream(stream)
+            with torch.cuda.stream(side):
+                for _ in range(3):
+                    zero()
                     step_fn(model, x, y, g, None)
-                for _ in range(args.warmup):
-                    graph.replay()
-                ts = time_steps(graph.replay, max(args.steps, 10), flush, stream)
-                row[path + "_ms"] = round(statistics.median(ts), 4)
-                del graph, model
-            row["fused_faster"] = row["fused_ms"] < row["materialised_ms"]
-            rows.append(row)
+            stream.wait_stream(side)
+            torch.cuda.synchronize()
+            zero()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                step_fn(model, x, y, g, None)
+            for _ in range(args.warmup):
+                graph.replay()
+            ts = time_steps(graph.replay, max(args.steps, 10), flush, stream)
+            row[path + "_ms"] = round(statistics.median(ts), 4)
+            del graph, model
+        row["fused_faster"] = row["fused_ms"] < row["materialised_ms"]
+        rows.append(row)
     return rows
 
 

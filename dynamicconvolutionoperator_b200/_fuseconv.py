@@ -100,7 +100,7 @@ class _FuseConv(torch.autograd.Function):
         out = torch.empty((n, cout, h, w), dtype=x.dtype, device=x.device)
         b = bias.contiguous() if bias is not None else None
         # the producer's own planes of x when it wrote them, else one staging pass
-        planes, nbytes = planes_in if planes_in is not None else _stage_planes(x)
+        planes, nbytes = planes_in[:2] if planes_in is not None else _stage_planes(x)
         _lib.call("ddpm_fuseconv_fwd_staged", planes.data_ptr(), nbytes, packed.data_ptr(),
                   b.data_ptr() if b is not None else None, out.data_ptr(),
                   n, cin, cout, h, w, _lib.dtype_code(x.dtype), _lib.stream_handle(x.device))
@@ -109,8 +109,9 @@ class _FuseConv(torch.autograd.Function):
         ctx.packed = packed
         ctx.has_bias = bias is not None
         # x came from the fused generator forward (its planes): the gradient of x
-        # goes to that generator's backward, which reads it channel-last
-        ctx.grad_nhwc = planes_in is not None and nhwc_grad_ok(x)
+        # goes to that generator's backward, which reads it channel-last where
+        # its producer said so (the fully fused backward kernels, K <= 3)
+        ctx.grad_nhwc = planes_in is not None and planes_in[2] and nhwc_grad_ok(x)
         return out
 
     @staticmethod
@@ -168,7 +169,7 @@ def fuse_conv(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None) 
     if held is not None:
         delattr(x, FUSE_PLANES_ATTR)
         if held[2] == x._version and x.is_contiguous():
-            planes_in = (held[0], held[1])
+            planes_in = (held[0], held[1], held[3])
     return _FuseConv.apply(x, weight, bias, planes_in)
 
 

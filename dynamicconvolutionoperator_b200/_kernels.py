@@ -11,7 +11,6 @@ Triton and no CPU or eager-PyTorch fallback: non-CUDA tensors raise.
 from __future__ import annotations
 
 import torch
-import torch.nn.functional as F
 
 from . import _lib
 from ._gradbuf import grad_buffer, grads_written
@@ -107,8 +106,10 @@ def fused_dynamic_cat(x, kernels, kernel_size, dilations):
 # Limits of the fused generator kernels of this build (tcgen05 tiles hold the
 # padded channel count in shared memory and TMEM).
 FUSED_MAX_CHANNELS = 64
-# Kernel sizes of the fused forward, and of the flash-style recompute backward
-# kernels (K <= 3, like the reference's fused training, ``triton_impl.py:320``).
+# Kernel sizes of the fused forward, and of the fully fused (flash-style
+# recompute) backward kernels. At K = 5 the fused training path pairs the fused
+# forward and dX kernels with a materialised dK (``_k5_backward``); the
+# reference fuses training for K <= 3 only (``triton_impl.py:320``).
 FUSED_KERNEL_SIZES = (1, 3, 5)
 FUSED_TRAINING_KERNEL_SIZES = (1, 3)
 FUSED_BACKWARD_AVAILABLE = True
@@ -130,9 +131,10 @@ def fused_generator_supported(channels: int, kernel_size: int, dtype: torch.dtyp
 
 
 def fused_training_supported(kernel_size: int) -> bool:
-    """The flash-style recompute backward covers K <= 3, like the reference
-    (``triton_impl.py:320``)."""
-    return FUSED_BACKWARD_AVAILABLE and kernel_size in FUSED_TRAINING_KERNEL_SIZES
+    """Whether the fused generator path can train at this kernel size: K <= 3
+    with the fully fused backward, K = 5 with the split one (fused dX,
+    materialised dK). The reference stops at K <= 3 (``triton_impl.py:320``)."""
+    return FUSED_BACKWARD_AVAILABLE and kernel_size in FUSED_KERNEL_SIZES
 
 
 def auto_fuse_training(tokens: int, channels: int, kernel_size: int, dtype: torch.dtype) -> bool:
@@ -141,14 +143,19 @@ def auto_fuse_training(tokens: int, channels: int, kernel_size: int, dtype: torc
     The reference fuses above 16384 spatial tokens (and at exactly 16384 for
     FP32), a threshold it measured on an RTX 5090 (``triton_impl.py:313-316``).
     Measured on B200 with this library's kernels (``bench.py --crossover``:
-    B=1, C=64, K=3, square images from 32^2 to 256^2, CUDA-graph replays): the
-    fused step is faster at every size in FP32 (0.17 against 0.29 ms at 32^2,
-    0.60 against 3.19 ms at 256^2) and from 48^2 (2304 tokens) on in bf16; at
-    32^2 (1024 tokens) the materialised bf16 step is 3 % faster (0.132 against
-    0.136 ms, both launch-bound). So: FP32 always fuses; 16-bit types fuse
-    above 1024 tokens.
+    B=1, C=64, square images, CUDA-graph replays, L2 flushed):
+    K = 3: the fused step is faster at every size in FP32 (0.16 against 0.28 ms
+    at 32^2, 0.60 against 3.15 ms at 256^2); in bf16 the materialised step is
+    3-8 % faster up to 64^2 (4096 tokens; both launch-bound, e.g. 0.137
+    against 0.133 ms) and the fused one from 96^2 on (0.36 against 0.70 ms at
+    256^2). K = 5: the materialised step wins at 32^2 (0.60 against 0.67 ms
+    FP32, 0.15 against 0.17 ms bf16), the fused one from 64^2 on (bf16 0.85
+    against 1.86 ms at 256^2). So: K <= 3 FP32 always fuses, 16-bit types
+    fuse above 4096 tokens; K = 5 fuses above 1024 tokens.
     """
-    return dtype == torch.float32 or tokens > 1024
+    if kernel_size > 3:
+        return tokens > 1024
+    return dtype == torch.float32 or tokens > 4096
 
 
 # ------------------------------------------------------- weight packing ----
@@ -188,7 +195,8 @@ def _stage_operands(x, y, kernel_size, dilations):
 
 
 # Attribute of a cat output that carries its fuse-conv staged planes (written by
-# the forward itself) to the fuse conv: (planes, nbytes, output version).
+# the forward itself) to the fuse conv: (planes, nbytes, output version,
+# whether the output's backward reads its gradient channel-last).
 FUSE_PLANES_ATTR = "_ddpm_fuse_planes"
 
 
@@ -213,7 +221,8 @@ def _launch_gencat_fwd(x, y, packed, bias, kernel_size, dilations, staged=None,
             out.data_ptr(), planes.data_ptr(), nbytes,
             n, c, h, w, int(kernel_size), d0, d1, d2, code, stream,
         )
-        setattr(out, FUSE_PLANES_ATTR, (planes, nbytes, out._version))
+        setattr(out, FUSE_PLANES_ATTR, (planes, nbytes, out._version,
+                                        int(kernel_size) in FUSED_TRAINING_KERNEL_SIZES))
         return out
     _lib.call(
         "ddpm_gencat_fwd_staged",
@@ -265,7 +274,7 @@ class _GeneratorDynamicCat(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad_out):
         if ctx.kernel_size not in FUSED_TRAINING_KERNEL_SIZES:
-            return _recompute_backward(ctx, grad_out)
+            return _k5_backward(ctx, grad_out)
         x, y, weight, bias = ctx.saved_tensors
         packed = ctx.packed
         n, c, h, w = x.shape
@@ -335,32 +344,42 @@ class _GeneratorDynamicCat(torch.autograd.Function):
         return grad_x, grad_y, gw, gb, None, None, None
 
 
-def _recompute_backward(ctx, grad_out):
-    """Backward of the fused forward for kernel sizes the fused backward kernels
-    do not cover (K = 5): the taps are recomputed by the 1x1 generator
-    convolution (a library GEMM, as the reference's materialised path,
-    ``triton_impl.py:340-347``), the filter's gradients come from this library's
-    ``ddpm_dyncat_bwd``, and the generator's gradients from the convolution's
-    autograd. Only (x, y, weight, bias) were saved, as in the fused path."""
+def _k5_backward(ctx, grad_out):
+    """Backward of the fused forward at K = 5, where dY + dW has no fused
+    kernel (the 75 slots of a channel group do not fit the dY+dW kernel's
+    tensor memory and x halo): dX by the fused recompute kernel
+    (``ddpm_gencat_bwd_x_staged``: the taps never reach HBM), dK = shifted x *
+    g_b written once by ``ddpm_dyncat_bwd`` (tap gradient only, no taps read),
+    and dY, dW, db from dK by the 1x1 convolution's backward (cuDNN GEMMs, as
+    the reference's materialised path, ``triton_impl.py:340-347``). Only
+    (x, y, weight, bias) were saved, as in the fused path."""
     x, y, weight, bias = ctx.saved_tensors
     n, c, h, w = x.shape
     ks = ctx.kernel_size
+    d0, d1, d2 = ctx.dilations
+    code = _lib.dtype_code(x.dtype)
     need_x, need_y, need_w, need_b = ctx.needs_input_grad[:4]
-    with torch.enable_grad():
-        y_ = y.detach().requires_grad_(need_y)
-        w_ = weight.detach().reshape(3 * c * ks * ks, c, 1, 1).requires_grad_(need_w)
-        b_ = bias.detach().requires_grad_(need_b)
-        taps = F.conv2d(y_, w_, b_)
-    kernels = taps.detach().reshape(n, 3, c, ks * ks, h, w)
-    grad_x, grad_k = _dyncat_backward(x, kernels, grad_out, ks, ctx.dilations, need_x,
-                                      need_y or need_w or need_b)
-    wanted = [t for t, need in ((y_, need_y), (w_, need_w), (b_, need_b)) if need]
-    grads = iter(torch.autograd.grad(taps, wanted, grad_k.reshape(taps.shape)) if wanted else ())
-    del taps, kernels
-    gy = next(grads) if need_y else None
-    gw = next(grads).view_as(weight) if need_w else None
-    gb = next(grads) if need_b else None
-    return grad_x if need_x else None, gy, gw, gb, None, None, None
+    grad_out = grad_out.to(x.dtype).contiguous()
+    grad_x = torch.empty_like(x) if need_x else None
+    gy = gw = gb = None
+    rows = 3 * c * ks * ks
+    with torch.cuda.device(x.device):
+        stream = _lib.stream_handle(x.device)
+        if need_y or need_w or need_b:
+            dk = torch.empty((n, rows, h, w), dtype=x.dtype, device=x.device)
+            _lib.call("ddpm_dyncat_bwd", x.data_ptr(), code, None, grad_out.data_ptr(), code,
+                      None, dk.data_ptr(), n, c, h, w, ks, d0, d1, d2, stream)
+            gy, gw, gb = torch.ops.aten.convolution_backward(
+                dk, y, weight.reshape(rows, c, 1, 1), [rows], [1, 1], [0, 0], [1, 1], False,
+                [0, 0], 1, [need_y, need_w, need_b])
+            del dk
+        if need_x:
+            staged = ctx.staged
+            _lib.call("ddpm_gencat_bwd_x_staged", staged.data_ptr(), staged.numel(),
+                      ctx.packed.data_ptr(), bias.data_ptr(), grad_out.data_ptr(),
+                      grad_x.data_ptr(), n, c, h, w, ks, d0, d1, d2, code, stream)
+    gw = gw.view_as(weight) if need_w else None
+    return grad_x, gy if need_y else None, gw, gb if need_b else None, None, None, None
 
 
 def fused_generator_dynamic_cat(x, y, weight, bias, kernel_size, dilations, *,

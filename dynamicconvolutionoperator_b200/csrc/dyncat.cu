@@ -781,9 +781,11 @@ int dispatch_bwd(int ks, const void* x, const void* k, const void* g, void* gx, 
   return set_error(DDPM_ERR_UNSUPPORTED, "kernel_size %d not supported (1, 3, 5, 7)", ks);
 }
 
+// `need_k`: the taps are read (the forward and the data gradient; the tap
+// gradient alone does not read them).
 int check_common(const void* x, int xdt, const void* k, int kdt, int n, int c, int h, int w,
-                 int ks, int d0, int d1, int d2) {
-  DDPM_CHECK_ARG(x != nullptr && k != nullptr, "null input pointer");
+                 int ks, int d0, int d1, int d2, bool need_k = true) {
+  DDPM_CHECK_ARG(x != nullptr && (k != nullptr || !need_k), "null input pointer");
   DDPM_CHECK_ARG(dtype_size(xdt) > 0 && dtype_size(kdt) > 0, "unknown dtype code (%d, %d)", xdt,
                  kdt);
   DDPM_CHECK_ARG(n >= 1 && c >= 1 && h >= 1 && w >= 1, "sizes must be positive (n=%d c=%d h=%d w=%d)",
@@ -845,7 +847,7 @@ int dyncat_fwd(const void* x, int xdt, const void* k, int kdt, void* out, int n,
 
 int dyncat_bwd(const void* x, int xdt, const void* k, const void* g, int kdt, void* gx, void* gk,
                int n, int c, int h, int w, int ks, int d0, int d1, int d2, cudaStream_t st) {
-  int rc = check_common(x, xdt, k, kdt, n, c, h, w, ks, d0, d1, d2);
+  int rc = check_common(x, xdt, k, kdt, n, c, h, w, ks, d0, d1, d2, gx != nullptr);
   if (rc) return rc;
   DDPM_CHECK_ARG(g != nullptr, "null grad_out pointer");
   if (gx == nullptr && gk == nullptr) return DDPM_OK;

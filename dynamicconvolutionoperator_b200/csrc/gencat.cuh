@@ -628,16 +628,17 @@ int max_smem_optin();
 // [part][n][G][Hp][Wp][8]: 16-byte rows of 8 channels, G = round16(C+1)/8
 // groups; channel C is the constant one of the bias / db column (1 at every
 // position), channels above it are zero. Plane row i holds image row i - ph
-// (ph = (K/2) * max dilation), plane column j holds image column j - 8, and
-// Wp = 128 * ceil(W / 128) + 16, so a 144-pixel segment starting 8 columns left
-// of any 128-pixel row tile, at any row within the dilation halo, is in range.
+// (ph = (K/2) * max dilation), plane column j holds image column j - pw (pw =
+// 8 for K <= 3, 16 for K = 5), and Wp = 128 * ceil(W / 128) + 2 pw, so a
+// (128 + 2 pw)-pixel segment starting pw columns left of any 128-pixel row
+// tile, at any row within the dilation halo, is in range.
 // FP32 stores a bf16 hi part and a bf16 residual part.
 //
 // x plane (after the y plane, 256-byte aligned): x in FP32, 4 channels per
 // 16-byte cell, [n][Cq][H][W][4] with Cq = ceil(C/4) (channels >= C zero); not
 // padded: it is read by TMA, which zero-fills outside the image.
 struct StageLayout {
-  int N, C, H, W, G, ph, Hp, Wp, parts, Cq;
+  int N, C, H, W, G, ph, pw, Hp, Wp, parts, Cq;
   size_t part_bytes, x_offset, x_bytes;
   __host__ __device__ size_t y_bytes() const { return part_bytes * parts; }
   __host__ __device__ size_t total_bytes() const { return x_offset + x_bytes; }
@@ -653,8 +654,11 @@ struct StageLayout {
     L.W = w;
     L.G = (c + 1 + 15) / 16 * 2;
     L.ph = (ks / 2) * max3(d0, d1, d2);
+    // columns: 8 (K <= 3) or 16 (K = 5) zero columns before image column 0,
+    // the dX kernels' row segment offset, so a segment starts at a 16-pixel block
+    L.pw = ks <= 3 ? 8 : 16;
     L.Hp = h + 2 * L.ph;
-    L.Wp = (w + kTileM - 1) / kTileM * kTileM + 16;
+    L.Wp = (w + kTileM - 1) / kTileM * kTileM + 2 * L.pw;
     L.parts = dt == DDPM_F32 ? 2 : 1;
     L.part_bytes = (size_t)n * L.G * L.Hp * L.Wp * 16;
     L.Cq = (c + 3) / 4;
@@ -670,18 +674,18 @@ int stage(const void* x, const void* y, void* staged, size_t staged_bytes, int n
 // TMA descriptors of the staged planes for 8 x 16 pixel tiles (64-bit element
 // views): x halo box {32 px, 8 + 2R rows, 4 channel quads}, coordinates
 // ((w0 - 8) * 2, h0 - R, 4 * cg, n); y tile box {16 px, 8 rows, ygroups
-// channel groups}, coordinates ((w0 + 8) * 2, h0 + ph, 0, part * N + n).
+// channel groups}, coordinates ((w0 + pw) * 2, h0 + ph, 0, part * N + n).
 // False when the driver rejects one (callers then stage from x and y).
 // `halo_cols` and `quads` (4-channel cells per box) set the x box for other
 // tile geometries (the K = 5 forward: 48 columns from w0 - 16, 2 or 1 quads).
 bool encode_stage_maps(CUtensorMap* xmap, CUtensorMap* ymap, int R, int ygroups,
                        const uint8_t* staged, const StageLayout& sl, int halo_cols = kHaloCols,
                        int quads = 4);
-// Tensor map reading a 144-pixel row segment of the y plane ([group][pixel][8
-// channels], all `ngroups` channel groups of one part) as one 5-D box:
-// coordinates (0, first plane column / 16, plane row, 0, part * N + n).
+// Tensor map reading a (16 * blocks)-pixel row segment of the y plane
+// ([group][pixel][8 channels], all `ngroups` channel groups of one part) as one
+// 5-D box: coordinates (0, first plane column / 16, plane row, 0, part * N + n).
 bool encode_stage_segment_map(CUtensorMap* map, int ngroups, const uint8_t* staged,
-                              const StageLayout& sl);
+                              const StageLayout& sl, int blocks = 9);
 
 }  // namespace gencat
 }  // namespace ddpm

@@ -47,7 +47,10 @@ namespace {
 
 using namespace gencat;
 
-constexpr int kSeg = 144;  // staged pixels per row segment (128 + 8 on each side)
+// Staged pixels per row segment: 128 plus kSegOff on each side (8 for K <= 3,
+// whose dilation halos reach 8 pixels; 16 for K = 5, halos up to 16).
+__host__ __device__ constexpr int seg_off(int ks) { return ks <= 3 ? 8 : 16; }
+__host__ __device__ constexpr int seg_px(int ks) { return kTileM + 2 * seg_off(ks); }
 
 // Sixteen 16-bit values (two 16-byte vectors, element 0 in the low half of the
 // first word) as floats; FP32 instances never take this path.
@@ -79,7 +82,10 @@ struct BxCfg {
   // units in flight (16-bit staged: a third unit buffer fits and keeps one
   // more unit's copies outstanding)
   static constexpr int kUnitBufs = (kStaged && !kSplit) ? 3 : 2;
-  static constexpr int kWStages = kSplit ? 4 : 6;
+  // FP32 at K = 5: 160-pixel segments and 75 bias rows leave room for two
+  static constexpr int kWStages = kSplit ? (KS >= 5 ? 2 : 4) : 6;
+  static constexpr int kSeg = seg_px(KS);
+  static constexpr int kOff = seg_off(KS);
   static constexpr bool kBiasInGemm = !kSplit;
   static constexpr int kIssuers = 2;        // MMA issuer warps (alternate chunks)
   static constexpr int kFirstProducerWarp = 1 + kIssuers;
@@ -100,10 +106,12 @@ struct BxSmem {
 
 // One unit buffer = the y row segment (both parts) + the gradient row segment.
 // C=64: fp32 2x36 + 2x36 + 4x16 + 7 KB = 215 KB; bf16 2x23 + 2x18 + 6x10 KB = 143 KB
-// (3 unit buffers when staged: 184 KB).
+// (3 unit buffers when staged: 184 KB). K = 5: fp32 2x40 + 2x40 + 2x16 + 19 KB
+// = 211 KB; bf16 staged 3x25 + 3x20 + 6x10 KB = 196 KB.
 template <typename T, int KS, bool kStaged>
 __host__ __device__ inline BxSmem bx_smem_layout(int Cp, int Ck, int C) {
   using Cfg = BxCfg<T, KS, kStaged>;
+  constexpr int kSeg = Cfg::kSeg;
   BxSmem L;
   L.reg_part = (uint32_t)Ck * kSeg * 2;
   L.reg_bytes = Cfg::kParts * L.reg_part;
@@ -131,7 +139,7 @@ struct BxParams {
   const uint8_t* staged;  // staged y, or null (stage from y)
   StageLayout sl;
   CUtensorMap gmap;       // grad_out {W, H, 4C, N}, box {kSeg, 1, Cp, 1} (staged path)
-  CUtensorMap ymap;       // y-plane row segment, box of 9 16-px blocks x Ck/8 groups
+  CUtensorMap ymap;       // y-plane row segment, box of kSeg/16 16-px blocks x Ck/8 groups
   int g_tma;              // gmap is valid
   int y_tma;              // ymap is valid
   // grad_out channel-last [N][H][W][4C] (16-bit, C == 64, staged): gmap is then
@@ -141,17 +149,18 @@ struct BxParams {
   int* status;
 };
 
-// Gradient row segment g_b[:, hr, w0-8 .. w0+135] of one unit into `gs`
-// ([Cp][kSeg], I/O dtype): one channel per thread (threads tid, tid + nthr,
+// Gradient row segment g_b[:, hr, w0-OFF .. w0-OFF+SEG-1] of one unit into
+// `gs` ([Cp][SEG], I/O dtype): one channel per thread (threads tid, tid + nthr,
 // ...), 1-D bulk copies counted on `bar` when every row start is 16-byte
 // aligned, zero outside the image.
-template <typename T>
+template <typename T, int SEG, int OFF>
 __device__ __forceinline__ void stage_grad_rows(T* gs, const T* gout, uint64_t* bar, int tid,
                                                 int nthr, int n, int b, int hr, int w0, int C,
                                                 int Cp, int H, int W, size_t P, uint32_t g_bytes,
                                                 bool g_bulk) {
-  const int lo = w0 - 8 < 0 ? 0 : w0 - 8;
-  const int hi = w0 + kSeg - 8 > W ? W : w0 + kSeg - 8;
+  constexpr int kSeg = SEG;
+  const int lo = w0 - OFF < 0 ? 0 : w0 - OFF;
+  const int hi = w0 + kSeg - OFF > W ? W : w0 + kSeg - OFF;
   const bool row_ok = hr >= 0 && hr < H;
   if (!row_ok) {
     // the whole segment is outside the image: vector zero stores over all threads
@@ -163,14 +172,14 @@ __device__ __forceinline__ void stage_grad_rows(T* gs, const T* gout, uint64_t* 
     T* dst = gs + (size_t)c * kSeg;
     const T* src = gout + ((size_t)n * 4 * C + (size_t)(b + 1) * C + c) * P + (size_t)hr * W;
     if (c < C && g_bulk) {
-      for (int x = 0; x < lo - (w0 - 8); ++x) dst[x] = T(0.f);
-      for (int x = hi - (w0 - 8); x < kSeg; ++x) dst[x] = T(0.f);
+      for (int x = 0; x < lo - (w0 - OFF); ++x) dst[x] = T(0.f);
+      for (int x = hi - (w0 - OFF); x < kSeg; ++x) dst[x] = T(0.f);
       const uint32_t bytes = (uint32_t)(hi - lo) * sizeof(T);
       tc::mbar_expect_tx(bar, bytes);  // before the copy can complete
-      tc::bulk_g2s(dst + (lo - (w0 - 8)), src + lo, bytes, bar);
+      tc::bulk_g2s(dst + (lo - (w0 - OFF)), src + lo, bytes, bar);
     } else {
       for (int x = 0; x < kSeg; ++x) {
-        const int col = w0 - 8 + x;
+        const int col = w0 - OFF + x;
         dst[x] = (c < C && col >= 0 && col < W) ? src[col] : T(0.f);
       }
     }
@@ -186,6 +195,8 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
   constexpr int NU = Cfg::kUnitBufs;
   constexpr int KK = KS * KS;
   constexpr int r = KS / 2;
+  constexpr int kSeg = Cfg::kSeg;
+  constexpr int kOff = Cfg::kOff;
   extern __shared__ __align__(1024) uint8_t smem[];
   __shared__ uint32_t tmem_base_s;
   __shared__ int abort_s;
@@ -298,8 +309,8 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
             }
             tc::tc_fence_after();
             const int dx = (kj - r) * d;
-            // window: pixels (8 - dx) .. (8 - dx) + 127 of the staged segment
-            const uint64_t ad = a_base + (uint64_t)(8 - dx);
+            // window: pixels (kOff - dx) .. (kOff - dx) + 127 of the staged segment
+            const uint64_t ad = a_base + (uint64_t)(kOff - dx);
             const uint64_t bd =
                 tc::smem_desc(tc::smem_u32(smem + L.w + s * L.w_bytes), b_lbo, 128);
             const uint32_t dt = tmem_base + j * Cp;
@@ -347,7 +358,8 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
         T* gs = reinterpret_cast<T*>(smem + L.gs + ub * L.g_bytes);
         if constexpr (kStaged) {
           // staged y: one bulk copy per (part, channel group); plane row hr + ph,
-          // plane columns w0 .. w0+143 = image columns w0-8 .. w0+135
+          // plane columns w0 .. w0+kSeg-1 = image columns w0-kOff .. (the
+          // plane's column padding equals kOff)
           if (!warp_wait(&r_empty[ub], ((uq / NU) & 1) ^ 1, abort_flag) ||
               !warp_wait(&g_empty[ub], ((uq / NU) & 1) ^ 1, abort_flag)) {
             fail(abort_flag, p.status, 23);
@@ -380,15 +392,15 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
 #pragma unroll
                 for (int bx = 0; bx < kBoxes; ++bx)
                   tc::tma_load_5d(reinterpret_cast<uint8_t*>(gs) + bx * kSeg * 128, &p.gmap,
-                                  bx * (64 / kBoxes), b + 1, w0 - 8, hr, n, &u_full[ub]);
+                                  bx * (64 / kBoxes), b + 1, w0 - kOff, hr, n, &u_full[ub]);
               } else {
-                tc::tma_load_4d(gs, &p.gmap, w0 - 8, hr, (b + 1) * C, n, &u_full[ub]);
+                tc::tma_load_4d(gs, &p.gmap, w0 - kOff, hr, (b + 1) * C, n, &u_full[ub]);
               }
             }
           }
           if (!p.g_tma)
-            stage_grad_rows<T>(gs, gout, &u_full[ub], pt, Cfg::kProducers, n, b, hr, w0, C, Cp,
-                               H, W, P, L.g_bytes, g_bulk);
+            stage_grad_rows<T, kSeg, kOff>(gs, gout, &u_full[ub], pt, Cfg::kProducers, n, b, hr,
+                                           w0, C, Cp, H, W, P, L.g_bytes, g_bulk);
           __syncwarp();
           if (pt != 0) tc::mbar_arrive(&u_full[ub]);
         } else {
@@ -403,7 +415,7 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
             for (int e = 0; e < 8; ++e) {
               const int c = kg * 8 + e;
               if (item < items && c < C)
-                v[e] = load_raw8<T>(y + ((size_t)n * C + c) * P, H, W, hr, w0 - 8 + jb * 8);
+                v[e] = load_raw8<T>(y + ((size_t)n * C + c) * P, H, W, hr, w0 - kOff + jb * 8);
               else if (c == ones_c)
                 v[e].ones();
               else
@@ -417,9 +429,9 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
                 break;
               }
               waited = true;
-              // (2) gradient row segment, one channel per thread: columns w0-8 .. w0+135
-              stage_grad_rows<T>(gs, gout, &u_full[ub], pt, Cfg::kProducers, n, b, hr, w0, C,
-                                 Cp, H, W, P, L.g_bytes, g_bulk);
+              // (2) gradient row segment, one channel per thread: columns w0-kOff ..
+              stage_grad_rows<T, kSeg, kOff>(gs, gout, &u_full[ub], pt, Cfg::kProducers, n, b,
+                                             hr, w0, C, Cp, H, W, P, L.g_bytes, g_bulk);
             }
             if (item < items)
               store_transposed<T, Op, Cfg::kSplit>(reg + (kg * kSeg + jb * 8) * 16, L.reg_part, v);
@@ -503,7 +515,7 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
           // gradient segment is zero outside the image.
           static_assert(Cfg::kBlkPerWG == 1, "staged epilogue: one block per warpgroup");
           const bool blk_ok = wg < nblk;
-          const T* gcol = gs + (size_t)(wg * 16) * kSeg + (m + 8);
+          const T* gcol = gs + (size_t)(wg * 16) * kSeg + (m + kOff);
           const uint32_t tcol = tmem_base + ((uint32_t)(quad * 32) << 16) + wg * 16;
           float dv[2][16];
           if (!warp_wait(&t_full[tq % NB], (tq / NB) & 1, abort_flag)) {
@@ -531,10 +543,10 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
               const int dx = (kj - r) * d;
               float gv[16];
               if constexpr (kNhwc) {
-                // pixel row m + 8 - dx of the swizzled [kSeg][128 bytes]
+                // pixel row m + kOff - dx of the swizzled [kSeg][128 bytes]
                 // segment(s): this block's channel chunks, chunk j of row r at
                 // j ^ (r & 7)
-                const int pr = m + 8 - dx;
+                const int pr = m + kOff - dx;
                 if constexpr (sizeof(T) == 4) {
                   // FP32: box wg / 2 holds channels 32 (wg / 2) .. +31; the
                   // block's 16 channels are chunks 4 (wg % 2) .. +3
@@ -581,7 +593,7 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
           for (int kj = 0; kj < KS; ++kj, ++tq) {
             const int tap = ki * KS + kj;
             const int dx = (kj - r) * d;
-            // g_b at (h - dy, w - dx): staged column m + 8 - dx (zero off-image)
+            // g_b at (h - dy, w - dx): staged column m + kOff - dx (zero off-image)
             const bool ok = px_ok && (unsigned)(w - dx) < (unsigned)W;
             const int j = tq % NB;
             if (!warp_wait(&t_full[j], (tq / NB) & 1, abort_flag)) {
@@ -598,7 +610,7 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
               float dv1[16];
               tc::tmem_ld16(tmem_base + ((uint32_t)(quad * 32) << 16) + j * Cp + blk * 16, dv1);
               float gv1[16];
-              const T* gcol = gs + (size_t)(blk * 16) * kSeg + (m + 8 - dx);
+              const T* gcol = gs + (size_t)(blk * 16) * kSeg + (m + kOff - dx);
 #pragma unroll
               for (int cl = 0; cl < 16; ++cl) gv1[cl] = ok ? to_f32<T>(gcol[cl * kSeg]) : 0.f;
               tc::tmem_ld_wait();
@@ -685,6 +697,7 @@ int dispatch(int ks, const BxParams& prm, cudaStream_t st) {
   switch (ks) {
     case 1: return launch<T, 1>(prm, st);
     case 3: return launch<T, 3>(prm, st);
+    case 5: return launch<T, 5>(prm, st);
   }
   return set_error(DDPM_ERR_UNSUPPORTED, "fused generator: kernel_size %d not supported", ks);
 }
@@ -696,13 +709,14 @@ int dispatch(int ks, const BxParams& prm, cudaStream_t st) {
 int gencat_bwd_x(const void* y, const void* staged, size_t staged_bytes, const void* wpack,
                  const void* bias, const void* gout, void* gx, int n, int c, int h, int w, int ks,
                  int d0, int d1, int d2, int dt, cudaStream_t st, int g_nhwc) {
-  int rc = gencat::check_shape_bwd(n, c, h, w, ks, d0, d1, d2, dt);
+  int rc = gencat::check_shape(n, c, h, w, ks, d0, d1, d2, dt);
   if (rc) return rc;
   DDPM_CHECK_ARG((y || staged) && wpack && bias && gout && gx, "null pointer");
   if (g_nhwc && (c != 64 || staged == nullptr))
     return set_error(DDPM_ERR_UNSUPPORTED,
                      "a channel-last grad_out needs C == 64 and staged operands");
   const gencat::PackLayout pl = gencat::PackLayout::make(c, ks, dt);
+  const int kSegPx = seg_px(ks);
   BxParams prm{};
   prm.y = y;
   prm.wpack = static_cast<const uint8_t*>(wpack) + pl.bx_offset();
@@ -728,7 +742,10 @@ int gencat_bwd_x(const void* y, const void* staged, size_t staged_bytes, const v
                        prm.sl.y_bytes());
     DDPM_CHECK_ARG((reinterpret_cast<uintptr_t>(staged) & 15u) == 0,
                    "staged y must be 16-byte aligned");
-    prm.y_tma = gencat::encode_stage_segment_map(&prm.ymap, pl.Ck / 8, prm.staged, prm.sl) ? 1 : 0;
+    prm.y_tma = gencat::encode_stage_segment_map(&prm.ymap, pl.Ck / 8, prm.staged, prm.sl,
+                                                 kSegPx / 16)
+                    ? 1
+                    : 0;
     // gradient segments by TMA when the row pitch and base allow a tensor map
     const int es = dtype_size(dt);
     if (g_nhwc) {
@@ -742,7 +759,7 @@ int gencat_bwd_x(const void* y, const void* staged, size_t staged_bytes, const v
                                    (uint64_t)4 * c * w * es, (uint64_t)4 * c * w * h * es};
       // 128 bytes of channels per box (the 128-byte swizzle span): 64 16-bit
       // or 32 FP32 channels; FP32 takes two boxes per unit
-      const uint32_t box[5] = {(uint32_t)(128 / es), 1, (uint32_t)kSeg, 1, 1};
+      const uint32_t box[5] = {(uint32_t)(128 / es), 1, (uint32_t)kSegPx, 1, 1};
       if (encode_tmap(&prm.gmap, ty, 5, gout, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B) !=
           DDPM_OK)
         return DDPM_ERR_CUDA;  // the message is set
@@ -755,7 +772,7 @@ int gencat_bwd_x(const void* y, const void* staged, size_t staged_bytes, const v
       const uint64_t dims[4] = {(uint64_t)w, (uint64_t)h, (uint64_t)4 * c, (uint64_t)n};
       const uint64_t strides[3] = {(uint64_t)w * es, (uint64_t)h * w * es,
                                    (uint64_t)4 * c * h * w * es};
-      const uint32_t box[4] = {(uint32_t)kSeg, 1, (uint32_t)pl.Cp, 1};
+      const uint32_t box[4] = {(uint32_t)kSegPx, 1, (uint32_t)pl.Cp, 1};
       if (encode_tmap(&prm.gmap, ty, 4, gout, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE) ==
           DDPM_OK)
         prm.g_tma = 1;

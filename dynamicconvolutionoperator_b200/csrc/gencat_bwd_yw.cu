@@ -827,7 +827,7 @@ struct DywMaps {
   CUtensorMap xmap;  // staged x plane (64-bit view) {W*2, H, Cq, N}, box {64, 8+2R, 4, 1}
   CUtensorMap ymap;  // staged y plane (64-bit view) {Wp*2, Hp, G, parts*N}, box {32, 8, G, 1}
   CUtensorMap gmap;  // grad_out {W, H, C, 4, N}, box {16, 8, 16, 3, 1} (kGTma only)
-  int ph;            // y-plane row offset
+  int ph, pw;        // y-plane row / column offsets
 };
 
 // D_y of the it-th tile of a split (64 columns at `dy_col`, double buffered)
@@ -1218,12 +1218,12 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
       tile_origin(tile, p.tiles_w, p.tiles_h, n, h0, w0);
       uint8_t* ys = smem + L.y + yb * L.y_bytes;
       if constexpr (kStaged) {
-        // y plane rows h0+ph .. +7, columns w0+8 .. w0+23, every channel group
+        // y plane rows h0+ph .. +7, columns w0+pw .. w0+pw+15, every channel group
         if (pt == 0) {
           tc::mbar_arrive_expect_tx(&y_full[yb], L.y_bytes);
-          tc::tma_load_4d(ys, &maps.ymap, (w0 + 8) * 2, h0 + maps.ph, 0, n, &y_full[yb]);
+          tc::tma_load_4d(ys, &maps.ymap, (w0 + maps.pw) * 2, h0 + maps.ph, 0, n, &y_full[yb]);
           if constexpr (Cfg::kSplit)
-            tc::tma_load_4d(ys + kTileM * Nw * 2, &maps.ymap, (w0 + 8) * 2, h0 + maps.ph, 0,
+            tc::tma_load_4d(ys + kTileM * Nw * 2, &maps.ymap, (w0 + maps.pw) * 2, h0 + maps.ph, 0,
                             p.N + n, &y_full[yb]);
         } else {
           tc::mbar_arrive(&y_full[yb]);
@@ -1597,6 +1597,7 @@ int gencat_bwd_yw(const void* x, const void* y, const void* staged, size_t stage
         use_staged = gencat::encode_stage_maps(&maps.xmap, &maps.ymap, R, sl.G,
                                                static_cast<const uint8_t*>(staged), sl);
         maps.ph = sl.ph;
+        maps.pw = sl.pw;
         // gradient tiles by TMA (16-bit) when the row pitch and base allow a map
         const size_t es = (size_t)dtype_size(dt);
         if (g_nhwc && dt == DDPM_F32) {

@@ -197,7 +197,7 @@ __device__ __forceinline__ void store_plane_group(const FwdParams& p, int n, int
 // Tensor maps of the staged operands (separate grid-constant parameter).
 struct FwdMaps {
   CUtensorMap xmap, ymap;  // see gencat::encode_stage_maps
-  int ph;
+  int ph, pw;              // y-plane row / column offsets
 };
 
 template <typename T, int KS, bool kStaged>
@@ -362,12 +362,12 @@ gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
       tile_origin(tile, p.tiles_w, p.tiles_h, n, h0, w0);
       uint8_t* ys = smem + L.y + yb * L.y_bytes;
       if constexpr (kStaged) {
-        // y plane rows h0+ph .. +7, columns w0+8 .. w0+23, channel groups 0 .. Ck/8-1
+        // y plane rows h0+ph .. +7, columns w0+pw .. w0+pw+15, channel groups 0 .. Ck/8-1
         if (pt == 0) {
           tc::mbar_arrive_expect_tx(&y_full[yb], L.y_bytes);
-          tc::tma_load_4d(ys, &maps.ymap, (w0 + 8) * 2, h0 + maps.ph, 0, n, &y_full[yb]);
+          tc::tma_load_4d(ys, &maps.ymap, (w0 + maps.pw) * 2, h0 + maps.ph, 0, n, &y_full[yb]);
           if constexpr (Cfg::kSplit)
-            tc::tma_load_4d(ys + kTileM * Ck * 2, &maps.ymap, (w0 + 8) * 2, h0 + maps.ph, 0,
+            tc::tma_load_4d(ys + kTileM * Ck * 2, &maps.ymap, (w0 + maps.pw) * 2, h0 + maps.ph, 0,
                             p.N + n, &y_full[yb]);
         } else if (!(withhold && it == 0)) {
           tc::mbar_arrive(&y_full[yb]);
@@ -670,6 +670,7 @@ int gencat_fwd_ex(const void* x, const void* y, const void* staged, size_t stage
                                            static_cast<const uint8_t*>(staged), sl,
                                            gencat::fwd_halo_cols(ks), cgw / 4);
     maps.ph = sl.ph;
+    maps.pw = sl.pw;
   }
   DDPM_CHECK_ARG(use_staged || (x && y), "tensor maps unavailable: x and y are needed");
   switch (dt) {

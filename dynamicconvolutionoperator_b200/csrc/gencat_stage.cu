@@ -37,7 +37,7 @@ __global__ void __launch_bounds__(256) stage_y_kernel(const T* __restrict__ y,
     const int g = item & 7, c = item >> 3;
     Raw8<T> v;
     if (c < L.C)
-      v = load_raw8<T>(y + ((size_t)n * L.C + c) * P, L.H, L.W, hr, j0 - 8 + g * 8);
+      v = load_raw8<T>(y + ((size_t)n * L.C + c) * P, L.H, L.W, hr, j0 - L.pw + g * 8);
     else if (c == L.C)
       v.ones();
     else
@@ -217,14 +217,15 @@ bool encode_stage_maps(CUtensorMap* xmap, CUtensorMap* ymap, int R, int ygroups,
 }
 
 bool encode_stage_segment_map(CUtensorMap* map, int ngroups, const uint8_t* staged,
-                              const StageLayout& sl) {
+                              const StageLayout& sl, int blocks) {
   // 16-pixel blocks of 256 bytes as the two inner dimensions, so one box of
-  // 9 blocks x ngroups lands as [group][144 px][16 B] (group stride 2304 B)
+  // `blocks` blocks x ngroups lands as [group][16 * blocks px][16 B] (9 blocks:
+  // group stride 2304 B)
   const uint64_t d[5] = {32, (uint64_t)sl.Wp / 16, (uint64_t)sl.Hp, (uint64_t)sl.G,
                          (uint64_t)sl.parts * sl.N};
   const uint64_t s[4] = {256, (uint64_t)sl.Wp * 16, (uint64_t)sl.Hp * sl.Wp * 16,
                          (uint64_t)sl.G * sl.Hp * sl.Wp * 16};
-  const uint32_t box[5] = {32, 9, 1, (uint32_t)ngroups, 1};
+  const uint32_t box[5] = {32, (uint32_t)blocks, 1, (uint32_t)ngroups, 1};
   if (encode_tmap(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 5, staged, d, s, box,
                   CU_TENSOR_MAP_SWIZZLE_NONE) != DDPM_OK) {
     clear_error();

@@ -89,7 +89,8 @@ DDPM_API int ddpm_dyncat_fwd(const void* x, int x_dtype,
  *               + sum_{b,tap} kernels[b,c,tap,q-off*d_b] * grad_out[(b+1)C+c, q-off*d_b]
  *   grad_k[b,c,tap,p] = x[c, p+off*d_b] * grad_out[(b+1)C+c, p]
  * grad_out has `k_dtype`; grad_x has `x_dtype`; grad_k has `k_dtype`.
- * Either output may be NULL to skip it (one fused launch computes both).
+ * Either output may be NULL to skip it (one fused launch computes both);
+ * `kernels` may be NULL when grad_x is (grad_k does not read the taps).
  */
 DDPM_API int ddpm_dyncat_bwd(const void* x, int x_dtype,
                     const void* kernels, const void* grad_out, int k_dtype,

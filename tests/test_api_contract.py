@@ -95,22 +95,27 @@ def test_fuse_bias_fold_matches_conv2d():
 
 def test_training_crossover_follows_the_b200_measurement():
     """The reference's rule (``triton_impl.py:313-316``: fuse above 16384
-    tokens) was measured on an RTX 5090; on B200 the fused step wins at every
-    measured size in FP32 and above 1024 tokens in 16-bit types."""
+    tokens) was measured on an RTX 5090; on B200 the K = 3 fused step wins at
+    every measured size in FP32 and above 4096 tokens in 16-bit types, the
+    K = 5 one above 1024 tokens in every dtype."""
     from dynamicconvolutionoperator_b200 import _kernels
 
     for tokens in (1, 1024, 16384, 65536):
         assert _kernels.auto_fuse_training(tokens, 64, 3, torch.float32)
     for dt in (torch.bfloat16, torch.float16):
-        assert _kernels.auto_fuse_training(1025, 64, 3, dt)
+        assert _kernels.auto_fuse_training(4097, 64, 3, dt)
         assert _kernels.auto_fuse_training(16384, 64, 3, dt)
-        assert not _kernels.auto_fuse_training(1024, 64, 3, dt)
+        assert not _kernels.auto_fuse_training(4096, 64, 3, dt)
+    for dt in (torch.float32, torch.bfloat16):
+        assert _kernels.auto_fuse_training(1025, 64, 5, dt)
+        assert not _kernels.auto_fuse_training(1024, 64, 5, dt)
 
 
 def test_fused_kernel_limits():
     """Forward: C <= 64, K in {1, 3} with halo (K/2) * max(dilation) <= 8 or
-    K = 5 with halo <= 16; the recompute backward kernels cover K <= 3
-    (reference ``triton_impl.py:320``)."""
+    K = 5 with halo <= 16; fused training at every such K (the fully fused
+    backward kernels at K <= 3, the reference's limit, ``triton_impl.py:320``;
+    fused dX with a materialised dK at K = 5)."""
     from dynamicconvolutionoperator_b200 import _kernels
 
     ok = _kernels.fused_generator_supported
@@ -120,17 +125,18 @@ def test_fused_kernel_limits():
     assert not ok(64, 5, torch.float32, (1, 9, 4)) and not ok(64, 7, torch.bfloat16)
     assert ok(64, 3, torch.float16, (1, 3, 8)) and not ok(64, 3, torch.float16, (1, 3, 9))
     assert not ok(64, 3, torch.float64)
-    assert [k for k in (1, 3, 5, 7) if _kernels.fused_training_supported(k)] == [1, 3]
+    assert [k for k in (1, 3, 5, 7) if _kernels.fused_training_supported(k)] == [1, 3, 5]
+    assert _kernels.FUSED_TRAINING_KERNEL_SIZES == (1, 3)
 
 
 @pytest.mark.parametrize(
     "hw,ks,requested,expect",
     [((128, 128), 3, None, True), ((128, 127), 3, None, True), ((32, 32), 3, None, True),
-     ((256, 256), 5, None, False),
+     ((256, 256), 5, None, True), ((256, 256), 5, False, False),
      ((256, 256), 3, False, False), ((8, 8), 3, True, True), ((8, 8), 7, True, False)],
 )
 def test_module_training_path_choice(hw, ks, requested, expect):
     """``fused_generator_training``: None follows the crossover, True / False
-    force the path, and K > 3 always materialises."""
+    force the path, and K > 5 always materialises."""
     m = DDPM(4, ks, fused_generator_training=requested)
     assert m._use_fused_training(torch.empty(1, 4, *hw)) is expect

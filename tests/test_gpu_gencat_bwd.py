@@ -44,7 +44,7 @@ def _stage(xd, yd, ks, dil):
 
 
 @pytest.mark.parametrize("shape", SHAPES)
-@pytest.mark.parametrize("ks", [1, 3])
+@pytest.mark.parametrize("ks", [1, 3, 5])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("staged", [False, True])
 def test_gencat_bwd_x(shape, ks, dtype, staged):
@@ -150,21 +150,44 @@ def test_gencat_bwd_yw(shape, ks, dtype, staged):
         assert err <= (2e-4 if dtype == torch.float32 else 1e-2), err
 
 
-def test_fused_autograd_matches_oracle_all_grads():
-    """End to end through fused_generator_dynamic_cat + autograd (fp32)."""
+@pytest.mark.parametrize("ks", [3, 5])
+def test_fused_autograd_matches_oracle_all_grads(ks):
+    """End to end through fused_generator_dynamic_cat + autograd (fp32). At
+    K = 5 the forward is fused and the backward recomputes the taps with the
+    1x1 generator convolution (cuDNN, TF32 off here) and takes the filter's
+    gradients from ddpm_dyncat_bwd."""
     from dynamicconvolutionoperator_b200 import fused_generator_dynamic_cat
 
-    shape, ks = (2, 24, 16, 40), 3
+    shape = (2, 24, 16, 40)
     x, y, wt, b = _case(shape, ks, torch.float32, seed=12)
     n, c, h, w = shape
     g = torch.randn((n, 4 * c, h, w), generator=torch.Generator().manual_seed(13))
     gold = _gold_grads(x, y, wt, b, g, ks, (1, 3, 5))
     ts = [t.cuda().requires_grad_(True) for t in (x, y, wt, b)]
-    out = fused_generator_dynamic_cat(*ts, ks, (1, 3, 5))
-    grads = torch.autograd.grad(out, ts, g.cuda())
+    with torch.backends.cudnn.flags(enabled=True, allow_tf32=False):
+        out = fused_generator_dynamic_cat(*ts, ks, (1, 3, 5))
+        grads = torch.autograd.grad(out, ts, g.cuda())
     for got, ref in zip(grads, gold):
         scale = max(ref.abs().max().item(), 1.0)
         assert (got.double().cpu() - ref).abs().max().item() <= 2e-4 * scale
+
+
+def test_fused_k5_autograd_partial_grads_bf16():
+    """K = 5, bf16, only some inputs requiring gradients: the recompute
+    backward returns None for the others and matches the oracle for the rest."""
+    from dynamicconvolutionoperator_b200 import fused_generator_dynamic_cat
+
+    shape, ks = (1, 16, 12, 20), 5
+    x, y, wt, b = _case(shape, ks, torch.bfloat16, seed=14)
+    n, c, h, w = shape
+    g = torch.randn((n, 4 * c, h, w), generator=torch.Generator().manual_seed(15)).bfloat16()
+    gold = _gold_grads(x, y, wt, b, g, ks, (1, 3, 5))
+    xd, yd, wd, bd = x.cuda(), y.cuda().requires_grad_(True), wt.cuda().requires_grad_(True), b.cuda()
+    out = fused_generator_dynamic_cat(xd, yd, wd, bd, ks, (1, 3, 5))
+    gy, gw = torch.autograd.grad(out, (yd, wd), g.cuda())
+    for got, ref in ((gy, gold[1]), (gw, gold[2])):
+        scale = max(ref.abs().max().item(), 1.0)
+        assert (got.double().cpu() - ref).abs().max().item() <= 3e-2 * scale
 
 
 @pytest.mark.parametrize("shape", [(1, 64, 20, 24), (2, 40, 19, 24)])
@@ -248,6 +271,39 @@ def test_channel_last_grad_out_matches_nchw(shape, ks, dtype):
         assert torch.isfinite(a).all()
         scale = r.double().abs().max().item() + 1e-12
         assert (a.double() - r.double()).abs().max().item() / scale <= 1e-2
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_k5_bwd_x_channel_last_and_max_halo(dtype):
+    """K = 5 dX: the channel-last entry point matches the NCHW one bit for bit,
+    and the largest halo (16, dilations (1, 8, 4)) matches the oracle on a
+    shape whose rows span two 128-pixel tiles; dY + dW at K = 5 is not a fused
+    entry point (DDPM_ERR_UNSUPPORTED before any launch)."""
+    from dynamicconvolutionoperator_b200 import _kernels, _lib
+
+    shape, ks, dil = (1, 64, 13, 150), 5, (1, 8, 4)
+    x, y, wt, b = _case(shape, ks, dtype, seed=21)
+    n, c, h, w = shape
+    g = torch.randn((n, 4 * c, h, w), generator=torch.Generator().manual_seed(22)).to(dtype)
+    gx_gold, *_ = _gold_grads(x, y, wt, b, g, ks, dil)
+    xd, yd, wd, bd, gd = x.cuda(), y.cuda(), wt.cuda(), b.cuda(), g.cuda()
+    packed = _kernels.pack_generator_weight(wd, bd, c, ks)
+    st, nb = _stage(None, yd, ks, dil)
+    code = _lib.dtype_code(dtype)
+    stream = _lib.stream_handle(yd.device)
+    out = {}
+    for sfx, gg in (("", gd), ("_nhwc", gd.contiguous(memory_format=torch.channels_last))):
+        gx = torch.full_like(xd, float("nan"))
+        _lib.call("ddpm_gencat_bwd_x_staged" + sfx, st.data_ptr(), nb, packed.data_ptr(),
+                  bd.data_ptr(), gg.data_ptr(), gx.data_ptr(), n, c, h, w, ks, *dil, code, stream)
+        out[sfx] = gx
+    torch.cuda.synchronize()
+    assert torch.equal(out[""], out["_nhwc"])
+    rtol, atol = TOL[dtype]
+    torch.testing.assert_close(out[""].double().cpu(), gx_gold, rtol=rtol, atol=atol)
+    rc = _lib.load().ddpm_gencat_bwd_yw_staged(1, 1 << 20, 1, 1, 1, 1, 1, 1, 1 << 20,
+                                               n, c, h, w, ks, *dil, code, None)
+    assert rc == -2
 
 
 def test_channel_last_grad_out_rejected_outside_its_limits():
