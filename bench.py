@@ -508,9 +508,9 @@ def library_kernels(model, x, y, dtype, device, materialised=True):
         _lib.call("ddpm_fuseconv_bwd_data_staged", gplanes.data_ptr(), gp_bytes,
                   fpacked.data_ptr(), fgx.data_ptr(), n, 4 * C, C, H, W, code, sh)
 
-    # as in the step: for 16-bit data at C=64 the fuse conv hands the generator
-    # backward its gradient channel-last, and the *_nhwc entry points read it so
-    nhwc = dtype != torch.float32 and C == 64
+    # as in the step: at C=64 the fuse conv hands the generator backward its
+    # gradient channel-last, and the *_nhwc entry points read it so
+    nhwc = C == 64
     gout_g = gout.contiguous(memory_format=torch.channels_last) if nhwc else gout
     sfx = "_nhwc" if nhwc else ""
 

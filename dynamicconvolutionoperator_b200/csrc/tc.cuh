@@ -143,6 +143,29 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, int c0,
       : "memory");
 }
 
+// Element-wise add of a shared-memory box into a global tensor (TMA reduction,
+// 4-D tensor map), as a bulk async-group of the calling thread; coordinates
+// must not be negative.
+__device__ __forceinline__ void tma_reduce_add_4d(const void* tmap, const void* src, int c0,
+                                                  int c1, int c2, int c3) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.4d.global.shared::cta.add.tile.bulk_group"
+      " [%0, {%2, %3, %4, %5}], [%1];" ::"l"(reinterpret_cast<uint64_t>(tmap)),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Wait until every bulk async-group of this thread has read its source.
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Wait until every bulk async-group of this thread has completed.
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 // 5-D variant of tma_load_4d.
 __device__ __forceinline__ void tma_load_5d(void* dst, const void* tmap, int c0, int c1, int c2,
                                             int c3, int c4, uint64_t* bar) {
