@@ -408,8 +408,9 @@ NCU_TRAFFIC_BYTES: dict[tuple[str, str], float] = {
     ("gencat_fwd", "torch.bfloat16"): 42377472,
     ("gencat_bwd_x", "torch.float32"): 91352320,
     ("gencat_bwd_x", "torch.bfloat16"): 45458944 + 896000,  # channel-last grad_out
-    ("gencat_bwd_yw", "torch.float32"): 114652928,
-    ("gencat_bwd_yw", "torch.bfloat16"): 69589504 + 3247104,  # channel-last grad_out
+    # channel-last grad_out, D_y drained by TMA reductions
+    ("gencat_bwd_yw", "torch.float32"): 105654784 + 8497664,
+    ("gencat_bwd_yw", "torch.bfloat16"): 69647872 + 3415040,
     ("fuseconv_fwd", "torch.float32"): 75615744,
     ("fuseconv_fwd", "torch.bfloat16"): 36270848,
     ("fuseconv_dgrad", "torch.float32"): 27409920,
@@ -587,13 +588,44 @@ def kernel_roofline(model, x, y, dtype, steps, device, materialised=True):
     return res
 
 
+def profile_k5_forward(args, device, dtype):
+    """The fused K=5 forward of configs[2] (B=``--batch``, C=64, 128x128,
+    dilations 1/3/5): staging plus ``ddpm_gencat_fwd_staged``, launched
+    ``--profile-iters`` times."""
+    from dynamicconvolutionoperator_b200 import _kernels, _lib
+
+    ks, hw = 5, 128
+    torch.manual_seed(0)
+    gen = torch.nn.Conv2d(C, 3 * C * ks * ks, 1).to(device=device, dtype=dtype)
+    g = torch.Generator().manual_seed(9)
+    x, y = (torch.randn((args.batch, C, hw, hw), generator=g).to(dtype).to(device)
+            for _ in range(2))
+    n = args.batch
+    code = _lib.dtype_code(dtype)
+    sh = _lib.stream_handle(device)
+    packed = _kernels.pack_generator_weight(gen.weight.detach(), gen.bias.detach(), C, ks)
+    sb = int(_lib.load().ddpm_gencat_stage_bytes(n, C, hw, hw, ks, *DILATIONS, code))
+    st = torch.empty(sb, dtype=torch.uint8, device=device)
+    out = torch.empty((n, 4 * C, hw, hw), dtype=dtype, device=device)
+    for _ in range(args.profile_iters):
+        _lib.call("ddpm_gencat_stage", x.data_ptr(), y.data_ptr(), st.data_ptr(), sb, n, C, hw, hw,
+                  ks, *DILATIONS, code, sh)
+        _lib.call("ddpm_gencat_fwd_staged", st.data_ptr(), sb, packed.data_ptr(),
+                  gen.bias.data_ptr(), out.data_ptr(), n, C, hw, hw, ks, *DILATIONS, code, sh)
+    torch.cuda.synchronize()
+
+
 def profile_kernel(args):
     """Launch one library kernel ``--profile-iters`` times at B=``--batch``
     C=64 256x256 K=3 (the target of the committed ncu captures; prints
-    nothing but 'ok')."""
+    nothing but 'ok'); ``gencat_fwd_k5``: the fused K=5 forward at 128x128."""
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
     dtype = DTYPES[args.dtype]
+    if args.profile_kernel == "gencat_fwd_k5":
+        profile_k5_forward(args, device, dtype)
+        print("ok")
+        return 0
     model, _ = build_model(dtype, args.path, device)
     x, y, _ = [t.to(device) for t in make_inputs(args.batch, dtype, 0)]
     keep, kernels = library_kernels(model, x, y, dtype, device,
