@@ -406,7 +406,7 @@ NCU_TRAFFIC_BYTES: dict[tuple[str, str], float] = {
     # passes of their own, profiles/staging_256.md)
     ("gencat_fwd", "torch.float32"): 115258624,
     ("gencat_fwd", "torch.bfloat16"): 42377472,
-    ("gencat_bwd_x", "torch.float32"): 91352320,
+    ("gencat_bwd_x", "torch.float32"): 86148096 + 5298688,  # channel-last grad_out
     ("gencat_bwd_x", "torch.bfloat16"): 45458944 + 896000,  # channel-last grad_out
     # channel-last grad_out, D_y drained by TMA reductions
     ("gencat_bwd_yw", "torch.float32"): 105654784 + 8497664,
