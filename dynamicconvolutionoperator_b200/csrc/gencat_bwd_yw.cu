@@ -962,7 +962,7 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
     }
     tc::mbar_init(w_done, 1);
     tc::mbar_init(g_full, 1);
-    tc::mbar_init(g_empty, 8);
+    tc::mbar_init(g_empty, 256);
     tc::mbar_init(lo_full, 256);
     tc::mbar_init(lo_empty, 2);
     tc::fence_mbar_init();
@@ -1335,8 +1335,22 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
               gv[b][i] = f2_pack(to_f32<T>(gs[(b * 16 + 2 * i) * kTileM]),
                                  to_f32<T>(gs[(b * 16 + 2 * i + 1) * kTileM]));
         }
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(g_empty);
+        // The next tile's gradient arrives by TMA into this buffer once the
+        // arrivals below are in: every thread first waits for its own loads (a
+        // use of every loaded value here; the compiler may otherwise place the
+        // conversions after the arrival) and orders them before the async
+        // proxy's writes. With one leader arrival after __syncwarp, and the
+        // values consumed later, the TMA overwrote words still being loaded.
+        {
+          unsigned long long dep = 0;
+#pragma unroll
+          for (int b = 0; b < 3; ++b)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) dep ^= gv[b][i];
+          asm volatile("" ::"l"(dep));
+        }
+        tc::fence_proxy_async_smem();
+        tc::mbar_arrive(g_empty);
       } else if (p.g_nhwc) {
         load_gv_nhwc<T>(gv, gout, n, H, W, C, cg, h, w, px_ok);
       } else {

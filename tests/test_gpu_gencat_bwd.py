@@ -318,3 +318,46 @@ def test_channel_last_grad_out_rejected_outside_its_limits():
         rc = lib.ddpm_gencat_bwd_x_staged_nhwc(p, 16, p, p, p, p, 1, c, 8, 16, 3, 1, 3, 5, code,
                                                stream)
         assert rc == -2, (c, code, rc)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_channel_last_dyw_many_tiles_per_cta(dtype):
+    """dY + dW with the gradient tile by TMA (channel-last and NCHW) against the
+    unstaged pass at B=2, 256^2: about 28 tiles per CTA, so the gradient
+    buffer is refilled while earlier tiles are in flight. (A release of that
+    buffer before every thread's loads had completed once corrupted a few
+    tiles of dY and dW here, and only here.)"""
+    from dynamicconvolutionoperator_b200 import _kernels, _lib
+
+    shape, ks = (2, 64, 256, 256), 3
+    x, y, wt, b = _case(shape, ks, dtype, seed=31)
+    n, c, h, w = shape
+    g = torch.randn((n, 4 * c, h, w), generator=torch.Generator().manual_seed(32)).to(dtype)
+    xd, yd, wd, bd, gd = x.cuda(), y.cuda(), wt.cuda(), b.cuda(), g.cuda()
+    packed = _kernels.pack_generator_weight(wd, bd, c, ks)
+    st, nb = _stage(xd, yd, ks, (1, 3, 5))
+    code = _lib.dtype_code(dtype)
+    stream = _lib.stream_handle(xd.device)
+    ws_bytes = int(_lib.load().ddpm_gencat_bwd_workspace_bytes(n, c, h, w, ks))
+    res = {}
+    for name in ("unstaged", "staged", "staged_nhwc"):
+        gy = torch.full_like(yd, float("nan"))
+        gw = torch.full((3 * c * ks * ks, c), float("nan"), dtype=dtype, device="cuda")
+        gb = torch.full((3 * c * ks * ks,), float("nan"), dtype=dtype, device="cuda")
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+        if name == "unstaged":
+            _lib.call("ddpm_gencat_bwd_yw", xd.data_ptr(), yd.data_ptr(), packed.data_ptr(),
+                      gd.data_ptr(), gy.data_ptr(), gw.data_ptr(), gb.data_ptr(), ws.data_ptr(),
+                      ws_bytes, n, c, h, w, ks, 1, 3, 5, code, stream)
+        else:
+            gg = gd.contiguous(memory_format=torch.channels_last) if name.endswith("nhwc") else gd
+            _lib.call("ddpm_gencat_bwd_yw_" + name, st.data_ptr(), nb, packed.data_ptr(),
+                      gg.data_ptr(), gy.data_ptr(), gw.data_ptr(), gb.data_ptr(), ws.data_ptr(),
+                      ws_bytes, n, c, h, w, ks, 1, 3, 5, code, stream)
+        res[name] = (gy.double(), gw.double(), gb.double())
+    torch.cuda.synchronize()
+    for name in ("staged", "staged_nhwc"):
+        for got, ref in zip(res[name], res["unstaged"]):
+            scale = ref.abs().max().item()
+            assert (got - ref).abs().max().item() <= 2e-2 * scale, name
+
