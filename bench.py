@@ -828,7 +828,7 @@ def inference_lines(args, device):
     """DDPM inference (forward only, no autograd), B=1, C=64,
     128x128, K=3 and K=5, fp32 and bf16, through the fused generator path
     (``fused_generator_inference=True``, the default) and the materialised
-    path (the 1x1 generator on cuDNN, then this library's filter kernels);
+    path (the 1x1 generator as cuBLAS GEMMs, then this library's filter kernels);
     graph-replayed device time, L2 flushed between steps."""
     from dynamicconvolutionoperator_b200 import DDPM
 

@@ -142,20 +142,21 @@ def auto_fuse_training(tokens: int, channels: int, kernel_size: int, dtype: torc
 
     The reference fuses above 16384 spatial tokens (and at exactly 16384 for
     FP32), a threshold it measured on an RTX 5090 (``triton_impl.py:313-316``).
-    Measured on B200 with this library's kernels (``bench.py --crossover``:
-    B=1, C=64, square images, CUDA-graph replays, L2 flushed):
-    K = 3: the fused step is faster at every size in FP32 (0.16 against 0.28 ms
-    at 32^2, 0.60 against 3.15 ms at 256^2); in bf16 the materialised step is
-    3-8 % faster up to 64^2 (4096 tokens; both launch-bound, e.g. 0.137
-    against 0.133 ms) and the fused one from 96^2 on (0.36 against 0.70 ms at
-    256^2). K = 5: the materialised step wins at 32^2 (0.60 against 0.67 ms
-    FP32, 0.15 against 0.17 ms bf16), the fused one from 64^2 on (bf16 0.85
-    against 1.86 ms at 256^2). So: K <= 3 FP32 always fuses, 16-bit types
-    fuse above 4096 tokens; K = 5 fuses above 1024 tokens.
+    Measured on B200 with this library's kernels and the GEMM generator of the
+    materialised path (``bench.py --crossover``: B=1, C=64, square images,
+    CUDA-graph replays, L2 flushed): K = 3 FP32 fuses faster at every size
+    (0.170 against 0.186 ms at 32^2, 0.590 against 1.98 ms at 256^2); 16-bit
+    training is faster materialised up to 64^2 (4096 tokens: 0.137 against
+    0.129 ms bf16, both launch-bound) and fused from 96^2 on (0.350 against
+    0.459 ms at 256^2); K = 5 FP32 is faster materialised at 32^2 (0.277
+    against 0.252 ms) and fused from 64^2 on (3.58 against 4.86 ms at 256^2),
+    K = 5 bf16 ties at 64^2 and fuses faster from 128^2 on (0.78 against
+    1.10 ms at 256^2). So: 16-bit types fuse above 4096 tokens; FP32 always
+    at K <= 3 and above 1024 tokens at K = 5.
     """
-    if kernel_size > 3:
-        return tokens > 1024
-    return dtype == torch.float32 or tokens > 4096
+    if dtype != torch.float32:
+        return tokens > 4096
+    return kernel_size <= 3 or tokens > 1024
 
 
 # ------------------------------------------------------- weight packing ----
@@ -344,14 +345,84 @@ class _GeneratorDynamicCat(torch.autograd.Function):
         return grad_x, grad_y, gw, gb, None, None, None
 
 
+# ------------------------------------------------ materialised generator ----
+def _augmented(y: torch.Tensor) -> torch.Tensor:
+    """y as ``[N, k, H*W]`` with a constant-one channel at index C (the bias
+    column of the GEMM) and zero channels up to k = round8(C + 1)."""
+    n, c, h, w = y.shape
+    k = (c + 1 + 7) // 8 * 8
+    p = h * w
+    parts = [y.reshape(n, c, p), y.new_ones((n, 1, p))]
+    if k > c + 1:
+        parts.append(y.new_zeros((n, k - c - 1, p)))
+    return torch.cat(parts, 1)
+
+
+def _augmented_weight(weight: torch.Tensor, bias: torch.Tensor | None, k: int) -> torch.Tensor:
+    rows, c = weight.shape[0], weight.numel() // weight.shape[0]
+    parts = [weight.reshape(rows, c)]
+    parts.append(bias.reshape(rows, 1) if bias is not None else weight.new_zeros((rows, 1)))
+    if k > c + 1:
+        parts.append(weight.new_zeros((rows, k - c - 1)))
+    return torch.cat(parts, 1)
+
+
+def _generator_grads(grad, y, weight, ya, need_y, need_wb):
+    """dY = W^T grad and (dW | db) = grad . ya^T of the GEMM generator (the
+    per-sample products summed in FP32; one product for N = 1)."""
+    n, c = y.shape[0], y.shape[1]
+    rows = weight.shape[0]
+    gy = gwa = None
+    if need_y:
+        gy = torch.matmul(weight.reshape(rows, c).t(), grad).view_as(y)
+    if need_wb:
+        gwa = torch.matmul(grad, ya.transpose(1, 2))
+        acc = torch.float32 if grad.dtype in (torch.bfloat16, torch.float16) else grad.dtype
+        gwa = (gwa[0] if n == 1 else gwa.sum(0, dtype=acc)).to(grad.dtype)
+    return gy, gwa
+
+
+class _GeneratorGemm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, y, weight, bias):
+        ya = _augmented(y)
+        ctx.save_for_backward(y, weight, ya)
+        ctx.has_bias = bias is not None
+        return torch.matmul(_augmented_weight(weight, bias, ya.shape[1]), ya)
+
+    @staticmethod
+    def backward(ctx, grad):
+        y, weight, ya = ctx.saved_tensors
+        need_y, need_w, need_b = ctx.needs_input_grad
+        gy, gwa = _generator_grads(grad.contiguous(), y, weight, ya, need_y, need_w or need_b)
+        c = y.shape[1]
+        gw = gwa[:, :c].reshape(weight.shape) if need_w else None
+        gb = gwa[:, c].contiguous() if (need_b and ctx.has_bias) else None
+        return gy, gw, gb
+
+
+def generator_taps(y: torch.Tensor, weight: torch.Tensor,
+                   bias: torch.Tensor | None) -> torch.Tensor:
+    """The 1x1 generator convolution ``F.conv2d(y, weight, bias)`` of the
+    materialised path (reference ``triton_impl.py:340-347``) as one batched
+    GEMM on cuBLAS, ``[N, 3CK^2, H*W]``, with the bias folded in as a
+    constant-one input channel (one rounding of W.y + b, as in the fused
+    path); its backward is two GEMMs (dY = W^T dK; dW and db together from dK
+    times the augmented y). Measured on B200 at C=64, 128^2, K=5: forward
+    0.060 ms bf16 / 0.306 ms fp32 against 0.214 / 0.574 ms for the cuDNN
+    convolution, whose 1x1 kernel choice is an sm_75 one; backward 0.088 /
+    0.67 ms against 0.120 / 1.41 ms."""
+    return _GeneratorGemm.apply(y, weight, bias)
+
+
 def _k5_backward(ctx, grad_out):
     """Backward of the fused forward at K = 5, where dY + dW has no fused
     kernel (the 75 slots of a channel group do not fit the dY+dW kernel's
     tensor memory and x halo): dX by the fused recompute kernel
     (``ddpm_gencat_bwd_x_staged``: the taps never reach HBM), dK = shifted x *
     g_b written once by ``ddpm_dyncat_bwd`` (tap gradient only, no taps read),
-    and dY, dW, db from dK by the 1x1 convolution's backward (cuDNN GEMMs, as
-    the reference's materialised path, ``triton_impl.py:340-347``). Only
+    and dY, dW, db from dK by cuBLAS GEMMs (dY = W^T dK; dW and db together
+    from dK times the augmented y, whose constant-one channel gives db). Only
     (x, y, weight, bias) were saved, as in the fused path."""
     x, y, weight, bias = ctx.saved_tensors
     n, c, h, w = x.shape
@@ -369,9 +440,12 @@ def _k5_backward(ctx, grad_out):
             dk = torch.empty((n, rows, h, w), dtype=x.dtype, device=x.device)
             _lib.call("ddpm_dyncat_bwd", x.data_ptr(), code, None, grad_out.data_ptr(), code,
                       None, dk.data_ptr(), n, c, h, w, ks, d0, d1, d2, stream)
-            gy, gw, gb = torch.ops.aten.convolution_backward(
-                dk, y, weight.reshape(rows, c, 1, 1), [rows], [1, 1], [0, 0], [1, 1], False,
-                [0, 0], 1, [need_y, need_w, need_b])
+            gy, gwa = _generator_grads(dk.view(n, rows, h * w), y, weight,
+                                       _augmented(y) if (need_w or need_b) else None,
+                                       need_y, need_w or need_b)
+            if gwa is not None:
+                gw = gwa[:, :c].contiguous()
+                gb = gwa[:, c].contiguous()
             del dk
         if need_x:
             staged = ctx.staged

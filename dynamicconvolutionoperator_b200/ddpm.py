@@ -134,7 +134,7 @@ class DDPM(nn.Module):
             return _kernels.fused_generator_dynamic_cat(
                 x, y, weight, bias, self.kernel_size, self.dilations, _fuse_planes=fuse_planes,
             )
-        kernels = F.conv2d(y, weight, bias).reshape(
+        kernels = _kernels.generator_taps(y, weight, bias).reshape(
             x.shape[0],
             len(self.dilations),
             self.dim,
