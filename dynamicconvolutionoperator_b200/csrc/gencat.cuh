@@ -612,7 +612,7 @@ __device__ __forceinline__ void round_taps(float (&v)[16]) {
 
 // Host helpers (gencat_common.cu).
 int check_shape(int n, int c, int h, int w, int ks, int d0, int d1, int d2, int dt);
-// check_shape plus the backward kernels' limit K <= 3.
+// check_shape plus the dY + dW kernels' limit K <= 3.
 int check_shape_bwd(int n, int c, int h, int w, int ks, int d0, int d1, int d2, int dt);
 int status_ptr(int** out);
 int read_status(int reset, int* code);

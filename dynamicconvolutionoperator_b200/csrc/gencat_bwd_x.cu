@@ -8,7 +8,8 @@
 // The taps needed at q are the generator outputs at the SHIFTED pixel q - o.
 // Tile = 128 consecutive pixels of one image row (TMEM lane m <-> column
 // w0 + m). Work advances in units = (tile, branch b, kernel row ki): the y row
-// h - (ki - r) d_b, columns w0-8 .. w0+135, is staged once per unit in the
+// h - (ki - r) d_b, columns w0-8 .. w0+135 (w0-16 .. w0+143 at K = 5, whose
+// halos reach 16), is staged once per unit in the
 // K-major interleaved operand layout ([channel group][pixel][8]); pixel rows
 // are 16 bytes apart, so the operand of tap (ki, kj) is the staged segment
 // with the descriptor start moved by (8 - dx) pixels, and each (b, tap) chunk
@@ -47,7 +48,7 @@ namespace {
 
 using namespace gencat;
 
-// Staged pixels per row segment: 128 plus kSegOff on each side (8 for K <= 3,
+// Staged pixels per row segment: 128 plus seg_off(K) on each side (8 for K <= 3,
 // whose dilation halos reach 8 pixels; 16 for K = 5, halos up to 16).
 __host__ __device__ constexpr int seg_off(int ks) { return ks <= 3 ? 8 : 16; }
 __host__ __device__ constexpr int seg_px(int ks) { return kTileM + 2 * seg_off(ks); }

@@ -46,8 +46,7 @@ int check_shape_bwd(int n, int c, int h, int w, int ks, int d0, int d1, int d2, 
   const int rc = check_shape(n, c, h, w, ks, d0, d1, d2, dt);
   if (rc) return rc;
   if (ks > 3)
-    return set_error(DDPM_ERR_UNSUPPORTED, "fused generator backward supports K in {1, 3} (got %d)",
-                     ks);
+    return set_error(DDPM_ERR_UNSUPPORTED, "fused dY + dW supports K in {1, 3} (got %d)", ks);
   return DDPM_OK;
 }
 
