@@ -107,9 +107,10 @@ def fused_dynamic_cat(x, kernels, kernel_size, dilations):
 # padded channel count in shared memory and TMEM).
 FUSED_MAX_CHANNELS = 64
 # Kernel sizes of the fused forward, and of the fully fused (flash-style
-# recompute) backward kernels. At K = 5 the fused training path pairs the fused
-# forward and dX kernels with a materialised dK (``_k5_backward``); the
-# reference fuses training for K <= 3 only (``triton_impl.py:320``).
+# recompute) backward kernels in every dtype. At K = 5 the fused backward
+# kernels cover 16-bit data (``_fused_dyw_ok``); FP32 pairs the fused forward
+# and dX kernels with a materialised dK (``_k5_backward``). The reference
+# fuses training for K <= 3 only (``triton_impl.py:320``).
 FUSED_KERNEL_SIZES = (1, 3, 5)
 FUSED_TRAINING_KERNEL_SIZES = (1, 3)
 FUSED_BACKWARD_AVAILABLE = True
@@ -130,6 +131,22 @@ def fused_generator_supported(channels: int, kernel_size: int, dtype: torch.dtyp
     )
 
 
+# Largest dilation halo of the fused dY + dW kernel at K = 5: its x halo
+# (16 channels x (8 + 2R) rows x (16 + 2R) FP32 cells, 63 KB at R = 10) shares
+# shared memory with the operand rings.
+FUSED_DYW_MAX_HALO_K5 = 10
+
+
+def _fused_dyw_ok(kernel_size: int, dtype: torch.dtype, width: int, dilations) -> bool:
+    """Whether the fused dY + dW kernel covers this backward: K <= 3 always;
+    K = 5 for 16-bit data with halos up to 10 whose rows allow the gradient
+    tile's tensor map (W % 8 == 0). FP32 has no room for the wider K = 5 halo
+    beside its hi / lo operand rings."""
+    return kernel_size in FUSED_TRAINING_KERNEL_SIZES or (
+        kernel_size == 5 and dtype != torch.float32 and width % 8 == 0
+        and 2 * max(dilations) <= FUSED_DYW_MAX_HALO_K5)
+
+
 def fused_training_supported(kernel_size: int) -> bool:
     """Whether the fused generator path can train at this kernel size: K <= 3
     with the fully fused backward, K = 5 with the split one (fused dX,
@@ -145,18 +162,18 @@ def auto_fuse_training(tokens: int, channels: int, kernel_size: int, dtype: torc
     Measured on B200 with this library's kernels and the GEMM generator of the
     materialised path (``bench.py --crossover``: B=1, C=64, square images,
     CUDA-graph replays, L2 flushed): K = 3 FP32 fuses faster at every size
-    (0.170 against 0.186 ms at 32^2, 0.590 against 1.98 ms at 256^2); 16-bit
-    training is faster materialised up to 64^2 (4096 tokens: 0.137 against
-    0.129 ms bf16, both launch-bound) and fused from 96^2 on (0.350 against
-    0.459 ms at 256^2); K = 5 FP32 is faster materialised at 32^2 (0.277
-    against 0.252 ms) and fused from 64^2 on (3.58 against 4.86 ms at 256^2),
-    K = 5 bf16 ties at 64^2 and fuses faster from 128^2 on (0.78 against
-    1.10 ms at 256^2). So: 16-bit types fuse above 4096 tokens; FP32 always
-    at K <= 3 and above 1024 tokens at K = 5.
+    (0.170 against 0.186 ms at 32^2, 0.590 against 1.98 ms at 256^2); K = 3
+    16-bit training is faster materialised up to 64^2 (4096 tokens: 0.137
+    against 0.129 ms bf16, both launch-bound) and fused from 96^2 on (0.350
+    against 0.459 ms at 256^2); K = 5 is faster materialised at 32^2 (0.277
+    against 0.252 ms FP32, 0.160 against 0.150 ms bf16) and fused from 64^2
+    on (bf16 0.645 against 1.10 ms, FP32 3.58 against 4.87 ms at 256^2). So:
+    K <= 3 FP32 always fuses, K <= 3 16-bit types above 4096 tokens, K = 5
+    above 1024 tokens.
     """
-    if dtype != torch.float32:
-        return tokens > 4096
-    return kernel_size <= 3 or tokens > 1024
+    if kernel_size > 3:
+        return tokens > 1024
+    return dtype == torch.float32 or tokens > 4096
 
 
 # ------------------------------------------------------- weight packing ----
@@ -223,7 +240,8 @@ def _launch_gencat_fwd(x, y, packed, bias, kernel_size, dilations, staged=None,
             n, c, h, w, int(kernel_size), d0, d1, d2, code, stream,
         )
         setattr(out, FUSE_PLANES_ATTR, (planes, nbytes, out._version,
-                                        int(kernel_size) in FUSED_TRAINING_KERNEL_SIZES))
+                                        _fused_dyw_ok(int(kernel_size), x.dtype, w,
+                                                      _dil(dilations))))
         return out
     _lib.call(
         "ddpm_gencat_fwd_staged",
@@ -275,7 +293,15 @@ class _GeneratorDynamicCat(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad_out):
         if ctx.kernel_size not in FUSED_TRAINING_KERNEL_SIZES:
-            return _k5_backward(ctx, grad_out)
+            # K = 5: the fused dY + dW kernel where it applies (all three
+            # gradients, or dX alone), else dK materialised
+            x = ctx.saved_tensors[0]
+            need_x, need_y, need_w, need_b = ctx.needs_input_grad[:4]
+            some = need_y or need_w or need_b
+            fused = _fused_dyw_ok(ctx.kernel_size, x.dtype, x.shape[3], ctx.dilations) and (
+                (need_y and need_w and need_b) or not some)
+            if not fused:
+                return _k5_backward(ctx, grad_out)
         x, y, weight, bias = ctx.saved_tensors
         packed = ctx.packed
         n, c, h, w = x.shape
@@ -416,9 +442,10 @@ def generator_taps(y: torch.Tensor, weight: torch.Tensor,
 
 
 def _k5_backward(ctx, grad_out):
-    """Backward of the fused forward at K = 5, where dY + dW has no fused
-    kernel (the 75 slots of a channel group do not fit the dY+dW kernel's
-    tensor memory and x halo): dX by the fused recompute kernel
+    """Backward of the fused forward at K = 5 where the fused dY + dW kernel
+    does not apply (FP32, whose hi / lo operand rings leave no room for the
+    K = 5 halo; rows the gradient tile's tensor map cannot address; a subset of
+    the gradients): dX by the fused recompute kernel
     (``ddpm_gencat_bwd_x_staged``: the taps never reach HBM), dK = shifted x *
     g_b written once by ``ddpm_dyncat_bwd`` (tap gradient only, no taps read),
     and dY, dW, db from dK by cuBLAS GEMMs (dY = W^T dK; dW and db together

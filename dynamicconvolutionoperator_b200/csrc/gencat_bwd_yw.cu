@@ -45,11 +45,12 @@ constexpr int kDkBytes = kTileM * 128 * 2;  // one dK tile part (bf16 / fp16)
 // is padding (zero rows). gv[b][i] = the pair (g_b[2i], g_b[2i+1]) of this
 // pixel's 16-channel group, packed; products and conversions run on f32x2 /
 // bf16x2 pairs.
+// `cols`: cells per halo row (kHaloCols, or 16 + 2R for K = 5).
 template <typename T, typename Op, bool kSplit, int KS, int OCT, int J0 = 0, int JN = 8>
 __device__ __forceinline__ void build_octet(uint8_t* dk, const float4* xc, int xr_plane,
                                             const unsigned long long (&gv)[3][8],
                                             const int (&dil)[3], int m,
-                                            uint32_t lo_off = kDkBytes) {
+                                            uint32_t lo_off = kDkBytes, int cols = kHaloCols) {
   constexpr int KK = KS * KS;
   constexpr int r = KS / 2;
   const uint32_t base = (m >> 3) * 2048 + (m & 7) * 16;
@@ -61,7 +62,7 @@ __device__ __forceinline__ void build_octet(uint8_t* dk, const float4* xc, int x
     if (s < 3 * KK) {
       const int b = s / KK, tap = s % KK;
       const int dy = (tap / KS - r) * dil[b], dx = (tap % KS - r) * dil[b];
-      const float4* cell = xc + dy * kHaloCols + dx;
+      const float4* cell = xc + dy * cols + dx;
 #pragma unroll
       for (int q4 = 0; q4 < 4; ++q4) {
         const float4 v = cell[q4 * xr_plane];
@@ -94,26 +95,23 @@ __device__ __forceinline__ void build_dk(uint8_t* dk, int octet, const float4* x
 
 // Half of an octet (slots 4*half .. 4*half+3): two builder threads per pixel.
 // lo_off: bytes from a slot's hi part to its lo part (FP32).
-template <typename T, typename Op, bool kSplit, int KS>
+template <typename T, typename Op, bool kSplit, int KS, int O = 0>
 __device__ __forceinline__ void build_dk_half(uint8_t* dk, int octet, int half, const float4* xc,
                                               int xr_plane, const unsigned long long (&gv)[3][8],
                                               const int (&dil)[3], int m,
-                                              uint32_t lo_off = kDkBytes) {
-#define DDPM_BUILD_CASE(O, H)                                                           \
-  case O * 2 + H:                                                                       \
-    build_octet<T, Op, kSplit, KS, O, H * 4, 4>(dk, xc, xr_plane, gv, dil, m, lo_off);  \
-    break;
-  switch (octet * 2 + half) {
-    DDPM_BUILD_CASE(0, 0)
-    DDPM_BUILD_CASE(0, 1)
-    DDPM_BUILD_CASE(1, 0)
-    DDPM_BUILD_CASE(1, 1)
-    DDPM_BUILD_CASE(2, 0)
-    DDPM_BUILD_CASE(2, 1)
-    DDPM_BUILD_CASE(3, 0)
-    default: build_octet<T, Op, kSplit, KS, 3, 4, 4>(dk, xc, xr_plane, gv, dil, m, lo_off); break;
+                                              uint32_t lo_off = kDkBytes, int cols = kHaloCols) {
+  constexpr int kOct = (3 * KS * KS + 7) / 8;
+  if constexpr (O < kOct) {
+    if (octet == O || O == kOct - 1) {
+      if (half == 0)
+        build_octet<T, Op, kSplit, KS, O, 0, 4>(dk, xc, xr_plane, gv, dil, m, lo_off, cols);
+      else
+        build_octet<T, Op, kSplit, KS, O, 4, 4>(dk, xc, xr_plane, gv, dil, m, lo_off, cols);
+      return;
+    }
+    build_dk_half<T, Op, kSplit, KS, O + 1>(dk, octet, half, xc, xr_plane, gv, dil, m, lo_off,
+                                            cols);
   }
-#undef DDPM_BUILD_CASE
 }
 
 // g_b[cg16*16 + cl, pixel] for the three branches (zero off-image / c >= C).
@@ -729,8 +727,9 @@ __global__ void gencat_wreduce_kernel(const float* __restrict__ partial, T* __re
 // ========================================================== dY + dW ==========
 // One pass builds every dK tile once and feeds both GEMMs (the separate dY and
 // dW kernels above each build all of dK). CTA = (16-channel group cg, spatial
-// split): D_w of the cg's octets (<= 4 x Nw TMEM columns) accumulates over the
-// split's tiles; per tile, D_y (128 pixels x Cp, double buffered at columns
+// split; at K = 5 also an octet set: the cg's 10 octets in sets of <= 4): D_w
+// of the CTA's octets (<= 4 x Nw TMEM columns) accumulates over the split's
+// tiles; per tile, D_y (128 pixels x Cp, double buffered at columns
 // 384 / 448) holds the cg's share of dY and is added into an FP32 dY
 // accumulator with reductions to global memory (the other channel groups'
 // CTAs add theirs); the x-halo producer warps do that drain for the previous
@@ -779,6 +778,18 @@ struct DywSmem {
   uint32_t xr, y, dk, w, g, dyb, bars, total, xr_bytes, y_bytes, dk_bytes, w_bytes, g_bytes;
 };
 
+// x halo of the dY+dW kernel: `dyw_halo_cols` cells per row starting
+// `dyw_halo_off` columns left of the tile: 32 from w0 - 8 for K <= 3 (halos up
+// to 8); for K = 5 exactly the 16 + 2R columns its halo R needs (a 48-column
+// halo of 16 channels at R = 10 would not fit beside the operand rings).
+__host__ __device__ inline int dyw_halo_cols(int ks, int R) {
+  return ks <= 3 ? kHaloCols : 16 + 2 * R;
+}
+__host__ __device__ inline int dyw_halo_off(int ks, int R) { return ks <= 3 ? 8 : R; }
+// K = 5: a channel group's 10 octets of slots do not fit as D_w accumulators
+// (80 columns each) beside D_y in TMEM, so CTAs take sets of at most 4.
+constexpr int kDywSetOct = 4;
+
 // D_y drain buffers: one per TMEM lane quadrant (the drain warp's 32 pixels =
 // 2 rows x 16 columns), 8 channels at a time: [8 ch][2 rows][16 px] FP32.
 constexpr uint32_t kDyChunkBytes = 8 * 2 * 16 * 4;
@@ -792,7 +803,7 @@ template <typename T, int KS, bool kGTma = false, bool kLoRing = false>
 __host__ __device__ inline DywSmem dyw_smem_layout(int Cp, int Nw, int R, int nx) {
   using Cfg = DywCfg<T, KS, false, kGTma, kLoRing>;
   DywSmem L;
-  L.xr_bytes = (uint32_t)16 * (kTileH + 2 * R) * kHaloCols * 4;
+  L.xr_bytes = (uint32_t)16 * (kTileH + 2 * R) * dyw_halo_cols(KS, R) * 4;
   L.y_bytes = (uint32_t)Cfg::kParts * kTileM * Nw * 2;
   // lo ring: dk_bytes / w_bytes are one part; the lo buffer follows the hi slots
   L.dk_bytes = (uint32_t)(kLoRing ? 1 : Cfg::kParts) * kDkBytes;
@@ -820,6 +831,7 @@ struct DywParams {
   int d[3];
   int tiles_w, tiles_h, num_tiles;
   int ngroups, ncg, splits;
+  int nsets;          // octet sets per channel group (K = 5: 3 sets of <= 4 octets)
   int nx;             // x-halo buffers (1 or 2)
   // grad_out channel-last [N][H][W][4C] (kGTma only): gmap {C, 4, W, H, N}, box
   // {16, 3, 16, 8, 1}, landing as [8 rows][16 px][3 branches][16 channels]
@@ -913,7 +925,12 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
   const size_t P = (size_t)H * W;
   const DywSmem L = dyw_smem_layout<T, KS, kGTma, kLoRing>(Cp, Nw, R, NX);
   const int cg = blockIdx.x % p.ncg;
-  const int split = blockIdx.x / p.ncg;
+  const int oset = (blockIdx.x / p.ncg) % p.nsets;
+  const int split = blockIdx.x / (p.ncg * p.nsets);
+  // this CTA's octets of the channel group (all of them for K <= 3)
+  const int oct0 = p.nsets == 1 ? 0 : oset * kDywSetOct;
+  const int oct1 = p.nsets == 1 ? NOCT : min(oct0 + kDywSetOct, NOCT);
+  const int xcols = dyw_halo_cols(KS, R), xoff = dyw_halo_off(KS, R);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint64_t* x_full = bars;             // [2] (NX used)
   uint64_t* x_empty = x_full + 2;      // [2]
@@ -931,7 +948,7 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
   uint64_t* lo_full = g_empty + 1;     // [1] (kLoRing: the lo buffer)
   uint64_t* lo_empty = lo_full + 1;    // [1]
   const int xr_rows = kTileH + 2 * R;
-  const int xr_plane = xr_rows * kHaloCols;
+  const int xr_plane = xr_rows * xcols;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
@@ -984,7 +1001,7 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
       constexpr int kLoads = kLoRing ? 2 : 1;
       const size_t w_group = (size_t)Cfg::kParts * 128 * Cp * 2;
       for (int tile = split; tile < p.num_tiles; tile += p.splits) {
-        for (int oct = 0; oct < NOCT; ++oct) {
+        for (int oct = oct0; oct < oct1; ++oct) {
           for (int part = 0; part < kLoads; ++part, ++wq) {
             const int s = wq % S;
             if (!tc::mbar_wait(&w_empty[s], ((wq / S) & 1) ^ 1, abort_flag, kWaitNs)) {
@@ -1019,7 +1036,7 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
           // per octet: lo * W_hi, release lo; hi * W_hi; hi * W_lo
           const uint64_t lo_d =
               tc::smem_desc(tc::smem_u32(smem + L.dk + 2 * kDkBytes), 128, 2048);
-          for (int oct = 0; oct < NOCT; ++oct, ++kq) {
+          for (int oct = oct0; oct < oct1; ++oct, ++kq) {
             const int hb = kq & 1;
             const int s_hi = wq % S;
             if (!tc::mbar_wait(&k_full[hb], (kq >> 1) & 1, abort_flag, kWaitNs) ||
@@ -1035,7 +1052,7 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks)
               tc::mma_f16(dt, lo_d + ks * (256 >> 4), bh + ks * b_step, idesc,
-                          (oct > 0 || ks > 0) ? 1u : 0u);
+                          (oct > oct0 || ks > 0) ? 1u : 0u);
             tc::mma_commit(lo_empty);
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks)
@@ -1059,7 +1076,7 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
           tc::mma_commit(&d_full[tb]);
           continue;
         }
-        for (int oct = 0; oct < NOCT; ++oct, ++wq, ++kq) {
+        for (int oct = oct0; oct < oct1; ++oct, ++wq, ++kq) {
           const int s = wq % S, ks_ = kq % NS;
           if (!tc::mbar_wait(&k_full[ks_], (kq / NS) & 1, abort_flag, kWaitNs) ||
               !tc::mbar_wait(&w_full[s], (wq / S) & 1, abort_flag, kWaitNs)) {
@@ -1075,7 +1092,7 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
           for (int ks = 0; ks < 8; ++ks) {
             const uint64_t a_k = ad + ks * (256 >> 4);
             const uint64_t b_k = bd + ks * b_step;
-            tc::mma_f16(dt, a_k, b_k, idesc, (oct > 0 || ks > 0) ? 1u : 0u);
+            tc::mma_f16(dt, a_k, b_k, idesc, (oct > oct0 || ks > 0) ? 1u : 0u);
             if constexpr (Cfg::kSplit) {
               tc::mma_f16(dt, a_k + (kDkBytes >> 4), b_k, idesc, 1u);
               tc::mma_f16(dt, a_k, b_k + b_lo, idesc, 1u);
@@ -1112,7 +1129,7 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
           // per octet: lo * y_hi, release lo; hi * y_hi + hi * y_lo
           const uint64_t lo_d =
               tc::smem_desc(tc::smem_u32(smem + L.dk + 2 * kDkBytes), 2048, 128);
-          for (int oct = 0; oct < NOCT; ++oct, ++kq) {
+          for (int oct = oct0; oct < oct1; ++oct, ++kq) {
             const int hb = kq & 1;
             if (!tc::mbar_wait(&k_full[hb], (kq >> 1) & 1, abort_flag, kWaitNs) ||
                 !tc::mbar_wait(lo_full, kq & 1, abort_flag, kWaitNs)) {
@@ -1122,7 +1139,7 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
             tc::tc_fence_after();
             const uint64_t hi_d =
                 tc::smem_desc(tc::smem_u32(smem + L.dk + hb * kDkBytes), 2048, 128);
-            const uint32_t dt = tmem_base + oct * Nw;
+            const uint32_t dt = tmem_base + (oct - oct0) * Nw;
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks)
               tc::mma_f16(dt, lo_d + ks * ((2 * 2048) >> 4), yd + ks * b_step, idesc,
@@ -1141,7 +1158,7 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
           first = false;
           continue;
         }
-        for (int oct = 0; oct < NOCT; ++oct, ++kq) {
+        for (int oct = oct0; oct < oct1; ++oct, ++kq) {
           const int ks_ = kq % NS;
           if (!tc::mbar_wait(&k_full[ks_], (kq / NS) & 1, abort_flag, kWaitNs)) {
             fail(abort_flag, p.status, 54);
@@ -1151,7 +1168,7 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
           // A: dK, MN-major (rows are M, pixels are K): K-group stride 2048, M-group 128
           const uint64_t ad =
               tc::smem_desc(tc::smem_u32(smem + L.dk + ks_ * L.dk_bytes), 2048, 128);
-          const uint32_t dt = tmem_base + oct * Nw;
+          const uint32_t dt = tmem_base + (oct - oct0) * Nw;
 #pragma unroll
           for (int ks = 0; ks < 8; ++ks) {
             const uint64_t a_k = ad + ks * ((2 * 2048) >> 4);
@@ -1196,7 +1213,7 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
         // columns w0-8 .. w0+23 (x in 8-byte units), rows h0-R .., quads 4cg .. 4cg+3
         if (pt == 0) {
           tc::mbar_arrive_expect_tx(&x_full[xb], L.xr_bytes);
-          tc::tma_load_4d(xr, &maps.xmap, (w0 - 8) * 2, h0 - R, cg * 4, n, &x_full[xb]);
+          tc::tma_load_4d(xr, &maps.xmap, (w0 - xoff) * 2, h0 - R, cg * 4, n, &x_full[xb]);
         } else {
           tc::mbar_arrive(&x_full[xb]);
         }
@@ -1363,8 +1380,8 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
         break;
       }
       const float4* xc = reinterpret_cast<const float4*>(smem + L.xr + xb * L.xr_bytes) +
-                         (mr + R) * kHaloCols + (mc + 8);
-      for (int oct = 0; oct < NOCT; ++oct, ++kq) {
+                         (mr + R) * xcols + (mc + xoff);
+      for (int oct = oct0; oct < oct1; ++oct, ++kq) {
         const int ks_ = kq % NS;
         if (!warp_wait(&k_empty[ks_], ((kq / NS) & 1) ^ 1, abort_flag) ||
             (kLoRing && !warp_wait(lo_empty, (kq & 1) ^ 1, abort_flag))) {
@@ -1375,7 +1392,7 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
         // lo ring: hi part in slot ks_, lo part in the buffer after both slots
         const uint32_t lo_off = kLoRing ? (uint32_t)(2 - ks_) * kDkBytes : (uint32_t)kDkBytes;
         build_dk_half<T, Op, Cfg::kSplit, KS>(smem + L.dk + ks_ * L.dk_bytes, oct, half, xc,
-                                              xr_plane, gv, dil, m, lo_off);
+                                              xr_plane, gv, dil, m, lo_off, xcols);
         tc::fence_proxy_async_smem();
         tc::mbar_arrive(&k_full[ks_]);
         if constexpr (kLoRing) tc::mbar_arrive(lo_full);
@@ -1386,12 +1403,12 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
     // D_w of this CTA's split: lane = weight row, half h drains octets 2h, 2h+1
     if (!failed && warp_wait(w_done, 0, abort_flag)) {
       tc::tc_fence_after();
-      for (int oct = 2 * half; oct < 2 * half + 2 && oct < NOCT; ++oct) {
-        const int g = cg * NOCT + oct;
+      for (int lo = 2 * half; lo < 2 * half + 2 && oct0 + lo < oct1; ++lo) {
+        const int g = cg * NOCT + oct0 + lo;
         float* dst = p.partial + (((size_t)split * p.ngroups + g) * 128 + m) * Nw;
         for (int c0 = 0; c0 < Nw; c0 += 16) {
           float dv[16];
-          tc::tmem_ld16(tmem_base + ((uint32_t)(quad * 32) << 16) + oct * Nw + c0, dv);
+          tc::tmem_ld16(tmem_base + ((uint32_t)(quad * 32) << 16) + lo * Nw + c0, dv);
           tc::tmem_ld_wait();
 #pragma unroll
           for (int k = 0; k < 16; k += 4)
@@ -1501,7 +1518,7 @@ WPlan plan_w(int n, int c, int h, int w, int ks) {
 // Merged dY + dW pass: CTAs = channel groups x splits; workspace = D_w partials,
 // then (16-bit dY only) the FP32 dY accumulator at a 256-byte aligned offset.
 struct DywPlan {
-  int Nw, ncg, splits;
+  int Nw, ncg, nsets, splits;  // CTAs = ncg x nsets x splits
   size_t partial_bytes, acc_offset, ws_bytes;  // ws_bytes includes the accumulator
 };
 
@@ -1510,9 +1527,11 @@ DywPlan plan_dyw(int n, int c, int h, int w, int ks) {
   DywPlan q;
   q.Nw = gencat::augmented_channels(c);
   q.ncg = pl.Cp / 16;
+  const int noct = (3 * ks * ks + 7) / 8;
+  q.nsets = ks <= 3 ? 1 : (noct + kDywSetOct - 1) / kDywSetOct;
   const int tiles = n * ((h + gencat::kTileH - 1) / gencat::kTileH) *
                     ((w + gencat::kTileW - 1) / gencat::kTileW);
-  int sp = num_sms() / q.ncg;
+  int sp = num_sms() / (q.ncg * q.nsets);
   if (sp < 1) sp = 1;
   if (sp > tiles) sp = tiles;
   q.splits = sp;
@@ -1528,7 +1547,7 @@ int launch_dyw_k(const DywParams& prm, const DywMaps& maps, cudaStream_t st) {
   const DywSmem L = dyw_smem_layout<T, KS, kGTma, kLoRing>(prm.Cp, prm.Nw, prm.R, prm.nx);
   auto fn = gencat_bwd_dyw_kernel<T, KS, kStaged, kGTma, kLoRing>;
   DDPM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total));
-  fn<<<prm.ncg * prm.splits, Cfg::kThreads, L.total, st>>>(prm, maps);
+  fn<<<prm.ncg * prm.nsets * prm.splits, Cfg::kThreads, L.total, st>>>(prm, maps);
   DDPM_CHECK_LAUNCH("gencat_bwd_dyw_kernel");
   return DDPM_OK;
 }
@@ -1553,12 +1572,15 @@ int launch_dyw(DywParams prm, const DywMaps& maps, bool staged, bool g_tma, cuda
       return launch_dyw_k<T, KS, true, false, true>(prm, maps, st);
     }
   }
-  for (int nx = kMaxX; nx >= 1; --nx)
-    if ((int)dyw_smem_layout<T, KS>(prm.Cp, prm.Nw, prm.R, nx).total <= lim) {
-      prm.nx = nx;
-      return staged ? launch_dyw_k<T, KS, true, false>(prm, maps, st)
-                    : launch_dyw_k<T, KS, false, false>(prm, maps, st);
-    }
+  if constexpr (KS <= 3) {
+    for (int nx = kMaxX; nx >= 1; --nx)
+      if ((int)dyw_smem_layout<T, KS>(prm.Cp, prm.Nw, prm.R, nx).total <= lim) {
+        prm.nx = nx;
+        return staged ? launch_dyw_k<T, KS, true, false>(prm, maps, st)
+                      : launch_dyw_k<T, KS, false, false>(prm, maps, st);
+      }
+  }
+  // K = 5 runs only with staged operands and the gradient tile by TMA
   return set_error(DDPM_ERR_UNSUPPORTED, "dY+dW tile does not fit in shared memory");
 }
 
@@ -1580,8 +1602,10 @@ int finish_dyw(const DywParams& prm, void* gy, void* gw, void* gb, int c, int ks
 }  // namespace
 
 size_t gencat_bwd_workspace_bytes(int n, int c, int h, int w, int ks) {
-  if (n < 1 || c < 1 || c > gencat::kMaxChannels || h < 1 || w < 1 || (ks != 1 && ks != 3))
+  if (n < 1 || c < 1 || c > gencat::kMaxChannels || h < 1 || w < 1 ||
+      (ks != 1 && ks != 3 && ks != 5))
     return 0;
+  if (ks == 5) return plan_dyw(n, c, h, w, ks).ws_bytes;  // the merged pass only
   const size_t a = plan_w(n, c, h, w, ks).ws_bytes;
   const size_t b = plan_dyw(n, c, h, w, ks).ws_bytes;
   return a > b ? a : b;
@@ -1593,8 +1617,16 @@ int gencat_bwd_yw(const void* x, const void* y, const void* staged, size_t stage
                   const void* wpack, const void* gout, void* gy, void* gw, void* gb,
                   void* workspace, size_t ws_bytes, int n, int c, int h, int w, int ks, int d0,
                   int d1, int d2, int dt, cudaStream_t st, int g_nhwc) {
-  int rc = gencat::check_shape_bwd(n, c, h, w, ks, d0, d1, d2, dt);
+  // K = 5: the merged pass with staged operands, 16-bit data (the gradient tile
+  // by TMA; FP32's hi / lo operand rings leave no room for its wider halo)
+  int rc = ks == 5 ? gencat::check_shape(n, c, h, w, ks, d0, d1, d2, dt)
+                   : gencat::check_shape_bwd(n, c, h, w, ks, d0, d1, d2, dt);
   if (rc) return rc;
+  if (ks == 5 && (dt == DDPM_F32 || staged == nullptr || gy == nullptr || gw == nullptr ||
+                  gb == nullptr || workspace == nullptr || 2 * max3(d0, d1, d2) > 10))
+    return set_error(DDPM_ERR_UNSUPPORTED,
+                     "fused dY + dW at K = 5 needs 16-bit data, staged operands, all three "
+                     "gradients, the workspace and a dilation halo <= 10");
   DDPM_CHECK_ARG(((x && y) || staged) && wpack && gout, "null pointer");
   if (g_nhwc && (c != 64 || staged == nullptr))
     return set_error(DDPM_ERR_UNSUPPORTED,
@@ -1648,13 +1680,15 @@ int gencat_bwd_yw(const void* x, const void* y, const void* staged, size_t stage
       dp.ngroups = pl.NG;
       dp.ncg = q.ncg;
       dp.splits = q.splits;
+      dp.nsets = q.nsets;
       dp.status = status;
       bool use_staged = false, g_tma = false;
       DywMaps maps{};
       if (staged != nullptr) {
         const gencat::StageLayout sl = gencat::StageLayout::make(n, c, h, w, ks, d0, d1, d2, dt);
         use_staged = gencat::encode_stage_maps(&maps.xmap, &maps.ymap, R, sl.G,
-                                               static_cast<const uint8_t*>(staged), sl);
+                                               static_cast<const uint8_t*>(staged), sl,
+                                               dyw_halo_cols(ks, R));
         maps.ph = sl.ph;
         maps.pw = sl.pw;
         // gradient tiles by TMA (16-bit) when the row pitch and base allow a map
@@ -1714,6 +1748,18 @@ int gencat_bwd_yw(const void* x, const void* y, const void* staged, size_t stage
         case DDPM_F16 * 10 + 3: rc = launch_dyw<__half, 3>(dp, maps, use_staged, g_tma, st); break;
         case DDPM_F32 * 10 + 1: rc = launch_dyw<float, 1>(dp, maps, use_staged, g_tma, st); break;
         case DDPM_F32 * 10 + 3: rc = launch_dyw<float, 3>(dp, maps, use_staged, g_tma, st); break;
+        case DDPM_BF16 * 10 + 5:
+          rc = use_staged && g_tma ? launch_dyw<__nv_bfloat16, 5>(dp, maps, true, true, st)
+                                   : set_error(DDPM_ERR_UNSUPPORTED,
+                                               "fused dY + dW at K = 5 needs the gradient tile "
+                                               "by TMA (16-byte aligned rows)");
+          break;
+        case DDPM_F16 * 10 + 5:
+          rc = use_staged && g_tma ? launch_dyw<__half, 5>(dp, maps, true, true, st)
+                                   : set_error(DDPM_ERR_UNSUPPORTED,
+                                               "fused dY + dW at K = 5 needs the gradient tile "
+                                               "by TMA (16-byte aligned rows)");
+          break;
         default: rc = set_error(DDPM_ERR_UNSUPPORTED, "unsupported dtype/kernel size");
       }
       if (rc) return rc;

@@ -268,8 +268,9 @@ def test_training_step_hands_the_generator_a_channel_last_gradient(dtype, monkey
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 def test_k5_training_takes_the_fused_forward_and_dx(dtype, monkeypatch):
     """K = 5 training through the fused path: the fused forward (writing the
-    fuse conv's planes), the fused dX kernel, dK from the filter backward
-    (tap gradient only) and an NCHW gradient of the generator output; every
+    fuse conv's planes) and the fused dX kernel; for bf16 the fused dY + dW
+    kernel with a channel-last gradient of the generator output, for FP32 dK
+    from the filter backward (tap gradient only) and an NCHW gradient; every
     gradient within the oracle's tolerance."""
     from dynamicconvolutionoperator_b200 import _lib
 
@@ -284,8 +285,12 @@ def test_k5_training_takes_the_fused_forward_and_dx(dtype, monkeypatch):
     stats, fails = ddpm_parity((1, 64, 40, 48), 5, dtype, seed=62, input_seed=63,
                                fused_generator_training=True)
     _assert_ok(stats, fails)
-    assert {"ddpm_gencat_fwd_staged_planes", "ddpm_gencat_bwd_x_staged",
-            "ddpm_dyncat_bwd"} <= set(calls), calls
-    assert not any(n.endswith("_nhwc") for n in calls), calls
-    assert "ddpm_dyncat_fwd" not in calls, calls
+    assert "ddpm_gencat_fwd_staged_planes" in calls and "ddpm_dyncat_fwd" not in calls, calls
+    if dtype == torch.float32:
+        assert {"ddpm_gencat_bwd_x_staged", "ddpm_dyncat_bwd"} <= set(calls), calls
+        assert not any(n.endswith("_nhwc") for n in calls), calls
+    else:
+        assert {"ddpm_fuseconv_bwd_nhwc", "ddpm_gencat_bwd_x_staged_nhwc",
+                "ddpm_gencat_bwd_yw_staged_nhwc"} <= set(calls), calls
+        assert "ddpm_dyncat_bwd" not in calls, calls
 

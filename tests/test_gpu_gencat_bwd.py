@@ -277,8 +277,8 @@ def test_channel_last_grad_out_matches_nchw(shape, ks, dtype):
 def test_k5_bwd_x_channel_last_and_max_halo(dtype):
     """K = 5 dX: the channel-last entry point matches the NCHW one bit for bit,
     and the largest halo (16, dilations (1, 8, 4)) matches the oracle on a
-    shape whose rows span two 128-pixel tiles; dY + dW at K = 5 is not a fused
-    entry point (DDPM_ERR_UNSUPPORTED before any launch)."""
+    shape whose rows span two 128-pixel tiles; the fused dY + dW kernel covers
+    K = 5 halos up to 10 only (DDPM_ERR_UNSUPPORTED before any launch)."""
     from dynamicconvolutionoperator_b200 import _kernels, _lib
 
     shape, ks, dil = (1, 64, 13, 150), 5, (1, 8, 4)
@@ -360,4 +360,56 @@ def test_channel_last_dyw_many_tiles_per_cta(dtype):
         for got, ref in zip(res[name], res["unstaged"]):
             scale = ref.abs().max().item()
             assert (got - ref).abs().max().item() <= 2e-2 * scale, name
+
+
+@pytest.mark.parametrize("shape", [(1, 64, 40, 48), (2, 24, 17, 40), (1, 64, 24, 136)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_k5_fused_dyw_matches_oracle(shape, dtype):
+    """K = 5 fused dY + dW (16-bit, staged, gradient tile by TMA; octet sets
+    of <= 4 per CTA, 36-column x halo at halo 10) against the float64 oracle,
+    through the NCHW entry and, at C = 64, the channel-last one."""
+    from dynamicconvolutionoperator_b200 import _kernels, _lib
+
+    ks, dil = 5, (1, 3, 5)
+    x, y, wt, b = _case(shape, ks, dtype, seed=41)
+    n, c, h, w = shape
+    g = torch.randn((n, 4 * c, h, w), generator=torch.Generator().manual_seed(42)).to(dtype)
+    _, gy_gold, gw_gold, gb_gold = _gold_grads(x, y, wt, b, g, ks, dil)
+    xd, yd, wd, bd, gd = x.cuda(), y.cuda(), wt.cuda(), b.cuda(), g.cuda()
+    packed = _kernels.pack_generator_weight(wd, bd, c, ks)
+    st, nb = _stage(xd, yd, ks, dil)
+    code = _lib.dtype_code(dtype)
+    stream = _lib.stream_handle(xd.device)
+    ws_bytes = int(_lib.load().ddpm_gencat_bwd_workspace_bytes(n, c, h, w, ks))
+    assert ws_bytes > 0
+    variants = [("", gd)] + ([("_nhwc", gd.contiguous(memory_format=torch.channels_last))]
+                             if c == 64 else [])
+    for sfx, gg in variants:
+        gy = torch.full_like(yd, float("nan"))
+        gw = torch.full((3 * c * ks * ks, c), float("nan"), dtype=dtype, device="cuda")
+        gb = torch.full((3 * c * ks * ks,), float("nan"), dtype=dtype, device="cuda")
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+        _lib.call("ddpm_gencat_bwd_yw_staged" + sfx, st.data_ptr(), nb, packed.data_ptr(),
+                  gg.data_ptr(), gy.data_ptr(), gw.data_ptr(), gb.data_ptr(), ws.data_ptr(),
+                  ws_bytes, n, c, h, w, ks, *dil, code, stream)
+        torch.cuda.synchronize()
+        for got, ref in ((gy, gy_gold), (gw.view(-1, c, 1, 1), gw_gold), (gb, gb_gold)):
+            scale = max(ref.abs().max().item(), 1.0)
+            assert (got.double().cpu() - ref).abs().max().item() <= 3e-2 * scale, sfx
+
+
+def test_k5_fused_dyw_limits():
+    """FP32, unstaged operands and halos above 10 are not fused dY + dW
+    shapes at K = 5 (DDPM_ERR_UNSUPPORTED before any launch)."""
+    from dynamicconvolutionoperator_b200 import _kernels, _lib
+
+    lib = _lib.load()
+    for code in (0,):
+        rc = lib.ddpm_gencat_bwd_yw_staged(1, 1 << 20, 1, 1, 1, 1, 1, 1, 1 << 20,
+                                           1, 64, 16, 16, 5, 1, 3, 5, code, None)
+        assert rc == -2
+    assert not _kernels._fused_dyw_ok(5, torch.bfloat16, 48, (1, 6, 4))
+    assert _kernels._fused_dyw_ok(5, torch.bfloat16, 48, (1, 3, 5))
+    assert not _kernels._fused_dyw_ok(5, torch.bfloat16, 44, (1, 3, 5))
+    assert not _kernels._fused_dyw_ok(5, torch.float32, 48, (1, 3, 5))
 
