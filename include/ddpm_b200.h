@@ -109,7 +109,9 @@ DDPM_API int ddpm_dyncat_bwd(const void* x, int x_dtype,
  * aligned) and pass it to every fused launch that uses that weight.
  * Limits of this build: C <= 64; K in {1, 3} with dilation halos
  * (K/2)*max(d) <= 8, or K = 5 with halos <= 16 (the forward and dX entry
- * points; the dY + dW entry points cover K in {1, 3}); other sizes return
+ * points; the dY + dW entry points cover K = 5 for 16-bit data through the
+ * staged merged pass, halos <= 10, rows of a multiple of 8 pixels); other
+ * sizes return
  * DDPM_ERR_UNSUPPORTED (callers then take the materialised path).
  */
 DDPM_API size_t ddpm_gencat_pack_bytes(int c, int ksize, int dtype);
