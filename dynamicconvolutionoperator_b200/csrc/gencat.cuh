@@ -475,6 +475,43 @@ template <> __device__ __forceinline__ unsigned long long uncvt2<__half>(uint32_
   return f2_pack(f.x, f.y);
 }
 
+// acc (two FP32 lanes) += a * b per lane, where a and b each hold two Op
+// values (first value in bits 0-15): one mixed-precision FMA per lane
+// (`fma.rn.f32.bf16` / `.f16`, 16-bit multiplicands, FP32 addend and result),
+// so no conversion of a or b to FP32 is issued. Fused with one rounding, like
+// fmaf(float(a), float(b), acc): the same result bit for bit.
+template <typename Op>
+__device__ __forceinline__ unsigned long long fma_io2(uint32_t a, uint32_t b,
+                                                      unsigned long long acc);
+template <>
+__device__ __forceinline__ unsigned long long fma_io2<__nv_bfloat16>(uint32_t a, uint32_t b,
+                                                                     unsigned long long acc) {
+  float lo, hi;
+  f2_unpack(acc, lo, hi);
+  asm("{\n\t.reg .b16 al, ah, bl, bh;\n\t"
+      "mov.b32 {al, ah}, %2;\n\t"
+      "mov.b32 {bl, bh}, %3;\n\t"
+      "fma.rn.f32.bf16 %0, al, bl, %0;\n\t"
+      "fma.rn.f32.bf16 %1, ah, bh, %1;\n\t}"
+      : "+f"(lo), "+f"(hi)
+      : "r"(a), "r"(b));
+  return f2_pack(lo, hi);
+}
+template <>
+__device__ __forceinline__ unsigned long long fma_io2<__half>(uint32_t a, uint32_t b,
+                                                              unsigned long long acc) {
+  float lo, hi;
+  f2_unpack(acc, lo, hi);
+  asm("{\n\t.reg .b16 al, ah, bl, bh;\n\t"
+      "mov.b32 {al, ah}, %2;\n\t"
+      "mov.b32 {bl, bh}, %3;\n\t"
+      "fma.rn.f32.f16 %0, al, bl, %0;\n\t"
+      "fma.rn.f32.f16 %1, ah, bh, %1;\n\t}"
+      : "+f"(lo), "+f"(hi)
+      : "r"(a), "r"(b));
+  return f2_pack(lo, hi);
+}
+
 // Eight floats, held as four packed pairs, stored as one 16-byte operand row;
 // with kSplit also the residual (v - hi) row at dst_lo (exact subtraction).
 template <typename Op, bool kSplit>

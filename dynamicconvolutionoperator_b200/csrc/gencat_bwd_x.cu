@@ -53,29 +53,6 @@ using namespace gencat;
 __host__ __device__ constexpr int seg_off(int ks) { return ks <= 3 ? 8 : 16; }
 __host__ __device__ constexpr int seg_px(int ks) { return kTileM + 2 * seg_off(ks); }
 
-// Sixteen 16-bit values (two 16-byte vectors, element 0 in the low half of the
-// first word) as floats; FP32 instances never take this path.
-template <typename T>
-__device__ __forceinline__ void unpack16(const uint4& a, const uint4& b, float (&v)[16]) {
-  if constexpr (sizeof(T) == 2) {
-    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-        v[2 * i] = __uint_as_float(w[i] << 16);
-        v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
-      } else {
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
-        v[2 * i] = f.x;
-        v[2 * i + 1] = f.y;
-      }
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = 0.f;
-  }
-}
-
 template <typename T, int KS, bool kStaged = false>
 struct BxCfg {
   static constexpr bool kSplit = IoTraits<T>::kSplit;
@@ -540,36 +517,42 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
               tc::tc_fence_after();
               if (blk_ok) tc::tmem_ld16(tcol + (tn % NB) * Cp, dv[cur ^ 1]);
             }
-            if (blk_ok) {
+            if constexpr (kNhwc && sizeof(T) == 2) {
+              if (blk_ok) {
+                // 16-bit channel-last: the block's channels are chunks 2wg and
+                // 2wg+1 (8 each) of swizzled pixel row m + kOff - dx (chunk j
+                // of row r at j ^ (r & 7)); each word of two gradient values
+                // meets the matching pair of rounded taps in two
+                // mixed-precision FMAs (no conversion of either to FP32)
+                const int pr = m + kOff - (kj - r) * d;
+                const uint8_t* row = reinterpret_cast<const uint8_t*>(gs) + pr * 128;
+                const uint4 v0 = *reinterpret_cast<const uint4*>(row + (((2 * wg) ^ (pr & 7)) * 16));
+                const uint4 v1 =
+                    *reinterpret_cast<const uint4*>(row + (((2 * wg + 1) ^ (pr & 7)) * 16));
+                const uint32_t gw[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                  acc2[i] = fma_io2<Op>(cvt2<Op>(dv[cur][2 * i], dv[cur][2 * i + 1]), gw[i], acc2[i]);
+              }
+            } else if (blk_ok) {
               const int dx = (kj - r) * d;
               float gv[16];
               if constexpr (kNhwc) {
-                // pixel row m + kOff - dx of the swizzled [kSeg][128 bytes]
-                // segment(s): this block's channel chunks, chunk j of row r at
-                // j ^ (r & 7)
+                // FP32 (16-bit takes the branch above): pixel row m + kOff - dx
+                // of the swizzled [kSeg][128 bytes] segments; box wg / 2 holds
+                // channels 32 (wg / 2) .. +31, the block's 16 channels are its
+                // chunks 4 (wg % 2) .. +3, chunk j of row r at j ^ (r & 7)
                 const int pr = m + kOff - dx;
-                if constexpr (sizeof(T) == 4) {
-                  // FP32: box wg / 2 holds channels 32 (wg / 2) .. +31; the
-                  // block's 16 channels are chunks 4 (wg % 2) .. +3
-                  const uint8_t* row = reinterpret_cast<const uint8_t*>(gs) +
-                                       (wg >> 1) * kSeg * 128 + pr * 128;
+                const uint8_t* row = reinterpret_cast<const uint8_t*>(gs) +
+                                     (wg >> 1) * kSeg * 128 + pr * 128;
 #pragma unroll
-                  for (int k = 0; k < 4; ++k) {
-                    const float4 v = *reinterpret_cast<const float4*>(
-                        row + ((((wg & 1) * 4 + k) ^ (pr & 7)) * 16));
-                    gv[4 * k] = v.x;
-                    gv[4 * k + 1] = v.y;
-                    gv[4 * k + 2] = v.z;
-                    gv[4 * k + 3] = v.w;
-                  }
-                } else {
-                  // 16-bit: chunks 2wg and 2wg+1 (8 channels each)
-                  const uint8_t* row = reinterpret_cast<const uint8_t*>(gs) + pr * 128;
-                  const uint4 v0 =
-                      *reinterpret_cast<const uint4*>(row + (((2 * wg) ^ (pr & 7)) * 16));
-                  const uint4 v1 =
-                      *reinterpret_cast<const uint4*>(row + (((2 * wg + 1) ^ (pr & 7)) * 16));
-                  unpack16<T>(v0, v1, gv);
+                for (int k = 0; k < 4; ++k) {
+                  const float4 v = *reinterpret_cast<const float4*>(
+                      row + ((((wg & 1) * 4 + k) ^ (pr & 7)) * 16));
+                  gv[4 * k] = v.x;
+                  gv[4 * k + 1] = v.y;
+                  gv[4 * k + 2] = v.z;
+                  gv[4 * k + 3] = v.w;
                 }
               } else {
 #pragma unroll
