@@ -131,15 +131,15 @@ def fused_generator_supported(channels: int, kernel_size: int, dtype: torch.dtyp
     )
 
 
-# Largest dilation halo of the fused dY + dW kernel at K = 5: its x halo
-# (16 channels x (8 + 2R) rows x (16 + 2R) FP32 cells, 63 KB at R = 10) shares
-# shared memory with the operand rings.
-FUSED_DYW_MAX_HALO_K5 = 10
+# Largest dilation halo of the fused dY + dW kernel at K = 5: the forward's
+# (its x halo of 16 channels x (8 + 2R) rows x (16 + 2R) 16-bit cells, 60 KB
+# at R = 16, fits beside the operand rings).
+FUSED_DYW_MAX_HALO_K5 = 16
 
 
 def _fused_dyw_ok(kernel_size: int, dtype: torch.dtype, width: int, dilations) -> bool:
     """Whether the fused dY + dW kernel covers this backward: K <= 3 always;
-    K = 5 for 16-bit data with halos up to 10 whose rows allow the gradient
+    K = 5 for 16-bit data (halos up to 16) whose rows allow the gradient
     tile's tensor map (W % 8 == 0). FP32 has no room for the wider K = 5 halo
     beside its hi / lo operand rings."""
     return kernel_size in FUSED_TRAINING_KERNEL_SIZES or (

@@ -512,6 +512,21 @@ __device__ __forceinline__ unsigned long long fma_io2<__half>(uint32_t a, uint32
   return f2_pack(lo, hi);
 }
 
+// a * b per 16-bit lane, rounded once to Op (round to nearest even): the
+// exact product of two 16-bit values rounded to the type, the same value as
+// the FP32 product (exact) converted with cvt2.
+template <typename Op> __device__ __forceinline__ uint32_t mul_io2(uint32_t a, uint32_t b);
+template <> __device__ __forceinline__ uint32_t mul_io2<__nv_bfloat16>(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+template <> __device__ __forceinline__ uint32_t mul_io2<__half>(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
 // Eight floats, held as four packed pairs, stored as one 16-byte operand row;
 // with kSplit also the residual (v - hi) row at dst_lo (exact subtraction).
 template <typename Op, bool kSplit>
@@ -671,11 +686,14 @@ int max_smem_optin();
 // tile, at any row within the dilation halo, is in range.
 // FP32 stores a bf16 hi part and a bf16 residual part.
 //
-// x plane (after the y plane, 256-byte aligned): x in FP32, 4 channels per
-// 16-byte cell, [n][Cq][H][W][4] with Cq = ceil(C/4) (channels >= C zero); not
-// padded: it is read by TMA, which zero-fills outside the image.
+// x plane (after the y plane, 256-byte aligned): 16-byte cells
+// [n][Cq][H][W][cell] with Cq = ceil(C / xcell) (channels >= C zero); FP32
+// data as FP32 cells of xcell = 4 channels, 16-bit data in its own type,
+// xcell = 8 channels per cell (half the bytes; the consumers multiply the
+// 16-bit values directly). Not padded: it is read by TMA, which zero-fills
+// outside the image.
 struct StageLayout {
-  int N, C, H, W, G, ph, pw, Hp, Wp, parts, Cq;
+  int N, C, H, W, G, ph, pw, Hp, Wp, parts, Cq, xcell;
   size_t part_bytes, x_offset, x_bytes;
   __host__ __device__ size_t y_bytes() const { return part_bytes * parts; }
   __host__ __device__ size_t total_bytes() const { return x_offset + x_bytes; }
@@ -698,7 +716,8 @@ struct StageLayout {
     L.Wp = (w + kTileM - 1) / kTileM * kTileM + 2 * L.pw;
     L.parts = dt == DDPM_F32 ? 2 : 1;
     L.part_bytes = (size_t)n * L.G * L.Hp * L.Wp * 16;
-    L.Cq = (c + 3) / 4;
+    L.xcell = dt == DDPM_F32 ? 4 : 8;
+    L.Cq = (c + L.xcell - 1) / L.xcell;
     L.x_offset = (L.y_bytes() + 255) / 256 * 256;
     L.x_bytes = (size_t)n * L.Cq * h * w * 16;
     return L;
@@ -709,15 +728,13 @@ size_t stage_bytes(int n, int c, int h, int w, int ks, int d0, int d1, int d2, i
 int stage(const void* x, const void* y, void* staged, size_t staged_bytes, int n, int c, int h,
           int w, int ks, int d0, int d1, int d2, int dt, cudaStream_t st);
 // TMA descriptors of the staged planes for 8 x 16 pixel tiles (64-bit element
-// views): x halo box {32 px, 8 + 2R rows, 4 channel quads}, coordinates
-// ((w0 - 8) * 2, h0 - R, 4 * cg, n); y tile box {16 px, 8 rows, ygroups
+// views): x halo box {halo_cols px, 8 + 2R rows, `cells` x cells}, coordinates
+// ((w0 - off) * 2, h0 - R, first cell, n); y tile box {16 px, 8 rows, ygroups
 // channel groups}, coordinates ((w0 + pw) * 2, h0 + ph, 0, part * N + n).
 // False when the driver rejects one (callers then stage from x and y).
-// `halo_cols` and `quads` (4-channel cells per box) set the x box for other
-// tile geometries (the K = 5 forward: 48 columns from w0 - 16, 2 or 1 quads).
+// `cells` = the channels a CTA stages / sl.xcell.
 bool encode_stage_maps(CUtensorMap* xmap, CUtensorMap* ymap, int R, int ygroups,
-                       const uint8_t* staged, const StageLayout& sl, int halo_cols = kHaloCols,
-                       int quads = 4);
+                       const uint8_t* staged, const StageLayout& sl, int halo_cols, int cells);
 // Tensor map reading a (16 * blocks)-pixel row segment of the y plane
 // ([group][pixel][8 channels], all `ngroups` channel groups of one part) as one
 // 5-D box: coordinates (0, first plane column / 16, plane row, 0, part * N + n).

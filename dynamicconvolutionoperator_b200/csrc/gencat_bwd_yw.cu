@@ -26,6 +26,7 @@
 // channel at index C so column C of D_w is db) accumulates over all tiles of
 // the split; partials go to a workspace and a short kernel reduces them into
 // the Conv2d weight layout.
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -112,6 +113,69 @@ __device__ __forceinline__ void build_dk_half(uint8_t* dk, int octet, int half, 
     build_dk_half<T, Op, kSplit, KS, O + 1>(dk, octet, half, xc, xr_plane, gv, dil, m, lo_off,
                                             cols);
   }
+}
+
+// The same octet half from an x halo of 8-channel 16-bit cells (staged 16-bit
+// data): gw[b][i] = the raw pair (g_b[2i], g_b[2i+1]) of the pixel's 16
+// channels; each dK pair is one packed 16-bit multiply of an x word and a g
+// word, rounded once (the value the FP32 product and conversion give).
+template <typename T, typename Op, int KS, int OCT, int J0>
+__device__ __forceinline__ void build_octet_io(uint8_t* dk, const uint4* xc, int xr_plane,
+                                               const uint32_t (&gw)[3][8], const int (&dil)[3],
+                                               int m, int cols) {
+  constexpr int KK = KS * KS;
+  constexpr int r = KS / 2;
+  const uint32_t base = (m >> 3) * 2048 + (m & 7) * 16;
+#pragma unroll
+  for (int j = J0; j < J0 + 4; ++j) {
+    const int s = OCT * 8 + j;
+    uint32_t pw[8];
+    if (s < 3 * KK) {
+      const int b = s / KK, tap = s % KK;
+      const int dy = (tap / KS - r) * dil[b], dx = (tap % KS - r) * dil[b];
+      const uint4* cell = xc + dy * cols + dx;
+#pragma unroll
+      for (int c8 = 0; c8 < 2; ++c8) {
+        const uint4 v = cell[c8 * xr_plane];
+        pw[c8 * 4 + 0] = mul_io2<Op>(v.x, gw[b][c8 * 4 + 0]);
+        pw[c8 * 4 + 1] = mul_io2<Op>(v.y, gw[b][c8 * 4 + 1]);
+        pw[c8 * 4 + 2] = mul_io2<Op>(v.z, gw[b][c8 * 4 + 2]);
+        pw[c8 * 4 + 3] = mul_io2<Op>(v.w, gw[b][c8 * 4 + 3]);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) pw[i] = 0u;
+    }
+    const uint32_t off = base + (j * 2) * 128;
+    *reinterpret_cast<uint4*>(dk + off) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
+    *reinterpret_cast<uint4*>(dk + off + 128) = make_uint4(pw[4], pw[5], pw[6], pw[7]);
+  }
+}
+
+template <typename T, typename Op, int KS, int O = 0>
+__device__ __forceinline__ void build_dk_half_io(uint8_t* dk, int octet, int half, const uint4* xc,
+                                                 int xr_plane, const uint32_t (&gw)[3][8],
+                                                 const int (&dil)[3], int m, int cols) {
+  constexpr int kOct = (3 * KS * KS + 7) / 8;
+  if constexpr (O < kOct) {
+    if (octet == O || O == kOct - 1) {
+      if (half == 0)
+        build_octet_io<T, Op, KS, O, 0>(dk, xc, xr_plane, gw, dil, m, cols);
+      else
+        build_octet_io<T, Op, KS, O, 4>(dk, xc, xr_plane, gw, dil, m, cols);
+      return;
+    }
+    build_dk_half_io<T, Op, KS, O + 1>(dk, octet, half, xc, xr_plane, gw, dil, m, cols);
+  }
+}
+
+// Two 16-bit values as one word, the first in bits 0-15.
+template <typename T>
+__device__ __forceinline__ uint32_t pack_raw2(T lo, T hi) {
+  uint16_t a, b;
+  memcpy(&a, &lo, 2);
+  memcpy(&b, &hi, 2);
+  return (uint32_t)a | ((uint32_t)b << 16);
 }
 
 // g_b[cg16*16 + cl, pixel] for the three branches (zero off-image / c >= C).
@@ -761,7 +825,9 @@ struct DywCfg {
   static constexpr bool kLoRing = kLoRingArg;
   static_assert(!kLoRing || kSplit, "the lo ring is for the FP32 split operands");
   static constexpr int kParts = kSplit ? 2 : 1;
-  static constexpr int kDkSlots = kSplit ? (kLoRing ? 2 : 1) : 2;  // lo ring: hi slots
+  // dK stages between builders and MMAs (lo ring: the hi slots); staged 16-bit
+  // data at K <= 3 has the room for a third beside its 16-bit x halos
+  static constexpr int kDkSlots = kSplit ? (kLoRing ? 2 : 1) : ((kStaged && KS <= 3) ? 3 : 2);
   static constexpr int kXBufs = kSplit ? 1 : 2;  // at most; DywParams::nx is the count used
   static constexpr int kYBufs = kSplit ? 1 : 2;
   static constexpr int kWStages = kLoRing ? 3 : 2;
@@ -772,6 +838,10 @@ struct DywCfg {
   static constexpr int kFirstXWarp = 3, kFirstYWarp = 7, kFirstBuilderWarp = 11;
   static constexpr int kThreads = 32 * (kFirstBuilderWarp + 8);
   static constexpr uint32_t kDyCol = 384;
+  // x halo cells: staged 16-bit data as 8-channel cells in the I/O type (kXIo:
+  // one packed multiply per dK pair), otherwise FP32 cells of 4 channels
+  static constexpr bool kXIo = kStaged && !kSplit;
+  static constexpr int kXCells = kXIo ? 2 : 4;  // cells per pixel (16 channels)
 };
 
 struct DywSmem {
@@ -780,8 +850,8 @@ struct DywSmem {
 
 // x halo of the dY+dW kernel: `dyw_halo_cols` cells per row starting
 // `dyw_halo_off` columns left of the tile: 32 from w0 - 8 for K <= 3 (halos up
-// to 8); for K = 5 exactly the 16 + 2R columns its halo R needs (a 48-column
-// halo of 16 channels at R = 10 would not fit beside the operand rings).
+// to 8); for K = 5 exactly the 16 + 2R columns its halo R needs (16-bit cells:
+// two x buffers up to R = 11, one up to R = 16).
 __host__ __device__ inline int dyw_halo_cols(int ks, int R) {
   return ks <= 3 ? kHaloCols : 16 + 2 * R;
 }
@@ -798,12 +868,14 @@ constexpr uint32_t kDyChunkBytes = 8 * 2 * 16 * 4;
 // (kGTma) the gradient tile [branch][channel][8 rows][16 px] and the four
 // D_y drain buffers (4 KB).
 // C=64, K=3, halo 5: fp32 36 + 40 + 64 + 2x32 + 4 KB = 208 KB;
-// bf16 2x36 + 2x20 + 2x32 + 2x16 (+ 12) + 4 KB = 212 (224) KB.
-template <typename T, int KS, bool kGTma = false, bool kLoRing = false>
+// bf16 2x36 + 2x20 + 2x32 + 2x16 (+ 12) + 4 KB = 212 (224) KB; staged bf16
+// (16-bit x cells, three dK stages) 2x18 + 2x20 + 3x32 + 2x16 (+ 12) + 4 KB =
+// 208 (220) KB.
+template <typename T, int KS, bool kGTma = false, bool kLoRing = false, bool kStaged = false>
 __host__ __device__ inline DywSmem dyw_smem_layout(int Cp, int Nw, int R, int nx) {
-  using Cfg = DywCfg<T, KS, false, kGTma, kLoRing>;
+  using Cfg = DywCfg<T, KS, kStaged, kGTma, kLoRing>;
   DywSmem L;
-  L.xr_bytes = (uint32_t)16 * (kTileH + 2 * R) * dyw_halo_cols(KS, R) * 4;
+  L.xr_bytes = (uint32_t)Cfg::kXCells * (kTileH + 2 * R) * dyw_halo_cols(KS, R) * 16;
   L.y_bytes = (uint32_t)Cfg::kParts * kTileM * Nw * 2;
   // lo ring: dk_bytes / w_bytes are one part; the lo buffer follows the hi slots
   L.dk_bytes = (uint32_t)(kLoRing ? 1 : Cfg::kParts) * kDkBytes;
@@ -923,7 +995,7 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
 
   const int C = p.C, Cp = p.Cp, H = p.H, W = p.W, R = p.R, Nw = p.Nw;
   const size_t P = (size_t)H * W;
-  const DywSmem L = dyw_smem_layout<T, KS, kGTma, kLoRing>(Cp, Nw, R, NX);
+  const DywSmem L = dyw_smem_layout<T, KS, kGTma, kLoRing, kStaged>(Cp, Nw, R, NX);
   const int cg = blockIdx.x % p.ncg;
   const int oset = (blockIdx.x / p.ncg) % p.nsets;
   const int split = blockIdx.x / (p.ncg * p.nsets);
@@ -1213,7 +1285,8 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
         // columns w0-8 .. w0+23 (x in 8-byte units), rows h0-R .., quads 4cg .. 4cg+3
         if (pt == 0) {
           tc::mbar_arrive_expect_tx(&x_full[xb], L.xr_bytes);
-          tc::tma_load_4d(xr, &maps.xmap, (w0 - xoff) * 2, h0 - R, cg * 4, n, &x_full[xb]);
+          tc::tma_load_4d(xr, &maps.xmap, (w0 - xoff) * 2, h0 - R, cg * Cfg::kXCells, n,
+                          &x_full[xb]);
         } else {
           tc::mbar_arrive(&x_full[xb]);
         }
@@ -1326,8 +1399,12 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
       const bool px_ok = (h < H) && (w < W);
       const size_t pix = px_ok ? (size_t)h * W + w : 0;
       const T* gn = gout + (size_t)n * 4 * C * P;
+      // gradient pairs of the pixel's 16 channels per branch: as f32x2 (gv) for
+      // the FP32-cell builders, as raw 16-bit pairs (gw) for kXIo
       unsigned long long gv[3][8];
+      uint32_t gw[3][8];
       if constexpr (kGTma) {
+        static_assert(!kGTma || Cfg::kXIo, "the gradient tile by TMA implies staged 16-bit x cells");
         if (!warp_wait(g_full, xq & 1, abort_flag)) {
           fail(abort_flag, p.status, 47);
           failed = true;
@@ -1339,9 +1416,8 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
 #pragma unroll
           for (int b = 0; b < 3; ++b) {
             const uint4 v0 = gq[2 * b], v1 = gq[2 * b + 1];
-            const uint32_t wv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-#pragma unroll
-            for (int i = 0; i < 8; ++i) gv[b][i] = uncvt2<T>(wv[i]);
+            gw[b][0] = v0.x; gw[b][1] = v0.y; gw[b][2] = v0.z; gw[b][3] = v0.w;
+            gw[b][4] = v1.x; gw[b][5] = v1.y; gw[b][6] = v1.z; gw[b][7] = v1.w;
           }
         } else {
           const T* gs = reinterpret_cast<const T*>(smem + L.g) + m;
@@ -1349,29 +1425,40 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
           for (int b = 0; b < 3; ++b)
 #pragma unroll
             for (int i = 0; i < 8; ++i)
-              gv[b][i] = f2_pack(to_f32<T>(gs[(b * 16 + 2 * i) * kTileM]),
-                                 to_f32<T>(gs[(b * 16 + 2 * i + 1) * kTileM]));
+              gw[b][i] = pack_raw2<T>(gs[(b * 16 + 2 * i) * kTileM], gs[(b * 16 + 2 * i + 1) * kTileM]);
         }
         // The next tile's gradient arrives by TMA into this buffer once the
         // arrivals below are in: every thread first waits for its own loads (a
         // use of every loaded value here; the compiler may otherwise place the
-        // conversions after the arrival) and orders them before the async
-        // proxy's writes. With one leader arrival after __syncwarp, and the
-        // values consumed later, the TMA overwrote words still being loaded.
+        // uses after the arrival) and orders them before the async proxy's
+        // writes. With one leader arrival after __syncwarp, and the values
+        // consumed later, the TMA overwrote words still being loaded.
         {
-          unsigned long long dep = 0;
+          uint32_t dep = 0;
 #pragma unroll
           for (int b = 0; b < 3; ++b)
 #pragma unroll
-            for (int i = 0; i < 8; ++i) dep ^= gv[b][i];
-          asm volatile("" ::"l"(dep));
+            for (int i = 0; i < 8; ++i) dep ^= gw[b][i];
+          asm volatile("" ::"r"(dep));
         }
         tc::fence_proxy_async_smem();
         tc::mbar_arrive(g_empty);
-      } else if (p.g_nhwc) {
-        load_gv_nhwc<T>(gv, gout, n, H, W, C, cg, h, w, px_ok);
       } else {
-        load_gv<T>(gv, gn, C, P, cg, pix, px_ok);
+        if (p.g_nhwc)
+          load_gv_nhwc<T>(gv, gout, n, H, W, C, cg, h, w, px_ok);
+        else
+          load_gv<T>(gv, gn, C, P, cg, pix, px_ok);
+        if constexpr (Cfg::kXIo) {
+          // exact: the values came from the 16-bit gradient
+#pragma unroll
+          for (int b = 0; b < 3; ++b)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              float lo, hi;
+              f2_unpack(gv[b][i], lo, hi);
+              gw[b][i] = cvt2<Op>(lo, hi);
+            }
+        }
       }
       const int xb = xq & nx_sh;
       if (!warp_wait(&x_full[xb], (xq >> nx_sh) & 1, abort_flag)) {
@@ -1379,8 +1466,9 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
         failed = true;
         break;
       }
-      const float4* xc = reinterpret_cast<const float4*>(smem + L.xr + xb * L.xr_bytes) +
-                         (mr + R) * xcols + (mc + xoff);
+      const int xcell0 = (mr + R) * xcols + (mc + xoff);
+      const float4* xc = reinterpret_cast<const float4*>(smem + L.xr + xb * L.xr_bytes) + xcell0;
+      const uint4* xci = reinterpret_cast<const uint4*>(smem + L.xr + xb * L.xr_bytes) + xcell0;
       for (int oct = oct0; oct < oct1; ++oct, ++kq) {
         const int ks_ = kq % NS;
         if (!warp_wait(&k_empty[ks_], ((kq / NS) & 1) ^ 1, abort_flag) ||
@@ -1391,8 +1479,12 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
         }
         // lo ring: hi part in slot ks_, lo part in the buffer after both slots
         const uint32_t lo_off = kLoRing ? (uint32_t)(2 - ks_) * kDkBytes : (uint32_t)kDkBytes;
-        build_dk_half<T, Op, Cfg::kSplit, KS>(smem + L.dk + ks_ * L.dk_bytes, oct, half, xc,
-                                              xr_plane, gv, dil, m, lo_off, xcols);
+        if constexpr (Cfg::kXIo)
+          build_dk_half_io<T, Op, KS>(smem + L.dk + ks_ * L.dk_bytes, oct, half, xci, xr_plane,
+                                      gw, dil, m, xcols);
+        else
+          build_dk_half<T, Op, Cfg::kSplit, KS>(smem + L.dk + ks_ * L.dk_bytes, oct, half, xc,
+                                                xr_plane, gv, dil, m, lo_off, xcols);
         tc::fence_proxy_async_smem();
         tc::mbar_arrive(&k_full[ks_]);
         if constexpr (kLoRing) tc::mbar_arrive(lo_full);
@@ -1544,7 +1636,8 @@ DywPlan plan_dyw(int n, int c, int h, int w, int ks) {
 template <typename T, int KS, bool kStaged, bool kGTma, bool kLoRing = false>
 int launch_dyw_k(const DywParams& prm, const DywMaps& maps, cudaStream_t st) {
   using Cfg = DywCfg<T, KS, kStaged, kGTma, kLoRing>;
-  const DywSmem L = dyw_smem_layout<T, KS, kGTma, kLoRing>(prm.Cp, prm.Nw, prm.R, prm.nx);
+  const DywSmem L =
+      dyw_smem_layout<T, KS, kGTma, kLoRing, kStaged>(prm.Cp, prm.Nw, prm.R, prm.nx);
   auto fn = gencat_bwd_dyw_kernel<T, KS, kStaged, kGTma, kLoRing>;
   DDPM_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total));
   fn<<<prm.ncg * prm.nsets * prm.splits, Cfg::kThreads, L.total, st>>>(prm, maps);
@@ -1561,24 +1654,30 @@ int launch_dyw(DywParams prm, const DywMaps& maps, bool staged, bool g_tma, cuda
   if constexpr (!IoTraits<T>::kSplit) {
     if (staged && g_tma)
       for (int nx = kMaxX; nx >= 1; --nx)
-        if ((int)dyw_smem_layout<T, KS, true>(prm.Cp, prm.Nw, prm.R, nx).total <= lim) {
+        if ((int)dyw_smem_layout<T, KS, true, false, true>(prm.Cp, prm.Nw, prm.R, nx).total <=
+            lim) {
           prm.nx = nx;
           return launch_dyw_k<T, KS, true, true>(prm, maps, st);
         }
   } else {
     // FP32: the lo ring where it fits (halos up to 5 at C = 64)
-    if (staged && (int)dyw_smem_layout<T, KS, false, true>(prm.Cp, prm.Nw, prm.R, 1).total <= lim) {
+    if (staged &&
+        (int)dyw_smem_layout<T, KS, false, true, true>(prm.Cp, prm.Nw, prm.R, 1).total <= lim) {
       prm.nx = 1;
       return launch_dyw_k<T, KS, true, false, true>(prm, maps, st);
     }
   }
   if constexpr (KS <= 3) {
-    for (int nx = kMaxX; nx >= 1; --nx)
-      if ((int)dyw_smem_layout<T, KS>(prm.Cp, prm.Nw, prm.R, nx).total <= lim) {
+    for (int nx = kMaxX; nx >= 1; --nx) {
+      const uint32_t need =
+          staged ? dyw_smem_layout<T, KS, false, false, true>(prm.Cp, prm.Nw, prm.R, nx).total
+                 : dyw_smem_layout<T, KS>(prm.Cp, prm.Nw, prm.R, nx).total;
+      if ((int)need <= lim) {
         prm.nx = nx;
         return staged ? launch_dyw_k<T, KS, true, false>(prm, maps, st)
                       : launch_dyw_k<T, KS, false, false>(prm, maps, st);
       }
+    }
   }
   // K = 5 runs only with staged operands and the gradient tile by TMA
   return set_error(DDPM_ERR_UNSUPPORTED, "dY+dW tile does not fit in shared memory");
@@ -1623,10 +1722,10 @@ int gencat_bwd_yw(const void* x, const void* y, const void* staged, size_t stage
                    : gencat::check_shape_bwd(n, c, h, w, ks, d0, d1, d2, dt);
   if (rc) return rc;
   if (ks == 5 && (dt == DDPM_F32 || staged == nullptr || gy == nullptr || gw == nullptr ||
-                  gb == nullptr || workspace == nullptr || 2 * max3(d0, d1, d2) > 10))
+                  gb == nullptr || workspace == nullptr))
     return set_error(DDPM_ERR_UNSUPPORTED,
                      "fused dY + dW at K = 5 needs 16-bit data, staged operands, all three "
-                     "gradients, the workspace and a dilation halo <= 10");
+                     "gradients and the workspace");
   DDPM_CHECK_ARG(((x && y) || staged) && wpack && gout, "null pointer");
   if (g_nhwc && (c != 64 || staged == nullptr))
     return set_error(DDPM_ERR_UNSUPPORTED,
@@ -1688,7 +1787,7 @@ int gencat_bwd_yw(const void* x, const void* y, const void* staged, size_t stage
         const gencat::StageLayout sl = gencat::StageLayout::make(n, c, h, w, ks, d0, d1, d2, dt);
         use_staged = gencat::encode_stage_maps(&maps.xmap, &maps.ymap, R, sl.G,
                                                static_cast<const uint8_t*>(staged), sl,
-                                               dyw_halo_cols(ks, R));
+                                               dyw_halo_cols(ks, R), 16 / sl.xcell);
         maps.ph = sl.ph;
         maps.pw = sl.pw;
         // gradient tiles by TMA (16-bit) when the row pitch and base allow a map
@@ -1740,6 +1839,10 @@ int gencat_bwd_yw(const void* x, const void* y, const void* staged, size_t stage
         else
           clear_error();
       }
+      if (ks == 5 && !(use_staged && g_tma))
+        return set_error(DDPM_ERR_UNSUPPORTED,
+                         "fused dY + dW at K = 5 needs the gradient tile by TMA (16-byte aligned "
+                         "rows)");
       DDPM_CUDA_TRY(cudaMemsetAsync(dp.gy_acc, 0, (size_t)n * c * h * w * sizeof(float), st));
       switch (dt * 10 + ks) {
         case DDPM_BF16 * 10 + 1: rc = launch_dyw<__nv_bfloat16, 1>(dp, maps, use_staged, g_tma, st); break;
@@ -1748,18 +1851,8 @@ int gencat_bwd_yw(const void* x, const void* y, const void* staged, size_t stage
         case DDPM_F16 * 10 + 3: rc = launch_dyw<__half, 3>(dp, maps, use_staged, g_tma, st); break;
         case DDPM_F32 * 10 + 1: rc = launch_dyw<float, 1>(dp, maps, use_staged, g_tma, st); break;
         case DDPM_F32 * 10 + 3: rc = launch_dyw<float, 3>(dp, maps, use_staged, g_tma, st); break;
-        case DDPM_BF16 * 10 + 5:
-          rc = use_staged && g_tma ? launch_dyw<__nv_bfloat16, 5>(dp, maps, true, true, st)
-                                   : set_error(DDPM_ERR_UNSUPPORTED,
-                                               "fused dY + dW at K = 5 needs the gradient tile "
-                                               "by TMA (16-byte aligned rows)");
-          break;
-        case DDPM_F16 * 10 + 5:
-          rc = use_staged && g_tma ? launch_dyw<__half, 5>(dp, maps, true, true, st)
-                                   : set_error(DDPM_ERR_UNSUPPORTED,
-                                               "fused dY + dW at K = 5 needs the gradient tile "
-                                               "by TMA (16-byte aligned rows)");
-          break;
+        case DDPM_BF16 * 10 + 5: rc = launch_dyw<__nv_bfloat16, 5>(dp, maps, true, true, st); break;
+        case DDPM_F16 * 10 + 5: rc = launch_dyw<__half, 5>(dp, maps, true, true, st); break;
         default: rc = set_error(DDPM_ERR_UNSUPPORTED, "unsupported dtype/kernel size");
       }
       if (rc) return rc;

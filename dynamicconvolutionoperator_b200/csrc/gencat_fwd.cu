@@ -109,6 +109,11 @@ struct FwdCfg {
   static constexpr int kYItems = (16 * (kSplit ? 64 : 80) + kProducers - 1) / kProducers;
   static constexpr int kXItems =
       (kQ4 * (kHaloW / 8) * (kTileH + 2 * kMaxR) + kProducers - 1) / kProducers;
+  // x halo cells in shared memory: with staged operands 16-bit data arrives as
+  // 8-channel cells in the I/O type (kXIo: the epilogue multiplies the 16-bit
+  // values directly), otherwise as FP32 cells of 4 channels
+  static constexpr bool kXIo = kStaged && !kSplit;
+  static constexpr int kXCells = kXIo ? kCG / 8 : kQ4;  // cells per pixel
 };
 
 struct FwdSmem {
@@ -119,16 +124,17 @@ struct FwdSmem {
 
 // Resident weights of one channel group + y tile(s) + `nxb` (2, or 1 where two
 // do not fit: FP32 with halos >= 7) x-halo buffers.
-// C=64, K=3, halo 5: bf16 69 + 2x20 + 2x36 KB = 181 KB; fp32 108 + 32 + 72 KB = 214 KB.
-// C=64, K=5, halo 10 (8 / 4 channels): bf16 97.5 + 2x20 + 2x42 KB = 221.5 KB;
-// fp32 84 + 32 + 2x21 KB + 1.2 KB bias = 159 KB.
-template <typename T, int KS>
+// C=64, K=3, halo 5: bf16 69 + 2x20 + 2x36 KB = 181 KB (staged 16-bit x: 2x18,
+// 145 KB); fp32 108 + 32 + 72 KB = 214 KB.
+// C=64, K=5, halo 10 (8 / 4 channels): bf16 97.5 + 2x20 + 2x42 KB = 221.5 KB
+// (staged: 2x21, 179.5 KB); fp32 84 + 32 + 2x21 KB + 1.2 KB bias = 159 KB.
+template <typename T, int KS, bool kStaged = false>
 __host__ __device__ inline FwdSmem fwd_smem_layout(int Ck, int R, int nxb) {
-  using Cfg = FwdCfg<T, KS>;
+  using Cfg = FwdCfg<T, KS, kStaged>;
   FwdSmem L;
   L.y_bytes = (uint32_t)Cfg::kParts * kTileM * Ck * 2;
   L.w_bytes = (uint32_t)Cfg::kParts * Cfg::kRows * Ck * 2;  // the group's whole image
-  L.xr_bytes = (uint32_t)Cfg::kCG * (kTileH + 2 * R) * Cfg::kHaloW * 4;
+  L.xr_bytes = (uint32_t)Cfg::kXCells * (kTileH + 2 * R) * Cfg::kHaloW * 16;
   L.y = 0;
   L.w = L.y + Cfg::kYBufs * L.y_bytes;
   L.xr = L.w + L.w_bytes;
@@ -216,7 +222,7 @@ gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
 
   const int C = p.C, Ck = p.Ck, H = p.H, W = p.W, R = p.R;
   const size_t P = (size_t)H * W;
-  const FwdSmem L = fwd_smem_layout<T, KS>(Ck, R, p.nxb);
+  const FwdSmem L = fwd_smem_layout<T, KS, kStaged>(Ck, R, p.nxb);
   const int nx_sh = p.nxb - 1;  // 1 or 2 buffers: index = it & nx_sh, lap = it >> nx_sh
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint64_t* y_full = bars;           // [2]
@@ -400,8 +406,8 @@ gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
       if constexpr (kStaged) {
         if (pt == 0) {
           tc::mbar_arrive_expect_tx(&x_full[xb], L.xr_bytes);
-          tc::tma_load_4d(xr, &maps.xmap, (w0 - Cfg::kHaloOff) * 2, h0 - R, cg * kQ4, n,
-                          &x_full[xb]);
+          tc::tma_load_4d(xr, &maps.xmap, (w0 - Cfg::kHaloOff) * 2, h0 - R, cg * Cfg::kXCells,
+                          n, &x_full[xb]);
         } else {
           tc::mbar_arrive(&x_full[xb]);
         }
@@ -435,9 +441,10 @@ gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
         fail(abort_flag, p.status, 16);
         break;
       }
-      const float4* xr = reinterpret_cast<const float4*>(smem + L.xr + xb * L.xr_bytes);
       // this pixel's cell in the halo tile; a tap shifts it by (dy, dx)
-      const float4* xc = xr + (mr + R) * kHW + (mc + Cfg::kHaloOff);
+      const int xcell0 = (mr + R) * kHW + (mc + Cfg::kHaloOff);
+      const float4* xc = reinterpret_cast<const float4*>(smem + L.xr + xb * L.xr_bytes) + xcell0;
+      const uint4* xci = reinterpret_cast<const uint4*>(smem + L.xr + xb * L.xr_bytes) + xcell0;
       bool failed = false;
       for (int q = 0; q < Cfg::kSlots && !failed; ++q, ++tq) {
         if (tq % Cfg::kEpiWG != (uint32_t)wg) continue;  // another warpgroup's slot
@@ -471,6 +478,22 @@ gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
             }
 #pragma unroll
             for (int kj = 0; kj < KS; ++kj) {
+              if constexpr (Cfg::kXIo) {
+                // 8-channel 16-bit cells: each word of two x values meets the
+                // matching pair of rounded taps in two mixed-precision FMAs
+                const uint4* cell = xci + ((ki - r) * kHW + (kj - r)) * d;
+#pragma unroll
+                for (int c8 = 0; c8 < Cfg::kXCells; ++c8) {
+                  const uint4 v = cell[c8 * xr_plane];
+                  const uint32_t xw[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                  for (int i = 0; i < 4; ++i)
+                    acc[c8 * 4 + i] =
+                        fma_io2<Op>(cvt2<Op>(dv[kj][c8 * 8 + 2 * i], dv[kj][c8 * 8 + 2 * i + 1]),
+                                    xw[i], acc[c8 * 4 + i]);
+                }
+                continue;
+              }
               const float4* cell = xrow + (kj - r) * d;
 #pragma unroll
               for (int q4 = 0; q4 < kQ4; ++q4) {
@@ -508,8 +531,24 @@ gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
       // passthrough out[:, cg*kCG : (cg+1)*kCG] = x, written from the halo tile
       if (px_ok && (it % Cfg::kEpiWG) == (uint32_t)wg) {
         unsigned long long xp[kCG / 2];
+        if constexpr (Cfg::kXIo) {
 #pragma unroll
-        for (int q4 = 0; q4 < kQ4; ++q4) {
+          for (int c8 = 0; c8 < Cfg::kXCells; ++c8) {
+            const uint4 v = xci[c8 * xr_plane];
+            const uint32_t xw[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              xp[c8 * 4 + i] = uncvt2<Op>(xw[i]);
+              float e0, e1;
+              f2_unpack(xp[c8 * 4 + i], e0, e1);
+              const int c = cg * kCG + c8 * 8 + 2 * i;
+              if (c < C) on[(size_t)c * P + pix] = from_f32<T>(e0);
+              if (c + 1 < C) on[(size_t)(c + 1) * P + pix] = from_f32<T>(e1);
+            }
+          }
+        }
+#pragma unroll
+        for (int q4 = 0; q4 < (Cfg::kXIo ? 0 : kQ4); ++q4) {
           const float4 v = xc[q4 * xr_plane];
           const float e[4] = {v.x, v.y, v.z, v.w};
           xp[2 * q4] = f2_pack(v.x, v.y);
@@ -540,8 +579,8 @@ int launch_k(const FwdParams& prm, const FwdMaps& maps, cudaStream_t st) {
   using Cfg = FwdCfg<T, KS, kStaged>;
   FwdParams q = prm;
   q.nxb = 2;
-  if ((int)fwd_smem_layout<T, KS>(q.Ck, q.R, 2).total > max_smem_optin()) q.nxb = 1;
-  const FwdSmem L = fwd_smem_layout<T, KS>(q.Ck, q.R, q.nxb);
+  if ((int)fwd_smem_layout<T, KS, kStaged>(q.Ck, q.R, 2).total > max_smem_optin()) q.nxb = 1;
+  const FwdSmem L = fwd_smem_layout<T, KS, kStaged>(q.Ck, q.R, q.nxb);
   if ((int)L.total > max_smem_optin())
     return set_error(DDPM_ERR_UNSUPPORTED, "forward tile needs %u bytes of shared memory",
                      L.total);
@@ -668,7 +707,7 @@ int gencat_fwd_ex(const void* x, const void* y, const void* staged, size_t stage
                    "staged operands must be 256-byte aligned");
     use_staged = gencat::encode_stage_maps(&maps.xmap, &maps.ymap, prm.R, pl.Ck / 8,
                                            static_cast<const uint8_t*>(staged), sl,
-                                           gencat::fwd_halo_cols(ks), cgw / 4);
+                                           gencat::fwd_halo_cols(ks), cgw / sl.xcell);
     maps.ph = sl.ph;
     maps.pw = sl.pw;
   }

@@ -1,9 +1,12 @@
 // Staged operands of the fused generator backward (layout: StageLayout in
 // gencat.cuh). One pass over y writes it channel-last in the MMA operand type,
 // zero padded and with the constant-one bias channel; one pass over x writes
-// it as FP32 4-channel cells. The backward kernels then stage their tiles with
+// it as 16-byte cells (FP32: 4 channels; 16-bit types: 8 channels in the
+// input type). The backward kernels then stage their tiles with
 // 1-D bulk / TMA copies instead of per-thread loads and register transposes
 // (which bounded them by load latency).
+#include <cstring>
+
 #include "common.cuh"
 #include "gencat.cuh"
 
@@ -61,18 +64,21 @@ __global__ void __launch_bounds__(256) stage_y_kernel(const T* __restrict__ y,
   }
 }
 
-// x plane: thread = one 16-byte cell (n, channel quad q, h, w) = x[n, 4q .. 4q+3, h, w]
-// in FP32 (channels >= C zero); consecutive threads = consecutive columns.
+// x plane: thread = one 16-byte cell (n, cell q, h, w) = x[n, q*xcell ..
+// q*xcell + xcell-1, h, w]: FP32 cells of 4 channels, or 16-bit cells of 8
+// channels in the input type (channels >= C zero); consecutive threads =
+// consecutive columns.
 template <typename T>
 __global__ void __launch_bounds__(256) stage_x_kernel(const T* __restrict__ x,
-                                                      float4* __restrict__ xp,
+                                                      uint4* __restrict__ xp,
                                                       const StageLayout L) {
+  constexpr int kCh = sizeof(T) == 4 ? 4 : 8;  // channels per cell
   const size_t P = (size_t)L.H * L.W;
   const size_t cells = (size_t)L.N * L.Cq * P;
   const size_t stride = (size_t)gridDim.x * blockDim.x;
   // four cells per thread per round, all loads issued before the stores
   for (size_t i0 = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i0 < cells; i0 += 4 * stride) {
-    float v[4][4];
+    T v[4][kCh];
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
       const size_t i = i0 + r * stride;
@@ -80,57 +86,73 @@ __global__ void __launch_bounds__(256) stage_x_kernel(const T* __restrict__ x,
       const size_t nq = i / P;
       const int q = (int)(nq % L.Cq), n = (int)(nq / L.Cq);
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int c = 4 * q + k;
-        v[r][k] = (i < cells && c < L.C) ? to_f32<T>(__ldg(x + ((size_t)n * L.C + c) * P + pix))
-                                         : 0.f;
+      for (int k = 0; k < kCh; ++k) {
+        const int c = kCh * q + k;
+        v[r][k] = (i < cells && c < L.C) ? __ldg(x + ((size_t)n * L.C + c) * P + pix) : T(0.f);
       }
     }
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
       const size_t i = i0 + r * stride;
-      if (i < cells) xp[i] = make_float4(v[r][0], v[r][1], v[r][2], v[r][3]);
+      uint32_t wv[4];
+      memcpy(wv, v[r], 16);  // registers: the store below is one 16-byte store
+      if (i < cells) xp[i] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
     }
   }
 }
 
-// The same x plane from 16-byte vectors: block = (pixel range, (n, quad)),
-// thread = 8 consecutive pixels of the quad's four channels (four vector
-// loads), written as 8 consecutive cells (128 contiguous bytes); no index
+// The same x plane from 16-byte vectors: block = (pixel range, (n, cell)),
+// thread = 8 consecutive pixels of the cell's channels (one vector load per
+// channel), written as 8 consecutive cells (128 contiguous bytes); no index
 // division per cell. Needs H*W % 8 == 0 and a 16-byte aligned x.
 template <typename T>
 __global__ void __launch_bounds__(256) stage_x_vec_kernel(const T* __restrict__ x,
-                                                          float4* __restrict__ xp,
+                                                          uint4* __restrict__ xp,
                                                           const StageLayout L) {
   const size_t P = (size_t)L.H * L.W;
   const int nq = blockIdx.y, n = nq / L.Cq, q = nq - n * L.Cq;
   const size_t p0 = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;
   if (p0 >= P) return;
-  float v[4][8];
+  uint4* dst = xp + ((size_t)n * L.Cq + q) * P + p0;
+  if constexpr (sizeof(T) == 4) {
+    float v[4][8];
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const int c = 4 * q + k;
-    if (c < L.C) {
-      const T* src = x + ((size_t)n * L.C + c) * P + p0;
-      if constexpr (sizeof(T) == 4) {
-        const float4 a = __ldg(reinterpret_cast<const float4*>(src));
-        const float4 b = __ldg(reinterpret_cast<const float4*>(src) + 1);
+    for (int k = 0; k < 4; ++k) {
+      const int c = 4 * q + k;
+      if (c < L.C) {
+        const float4* src = reinterpret_cast<const float4*>(x + ((size_t)n * L.C + c) * P + p0);
+        const float4 a = __ldg(src);
+        const float4 b = __ldg(src + 1);
         v[k][0] = a.x; v[k][1] = a.y; v[k][2] = a.z; v[k][3] = a.w;
         v[k][4] = b.x; v[k][5] = b.y; v[k][6] = b.z; v[k][7] = b.w;
       } else {
-        const uint4 u = __ldg(reinterpret_cast<const uint4*>(src));
-        const T* e = reinterpret_cast<const T*>(&u);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[k][i] = to_f32<T>(e[i]);
+        for (int i = 0; i < 8; ++i) v[k][i] = 0.f;
       }
-    } else {
+    }
+    float4* dstf = reinterpret_cast<float4*>(dst);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) v[k][i] = 0.f;
+    for (int e = 0; e < 8; ++e) dstf[e] = make_float4(v[0][e], v[1][e], v[2][e], v[3][e]);
+  } else {
+    // u[k] = channel 8q + k at pixels p0 .. p0+7 (word j = pixels 2j, 2j+1);
+    // cell e, word k = channels (2k, 2k+1) at pixel p0 + e
+    uint32_t u[8][4];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int c = 8 * q + k;
+      uint4 t = make_uint4(0u, 0u, 0u, 0u);
+      if (c < L.C) t = __ldg(reinterpret_cast<const uint4*>(x + ((size_t)n * L.C + c) * P + p0));
+      u[k][0] = t.x; u[k][1] = t.y; u[k][2] = t.z; u[k][3] = t.w;
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const uint32_t sel = (e & 1) ? 0x7632u : 0x5410u;  // high or low halves
+      uint32_t w[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) w[k] = __byte_perm(u[2 * k][e >> 1], u[2 * k + 1][e >> 1], sel);
+      dst[e] = make_uint4(w[0], w[1], w[2], w[3]);
     }
   }
-  float4* dst = xp + ((size_t)n * L.Cq + q) * P + p0;
-#pragma unroll
-  for (int e = 0; e < 8; ++e) dst[e] = make_float4(v[0][e], v[1][e], v[2][e], v[3][e]);
 }
 
 template <typename T>
@@ -145,14 +167,14 @@ int launch_stage(const T* x, const T* y, uint8_t* staged, const StageLayout& L, 
       (size_t)L.N * L.Cq <= 65535u) {
     const dim3 grid((unsigned)((P / 8 + 255) / 256), (unsigned)(L.N * L.Cq));
     stage_x_vec_kernel<T><<<grid, 256, 0, st>>>(
-        x, reinterpret_cast<float4*>(staged + L.x_offset), L);
+        x, reinterpret_cast<uint4*>(staged + L.x_offset), L);
     DDPM_CHECK_LAUNCH("stage_x_vec_kernel");
   } else if (x != nullptr) {
     const size_t cells = (size_t)L.N * L.Cq * L.H * L.W;
     size_t blocks = (cells + 4 * 256 - 1) / (4 * 256);  // four cells per thread
     if (blocks > 65535u * 8u) blocks = 65535u * 8u;
     stage_x_kernel<T><<<(unsigned)blocks, 256, 0, st>>>(
-        x, reinterpret_cast<float4*>(staged + L.x_offset), L);
+        x, reinterpret_cast<uint4*>(staged + L.x_offset), L);
     DDPM_CHECK_LAUNCH("stage_x_kernel");
   }
   return DDPM_OK;
@@ -195,12 +217,12 @@ int stage(const void* x, const void* y, void* staged, size_t staged_bytes, int n
 }
 
 bool encode_stage_maps(CUtensorMap* xmap, CUtensorMap* ymap, int R, int ygroups,
-                       const uint8_t* staged, const StageLayout& sl, int halo_cols, int quads) {
+                       const uint8_t* staged, const StageLayout& sl, int halo_cols, int cells) {
   const uint64_t xd[4] = {(uint64_t)sl.W * 2, (uint64_t)sl.H, (uint64_t)sl.Cq, (uint64_t)sl.N};
   const uint64_t xs[3] = {(uint64_t)sl.W * 16, (uint64_t)sl.H * sl.W * 16,
                           (uint64_t)sl.Cq * sl.H * sl.W * 16};
   const uint32_t xb[4] = {(uint32_t)(2 * halo_cols), (uint32_t)(kTileH + 2 * R),
-                          (uint32_t)quads, 1};
+                          (uint32_t)cells, 1};
   const uint64_t yd[4] = {(uint64_t)sl.Wp * 2, (uint64_t)sl.Hp, (uint64_t)sl.G,
                           (uint64_t)sl.parts * sl.N};
   const uint64_t ys[3] = {(uint64_t)sl.Wp * 16, (uint64_t)sl.Hp * sl.Wp * 16,

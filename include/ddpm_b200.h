@@ -108,11 +108,10 @@ DDPM_API int ddpm_dyncat_bwd(const void* x, int x_dtype,
  * weight version into a buffer of ddpm_gencat_pack_bytes() bytes (16-byte
  * aligned) and pass it to every fused launch that uses that weight.
  * Limits of this build: C <= 64; K in {1, 3} with dilation halos
- * (K/2)*max(d) <= 8, or K = 5 with halos <= 16 (the forward and dX entry
- * points; the dY + dW entry points cover K = 5 for 16-bit data through the
- * staged merged pass, halos <= 10, rows of a multiple of 8 pixels); other
- * sizes return
- * DDPM_ERR_UNSUPPORTED (callers then take the materialised path).
+ * (K/2)*max(d) <= 8, or K = 5 with halos <= 16 (the dY + dW entry points
+ * cover K = 5 for 16-bit data through the staged merged pass, rows of a
+ * multiple of 8 pixels); other sizes return DDPM_ERR_UNSUPPORTED (callers
+ * then take the materialised path).
  */
 DDPM_API size_t ddpm_gencat_pack_bytes(int c, int ksize, int dtype);
 DDPM_API int ddpm_gencat_pack(const void* weight, const void* bias, int c, int ksize,
@@ -181,7 +180,8 @@ DDPM_API int ddpm_gencat_bwd_x(const void* y, const void* packed, const void* bi
  * Staged operands for the fused backward, written once per backward:
  * y channel-last, zero padded by the dilation halo, in the tensor-core operand
  * type (fp32: bf16 hi and residual parts) with the constant-one bias channel,
- * and (when x is given) x as FP32 cells of 4 channels. The backward kernels
+ * and (when x is given) x as 16-byte cells (fp32: FP32, 4 channels per cell;
+ * bf16 / fp16: the input type, 8 channels per cell). The backward kernels
  * then stage every tile with bulk / TMA copies. Same role as the per-tile x
  * and y loads inside `_generator_dynamic_cat_bwd_x` and
  * `_generator_dynamic_cat_bwd_y` / `_bwd_weight_partial` (reference

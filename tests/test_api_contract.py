@@ -115,7 +115,8 @@ def test_fused_kernel_limits():
     """Forward: C <= 64, K in {1, 3} with halo (K/2) * max(dilation) <= 8 or
     K = 5 with halo <= 16; fused training at every such K (the fully fused
     backward kernels at K <= 3, the reference's limit, ``triton_impl.py:320``;
-    fused dX with a materialised dK at K = 5)."""
+    at K = 5 fused dX, and fused dY + dW for 16-bit data with rows of a
+    multiple of 8 pixels, FP32 taking a materialised dK for dY / dW)."""
     from dynamicconvolutionoperator_b200 import _kernels
 
     ok = _kernels.fused_generator_supported
@@ -127,6 +128,9 @@ def test_fused_kernel_limits():
     assert not ok(64, 3, torch.float64)
     assert [k for k in (1, 3, 5, 7) if _kernels.fused_training_supported(k)] == [1, 3, 5]
     assert _kernels.FUSED_TRAINING_KERNEL_SIZES == (1, 3)
+    dyw = _kernels._fused_dyw_ok
+    assert dyw(3, torch.float32, 17, (1, 3, 5)) and dyw(5, torch.float16, 64, (1, 8, 4))
+    assert not dyw(5, torch.float32, 64, (1, 3, 5)) and not dyw(5, torch.bfloat16, 60, (1, 3, 5))
 
 
 @pytest.mark.parametrize(

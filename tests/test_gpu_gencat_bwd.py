@@ -78,7 +78,8 @@ def test_gencat_bwd_x(shape, ks, dtype, staged):
 def test_stage_layout(shape, ks, dil, dtype):
     """y plane = y channel-last, zero padded by the halo, ones channel at C,
     [part][n][G][Hp][Wp][8]; fp32 as bf16 hi + residual (hi + lo == y to
-    within bf16 of the residual). x plane = x in FP32, [n][ceil(C/4)][H][W][4]."""
+    within bf16 of the residual). x plane = 16-byte cells [n][ceil(C/k)][H][W][k]:
+    fp32 as FP32 (k = 4), 16-bit data in its own type (k = 8, the same bits)."""
     n, c, h, w = shape
     gen = torch.Generator().manual_seed(3)
     y = torch.randn(shape, generator=gen).to(dtype)
@@ -91,7 +92,8 @@ def test_stage_layout(shape, ks, dil, dtype):
     parts = 2 if dtype == torch.float32 else 1
     part_bytes = n * G * Hp * Wp * 16
     x_off = (parts * part_bytes + 255) // 256 * 256
-    cq = (c + 3) // 4
+    xcell = 4 if dtype == torch.float32 else 8
+    cq = (c + xcell - 1) // xcell
     assert nb == x_off + n * cq * h * w * 16
     want = torch.zeros((n, G * 8, Hp, Wp), dtype=torch.float64)
     want[:, :c, ph:ph + h, 8:8 + w] = y.double()
@@ -104,10 +106,11 @@ def test_stage_layout(shape, ks, dil, dtype):
     # fp32: |y - hi| <= 2^-8 |y| and the residual is rounded to bf16 again
     tol = 2.0 ** -15 * want.abs().max().item() if dtype == torch.float32 else 0.0
     assert (got - want).abs().max().item() <= tol
-    xp = raw[x_off:x_off + n * cq * h * w * 16].view(torch.float32).view(n, cq, h, w, 4)
-    xp = xp.permute(0, 1, 4, 2, 3).reshape(n, cq * 4, h, w)
-    assert torch.equal(xp[:, :c], x.float())
-    assert not xp[:, c:].any()
+    xp = raw[x_off:x_off + n * cq * h * w * 16].view(dtype).view(n, cq, h, w, xcell)
+    xp = xp.permute(0, 1, 4, 2, 3).reshape(n, cq * xcell, h, w)
+    bits = torch.int16 if xcell == 8 else torch.int32  # compare the bits
+    assert torch.equal(xp[:, :c].view(bits), x.view(bits))
+    assert not xp[:, c:].view(bits).any()
 
 
 @pytest.mark.parametrize("shape", SHAPES)
@@ -277,8 +280,7 @@ def test_channel_last_grad_out_matches_nchw(shape, ks, dtype):
 def test_k5_bwd_x_channel_last_and_max_halo(dtype):
     """K = 5 dX: the channel-last entry point matches the NCHW one bit for bit,
     and the largest halo (16, dilations (1, 8, 4)) matches the oracle on a
-    shape whose rows span two 128-pixel tiles; the fused dY + dW kernel covers
-    K = 5 halos up to 10 only (DDPM_ERR_UNSUPPORTED before any launch)."""
+    shape whose rows span two 128-pixel tiles."""
     from dynamicconvolutionoperator_b200 import _kernels, _lib
 
     shape, ks, dil = (1, 64, 13, 150), 5, (1, 8, 4)
@@ -301,9 +303,6 @@ def test_k5_bwd_x_channel_last_and_max_halo(dtype):
     assert torch.equal(out[""], out["_nhwc"])
     rtol, atol = TOL[dtype]
     torch.testing.assert_close(out[""].double().cpu(), gx_gold, rtol=rtol, atol=atol)
-    rc = _lib.load().ddpm_gencat_bwd_yw_staged(1, 1 << 20, 1, 1, 1, 1, 1, 1, 1 << 20,
-                                               n, c, h, w, ks, *dil, code, None)
-    assert rc == -2
 
 
 def test_channel_last_grad_out_rejected_outside_its_limits():
@@ -362,15 +361,19 @@ def test_channel_last_dyw_many_tiles_per_cta(dtype):
             assert (got - ref).abs().max().item() <= 2e-2 * scale, name
 
 
-@pytest.mark.parametrize("shape", [(1, 64, 40, 48), (2, 24, 17, 40), (1, 64, 24, 136)])
+@pytest.mark.parametrize("shape,dil", [((1, 64, 40, 48), (1, 3, 5)), ((2, 24, 17, 40), (1, 3, 5)),
+                                       ((1, 64, 24, 136), (1, 3, 5)), ((1, 64, 13, 152), (1, 8, 4)),
+                                       ((2, 16, 21, 24), (6, 2, 1))])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-def test_k5_fused_dyw_matches_oracle(shape, dtype):
+def test_k5_fused_dyw_matches_oracle(shape, dil, dtype):
     """K = 5 fused dY + dW (16-bit, staged, gradient tile by TMA; octet sets
-    of <= 4 per CTA, 36-column x halo at halo 10) against the float64 oracle,
-    through the NCHW entry and, at C = 64, the channel-last one."""
+    of <= 4 per CTA, an x halo of 16 + 2R columns: 36 at halo 10, 48 at the
+    largest halo 16 with one x buffer, 28 at halo 6 with two) against the
+    float64 oracle, through the NCHW entry and, at C = 64, the channel-last
+    one."""
     from dynamicconvolutionoperator_b200 import _kernels, _lib
 
-    ks, dil = 5, (1, 3, 5)
+    ks = 5
     x, y, wt, b = _case(shape, ks, dtype, seed=41)
     n, c, h, w = shape
     g = torch.randn((n, 4 * c, h, w), generator=torch.Generator().manual_seed(42)).to(dtype)
@@ -399,8 +402,9 @@ def test_k5_fused_dyw_matches_oracle(shape, dtype):
 
 
 def test_k5_fused_dyw_limits():
-    """FP32, unstaged operands and halos above 10 are not fused dY + dW
-    shapes at K = 5 (DDPM_ERR_UNSUPPORTED before any launch)."""
+    """FP32 and unstaged operands are not fused dY + dW shapes at K = 5
+    (DDPM_ERR_UNSUPPORTED before any launch); 16-bit data is, at every halo
+    the forward covers, when its rows allow the gradient tile's tensor map."""
     from dynamicconvolutionoperator_b200 import _kernels, _lib
 
     lib = _lib.load()
@@ -408,7 +412,7 @@ def test_k5_fused_dyw_limits():
         rc = lib.ddpm_gencat_bwd_yw_staged(1, 1 << 20, 1, 1, 1, 1, 1, 1, 1 << 20,
                                            1, 64, 16, 16, 5, 1, 3, 5, code, None)
         assert rc == -2
-    assert not _kernels._fused_dyw_ok(5, torch.bfloat16, 48, (1, 6, 4))
+    assert _kernels._fused_dyw_ok(5, torch.bfloat16, 48, (1, 8, 4))
     assert _kernels._fused_dyw_ok(5, torch.bfloat16, 48, (1, 3, 5))
     assert not _kernels._fused_dyw_ok(5, torch.bfloat16, 44, (1, 3, 5))
     assert not _kernels._fused_dyw_ok(5, torch.float32, 48, (1, 3, 5))
