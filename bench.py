@@ -405,12 +405,12 @@ NCU_TRAFFIC_BYTES: dict[tuple[str, str], float] = {
     # staged paths: the main kernel only (the staging copies are HBM-bound
     # passes of their own, profiles/staging_256.md)
     ("gencat_fwd", "torch.float32"): 115258624,
-    ("gencat_fwd", "torch.bfloat16"): 42377472,
+    ("gencat_fwd", "torch.bfloat16"): 19198976 + 13590272,  # 16-bit x cells
     ("gencat_bwd_x", "torch.float32"): 86148096 + 5298688,  # channel-last grad_out
-    ("gencat_bwd_x", "torch.bfloat16"): 45458944 + 896000,  # channel-last grad_out
+    ("gencat_bwd_x", "torch.bfloat16"): 45455616 + 169728,  # channel-last grad_out
     # channel-last grad_out, D_y drained by TMA reductions
     ("gencat_bwd_yw", "torch.float32"): 105654784 + 8497664,
-    ("gencat_bwd_yw", "torch.bfloat16"): 69647872 + 3415040,
+    ("gencat_bwd_yw", "torch.bfloat16"): 61231104 + 1570816,  # 16-bit x cells
     ("fuseconv_fwd", "torch.float32"): 75615744,
     ("fuseconv_fwd", "torch.bfloat16"): 36270848,
     ("fuseconv_dgrad", "torch.float32"): 27409920,
