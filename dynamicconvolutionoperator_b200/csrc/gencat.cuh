@@ -132,10 +132,11 @@ __device__ __forceinline__ void fail(volatile int* abort_flag, int* status, int 
   atomicCAS(status, 0, code);
 }
 
-// Warp-uniform bounded wait (all lanes see the same outcome).
+// Warp-uniform bounded wait (all lanes see the same outcome); `hint_ns` as in
+// tc::mbar_wait.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity,
-                                          volatile int* abort_flag) {
-  const bool ok = tc::mbar_wait(bar, parity, abort_flag, kWaitNs);
+                                          volatile int* abort_flag, uint32_t hint_ns = 0) {
+  const bool ok = tc::mbar_wait(bar, parity, abort_flag, kWaitNs, hint_ns);
   return __all_sync(0xffffffffu, ok);
 }
 

@@ -78,16 +78,21 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 
 // Wait for the phase with `parity` to complete, for at most `limit_ns`.
 // Returns false on timeout (the caller records the failure and unwinds);
-// `abort_flag` (shared) lets one role stop the others early.
+// `abort_flag` (shared) lets one role stop the others early. With `hint_ns`,
+// each try_wait may keep the thread suspended (not issuing) for up to that
+// long, waking when the phase completes; the abort flag and the limit are
+// then checked after every try.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          volatile int* abort_flag, uint64_t limit_ns) {
+                                          volatile int* abort_flag, uint64_t limit_ns,
+                                          uint32_t hint_ns = 0) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   uint32_t spins = 0;
   while (true) {
     // try_wait itself parks the thread for a short, hardware-chosen time
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((++spins & 63u) == 0) {
+    if (hint_ns != 0 ? mbar_try_wait_sleep(bar, parity, hint_ns) : mbar_try_wait(bar, parity))
+      return true;
+    if (hint_ns != 0 || (++spins & 63u) == 0) {
       if (abort_flag != nullptr && *abort_flag) return false;
       if (globaltimer_ns() - t0 > limit_ns) return false;
     }
