@@ -860,6 +860,10 @@ __host__ __device__ inline int dyw_halo_off(int ks, int R) { return ks <= 3 ? 8 
 // (80 columns each) beside D_y in TMEM, so CTAs take sets of at most 4.
 constexpr int kDywSetOct = 4;
 
+// Every wait of the merged dY + dW kernel lets a waiting thread stay suspended
+// (not issuing) for up to this long, woken by the phase's completion.
+constexpr uint32_t kHintNs = 100000;
+
 // D_y drain buffers: one per TMEM lane quadrant (the drain warp's 32 pixels =
 // 2 rows x 16 columns), 8 channels at a time: [8 ch][2 rows][16 px] FP32.
 constexpr uint32_t kDyChunkBytes = 8 * 2 * 16 * 4;
@@ -935,7 +939,7 @@ __device__ __forceinline__ bool drain_dy(const DywParams& p, const DywMaps& maps
                                          uint32_t dy_col, uint64_t* d_full, uint64_t* d_empty,
                                          volatile int* abort_flag, float* buf) {
   const int tb = it & 1;
-  if (!warp_wait(&d_full[tb], (it >> 1) & 1, abort_flag)) return false;
+  if (!warp_wait(&d_full[tb], (it >> 1) & 1, abort_flag, kHintNs)) return false;
   tc::tc_fence_after();
   float dv[4][16];
   const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + dy_col + tb * 64;
@@ -1076,7 +1080,7 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
         for (int oct = oct0; oct < oct1; ++oct) {
           for (int part = 0; part < kLoads; ++part, ++wq) {
             const int s = wq % S;
-            if (!tc::mbar_wait(&w_empty[s], ((wq / S) & 1) ^ 1, abort_flag, kWaitNs)) {
+            if (!tc::mbar_wait(&w_empty[s], ((wq / S) & 1) ^ 1, abort_flag, kWaitNs, kHintNs)) {
               fail(abort_flag, p.status, 50);
               goto done;
             }
@@ -1098,7 +1102,7 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
       uint32_t wq = 0, kq = 0, it = 0;
       for (int tile = split; tile < p.num_tiles; tile += p.splits, ++it) {
         const int tb = it & 1;
-        if (!tc::mbar_wait(&d_empty[tb], ((it >> 1) & 1) ^ 1, abort_flag, kWaitNs)) {
+        if (!tc::mbar_wait(&d_empty[tb], ((it >> 1) & 1) ^ 1, abort_flag, kWaitNs, kHintNs)) {
           fail(abort_flag, p.status, 51);
           goto done;
         }
@@ -1111,9 +1115,9 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
           for (int oct = oct0; oct < oct1; ++oct, ++kq) {
             const int hb = kq & 1;
             const int s_hi = wq % S;
-            if (!tc::mbar_wait(&k_full[hb], (kq >> 1) & 1, abort_flag, kWaitNs) ||
-                !tc::mbar_wait(lo_full, kq & 1, abort_flag, kWaitNs) ||
-                !tc::mbar_wait(&w_full[s_hi], (wq / S) & 1, abort_flag, kWaitNs)) {
+            if (!tc::mbar_wait(&k_full[hb], (kq >> 1) & 1, abort_flag, kWaitNs, kHintNs) ||
+                !tc::mbar_wait(lo_full, kq & 1, abort_flag, kWaitNs, kHintNs) ||
+                !tc::mbar_wait(&w_full[s_hi], (wq / S) & 1, abort_flag, kWaitNs, kHintNs)) {
               fail(abort_flag, p.status, 52);
               goto done;
             }
@@ -1132,7 +1136,7 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
             tc::mma_commit(&w_empty[s_hi]);
             ++wq;
             const int s_lo = wq % S;
-            if (!tc::mbar_wait(&w_full[s_lo], (wq / S) & 1, abort_flag, kWaitNs)) {
+            if (!tc::mbar_wait(&w_full[s_lo], (wq / S) & 1, abort_flag, kWaitNs, kHintNs)) {
               fail(abort_flag, p.status, 52);
               goto done;
             }
@@ -1150,8 +1154,8 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
         }
         for (int oct = oct0; oct < oct1; ++oct, ++wq, ++kq) {
           const int s = wq % S, ks_ = kq % NS;
-          if (!tc::mbar_wait(&k_full[ks_], (kq / NS) & 1, abort_flag, kWaitNs) ||
-              !tc::mbar_wait(&w_full[s], (wq / S) & 1, abort_flag, kWaitNs)) {
+          if (!tc::mbar_wait(&k_full[ks_], (kq / NS) & 1, abort_flag, kWaitNs, kHintNs) ||
+              !tc::mbar_wait(&w_full[s], (wq / S) & 1, abort_flag, kWaitNs, kHintNs)) {
             fail(abort_flag, p.status, 52);
             goto done;
           }
@@ -1190,7 +1194,7 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
       bool first = true;
       for (int tile = split; tile < p.num_tiles; tile += p.splits, ++it) {
         const int yb = it % NY;
-        if (!tc::mbar_wait(&y_full[yb], (it / NY) & 1, abort_flag, kWaitNs)) {
+        if (!tc::mbar_wait(&y_full[yb], (it / NY) & 1, abort_flag, kWaitNs, kHintNs)) {
           fail(abort_flag, p.status, 53);
           goto done;
         }
@@ -1203,8 +1207,8 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
               tc::smem_desc(tc::smem_u32(smem + L.dk + 2 * kDkBytes), 2048, 128);
           for (int oct = oct0; oct < oct1; ++oct, ++kq) {
             const int hb = kq & 1;
-            if (!tc::mbar_wait(&k_full[hb], (kq >> 1) & 1, abort_flag, kWaitNs) ||
-                !tc::mbar_wait(lo_full, kq & 1, abort_flag, kWaitNs)) {
+            if (!tc::mbar_wait(&k_full[hb], (kq >> 1) & 1, abort_flag, kWaitNs, kHintNs) ||
+                !tc::mbar_wait(lo_full, kq & 1, abort_flag, kWaitNs, kHintNs)) {
               fail(abort_flag, p.status, 54);
               goto done;
             }
@@ -1232,7 +1236,7 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
         }
         for (int oct = oct0; oct < oct1; ++oct, ++kq) {
           const int ks_ = kq % NS;
-          if (!tc::mbar_wait(&k_full[ks_], (kq / NS) & 1, abort_flag, kWaitNs)) {
+          if (!tc::mbar_wait(&k_full[ks_], (kq / NS) & 1, abort_flag, kWaitNs, kHintNs)) {
             fail(abort_flag, p.status, 54);
             goto done;
           }
@@ -1273,7 +1277,7 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
     bool failed = false;
     for (int tile = split; tile < p.num_tiles && !*abort_flag; tile += p.splits, ++xq) {
       const int xb = xq & nx_sh;
-      if (!warp_wait(&x_empty[xb], ((xq >> nx_sh) & 1) ^ 1, abort_flag)) {
+      if (!warp_wait(&x_empty[xb], ((xq >> nx_sh) & 1) ^ 1, abort_flag, kHintNs)) {
         fail(abort_flag, p.status, 55);
         failed = true;
         break;
@@ -1296,7 +1300,7 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
           if (warp == Cfg::kFirstXWarp + 1) {
             bool ok = true;
             if (lane == 0) {
-              ok = tc::mbar_wait(g_empty, (xq & 1) ^ 1, abort_flag, kWaitNs);
+              ok = tc::mbar_wait(g_empty, (xq & 1) ^ 1, abort_flag, kWaitNs, kHintNs);
               if (ok) {
                 tc::mbar_arrive_expect_tx(g_full, L.g_bytes);
                 if (p.g_nhwc)
@@ -1339,7 +1343,7 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
     bool failed = false;
     for (int tile = split; tile < p.num_tiles && !*abort_flag; tile += p.splits, ++it) {
       const int yb = it % NY;
-      if (!warp_wait(&y_empty[yb], ((it / NY) & 1) ^ 1, abort_flag)) {
+      if (!warp_wait(&y_empty[yb], ((it / NY) & 1) ^ 1, abort_flag, kHintNs)) {
         fail(abort_flag, p.status, 56);
         failed = true;
         break;
@@ -1405,7 +1409,7 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
       uint32_t gw[3][8];
       if constexpr (kGTma) {
         static_assert(!kGTma || Cfg::kXIo, "the gradient tile by TMA implies staged 16-bit x cells");
-        if (!warp_wait(g_full, xq & 1, abort_flag)) {
+        if (!warp_wait(g_full, xq & 1, abort_flag, kHintNs)) {
           fail(abort_flag, p.status, 47);
           failed = true;
           break;
@@ -1461,7 +1465,7 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
         }
       }
       const int xb = xq & nx_sh;
-      if (!warp_wait(&x_full[xb], (xq >> nx_sh) & 1, abort_flag)) {
+      if (!warp_wait(&x_full[xb], (xq >> nx_sh) & 1, abort_flag, kHintNs)) {
         fail(abort_flag, p.status, 57);
         failed = true;
         break;
@@ -1471,8 +1475,8 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
       const uint4* xci = reinterpret_cast<const uint4*>(smem + L.xr + xb * L.xr_bytes) + xcell0;
       for (int oct = oct0; oct < oct1; ++oct, ++kq) {
         const int ks_ = kq % NS;
-        if (!warp_wait(&k_empty[ks_], ((kq / NS) & 1) ^ 1, abort_flag) ||
-            (kLoRing && !warp_wait(lo_empty, (kq & 1) ^ 1, abort_flag))) {
+        if (!warp_wait(&k_empty[ks_], ((kq / NS) & 1) ^ 1, abort_flag, kHintNs) ||
+            (kLoRing && !warp_wait(lo_empty, (kq & 1) ^ 1, abort_flag, kHintNs))) {
           fail(abort_flag, p.status, 58);
           failed = true;
           break;
@@ -1493,7 +1497,7 @@ gencat_bwd_dyw_kernel(const DywParams p, const __grid_constant__ DywMaps maps) {
       tc::mbar_arrive(&x_empty[xb]);
     }
     // D_w of this CTA's split: lane = weight row, half h drains octets 2h, 2h+1
-    if (!failed && warp_wait(w_done, 0, abort_flag)) {
+    if (!failed && warp_wait(w_done, 0, abort_flag, kHintNs)) {
       tc::tc_fence_after();
       for (int lo = 2 * half; lo < 2 * half + 2 && oct0 + lo < oct1; ++lo) {
         const int g = cg * NOCT + oct0 + lo;

@@ -73,6 +73,10 @@ using namespace gencat;
 // a fault. Zero in normal operation.
 __device__ int g_test_skip_arrive;
 
+// Every wait of the forward kernel lets a waiting thread stay suspended (not
+// issuing) for up to this long, woken by the phase's completion.
+constexpr uint32_t kHintNs = 100000;
+
 template <typename T, int KS, bool kStaged = false>
 struct FwdCfg {
   static constexpr bool kSplit = IoTraits<T>::kSplit;
@@ -302,7 +306,7 @@ gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
       const uint64_t a_lo = (kTileM * Ck * 2) >> 4;        // hi -> lo part of the y tile
       const uint64_t b_lo = (Cfg::kRows * Ck * 2) >> 4;    // hi -> lo part of the weights
       const int nks = Ck / 16;
-      if (!tc::mbar_wait(w_full, 0, abort_flag, kWaitNs)) {
+      if (!tc::mbar_wait(w_full, 0, abort_flag, kWaitNs, kHintNs)) {
         fail(abort_flag, p.status, 10);
         goto done;
       }
@@ -310,7 +314,7 @@ gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
       uint32_t tq = 0, it = 0;
       for (int tile = first_tile; tile < p.num_tiles; tile += tile_step, ++it) {
         const int yb = it % NY;
-        if (!tc::mbar_wait(&y_full[yb], (it / NY) & 1, abort_flag, kWaitNs)) {
+        if (!tc::mbar_wait(&y_full[yb], (it / NY) & 1, abort_flag, kWaitNs, kHintNs)) {
           fail(abort_flag, p.status, 11);
           goto done;
         }
@@ -323,7 +327,7 @@ gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
           const uint32_t own = tq / Cfg::kEpiWG;
           const int j = (int)(tq % Cfg::kEpiWG) * Cfg::kBufPerWG + own % Cfg::kBufPerWG;
           if (!tc::mbar_wait(&t_empty[j], ((own / Cfg::kBufPerWG) & 1) ^ 1, abort_flag,
-                             kWaitNs)) {
+                             kWaitNs, kHintNs)) {
             fail(abort_flag, p.status, 12);
             goto done;
           }
@@ -349,7 +353,7 @@ gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
       // Teardown frees TMEM: wait until every issued MMA has completed
       // (w_full's phase 1, after the weight load's phase 0).
       tc::mma_commit(w_full);
-      if (!tc::mbar_wait(w_full, 1, abort_flag, kWaitNs)) fail(abort_flag, p.status, 17);
+      if (!tc::mbar_wait(w_full, 1, abort_flag, kWaitNs, kHintNs)) fail(abort_flag, p.status, 17);
     }
   } else if (warp < 2 + Cfg::kProducers / 32) {
     // ---- y-tile producers ----------------------------------------------------
@@ -360,7 +364,7 @@ gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
     uint32_t it = 0;
     for (int tile = first_tile; tile < p.num_tiles; tile += tile_step, ++it) {
       const int yb = it % NY;
-      if (!warp_wait(&y_empty[yb], ((it / NY) & 1) ^ 1, abort_flag)) {
+      if (!warp_wait(&y_empty[yb], ((it / NY) & 1) ^ 1, abort_flag, kHintNs)) {
         fail(abort_flag, p.status, 13);
         break;
       }
@@ -396,7 +400,7 @@ gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
     uint32_t it = 0;
     for (int tile = first_tile; tile < p.num_tiles; tile += tile_step, ++it) {
       const int xb = it & nx_sh;
-      if (!warp_wait(&x_empty[xb], ((it >> nx_sh) & 1) ^ 1, abort_flag)) {
+      if (!warp_wait(&x_empty[xb], ((it >> nx_sh) & 1) ^ 1, abort_flag, kHintNs)) {
         fail(abort_flag, p.status, 15);
         break;
       }
@@ -437,7 +441,7 @@ gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
       const size_t pix = (size_t)h * W + w;
       T* on = out + (size_t)n * 4 * C * P;
       const int xb = it & nx_sh;
-      if (!warp_wait(&x_full[xb], (it >> nx_sh) & 1, abort_flag)) {
+      if (!warp_wait(&x_full[xb], (it >> nx_sh) & 1, abort_flag, kHintNs)) {
         fail(abort_flag, p.status, 16);
         break;
       }
@@ -450,7 +454,7 @@ gencat_fwd_kernel(const FwdParams p, const __grid_constant__ FwdMaps maps) {
         if (tq % Cfg::kEpiWG != (uint32_t)wg) continue;  // another warpgroup's slot
         const uint32_t own = tq / Cfg::kEpiWG;
         const int j = wg * Cfg::kBufPerWG + own % Cfg::kBufPerWG;
-        if (!warp_wait(&t_full[j], (own / Cfg::kBufPerWG) & 1, abort_flag)) {
+        if (!warp_wait(&t_full[j], (own / Cfg::kBufPerWG) & 1, abort_flag, kHintNs)) {
           fail(abort_flag, p.status, 14);
           failed = true;
           break;
