@@ -513,6 +513,15 @@ __device__ __forceinline__ unsigned long long fma_io2<__half>(uint32_t a, uint32
   return f2_pack(lo, hi);
 }
 
+// Two 16-bit values as one word, the first in bits 0-15.
+template <typename T>
+__device__ __forceinline__ uint32_t pack_raw2(T lo, T hi) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value)
+    return (uint32_t)__bfloat16_as_ushort(lo) | ((uint32_t)__bfloat16_as_ushort(hi) << 16);
+  else
+    return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
+}
+
 // a * b per 16-bit lane, rounded once to Op (round to nearest even): the
 // exact product of two 16-bit values rounded to the type, the same value as
 // the FP32 product (exact) converted with cvt2.

@@ -523,19 +523,31 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
               tc::tc_fence_after();
               if (blk_ok) tc::tmem_ld16(tcol + (tn % NB) * Cp, dv[cur ^ 1]);
             }
-            if constexpr (kNhwc && sizeof(T) == 2) {
+            if constexpr (sizeof(T) == 2) {
               if (blk_ok) {
-                // 16-bit channel-last: the block's channels are chunks 2wg and
-                // 2wg+1 (8 each) of swizzled pixel row m + kOff - dx (chunk j
-                // of row r at j ^ (r & 7)); each word of two gradient values
-                // meets the matching pair of rounded taps in two
-                // mixed-precision FMAs (no conversion of either to FP32)
-                const int pr = m + kOff - (kj - r) * d;
-                const uint8_t* row = reinterpret_cast<const uint8_t*>(gs) + pr * 128;
-                const uint4 v0 = *reinterpret_cast<const uint4*>(row + (((2 * wg) ^ (pr & 7)) * 16));
-                const uint4 v1 =
-                    *reinterpret_cast<const uint4*>(row + (((2 * wg + 1) ^ (pr & 7)) * 16));
-                const uint32_t gw[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+                // 16-bit: each word of two gradient values meets the matching
+                // pair of rounded taps in two mixed-precision FMAs (no
+                // conversion of either to FP32)
+                uint32_t gw[8];
+                if constexpr (kNhwc) {
+                  // channel-last: the block's channels are chunks 2wg and 2wg+1
+                  // (8 each) of swizzled pixel row m + kOff - dx (chunk j of
+                  // row r at j ^ (r & 7))
+                  const int pr = m + kOff - (kj - r) * d;
+                  const uint8_t* row = reinterpret_cast<const uint8_t*>(gs) + pr * 128;
+                  const uint4 v0 =
+                      *reinterpret_cast<const uint4*>(row + (((2 * wg) ^ (pr & 7)) * 16));
+                  const uint4 v1 =
+                      *reinterpret_cast<const uint4*>(row + (((2 * wg + 1) ^ (pr & 7)) * 16));
+                  gw[0] = v0.x; gw[1] = v0.y; gw[2] = v0.z; gw[3] = v0.w;
+                  gw[4] = v1.x; gw[5] = v1.y; gw[6] = v1.z; gw[7] = v1.w;
+                } else {
+                  // [Cp][kSeg] segment: channel pairs of column m + kOff - dx
+                  const int dx = (kj - r) * d;
+#pragma unroll
+                  for (int i = 0; i < 8; ++i)
+                    gw[i] = pack_raw2<T>(gcol[(2 * i) * kSeg - dx], gcol[(2 * i + 1) * kSeg - dx]);
+                }
 #pragma unroll
                 for (int i = 0; i < 8; ++i)
                   acc2[i] = fma_io2<Op>(cvt2<Op>(dv[cur][2 * i], dv[cur][2 * i + 1]), gw[i], acc2[i]);
@@ -543,8 +555,9 @@ gencat_bwd_x_kernel(const __grid_constant__ BxParams p) {
             } else if (blk_ok) {
               const int dx = (kj - r) * d;
               float gv[16];
+              // FP32 (16-bit takes the branch above)
               if constexpr (kNhwc) {
-                // FP32 (16-bit takes the branch above): pixel row m + kOff - dx
+                // pixel row m + kOff - dx
                 // of the swizzled [kSeg][128 bytes] segments; box wg / 2 holds
                 // channels 32 (wg / 2) .. +31, the block's 16 channels are its
                 // chunks 4 (wg % 2) .. +3, chunk j of row r at j ^ (r & 7)

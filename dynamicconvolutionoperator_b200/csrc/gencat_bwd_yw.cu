@@ -26,7 +26,6 @@
 // channel at index C so column C of D_w is db) accumulates over all tiles of
 // the split; partials go to a workspace and a short kernel reduces them into
 // the Conv2d weight layout.
-#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -167,15 +166,6 @@ __device__ __forceinline__ void build_dk_half_io(uint8_t* dk, int octet, int hal
     }
     build_dk_half_io<T, Op, KS, O + 1>(dk, octet, half, xc, xr_plane, gw, dil, m, cols);
   }
-}
-
-// Two 16-bit values as one word, the first in bits 0-15.
-template <typename T>
-__device__ __forceinline__ uint32_t pack_raw2(T lo, T hi) {
-  uint16_t a, b;
-  memcpy(&a, &lo, 2);
-  memcpy(&b, &hi, 2);
-  return (uint32_t)a | ((uint32_t)b << 16);
 }
 
 // g_b[cg16*16 + cl, pixel] for the three branches (zero off-image / c >= C).
