@@ -61,3 +61,27 @@ def test_dyncat_bwd_rejects_halos_the_data_gradient_cannot_stage():
     assert rc != 0 and b"halo 40" in lib.ddpm_last_error()
     rc = lib.ddpm_dyncat_bwd(*args, 1, None, 1, 1, 8, 8, 3, 1, 65, 5, None)
     assert rc != 0 and b"halo" in lib.ddpm_last_error()
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape,ks,dil", [((2, 24, 15, 17), 3, (1, 3, 5)), ((1, 64, 256, 256), 5, (1, 8, 4)),
+                                          ((1, 5, 4, 3), 1, (1, 1, 1))])
+def test_stage_bytes_follow_the_staged_layout(dtype, shape, ks, dil):
+    """ddpm_gencat_stage_bytes (host arithmetic only): the y plane
+    [part][n][G][Hp][Wp][8] in 16-byte rows, then, 256-byte aligned, the x
+    plane of 16-byte cells holding 4 FP32 channels (fp32) or 8 channels in the
+    input type (bf16 / fp16); 0 for a halo the fused kernels do not cover."""
+    lib = _lib.load()
+    code = _lib.dtype_code(dtype)
+    n, c, h, w = shape
+    G = (c + 1 + 15) // 16 * 2
+    ph = (ks // 2) * max(dil)
+    pw = 8 if ks <= 3 else 16
+    Hp, Wp = h + 2 * ph, (w + 127) // 128 * 128 + 2 * pw
+    parts = 2 if dtype == torch.float32 else 1
+    x_off = (parts * n * G * Hp * Wp * 16 + 255) // 256 * 256
+    xcell = 4 if dtype == torch.float32 else 8
+    want = x_off + n * ((c + xcell - 1) // xcell) * h * w * 16
+    assert lib.ddpm_gencat_stage_bytes(n, c, h, w, ks, *dil, code) == want
+    if ks > 1:  # halos (K // 2) * 9 = 9 (K = 3, limit 8) and 18 (K = 5, limit 16)
+        assert lib.ddpm_gencat_stage_bytes(n, c, h, w, ks, 1, 9, 4, code) == 0
