@@ -64,6 +64,55 @@ __global__ void __launch_bounds__(256) stage_y_kernel(const T* __restrict__ y,
   }
 }
 
+// The y plane for 16-bit data: the same rows, transposed in the input type
+// (no FP32 round trip) through a [channel][128 + 8 px] tile of 16-bit values
+// (272-byte rows, 16-byte aligned); block = (n, plane row, 128-column strip).
+// Each thread issues all of its 16-byte pixel-vector loads (5 at most) before
+// its first shared store; the writes are 16-byte rows of 8 channels,
+// consecutive threads at consecutive plane columns.
+template <typename T>
+__global__ void __launch_bounds__(256) stage_y16_kernel(const T* __restrict__ y,
+                                                        uint4* __restrict__ out,
+                                                        const StageLayout L) {
+  constexpr int kCols = 128;
+  constexpr int kGroups = kCols / 8;  // 8-pixel vectors per channel row
+  constexpr int kItems = (kStageChannels * kGroups + 255) / 256;
+  __shared__ __align__(16) uint16_t tile[kStageChannels][kCols + 8];
+  const int ni = blockIdx.x, n = ni / L.Hp, i = ni - n * L.Hp;
+  const int hr = i - L.ph;                 // image row (may be outside the image)
+  const int j0 = blockIdx.y * kCols;       // first plane column of the block
+  const int items = L.G * 8 * kGroups;
+  const size_t P = (size_t)L.H * L.W;
+  Raw8<T> v[kItems];
+#pragma unroll
+  for (int u = 0; u < kItems; ++u) {
+    const int item = threadIdx.x + u * 256;
+    const int g = item % kGroups, c = item / kGroups;
+    if (item < items && c < L.C)
+      v[u] = load_raw8<T>(y + ((size_t)n * L.C + c) * P, L.H, L.W, hr, j0 - L.pw + g * 8);
+    else if (c == L.C)
+      v[u].ones();
+    else
+      v[u].zero();
+  }
+#pragma unroll
+  for (int u = 0; u < kItems; ++u) {
+    const int item = threadIdx.x + u * 256;
+    if (item < items)
+      *reinterpret_cast<uint4*>(&tile[item / kGroups][(item % kGroups) * 8]) = v[u].u;
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < L.G * kCols; idx += blockDim.x) {
+    const int kg = idx / kCols, x = idx - kg * kCols;
+    if (j0 + x >= L.Wp) continue;
+    uint32_t w[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      w[e] = (uint32_t)tile[kg * 8 + 2 * e][x] | ((uint32_t)tile[kg * 8 + 2 * e + 1][x] << 16);
+    out[L.row_offset(0, n, i, kg, j0 + x) / 16] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
 // x plane: thread = one 16-byte cell (n, cell q, h, w) = x[n, q*xcell ..
 // q*xcell + xcell-1, h, w]: FP32 cells of 4 channels, or 16-bit cells of 8
 // channels in the input type (channels >= C zero); consecutive threads =
@@ -159,9 +208,15 @@ template <typename T>
 int launch_stage(const T* x, const T* y, uint8_t* staged, const StageLayout& L, cudaStream_t st) {
   uint4* hi = reinterpret_cast<uint4*>(staged);
   uint4* lo = L.parts > 1 ? reinterpret_cast<uint4*>(staged + L.part_bytes) : nullptr;
-  const dim3 grid((unsigned)(L.N * L.Hp), (unsigned)((L.Wp + kStageCols - 1) / kStageCols));
-  stage_y_kernel<T><<<grid, 256, 0, st>>>(y, hi, lo, L);
-  DDPM_CHECK_LAUNCH("stage_y_kernel");
+  if constexpr (sizeof(T) == 2) {
+    const dim3 grid((unsigned)(L.N * L.Hp), (unsigned)((L.Wp + 127) / 128));
+    stage_y16_kernel<T><<<grid, 256, 0, st>>>(y, hi, L);
+    DDPM_CHECK_LAUNCH("stage_y16_kernel");
+  } else {
+    const dim3 grid((unsigned)(L.N * L.Hp), (unsigned)((L.Wp + kStageCols - 1) / kStageCols));
+    stage_y_kernel<T><<<grid, 256, 0, st>>>(y, hi, lo, L);
+    DDPM_CHECK_LAUNCH("stage_y_kernel");
+  }
   const size_t P = (size_t)L.H * L.W;
   if (x != nullptr && P % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15u) == 0 &&
       (size_t)L.N * L.Cq <= 65535u) {
