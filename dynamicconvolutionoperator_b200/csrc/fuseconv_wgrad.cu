@@ -513,6 +513,70 @@ __global__ void __launch_bounds__(256) fuseconv_dout_pack_kernel(const T* __rest
   }
 }
 
+// The same pre-pass for 16-bit dout, transposed in its own type (no FP32
+// round trip): a [channel][64 + 8 px] tile of 16-bit values (144-byte rows,
+// 16-byte aligned), each thread's two 16-byte loads issued before its first
+// shared store; the db partial sums the same FP32 values in the same order.
+template <typename T>
+__global__ void __launch_bounds__(256) fuseconv_dout_pack16_kernel(const T* __restrict__ dout,
+                                                                   uint4* __restrict__ hi,
+                                                                   float* __restrict__ dbp,
+                                                                   int H, int W, int Cout, int Np) {
+  constexpr int kGroups = kPackCols / 8;
+  constexpr int kItems = (fuseconv::kMaxCout * kGroups + 255) / 256;
+  __shared__ __align__(16) uint16_t tile[fuseconv::kMaxCout][kPackCols + 8];
+  const int nh = blockIdx.x, n = nh / H, h = nh - n * H;
+  const int w0 = blockIdx.y * kPackCols;
+  const size_t P = (size_t)H * W;
+  const T* src = dout + (size_t)n * Cout * P;
+  const int items = Np * kGroups;
+  Raw8<T> v[kItems];
+#pragma unroll
+  for (int u = 0; u < kItems; ++u) {
+    const int item = threadIdx.x + u * 256;
+    const int g = item % kGroups, c = item / kGroups;
+    if (item < items && c < Cout)
+      v[u] = load_raw8<T>(src + (size_t)c * P, H, W, h, w0 + g * 8);
+    else
+      v[u].zero();
+  }
+#pragma unroll
+  for (int u = 0; u < kItems; ++u) {
+    const int item = threadIdx.x + u * 256;
+    if (item < items)
+      *reinterpret_cast<uint4*>(&tile[item / kGroups][(item % kGroups) * 8]) = v[u].u;
+  }
+  __syncthreads();
+  // db partial: 4 threads per channel, 16 columns each
+  {
+    const int c = threadIdx.x >> 2, q = threadIdx.x & 3;
+    float acc = 0.f;
+    if (c < Np) {
+#pragma unroll
+      for (int x = 0; x < 16; ++x) {
+        const uint16_t b = tile[c][q * 16 + x];
+        if constexpr (std::is_same<T, __nv_bfloat16>::value)
+          acc += __uint_as_float((uint32_t)b << 16);
+        else
+          acc += __half2float(__ushort_as_half(b));
+      }
+    }
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    if (c < Np && q == 0) dbp[((size_t)nh * gridDim.y + blockIdx.y) * Np + c] = acc;
+  }
+  const int ng = Np / 8;
+  for (int idx = threadIdx.x; idx < ng * kPackCols; idx += blockDim.x) {
+    const int og = idx / kPackCols, x = idx - og * kPackCols;
+    if (w0 + x >= W) continue;
+    uint32_t w[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      w[e] = (uint32_t)tile[og * 8 + 2 * e][x] | ((uint32_t)tile[og * 8 + 2 * e + 1][x] << 16);
+    hi[((size_t)nh * ng + og) * W + w0 + x] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
 template <typename T>
 struct WtCfg {
   static constexpr bool kSplit = IoTraits<T>::kSplit;
@@ -836,9 +900,15 @@ int run_wgrad_tma(const void* cat, const void* gout, void* gw, void* gb, uint8_t
   prm.b_stage = ((Cfg::kSplit ? 6u : 3u) * prm.b_copy + 1023u) / 1024u * 1024u;
   prm.status = status;
 
-  fuseconv_dout_pack_kernel<T><<<dim3(n * h, t.strips), 256, 0, st>>>(
-      static_cast<const T*>(gout), hi, lo, dbp, h, w, cout, Np);
-  DDPM_CHECK_LAUNCH("fuseconv_dout_pack_kernel");
+  if constexpr (sizeof(T) == 2) {
+    fuseconv_dout_pack16_kernel<T><<<dim3(n * h, t.strips), 256, 0, st>>>(
+        static_cast<const T*>(gout), hi, dbp, h, w, cout, Np);
+    DDPM_CHECK_LAUNCH("fuseconv_dout_pack16_kernel");
+  } else {
+    fuseconv_dout_pack_kernel<T><<<dim3(n * h, t.strips), 256, 0, st>>>(
+        static_cast<const T*>(gout), hi, lo, dbp, h, w, cout, Np);
+    DDPM_CHECK_LAUNCH("fuseconv_dout_pack_kernel");
+  }
   if (gcat != nullptr) {
     int rc = fuseconv_dgrad_rowmajor(hi, lo, packed, gcat, n, cin, cout, h, w, dt, st, gcat_nhwc);
     if (rc == DDPM_ERR_UNSUPPORTED) rc = fuseconv_dgrad(gout, packed, gcat, n, cin, cout, h, w,
